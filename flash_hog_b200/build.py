@@ -1,0 +1,86 @@
+"""Build the in-tree CUDA libraries for sm_100a with nvcc.
+
+* ``libflashhog_b200.so`` -- the attention kernels and the C ABI declared in
+  ``include/flash_hog_b200.h``;
+* ``libfh_selftest.so`` -- the tcgen05 building-block unit test used by
+  ``tests/test_gpu_primitives.py``.
+
+Both are written next to this file so they travel with the source tree. Object
+files are cached under ``_build/`` keyed by source and header modification
+times, so an unchanged tree rebuilds in well under a second.
+"""
+
+from __future__ import annotations
+
+import os
+import shutil
+import subprocess
+import sys
+from concurrent.futures import ThreadPoolExecutor
+
+PKG = os.path.dirname(os.path.abspath(__file__))
+CSRC = os.path.join(PKG, "csrc")
+ROOT = os.path.dirname(PKG)
+BUILD_DIR = os.path.join(ROOT, "_build")
+
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-O2", "--expt-relaxed-constexpr",
+              "-I" + os.path.join(ROOT, "include"), "-I" + CSRC]
+
+MAIN_SOURCES = ["capi.cu", "fwd.cu", "bwd.cu", "bwdbwd.cu", "rowdot.cu"]
+SELFTEST_SOURCES = ["selftest.cu"]
+
+MAIN_LIB = os.path.join(PKG, "libflashhog_b200.so")
+SELFTEST_LIB = os.path.join(PKG, "libfh_selftest.so")
+
+
+def nvcc() -> str:
+    for cand in (shutil.which("nvcc"), "/usr/local/cuda/bin/nvcc"):
+        if cand and os.path.exists(cand):
+            return cand
+    raise RuntimeError("nvcc not found: the CUDA toolkit is required to build flash_hog_b200")
+
+
+def _headers_mtime() -> float:
+    paths = [os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith((".cuh", ".h"))]
+    inc = os.path.join(ROOT, "include")
+    paths += [os.path.join(inc, f) for f in os.listdir(inc) if f.endswith(".h")]
+    return max(os.path.getmtime(p) for p in paths)
+
+
+def _compile(src: str, verbose: bool) -> str:
+    os.makedirs(BUILD_DIR, exist_ok=True)
+    path = os.path.join(CSRC, src)
+    obj = os.path.join(BUILD_DIR, src.replace(".cu", ".o"))
+    if os.path.exists(obj) and os.path.getmtime(obj) >= max(os.path.getmtime(path), _headers_mtime()):
+        return obj
+    cmd = [nvcc(), *ARCH, *NVCC_FLAGS, "-c", path, "-o", obj]
+    if verbose:
+        cmd.insert(1, "-Xptxas=-v")
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"nvcc failed on {src}:\n{res.stdout}\n{res.stderr}")
+    if verbose and res.stderr:
+        print(res.stderr, file=sys.stderr)
+    return obj
+
+
+def _link(objs, out):
+    cmd = [nvcc(), *ARCH, "-shared", "-o", out, *objs]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"link of {os.path.basename(out)} failed:\n{res.stdout}\n{res.stderr}")
+
+
+def build(verbose: bool = False) -> None:
+    """Compile every CUDA source for sm_100a and link the two shared libraries."""
+    srcs = MAIN_SOURCES + SELFTEST_SOURCES
+    with ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 1)) as ex:
+        objs = dict(zip(srcs, ex.map(lambda s: _compile(s, verbose), srcs)))
+    _link([objs[s] for s in MAIN_SOURCES], MAIN_LIB)
+    _link([objs[s] for s in SELFTEST_SOURCES], SELFTEST_LIB)
+
+
+if __name__ == "__main__":
+    build(verbose="-v" in sys.argv)
+    print("built", MAIN_LIB, SELFTEST_LIB)

@@ -1,0 +1,160 @@
+// Shared pieces of the attention kernels: problem description, tile geometry,
+// operand-descriptor helpers and the role layout of a CTA.
+//
+// Every attention kernel here has the same shape:
+//   * a CTA owns BM = 128 "resident" rows (query rows for the query-tiled
+//     kernels, key rows for the key-tiled ones) -- these are the TMEM lanes;
+//   * it streams BN-row tiles of the other side through a TMA ring;
+//   * warp 4 is the TMA producer, warp 5 allocates TMEM and issues tcgen05.mma
+//     from one thread, warps 0-3 (one warpgroup, thread = TMEM lane = row) do
+//     the elementwise math and the epilogue;
+//   * score-like products land in TMEM, the elementwise warps turn them into
+//     bf16 operand panels in shared memory, and accumulating products read
+//     those panels.
+
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "tc05.cuh"
+
+namespace fh {
+
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+constexpr int kBM = 128;            // resident rows per CTA (= TMEM lanes)
+constexpr int kThreads = 192;       // 6 warps
+constexpr int kWarpProducer = 4;
+constexpr int kWarpMma = 5;
+constexpr int kEwThreads = 128;     // warps 0-3
+
+// Strides (in elements) of a (batch, seq, head, head_dim) tensor; head_dim stride is 1.
+struct Strides3 {
+  long long b, t, h;
+};
+
+struct AttnShape {
+  int B, H, Tq, Tk;
+  Strides3 sq;   // query-side tensors
+  Strides3 sk;   // key-side tensors
+  float scale;
+  int causal;
+};
+
+__device__ __forceinline__ size_t row_offset(const Strides3& s, int b, int t, int h) {
+  return static_cast<size_t>(b) * s.b + static_cast<size_t>(t) * s.t + static_cast<size_t>(h) * s.h;
+}
+
+// Index into a (B, H, T) fp32 statistics vector.
+__device__ __forceinline__ size_t stat_index(int b, int h, int t, int H, int T) {
+  return (static_cast<size_t>(b) * H + h) * T + t;
+}
+
+__device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
+  return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
+}
+
+// Loads `rows` rows x HD columns starting at sequence row `row0` of head (b, h)
+// into HD/64 consecutive 128B-swizzled panels at `dst` (panel stride rows*128).
+template <int HD>
+__device__ __forceinline__ void tma_rows(uint8_t* dst, const CUtensorMap* map, uint64_t* bar, int row0, int rows,
+                                         int h, int b) {
+#pragma unroll
+  for (int pnl = 0; pnl < HD / 64; ++pnl) tma_load_4d(dst + pnl * rows * 128, map, bar, pnl * 64, row0, h, b);
+}
+
+// Descriptor for k-step `ks` (16 bf16 along K) of a K-major operand whose K
+// extent is spread over 64-column panels of `rows` rows.
+__device__ __forceinline__ uint64_t desc_k(const uint8_t* base, int rows, int ks) {
+  const uint32_t a = smem_u32(base) + (ks >> 2) * rows * 128 + (ks & 3) * 32;
+  return smem_desc(a, 16, 1024, kSwizzle128B);
+}
+
+// Descriptor for k-step `ks` (16 rows along K) of an MN-major operand stored as
+// panels of `rows` K-rows x 64 MN-columns (panel stride rows*128).
+__device__ __forceinline__ uint64_t desc_mn(const uint8_t* base, int rows, int ks) {
+  const uint32_t a = smem_u32(base) + ks * 16 * 128;
+  return smem_desc(a, rows * 128, 1024, kSwizzle128B);
+}
+
+// D (+)= A * B^T, A = [128 x K] K-major panels (a_rows = 128), B = [N x K]
+// K-major panels (b_rows = N); K = 16 * ksteps.
+__device__ __forceinline__ void gemm_abt(uint32_t d, const uint8_t* a, const uint8_t* bm, int b_rows, int ksteps,
+                                         uint32_t idesc, bool acc) {
+  for (int ks = 0; ks < ksteps; ++ks)
+    umma_bf16(d, desc_k(a, kBM, ks), desc_k(bm, b_rows, ks), idesc, (acc || ks > 0) ? 1u : 0u);
+}
+
+// D (+)= A * B, A = [128 x K] K-major panels, B = [K x N] MN-major panels of
+// K rows (b_rows = K); K = 16 * ksteps.
+__device__ __forceinline__ void gemm_ab(uint32_t d, const uint8_t* a, const uint8_t* bm, int b_rows, int ksteps,
+                                        uint32_t idesc, bool acc) {
+  for (int ks = 0; ks < ksteps; ++ks)
+    umma_bf16(d, desc_k(a, kBM, ks), desc_mn(bm, b_rows, ks), idesc, (acc || ks > 0) ? 1u : 0u);
+}
+
+// Records the first device-side error of a launch and raises the CTA's abort flag.
+__device__ __forceinline__ void raise_error(int* status, volatile int* abort_flag, int code) {
+  *abort_flag = 1;
+  if (status) atomicCAS(status, 0, code);
+}
+
+// Loads 16 TMEM columns starting at `col` for this thread's lane.
+__device__ __forceinline__ void tmem_row16(uint32_t tmem, int warp, int col, uint32_t (&r)[16]) {
+  tmem_ld16(tmem + tmem_lane_base(warp) + col, r);
+}
+
+// Writes 16 floats as bf16 (32 contiguous bytes) to global memory.
+__device__ __forceinline__ void store_bf16x16(__nv_bfloat16* dst, const float (&v)[16]) {
+  uint4 a, c;
+  a.x = pack_bf16(v[0], v[1]);
+  a.y = pack_bf16(v[2], v[3]);
+  a.z = pack_bf16(v[4], v[5]);
+  a.w = pack_bf16(v[6], v[7]);
+  c.x = pack_bf16(v[8], v[9]);
+  c.y = pack_bf16(v[10], v[11]);
+  c.z = pack_bf16(v[12], v[13]);
+  c.w = pack_bf16(v[14], v[15]);
+  reinterpret_cast<uint4*>(dst)[0] = a;
+  reinterpret_cast<uint4*>(dst)[1] = c;
+}
+
+// Writes 16 floats as bf16 into chunks (2*c16, 2*c16+1) of row r of a
+// 128B-swizzled panel.
+__device__ __forceinline__ void stage_bf16x16(uint8_t* panel, int r, int c16, const float (&v)[16]) {
+  const uint32_t base = smem_u32(panel);
+  st_shared_v4(base + sw128_offset(r, 2 * c16), pack_bf16(v[0], v[1]), pack_bf16(v[2], v[3]),
+               pack_bf16(v[4], v[5]), pack_bf16(v[6], v[7]));
+  st_shared_v4(base + sw128_offset(r, 2 * c16 + 1), pack_bf16(v[8], v[9]), pack_bf16(v[10], v[11]),
+               pack_bf16(v[12], v[13]), pack_bf16(v[14], v[15]));
+}
+
+// Drains the TMEM accumulator columns [col, col+HD) of this thread's lane to a
+// bf16 row in global memory.
+template <int HD>
+__device__ __forceinline__ void tmem_row_to_global(uint32_t tmem, int warp, int col, __nv_bfloat16* dst,
+                                                   bool write) {
+#pragma unroll
+  for (int c = 0; c < HD; c += 16) {
+    uint32_t r[16];
+    tmem_row16(tmem, warp, col + c, r);
+    tmem_wait_ld();
+    reg_fence16(r);
+    float v[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+    if (write) store_bf16x16(dst + c, v);
+  }
+}
+
+template <int HD>
+__device__ __forceinline__ void zero_row_global(__nv_bfloat16* dst) {
+#pragma unroll
+  for (int c = 0; c < HD; c += 8) reinterpret_cast<uint4*>(dst + c)[0] = make_uint4(0, 0, 0, 0);
+}
+
+}  // namespace fh
