@@ -1,0 +1,350 @@
+"""Benchmark of the headline metric: attention double backward (bwd-of-bwd) TFLOP/s.
+
+Workload (per GPU, weak scaling): causal bf16 B4 H16 S2048 D64 -- BASELINE.json's
+``configs[1]``. One step = one double-backward pass over one batch: the
+D = rowsum(dO o O) pre-pass, the query-tiled pass (dQ', ddO, dD, B) and the
+key-tiled pass (dK', dV'), i.e. the work of the reference's
+``dot_product_attention_bwd_rule_bwd_rule``. Credited FLOPs are
+22 GEMM-equivalents x 2 x D per kept (query, key) pair (378.1 GFLOP per step).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Under torchrun every rank runs the workload on its own GPU (batch x heads of a
+global batch 4N; no collective on the data path) and rank 0 prints one JSON line
+with the aggregate over ranks (time = max over ranks).
+
+``--impl reference`` times the reference algorithm's CPU path instead: the
+reference's own CPU path (XLA on CPU) needs JAX, which is absent, so the oracle
+port (torch double autograd of naive attention, fp32, all host threads) stands
+in, on bounded samples of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "bwd-of-bwd TFLOP/s/GPU, causal bf16 B4 H16 S2048 D64, at 1/2/4/8 B200"
+B, H, S, D = 4, 16, 2048, 64
+CAUSAL = True
+SCALE = D ** -0.5
+N_SETS = 3  # rotating input sets, each larger than the 126 MB L2
+PEAKS_FILE = os.path.join(ROOT, "MEASURED_PEAKS.json")
+FALLBACK_PEAKS = {"bf16_tflops": 1590.0, "hbm_gbs": 6650.0}
+
+
+def pairs(b, h, s, causal):
+    return b * h * (s * (s + 1) // 2 if causal else s * s)
+
+
+def credited_flops(b, h, s, gemms=22):
+    return gemms * 2 * D * pairs(b, h, s, CAUSAL)
+
+
+def load_peaks():
+    if os.path.exists(PEAKS_FILE):
+        with open(PEAKS_FILE) as f:
+            p = json.load(f)
+        return p, "measured"
+    return FALLBACK_PEAKS, "fallback"
+
+
+# ----------------------------------------------------------------------------------
+# clocks
+# ----------------------------------------------------------------------------------
+
+class ClockSampler:
+    """Samples SM clocks and throttle reasons with nvidia-smi while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpus):
+        self.gpus = gpus
+        self.proc = None
+        self.file = None
+
+    def __enter__(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
+                 "-i", ",".join(str(g) for g in self.gpus)], stdout=self.file, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if self.proc is None or self.file is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        with open(self.file.name) as f:
+            rows = [[c.strip() for c in line.split(",")] for line in f if line.strip()]
+        os.unlink(self.file.name)
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        sm, smax, reasons, power = [], [], set(), []
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                smax.append(float(r[2]))
+                power.append(float(r[3]))
+            except (ValueError, IndexError):
+                continue
+            for i, n in enumerate(names):
+                if len(r) > 5 + i and r[5 + i].lower() == "active":
+                    reasons.add(n)
+        loaded = [c for c, p in zip(sm, power) if p > 200.0] or sm
+        return {"sm_mhz": statistics.median(loaded) if loaded else None,
+                "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm),
+                "power_w_max": max(power) if power else None}
+
+
+# ----------------------------------------------------------------------------------
+# reference arm and CPU baseline (the oracle port on host cores)
+# ----------------------------------------------------------------------------------
+
+def cpu_baseline_sample(steps=1, heads=1, threads=None):
+    """Times the oracle double backward on `heads` heads of the workload (fp32, CPU).
+
+    Each step: torch double autograd of naive attention (forward, backward and
+    backward-of-backward of B1 H`heads` S2048 D64 causal). Credited FLOPs are those
+    of the sampled heads' double backward only, so the rate is comparable with
+    the GPU's.
+    """
+    from oracle import attention_oracle as ora
+
+    threads = threads or os.cpu_count()
+    torch.set_num_threads(threads)
+    x = ora.make_inputs(1, heads, S, S, D, seed=0, dtype=torch.float32)
+    args = [x[n] for n in ("q", "k", "v", "do", "ddq", "ddk", "ddv")]
+    times = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        ora.autograd_all(*args, scale=SCALE, causal=CAUSAL)
+        times.append(time.perf_counter() - t0)
+    t = statistics.median(times)
+    value = credited_flops(1, heads, S) / t / 1e12
+    return {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "sample": f"{heads} of {B * H} heads of the workload per step (B1 H{heads} S{S} D{D} causal fp32, "
+                      f"torch double autograd of naive attention), median of {steps}"}, t
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    for _ in range(args.warmup):
+        cpu_baseline_sample(steps=1)
+    t0 = time.perf_counter()
+    base, _ = cpu_baseline_sample(steps=args.steps)
+    wall = time.perf_counter() - t0
+    n = args.gpus
+    line = {
+        "impl": "reference", "metric": METRIC, "value": base["value"], "unit": "TFLOP/s", "n_gpus": n,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * wall / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"bwdbwd causal B{B} H{H} S{S} D{D} per GPU (sampled: 1 head per step)",
+                   "reference_path": "oracle port: torch CPU double autograd (reference XLA CPU path needs JAX, "
+                                     "absent)"},
+        "cpu_baseline": base,
+        "e2e": {"value": base["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ----------------------------------------------------------------------------------
+# our arm
+# ----------------------------------------------------------------------------------
+
+def make_set(seed, device):
+    from flash_hog_b200 import MaskType
+    from flash_hog_b200 import _attention_impl as impl
+    from oracle.attention_oracle import make_inputs
+
+    x = make_inputs(B, H, S, S, D, seed=seed)
+    g = {k: v.to(device) for k, v in x.items()}
+    o, lse = impl.cuda_dot_product_attention(g["q"], g["k"], g["v"], MaskType.CAUSAL, SCALE, return_residual=True)
+    g["o"], g["lse"] = o, lse
+    return g
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--skip-e2e", action="store_true")
+    ap.add_argument("--skip-cpu", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+
+    from flash_hog_b200 import _capi
+    from flash_hog_b200 import flash_bwdbwd, MaskType
+
+    # Rank r holds batch rows [4r, 4r+4) of the global batch: distinct seeds.
+    sets = [make_set(1000 * rank + i, dev) for i in range(N_SETS)]
+    stats = torch.empty((N_SETS, 3, B, H, S), dtype=torch.float32, device=dev)
+    outs = [(torch.empty_like(s["q"]), torch.empty_like(s["q"]), torch.empty_like(s["k"]), torch.empty_like(s["k"]))
+            for s in sets]
+
+    def launch(i, ev=None):
+        s, (dq2, ddo, dk2, dv2), st = sets[i], outs[i], stats[i]
+        if ev is not None:
+            ev[0].record()
+        _capi.attn_rowdot(s["o"], s["do"], st[0])
+        if ev is not None:
+            ev[1].record()
+        _capi.attn_bwdbwd_pass(s["q"], s["k"], s["v"], s["do"], s["ddq"], s["ddk"], s["ddv"], s["lse"], st[0],
+                               dq2, ddo, dk2, dv2, st[1], st[2], SCALE, CAUSAL, _capi.PASS_QUERY)
+        if ev is not None:
+            ev[2].record()
+        _capi.attn_bwdbwd_pass(s["q"], s["k"], s["v"], s["do"], s["ddq"], s["ddk"], s["ddv"], s["lse"], st[0],
+                               dq2, ddo, dk2, dv2, st[1], st[2], SCALE, CAUSAL, _capi.PASS_KEY)
+        if ev is not None:
+            ev[3].record()
+
+    def barrier():
+        if dist is not None:
+            dist.barrier(device_ids=[local])
+
+    for i in range(args.warmup):
+        launch(i % N_SETS)
+    torch.cuda.synchronize()
+    if _capi.device_status() != 0:
+        raise RuntimeError("device-side error during warm-up")
+
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(list(range(world)) if rank == 0 else []) as clocks:
+        barrier()
+        torch.cuda.synchronize()
+        start.record()
+        for i in range(args.steps):
+            launch(i % N_SETS, evs[i])
+        stop.record()
+        torch.cuda.synchronize()
+        barrier()
+    if _capi.device_status() != 0:
+        raise RuntimeError("device-side error during the timed region")
+    ms = start.elapsed_time(stop) / args.steps
+    t_rowdot = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
+    t_q = statistics.mean(e[1].elapsed_time(e[2]) for e in evs)
+    t_k = statistics.mean(e[2].elapsed_time(e[3]) for e in evs)
+    if dist is not None:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+
+    # end to end through the public API, host buffers, copies inside the timed region
+    e2e = None
+    if not args.skip_e2e:
+        host = {k: v.cpu().pin_memory() for k, v in sets[0].items()}
+        names = ("q", "k", "v", "o", "do", "ddq", "ddk", "ddv", "lse")
+        h2d = sum(host[n].numel() * host[n].element_size() for n in names)
+        res_host = [torch.empty(host["q"].shape, dtype=torch.bfloat16).pin_memory() for _ in range(2)] + \
+                   [torch.empty(host["k"].shape, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+        d2h = sum(t.numel() * t.element_size() for t in res_host)
+
+        def e2e_step():
+            d = {n: host[n].to(dev, non_blocking=True) for n in names}
+            r = flash_bwdbwd(d["q"], d["k"], d["v"], d["o"], d["do"], d["ddq"], d["ddk"], d["ddv"], d["lse"],
+                             mask_type=MaskType.CAUSAL, scale=SCALE)
+            for dst, src in zip(res_host, r):
+                dst.copy_(src, non_blocking=True)
+
+        for _ in range(3):
+            e2e_step()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n_e2e = max(3, min(args.steps, 20))
+        barrier()
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(n_e2e):
+            e2e_step()
+        e1.record()
+        torch.cuda.synchronize()
+        barrier()
+        e2e_ms = e0.elapsed_time(e1) / n_e2e
+        if dist is not None:
+            t = torch.tensor([e2e_ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e2e_ms = float(t.item())
+        e2e = {"value": world * credited_flops(B, H, S) / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
+               "api": "flash_hog_b200.flash_bwdbwd"}
+
+    if dist is not None:
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+
+    peaks, peak_kind = load_peaks()
+    flops_q = credited_flops(B, H, S, gemms=14)
+    achieved = flops_q / (t_q * 1e-3) / 1e12
+    roofline = {"bound": "tensor", "kernel": "bwdbwd_q_kernel (query-tiled pass, 14 of 22 GEMM-eq)",
+                "achieved": achieved, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                "frac": achieved / peaks["bf16_tflops"], "peak_source": f"{peak_kind} bf16 dense (burst)",
+                "traffic": None,
+                "per_launch_ms": {"rowdot": t_rowdot, "query_pass": t_q, "key_pass": t_k},
+                "key_pass": {"achieved": credited_flops(B, H, S, gemms=8) / (t_k * 1e-3) / 1e12}}
+    cpu = None
+    if not args.skip_cpu:
+        cpu, _ = cpu_baseline_sample(steps=1, heads=4)
+    value = world * credited_flops(B, H, S) / (ms * 1e-3) / 1e12
+    line = {
+        "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"bwdbwd causal B{B} H{H} S{S} D{D} per GPU", "global_batch": B * world,
+                   "heads": H, "seq_len": S, "head_dim": D, "causal": True,
+                   "parallelism": f"dp{world} (batch x heads sharded, no collective)",
+                   "l2": f"{N_SETS} rotating input sets of ~136 MB each (> 126 MB L2)",
+                   "credited_gflop_per_step_per_gpu": credited_flops(B, H, S) / 1e9},
+        "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks.summary(),
+        "gpu_launches": 3 * args.steps,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

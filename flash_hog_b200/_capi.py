@@ -1,0 +1,203 @@
+"""ctypes binding of the C ABI in ``include/flash_hog_b200.h``.
+
+This is the counterpart of the reference's plugin loader
+(``flash_hog/jax/_tk_gpu.py:30-58``): it loads the in-tree shared library with
+ctypes (``FLASH_HOG_B200_LIB`` overrides the path, as ``FLASH_HOG_TK_LIB``
+does there) and exposes one thin wrapper per entry point taking torch CUDA
+tensors. There is no fallback: if the library is missing or a call fails, an
+exception is raised.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import functools
+import os
+
+import torch
+
+_LIB_ENV = "FLASH_HOG_B200_LIB"
+_LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libflashhog_b200.so")
+
+FH_OK = 0
+STATUS_NAMES = {
+    0: "FH_OK",
+    1: "FH_ERR_INVALID_ARGUMENT",
+    2: "FH_ERR_UNSUPPORTED",
+    3: "FH_ERR_LAUNCH",
+    4: "FH_ERR_DEVICE",
+    5: "FH_ERR_INJECTED",
+    6: "FH_ERR_NO_DEVICE",
+}
+
+# Every symbol include/flash_hog_b200.h declares.
+EXPORTED_SYMBOLS = (
+    "fh_attn_fwd",
+    "fh_attn_rowdot",
+    "fh_attn_bwd",
+    "fh_attn_bwdbwd",
+    "fh_attn_bwdbwd_pass",
+    "fh_device_status",
+    "fh_status_string",
+    "fh_last_error",
+    "fh_abi_version",
+)
+ABI_VERSION = 1
+
+
+class FlashHogError(RuntimeError):
+    """A C ABI call returned a non-zero status."""
+
+    def __init__(self, entry: str, status: int, message: str):
+        super().__init__(f"{entry}: {STATUS_NAMES.get(status, status)} ({message})")
+        self.entry = entry
+        self.status = status
+
+
+class FhStrides(ctypes.Structure):
+    _fields_ = [("batch", ctypes.c_int64), ("seq", ctypes.c_int64), ("head", ctypes.c_int64)]
+
+
+class FhAttnDims(ctypes.Structure):
+    _fields_ = [
+        ("batch", ctypes.c_int32),
+        ("heads", ctypes.c_int32),
+        ("seq_q", ctypes.c_int32),
+        ("seq_k", ctypes.c_int32),
+        ("head_dim", ctypes.c_int32),
+        ("q", FhStrides),
+        ("k", FhStrides),
+    ]
+
+
+def library_path() -> str:
+    return os.environ.get(_LIB_ENV) or _LIB_PATH
+
+
+@functools.cache
+def lib() -> ctypes.CDLL:
+    path = library_path()
+    if not os.path.exists(path):
+        raise RuntimeError(
+            f"flash_hog_b200 CUDA library not found at {path}; build it with `python -m flash_hog_b200.build`")
+    h = ctypes.CDLL(path)
+    vp, i32, f32 = ctypes.c_void_p, ctypes.c_int, ctypes.c_float
+    dims = ctypes.POINTER(FhAttnDims)
+    h.fh_attn_fwd.argtypes = [vp, dims, vp, vp, vp, vp, vp, f32, i32]
+    h.fh_attn_rowdot.argtypes = [vp, dims, vp, vp, vp]
+    h.fh_attn_bwd.argtypes = [vp, dims, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, f32, i32]
+    h.fh_attn_bwdbwd.argtypes = [vp, dims] + [vp] * 15 + [f32, i32]
+    h.fh_attn_bwdbwd_pass.argtypes = [vp, dims] + [vp] * 15 + [f32, i32, i32]
+    h.fh_device_status.argtypes = [vp, ctypes.POINTER(ctypes.c_int)]
+    h.fh_status_string.argtypes = [i32]
+    h.fh_status_string.restype = ctypes.c_char_p
+    h.fh_abi_version.argtypes = []
+    h.fh_last_error.argtypes = []
+    h.fh_last_error.restype = ctypes.c_char_p
+    for name in ("fh_attn_fwd", "fh_attn_rowdot", "fh_attn_bwd", "fh_attn_bwdbwd", "fh_attn_bwdbwd_pass",
+                 "fh_device_status", "fh_abi_version"):
+        getattr(h, name).restype = i32
+    if h.fh_abi_version() != ABI_VERSION:
+        raise RuntimeError(f"flash_hog_b200 ABI mismatch: library {h.fh_abi_version()}, binding {ABI_VERSION}")
+    return h
+
+
+def _check(entry: str, rc: int) -> None:
+    if rc != FH_OK:
+        detail = lib().fh_last_error().decode()
+        msg = lib().fh_status_string(rc).decode() + (f": {detail}" if detail else "")
+        raise FlashHogError(entry, rc, msg)
+
+
+def _ptr(t):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else ctypes.c_void_p(0)
+
+
+def _stream(device) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _strides(t: torch.Tensor) -> FhStrides:
+    """(batch, seq, head) element strides; a size-1 dimension is never stepped
+    over, so its stride is normalised (torch leaves it arbitrary)."""
+    (sb, st, sh, sd), (b, tq, h, d) = t.stride(), t.shape
+    if sd != 1 and d > 1:
+        raise ValueError("head_dim must be the contiguous dimension")
+    return FhStrides(sb if b > 1 else 0, st if tq > 1 else 8, sh if h > 1 else 0)
+
+
+def _layout_key(t: torch.Tensor):
+    s = _strides(t)
+    return tuple(t.shape), (s.batch, s.seq, s.head)
+
+
+def make_dims(q: torch.Tensor, k: torch.Tensor) -> FhAttnDims:
+    """Dims for BTNH tensors: q (B, Tq, H, D), k (B, Tk, H, D)."""
+    b, tq, h, d = q.shape
+    tk = k.shape[1]
+    return FhAttnDims(b, h, tq, tk, d, _strides(q), _strides(k))
+
+
+def _same_layout(ref: torch.Tensor, *others: torch.Tensor) -> None:
+    for t in others:
+        if _layout_key(t) != _layout_key(ref):
+            raise ValueError("tensors of one side must share shape and strides")
+        if t.dtype != torch.bfloat16 or t.device != ref.device:
+            raise ValueError("tensors must be bf16 on the same CUDA device")
+
+
+def attn_fwd(q, k, v, out, lse, scale: float, causal: bool) -> None:
+    _same_layout(q, out)
+    _same_layout(k, v)
+    dims = make_dims(q, k)
+    _check("fh_attn_fwd", lib().fh_attn_fwd(_stream(q.device), ctypes.byref(dims), _ptr(q), _ptr(k), _ptr(v),
+                                           _ptr(out), _ptr(lse), float(scale), int(causal)))
+
+
+def attn_rowdot(o, dO, delta) -> None:
+    _same_layout(o, dO)
+    dims = make_dims(o, o)
+    _check("fh_attn_rowdot", lib().fh_attn_rowdot(_stream(o.device), ctypes.byref(dims), _ptr(o), _ptr(dO),
+                                                 _ptr(delta)))
+
+
+def attn_bwd(q, k, v, o, dO, lse, dq, dk, dv, delta, scale: float, causal: bool) -> None:
+    _same_layout(q, o, dO, dq)
+    _same_layout(k, v, dk, dv)
+    dims = make_dims(q, k)
+    _check("fh_attn_bwd", lib().fh_attn_bwd(_stream(q.device), ctypes.byref(dims), _ptr(q), _ptr(k), _ptr(v),
+                                           _ptr(o), _ptr(dO), _ptr(lse), _ptr(dq), _ptr(dk), _ptr(dv),
+                                           _ptr(delta), float(scale), int(causal)))
+
+
+def attn_bwdbwd(q, k, v, dO, ddq, ddk, ddv, lse, delta, dq2, ddo, dk2, dv2, dd, bvec, scale: float,
+                causal: bool) -> None:
+    _same_layout(q, dO, ddq, dq2, ddo)
+    _same_layout(k, v, ddk, ddv, dk2, dv2)
+    dims = make_dims(q, k)
+    _check("fh_attn_bwdbwd", lib().fh_attn_bwdbwd(
+        _stream(q.device), ctypes.byref(dims), _ptr(q), _ptr(k), _ptr(v), _ptr(dO), _ptr(ddq), _ptr(ddk),
+        _ptr(ddv), _ptr(lse), _ptr(delta), _ptr(dq2), _ptr(ddo), _ptr(dk2), _ptr(dv2), _ptr(dd), _ptr(bvec),
+        float(scale), int(causal)))
+
+
+PASS_QUERY, PASS_KEY = 1, 2
+
+
+def attn_bwdbwd_pass(q, k, v, dO, ddq, ddk, ddv, lse, delta, dq2, ddo, dk2, dv2, dd, bvec, scale: float,
+                     causal: bool, which: int) -> None:
+    """One pass of the double backward (PASS_QUERY, PASS_KEY or both)."""
+    _same_layout(q, dO, ddq, dq2, ddo)
+    _same_layout(k, v, ddk, ddv, dk2, dv2)
+    dims = make_dims(q, k)
+    _check("fh_attn_bwdbwd_pass", lib().fh_attn_bwdbwd_pass(
+        _stream(q.device), ctypes.byref(dims), _ptr(q), _ptr(k), _ptr(v), _ptr(dO), _ptr(ddq), _ptr(ddk),
+        _ptr(ddv), _ptr(lse), _ptr(delta), _ptr(dq2), _ptr(ddo), _ptr(dk2), _ptr(dv2), _ptr(dd), _ptr(bvec),
+        float(scale), int(causal), int(which)))
+
+
+def device_status(device=None) -> int:
+    """Synchronises the current stream and returns (and clears) the device error code."""
+    code = ctypes.c_int(0)
+    lib().fh_device_status(_stream(device), ctypes.byref(code))
+    return int(code.value)

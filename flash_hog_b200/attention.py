@@ -1,0 +1,79 @@
+"""Public attention API with higher-order gradients on B200.
+
+Mirrors ``flash_hog/jax/attention.py``: ``dot_product_attention(query, key,
+value, is_causal=False, scale=None)`` on BTNH (or unbatched TNH) tensors. The
+reference nests two ``jax.custom_vjp``s so that differentiating the backward
+reaches a dedicated double-backward rule (``attention.py:52-60, 100-130``);
+here the same nesting is two ``torch.autograd.Function``s:
+
+* ``_DotProductAttention`` -- forward saves ``(q, k, v, L, O)``; its backward
+  calls ``_DotProductAttentionBwd`` (``attention.py:64-72``);
+* ``_DotProductAttentionBwd`` -- forward is the first-order backward and saves
+  ``(q, k, v, O, L, dO)`` (``attention.py:110-116``); its backward is the
+  double backward (``attention.py:119-125``).
+
+So ``torch.autograd.grad(..., create_graph=True)`` followed by a second
+``grad`` (grad-of-grad, Hessian-vector products) runs fwd -> bwd -> bwdbwd on
+the sm_100a kernels, as nested ``jax.grad`` does in the reference.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from flash_hog_b200 import _attention_impl as attn_impl
+from flash_hog_b200._attention_impl import MaskType
+
+
+def dot_product_attention(query, key, value, is_causal: bool = False, scale: float | None = None):
+    """softmax(scale * query key^T [+ causal mask]) value.
+
+    Dimensions: T query length, S key/value length, N heads, H head dim.
+    query (B, T, N, H) or (T, N H); key, value (B, S, N, H) or (S, N, H).
+    """
+    if scale is None:
+        scale = query.shape[-1] ** -0.5
+    if not (query.dtype == key.dtype == value.dtype):
+        raise TypeError("query, key and value must share a dtype")
+    mask_type = MaskType.CAUSAL if is_causal else MaskType.NO_MASK
+    unbatched = query.ndim == 3
+    if unbatched:
+        query, key, value = query.unsqueeze(0), key.unsqueeze(0), value.unsqueeze(0)
+    result = _DotProductAttention.apply(query, key, value, mask_type, float(scale))
+    if unbatched:
+        result = result.squeeze(0)
+    return result
+
+
+class _DotProductAttention(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, query, key, value, mask_type, scale):
+        out, activation = attn_impl.cuda_dot_product_attention(query, key, value, mask_type=mask_type, scale=scale,
+                                                               return_residual=True)
+        ctx.save_for_backward(query, key, value, activation, out)
+        ctx.mask_type, ctx.scale = mask_type, scale
+        return out
+
+    @staticmethod
+    def backward(ctx, g):
+        query, key, value, activation, out = ctx.saved_tensors
+        dq, dk, dv = _DotProductAttentionBwd.apply(query, key, value, activation, out, g, ctx.mask_type, ctx.scale)
+        return dq, dk, dv, None, None
+
+
+class _DotProductAttentionBwd(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, query, key, value, activation, out, g, mask_type, scale):
+        (dq, dk, dv), residual = attn_impl.dot_product_attention_bwd_rule_fwd_rule(
+            mask_type=mask_type, scale=scale, res=(query, key, value, activation, out), g=g)
+        ctx.save_for_backward(*residual)
+        ctx.mask_type, ctx.scale = mask_type, scale
+        return dq, dk, dv
+
+    @staticmethod
+    def backward(ctx, ddq, ddk, ddv):
+        res = ctx.saved_tensors
+        zeros = [torch.zeros_like(t) if c is None else c for c, t in zip((ddq, ddk, ddv), res[:3])]
+        (dq2, dk2, dv2, _, _), ddo = attn_impl.dot_product_attention_bwd_rule_bwd_rule(
+            mask_type=ctx.mask_type, scale=ctx.scale, res=res, g=tuple(zeros))
+        return dq2, dk2, dv2, None, None, ddo, None, None

@@ -1,0 +1,72 @@
+"""``flash_bwdbwd``: the attention double backward on the GPU.
+
+Mirrors the reference's double-backward entry points
+``flash_hog/jax/_pallas_gpu.py:51-114`` (``flash_bwdbwd``) and
+``flash_hog/jax/_tk_gpu.py:83-103`` (the native-plugin variant): same
+arguments, same return order ``(dQ2, dK2, dV2, ddO)``, unbatched (T, N, H)
+inputs accepted by adding a batch dimension (``_pallas_gpu.py:65-68``), and
+D = rowsum(dO o O) computed on the device before the kernels (``_tk_gpu.py:93``).
+
+Unlike the reference's TK path there is no per-call fallback and no gate on
+GPU generation: every call runs the sm_100a kernels or raises.
+"""
+
+from __future__ import annotations
+
+import dataclasses
+
+import torch
+
+from flash_hog_b200 import _capi
+from flash_hog_b200._attention_impl import MaskType, _bf16, _is_causal
+
+
+@dataclasses.dataclass(frozen=True)
+class TuningConfig:
+    """Accepted for signature compatibility with ``_pallas_gpu_kernel.py:22-29``.
+
+    Tile shapes are fixed by the sm_100a kernels (128 resident rows x 64
+    streamed rows); the fields are ignored.
+    """
+
+    tile_q: int = 128
+    tile_k: int = 64
+    max_concurrent_steps: int = 3
+    epilogue_tile_n: int = 64
+    grid_minor_dim: int = 0
+    grid_tile_width: int = 1
+
+
+def flash_bwdbwd(Q, K, V, O, dO, ddQ, ddK, ddV, L, mask_type: MaskType = MaskType.NO_MASK, scale=None,
+                 config: TuningConfig | None = None, return_stats: bool = False):
+    """Double backward of attention; BTNH in, ``(dQ2, dK2, dV2, ddO)`` out.
+
+    ``L`` is the forward log-sum-exp, (B, N, T) fp32 (natural log). Outputs
+    have the input dtype. With ``return_stats`` also returns the fp32 row
+    statistics ``(D, dD, B)``, each (B, N, T).
+    """
+    if Q.ndim == 3:
+        batched = [x.unsqueeze(0) for x in (Q, K, V, O, dO, ddQ, ddK, ddV, L)]
+        res = flash_bwdbwd(*batched, mask_type=mask_type, scale=scale, config=config, return_stats=return_stats)
+        outs = tuple(x.squeeze(0) for x in res[0]) if return_stats else tuple(x.squeeze(0) for x in res)
+        if return_stats:
+            return outs, tuple(x.squeeze(0) for x in res[1])
+        return outs
+    if scale is None:
+        scale = Q.shape[-1] ** -0.5
+    if Q.shape[2] != K.shape[2]:
+        raise NotImplementedError("grouped-query attention (q_heads != kv_heads) is not supported yet")
+    causal = _is_causal(mask_type)
+    q, k, v, o, do, ddq, ddk, ddv = (_bf16(x) for x in (Q, K, V, O, dO, ddQ, ddK, ddV))
+    b, t, n, _ = q.shape
+    lse = L.reshape(b, n, t).float().contiguous()
+    stats = torch.empty((3, b, n, t), dtype=torch.float32, device=q.device)
+    delta, dd, bvec = stats[0], stats[1], stats[2]
+    _capi.attn_rowdot(o, do, delta)
+    dq2, ddo = torch.empty_like(q), torch.empty_like(q)
+    dk2, dv2 = torch.empty_like(k), torch.empty_like(k)
+    _capi.attn_bwdbwd(q, k, v, do, ddq, ddk, ddv, lse, delta, dq2, ddo, dk2, dv2, dd, bvec, scale, causal)
+    outs = (dq2.to(Q.dtype), dk2.to(K.dtype), dv2.to(V.dtype), ddo.to(dO.dtype))
+    if return_stats:
+        return outs, (delta, dd, bvec)
+    return outs

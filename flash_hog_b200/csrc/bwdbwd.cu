@@ -1,0 +1,611 @@
+// Attention double backward (vjp of the attention vjp) on sm_100a.
+//
+// Two launches, no atomics, no (Nq, Nk) intermediate in global memory:
+//
+//  * query-tiled pass (`bwdbwd_q_kernel`): one CTA per 128 query rows of one
+//    (batch, head). It streams the key side (K, V, ddK, ddV) twice. The first
+//    sweep forms the row statistics
+//        dD = rowsum(ddS o P),  r1 = rowsum(dO ddV^T o P),  r2 = rowsum(dP o P),
+//        r3 = rowsum(dP o ddS o P),  B = r1 - dD r2 - D dD + r3,
+//    the second forms dS, dS2, ddP and P and accumulates
+//        dQ' = dS ddK + dS2 K,   ddO = ddP V + P ddV.
+//    dD and B are written to caller-provided scratch for the second pass.
+//    (Stats sweep merged as in flash_hog/csrc/tk_bwdbwd/stage1.cuh:187-195,231-237;
+//    per-element formulas of flash_hog/jax/_pallas_gpu_kernel.py:149-278.)
+//  * key-tiled pass (`bwdbwd_k_kernel`): one CTA per 128 key rows. It works on
+//    transposed scores (S^T = K Q^T, as flash_hog/csrc/tk_bwdbwd/stage2.cuh:172-178)
+//    so each thread owns a key row, streams the query side with its per-query
+//    statistics (L, D, dD, B) and accumulates
+//        dK' = dS^T ddQ + dS2^T Q,   dV' = ddP^T dO
+//    (flash_hog/jax/_pallas_gpu_kernel.py:309-416).
+//
+// Per kept (q, k) pair the two passes issue 14 + 8 = 22 bf16 GEMM-equivalents on
+// the tensor cores (tcgen05.mma, fp32 accumulation in TMEM).
+
+#include <cuda_runtime.h>
+
+#include <cmath>
+
+#include "kernels.h"
+
+namespace fh {
+namespace {
+
+struct BBArgs {
+  AttnShape sh;
+  const float* lse;
+  const float* delta;
+  float* dd;
+  float* bv;
+  __nv_bfloat16* dq2;
+  __nv_bfloat16* ddo;
+  __nv_bfloat16* dk2;
+  __nv_bfloat16* dv2;
+  int* status;
+};
+
+// ----------------------------------------------------------------------------------
+// query-tiled pass
+// ----------------------------------------------------------------------------------
+
+template <int HD>
+struct QPass {
+  static constexpr int BN = 64;                 // key rows per streamed tile
+  static constexpr int ST = 3;                  // ring depth
+  static constexpr int RES = kBM * HD * 2;      // one resident bf16 tile
+  static constexpr int STR = BN * HD * 2;       // one streamed bf16 tile
+  static constexpr int SLOT = 4 * STR;          // K | V | ddK | ddV
+  static constexpr int OPS = kBM * BN * 2;      // one bf16 operand panel set (dS, dS2, ddP or P)
+  static constexpr int SMEM = 1024 + 3 * RES + ST * SLOT + 4 * OPS;
+  static constexpr int C_S = 0, C_DDS = BN, C_DP = 2 * BN, C_DPA = 3 * BN;
+  static constexpr int C_DQ = 4 * BN, C_DDO = 4 * BN + HD;
+  static constexpr int TMEM_COLS = 512;
+  static_assert(C_DDO + HD <= TMEM_COLS, "TMEM budget");
+  static_assert(SMEM <= 232448, "shared memory budget");
+};
+
+template <int HD>
+__global__ void __launch_bounds__(kThreads, 1)
+    bwdbwd_q_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
+                    const __grid_constant__ CUtensorMap tm_ddq, const __grid_constant__ CUtensorMap tm_k,
+                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_ddk,
+                    const __grid_constant__ CUtensorMap tm_ddv, const BBArgs a) {
+  using G = QPass<HD>;
+  constexpr int BN = G::BN, ST = G::ST;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = align1024(smem_raw);
+  uint8_t* s_q = sm;
+  uint8_t* s_do = s_q + G::RES;
+  uint8_t* s_ddq = s_do + G::RES;
+  uint8_t* s_ring = s_ddq + G::RES;
+  uint8_t* s_ops = s_ring + ST * G::SLOT;  // dS | dS2 | ddP | P
+  __shared__ uint64_t bar_res, bar_full[ST], bar_empty[ST];
+  __shared__ uint64_t bar_sc_full, bar_sc_empty, bar_ops_full, bar_ops_empty, bar_acc;
+  __shared__ uint32_t tmem_base;
+  __shared__ int abort_flag;
+
+  const AttnShape& sh = a.sh;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int h = blockIdx.x, b = blockIdx.y;
+  const int qt = gridDim.z - 1 - blockIdx.z;  // longest causal rows first
+  const int q0 = qt * kBM;
+  const int kv_end = sh.causal ? min(sh.Tk, q0 + kBM) : sh.Tk;
+  const int n = (kv_end + BN - 1) / BN;  // key tiles per sweep (>= 1)
+  const int total = 2 * n;
+
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    mbar_init(&bar_res, 1);
+    for (int s = 0; s < ST; ++s) {
+      mbar_init(&bar_full[s], 1);
+      mbar_init(&bar_empty[s], 1);
+    }
+    mbar_init(&bar_sc_full, 1);
+    mbar_init(&bar_sc_empty, kEwThreads);
+    mbar_init(&bar_ops_full, kEwThreads);
+    mbar_init(&bar_ops_empty, 1);
+    mbar_init(&bar_acc, 1);
+    mbar_fence_init();
+  }
+  if (warp == kWarpMma) tmem_alloc(&tmem_base, G::TMEM_COLS);
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base;
+
+  if (warp == kWarpProducer) {
+    // ------------------------------ TMA producer ------------------------------
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_q);
+      tma_prefetch_desc(&tm_k);
+      mbar_arrive_expect_tx(&bar_res, 3 * G::RES);
+      tma_rows<HD>(s_q, &tm_q, &bar_res, q0, kBM, h, b);
+      tma_rows<HD>(s_do, &tm_do, &bar_res, q0, kBM, h, b);
+      tma_rows<HD>(s_ddq, &tm_ddq, &bar_res, q0, kBM, h, b);
+      int issued = 0;
+      for (int it = 0; it < total; ++it) {
+        const int s = it % ST;
+        if (it >= ST && !mbar_wait(&bar_empty[s], ((it / ST) - 1) & 1, &abort_flag)) {
+          raise_error(a.status, &abort_flag, kDevTimeoutSlotEmpty);
+          break;
+        }
+        const int k0 = (it % n) * BN;
+        uint8_t* slot = s_ring + s * G::SLOT;
+        mbar_arrive_expect_tx(&bar_full[s], G::SLOT);
+        tma_rows<HD>(slot, &tm_k, &bar_full[s], k0, BN, h, b);
+        tma_rows<HD>(slot + G::STR, &tm_v, &bar_full[s], k0, BN, h, b);
+        tma_rows<HD>(slot + 2 * G::STR, &tm_ddk, &bar_full[s], k0, BN, h, b);
+        tma_rows<HD>(slot + 3 * G::STR, &tm_ddv, &bar_full[s], k0, BN, h, b);
+        issued = it + 1;
+      }
+      // Every issued copy must land before this CTA's shared memory is released.
+      bool drained = mbar_wait(&bar_res, 0, nullptr);
+      for (int it = issued > ST ? issued - ST : 0; it < issued; ++it)
+        drained &= mbar_wait(&bar_full[it % ST], (it / ST) & 1, nullptr);
+      if (!drained) raise_error(a.status, &abort_flag, kDevTimeoutDrain);
+    }
+  } else if (warp == kWarpMma) {
+    // ------------------------------ MMA issuer --------------------------------
+    if (lane == 0) {
+      const uint32_t id_sc = idesc_bf16_f32(kBM, BN, false, false);
+      const uint32_t id_out = idesc_bf16_f32(kBM, HD, false, true);
+      bool ok = mbar_wait(&bar_res, 0, &abort_flag);
+      if (!ok) raise_error(a.status, &abort_flag, kDevTimeoutTmaFull);
+      for (int it = 0; ok && it <= total; ++it) {
+        if (it < total) {
+          const int s = it % ST;
+          if (!mbar_wait(&bar_full[s], (it / ST) & 1, &abort_flag)) {
+            raise_error(a.status, &abort_flag, kDevTimeoutTmaFull);
+            ok = false;
+            break;
+          }
+          if (it > 0 && !mbar_wait(&bar_sc_empty, (it - 1) & 1, &abort_flag)) {
+            raise_error(a.status, &abort_flag, kDevTimeoutEpilogue);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint8_t* slot = s_ring + s * G::SLOT;
+          gemm_abt(tmem + G::C_S, s_q, slot, BN, HD / 16, id_sc, false);                    // S   = Q K^T
+          gemm_abt(tmem + G::C_DDS, s_ddq, slot, BN, HD / 16, id_sc, false);                // ddS = ddQ K^T
+          gemm_abt(tmem + G::C_DDS, s_q, slot + 2 * G::STR, BN, HD / 16, id_sc, true);      //     + Q ddK^T
+          gemm_abt(tmem + G::C_DP, s_do, slot + G::STR, BN, HD / 16, id_sc, false);         // dP  = dO V^T
+          gemm_abt(tmem + G::C_DPA, s_do, slot + 3 * G::STR, BN, HD / 16, id_sc, false);    // dPa = dO ddV^T
+          umma_commit(&bar_sc_full);
+          if (it < n) umma_commit(&bar_empty[s]);  // stats sweep: slot free once scored
+        }
+        const int jp = it - 1 - n;  // second-sweep tile whose operand panels are due
+        if (jp >= 0) {
+          if (!mbar_wait(&bar_ops_full, jp & 1, &abort_flag)) {
+            raise_error(a.status, &abort_flag, kDevTimeoutEpilogue);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const int sp = (it - 1) % ST;
+          const uint8_t* slot = s_ring + sp * G::SLOT;
+          const bool acc = jp > 0;
+          gemm_ab(tmem + G::C_DQ, s_ops, slot + 2 * G::STR, BN, BN / 16, id_out, acc);              // dQ' += dS ddK
+          gemm_ab(tmem + G::C_DQ, s_ops + G::OPS, slot, BN, BN / 16, id_out, true);               //      + dS2 K
+          gemm_ab(tmem + G::C_DDO, s_ops + 2 * G::OPS, slot + G::STR, BN, BN / 16, id_out, acc);  // ddO += ddP V
+          gemm_ab(tmem + G::C_DDO, s_ops + 3 * G::OPS, slot + 3 * G::STR, BN, BN / 16, id_out, true);  // + P ddV
+          umma_commit(&bar_ops_empty);
+          umma_commit(&bar_empty[sp]);
+        }
+      }
+      if (ok) umma_commit(&bar_acc);
+    }
+  } else {
+    // --------------------------- elementwise warps ----------------------------
+    const int r = threadIdx.x;  // TMEM lane = query row inside the tile
+    const int row = q0 + r;
+    const bool row_ok = row < sh.Tq;
+    const size_t vi = stat_index(b, h, row_ok ? row : 0, sh.H, sh.Tq);
+    const float lg = row_ok ? a.lse[vi] * kLog2e : 0.f;
+    const float dv = row_ok ? a.delta[vi] : 0.f;
+    const float sc = sh.scale, sc2 = sh.scale * kLog2e;
+    float dD = 0.f, r1 = 0.f, r2 = 0.f, r3 = 0.f, Bv = 0.f;
+    bool ok = true;
+    for (int it = 0; it < total; ++it) {
+      const int j = it % n;
+      const bool sweep2 = it >= n;
+      const int k0 = j * BN;
+      ok = __all_sync(0xffffffffu, mbar_wait(&bar_sc_full, it & 1, &abort_flag));
+      if (ok && sweep2 && j > 0) ok = __all_sync(0xffffffffu, mbar_wait(&bar_ops_empty, (j - 1) & 1, &abort_flag));
+      if (!ok) break;
+      tc_fence_after();
+      const bool need_mask = (k0 + BN > sh.Tk) || (sh.causal && k0 + BN - 1 > q0);
+#pragma unroll 1
+      for (int c = 0; c < BN / 16; ++c) {
+        uint32_t vs[16], vdds[16], vdp[16], vdpa[16];
+        tmem_row16(tmem, warp, G::C_S + c * 16, vs);
+        tmem_row16(tmem, warp, G::C_DDS + c * 16, vdds);
+        tmem_row16(tmem, warp, G::C_DP + c * 16, vdp);
+        tmem_row16(tmem, warp, G::C_DPA + c * 16, vdpa);
+        tmem_wait_ld();
+        reg_fence16(vs);
+        reg_fence16(vdds);
+        reg_fence16(vdp);
+        reg_fence16(vdpa);
+        if (!sweep2) {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int key = k0 + c * 16 + i;
+            float s = fmaf(__uint_as_float(vs[i]), sc2, -lg);
+            if (need_mask && (key >= sh.Tk || (sh.causal && key > row))) s = -INFINITY;
+            const float p = ex2(s);
+            const float dds = __uint_as_float(vdds[i]) * sc;
+            const float dp = __uint_as_float(vdp[i]);
+            const float t = dds * p;
+            dD += t;
+            r3 = fmaf(t, dp, r3);
+            r1 = fmaf(__uint_as_float(vdpa[i]), p, r1);
+            r2 = fmaf(dp, p, r2);
+          }
+        } else {
+          float o_ds[16], o_ds2[16], o_ddp[16], o_p[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int key = k0 + c * 16 + i;
+            float s = fmaf(__uint_as_float(vs[i]), sc2, -lg);
+            if (need_mask && (key >= sh.Tk || (sh.causal && key > row))) s = -INFINITY;
+            const float p = ex2(s);
+            const float dds = __uint_as_float(vdds[i]) * sc;
+            const float dp = __uint_as_float(vdp[i]);
+            const float u = dds - dD;
+            const float ps = p * sc;
+            o_p[i] = p;
+            o_ddp[i] = p * u;
+            o_ds[i] = ps * (dp - dv);
+            const float dp2 = fmaf(-dds, dv, fmaf(dp, u, __uint_as_float(vdpa[i])));
+            o_ds2[i] = ps * (dp2 - Bv);
+          }
+          stage_bf16x16(s_ops, r, c, o_ds);
+          stage_bf16x16(s_ops + G::OPS, r, c, o_ds2);
+          stage_bf16x16(s_ops + 2 * G::OPS, r, c, o_ddp);
+          stage_bf16x16(s_ops + 3 * G::OPS, r, c, o_p);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&bar_sc_empty);
+      if (sweep2) {
+        fence_async_smem();
+        mbar_arrive(&bar_ops_full);
+      }
+      if (it == n - 1) Bv = r1 - dD * r2 - dv * dD + r3;
+    }
+    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&bar_acc, 0, &abort_flag));
+    if (ok) {
+      tc_fence_after();
+      const int srow = row_ok ? row : 0;
+      tmem_row_to_global<HD>(tmem, warp, G::C_DQ, a.dq2 + row_offset(sh.sq, b, srow, h), row_ok);
+      tmem_row_to_global<HD>(tmem, warp, G::C_DDO, a.ddo + row_offset(sh.sq, b, srow, h), row_ok);
+      if (row_ok) {
+        a.dd[vi] = dD;
+        a.bv[vi] = Bv;
+      }
+    } else if (threadIdx.x == 0) {
+      raise_error(a.status, &abort_flag, kDevTimeoutMma);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kWarpMma) tmem_dealloc(tmem, G::TMEM_COLS);
+}
+
+// ----------------------------------------------------------------------------------
+// key-tiled pass
+// ----------------------------------------------------------------------------------
+
+template <int HD>
+struct KPass {
+  static constexpr int BN = 64;                 // query rows per streamed tile
+  static constexpr int ST = 3;
+  static constexpr int RES = kBM * HD * 2;
+  static constexpr int STR = BN * HD * 2;
+  static constexpr int VEC = BN * 4;            // one fp32 statistic per streamed query
+  static constexpr int SLOT = 3 * STR + 4 * VEC;  // Q | dO | ddQ | L, D, dD, B
+  static constexpr int OPS = kBM * BN * 2;
+  static constexpr int SMEM = 1024 + 4 * RES + ST * SLOT + 3 * OPS;
+  static constexpr int C_S = 0, C_DDS = BN, C_DP = 2 * BN, C_DPA = 3 * BN;
+  static constexpr int C_DK = 4 * BN, C_DV = 4 * BN + HD;
+  static constexpr int TMEM_COLS = 512;
+  static_assert(SLOT % 1024 == 0, "slots must keep panels 1024-byte aligned");
+  static_assert(C_DV + HD <= TMEM_COLS, "TMEM budget");
+  static_assert(SMEM <= 232448, "shared memory budget");
+};
+
+template <int HD>
+__global__ void __launch_bounds__(kThreads, 1)
+    bwdbwd_k_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
+                    const __grid_constant__ CUtensorMap tm_ddk, const __grid_constant__ CUtensorMap tm_ddv,
+                    const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
+                    const __grid_constant__ CUtensorMap tm_ddq, const BBArgs a) {
+  using G = KPass<HD>;
+  constexpr int BN = G::BN, ST = G::ST;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = align1024(smem_raw);
+  uint8_t* s_k = sm;
+  uint8_t* s_v = s_k + G::RES;
+  uint8_t* s_ddk = s_v + G::RES;
+  uint8_t* s_ddv = s_ddk + G::RES;
+  uint8_t* s_ring = s_ddv + G::RES;
+  uint8_t* s_ops = s_ring + ST * G::SLOT;  // dS^T | dS2^T | ddP^T
+  __shared__ uint64_t bar_res, bar_full[ST], bar_empty[ST];
+  __shared__ uint64_t bar_sc_full, bar_sc_empty, bar_ops_full, bar_ops_empty, bar_acc;
+  __shared__ uint32_t tmem_base;
+  __shared__ int abort_flag;
+
+  const AttnShape& sh = a.sh;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int h = blockIdx.x, b = blockIdx.y;
+  const int kt = blockIdx.z;  // key tile 0 carries the most causal work
+  const int k0 = kt * kBM;
+  const int nq_tiles = (sh.Tq + BN - 1) / BN;
+  const int qt_begin = sh.causal ? k0 / BN : 0;
+  const int n = nq_tiles > qt_begin ? nq_tiles - qt_begin : 0;
+
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    mbar_init(&bar_res, 1);
+    for (int s = 0; s < ST; ++s) {
+      mbar_init(&bar_full[s], 1);
+      mbar_init(&bar_empty[s], 1);
+    }
+    mbar_init(&bar_sc_full, 1);
+    mbar_init(&bar_sc_empty, kEwThreads);
+    mbar_init(&bar_ops_full, kEwThreads);
+    mbar_init(&bar_ops_empty, 1);
+    mbar_init(&bar_acc, 1);
+    mbar_fence_init();
+  }
+  if (warp == kWarpMma) tmem_alloc(&tmem_base, G::TMEM_COLS);
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base;
+
+  if (warp == kWarpProducer) {
+    // ---------------------- TMA producer (whole warp) -----------------------
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_k);
+      tma_prefetch_desc(&tm_q);
+      mbar_arrive_expect_tx(&bar_res, 4 * G::RES);
+      tma_rows<HD>(s_k, &tm_k, &bar_res, k0, kBM, h, b);
+      tma_rows<HD>(s_v, &tm_v, &bar_res, k0, kBM, h, b);
+      tma_rows<HD>(s_ddk, &tm_ddk, &bar_res, k0, kBM, h, b);
+      tma_rows<HD>(s_ddv, &tm_ddv, &bar_res, k0, kBM, h, b);
+    }
+    int issued = 0;
+    for (int it = 0; it < n; ++it) {
+      const int s = it % ST;
+      const int q0 = (qt_begin + it) * BN;
+      // Per-query statistics of this tile (two rows per lane), fetched before
+      // waiting for the slot so their latency overlaps the wait.
+      float st[2][4];
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const int q = q0 + lane + 32 * k;
+        const bool v = q < sh.Tq;
+        const size_t idx = stat_index(b, h, v ? q : 0, sh.H, sh.Tq);
+        st[k][0] = v ? a.lse[idx] : 0.f;
+        st[k][1] = v ? a.delta[idx] : 0.f;
+        st[k][2] = v ? a.dd[idx] : 0.f;
+        st[k][3] = v ? a.bv[idx] : 0.f;
+      }
+      bool ok = true;
+      if (it >= ST) ok = mbar_wait(&bar_empty[s], ((it / ST) - 1) & 1, &abort_flag);
+      if (!__all_sync(0xffffffffu, ok)) {
+        if (lane == 0) raise_error(a.status, &abort_flag, kDevTimeoutSlotEmpty);
+        break;
+      }
+      uint8_t* slot = s_ring + s * G::SLOT;
+      float* sv = reinterpret_cast<float*>(slot + 3 * G::STR);
+#pragma unroll
+      for (int k = 0; k < 2; ++k)
+#pragma unroll
+        for (int m = 0; m < 4; ++m) sv[m * BN + lane + 32 * k] = st[k][m];
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&bar_full[s], 3 * G::STR);
+        tma_rows<HD>(slot, &tm_q, &bar_full[s], q0, BN, h, b);
+        tma_rows<HD>(slot + G::STR, &tm_do, &bar_full[s], q0, BN, h, b);
+        tma_rows<HD>(slot + 2 * G::STR, &tm_ddq, &bar_full[s], q0, BN, h, b);
+      }
+      __syncwarp();
+      issued = it + 1;
+    }
+    if (lane == 0) {
+      bool drained = mbar_wait(&bar_res, 0, nullptr);
+      for (int it = issued > ST ? issued - ST : 0; it < issued; ++it)
+        drained &= mbar_wait(&bar_full[it % ST], (it / ST) & 1, nullptr);
+      if (!drained) raise_error(a.status, &abort_flag, kDevTimeoutDrain);
+    }
+  } else if (warp == kWarpMma) {
+    // ------------------------------ MMA issuer --------------------------------
+    if (lane == 0 && n > 0) {
+      const uint32_t id_sc = idesc_bf16_f32(kBM, BN, false, false);
+      const uint32_t id_out = idesc_bf16_f32(kBM, HD, false, true);
+      bool ok = mbar_wait(&bar_res, 0, &abort_flag);
+      if (!ok) raise_error(a.status, &abort_flag, kDevTimeoutTmaFull);
+      for (int it = 0; ok && it <= n; ++it) {
+        if (it < n) {
+          const int s = it % ST;
+          if (!mbar_wait(&bar_full[s], (it / ST) & 1, &abort_flag)) {
+            raise_error(a.status, &abort_flag, kDevTimeoutTmaFull);
+            ok = false;
+            break;
+          }
+          if (it > 0 && !mbar_wait(&bar_sc_empty, (it - 1) & 1, &abort_flag)) {
+            raise_error(a.status, &abort_flag, kDevTimeoutEpilogue);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint8_t* slot = s_ring + s * G::SLOT;
+          gemm_abt(tmem + G::C_S, s_k, slot, BN, HD / 16, id_sc, false);                  // S^T   = K Q^T
+          gemm_abt(tmem + G::C_DDS, s_k, slot + 2 * G::STR, BN, HD / 16, id_sc, false);   // ddS^T = K ddQ^T
+          gemm_abt(tmem + G::C_DDS, s_ddk, slot, BN, HD / 16, id_sc, true);               //       + ddK Q^T
+          gemm_abt(tmem + G::C_DP, s_v, slot + G::STR, BN, HD / 16, id_sc, false);        // dP^T  = V dO^T
+          gemm_abt(tmem + G::C_DPA, s_ddv, slot + G::STR, BN, HD / 16, id_sc, false);     // dPa^T = ddV dO^T
+          umma_commit(&bar_sc_full);
+        }
+        const int jp = it - 1;
+        if (jp >= 0) {
+          if (!mbar_wait(&bar_ops_full, jp & 1, &abort_flag)) {
+            raise_error(a.status, &abort_flag, kDevTimeoutEpilogue);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const int sp = jp % ST;
+          const uint8_t* slot = s_ring + sp * G::SLOT;
+          const bool acc = jp > 0;
+          gemm_ab(tmem + G::C_DK, s_ops, slot + 2 * G::STR, BN, BN / 16, id_out, acc);            // dK' += dS^T ddQ
+          gemm_ab(tmem + G::C_DK, s_ops + G::OPS, slot, BN, BN / 16, id_out, true);             //      + dS2^T Q
+          gemm_ab(tmem + G::C_DV, s_ops + 2 * G::OPS, slot + G::STR, BN, BN / 16, id_out, acc);  // dV' += ddP^T dO
+          umma_commit(&bar_ops_empty);
+          umma_commit(&bar_empty[sp]);
+        }
+      }
+      if (ok) umma_commit(&bar_acc);
+    }
+  } else {
+    // --------------------------- elementwise warps ----------------------------
+    const int r = threadIdx.x;  // TMEM lane = key row inside the tile
+    const int key = k0 + r;
+    const bool key_ok = key < sh.Tk;
+    const float sc = sh.scale, sc2 = sh.scale * kLog2e;
+    bool ok = true;
+    for (int it = 0; it < n; ++it) {
+      const int s = it % ST;
+      const int q0 = (qt_begin + it) * BN;
+      ok = __all_sync(0xffffffffu, mbar_wait(&bar_sc_full, it & 1, &abort_flag));
+      if (ok && it > 0) ok = __all_sync(0xffffffffu, mbar_wait(&bar_ops_empty, (it - 1) & 1, &abort_flag));
+      if (!ok) break;
+      tc_fence_after();
+      const float* sv = reinterpret_cast<const float*>(s_ring + s * G::SLOT + 3 * G::STR);
+      const bool need_mask = (q0 + BN > sh.Tq) || (sh.causal && q0 < k0 + kBM - 1);
+#pragma unroll 1
+      for (int c = 0; c < BN / 16; ++c) {
+        uint32_t vs[16], vdds[16], vdp[16], vdpa[16];
+        tmem_row16(tmem, warp, G::C_S + c * 16, vs);
+        tmem_row16(tmem, warp, G::C_DDS + c * 16, vdds);
+        tmem_row16(tmem, warp, G::C_DP + c * 16, vdp);
+        tmem_row16(tmem, warp, G::C_DPA + c * 16, vdpa);
+        tmem_wait_ld();
+        reg_fence16(vs);
+        reg_fence16(vdds);
+        reg_fence16(vdp);
+        reg_fence16(vdpa);
+        float o_ds[16], o_ds2[16], o_ddp[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int col = c * 16 + i;
+          const int q = q0 + col;
+          const float lq = sv[col] * kLog2e;
+          const float dq = sv[BN + col];
+          const float ddq = sv[2 * BN + col];
+          const float bq = sv[3 * BN + col];
+          float s = fmaf(__uint_as_float(vs[i]), sc2, -lq);
+          if (need_mask && (q >= sh.Tq || (sh.causal && q < key))) s = -INFINITY;
+          const float p = ex2(s);
+          const float dds = __uint_as_float(vdds[i]) * sc;
+          const float dp = __uint_as_float(vdp[i]);
+          const float u = dds - ddq;
+          const float ps = p * sc;
+          o_ddp[i] = p * u;
+          o_ds[i] = ps * (dp - dq);
+          const float dp2 = fmaf(-dds, dq, fmaf(dp, u, __uint_as_float(vdpa[i])));
+          o_ds2[i] = ps * (dp2 - bq);
+        }
+        stage_bf16x16(s_ops, r, c, o_ds);
+        stage_bf16x16(s_ops + G::OPS, r, c, o_ds2);
+        stage_bf16x16(s_ops + 2 * G::OPS, r, c, o_ddp);
+      }
+      tc_fence_before();
+      mbar_arrive(&bar_sc_empty);
+      fence_async_smem();
+      mbar_arrive(&bar_ops_full);
+    }
+    const int skey = key_ok ? key : 0;
+    __nv_bfloat16* dk_row = a.dk2 + row_offset(sh.sk, b, skey, h);
+    __nv_bfloat16* dv_row = a.dv2 + row_offset(sh.sk, b, skey, h);
+    if (n == 0) {
+      // No query sees these keys (causal with Tk > Tq): the gradients are zero.
+      if (key_ok) {
+        zero_row_global<HD>(dk_row);
+        zero_row_global<HD>(dv_row);
+      }
+    } else {
+      if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&bar_acc, 0, &abort_flag));
+      if (ok) {
+        tc_fence_after();
+        tmem_row_to_global<HD>(tmem, warp, G::C_DK, dk_row, key_ok);
+        tmem_row_to_global<HD>(tmem, warp, G::C_DV, dv_row, key_ok);
+      } else if (threadIdx.x == 0) {
+        raise_error(a.status, &abort_flag, kDevTimeoutMma);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kWarpMma) tmem_dealloc(tmem, G::TMEM_COLS);
+}
+
+template <int HD>
+int launch_bwdbwd_hd(const AttnShape& s, const BwdBwdPtrs& p, int passes, int* status, cudaStream_t stream) {
+  using GQ = QPass<HD>;
+  using GK = KPass<HD>;
+  CUtensorMap mq[7], mk[7];
+  // Query-tiled pass: 128-row query tiles, 64-row key tiles.
+  bool ok = make_seq_map(&mq[0], p.q, HD, s.Tq, s.H, s.B, s.sq, kBM) &&
+            make_seq_map(&mq[1], p.dO, HD, s.Tq, s.H, s.B, s.sq, kBM) &&
+            make_seq_map(&mq[2], p.ddq, HD, s.Tq, s.H, s.B, s.sq, kBM) &&
+            make_seq_map(&mq[3], p.k, HD, s.Tk, s.H, s.B, s.sk, GQ::BN) &&
+            make_seq_map(&mq[4], p.v, HD, s.Tk, s.H, s.B, s.sk, GQ::BN) &&
+            make_seq_map(&mq[5], p.ddk, HD, s.Tk, s.H, s.B, s.sk, GQ::BN) &&
+            make_seq_map(&mq[6], p.ddv, HD, s.Tk, s.H, s.B, s.sk, GQ::BN);
+  // Key-tiled pass: 128-row key tiles, 64-row query tiles.
+  ok = ok && make_seq_map(&mk[0], p.k, HD, s.Tk, s.H, s.B, s.sk, kBM) &&
+       make_seq_map(&mk[1], p.v, HD, s.Tk, s.H, s.B, s.sk, kBM) &&
+       make_seq_map(&mk[2], p.ddk, HD, s.Tk, s.H, s.B, s.sk, kBM) &&
+       make_seq_map(&mk[3], p.ddv, HD, s.Tk, s.H, s.B, s.sk, kBM) &&
+       make_seq_map(&mk[4], p.q, HD, s.Tq, s.H, s.B, s.sq, GK::BN) &&
+       make_seq_map(&mk[5], p.dO, HD, s.Tq, s.H, s.B, s.sq, GK::BN) &&
+       make_seq_map(&mk[6], p.ddq, HD, s.Tq, s.H, s.B, s.sq, GK::BN);
+  if (!ok) return kInvalidArgument;
+  if (ensure_smem_limit(reinterpret_cast<const void*>(&bwdbwd_q_kernel<HD>), GQ::SMEM) != kOk ||
+      ensure_smem_limit(reinterpret_cast<const void*>(&bwdbwd_k_kernel<HD>), GK::SMEM) != kOk)
+    return kLaunchFailed;
+  BBArgs args{s,
+              p.lse,
+              p.delta,
+              p.dd,
+              p.bv,
+              static_cast<__nv_bfloat16*>(p.dq2),
+              static_cast<__nv_bfloat16*>(p.ddo),
+              static_cast<__nv_bfloat16*>(p.dk2),
+              static_cast<__nv_bfloat16*>(p.dv2),
+              status};
+  if (passes & kPassQuery) {
+    const dim3 gq(s.H, s.B, (s.Tq + kBM - 1) / kBM);
+    bwdbwd_q_kernel<HD><<<gq, kThreads, GQ::SMEM, stream>>>(mq[0], mq[1], mq[2], mq[3], mq[4], mq[5], mq[6], args);
+    if (cudaGetLastError() != cudaSuccess) return kLaunchFailed;
+  }
+  if (passes & kPassKey) {
+    const dim3 gk(s.H, s.B, (s.Tk + kBM - 1) / kBM);
+    bwdbwd_k_kernel<HD><<<gk, kThreads, GK::SMEM, stream>>>(mk[0], mk[1], mk[2], mk[3], mk[4], mk[5], mk[6], args);
+    if (cudaGetLastError() != cudaSuccess) return kLaunchFailed;
+  }
+  return kOk;
+}
+
+}  // namespace
+
+int launch_bwdbwd(const AttnShape& s, int hd, const BwdBwdPtrs& p, int passes, int* status, cudaStream_t stream) {
+  if (hd == 64) return launch_bwdbwd_hd<64>(s, p, passes, status, stream);
+  return kUnsupported;
+}
+
+}  // namespace fh

@@ -1,0 +1,277 @@
+// C ABI entry points (include/flash_hog_b200.h): argument validation, device
+// selection from the stream, per-device one-time set-up, host-side fault
+// injection, and dispatch to the kernel launchers.
+
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <set>
+#include <utility>
+
+#include "flash_hog_b200.h"
+#include "kernels.h"
+#include "tmap.h"
+
+namespace fh {
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+
+std::mutex g_mutex;
+thread_local char g_last_error[256] = "";
+
+// Records a detail message for fh_last_error() and returns `code`.
+int fail(int code, const char* what) {
+  std::snprintf(g_last_error, sizeof(g_last_error), "%s", what);
+  return code;
+}
+int* g_status_word[kMaxDevices] = {nullptr};
+std::set<std::pair<int, const void*>> g_smem_done;
+
+int current_device() {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) return -1;
+  return dev;
+}
+
+// Makes the stream's device current *and* binds its primary context to the
+// calling thread. Callers such as autograd worker threads may have a current
+// device in their own CUDA runtime without a driver context bound to the
+// thread; TMA descriptor encoding needs one (else CUDA_ERROR_INVALID_CONTEXT).
+int select_stream_device(cudaStream_t stream) {
+  int dev = current_device();
+  if (stream != nullptr) {
+    int sdev = -1;
+    if (cudaStreamGetDevice(stream, &sdev) == cudaSuccess) {
+      dev = sdev;
+    } else {
+      // Follow the CUDA convention that the stream belongs to the current device.
+      cudaGetLastError();
+    }
+  }
+  if (dev < 0) return fail(kNoDevice, "no current CUDA device");
+  if (cudaSetDevice(dev) != cudaSuccess) return fail(kNoDevice, "cudaSetDevice failed");
+  return kOk;
+}
+
+// Per-device status word (allocated once, zeroed).
+int* status_word() {
+  const int dev = current_device();
+  if (dev < 0 || dev >= kMaxDevices) return nullptr;
+  std::lock_guard<std::mutex> lock(g_mutex);
+  if (!g_status_word[dev]) {
+    int* p = nullptr;
+    if (cudaMalloc(&p, sizeof(int)) != cudaSuccess) return nullptr;
+    if (cudaMemset(p, 0, sizeof(int)) != cudaSuccess) return nullptr;
+    g_status_word[dev] = p;
+  }
+  return g_status_word[dev];
+}
+
+// FLASH_HOG_B200_INJECT_ERROR=<entry>[,<entry>...] or "all": the named entry
+// points return FH_ERR_INJECTED without launching anything. Host-side fault
+// injection for the callers' error paths; nothing reaches the GPU.
+bool injected(const char* entry) {
+  const char* env = std::getenv("FLASH_HOG_B200_INJECT_ERROR");
+  if (!env || !*env) return false;
+  if (std::strcmp(env, "all") == 0) return true;
+  const size_t n = std::strlen(entry);
+  for (const char* p = env; *p;) {
+    const char* e = std::strchr(p, ',');
+    const size_t len = e ? static_cast<size_t>(e - p) : std::strlen(p);
+    if (len == n && std::strncmp(p, entry, n) == 0) return true;
+    if (!e) break;
+    p = e + 1;
+  }
+  return false;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+bool strides_ok(const fh_strides& s) {
+  return s.batch >= 0 && s.seq > 0 && s.head >= 0 && s.batch % 8 == 0 && s.seq % 8 == 0 && s.head % 8 == 0;
+}
+
+int validate(const fh_attn_dims* d, AttnShape* out, float scale, int causal) {
+  g_last_error[0] = 0;
+  if (!d) return fail(kInvalidArgument, "dims is NULL");
+  if (d->batch < 1 || d->heads < 1 || d->seq_q < 1 || d->seq_k < 1)
+    return fail(kInvalidArgument, "batch, heads, seq_q and seq_k must be >= 1");
+  if (d->head_dim != 64) return fail(kUnsupported, "head_dim must be 64");
+  if (!strides_ok(d->q) || !strides_ok(d->k))
+    return fail(kInvalidArgument, "strides must be non-negative multiples of 8 elements (seq stride > 0)");
+  if (!(scale == scale)) return fail(kInvalidArgument, "scale is NaN");
+  out->B = d->batch;
+  out->H = d->heads;
+  out->Tq = d->seq_q;
+  out->Tk = d->seq_k;
+  out->sq = Strides3{d->q.batch, d->q.seq, d->q.head};
+  out->sk = Strides3{d->k.batch, d->k.seq, d->k.head};
+  out->scale = scale;
+  out->causal = causal ? 1 : 0;
+  return kOk;
+}
+
+constexpr const char* kAlignMsg = "a tensor pointer is NULL or not 16-byte aligned";
+
+template <typename... P>
+bool all_aligned(P... ptrs) {
+  return (... && (ptrs != nullptr && aligned16(ptrs)));
+}
+
+}  // namespace
+
+int ensure_smem_limit(const void* func, int bytes) {
+  const int dev = current_device();
+  std::lock_guard<std::mutex> lock(g_mutex);
+  auto key = std::make_pair(dev, func);
+  if (g_smem_done.count(key)) return kOk;
+  if (cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess)
+    return fail(kLaunchFailed, "cudaFuncSetAttribute(MaxDynamicSharedMemorySize) failed");
+  g_smem_done.insert(key);
+  return kOk;
+}
+
+bool make_seq_map(CUtensorMap* map, const void* base, int hd, int seq, int heads, int batch, const Strides3& st,
+                  int rows) {
+  const uint64_t dims[4] = {static_cast<uint64_t>(hd), static_cast<uint64_t>(seq), static_cast<uint64_t>(heads),
+                            static_cast<uint64_t>(batch)};
+  // Size-1 dimensions may carry any stride; give them a legal one.
+  const uint64_t sb = st.b > 0 ? st.b : 8, sh = st.h > 0 ? st.h : 8;
+  const uint64_t strides[3] = {static_cast<uint64_t>(st.t) * 2, sh * 2, sb * 2};
+  const uint32_t box[4] = {64, static_cast<uint32_t>(rows), 1, 1};
+  int cu = 0;
+  if (make_tmap_bf16(map, base, 4, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, &cu)) return true;
+  char msg[240];
+  std::snprintf(msg, sizeof(msg),
+                "cuTensorMapEncodeTiled failed (CUresult %d) for base %p dims {%llu,%llu,%llu,%llu} "
+                "strides {%llu,%llu,%llu} box rows %d",
+                cu, base, (unsigned long long)dims[0], (unsigned long long)dims[1], (unsigned long long)dims[2],
+                (unsigned long long)dims[3], (unsigned long long)strides[0], (unsigned long long)strides[1],
+                (unsigned long long)strides[2], rows);
+  fail(kInvalidArgument, msg);
+  return false;
+}
+
+}  // namespace fh
+
+using namespace fh;
+
+extern "C" {
+
+int fh_abi_version(void) { return FH_ABI_VERSION; }
+
+const char* fh_last_error(void) { return g_last_error; }
+
+const char* fh_status_string(int status) {
+  switch (status) {
+    case FH_OK: return "ok";
+    case FH_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case FH_ERR_UNSUPPORTED: return "unsupported configuration";
+    case FH_ERR_LAUNCH: return "kernel launch failed";
+    case FH_ERR_DEVICE: return "device-side error (bounded wait expired)";
+    case FH_ERR_INJECTED: return "injected error";
+    case FH_ERR_NO_DEVICE: return "no CUDA device";
+    default: return "unknown status";
+  }
+}
+
+int fh_attn_fwd(void* stream, const fh_attn_dims* dims, const void* q, const void* k, const void* v, void* o,
+                float* lse, float scale, int causal) {
+  if (injected("fh_attn_fwd")) return FH_ERR_INJECTED;
+  AttnShape s;
+  int rc = validate(dims, &s, scale, causal);
+  if (rc != kOk) return rc;
+  if (!all_aligned(q, k, v, o) || !lse) return fail(FH_ERR_INVALID_ARGUMENT, kAlignMsg);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if ((rc = select_stream_device(st)) != kOk) return rc;
+  int* status = status_word();
+  if (!status) return FH_ERR_NO_DEVICE;
+  return launch_fwd(s, dims->head_dim, FwdPtrs{q, k, v, o, lse}, status, st);
+}
+
+int fh_attn_rowdot(void* stream, const fh_attn_dims* dims, const void* o, const void* dO, float* delta) {
+  if (injected("fh_attn_rowdot")) return FH_ERR_INJECTED;
+  AttnShape s;
+  int rc = validate(dims, &s, 1.f, 0);
+  if (rc != kOk) return rc;
+  if (!all_aligned(o, dO) || !delta) return fail(FH_ERR_INVALID_ARGUMENT, kAlignMsg);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if ((rc = select_stream_device(st)) != kOk) return rc;
+  return launch_rowdot(s, dims->head_dim, o, dO, delta, st);
+}
+
+int fh_attn_bwd(void* stream, const fh_attn_dims* dims, const void* q, const void* k, const void* v, const void* o,
+                const void* dO, const float* lse, void* dq, void* dk, void* dv, float* delta, float scale,
+                int causal) {
+  if (injected("fh_attn_bwd")) return FH_ERR_INJECTED;
+  AttnShape s;
+  int rc = validate(dims, &s, scale, causal);
+  if (rc != kOk) return rc;
+  if (!all_aligned(q, k, v, o, dO, dq, dk, dv) || !lse || !delta) return fail(FH_ERR_INVALID_ARGUMENT, kAlignMsg);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if ((rc = select_stream_device(st)) != kOk) return rc;
+  int* status = status_word();
+  if (!status) return FH_ERR_NO_DEVICE;
+  return launch_bwd(s, dims->head_dim, BwdPtrs{q, k, v, o, dO, lse, dq, dk, dv, delta}, status, st);
+}
+
+static int bwdbwd_entry(const char* entry, void* stream, const fh_attn_dims* dims, const void* q, const void* k,
+                        const void* v, const void* dO, const void* ddq, const void* ddk, const void* ddv,
+                        const float* lse, const float* delta, void* dq2, void* ddo, void* dk2, void* dv2, float* dd,
+                        float* bvec, float scale, int causal, int passes) {
+  if (injected(entry)) return FH_ERR_INJECTED;
+  AttnShape s;
+  int rc = validate(dims, &s, scale, causal);
+  if (rc != kOk) return rc;
+  if (passes < 1 || passes > 3) return fail(FH_ERR_INVALID_ARGUMENT, "pass must be 1, 2 or 3");
+  if (!all_aligned(q, k, v, dO, ddq, ddk, ddv) || !lse || !delta || !dd || !bvec)
+    return fail(FH_ERR_INVALID_ARGUMENT, kAlignMsg);
+  if ((passes & kPassQuery) && !all_aligned(dq2, ddo)) return fail(FH_ERR_INVALID_ARGUMENT, kAlignMsg);
+  if ((passes & kPassKey) && !all_aligned(dk2, dv2)) return fail(FH_ERR_INVALID_ARGUMENT, kAlignMsg);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if ((rc = select_stream_device(st)) != kOk) return rc;
+  int* status = status_word();
+  if (!status) return FH_ERR_NO_DEVICE;
+  return launch_bwdbwd(s, dims->head_dim,
+                       BwdBwdPtrs{q, k, v, dO, ddq, ddk, ddv, lse, delta, dq2, ddo, dk2, dv2, dd, bvec}, passes,
+                       status, st);
+}
+
+int fh_attn_bwdbwd(void* stream, const fh_attn_dims* dims, const void* q, const void* k, const void* v,
+                   const void* dO, const void* ddq, const void* ddk, const void* ddv, const float* lse,
+                   const float* delta, void* dq2, void* ddo, void* dk2, void* dv2, float* dd, float* bvec,
+                   float scale, int causal) {
+  return bwdbwd_entry("fh_attn_bwdbwd", stream, dims, q, k, v, dO, ddq, ddk, ddv, lse, delta, dq2, ddo, dk2, dv2,
+                      dd, bvec, scale, causal, kPassQuery | kPassKey);
+}
+
+int fh_attn_bwdbwd_pass(void* stream, const fh_attn_dims* dims, const void* q, const void* k, const void* v,
+                        const void* dO, const void* ddq, const void* ddk, const void* ddv, const float* lse,
+                        const float* delta, void* dq2, void* ddo, void* dk2, void* dv2, float* dd, float* bvec,
+                        float scale, int causal, int pass) {
+  return bwdbwd_entry("fh_attn_bwdbwd_pass", stream, dims, q, k, v, dO, ddq, ddk, ddv, lse, delta, dq2, ddo, dk2,
+                      dv2, dd, bvec, scale, causal, pass);
+}
+
+int fh_device_status(void* stream, int* code) {
+  if (!code) return FH_ERR_INVALID_ARGUMENT;
+  *code = 0;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int rc = select_stream_device(st);
+  if (rc != kOk) return rc;
+  int* word = status_word();
+  if (!word) return FH_ERR_NO_DEVICE;
+  if (cudaStreamSynchronize(st) != cudaSuccess) return FH_ERR_LAUNCH;
+  int host = 0;
+  if (cudaMemcpy(&host, word, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return FH_ERR_LAUNCH;
+  if (host != 0 && cudaMemset(word, 0, sizeof(int)) != cudaSuccess) return FH_ERR_LAUNCH;
+  *code = host;
+  return host == 0 ? FH_OK : FH_ERR_DEVICE;
+}
+
+}  // extern "C"

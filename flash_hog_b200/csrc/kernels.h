@@ -1,0 +1,56 @@
+// Internal launch interface between the C ABI (capi.cu) and the kernels.
+
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include "attn_common.cuh"
+
+namespace fh {
+
+// Return codes shared with include/flash_hog_b200.h.
+enum HostStatus : int {
+  kOk = 0,
+  kInvalidArgument = 1,
+  kUnsupported = 2,
+  kLaunchFailed = 3,
+  kDeviceError = 4,
+  kInjected = 5,
+  kNoDevice = 6,
+};
+
+struct FwdPtrs {
+  const void *q, *k, *v;
+  void* o;
+  float* lse;
+};
+
+struct BwdPtrs {
+  const void *q, *k, *v, *o, *dO;
+  const float* lse;
+  void *dq, *dk, *dv;
+  float* delta;  // scratch: rowsum(dO * O), written by the first kernel
+};
+
+struct BwdBwdPtrs {
+  const void *q, *k, *v, *dO, *ddq, *ddk, *ddv;
+  const float *lse, *delta;
+  void *dq2, *ddo, *dk2, *dv2;
+  float *dd, *bv;  // scratch written by the query-tiled pass, read by the key-tiled pass
+};
+
+int launch_fwd(const AttnShape& s, int hd, const FwdPtrs& p, int* status, cudaStream_t stream);
+int launch_rowdot(const AttnShape& s, int hd, const void* o, const void* dO, float* delta, cudaStream_t stream);
+int launch_bwd(const AttnShape& s, int hd, const BwdPtrs& p, int* status, cudaStream_t stream);
+// passes: bitmask of kPassQuery (query-tiled: dQ', ddO, dD, B) and kPassKey (key-tiled: dK', dV').
+enum BwdBwdPass : int { kPassQuery = 1, kPassKey = 2 };
+int launch_bwdbwd(const AttnShape& s, int hd, const BwdBwdPtrs& p, int passes, int* status, cudaStream_t stream);
+
+// Sets the dynamic shared memory limit of `func` on the current device once.
+int ensure_smem_limit(const void* func, int bytes);
+
+// 4-D (head_dim, seq, head, batch) bf16 map with a {64, rows, 1, 1} box.
+bool make_seq_map(CUtensorMap* map, const void* base, int hd, int seq, int heads, int batch, const Strides3& st,
+                  int rows);
+
+}  // namespace fh

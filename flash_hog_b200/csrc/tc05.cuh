@@ -87,7 +87,8 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 }
 
 // Waits for the phase with the given parity to complete. Gives up (returns
-// false) after kWaitLimitNs, or early once another role raised `abort_flag`.
+// false) after kWaitLimitNs, or early once another role raised `abort_flag`
+// (pass nullptr to ignore the flag, as the teardown drain does).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
   const uint32_t a = smem_u32(bar);
   if (mbar_try_wait(a, parity)) return true;
@@ -96,7 +97,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
 #pragma unroll 1
     for (int i = 0; i < 32; ++i)
       if (mbar_try_wait(a, parity)) return true;
-    if (*abort_flag) return false;
+    if (abort_flag && *abort_flag) return false;
     if (global_timer_ns() - t0 > kWaitLimitNs) return false;
   }
 }

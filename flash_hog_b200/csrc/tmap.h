@@ -33,8 +33,9 @@ inline EncodeTiledFn encode_tiled_fn() {
 // Returns false if the driver rejects the description.
 inline bool make_tmap_bf16(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
                            const uint64_t* strides_bytes, const uint32_t* box,
-                           CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
+                           CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B, int* cu_result = nullptr) {
   EncodeTiledFn fn = encode_tiled_fn();
+  if (cu_result) *cu_result = -1;
   if (!fn) return false;
   cuuint64_t d[5], s[4];
   cuuint32_t b[5], e[5];
@@ -47,6 +48,7 @@ inline bool make_tmap_bf16(CUtensorMap* map, const void* base, int rank, const u
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, static_cast<cuuint32_t>(rank), const_cast<void*>(base), d,
                   s, b, e, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (cu_result) *cu_result = static_cast<int>(r);
   return r == CUDA_SUCCESS;
 }
 

@@ -1,0 +1,147 @@
+/*
+ * flash_hog_b200 -- C ABI of the B200 (sm_100a) attention hot path of Flash Hog:
+ * forward, first-order backward and double backward (vjp of the vjp).
+ *
+ * The reference reaches its native double backward through one XLA FFI handler,
+ * `TkBwdBwd` (flash_hog/csrc/tk_bwdbwd/ffi.cu:79-98), registered with
+ * `jax.ffi.register_ffi_target("tk_bwdbwd", ...)` (flash_hog/jax/_tk_gpu.py:57)
+ * and called through `jax.ffi.ffi_call` (flash_hog/jax/_tk_gpu.py:96-100). Its
+ * forward and first-order backward are cuDNN custom calls
+ * (flash_hog/jax/_attention_impl.py:224-261). The entry points below replace
+ * those three call sites with plain C functions: raw device pointers, sizes,
+ * strides, a stream, an int status. No torch or XLA types cross this boundary.
+ *
+ * Conventions shared by all entry points
+ *  - Every bf16 tensor is addressed as (batch, seq, head, head_dim) with the
+ *    element strides given in fh_attn_dims (head_dim stride 1). BTNH, the layout
+ *    of the reference API (flash_hog/jax/attention.py:19-49), and BHTD, the
+ *    layout of the reference's native kernels (ffi.cu:7-10), are both strided
+ *    views of this form. Strides must be multiples of 8 elements and base
+ *    pointers 16-byte aligned (TMA requirements).
+ *  - Per-query fp32 vectors (lse, delta, dd, bvec) are (batch, head, seq_q)
+ *    contiguous, the layout of the cuDNN log-sum-exp the reference saves
+ *    (flash_hog/jax/_attention_impl.py:114-139). lse is the natural-log
+ *    log-sum-exp of the scaled, masked scores.
+ *  - causal != 0 applies the top-left mask (query i sees keys j <= i), the mask
+ *    of flash_hog/jax/_pallas_gpu_kernel.py:37-41.
+ *  - head_dim must be 64 in this version; seq_q, seq_k >= 1 (no divisibility
+ *    requirement: ragged edges are masked).
+ *  - Calls are asynchronous on `stream` (a cudaStream_t, may be NULL for the
+ *    legacy default stream) and never allocate device memory except a 4-byte
+ *    status word per device on first use. Scratch buffers are the caller's, as
+ *    XLA owns the scratch outputs of TkBwdBwd.
+ *  - A returned FH_OK means the work was enqueued. Device-side failures (a
+ *    bounded wait that expired) are reported by fh_device_status().
+ *  - Re-entrant: the per-device one-time set-up is guarded by a mutex (the
+ *    reference handler uses an unsynchronised static flag, ffi.cu:41-46).
+ */
+#ifndef FLASH_HOG_B200_H_
+#define FLASH_HOG_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. 1 and 3 correspond to ffi::Error::InvalidArgument and
+ * ffi::Error::Internal of the reference handler (ffi.cu:36-39, 74-76). */
+enum fh_status {
+  FH_OK = 0,
+  FH_ERR_INVALID_ARGUMENT = 1,
+  FH_ERR_UNSUPPORTED = 2,
+  FH_ERR_LAUNCH = 3,
+  FH_ERR_DEVICE = 4,
+  FH_ERR_INJECTED = 5,
+  FH_ERR_NO_DEVICE = 6
+};
+
+/* Element strides of a (batch, seq, head, head_dim) tensor; head_dim stride is 1. */
+typedef struct fh_strides {
+  int64_t batch;
+  int64_t seq;
+  int64_t head;
+} fh_strides;
+
+typedef struct fh_attn_dims {
+  int32_t batch;
+  int32_t heads;
+  int32_t seq_q;
+  int32_t seq_k;
+  int32_t head_dim;
+  fh_strides q; /* Q, O, dO, ddQ and the query-side outputs dQ, dQ', ddO */
+  fh_strides k; /* K, V, ddK, ddV and the key-side outputs dK, dV, dK', dV' */
+} fh_attn_dims;
+
+/* Forward: o = softmax(scale * q k^T + mask) v, lse = logsumexp(scale * q k^T + mask).
+ * Replaces the cuDNN forward with residuals, flash_hog/jax/_attention_impl.py:224-239
+ * (`cuda_dot_product_attention(..., return_residual=True)`). */
+int fh_attn_fwd(void* stream, const fh_attn_dims* dims, const void* q, const void* k, const void* v, void* o,
+                float* lse, float scale, int causal);
+
+/* D = rowsum(dO * o) per query row, fp32 (batch, head, seq_q).
+ * Replaces the XLA einsum of flash_hog/jax/_tk_gpu.py:93 and
+ * flash_hog/jax/_pallas_gpu_kernel.py:110. */
+int fh_attn_rowdot(void* stream, const fh_attn_dims* dims, const void* o, const void* dO, float* delta);
+
+/* First-order backward: dq, dk, dv from (q, k, v, o, dO, lse). `delta` is
+ * caller scratch of batch*heads*seq_q floats (receives rowsum(dO * o)).
+ * Replaces the cuDNN backward, flash_hog/jax/_attention_impl.py:242-261. */
+int fh_attn_bwd(void* stream, const fh_attn_dims* dims, const void* q, const void* k, const void* v, const void* o,
+                const void* dO, const float* lse, void* dq, void* dk, void* dv, float* delta, float scale,
+                int causal);
+
+/* Double backward: given the first-order residuals (q, k, v, dO, lse, delta) and
+ * the cotangents (ddq, ddk, ddv) of (dq, dk, dv), computes
+ *   dq2 = d<(dq,dk,dv),(ddq,ddk,ddv)>/dq, dk2 (/dk), dv2 (/dv), ddo (/dO).
+ * `delta` = rowsum(dO * o) (fh_attn_rowdot). `dd` and `bvec` are caller
+ * scratch of batch*heads*seq_q floats each; on return they hold the row
+ * statistics dD = rowsum(ddS * P) and B = rowsum(dP2 * P).
+ * Same buffers, order and meaning as TkBwdBwd (flash_hog/csrc/tk_bwdbwd/ffi.cu:79-98:
+ * Q,K,V,dO,ddQ,ddK,ddV,L,D -> dQ2,ddO,dK2,dV2,dD,B; attribute scale), plus the
+ * mask flag and the non-causal, cross-length and strided cases of the Pallas
+ * rule flash_hog/jax/_pallas_gpu_kernel.py:49-422. */
+int fh_attn_bwdbwd(void* stream, const fh_attn_dims* dims, const void* q, const void* k, const void* v,
+                   const void* dO, const void* ddq, const void* ddk, const void* ddv, const float* lse,
+                   const float* delta, void* dq2, void* ddo, void* dk2, void* dv2, float* dd, float* bvec,
+                   float scale, int causal);
+
+/* One pass of fh_attn_bwdbwd, same arguments plus `pass`:
+ *   FH_PASS_QUERY (1): the query-tiled pass -- writes dq2, ddo, dd, bvec
+ *                      (dk2, dv2 unused, may be NULL);
+ *   FH_PASS_KEY   (2): the key-tiled pass -- reads dd, bvec, writes dk2, dv2
+ *                      (dq2, ddo unused, may be NULL);
+ *   3: both, identical to fh_attn_bwdbwd.
+ * The reference runs the same two stages as separate kernels and times them
+ * separately (flash_hog/csrc/tk_bwdbwd/ffi.cu:71-73, BENCHMARKS.md:45-46); this
+ * entry lets a caller schedule or time them one at a time. */
+enum fh_bwdbwd_pass { FH_PASS_QUERY = 1, FH_PASS_KEY = 2 };
+int fh_attn_bwdbwd_pass(void* stream, const fh_attn_dims* dims, const void* q, const void* k, const void* v,
+                        const void* dO, const void* ddq, const void* ddk, const void* ddv, const float* lse,
+                        const float* delta, void* dq2, void* ddo, void* dk2, void* dv2, float* dd, float* bvec,
+                        float scale, int causal, int pass);
+
+/* Synchronises `stream`, then reads and clears the status word the kernels of
+ * the current device record device-side failures in. *code receives 0 or one
+ * of the device error codes (1..5: which bounded wait expired). Returns FH_OK,
+ * or FH_ERR_DEVICE when *code != 0. */
+int fh_device_status(void* stream, int* code);
+
+/* Detail message of the last non-FH_OK status returned on this thread by an
+ * entry point (empty if none). The reference handler carries such text in
+ * ffi::Error (ffi.cu:36-39, 74-76). */
+const char* fh_last_error(void);
+
+/* Human-readable name of an fh_status value. */
+const char* fh_status_string(int status);
+
+/* ABI version of this header (bumped on any signature change). */
+int fh_abi_version(void);
+
+#define FH_ABI_VERSION 1
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FLASH_HOG_B200_H_ */

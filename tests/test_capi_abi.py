@@ -1,0 +1,92 @@
+"""The C ABI library loads, exports every symbol the header declares, and
+rejects bad arguments with the documented status codes -- all without a GPU
+(validation precedes any CUDA call)."""
+
+import ctypes
+import os
+import re
+import subprocess
+import sys
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "flash_hog_b200.h")
+
+
+def _declared():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"^\s*(?:int|const char\*)\s+(fh_\w+)\s*\(", text, re.M)))
+
+
+def test_header_declares_the_binding_symbols():
+    from flash_hog_b200 import _capi
+
+    assert _declared() == sorted(_capi.EXPORTED_SYMBOLS)
+
+
+def test_library_exports_every_declared_symbol():
+    from flash_hog_b200 import _capi
+
+    lib = ctypes.CDLL(_capi.library_path())
+    for name in _declared():
+        assert hasattr(lib, name), name
+    h = _capi.lib()
+    assert h.fh_abi_version() == _capi.ABI_VERSION
+    assert h.fh_status_string(0) == b"ok"
+    assert h.fh_status_string(5) == b"injected error"
+
+
+def _dims(**kw):
+    from flash_hog_b200._capi import FhAttnDims, FhStrides
+
+    d = dict(batch=1, heads=2, seq_q=128, seq_k=128, head_dim=64)
+    d.update(kw)
+    st = FhStrides(128 * 2 * 64, 2 * 64, 64)
+    return FhAttnDims(d["batch"], d["heads"], d["seq_q"], d["seq_k"], d["head_dim"], st, st)
+
+
+def _fwd(dims, ptr=64):
+    from flash_hog_b200._capi import lib
+
+    p = ctypes.c_void_p(ptr)
+    return lib().fh_attn_fwd(None, ctypes.byref(dims) if dims is not None else None, p, p, p, p, p, 0.125, 1)
+
+
+def test_argument_validation_codes():
+    assert _fwd(None) == 1                      # null dims
+    assert _fwd(_dims(head_dim=32)) == 2        # unsupported head_dim
+    assert _fwd(_dims(seq_q=0)) == 1            # empty sequence
+    assert _fwd(_dims(batch=0)) == 1
+    assert _fwd(_dims(), ptr=8) == 1            # pointers not 16-byte aligned
+    d = _dims()
+    d.q.seq = 12                                # stride not a multiple of 8 elements
+    assert _fwd(d) == 1
+
+
+def test_error_injection_is_host_side():
+    """FLASH_HOG_B200_INJECT_ERROR makes the named entry return FH_ERR_INJECTED
+    before any validation or CUDA call (checked in a fresh process)."""
+    code = (
+        "import ctypes,sys; sys.path.insert(0, %r)\n"
+        "from flash_hog_b200 import _capi\n"
+        "h=_capi.lib(); d=_capi.FhAttnDims()\n"
+        "p=ctypes.c_void_p(0)\n"
+        "print(h.fh_attn_bwdbwd(None, ctypes.byref(d), *([p]*15), 0.1, 1), h.fh_attn_fwd(None, None, p,p,p,p,p, 0.1, 0))\n"
+    ) % ROOT
+    env = dict(os.environ, FLASH_HOG_B200_INJECT_ERROR="fh_attn_bwdbwd")
+    out = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=120)
+    assert out.returncode == 0, out.stderr
+    assert out.stdout.split() == ["5", "1"]
+
+
+def test_python_errors_are_loud():
+    import torch
+
+    import flash_hog_b200 as fhb
+    from flash_hog_b200._capi import FlashHogError
+
+    q = torch.zeros(1, 128, 2, 64)
+    with pytest.raises(ValueError):
+        fhb.dot_product_attention(q, q, q)      # CPU tensors: no CPU fallback
+    assert issubclass(FlashHogError, RuntimeError)

@@ -1,0 +1,170 @@
+"""GPU parity of the sm_100a kernels against the CPU oracle (through the C ABI).
+
+Edge cases follow what the reference exercises or documents: causal and
+non-causal, Nq != Nk cross attention (the golden file's 128 x 256 shape),
+BTNH and BHTD layouts, ragged lengths that are not tile multiples, and the
+headline configuration at full size checked on sampled heads.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import attention_oracle as ora
+from parity_util import assert_close, case_inputs, np64, oracle_bwdbwd, select_heads
+
+pytestmark = pytest.mark.gpu
+
+CASES = [
+    # b, h, tq, tk, causal
+    (1, 2, 128, 128, True),
+    (1, 2, 128, 128, False),
+    (1, 1, 128, 256, False),   # golden-file shape: Nq=128, Nk=256
+    (2, 2, 256, 256, True),
+    (1, 2, 256, 384, False),
+    (1, 2, 384, 256, True),
+    (1, 1, 200, 200, True),    # ragged: not a multiple of any tile
+    (1, 2, 72, 136, False),    # ragged cross attention
+    (2, 3, 512, 512, True),
+]
+
+
+def _cuda(x):
+    return {k: v.cuda() for k, v in x.items()}
+
+
+@pytest.mark.parametrize("b,h,tq,tk,causal", CASES)
+def test_bwdbwd_matches_oracle(b, h, tq, tk, causal):
+    from flash_hog_b200 import MaskType, flash_bwdbwd
+    from flash_hog_b200._capi import device_status
+
+    x = case_inputs(b, h, tq, tk, seed=11 * tq + tk, causal=causal)
+    (rq2, rk2, rv2, rdo), (rd, rdd, rb) = oracle_bwdbwd(x, causal)
+    g = _cuda(x)
+    mask = MaskType.CAUSAL if causal else MaskType.NO_MASK
+    (dq2, dk2, dv2, ddo), (d, dd, bv) = flash_bwdbwd(g["q"], g["k"], g["v"], g["o"], g["do"], g["ddq"], g["ddk"],
+                                                     g["ddv"], g["lse"], mask_type=mask, return_stats=True)
+    torch.cuda.synchronize()
+    assert device_status() == 0
+    assert_close("D", np64(d), rd)
+    assert_close("dD", np64(dd), rdd)
+    assert_close("B", np64(bv), rb)
+    assert_close("dQ2", np64(dq2), rq2)
+    assert_close("dK2", np64(dk2), rk2)
+    assert_close("dV2", np64(dv2), rv2)
+    assert_close("ddO", np64(ddo), rdo)
+
+
+@pytest.mark.parametrize("b,h,tq,tk,causal", CASES)
+def test_fwd_bwd_match_oracle(b, h, tq, tk, causal):
+    from flash_hog_b200 import MaskType
+    from flash_hog_b200 import _attention_impl as impl
+    from flash_hog_b200._capi import device_status
+
+    x = case_inputs(b, h, tq, tk, seed=7 * tq + tk, causal=causal)
+    g = _cuda(x)
+    mask = MaskType.CAUSAL if causal else MaskType.NO_MASK
+    scale = 64 ** -0.5
+    out, lse = impl.cuda_dot_product_attention(g["q"], g["k"], g["v"], mask, scale, return_residual=True)
+    torch.cuda.synchronize()
+    assert device_status() == 0
+    ro, rl = ora.attention_fwd(np64(x["q"]), np64(x["k"]), np64(x["v"]), causal=causal)
+    assert_close("O", np64(out), ro)
+    assert ora.max_abs(np64(lse), rl) <= 2e-3
+    # first-order backward from the oracle's residuals
+    dq, dk, dv = impl.dot_product_attention_bwd_rule(mask, scale, (g["q"], g["k"], g["v"], g["lse"], g["o"]),
+                                                     g["do"])
+    torch.cuda.synchronize()
+    assert device_status() == 0
+    rq, rk, rv = ora.attention_bwd(np64(x["q"]), np64(x["k"]), np64(x["v"]), np64(x["o"]), np64(x["lse"]),
+                                   np64(x["do"]), causal=causal)
+    assert_close("dQ", np64(dq), rq)
+    assert_close("dK", np64(dk), rk)
+    assert_close("dV", np64(dv), rv)
+
+
+@pytest.mark.parametrize("causal", [True, False])
+def test_nested_autograd_matches_double_autograd(causal):
+    """grad-of-grad through the public API vs torch double autograd of naive attention."""
+    import flash_hog_b200 as fhb
+
+    x = ora.make_inputs(2, 2, 256, 256, 64, seed=5)
+    ref = ora.autograd_all(*(x[n].double() for n in ("q", "k", "v", "do", "ddq", "ddk", "ddv")), causal=causal)
+    q, k, v, do = (x[n].cuda().requires_grad_(True) for n in ("q", "k", "v", "do"))
+    out = fhb.dot_product_attention(q, k, v, is_causal=causal)
+    dq, dk, dv = torch.autograd.grad(out, (q, k, v), do, create_graph=True)
+    dq2, dk2, dv2, ddo = torch.autograd.grad((dq, dk, dv), (q, k, v, do),
+                                             (x["ddq"].cuda(), x["ddk"].cuda(), x["ddv"].cuda()))
+    torch.cuda.synchronize()
+    for name, got in dict(o=out, dq=dq, dk=dk, dv=dv, dq2=dq2, dk2=dk2, dv2=dv2, ddo=ddo).items():
+        assert_close(name, np64(got), ref[name].numpy())
+
+
+def test_unbatched_and_bhtd_layouts():
+    """TNH inputs (reference's unbatched form) and BHTD-strided views give the BTNH results."""
+    from flash_hog_b200 import MaskType, flash_bwdbwd
+
+    x = _cuda(case_inputs(1, 2, 256, 256, seed=3, causal=True))
+    args = [x[n] for n in ("q", "k", "v", "o", "do", "ddq", "ddk", "ddv")]
+    full = flash_bwdbwd(*args, x["lse"], mask_type=MaskType.CAUSAL)
+    unb = flash_bwdbwd(*(a[0] for a in args), x["lse"][0], mask_type=MaskType.CAUSAL)
+    # BHTD storage, presented to the kernels as a strided BTNH view
+    bhtd = [a.transpose(1, 2).contiguous().transpose(1, 2) for a in args]
+    from flash_hog_b200 import _capi
+    q, k, v, o, do, ddq, ddk, ddv = bhtd
+    delta = torch.empty_like(x["lse"])
+    dd, bv = torch.empty_like(delta), torch.empty_like(delta)
+    dq2, ddo = torch.empty_like(q), torch.empty_like(q)
+    dk2, dv2 = torch.empty_like(k), torch.empty_like(k)
+    _capi.attn_rowdot(o, do, delta)
+    _capi.attn_bwdbwd(q, k, v, do, ddq, ddk, ddv, x["lse"], delta, dq2, ddo, dk2, dv2, dd, bv, 0.125, True)
+    torch.cuda.synchronize()
+    for a, u, s in zip(full, unb, (dq2, dk2, dv2, ddo)):
+        assert torch.equal(a[0], u)
+        assert torch.equal(a, s)
+
+
+def test_headline_config_full_size_sampled_heads():
+    """B4 H16 S2048 D64 causal at full size; oracle on sampled (batch, head) pairs;
+    determinism (bitwise) and batch x heads sharding (a shard's result equals the
+    matching slice of the full run, bit for bit)."""
+    from flash_hog_b200 import MaskType, flash_bwdbwd
+
+    b, h, s = 4, 16, 2048
+    x = ora.make_inputs(b, h, s, s, 64, seed=0)
+    g = _cuda(x)
+    from flash_hog_b200 import _attention_impl as impl
+    o, lse = impl.cuda_dot_product_attention(g["q"], g["k"], g["v"], MaskType.CAUSAL, 0.125, return_residual=True)
+    args = [g[n] for n in ("q", "k", "v")] + [o] + [g[n] for n in ("do", "ddq", "ddk", "ddv")] + [lse]
+    out1 = flash_bwdbwd(*args, mask_type=MaskType.CAUSAL)
+    out2 = flash_bwdbwd(*args, mask_type=MaskType.CAUSAL)
+    torch.cuda.synchronize()
+    for a1, a2 in zip(out1, out2):
+        assert torch.equal(a1, a2), "double backward is not deterministic"
+    # sharding: batch 1..2 and heads 4..11 as an independent call
+    sl = [a[1:3, :, 4:12].contiguous() for a in args[:-1]] + [lse[1:3, 4:12].contiguous()]
+    shard = flash_bwdbwd(*sl, mask_type=MaskType.CAUSAL)
+    torch.cuda.synchronize()
+    for full, part in zip(out1, shard):
+        assert torch.equal(full[1:3, :, 4:12], part)
+    heads = [(0, 0), (3, 15), (2, 7)]
+    xs = dict(x)
+    xs["o"], xs["lse"] = o.cpu(), lse.cpu()
+    (rq2, rk2, rv2, rdo), _ = oracle_bwdbwd(xs, True, heads=heads)
+    for name, got, ref in zip(("dQ2", "dK2", "dV2", "ddO"), out1, (rq2, rk2, rv2, rdo)):
+        assert_close(name, select_heads(got, heads), ref)
+
+
+def test_device_status_clean_and_fp32_inputs():
+    """fp32 inputs are cast to bf16 (as the reference's native plugin does) and the
+    result returns in fp32; no device error is recorded."""
+    import flash_hog_b200 as fhb
+    from flash_hog_b200._capi import device_status
+
+    x = ora.make_inputs(1, 2, 256, 256, 64, seed=9, dtype=torch.float32)
+    q, k, v = (x[n].cuda() for n in ("q", "k", "v"))
+    out = fhb.dot_product_attention(q, k, v, is_causal=True)
+    assert out.dtype == torch.float32
+    ro, _ = ora.attention_fwd(np64(x["q"]), np64(x["k"]), np64(x["v"]), causal=True)
+    assert_close("O fp32-in", np64(out), ro)
+    assert device_status() == 0
