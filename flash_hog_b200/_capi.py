@@ -37,6 +37,7 @@ EXPORTED_SYMBOLS = (
     "fh_attn_bwd",
     "fh_attn_bwdbwd",
     "fh_attn_bwdbwd_pass",
+    "fh_attn_bwdbwd_noalloc",
     "fh_device_status",
     "fh_status_string",
     "fh_last_error",
@@ -88,6 +89,7 @@ def lib() -> ctypes.CDLL:
     h.fh_attn_bwd.argtypes = [vp, dims, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, f32, i32]
     h.fh_attn_bwdbwd.argtypes = [vp, dims] + [vp] * 15 + [f32, i32]
     h.fh_attn_bwdbwd_pass.argtypes = [vp, dims] + [vp] * 15 + [f32, i32, i32]
+    h.fh_attn_bwdbwd_noalloc.argtypes = [vp, dims] + [vp] * 13 + [f32, i32, vp]
     h.fh_device_status.argtypes = [vp, ctypes.POINTER(ctypes.c_int)]
     h.fh_status_string.argtypes = [i32]
     h.fh_status_string.restype = ctypes.c_char_p
@@ -95,7 +97,7 @@ def lib() -> ctypes.CDLL:
     h.fh_last_error.argtypes = []
     h.fh_last_error.restype = ctypes.c_char_p
     for name in ("fh_attn_fwd", "fh_attn_rowdot", "fh_attn_bwd", "fh_attn_bwdbwd", "fh_attn_bwdbwd_pass",
-                 "fh_device_status", "fh_abi_version"):
+                 "fh_attn_bwdbwd_noalloc", "fh_device_status", "fh_abi_version"):
         getattr(h, name).restype = i32
     if h.fh_abi_version() != ABI_VERSION:
         raise RuntimeError(f"flash_hog_b200 ABI mismatch: library {h.fh_abi_version()}, binding {ABI_VERSION}")

@@ -275,3 +275,88 @@ int fh_device_status(void* stream, int* code) {
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------------------------
+// Allocation-free double backward
+// ------------------------------------------------------------------------------------
+//
+// Some callers of this library cannot allocate device memory on the call path:
+// an XLA FFI handler only receives the buffers XLA assigned before the
+// computation started, and JAX reserves most of the GPU for its own pool up
+// front, so a handler that calls cudaMalloc competes for (or fails to get) the
+// remainder; inference servers that reserve their whole memory budget at start
+// and never allocate per request are in the same position. They still own the
+// inputs and outputs, but have nowhere to put the double backward's per-query
+// scratch (D, dD, B). For them the scratch lives in a fixed file-scope device
+// array instead.
+
+namespace fh {
+namespace {
+
+// Capacity of the static scratch in query rows (batch * heads * seq_q).
+constexpr long long kNoAllocMaxRows = 1LL << 19;
+
+// D | dD | B for up to kNoAllocMaxRows query rows: 3 x 2 MiB = 6 MiB, held by
+// every GPU on which this library's module is loaded until the process exits.
+static __device__ __align__(256) float g_noalloc_scratch[3 * kNoAllocMaxRows];
+
+float* g_noalloc_ptr[kMaxDevices] = {nullptr};
+
+// Device address of g_noalloc_scratch on the current device. Host code cannot
+// use the array's name as a device address (it names a host-side shadow), so
+// the address is looked up once per device, with that device current.
+int noalloc_scratch(float** out) {
+  const int dev = current_device();
+  if (dev < 0 || dev >= kMaxDevices) return fail(kNoDevice, "no current CUDA device");
+  std::lock_guard<std::mutex> lock(g_mutex);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      char msg[200];
+      std::snprintf(msg, sizeof(msg), "cudaGetSymbolAddress of the static scratch failed: %s",
+                    cudaGetErrorString(e));
+      return fail(kLaunchFailed, msg);
+    }
+    g_noalloc_ptr[dev] = static_cast<float*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return kOk;
+}
+
+}  // namespace
+}  // namespace fh
+
+extern "C" int fh_attn_bwdbwd_noalloc(void* stream, const fh_attn_dims* dims, const void* q, const void* k,
+                                      const void* v, const void* o, const void* dO, const void* ddq,
+                                      const void* ddk, const void* ddv, const float* lse, void* dq2, void* ddo,
+                                      void* dk2, void* dv2, float scale, int causal, int* device_status) {
+  if (injected("fh_attn_bwdbwd_noalloc")) return FH_ERR_INJECTED;
+  AttnShape s;
+  int rc = validate(dims, &s, scale, causal);
+  if (rc != kOk) return rc;
+  const long long rows = static_cast<long long>(s.B) * s.H * s.Tq;
+  if (rows > kNoAllocMaxRows) {
+    char msg[240];
+    std::snprintf(msg, sizeof(msg),
+                  "batch*heads*seq_q = %lld exceeds the %lld query rows of fh_attn_bwdbwd_noalloc's static "
+                  "scratch; use fh_attn_bwdbwd with caller-provided scratch",
+                  rows, kNoAllocMaxRows);
+    return fail(FH_ERR_INVALID_ARGUMENT, msg);
+  }
+  if (!all_aligned(q, k, v, o, dO, ddq, ddk, ddv, dq2, ddo, dk2, dv2) || !lse)
+    return fail(FH_ERR_INVALID_ARGUMENT, kAlignMsg);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if ((rc = select_stream_device(st)) != kOk) return rc;
+  float* scratch = nullptr;
+  if ((rc = noalloc_scratch(&scratch)) != kOk) return rc;
+  // Every element the kernels read is written earlier in the same call (D by
+  // rowdot, dD and B by the query-tiled pass), so nothing needs clearing.
+  float* delta = scratch;
+  float* dd = scratch + kNoAllocMaxRows;
+  float* bv = scratch + 2 * kNoAllocMaxRows;
+  rc = launch_rowdot(s, dims->head_dim, o, dO, delta, st);
+  if (rc != kOk) return rc;
+  return launch_bwdbwd(s, dims->head_dim, BwdBwdPtrs{q, k, v, dO, ddq, ddk, ddv, lse, delta, dq2, ddo, dk2, dv2, dd, bv},
+                       kPassQuery | kPassKey, device_status, st);
+}

@@ -121,6 +121,33 @@ int fh_attn_bwdbwd_pass(void* stream, const fh_attn_dims* dims, const void* q, c
                         const float* delta, void* dq2, void* ddo, void* dk2, void* dv2, float* dd, float* bvec,
                         float scale, int causal, int pass);
 
+/* Allocation-free double backward. No counterpart in the reference: it exists
+ * for callers that cannot allocate device memory while they run -- an XLA FFI
+ * handler only gets the buffers XLA assigned up front (and JAX reserves most of
+ * the GPU for its own pool), and servers that reserve their whole memory budget
+ * at start-up never allocate per request. Such a caller still passes the inputs
+ * (q, k, v, o, dO, ddq, ddk, ddv, lse) and outputs (dq2, ddo, dk2, dv2) as for
+ * fh_attn_bwdbwd, but no scratch: D = rowsum(dO * o), dD and B live in a 6 MiB
+ * static device array inside the library (3 x 2^19 floats).
+ *  - Limit: batch * heads * seq_q <= 524288 query rows; larger problems get
+ *    FH_ERR_INVALID_ARGUMENT (see fh_last_error()) -- use fh_attn_bwdbwd.
+ *  - It never calls cudaMalloc/cudaFree or any allocating routine. The first
+ *    call on each device looks up the array's device address
+ *    (cudaGetSymbolAddress, once per device); make that first call before any
+ *    stream capture.
+ *  - Every call shares the one array and leaves its contents behind. Nothing in
+ *    it needs to start at zero (each call writes all it reads), but calls whose
+ *    GPU work overlaps (different streams, no ordering between them) race on it.
+ *  - The array is held by every GPU on which the library's module is loaded,
+ *    until the process exits.
+ *  - device_status: optional (may be NULL) caller-owned, zeroed device int in
+ *    which the kernels record a device-side error code (fh_device_status() reads
+ *    the library's own word, which this entry point does not use). */
+int fh_attn_bwdbwd_noalloc(void* stream, const fh_attn_dims* dims, const void* q, const void* k, const void* v,
+                           const void* o, const void* dO, const void* ddq, const void* ddk, const void* ddv,
+                           const float* lse, void* dq2, void* ddo, void* dk2, void* dv2, float scale, int causal,
+                           int* device_status);
+
 /* Synchronises `stream`, then reads and clears the status word the kernels of
  * the current device record device-side failures in. *code receives 0 or one
  * of the device error codes (1..5: which bounded wait expired). Returns FH_OK,
