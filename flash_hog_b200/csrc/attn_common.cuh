@@ -103,9 +103,10 @@ __device__ __forceinline__ void raise_error(int* status, volatile int* abort_fla
   if (status) atomicCAS(status, 0, code);
 }
 
-// Loads 16 TMEM columns starting at `col` for this thread's lane.
+// Loads 16 TMEM columns starting at `col` for this thread's lane. A warp may
+// only reach the 32 lanes of its sub-partition: lanes 32*(warp % 4) ... +31.
 __device__ __forceinline__ void tmem_row16(uint32_t tmem, int warp, int col, uint32_t (&r)[16]) {
-  tmem_ld16(tmem + tmem_lane_base(warp) + col, r);
+  tmem_ld16(tmem + tmem_lane_base(warp & 3) + col, r);
 }
 
 // Writes 16 floats as bf16 (32 contiguous bytes) to global memory.

@@ -45,6 +45,42 @@ struct BBArgs {
 };
 
 // ----------------------------------------------------------------------------------
+// CTA layout shared by both passes
+// ----------------------------------------------------------------------------------
+//
+// 10 warps. Warps 0-7 are two elementwise warpgroups: thread (warp, lane) owns
+// TMEM lane 32*(warp%4)+lane (one resident row) and warpgroup w = warp/4 owns
+// columns [32w, 32w+32) of every 64-column streamed tile. Each thread loads its
+// 32-column share of all four score tiles into registers and releases the
+// score TMEM at once, so the tensor core computes the next tile's scores while
+// the registers of this tile are turned into operand panels. Warp 8 is the
+// TMA producer, warp 9 allocates TMEM and issues every tcgen05.mma.
+constexpr int kBBThreads = 320;
+constexpr int kBBEw = 256;
+constexpr int kBBWarpProducer = 8;
+constexpr int kBBWarpMma = 9;
+
+// Writes 16 packed bf16 pairs (32 bf16) into 16-byte chunks (c, c+1, c+2, c+3)
+// of row r of a 128B-swizzled panel.
+__device__ __forceinline__ void stage_packed32(uint8_t* panel, int r, int c, const uint32_t (&v)[16]) {
+  const uint32_t base = smem_u32(panel);
+#pragma unroll
+  for (int k = 0; k < 4; ++k)
+    st_shared_v4(base + sw128_offset(r, c + k), v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+}
+
+// Loads this thread's 32-column share (two x16 loads) of a score tile.
+__device__ __forceinline__ void tmem_share32(uint32_t tmem, int warp, int col, uint32_t (&r)[32]) {
+  tmem_ld16(tmem + tmem_lane_base(warp & 3) + col, *reinterpret_cast<uint32_t(*)[16]>(&r[0]));
+  tmem_ld16(tmem + tmem_lane_base(warp & 3) + col + 16, *reinterpret_cast<uint32_t(*)[16]>(&r[16]));
+}
+
+__device__ __forceinline__ void reg_fence32(uint32_t (&r)[32]) {
+#pragma unroll
+  for (int i = 0; i < 32; ++i) asm volatile("" : "+r"(r[i])::"memory");
+}
+
+// ----------------------------------------------------------------------------------
 // query-tiled pass
 // ----------------------------------------------------------------------------------
 
@@ -55,17 +91,18 @@ struct QPass {
   static constexpr int RES = kBM * HD * 2;      // one resident bf16 tile
   static constexpr int STR = BN * HD * 2;       // one streamed bf16 tile
   static constexpr int SLOT = 4 * STR;          // K | V | ddK | ddV
-  static constexpr int OPS = kBM * BN * 2;      // one bf16 operand panel set (dS, dS2, ddP or P)
+  static constexpr int OPS = kBM * BN * 2;      // one bf16 operand panel (dS, dS2, ddP or P)
   static constexpr int SMEM = 1024 + 3 * RES + ST * SLOT + 4 * OPS;
   static constexpr int C_S = 0, C_DDS = BN, C_DP = 2 * BN, C_DPA = 3 * BN;
   static constexpr int C_DQ = 4 * BN, C_DDO = 4 * BN + HD;
   static constexpr int TMEM_COLS = 512;
   static_assert(C_DDO + HD <= TMEM_COLS, "TMEM budget");
   static_assert(SMEM <= 232448, "shared memory budget");
+  static_assert(BN == 64, "two warpgroups x 32 columns");
 };
 
 template <int HD>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kBBThreads, 1)
     bwdbwd_q_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
                     const __grid_constant__ CUtensorMap tm_ddq, const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_ddk,
@@ -80,7 +117,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* s_ring = s_ddq + G::RES;
   uint8_t* s_ops = s_ring + ST * G::SLOT;  // dS | dS2 | ddP | P
   __shared__ uint64_t bar_res, bar_full[ST], bar_empty[ST];
-  __shared__ uint64_t bar_sc_full, bar_sc_empty, bar_ops_full, bar_ops_empty, bar_acc;
+  __shared__ uint64_t bar_sc_full, bar_sc_empty, bar_ops_full, bar_ops_empty, bar_acc, bar_red;
+  __shared__ float red[4][2][kBM];  // stats-sweep partial sums: statistic, warpgroup, row
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
 
@@ -101,18 +139,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bar_empty[s], 1);
     }
     mbar_init(&bar_sc_full, 1);
-    mbar_init(&bar_sc_empty, kEwThreads);
-    mbar_init(&bar_ops_full, kEwThreads);
+    mbar_init(&bar_sc_empty, kBBEw);
+    mbar_init(&bar_ops_full, kBBEw);
     mbar_init(&bar_ops_empty, 1);
     mbar_init(&bar_acc, 1);
+    mbar_init(&bar_red, kBBEw);
     mbar_fence_init();
   }
-  if (warp == kWarpMma) tmem_alloc(&tmem_base, G::TMEM_COLS);
+  if (warp == kBBWarpMma) tmem_alloc(&tmem_base, G::TMEM_COLS);
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_base;
 
-  if (warp == kWarpProducer) {
+  if (warp == kBBWarpProducer) {
     // ------------------------------ TMA producer ------------------------------
     if (lane == 0) {
       tma_prefetch_desc(&tm_q);
@@ -143,8 +182,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         drained &= mbar_wait(&bar_full[it % ST], (it / ST) & 1, nullptr);
       if (!drained) raise_error(a.status, &abort_flag, kDevTimeoutDrain);
     }
-  } else if (warp == kWarpMma) {
+  } else if (warp == kBBWarpMma) {
     // ------------------------------ MMA issuer --------------------------------
+    // Iteration it issues the scores of tile it, then the operand products of
+    // tile it-1 (second sweep only): the tensor core scores one tile ahead of
+    // the elementwise warps.
     if (lane == 0) {
       const uint32_t id_sc = idesc_bf16_f32(kBM, BN, false, false);
       const uint32_t id_out = idesc_bf16_f32(kBM, HD, false, true);
@@ -196,7 +238,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // --------------------------- elementwise warps ----------------------------
-    const int r = threadIdx.x;  // TMEM lane = query row inside the tile
+    const int wg = warp >> 2;                // column half of every tile
+    const int r = (warp & 3) * 32 + lane;    // TMEM lane = query row inside the tile
+    const int cb = wg * 32;
     const int row = q0 + r;
     const bool row_ok = row < sh.Tq;
     const size_t vi = stat_index(b, h, row_ok ? row : 0, sh.H, sh.Tq);
@@ -208,80 +252,100 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int it = 0; it < total; ++it) {
       const int j = it % n;
       const bool sweep2 = it >= n;
-      const int k0 = j * BN;
+      const int kc = j * BN + cb;  // first key of this thread's columns
       ok = __all_sync(0xffffffffu, mbar_wait(&bar_sc_full, it & 1, &abort_flag));
-      if (ok && sweep2 && j > 0) ok = __all_sync(0xffffffffu, mbar_wait(&bar_ops_empty, (j - 1) & 1, &abort_flag));
       if (!ok) break;
       tc_fence_after();
-      const bool need_mask = (k0 + BN > sh.Tk) || (sh.causal && k0 + BN - 1 > q0);
-#pragma unroll 1
-      for (int c = 0; c < BN / 16; ++c) {
-        uint32_t vs[16], vdds[16], vdp[16], vdpa[16];
-        tmem_row16(tmem, warp, G::C_S + c * 16, vs);
-        tmem_row16(tmem, warp, G::C_DDS + c * 16, vdds);
-        tmem_row16(tmem, warp, G::C_DP + c * 16, vdp);
-        tmem_row16(tmem, warp, G::C_DPA + c * 16, vdpa);
-        tmem_wait_ld();
-        reg_fence16(vs);
-        reg_fence16(vdds);
-        reg_fence16(vdp);
-        reg_fence16(vdpa);
-        if (!sweep2) {
+      uint32_t vs[32], vdds[32], vdp[32], vdpa[32];
+      tmem_share32(tmem, warp, G::C_S + cb, vs);
+      tmem_share32(tmem, warp, G::C_DDS + cb, vdds);
+      tmem_share32(tmem, warp, G::C_DP + cb, vdp);
+      tmem_share32(tmem, warp, G::C_DPA + cb, vdpa);
+      tmem_wait_ld();
+      reg_fence32(vs);
+      reg_fence32(vdds);
+      reg_fence32(vdp);
+      reg_fence32(vdpa);
+      tc_fence_before();
+      mbar_arrive(&bar_sc_empty);  // the tensor core may score the next tile now
+      const bool need_mask = (kc + 32 > sh.Tk) || (sh.causal && kc + 31 > row);
+      if (!sweep2) {
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int key = k0 + c * 16 + i;
-            float s = fmaf(__uint_as_float(vs[i]), sc2, -lg);
-            if (need_mask && (key >= sh.Tk || (sh.causal && key > row))) s = -INFINITY;
-            const float p = ex2(s);
-            const float dds = __uint_as_float(vdds[i]) * sc;
-            const float dp = __uint_as_float(vdp[i]);
-            const float t = dds * p;
-            dD += t;
-            r3 = fmaf(t, dp, r3);
-            r1 = fmaf(__uint_as_float(vdpa[i]), p, r1);
-            r2 = fmaf(dp, p, r2);
-          }
-        } else {
-          float o_ds[16], o_ds2[16], o_ddp[16], o_p[16];
+        for (int i = 0; i < 32; ++i) {
+          float s = fmaf(__uint_as_float(vs[i]), sc2, -lg);
+          if (need_mask && (kc + i >= sh.Tk || (sh.causal && kc + i > row))) s = -INFINITY;
+          const float p = ex2(s);
+          const float dds = __uint_as_float(vdds[i]) * sc;
+          const float dp = __uint_as_float(vdp[i]);
+          const float t = dds * p;
+          dD += t;
+          r3 = fmaf(t, dp, r3);
+          r1 = fmaf(__uint_as_float(vdpa[i]), p, r1);
+          r2 = fmaf(dp, p, r2);
+        }
+        if (it == n - 1) {
+          // Combine the two warpgroups' column halves (same order on both sides).
+          red[0][wg][r] = dD;
+          red[1][wg][r] = r1;
+          red[2][wg][r] = r2;
+          red[3][wg][r] = r3;
+          mbar_arrive(&bar_red);
+          ok = __all_sync(0xffffffffu, mbar_wait(&bar_red, 0, &abort_flag));
+          if (!ok) break;
+          dD = red[0][0][r] + red[0][1][r];
+          r1 = red[1][0][r] + red[1][1][r];
+          r2 = red[2][0][r] + red[2][1][r];
+          r3 = red[3][0][r] + red[3][1][r];
+          Bv = r1 - dD * r2 - dv * dD + r3;
+        }
+      } else {
+        if (j > 0) ok = __all_sync(0xffffffffu, mbar_wait(&bar_ops_empty, (j - 1) & 1, &abort_flag));
+        if (!ok) break;
+        uint32_t o_ds[16], o_ds2[16], o_ddp[16], o_p[16];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int key = k0 + c * 16 + i;
-            float s = fmaf(__uint_as_float(vs[i]), sc2, -lg);
-            if (need_mask && (key >= sh.Tk || (sh.causal && key > row))) s = -INFINITY;
+        for (int i = 0; i < 32; i += 2) {
+          float pp[2], ddp[2], ds[2], ds2[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int kk = kc + i + e;
+            float s = fmaf(__uint_as_float(vs[i + e]), sc2, -lg);
+            if (need_mask && (kk >= sh.Tk || (sh.causal && kk > row))) s = -INFINITY;
             const float p = ex2(s);
-            const float dds = __uint_as_float(vdds[i]) * sc;
-            const float dp = __uint_as_float(vdp[i]);
+            const float dds = __uint_as_float(vdds[i + e]) * sc;
+            const float dp = __uint_as_float(vdp[i + e]);
             const float u = dds - dD;
             const float ps = p * sc;
-            o_p[i] = p;
-            o_ddp[i] = p * u;
-            o_ds[i] = ps * (dp - dv);
-            const float dp2 = fmaf(-dds, dv, fmaf(dp, u, __uint_as_float(vdpa[i])));
-            o_ds2[i] = ps * (dp2 - Bv);
+            pp[e] = p;
+            ddp[e] = p * u;
+            ds[e] = ps * (dp - dv);
+            const float dp2 = fmaf(-dds, dv, fmaf(dp, u, __uint_as_float(vdpa[i + e])));
+            ds2[e] = ps * (dp2 - Bv);
           }
-          stage_bf16x16(s_ops, r, c, o_ds);
-          stage_bf16x16(s_ops + G::OPS, r, c, o_ds2);
-          stage_bf16x16(s_ops + 2 * G::OPS, r, c, o_ddp);
-          stage_bf16x16(s_ops + 3 * G::OPS, r, c, o_p);
+          o_p[i / 2] = pack_bf16(pp[0], pp[1]);
+          o_ddp[i / 2] = pack_bf16(ddp[0], ddp[1]);
+          o_ds[i / 2] = pack_bf16(ds[0], ds[1]);
+          o_ds2[i / 2] = pack_bf16(ds2[0], ds2[1]);
         }
-      }
-      tc_fence_before();
-      mbar_arrive(&bar_sc_empty);
-      if (sweep2) {
+        stage_packed32(s_ops, r, 4 * wg, o_ds);
+        stage_packed32(s_ops + G::OPS, r, 4 * wg, o_ds2);
+        stage_packed32(s_ops + 2 * G::OPS, r, 4 * wg, o_ddp);
+        stage_packed32(s_ops + 3 * G::OPS, r, 4 * wg, o_p);
         fence_async_smem();
         mbar_arrive(&bar_ops_full);
       }
-      if (it == n - 1) Bv = r1 - dD * r2 - dv * dD + r3;
     }
     if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&bar_acc, 0, &abort_flag));
     if (ok) {
       tc_fence_after();
       const int srow = row_ok ? row : 0;
-      tmem_row_to_global<HD>(tmem, warp, G::C_DQ, a.dq2 + row_offset(sh.sq, b, srow, h), row_ok);
-      tmem_row_to_global<HD>(tmem, warp, G::C_DDO, a.ddo + row_offset(sh.sq, b, srow, h), row_ok);
-      if (row_ok) {
-        a.dd[vi] = dD;
-        a.bv[vi] = Bv;
+      if (wg == 0) {
+        tmem_row_to_global<HD>(tmem, warp, G::C_DQ, a.dq2 + row_offset(sh.sq, b, srow, h), row_ok);
+        if (row_ok) {
+          a.dd[vi] = dD;
+          a.bv[vi] = Bv;
+        }
+      } else {
+        tmem_row_to_global<HD>(tmem, warp, G::C_DDO, a.ddo + row_offset(sh.sq, b, srow, h), row_ok);
       }
     } else if (threadIdx.x == 0) {
       raise_error(a.status, &abort_flag, kDevTimeoutMma);
@@ -290,7 +354,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == kWarpMma) tmem_dealloc(tmem, G::TMEM_COLS);
+  if (warp == kBBWarpMma) tmem_dealloc(tmem, G::TMEM_COLS);
 }
 
 // ----------------------------------------------------------------------------------
@@ -313,10 +377,11 @@ struct KPass {
   static_assert(SLOT % 1024 == 0, "slots must keep panels 1024-byte aligned");
   static_assert(C_DV + HD <= TMEM_COLS, "TMEM budget");
   static_assert(SMEM <= 232448, "shared memory budget");
+  static_assert(BN == 64, "two warpgroups x 32 columns");
 };
 
 template <int HD>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kBBThreads, 1)
     bwdbwd_k_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                     const __grid_constant__ CUtensorMap tm_ddk, const __grid_constant__ CUtensorMap tm_ddv,
                     const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
@@ -353,18 +418,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bar_empty[s], 1);
     }
     mbar_init(&bar_sc_full, 1);
-    mbar_init(&bar_sc_empty, kEwThreads);
-    mbar_init(&bar_ops_full, kEwThreads);
+    mbar_init(&bar_sc_empty, kBBEw);
+    mbar_init(&bar_ops_full, kBBEw);
     mbar_init(&bar_ops_empty, 1);
     mbar_init(&bar_acc, 1);
     mbar_fence_init();
   }
-  if (warp == kWarpMma) tmem_alloc(&tmem_base, G::TMEM_COLS);
+  if (warp == kBBWarpMma) tmem_alloc(&tmem_base, G::TMEM_COLS);
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_base;
 
-  if (warp == kWarpProducer) {
+  if (warp == kBBWarpProducer) {
     // ---------------------- TMA producer (whole warp) -----------------------
     if (lane == 0) {
       tma_prefetch_desc(&tm_k);
@@ -387,7 +452,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int q = q0 + lane + 32 * k;
         const bool v = q < sh.Tq;
         const size_t idx = stat_index(b, h, v ? q : 0, sh.H, sh.Tq);
-        st[k][0] = v ? a.lse[idx] : 0.f;
+        st[k][0] = v ? a.lse[idx] * kLog2e : 0.f;
         st[k][1] = v ? a.delta[idx] : 0.f;
         st[k][2] = v ? a.dd[idx] : 0.f;
         st[k][3] = v ? a.bv[idx] : 0.f;
@@ -420,7 +485,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         drained &= mbar_wait(&bar_full[it % ST], (it / ST) & 1, nullptr);
       if (!drained) raise_error(a.status, &abort_flag, kDevTimeoutDrain);
     }
-  } else if (warp == kWarpMma) {
+  } else if (warp == kBBWarpMma) {
     // ------------------------------ MMA issuer --------------------------------
     if (lane == 0 && n > 0) {
       const uint32_t id_sc = idesc_bf16_f32(kBM, BN, false, false);
@@ -471,77 +536,76 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // --------------------------- elementwise warps ----------------------------
-    const int r = threadIdx.x;  // TMEM lane = key row inside the tile
+    const int wg = warp >> 2;
+    const int r = (warp & 3) * 32 + lane;  // TMEM lane = key row inside the tile
+    const int cb = wg * 32;
     const int key = k0 + r;
     const bool key_ok = key < sh.Tk;
     const float sc = sh.scale, sc2 = sh.scale * kLog2e;
     bool ok = true;
     for (int it = 0; it < n; ++it) {
       const int s = it % ST;
-      const int q0 = (qt_begin + it) * BN;
+      const int qc = (qt_begin + it) * BN + cb;  // first query of this thread's columns
       ok = __all_sync(0xffffffffu, mbar_wait(&bar_sc_full, it & 1, &abort_flag));
-      if (ok && it > 0) ok = __all_sync(0xffffffffu, mbar_wait(&bar_ops_empty, (it - 1) & 1, &abort_flag));
       if (!ok) break;
       tc_fence_after();
-      const float* sv = reinterpret_cast<const float*>(s_ring + s * G::SLOT + 3 * G::STR);
-      const bool need_mask = (q0 + BN > sh.Tq) || (sh.causal && q0 < k0 + kBM - 1);
-#pragma unroll 1
-      for (int c = 0; c < BN / 16; ++c) {
-        uint32_t vs[16], vdds[16], vdp[16], vdpa[16];
-        tmem_row16(tmem, warp, G::C_S + c * 16, vs);
-        tmem_row16(tmem, warp, G::C_DDS + c * 16, vdds);
-        tmem_row16(tmem, warp, G::C_DP + c * 16, vdp);
-        tmem_row16(tmem, warp, G::C_DPA + c * 16, vdpa);
-        tmem_wait_ld();
-        reg_fence16(vs);
-        reg_fence16(vdds);
-        reg_fence16(vdp);
-        reg_fence16(vdpa);
-        float o_ds[16], o_ds2[16], o_ddp[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int col = c * 16 + i;
-          const int q = q0 + col;
-          const float lq = sv[col] * kLog2e;
-          const float dq = sv[BN + col];
-          const float ddq = sv[2 * BN + col];
-          const float bq = sv[3 * BN + col];
-          float s = fmaf(__uint_as_float(vs[i]), sc2, -lq);
-          if (need_mask && (q >= sh.Tq || (sh.causal && q < key))) s = -INFINITY;
-          const float p = ex2(s);
-          const float dds = __uint_as_float(vdds[i]) * sc;
-          const float dp = __uint_as_float(vdp[i]);
-          const float u = dds - ddq;
-          const float ps = p * sc;
-          o_ddp[i] = p * u;
-          o_ds[i] = ps * (dp - dq);
-          const float dp2 = fmaf(-dds, dq, fmaf(dp, u, __uint_as_float(vdpa[i])));
-          o_ds2[i] = ps * (dp2 - bq);
-        }
-        stage_bf16x16(s_ops, r, c, o_ds);
-        stage_bf16x16(s_ops + G::OPS, r, c, o_ds2);
-        stage_bf16x16(s_ops + 2 * G::OPS, r, c, o_ddp);
-      }
+      uint32_t vs[32], vdds[32], vdp[32], vdpa[32];
+      tmem_share32(tmem, warp, G::C_S + cb, vs);
+      tmem_share32(tmem, warp, G::C_DDS + cb, vdds);
+      tmem_share32(tmem, warp, G::C_DP + cb, vdp);
+      tmem_share32(tmem, warp, G::C_DPA + cb, vdpa);
+      tmem_wait_ld();
+      reg_fence32(vs);
+      reg_fence32(vdds);
+      reg_fence32(vdp);
+      reg_fence32(vdpa);
       tc_fence_before();
       mbar_arrive(&bar_sc_empty);
+      if (it > 0) ok = __all_sync(0xffffffffu, mbar_wait(&bar_ops_empty, (it - 1) & 1, &abort_flag));
+      if (!ok) break;
+      const float* sv = reinterpret_cast<const float*>(s_ring + s * G::SLOT + 3 * G::STR) + cb;
+      const bool need_mask = (qc + 32 > sh.Tq) || (sh.causal && qc < key);
+      uint32_t o_ds[16], o_ds2[16], o_ddp[16];
+#pragma unroll
+      for (int i = 0; i < 32; i += 2) {
+        float ddp[2], ds[2], ds2[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int col = i + e;
+          const int q = qc + col;
+          float s = fmaf(__uint_as_float(vs[col]), sc2, -sv[col]);
+          if (need_mask && (q >= sh.Tq || (sh.causal && q < key))) s = -INFINITY;
+          const float p = ex2(s);
+          const float dq = sv[BN + col];
+          const float dds = __uint_as_float(vdds[col]) * sc;
+          const float dp = __uint_as_float(vdp[col]);
+          const float u = dds - sv[2 * BN + col];
+          const float ps = p * sc;
+          ddp[e] = p * u;
+          ds[e] = ps * (dp - dq);
+          const float dp2 = fmaf(-dds, dq, fmaf(dp, u, __uint_as_float(vdpa[col])));
+          ds2[e] = ps * (dp2 - sv[3 * BN + col]);
+        }
+        o_ddp[i / 2] = pack_bf16(ddp[0], ddp[1]);
+        o_ds[i / 2] = pack_bf16(ds[0], ds[1]);
+        o_ds2[i / 2] = pack_bf16(ds2[0], ds2[1]);
+      }
+      stage_packed32(s_ops, r, 4 * wg, o_ds);
+      stage_packed32(s_ops + G::OPS, r, 4 * wg, o_ds2);
+      stage_packed32(s_ops + 2 * G::OPS, r, 4 * wg, o_ddp);
       fence_async_smem();
       mbar_arrive(&bar_ops_full);
     }
     const int skey = key_ok ? key : 0;
-    __nv_bfloat16* dk_row = a.dk2 + row_offset(sh.sk, b, skey, h);
-    __nv_bfloat16* dv_row = a.dv2 + row_offset(sh.sk, b, skey, h);
+    __nv_bfloat16* dst = (wg == 0 ? a.dk2 : a.dv2) + row_offset(sh.sk, b, skey, h);
     if (n == 0) {
       // No query sees these keys (causal with Tk > Tq): the gradients are zero.
-      if (key_ok) {
-        zero_row_global<HD>(dk_row);
-        zero_row_global<HD>(dv_row);
-      }
+      if (key_ok) zero_row_global<HD>(dst);
     } else {
       if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&bar_acc, 0, &abort_flag));
       if (ok) {
         tc_fence_after();
-        tmem_row_to_global<HD>(tmem, warp, G::C_DK, dk_row, key_ok);
-        tmem_row_to_global<HD>(tmem, warp, G::C_DV, dv_row, key_ok);
+        tmem_row_to_global<HD>(tmem, warp, wg == 0 ? G::C_DK : G::C_DV, dst, key_ok);
       } else if (threadIdx.x == 0) {
         raise_error(a.status, &abort_flag, kDevTimeoutMma);
       }
@@ -550,7 +614,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == kWarpMma) tmem_dealloc(tmem, G::TMEM_COLS);
+  if (warp == kBBWarpMma) tmem_dealloc(tmem, G::TMEM_COLS);
 }
 
 template <int HD>
@@ -590,12 +654,12 @@ int launch_bwdbwd_hd(const AttnShape& s, const BwdBwdPtrs& p, int passes, int* s
               status};
   if (passes & kPassQuery) {
     const dim3 gq(s.H, s.B, (s.Tq + kBM - 1) / kBM);
-    bwdbwd_q_kernel<HD><<<gq, kThreads, GQ::SMEM, stream>>>(mq[0], mq[1], mq[2], mq[3], mq[4], mq[5], mq[6], args);
+    bwdbwd_q_kernel<HD><<<gq, kBBThreads, GQ::SMEM, stream>>>(mq[0], mq[1], mq[2], mq[3], mq[4], mq[5], mq[6], args);
     if (cudaGetLastError() != cudaSuccess) return kLaunchFailed;
   }
   if (passes & kPassKey) {
     const dim3 gk(s.H, s.B, (s.Tk + kBM - 1) / kBM);
-    bwdbwd_k_kernel<HD><<<gk, kThreads, GK::SMEM, stream>>>(mk[0], mk[1], mk[2], mk[3], mk[4], mk[5], mk[6], args);
+    bwdbwd_k_kernel<HD><<<gk, kBBThreads, GK::SMEM, stream>>>(mk[0], mk[1], mk[2], mk[3], mk[4], mk[5], mk[6], args);
     if (cudaGetLastError() != cudaSuccess) return kLaunchFailed;
   }
   return kOk;
