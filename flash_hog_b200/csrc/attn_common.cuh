@@ -97,6 +97,55 @@ __device__ __forceinline__ void gemm_ab(uint32_t d, const uint8_t* a, const uint
     umma_bf16(d, desc_k(a, kBM, ks), desc_mn(bm, b_rows, ks), idesc, (acc || ks > 0) ? 1u : 0u);
 }
 
+// ---- precomputed descriptors ----------------------------------------------------
+// A descriptor's low 14 bits hold (shared address >> 4); every operand of a
+// k-step chain differs from the chain's first descriptor by a compile-time
+// offset in those bits, so the issuing thread adds an immediate per k-step.
+
+// Base descriptor of a K-major operand (128B swizzle, 8-row groups 1024 B apart).
+__device__ __forceinline__ uint64_t kdesc(const void* p) { return smem_desc(smem_u32(p), 16, 1024, kSwizzle128B); }
+
+// Base descriptor of an MN-major operand whose 64-column panels are
+// `panel_bytes` apart.
+__device__ __forceinline__ uint64_t mndesc(const void* p, uint32_t panel_bytes) {
+  return smem_desc(smem_u32(p), panel_bytes, 1024, kSwizzle128B);
+}
+
+// Descriptor offset of k-step ks of a K-major operand whose 64-column K panels
+// are PANEL bytes apart: 32 bytes per k-step inside a panel.
+template <int PANEL>
+__device__ __forceinline__ constexpr uint64_t koff(int ks) {
+  return static_cast<uint64_t>((ks >> 2) * (PANEL >> 4) + (ks & 3) * 2);
+}
+
+// Descriptor offset of k-step ks of an MN-major operand: 16 rows of 128 bytes.
+__device__ __forceinline__ constexpr uint64_t mnoff(int ks) { return static_cast<uint64_t>(ks * 128); }
+
+// KSTEPS chained tcgen05.mma into d: A K-major (panels A_PANEL bytes apart);
+// B K-major (panels B_PANEL apart) or MN-major. The first k-step overwrites d
+// unless `acc`.
+template <int KSTEPS, int A_PANEL, int B_PANEL, bool B_MN>
+__device__ __forceinline__ void umma_chain(uint32_t d, uint64_t a0, uint64_t b0, uint32_t idesc, bool acc) {
+#pragma unroll
+  for (int ks = 0; ks < KSTEPS; ++ks)
+    umma_bf16(d, a0 + koff<A_PANEL>(ks), b0 + (B_MN ? mnoff(ks) : koff<B_PANEL>(ks)), idesc,
+              (acc || ks > 0) ? 1u : 0u);
+}
+
+// Loads a pair of BN-row tiles (X then Y) of HD columns into "pair" panels:
+// panel p holds X's rows then Y's rows (2*BN rows of 128 bytes), so the pair is
+// one 2*BN-row K-major operand and each half is an MN-major operand with panel
+// stride 2*BN*128.
+template <int HD>
+__device__ __forceinline__ void tma_pair(uint8_t* dst, const CUtensorMap* mx, const CUtensorMap* my, uint64_t* bar,
+                                         int row0, int bn, int h, int b) {
+#pragma unroll
+  for (int pnl = 0; pnl < HD / 64; ++pnl) {
+    tma_load_4d(dst + pnl * 2 * bn * 128, mx, bar, pnl * 64, row0, h, b);
+    tma_load_4d(dst + pnl * 2 * bn * 128 + bn * 128, my, bar, pnl * 64, row0, h, b);
+  }
+}
+
 // Records the first device-side error of a launch and raises the CTA's abort flag.
 __device__ __forceinline__ void raise_error(int* status, volatile int* abort_flag, int code) {
   *abort_flag = 1;

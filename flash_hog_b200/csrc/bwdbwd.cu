@@ -86,12 +86,15 @@ __device__ __forceinline__ void reg_fence32(uint32_t (&r)[32]) {
 
 template <int HD>
 struct QPass {
-  static constexpr int BN = 64;                 // key rows per streamed tile
-  static constexpr int ST = 3;                  // ring depth
-  static constexpr int RES = kBM * HD * 2;      // one resident bf16 tile
-  static constexpr int STR = BN * HD * 2;       // one streamed bf16 tile
-  static constexpr int SLOT = 4 * STR;          // K | V | ddK | ddV
-  static constexpr int OPS = kBM * BN * 2;      // one bf16 operand panel (dS, dS2, ddP or P)
+  static constexpr int BN = 64;                    // key rows per streamed tile
+  static constexpr int ST = 3;                     // ring depth
+  static constexpr int RES = kBM * HD * 2;         // one resident bf16 tile (panels of 128 rows)
+  static constexpr int RES_PANEL = kBM * 128;
+  static constexpr int STR = BN * HD * 2;          // one streamed bf16 tile
+  static constexpr int PAIR = 2 * STR;             // two streamed tiles as pair panels
+  static constexpr int PAIR_PANEL = 2 * BN * 128;
+  static constexpr int SLOT = 2 * PAIR;            // (K | ddK) pair, (V | ddV) pair
+  static constexpr int OPS = kBM * BN * 2;         // one bf16 operand panel (dS, dS2, ddP or P)
   static constexpr int SMEM = 1024 + 3 * RES + ST * SLOT + 4 * OPS;
   static constexpr int C_S = 0, C_DDS = BN, C_DP = 2 * BN, C_DPA = 3 * BN;
   static constexpr int C_DQ = 4 * BN, C_DDO = 4 * BN + HD;
@@ -100,6 +103,61 @@ struct QPass {
   static_assert(SMEM <= 232448, "shared memory budget");
   static_assert(BN == 64, "two warpgroups x 32 columns");
 };
+
+// Elementwise part of the query-tiled pass for this thread's 32 columns.
+// Stats sweep: accumulates the row partial sums. Second sweep: writes dS, dS2,
+// ddP and P as packed bf16 pairs.
+template <bool MASK>
+__device__ __forceinline__ void q_stats32(const uint32_t (&vs)[32], const uint32_t (&vdds)[32],
+                                          const uint32_t (&vdp)[32], const uint32_t (&vdpa)[32], int kc, int row,
+                                          int tk, int causal, float sc, float sc2, float lg, float& dD, float& r1,
+                                          float& r2, float& r3) {
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    float s = fmaf(__uint_as_float(vs[i]), sc2, -lg);
+    if (MASK && (kc + i >= tk || (causal && kc + i > row))) s = -INFINITY;
+    const float p = ex2(s);
+    const float t = __uint_as_float(vdds[i]) * sc * p;
+    const float dp = __uint_as_float(vdp[i]);
+    dD += t;
+    r3 = fmaf(t, dp, r3);
+    r1 = fmaf(__uint_as_float(vdpa[i]), p, r1);
+    r2 = fmaf(dp, p, r2);
+  }
+}
+
+template <bool MASK>
+__device__ __forceinline__ void q_ops32(const uint32_t (&vs)[32], const uint32_t (&vdds)[32],
+                                        const uint32_t (&vdp)[32], const uint32_t (&vdpa)[32], int kc, int row, int tk,
+                                        int causal, float sc, float sc2, float lg, float dv, float dD, float Bv,
+                                        uint32_t (&o_ds)[16], uint32_t (&o_ds2)[16], uint32_t (&o_ddp)[16],
+                                        uint32_t (&o_p)[16]) {
+  const float nscdv = -sc * dv;
+#pragma unroll
+  for (int i = 0; i < 32; i += 2) {
+    float pp[2], ddp[2], ds[2], ds2[2];
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int c = i + e;
+      float s = fmaf(__uint_as_float(vs[c]), sc2, -lg);
+      if (MASK && (kc + c >= tk || (causal && kc + c > row))) s = -INFINITY;
+      const float p = ex2(s);
+      const float vd = __uint_as_float(vdds[c]);
+      const float dp = __uint_as_float(vdp[c]);
+      const float u = fmaf(vd, sc, -dD);                                   // ddS - dD
+      const float ps = p * sc;
+      pp[e] = p;
+      ddp[e] = p * u;
+      ds[e] = ps * (dp - dv);
+      const float dp2 = fmaf(vd, nscdv, fmaf(dp, u, __uint_as_float(vdpa[c])));  // dPa + dP(ddS-dD) - ddS D
+      ds2[e] = ps * (dp2 - Bv);
+    }
+    o_p[i / 2] = pack_bf16(pp[0], pp[1]);
+    o_ddp[i / 2] = pack_bf16(ddp[0], ddp[1]);
+    o_ds[i / 2] = pack_bf16(ds[0], ds[1]);
+    o_ds2[i / 2] = pack_bf16(ds2[0], ds2[1]);
+  }
+}
 
 template <int HD>
 __global__ void __launch_bounds__(kBBThreads, 1)
@@ -170,10 +228,8 @@ __global__ void __launch_bounds__(kBBThreads, 1)
         const int k0 = (it % n) * BN;
         uint8_t* slot = s_ring + s * G::SLOT;
         mbar_arrive_expect_tx(&bar_full[s], G::SLOT);
-        tma_rows<HD>(slot, &tm_k, &bar_full[s], k0, BN, h, b);
-        tma_rows<HD>(slot + G::STR, &tm_v, &bar_full[s], k0, BN, h, b);
-        tma_rows<HD>(slot + 2 * G::STR, &tm_ddk, &bar_full[s], k0, BN, h, b);
-        tma_rows<HD>(slot + 3 * G::STR, &tm_ddv, &bar_full[s], k0, BN, h, b);
+        tma_pair<HD>(slot, &tm_k, &tm_ddk, &bar_full[s], k0, BN, h, b);
+        tma_pair<HD>(slot + G::PAIR, &tm_v, &tm_ddv, &bar_full[s], k0, BN, h, b);
         issued = it + 1;
       }
       // Every issued copy must land before this CTA's shared memory is released.
@@ -186,10 +242,18 @@ __global__ void __launch_bounds__(kBBThreads, 1)
     // ------------------------------ MMA issuer --------------------------------
     // Iteration it issues the scores of tile it, then the operand products of
     // tile it-1 (second sweep only): the tensor core scores one tile ahead of
-    // the elementwise warps.
+    // the elementwise warps. Products sharing an A operand are one N=128 MMA:
+    //   [S | Q ddK^T] = Q [K ; ddK]^T,  ddS += ddQ K^T,  [dP | dPa] = dO [V ; ddV]^T.
     if (lane == 0) {
-      const uint32_t id_sc = idesc_bf16_f32(kBM, BN, false, false);
+      constexpr int KS = HD / 16, KO = BN / 16;
+      const uint32_t id128 = idesc_bf16_f32(kBM, 2 * BN, false, false);
+      const uint32_t id64 = idesc_bf16_f32(kBM, BN, false, false);
       const uint32_t id_out = idesc_bf16_f32(kBM, HD, false, true);
+      const uint64_t a_q = kdesc(s_q), a_do = kdesc(s_do), a_ddq = kdesc(s_ddq);
+      const uint64_t b_ring = kdesc(s_ring);                       // pair (K | ddK) of slot 0, K-major
+      const uint64_t mn_ring = mndesc(s_ring, G::PAIR_PANEL);      // K of slot 0, MN-major
+      const uint64_t a_ops = kdesc(s_ops);
+      constexpr uint64_t kSlot = G::SLOT >> 4, kPair = G::PAIR >> 4, kHalf = (BN * 128) >> 4, kOps = G::OPS >> 4;
       bool ok = mbar_wait(&bar_res, 0, &abort_flag);
       if (!ok) raise_error(a.status, &abort_flag, kDevTimeoutTmaFull);
       for (int it = 0; ok && it <= total; ++it) {
@@ -206,12 +270,10 @@ __global__ void __launch_bounds__(kBBThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint8_t* slot = s_ring + s * G::SLOT;
-          gemm_abt(tmem + G::C_S, s_q, slot, BN, HD / 16, id_sc, false);                    // S   = Q K^T
-          gemm_abt(tmem + G::C_DDS, s_ddq, slot, BN, HD / 16, id_sc, false);                // ddS = ddQ K^T
-          gemm_abt(tmem + G::C_DDS, s_q, slot + 2 * G::STR, BN, HD / 16, id_sc, true);      //     + Q ddK^T
-          gemm_abt(tmem + G::C_DP, s_do, slot + G::STR, BN, HD / 16, id_sc, false);         // dP  = dO V^T
-          gemm_abt(tmem + G::C_DPA, s_do, slot + 3 * G::STR, BN, HD / 16, id_sc, false);    // dPa = dO ddV^T
+          const uint64_t bk = b_ring + s * kSlot;
+          umma_chain<KS, G::RES_PANEL, G::PAIR_PANEL, false>(tmem + G::C_S, a_q, bk, id128, false);
+          umma_chain<KS, G::RES_PANEL, G::PAIR_PANEL, false>(tmem + G::C_DDS, a_ddq, bk, id64, true);
+          umma_chain<KS, G::RES_PANEL, G::PAIR_PANEL, false>(tmem + G::C_DP, a_do, bk + kPair, id128, false);
           umma_commit(&bar_sc_full);
           if (it < n) umma_commit(&bar_empty[s]);  // stats sweep: slot free once scored
         }
@@ -224,12 +286,13 @@ __global__ void __launch_bounds__(kBBThreads, 1)
           }
           tc_fence_after();
           const int sp = (it - 1) % ST;
-          const uint8_t* slot = s_ring + sp * G::SLOT;
+          const uint64_t mk = mn_ring + sp * kSlot;   // K; ddK = +kHalf; V = +kPair; ddV = +kPair+kHalf
           const bool acc = jp > 0;
-          gemm_ab(tmem + G::C_DQ, s_ops, slot + 2 * G::STR, BN, BN / 16, id_out, acc);              // dQ' += dS ddK
-          gemm_ab(tmem + G::C_DQ, s_ops + G::OPS, slot, BN, BN / 16, id_out, true);               //      + dS2 K
-          gemm_ab(tmem + G::C_DDO, s_ops + 2 * G::OPS, slot + G::STR, BN, BN / 16, id_out, acc);  // ddO += ddP V
-          gemm_ab(tmem + G::C_DDO, s_ops + 3 * G::OPS, slot + 3 * G::STR, BN, BN / 16, id_out, true);  // + P ddV
+          umma_chain<KO, G::OPS, 0, true>(tmem + G::C_DQ, a_ops, mk + kHalf, id_out, acc);               // dQ' += dS ddK
+          umma_chain<KO, G::OPS, 0, true>(tmem + G::C_DQ, a_ops + kOps, mk, id_out, true);               //      + dS2 K
+          umma_chain<KO, G::OPS, 0, true>(tmem + G::C_DDO, a_ops + 2 * kOps, mk + kPair, id_out, acc);   // ddO += ddP V
+          umma_chain<KO, G::OPS, 0, true>(tmem + G::C_DDO, a_ops + 3 * kOps, mk + kPair + kHalf, id_out,
+                                          true);                                                         //      + P ddV
           umma_commit(&bar_ops_empty);
           umma_commit(&bar_empty[sp]);
         }
@@ -270,19 +333,10 @@ __global__ void __launch_bounds__(kBBThreads, 1)
       mbar_arrive(&bar_sc_empty);  // the tensor core may score the next tile now
       const bool need_mask = (kc + 32 > sh.Tk) || (sh.causal && kc + 31 > row);
       if (!sweep2) {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          float s = fmaf(__uint_as_float(vs[i]), sc2, -lg);
-          if (need_mask && (kc + i >= sh.Tk || (sh.causal && kc + i > row))) s = -INFINITY;
-          const float p = ex2(s);
-          const float dds = __uint_as_float(vdds[i]) * sc;
-          const float dp = __uint_as_float(vdp[i]);
-          const float t = dds * p;
-          dD += t;
-          r3 = fmaf(t, dp, r3);
-          r1 = fmaf(__uint_as_float(vdpa[i]), p, r1);
-          r2 = fmaf(dp, p, r2);
-        }
+        if (need_mask)
+          q_stats32<true>(vs, vdds, vdp, vdpa, kc, row, sh.Tk, sh.causal, sc, sc2, lg, dD, r1, r2, r3);
+        else
+          q_stats32<false>(vs, vdds, vdp, vdpa, kc, row, sh.Tk, sh.causal, sc, sc2, lg, dD, r1, r2, r3);
         if (it == n - 1) {
           // Combine the two warpgroups' column halves (same order on both sides).
           red[0][wg][r] = dD;
@@ -299,33 +353,15 @@ __global__ void __launch_bounds__(kBBThreads, 1)
           Bv = r1 - dD * r2 - dv * dD + r3;
         }
       } else {
+        uint32_t o_ds[16], o_ds2[16], o_ddp[16], o_p[16];
+        if (need_mask)
+          q_ops32<true>(vs, vdds, vdp, vdpa, kc, row, sh.Tk, sh.causal, sc, sc2, lg, dv, dD, Bv, o_ds, o_ds2, o_ddp,
+                        o_p);
+        else
+          q_ops32<false>(vs, vdds, vdp, vdpa, kc, row, sh.Tk, sh.causal, sc, sc2, lg, dv, dD, Bv, o_ds, o_ds2,
+                         o_ddp, o_p);
         if (j > 0) ok = __all_sync(0xffffffffu, mbar_wait(&bar_ops_empty, (j - 1) & 1, &abort_flag));
         if (!ok) break;
-        uint32_t o_ds[16], o_ds2[16], o_ddp[16], o_p[16];
-#pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          float pp[2], ddp[2], ds[2], ds2[2];
-#pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int kk = kc + i + e;
-            float s = fmaf(__uint_as_float(vs[i + e]), sc2, -lg);
-            if (need_mask && (kk >= sh.Tk || (sh.causal && kk > row))) s = -INFINITY;
-            const float p = ex2(s);
-            const float dds = __uint_as_float(vdds[i + e]) * sc;
-            const float dp = __uint_as_float(vdp[i + e]);
-            const float u = dds - dD;
-            const float ps = p * sc;
-            pp[e] = p;
-            ddp[e] = p * u;
-            ds[e] = ps * (dp - dv);
-            const float dp2 = fmaf(-dds, dv, fmaf(dp, u, __uint_as_float(vdpa[i + e])));
-            ds2[e] = ps * (dp2 - Bv);
-          }
-          o_p[i / 2] = pack_bf16(pp[0], pp[1]);
-          o_ddp[i / 2] = pack_bf16(ddp[0], ddp[1]);
-          o_ds[i / 2] = pack_bf16(ds[0], ds[1]);
-          o_ds2[i / 2] = pack_bf16(ds2[0], ds2[1]);
-        }
         stage_packed32(s_ops, r, 4 * wg, o_ds);
         stage_packed32(s_ops + G::OPS, r, 4 * wg, o_ds2);
         stage_packed32(s_ops + 2 * G::OPS, r, 4 * wg, o_ddp);
@@ -363,12 +399,15 @@ __global__ void __launch_bounds__(kBBThreads, 1)
 
 template <int HD>
 struct KPass {
-  static constexpr int BN = 64;                 // query rows per streamed tile
+  static constexpr int BN = 64;                    // query rows per streamed tile
   static constexpr int ST = 3;
   static constexpr int RES = kBM * HD * 2;
+  static constexpr int RES_PANEL = kBM * 128;
   static constexpr int STR = BN * HD * 2;
-  static constexpr int VEC = BN * 4;            // one fp32 statistic per streamed query
-  static constexpr int SLOT = 3 * STR + 4 * VEC;  // Q | dO | ddQ | L, D, dD, B
+  static constexpr int PAIR = 2 * STR;
+  static constexpr int PAIR_PANEL = 2 * BN * 128;
+  static constexpr int VEC = BN * 4;               // one fp32 statistic per streamed query
+  static constexpr int SLOT = PAIR + STR + 4 * VEC;  // (Q | ddQ) pair, dO, then L, D, dD, B
   static constexpr int OPS = kBM * BN * 2;
   static constexpr int SMEM = 1024 + 4 * RES + ST * SLOT + 3 * OPS;
   static constexpr int C_S = 0, C_DDS = BN, C_DP = 2 * BN, C_DPA = 3 * BN;
@@ -379,6 +418,37 @@ struct KPass {
   static_assert(SMEM <= 232448, "shared memory budget");
   static_assert(BN == 64, "two warpgroups x 32 columns");
 };
+
+template <bool MASK>
+__device__ __forceinline__ void k_ops32(const uint32_t (&vs)[32], const uint32_t (&vdds)[32],
+                                        const uint32_t (&vdp)[32], const uint32_t (&vdpa)[32], const float* sv,
+                                        int qc, int key, int tq, int causal, float sc, float sc2,
+                                        uint32_t (&o_ds)[16], uint32_t (&o_ds2)[16], uint32_t (&o_ddp)[16]) {
+  constexpr int BN = 64;
+#pragma unroll
+  for (int i = 0; i < 32; i += 2) {
+    float ddp[2], ds[2], ds2[2];
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int c = i + e;
+      float s = fmaf(__uint_as_float(vs[c]), sc2, -sv[c]);
+      if (MASK && (qc + c >= tq || (causal && qc + c < key))) s = -INFINITY;
+      const float p = ex2(s);
+      const float dq = sv[BN + c];
+      const float vd = __uint_as_float(vdds[c]);
+      const float dp = __uint_as_float(vdp[c]);
+      const float u = fmaf(vd, sc, -sv[2 * BN + c]);
+      const float ps = p * sc;
+      ddp[e] = p * u;
+      ds[e] = ps * (dp - dq);
+      const float dp2 = fmaf(-vd * sc, dq, fmaf(dp, u, __uint_as_float(vdpa[c])));
+      ds2[e] = ps * (dp2 - sv[3 * BN + c]);
+    }
+    o_ddp[i / 2] = pack_bf16(ddp[0], ddp[1]);
+    o_ds[i / 2] = pack_bf16(ds[0], ds[1]);
+    o_ds2[i / 2] = pack_bf16(ds2[0], ds2[1]);
+  }
+}
 
 template <int HD>
 __global__ void __launch_bounds__(kBBThreads, 1)
@@ -464,17 +534,16 @@ __global__ void __launch_bounds__(kBBThreads, 1)
         break;
       }
       uint8_t* slot = s_ring + s * G::SLOT;
-      float* sv = reinterpret_cast<float*>(slot + 3 * G::STR);
+      float* sv = reinterpret_cast<float*>(slot + G::PAIR + G::STR);
 #pragma unroll
       for (int k = 0; k < 2; ++k)
 #pragma unroll
         for (int m = 0; m < 4; ++m) sv[m * BN + lane + 32 * k] = st[k][m];
       __syncwarp();
       if (lane == 0) {
-        mbar_arrive_expect_tx(&bar_full[s], 3 * G::STR);
-        tma_rows<HD>(slot, &tm_q, &bar_full[s], q0, BN, h, b);
-        tma_rows<HD>(slot + G::STR, &tm_do, &bar_full[s], q0, BN, h, b);
-        tma_rows<HD>(slot + 2 * G::STR, &tm_ddq, &bar_full[s], q0, BN, h, b);
+        mbar_arrive_expect_tx(&bar_full[s], G::PAIR + G::STR);
+        tma_pair<HD>(slot, &tm_q, &tm_ddq, &bar_full[s], q0, BN, h, b);
+        tma_rows<HD>(slot + G::PAIR, &tm_do, &bar_full[s], q0, BN, h, b);
       }
       __syncwarp();
       issued = it + 1;
@@ -487,9 +556,19 @@ __global__ void __launch_bounds__(kBBThreads, 1)
     }
   } else if (warp == kBBWarpMma) {
     // ------------------------------ MMA issuer --------------------------------
+    //   [S^T | K ddQ^T] = K [Q ; ddQ]^T,  ddS^T += ddK Q^T,  dP^T = V dO^T,  dPa^T = ddV dO^T
     if (lane == 0 && n > 0) {
-      const uint32_t id_sc = idesc_bf16_f32(kBM, BN, false, false);
+      constexpr int KS = HD / 16, KO = BN / 16;
+      const uint32_t id128 = idesc_bf16_f32(kBM, 2 * BN, false, false);
+      const uint32_t id64 = idesc_bf16_f32(kBM, BN, false, false);
       const uint32_t id_out = idesc_bf16_f32(kBM, HD, false, true);
+      const uint64_t a_k = kdesc(s_k), a_v = kdesc(s_v), a_ddk = kdesc(s_ddk), a_ddv = kdesc(s_ddv);
+      const uint64_t b_ring = kdesc(s_ring);                          // pair (Q | ddQ) of slot 0
+      const uint64_t b_do = kdesc(s_ring + G::PAIR);                  // dO of slot 0
+      const uint64_t mn_ring = mndesc(s_ring, G::PAIR_PANEL);         // Q of slot 0, MN-major
+      const uint64_t mn_do = mndesc(s_ring + G::PAIR, BN * 128);      // dO of slot 0, MN-major
+      const uint64_t a_ops = kdesc(s_ops);
+      constexpr uint64_t kSlot = G::SLOT >> 4, kHalf = (BN * 128) >> 4, kOps = G::OPS >> 4;
       bool ok = mbar_wait(&bar_res, 0, &abort_flag);
       if (!ok) raise_error(a.status, &abort_flag, kDevTimeoutTmaFull);
       for (int it = 0; ok && it <= n; ++it) {
@@ -506,12 +585,11 @@ __global__ void __launch_bounds__(kBBThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint8_t* slot = s_ring + s * G::SLOT;
-          gemm_abt(tmem + G::C_S, s_k, slot, BN, HD / 16, id_sc, false);                  // S^T   = K Q^T
-          gemm_abt(tmem + G::C_DDS, s_k, slot + 2 * G::STR, BN, HD / 16, id_sc, false);   // ddS^T = K ddQ^T
-          gemm_abt(tmem + G::C_DDS, s_ddk, slot, BN, HD / 16, id_sc, true);               //       + ddK Q^T
-          gemm_abt(tmem + G::C_DP, s_v, slot + G::STR, BN, HD / 16, id_sc, false);        // dP^T  = V dO^T
-          gemm_abt(tmem + G::C_DPA, s_ddv, slot + G::STR, BN, HD / 16, id_sc, false);     // dPa^T = ddV dO^T
+          const uint64_t bq = b_ring + s * kSlot, bo = b_do + s * kSlot;
+          umma_chain<KS, G::RES_PANEL, G::PAIR_PANEL, false>(tmem + G::C_S, a_k, bq, id128, false);
+          umma_chain<KS, G::RES_PANEL, G::PAIR_PANEL, false>(tmem + G::C_DDS, a_ddk, bq, id64, true);
+          umma_chain<KS, G::RES_PANEL, BN * 128, false>(tmem + G::C_DP, a_v, bo, id64, false);
+          umma_chain<KS, G::RES_PANEL, BN * 128, false>(tmem + G::C_DPA, a_ddv, bo, id64, false);
           umma_commit(&bar_sc_full);
         }
         const int jp = it - 1;
@@ -523,11 +601,11 @@ __global__ void __launch_bounds__(kBBThreads, 1)
           }
           tc_fence_after();
           const int sp = jp % ST;
-          const uint8_t* slot = s_ring + sp * G::SLOT;
+          const uint64_t mq = mn_ring + sp * kSlot, mo = mn_do + sp * kSlot;
           const bool acc = jp > 0;
-          gemm_ab(tmem + G::C_DK, s_ops, slot + 2 * G::STR, BN, BN / 16, id_out, acc);            // dK' += dS^T ddQ
-          gemm_ab(tmem + G::C_DK, s_ops + G::OPS, slot, BN, BN / 16, id_out, true);             //      + dS2^T Q
-          gemm_ab(tmem + G::C_DV, s_ops + 2 * G::OPS, slot + G::STR, BN, BN / 16, id_out, acc);  // dV' += ddP^T dO
+          umma_chain<KO, G::OPS, 0, true>(tmem + G::C_DK, a_ops, mq + kHalf, id_out, acc);       // dK' += dS^T ddQ
+          umma_chain<KO, G::OPS, 0, true>(tmem + G::C_DK, a_ops + kOps, mq, id_out, true);       //      + dS2^T Q
+          umma_chain<KO, G::OPS, 0, true>(tmem + G::C_DV, a_ops + 2 * kOps, mo, id_out, acc);    // dV' += ddP^T dO
           umma_commit(&bar_ops_empty);
           umma_commit(&bar_empty[sp]);
         }
@@ -561,35 +639,15 @@ __global__ void __launch_bounds__(kBBThreads, 1)
       reg_fence32(vdpa);
       tc_fence_before();
       mbar_arrive(&bar_sc_empty);
-      if (it > 0) ok = __all_sync(0xffffffffu, mbar_wait(&bar_ops_empty, (it - 1) & 1, &abort_flag));
-      if (!ok) break;
-      const float* sv = reinterpret_cast<const float*>(s_ring + s * G::SLOT + 3 * G::STR) + cb;
+      const float* sv = reinterpret_cast<const float*>(s_ring + s * G::SLOT + G::PAIR + G::STR) + cb;
       const bool need_mask = (qc + 32 > sh.Tq) || (sh.causal && qc < key);
       uint32_t o_ds[16], o_ds2[16], o_ddp[16];
-#pragma unroll
-      for (int i = 0; i < 32; i += 2) {
-        float ddp[2], ds[2], ds2[2];
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int col = i + e;
-          const int q = qc + col;
-          float s = fmaf(__uint_as_float(vs[col]), sc2, -sv[col]);
-          if (need_mask && (q >= sh.Tq || (sh.causal && q < key))) s = -INFINITY;
-          const float p = ex2(s);
-          const float dq = sv[BN + col];
-          const float dds = __uint_as_float(vdds[col]) * sc;
-          const float dp = __uint_as_float(vdp[col]);
-          const float u = dds - sv[2 * BN + col];
-          const float ps = p * sc;
-          ddp[e] = p * u;
-          ds[e] = ps * (dp - dq);
-          const float dp2 = fmaf(-dds, dq, fmaf(dp, u, __uint_as_float(vdpa[col])));
-          ds2[e] = ps * (dp2 - sv[3 * BN + col]);
-        }
-        o_ddp[i / 2] = pack_bf16(ddp[0], ddp[1]);
-        o_ds[i / 2] = pack_bf16(ds[0], ds[1]);
-        o_ds2[i / 2] = pack_bf16(ds2[0], ds2[1]);
-      }
+      if (need_mask)
+        k_ops32<true>(vs, vdds, vdp, vdpa, sv, qc, key, sh.Tq, sh.causal, sc, sc2, o_ds, o_ds2, o_ddp);
+      else
+        k_ops32<false>(vs, vdds, vdp, vdpa, sv, qc, key, sh.Tq, sh.causal, sc, sc2, o_ds, o_ds2, o_ddp);
+      if (it > 0) ok = __all_sync(0xffffffffu, mbar_wait(&bar_ops_empty, (it - 1) & 1, &abort_flag));
+      if (!ok) break;
       stage_packed32(s_ops, r, 4 * wg, o_ds);
       stage_packed32(s_ops + G::OPS, r, 4 * wg, o_ds2);
       stage_packed32(s_ops + 2 * G::OPS, r, 4 * wg, o_ddp);
