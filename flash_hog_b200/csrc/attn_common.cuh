@@ -132,6 +132,15 @@ __device__ __forceinline__ void umma_chain(uint32_t d, uint64_t a0, uint64_t b0,
               (acc || ks > 0) ? 1u : 0u);
 }
 
+// KSTEPS chained tcgen05.mma with A in TMEM (8 columns per k-step from a_tmem)
+// and B an MN-major shared-memory operand.
+template <int KSTEPS>
+__device__ __forceinline__ void umma_chain_ts(uint32_t d, uint32_t a_tmem, uint64_t b0, uint32_t idesc, bool acc) {
+#pragma unroll
+  for (int ks = 0; ks < KSTEPS; ++ks)
+    umma_bf16_ts(d, a_tmem + 8 * ks, b0 + mnoff(ks), idesc, (acc || ks > 0) ? 1u : 0u);
+}
+
 // Loads a pair of BN-row tiles (X then Y) of HD columns into "pair" panels:
 // panel p holds X's rows then Y's rows (2*BN rows of 128 bytes), so the pair is
 // one 2*BN-row K-major operand and each half is an MN-major operand with panel
@@ -183,11 +192,11 @@ __device__ __forceinline__ void stage_bf16x16(uint8_t* panel, int r, int c16, co
                pack_bf16(v[12], v[13]), pack_bf16(v[14], v[15]));
 }
 
-// Drains the TMEM accumulator columns [col, col+HD) of this thread's lane to a
-// bf16 row in global memory.
+// Drains the TMEM accumulator columns [col, col+HD) of this thread's lane,
+// times `mult`, to a bf16 row in global memory.
 template <int HD>
 __device__ __forceinline__ void tmem_row_to_global(uint32_t tmem, int warp, int col, __nv_bfloat16* dst,
-                                                   bool write) {
+                                                   bool write, float mult = 1.f) {
 #pragma unroll
   for (int c = 0; c < HD; c += 16) {
     uint32_t r[16];
@@ -196,7 +205,7 @@ __device__ __forceinline__ void tmem_row_to_global(uint32_t tmem, int warp, int 
     reg_fence16(r);
     float v[16];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]) * mult;
     if (write) store_bf16x16(dst + c, v);
   }
 }

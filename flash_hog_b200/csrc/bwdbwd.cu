@@ -48,28 +48,30 @@ struct BBArgs {
 // CTA layout shared by both passes
 // ----------------------------------------------------------------------------------
 //
-// 10 warps. Warps 0-7 are two elementwise warpgroups: thread (warp, lane) owns
-// TMEM lane 32*(warp%4)+lane (one resident row) and warpgroup w = warp/4 owns
-// columns [32w, 32w+32) of every 64-column streamed tile. Each thread loads its
-// 32-column share of all four score tiles into registers and releases the
-// score TMEM at once, so the tensor core computes the next tile's scores while
-// the registers of this tile are turned into operand panels. Warp 8 is the
-// TMA producer, warp 9 allocates TMEM and issues every tcgen05.mma.
+// 10 warps. Warp 0 allocates TMEM and issues every tcgen05.mma, warp 1 is the
+// TMA producer, warps 2-9 are two elementwise warpgroups: thread (warp, lane)
+// owns TMEM lane 32*(warp%4)+lane (one resident row) and warpgroup
+// w = (warp-2)/4 owns columns [32w, 32w+32) of every 64-row streamed tile.
+// Each thread loads its 32-column share of all four score tiles into registers
+// and releases the score buffer at once. The bf16 operands it produces (dS,
+// dS2, ddP, P) go back to TMEM with tcgen05.st and are read there as the A
+// operand of the accumulating MMAs. The MMA thread is event-driven: it issues
+// a tile's operand products as soon as its operands are in TMEM, and the next
+// tile's scores as soon as a score buffer and the tile's TMA data are ready.
 constexpr int kBBThreads = 320;
-constexpr int kBBEw = 256;
-constexpr int kBBWarpProducer = 8;
-constexpr int kBBWarpMma = 9;
+constexpr int kBBEwWarps = 8;  // elementwise arrivals are one per warp
+constexpr int kBBWarpMma = 0;
+constexpr int kBBWarpProducer = 1;
+constexpr int kBBFirstEwWarp = 2;
 
-// Writes 16 packed bf16 pairs (32 bf16) into 16-byte chunks (c, c+1, c+2, c+3)
-// of row r of a 128B-swizzled panel.
-__device__ __forceinline__ void stage_packed32(uint8_t* panel, int r, int c, const uint32_t (&v)[16]) {
-  const uint32_t base = smem_u32(panel);
-#pragma unroll
-  for (int k = 0; k < 4; ++k)
-    st_shared_v4(base + sw128_offset(r, c + k), v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+// All lanes of the warp have finished their TMEM / shared-memory accesses; one lane arrives.
+__device__ __forceinline__ void warp_arrive(uint64_t* bar) {
+  tc_fence_before();
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) mbar_arrive(bar);
 }
 
-// Loads this thread's 32-column share (two x16 loads) of a score tile.
+// This thread's 32-column share of a score tile (two x16 loads).
 __device__ __forceinline__ void tmem_share32(uint32_t tmem, int warp, int col, uint32_t (&r)[32]) {
   tmem_ld16(tmem + tmem_lane_base(warp & 3) + col, *reinterpret_cast<uint32_t(*)[16]>(&r[0]));
   tmem_ld16(tmem + tmem_lane_base(warp & 3) + col + 16, *reinterpret_cast<uint32_t(*)[16]>(&r[16]));
@@ -80,6 +82,16 @@ __device__ __forceinline__ void reg_fence32(uint32_t (&r)[32]) {
   for (int i = 0; i < 32; ++i) asm volatile("" : "+r"(r[i])::"memory");
 }
 
+// Bounded idle step of the event-driven MMA issuer: false once the CTA aborts
+// or the issuer has made no progress for kWaitLimitNs.
+__device__ __forceinline__ bool issuer_idle(unsigned long long& since, volatile int* abort_flag) {
+  __nanosleep(32);
+  if (*abort_flag) return false;
+  const unsigned long long now = global_timer_ns();
+  if (since == 0) since = now;
+  return now - since <= kWaitLimitNs;
+}
+
 // ----------------------------------------------------------------------------------
 // query-tiled pass
 // ----------------------------------------------------------------------------------
@@ -87,26 +99,28 @@ __device__ __forceinline__ void reg_fence32(uint32_t (&r)[32]) {
 template <int HD>
 struct QPass {
   static constexpr int BN = 64;                    // key rows per streamed tile
-  static constexpr int ST = 3;                     // ring depth
+  static constexpr int ST = 4;                     // ring depth
   static constexpr int RES = kBM * HD * 2;         // one resident bf16 tile (panels of 128 rows)
   static constexpr int RES_PANEL = kBM * 128;
   static constexpr int STR = BN * HD * 2;          // one streamed bf16 tile
   static constexpr int PAIR = 2 * STR;             // two streamed tiles as pair panels
   static constexpr int PAIR_PANEL = 2 * BN * 128;
   static constexpr int SLOT = 2 * PAIR;            // (K | ddK) pair, (V | ddV) pair
-  static constexpr int OPS = kBM * BN * 2;         // one bf16 operand panel (dS, dS2, ddP or P)
-  static constexpr int SMEM = 1024 + 3 * RES + ST * SLOT + 4 * OPS;
-  static constexpr int C_S = 0, C_DDS = BN, C_DP = 2 * BN, C_DPA = 3 * BN;
-  static constexpr int C_DQ = 4 * BN, C_DDO = 4 * BN + HD;
+  static constexpr int SMEM = 1024 + 3 * RES + ST * SLOT;
+  // TMEM: score buffer 0 [0, 256); accumulators dQ', ddO; bf16 operands dS,
+  // dS2, ddP, P (BN/2 packed columns each). During the stats sweep the
+  // accumulator and operand columns hold score buffer 1.
+  static constexpr int C_S = 0, C_DDS = BN, C_DP = 2 * BN, C_DPA = 3 * BN, SCORE_COLS = 4 * BN;
+  static constexpr int C_DQ = SCORE_COLS, C_DDO = SCORE_COLS + HD, C_OPS = SCORE_COLS + 2 * HD;
+  static constexpr int OPS_COLS = BN / 2;
   static constexpr int TMEM_COLS = 512;
-  static_assert(C_DDO + HD <= TMEM_COLS, "TMEM budget");
+  static_assert(C_OPS + 4 * OPS_COLS <= TMEM_COLS, "TMEM budget");
+  static_assert(2 * SCORE_COLS <= TMEM_COLS, "stats sweep double-buffers the scores");
   static_assert(SMEM <= 232448, "shared memory budget");
   static_assert(BN == 64, "two warpgroups x 32 columns");
 };
 
-// Elementwise part of the query-tiled pass for this thread's 32 columns.
-// Stats sweep: accumulates the row partial sums. Second sweep: writes dS, dS2,
-// ddP and P as packed bf16 pairs.
+// Stats sweep: row partial sums over this thread's 32 columns.
 template <bool MASK>
 __device__ __forceinline__ void q_stats32(const uint32_t (&vs)[32], const uint32_t (&vdds)[32],
                                           const uint32_t (&vdp)[32], const uint32_t (&vdpa)[32], int kc, int row,
@@ -126,6 +140,9 @@ __device__ __forceinline__ void q_stats32(const uint32_t (&vs)[32], const uint32
   }
 }
 
+// Second sweep: packed bf16 pairs of dS/scale, dS2/scale, ddP and P for this
+// thread's 32 columns (the softmax scale of dS and dS2 is applied to dQ' in
+// the epilogue instead of per element).
 template <bool MASK>
 __device__ __forceinline__ void q_ops32(const uint32_t (&vs)[32], const uint32_t (&vdds)[32],
                                         const uint32_t (&vdp)[32], const uint32_t (&vdpa)[32], int kc, int row, int tk,
@@ -144,13 +161,12 @@ __device__ __forceinline__ void q_ops32(const uint32_t (&vs)[32], const uint32_t
       const float p = ex2(s);
       const float vd = __uint_as_float(vdds[c]);
       const float dp = __uint_as_float(vdp[c]);
-      const float u = fmaf(vd, sc, -dD);                                   // ddS - dD
-      const float ps = p * sc;
+      const float u = fmaf(vd, sc, -dD);                                            // ddS - dD
       pp[e] = p;
       ddp[e] = p * u;
-      ds[e] = ps * (dp - dv);
-      const float dp2 = fmaf(vd, nscdv, fmaf(dp, u, __uint_as_float(vdpa[c])));  // dPa + dP(ddS-dD) - ddS D
-      ds2[e] = ps * (dp2 - Bv);
+      ds[e] = p * (dp - dv);
+      const float dp2 = fmaf(vd, nscdv, fmaf(dp, u, __uint_as_float(vdpa[c])));   // dPa + dP(ddS-dD) - ddS D
+      ds2[e] = p * (dp2 - Bv);
     }
     o_p[i / 2] = pack_bf16(pp[0], pp[1]);
     o_ddp[i / 2] = pack_bf16(ddp[0], ddp[1]);
@@ -173,9 +189,8 @@ __global__ void __launch_bounds__(kBBThreads, 1)
   uint8_t* s_do = s_q + G::RES;
   uint8_t* s_ddq = s_do + G::RES;
   uint8_t* s_ring = s_ddq + G::RES;
-  uint8_t* s_ops = s_ring + ST * G::SLOT;  // dS | dS2 | ddP | P
   __shared__ uint64_t bar_res, bar_full[ST], bar_empty[ST];
-  __shared__ uint64_t bar_sc_full, bar_sc_empty, bar_ops_full, bar_ops_empty, bar_acc, bar_red;
+  __shared__ uint64_t bar_sc_full[2], bar_sc_empty[2], bar_ops_full, bar_ops_empty, bar_acc, bar_red;
   __shared__ float red[4][2][kBM];  // stats-sweep partial sums: statistic, warpgroup, row
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
@@ -188,6 +203,10 @@ __global__ void __launch_bounds__(kBBThreads, 1)
   const int kv_end = sh.causal ? min(sh.Tk, q0 + kBM) : sh.Tk;
   const int n = (kv_end + BN - 1) / BN;  // key tiles per sweep (>= 1)
   const int total = 2 * n;
+  // Score buffer of tile `it` and how many earlier tiles used that buffer:
+  // the stats sweep alternates buffers 0 and 1, the second sweep uses buffer 0.
+  auto buf_of = [n](int it) { return it < n ? (it & 1) : 0; };
+  auto use_of = [n](int it) { return it < n ? (it >> 1) : ((n + 1) >> 1) + (it - n); };
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
@@ -196,12 +215,14 @@ __global__ void __launch_bounds__(kBBThreads, 1)
       mbar_init(&bar_full[s], 1);
       mbar_init(&bar_empty[s], 1);
     }
-    mbar_init(&bar_sc_full, 1);
-    mbar_init(&bar_sc_empty, kBBEw);
-    mbar_init(&bar_ops_full, kBBEw);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bar_sc_full[i], 1);
+      mbar_init(&bar_sc_empty[i], kBBEwWarps);
+    }
+    mbar_init(&bar_ops_full, kBBEwWarps);
     mbar_init(&bar_ops_empty, 1);
     mbar_init(&bar_acc, 1);
-    mbar_init(&bar_red, kBBEw);
+    mbar_init(&bar_red, kBBEwWarps);
     mbar_fence_init();
   }
   if (warp == kBBWarpMma) tmem_alloc(&tmem_base, G::TMEM_COLS);
@@ -239,70 +260,68 @@ __global__ void __launch_bounds__(kBBThreads, 1)
       if (!drained) raise_error(a.status, &abort_flag, kDevTimeoutDrain);
     }
   } else if (warp == kBBWarpMma) {
-    // ------------------------------ MMA issuer --------------------------------
-    // Iteration it issues the scores of tile it, then the operand products of
-    // tile it-1 (second sweep only): the tensor core scores one tile ahead of
-    // the elementwise warps. Products sharing an A operand are one N=128 MMA:
-    //   [S | Q ddK^T] = Q [K ; ddK]^T,  ddS += ddQ K^T,  [dP | dPa] = dO [V ; ddV]^T.
+    // --------------------------- event-driven MMA issuer --------------------------
+    // Scores, products sharing an A operand as one N=128 MMA:
+    //   [S | Q ddK^T] = Q [K ; ddK]^T,  ddS += ddQ K^T,  [dP | dPa] = dO [V ; ddV]^T
+    // Operand products of a second-sweep tile (A in TMEM):
+    //   dQ'/scale += dS ddK + dS2 K,  ddO += ddP V + P ddV
     if (lane == 0) {
-      constexpr int KS = HD / 16, KO = BN / 16;
+      constexpr int KS = HD / 16, KO = BN / 16, OC = G::OPS_COLS;
       const uint32_t id128 = idesc_bf16_f32(kBM, 2 * BN, false, false);
       const uint32_t id64 = idesc_bf16_f32(kBM, BN, false, false);
       const uint32_t id_out = idesc_bf16_f32(kBM, HD, false, true);
       const uint64_t a_q = kdesc(s_q), a_do = kdesc(s_do), a_ddq = kdesc(s_ddq);
       const uint64_t b_ring = kdesc(s_ring);                       // pair (K | ddK) of slot 0, K-major
       const uint64_t mn_ring = mndesc(s_ring, G::PAIR_PANEL);      // K of slot 0, MN-major
-      const uint64_t a_ops = kdesc(s_ops);
-      constexpr uint64_t kSlot = G::SLOT >> 4, kPair = G::PAIR >> 4, kHalf = (BN * 128) >> 4, kOps = G::OPS >> 4;
+      constexpr uint64_t kSlot = G::SLOT >> 4, kPair = G::PAIR >> 4, kHalf = (BN * 128) >> 4;
+      const uint32_t t_ops = tmem + G::C_OPS;
       bool ok = mbar_wait(&bar_res, 0, &abort_flag);
       if (!ok) raise_error(a.status, &abort_flag, kDevTimeoutTmaFull);
-      for (int it = 0; ok && it <= total; ++it) {
-        if (it < total) {
-          const int s = it % ST;
-          if (!mbar_wait(&bar_full[s], (it / ST) & 1, &abort_flag)) {
-            raise_error(a.status, &abort_flag, kDevTimeoutTmaFull);
-            ok = false;
-            break;
-          }
-          if (it > 0 && !mbar_wait(&bar_sc_empty, (it - 1) & 1, &abort_flag)) {
-            raise_error(a.status, &abort_flag, kDevTimeoutEpilogue);
-            ok = false;
-            break;
-          }
+      int ns = 0, np = n;  // next tile to score, next second-sweep tile to multiply out
+      unsigned long long idle_since = 0;
+      while (ok && (ns < total || np < total)) {
+        if (np < ns && mbar_test(&bar_ops_full, (np - n) & 1)) {
           tc_fence_after();
-          const uint64_t bk = b_ring + s * kSlot;
-          umma_chain<KS, G::RES_PANEL, G::PAIR_PANEL, false>(tmem + G::C_S, a_q, bk, id128, false);
-          umma_chain<KS, G::RES_PANEL, G::PAIR_PANEL, false>(tmem + G::C_DDS, a_ddq, bk, id64, true);
-          umma_chain<KS, G::RES_PANEL, G::PAIR_PANEL, false>(tmem + G::C_DP, a_do, bk + kPair, id128, false);
-          umma_commit(&bar_sc_full);
-          if (it < n) umma_commit(&bar_empty[s]);  // stats sweep: slot free once scored
-        }
-        const int jp = it - 1 - n;  // second-sweep tile whose operand panels are due
-        if (jp >= 0) {
-          if (!mbar_wait(&bar_ops_full, jp & 1, &abort_flag)) {
-            raise_error(a.status, &abort_flag, kDevTimeoutEpilogue);
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const int sp = (it - 1) % ST;
+          const int sp = np % ST;
           const uint64_t mk = mn_ring + sp * kSlot;   // K; ddK = +kHalf; V = +kPair; ddV = +kPair+kHalf
-          const bool acc = jp > 0;
-          umma_chain<KO, G::OPS, 0, true>(tmem + G::C_DQ, a_ops, mk + kHalf, id_out, acc);               // dQ' += dS ddK
-          umma_chain<KO, G::OPS, 0, true>(tmem + G::C_DQ, a_ops + kOps, mk, id_out, true);               //      + dS2 K
-          umma_chain<KO, G::OPS, 0, true>(tmem + G::C_DDO, a_ops + 2 * kOps, mk + kPair, id_out, acc);   // ddO += ddP V
-          umma_chain<KO, G::OPS, 0, true>(tmem + G::C_DDO, a_ops + 3 * kOps, mk + kPair + kHalf, id_out,
-                                          true);                                                         //      + P ddV
+          const bool acc = np > n;
+          umma_chain_ts<KO>(tmem + G::C_DQ, t_ops, mk + kHalf, id_out, acc);
+          umma_chain_ts<KO>(tmem + G::C_DQ, t_ops + OC, mk, id_out, true);
+          umma_chain_ts<KO>(tmem + G::C_DDO, t_ops + 2 * OC, mk + kPair, id_out, acc);
+          umma_chain_ts<KO>(tmem + G::C_DDO, t_ops + 3 * OC, mk + kPair + kHalf, id_out, true);
           umma_commit(&bar_ops_empty);
           umma_commit(&bar_empty[sp]);
+          ++np;
+          idle_since = 0;
+          continue;
+        }
+        if (ns < total) {
+          const int s = ns % ST, sb = buf_of(ns), u = use_of(ns);
+          if (mbar_test(&bar_full[s], (ns / ST) & 1) && (u == 0 || mbar_test(&bar_sc_empty[sb], (u - 1) & 1))) {
+            tc_fence_after();
+            const uint64_t bk = b_ring + s * kSlot;
+            const uint32_t tb = tmem + sb * G::SCORE_COLS;
+            umma_chain<KS, G::RES_PANEL, G::PAIR_PANEL, false>(tb + G::C_S, a_q, bk, id128, false);
+            umma_chain<KS, G::RES_PANEL, G::PAIR_PANEL, false>(tb + G::C_DDS, a_ddq, bk, id64, true);
+            umma_chain<KS, G::RES_PANEL, G::PAIR_PANEL, false>(tb + G::C_DP, a_do, bk + kPair, id128, false);
+            umma_commit(&bar_sc_full[sb]);
+            if (ns < n) umma_commit(&bar_empty[s]);  // stats sweep: slot free once scored
+            ++ns;
+            idle_since = 0;
+            continue;
+          }
+        }
+        if (!issuer_idle(idle_since, &abort_flag)) {
+          raise_error(a.status, &abort_flag, kDevTimeoutEpilogue);
+          ok = false;
         }
       }
       if (ok) umma_commit(&bar_acc);
     }
   } else {
     // --------------------------- elementwise warps ----------------------------
-    const int wg = warp >> 2;                // column half of every tile
-    const int r = (warp & 3) * 32 + lane;    // TMEM lane = query row inside the tile
+    const int wg = (warp - kBBFirstEwWarp) >> 2;  // column half of every tile
+    const int r = (warp & 3) * 32 + lane;         // TMEM lane = query row inside the tile
     const int cb = wg * 32;
     const int row = q0 + r;
     const bool row_ok = row < sh.Tq;
@@ -316,21 +335,22 @@ __global__ void __launch_bounds__(kBBThreads, 1)
       const int j = it % n;
       const bool sweep2 = it >= n;
       const int kc = j * BN + cb;  // first key of this thread's columns
-      ok = __all_sync(0xffffffffu, mbar_wait(&bar_sc_full, it & 1, &abort_flag));
+      const int sb = buf_of(it);
+      ok = __all_sync(0xffffffffu, mbar_wait(&bar_sc_full[sb], use_of(it) & 1, &abort_flag));
       if (!ok) break;
       tc_fence_after();
+      const uint32_t tb = tmem + sb * G::SCORE_COLS;
       uint32_t vs[32], vdds[32], vdp[32], vdpa[32];
-      tmem_share32(tmem, warp, G::C_S + cb, vs);
-      tmem_share32(tmem, warp, G::C_DDS + cb, vdds);
-      tmem_share32(tmem, warp, G::C_DP + cb, vdp);
-      tmem_share32(tmem, warp, G::C_DPA + cb, vdpa);
+      tmem_share32(tb, warp, G::C_S + cb, vs);
+      tmem_share32(tb, warp, G::C_DDS + cb, vdds);
+      tmem_share32(tb, warp, G::C_DP + cb, vdp);
+      tmem_share32(tb, warp, G::C_DPA + cb, vdpa);
       tmem_wait_ld();
       reg_fence32(vs);
       reg_fence32(vdds);
       reg_fence32(vdp);
       reg_fence32(vdpa);
-      tc_fence_before();
-      mbar_arrive(&bar_sc_empty);  // the tensor core may score the next tile now
+      warp_arrive(&bar_sc_empty[sb]);  // the tensor core may reuse this score buffer now
       const bool need_mask = (kc + 32 > sh.Tk) || (sh.causal && kc + 31 > row);
       if (!sweep2) {
         if (need_mask)
@@ -343,7 +363,7 @@ __global__ void __launch_bounds__(kBBThreads, 1)
           red[1][wg][r] = r1;
           red[2][wg][r] = r2;
           red[3][wg][r] = r3;
-          mbar_arrive(&bar_red);
+          warp_arrive(&bar_red);
           ok = __all_sync(0xffffffffu, mbar_wait(&bar_red, 0, &abort_flag));
           if (!ok) break;
           dD = red[0][0][r] + red[0][1][r];
@@ -362,12 +382,15 @@ __global__ void __launch_bounds__(kBBThreads, 1)
                          o_ddp, o_p);
         if (j > 0) ok = __all_sync(0xffffffffu, mbar_wait(&bar_ops_empty, (j - 1) & 1, &abort_flag));
         if (!ok) break;
-        stage_packed32(s_ops, r, 4 * wg, o_ds);
-        stage_packed32(s_ops + G::OPS, r, 4 * wg, o_ds2);
-        stage_packed32(s_ops + 2 * G::OPS, r, 4 * wg, o_ddp);
-        stage_packed32(s_ops + 3 * G::OPS, r, 4 * wg, o_p);
-        fence_async_smem();
-        mbar_arrive(&bar_ops_full);
+        tc_fence_after();
+        // This warpgroup's 32 keys are packed columns [16 wg, 16 wg + 16) of each operand.
+        const uint32_t to = tmem + tmem_lane_base(warp & 3) + G::C_OPS + 16 * wg;
+        tmem_st16(to, o_ds);
+        tmem_st16(to + G::OPS_COLS, o_ds2);
+        tmem_st16(to + 2 * G::OPS_COLS, o_ddp);
+        tmem_st16(to + 3 * G::OPS_COLS, o_p);
+        tmem_wait_st();
+        warp_arrive(&bar_ops_full);
       }
     }
     if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&bar_acc, 0, &abort_flag));
@@ -375,7 +398,7 @@ __global__ void __launch_bounds__(kBBThreads, 1)
       tc_fence_after();
       const int srow = row_ok ? row : 0;
       if (wg == 0) {
-        tmem_row_to_global<HD>(tmem, warp, G::C_DQ, a.dq2 + row_offset(sh.sq, b, srow, h), row_ok);
+        tmem_row_to_global<HD>(tmem, warp, G::C_DQ, a.dq2 + row_offset(sh.sq, b, srow, h), row_ok, sc);
         if (row_ok) {
           a.dd[vi] = dD;
           a.bv[vi] = Bv;
@@ -383,7 +406,7 @@ __global__ void __launch_bounds__(kBBThreads, 1)
       } else {
         tmem_row_to_global<HD>(tmem, warp, G::C_DDO, a.ddo + row_offset(sh.sq, b, srow, h), row_ok);
       }
-    } else if (threadIdx.x == 0) {
+    } else if (threadIdx.x == kBBFirstEwWarp * 32) {
       raise_error(a.status, &abort_flag, kDevTimeoutMma);
     }
   }
@@ -400,7 +423,7 @@ __global__ void __launch_bounds__(kBBThreads, 1)
 template <int HD>
 struct KPass {
   static constexpr int BN = 64;                    // query rows per streamed tile
-  static constexpr int ST = 3;
+  static constexpr int ST = 4;
   static constexpr int RES = kBM * HD * 2;
   static constexpr int RES_PANEL = kBM * 128;
   static constexpr int STR = BN * HD * 2;
@@ -408,17 +431,20 @@ struct KPass {
   static constexpr int PAIR_PANEL = 2 * BN * 128;
   static constexpr int VEC = BN * 4;               // one fp32 statistic per streamed query
   static constexpr int SLOT = PAIR + STR + 4 * VEC;  // (Q | ddQ) pair, dO, then L, D, dD, B
-  static constexpr int OPS = kBM * BN * 2;
-  static constexpr int SMEM = 1024 + 4 * RES + ST * SLOT + 3 * OPS;
+  static constexpr int SMEM = 1024 + 4 * RES + ST * SLOT;
+  // TMEM: scores, accumulators dK', dV', bf16 operands dS^T, dS2^T, ddP^T (A of the MMAs).
   static constexpr int C_S = 0, C_DDS = BN, C_DP = 2 * BN, C_DPA = 3 * BN;
-  static constexpr int C_DK = 4 * BN, C_DV = 4 * BN + HD;
+  static constexpr int C_DK = 4 * BN, C_DV = 4 * BN + HD, C_OPS = 4 * BN + 2 * HD;
+  static constexpr int OPS_COLS = BN / 2;
   static constexpr int TMEM_COLS = 512;
   static_assert(SLOT % 1024 == 0, "slots must keep panels 1024-byte aligned");
-  static_assert(C_DV + HD <= TMEM_COLS, "TMEM budget");
+  static_assert(C_OPS + 3 * OPS_COLS <= TMEM_COLS, "TMEM budget");
   static_assert(SMEM <= 232448, "shared memory budget");
   static_assert(BN == 64, "two warpgroups x 32 columns");
 };
 
+// Packed bf16 pairs of dS^T/scale, dS2^T/scale and ddP^T for this thread's 32
+// query columns (the scale of dS, dS2 is applied to dK' in the epilogue).
 template <bool MASK>
 __device__ __forceinline__ void k_ops32(const uint32_t (&vs)[32], const uint32_t (&vdds)[32],
                                         const uint32_t (&vdp)[32], const uint32_t (&vdpa)[32], const float* sv,
@@ -438,11 +464,10 @@ __device__ __forceinline__ void k_ops32(const uint32_t (&vs)[32], const uint32_t
       const float vd = __uint_as_float(vdds[c]);
       const float dp = __uint_as_float(vdp[c]);
       const float u = fmaf(vd, sc, -sv[2 * BN + c]);
-      const float ps = p * sc;
       ddp[e] = p * u;
-      ds[e] = ps * (dp - dq);
+      ds[e] = p * (dp - dq);
       const float dp2 = fmaf(-vd * sc, dq, fmaf(dp, u, __uint_as_float(vdpa[c])));
-      ds2[e] = ps * (dp2 - sv[3 * BN + c]);
+      ds2[e] = p * (dp2 - sv[3 * BN + c]);
     }
     o_ddp[i / 2] = pack_bf16(ddp[0], ddp[1]);
     o_ds[i / 2] = pack_bf16(ds[0], ds[1]);
@@ -465,7 +490,6 @@ __global__ void __launch_bounds__(kBBThreads, 1)
   uint8_t* s_ddk = s_v + G::RES;
   uint8_t* s_ddv = s_ddk + G::RES;
   uint8_t* s_ring = s_ddv + G::RES;
-  uint8_t* s_ops = s_ring + ST * G::SLOT;  // dS^T | dS2^T | ddP^T
   __shared__ uint64_t bar_res, bar_full[ST], bar_empty[ST];
   __shared__ uint64_t bar_sc_full, bar_sc_empty, bar_ops_full, bar_ops_empty, bar_acc;
   __shared__ uint32_t tmem_base;
@@ -488,8 +512,8 @@ __global__ void __launch_bounds__(kBBThreads, 1)
       mbar_init(&bar_empty[s], 1);
     }
     mbar_init(&bar_sc_full, 1);
-    mbar_init(&bar_sc_empty, kBBEw);
-    mbar_init(&bar_ops_full, kBBEw);
+    mbar_init(&bar_sc_empty, kBBEwWarps);
+    mbar_init(&bar_ops_full, kBBEwWarps);
     mbar_init(&bar_ops_empty, 1);
     mbar_init(&bar_acc, 1);
     mbar_fence_init();
@@ -555,10 +579,11 @@ __global__ void __launch_bounds__(kBBThreads, 1)
       if (!drained) raise_error(a.status, &abort_flag, kDevTimeoutDrain);
     }
   } else if (warp == kBBWarpMma) {
-    // ------------------------------ MMA issuer --------------------------------
+    // --------------------------- event-driven MMA issuer --------------------------
     //   [S^T | K ddQ^T] = K [Q ; ddQ]^T,  ddS^T += ddK Q^T,  dP^T = V dO^T,  dPa^T = ddV dO^T
+    //   dK'/scale += dS^T ddQ + dS2^T Q,  dV' += ddP^T dO   (A in TMEM)
     if (lane == 0 && n > 0) {
-      constexpr int KS = HD / 16, KO = BN / 16;
+      constexpr int KS = HD / 16, KO = BN / 16, OC = G::OPS_COLS;
       const uint32_t id128 = idesc_bf16_f32(kBM, 2 * BN, false, false);
       const uint32_t id64 = idesc_bf16_f32(kBM, BN, false, false);
       const uint32_t id_out = idesc_bf16_f32(kBM, HD, false, true);
@@ -567,54 +592,52 @@ __global__ void __launch_bounds__(kBBThreads, 1)
       const uint64_t b_do = kdesc(s_ring + G::PAIR);                  // dO of slot 0
       const uint64_t mn_ring = mndesc(s_ring, G::PAIR_PANEL);         // Q of slot 0, MN-major
       const uint64_t mn_do = mndesc(s_ring + G::PAIR, BN * 128);      // dO of slot 0, MN-major
-      const uint64_t a_ops = kdesc(s_ops);
-      constexpr uint64_t kSlot = G::SLOT >> 4, kHalf = (BN * 128) >> 4, kOps = G::OPS >> 4;
+      constexpr uint64_t kSlot = G::SLOT >> 4, kHalf = (BN * 128) >> 4;
+      const uint32_t t_ops = tmem + G::C_OPS;
       bool ok = mbar_wait(&bar_res, 0, &abort_flag);
       if (!ok) raise_error(a.status, &abort_flag, kDevTimeoutTmaFull);
-      for (int it = 0; ok && it <= n; ++it) {
-        if (it < n) {
-          const int s = it % ST;
-          if (!mbar_wait(&bar_full[s], (it / ST) & 1, &abort_flag)) {
-            raise_error(a.status, &abort_flag, kDevTimeoutTmaFull);
-            ok = false;
-            break;
-          }
-          if (it > 0 && !mbar_wait(&bar_sc_empty, (it - 1) & 1, &abort_flag)) {
-            raise_error(a.status, &abort_flag, kDevTimeoutEpilogue);
-            ok = false;
-            break;
-          }
+      int ns = 0, np = 0;  // next tile to score, next tile to multiply out
+      unsigned long long idle_since = 0;
+      while (ok && np < n) {
+        if (np < ns && mbar_test(&bar_ops_full, np & 1)) {
           tc_fence_after();
-          const uint64_t bq = b_ring + s * kSlot, bo = b_do + s * kSlot;
-          umma_chain<KS, G::RES_PANEL, G::PAIR_PANEL, false>(tmem + G::C_S, a_k, bq, id128, false);
-          umma_chain<KS, G::RES_PANEL, G::PAIR_PANEL, false>(tmem + G::C_DDS, a_ddk, bq, id64, true);
-          umma_chain<KS, G::RES_PANEL, BN * 128, false>(tmem + G::C_DP, a_v, bo, id64, false);
-          umma_chain<KS, G::RES_PANEL, BN * 128, false>(tmem + G::C_DPA, a_ddv, bo, id64, false);
-          umma_commit(&bar_sc_full);
-        }
-        const int jp = it - 1;
-        if (jp >= 0) {
-          if (!mbar_wait(&bar_ops_full, jp & 1, &abort_flag)) {
-            raise_error(a.status, &abort_flag, kDevTimeoutEpilogue);
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const int sp = jp % ST;
+          const int sp = np % ST;
           const uint64_t mq = mn_ring + sp * kSlot, mo = mn_do + sp * kSlot;
-          const bool acc = jp > 0;
-          umma_chain<KO, G::OPS, 0, true>(tmem + G::C_DK, a_ops, mq + kHalf, id_out, acc);       // dK' += dS^T ddQ
-          umma_chain<KO, G::OPS, 0, true>(tmem + G::C_DK, a_ops + kOps, mq, id_out, true);       //      + dS2^T Q
-          umma_chain<KO, G::OPS, 0, true>(tmem + G::C_DV, a_ops + 2 * kOps, mo, id_out, acc);    // dV' += ddP^T dO
+          const bool acc = np > 0;
+          umma_chain_ts<KO>(tmem + G::C_DK, t_ops, mq + kHalf, id_out, acc);
+          umma_chain_ts<KO>(tmem + G::C_DK, t_ops + OC, mq, id_out, true);
+          umma_chain_ts<KO>(tmem + G::C_DV, t_ops + 2 * OC, mo, id_out, acc);
           umma_commit(&bar_ops_empty);
           umma_commit(&bar_empty[sp]);
+          ++np;
+          idle_since = 0;
+          continue;
+        }
+        if (ns < n) {
+          const int s = ns % ST;
+          if (mbar_test(&bar_full[s], (ns / ST) & 1) && (ns == 0 || mbar_test(&bar_sc_empty, (ns - 1) & 1))) {
+            tc_fence_after();
+            const uint64_t bq = b_ring + s * kSlot, bo = b_do + s * kSlot;
+            umma_chain<KS, G::RES_PANEL, G::PAIR_PANEL, false>(tmem + G::C_S, a_k, bq, id128, false);
+            umma_chain<KS, G::RES_PANEL, G::PAIR_PANEL, false>(tmem + G::C_DDS, a_ddk, bq, id64, true);
+            umma_chain<KS, G::RES_PANEL, BN * 128, false>(tmem + G::C_DP, a_v, bo, id64, false);
+            umma_chain<KS, G::RES_PANEL, BN * 128, false>(tmem + G::C_DPA, a_ddv, bo, id64, false);
+            umma_commit(&bar_sc_full);
+            ++ns;
+            idle_since = 0;
+            continue;
+          }
+        }
+        if (!issuer_idle(idle_since, &abort_flag)) {
+          raise_error(a.status, &abort_flag, kDevTimeoutEpilogue);
+          ok = false;
         }
       }
       if (ok) umma_commit(&bar_acc);
     }
   } else {
     // --------------------------- elementwise warps ----------------------------
-    const int wg = warp >> 2;
+    const int wg = (warp - kBBFirstEwWarp) >> 2;
     const int r = (warp & 3) * 32 + lane;  // TMEM lane = key row inside the tile
     const int cb = wg * 32;
     const int key = k0 + r;
@@ -637,8 +660,7 @@ __global__ void __launch_bounds__(kBBThreads, 1)
       reg_fence32(vdds);
       reg_fence32(vdp);
       reg_fence32(vdpa);
-      tc_fence_before();
-      mbar_arrive(&bar_sc_empty);
+      warp_arrive(&bar_sc_empty);
       const float* sv = reinterpret_cast<const float*>(s_ring + s * G::SLOT + G::PAIR + G::STR) + cb;
       const bool need_mask = (qc + 32 > sh.Tq) || (sh.causal && qc < key);
       uint32_t o_ds[16], o_ds2[16], o_ddp[16];
@@ -648,11 +670,13 @@ __global__ void __launch_bounds__(kBBThreads, 1)
         k_ops32<false>(vs, vdds, vdp, vdpa, sv, qc, key, sh.Tq, sh.causal, sc, sc2, o_ds, o_ds2, o_ddp);
       if (it > 0) ok = __all_sync(0xffffffffu, mbar_wait(&bar_ops_empty, (it - 1) & 1, &abort_flag));
       if (!ok) break;
-      stage_packed32(s_ops, r, 4 * wg, o_ds);
-      stage_packed32(s_ops + G::OPS, r, 4 * wg, o_ds2);
-      stage_packed32(s_ops + 2 * G::OPS, r, 4 * wg, o_ddp);
-      fence_async_smem();
-      mbar_arrive(&bar_ops_full);
+      tc_fence_after();
+      const uint32_t to = tmem + tmem_lane_base(warp & 3) + G::C_OPS + 16 * wg;
+      tmem_st16(to, o_ds);
+      tmem_st16(to + G::OPS_COLS, o_ds2);
+      tmem_st16(to + 2 * G::OPS_COLS, o_ddp);
+      tmem_wait_st();
+      warp_arrive(&bar_ops_full);
     }
     const int skey = key_ok ? key : 0;
     __nv_bfloat16* dst = (wg == 0 ? a.dk2 : a.dv2) + row_offset(sh.sk, b, skey, h);
@@ -663,8 +687,8 @@ __global__ void __launch_bounds__(kBBThreads, 1)
       if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&bar_acc, 0, &abort_flag));
       if (ok) {
         tc_fence_after();
-        tmem_row_to_global<HD>(tmem, warp, wg == 0 ? G::C_DK : G::C_DV, dst, key_ok);
-      } else if (threadIdx.x == 0) {
+        tmem_row_to_global<HD>(tmem, warp, wg == 0 ? G::C_DK : G::C_DV, dst, key_ok, wg == 0 ? sc : 1.f);
+      } else if (threadIdx.x == kBBFirstEwWarp * 32) {
         raise_error(a.status, &abort_flag, kDevTimeoutMma);
       }
     }
