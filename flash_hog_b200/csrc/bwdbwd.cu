@@ -48,21 +48,25 @@ struct BBArgs {
 // CTA layout shared by both passes
 // ----------------------------------------------------------------------------------
 //
-// 10 warps. Warp 0 allocates TMEM and issues every tcgen05.mma, warp 1 is the
-// TMA producer, warps 2-9 are two elementwise warpgroups: thread (warp, lane)
-// owns TMEM lane 32*(warp%4)+lane (one resident row) and warpgroup
-// w = (warp-2)/4 owns columns [32w, 32w+32) of every 64-row streamed tile.
-// Each thread loads its 32-column share of all four score tiles into registers
-// and releases the score buffer at once. The bf16 operands it produces (dS,
-// dS2, ddP, P) go back to TMEM with tcgen05.st and are read there as the A
-// operand of the accumulating MMAs. The MMA thread is event-driven: it issues
-// a tile's operand products as soon as its operands are in TMEM, and the next
-// tile's scores as soon as a score buffer and the tile's TMA data are ready.
-constexpr int kBBThreads = 320;
+// 11 warps. Warp 0 allocates TMEM and issues the score MMAs, warp 1 issues the
+// accumulating (operand) MMAs, warp 2 is the TMA producer, warps 3-10 are two
+// elementwise warpgroups: thread (warp, lane) owns TMEM lane 32*(warp%4)+lane
+// (one resident row) and warpgroup w = (warp-3)/4 owns columns [32w, 32w+32)
+// of every 64-row streamed tile. TMEM lane quadrants pin the elementwise warps
+// to all four schedulers, and their arithmetic starves a co-resident issuing
+// thread; two issuers on different schedulers halve that exposure and let the
+// score MMAs of the next tile and the operand MMAs of this tile be issued
+// independently, each as soon as its inputs are ready.
+// Each elementwise thread loads its 32-column share of all four score tiles
+// into registers and releases the score buffer at once. The bf16 operands it
+// produces (dS, dS2, ddP, P) go back to TMEM with tcgen05.st and are read there
+// as the A operand of the accumulating MMAs.
+constexpr int kBBThreads = 352;
 constexpr int kBBEwWarps = 8;  // elementwise arrivals are one per warp
-constexpr int kBBWarpMma = 0;
-constexpr int kBBWarpProducer = 1;
-constexpr int kBBFirstEwWarp = 2;
+constexpr int kBBWarpMma = 0;      // score MMAs; TMEM allocation
+constexpr int kBBWarpMmaOut = 1;   // operand (accumulating) MMAs
+constexpr int kBBWarpProducer = 2;
+constexpr int kBBFirstEwWarp = 3;
 
 // All lanes of the warp have finished their TMEM / shared-memory accesses; one lane arrives.
 __device__ __forceinline__ void warp_arrive(uint64_t* bar) {
@@ -80,16 +84,6 @@ __device__ __forceinline__ void tmem_share32(uint32_t tmem, int warp, int col, u
 __device__ __forceinline__ void reg_fence32(uint32_t (&r)[32]) {
 #pragma unroll
   for (int i = 0; i < 32; ++i) asm volatile("" : "+r"(r[i])::"memory");
-}
-
-// Bounded idle step of the event-driven MMA issuer: false once the CTA aborts
-// or the issuer has made no progress for kWaitLimitNs.
-__device__ __forceinline__ bool issuer_idle(unsigned long long& since, volatile int* abort_flag) {
-  __nanosleep(32);
-  if (*abort_flag) return false;
-  const unsigned long long now = global_timer_ns();
-  if (since == 0) since = now;
-  return now - since <= kWaitLimitNs;
 }
 
 // ----------------------------------------------------------------------------------
@@ -260,61 +254,64 @@ __global__ void __launch_bounds__(kBBThreads, 1)
       if (!drained) raise_error(a.status, &abort_flag, kDevTimeoutDrain);
     }
   } else if (warp == kBBWarpMma) {
-    // --------------------------- event-driven MMA issuer --------------------------
-    // Scores, products sharing an A operand as one N=128 MMA:
+    // ------------------------------ score MMA issuer ------------------------------
+    // Products sharing an A operand are one N=128 MMA:
     //   [S | Q ddK^T] = Q [K ; ddK]^T,  ddS += ddQ K^T,  [dP | dPa] = dO [V ; ddV]^T
-    // Operand products of a second-sweep tile (A in TMEM):
-    //   dQ'/scale += dS ddK + dS2 K,  ddO += ddP V + P ddV
     if (lane == 0) {
-      constexpr int KS = HD / 16, KO = BN / 16, OC = G::OPS_COLS;
+      constexpr int KS = HD / 16;
       const uint32_t id128 = idesc_bf16_f32(kBM, 2 * BN, false, false);
       const uint32_t id64 = idesc_bf16_f32(kBM, BN, false, false);
-      const uint32_t id_out = idesc_bf16_f32(kBM, HD, false, true);
       const uint64_t a_q = kdesc(s_q), a_do = kdesc(s_do), a_ddq = kdesc(s_ddq);
-      const uint64_t b_ring = kdesc(s_ring);                       // pair (K | ddK) of slot 0, K-major
-      const uint64_t mn_ring = mndesc(s_ring, G::PAIR_PANEL);      // K of slot 0, MN-major
-      constexpr uint64_t kSlot = G::SLOT >> 4, kPair = G::PAIR >> 4, kHalf = (BN * 128) >> 4;
-      const uint32_t t_ops = tmem + G::C_OPS;
+      const uint64_t b_ring = kdesc(s_ring);  // pair (K | ddK) of slot 0, K-major
+      constexpr uint64_t kSlot = G::SLOT >> 4, kPair = G::PAIR >> 4;
       bool ok = mbar_wait(&bar_res, 0, &abort_flag);
       if (!ok) raise_error(a.status, &abort_flag, kDevTimeoutTmaFull);
-      int ns = 0, np = n;  // next tile to score, next second-sweep tile to multiply out
-      unsigned long long idle_since = 0;
-      while (ok && (ns < total || np < total)) {
-        if (np < ns && mbar_test(&bar_ops_full, (np - n) & 1)) {
-          tc_fence_after();
-          const int sp = np % ST;
-          const uint64_t mk = mn_ring + sp * kSlot;   // K; ddK = +kHalf; V = +kPair; ddV = +kPair+kHalf
-          const bool acc = np > n;
-          umma_chain_ts<KO>(tmem + G::C_DQ, t_ops, mk + kHalf, id_out, acc);
-          umma_chain_ts<KO>(tmem + G::C_DQ, t_ops + OC, mk, id_out, true);
-          umma_chain_ts<KO>(tmem + G::C_DDO, t_ops + 2 * OC, mk + kPair, id_out, acc);
-          umma_chain_ts<KO>(tmem + G::C_DDO, t_ops + 3 * OC, mk + kPair + kHalf, id_out, true);
-          umma_commit(&bar_ops_empty);
-          umma_commit(&bar_empty[sp]);
-          ++np;
-          idle_since = 0;
-          continue;
+      for (int it = 0; ok && it < total; ++it) {
+        const int s = it % ST, sb = buf_of(it), u = use_of(it);
+        if (!mbar_wait(&bar_full[s], (it / ST) & 1, &abort_flag)) {
+          raise_error(a.status, &abort_flag, kDevTimeoutTmaFull);
+          break;
         }
-        if (ns < total) {
-          const int s = ns % ST, sb = buf_of(ns), u = use_of(ns);
-          if (mbar_test(&bar_full[s], (ns / ST) & 1) && (u == 0 || mbar_test(&bar_sc_empty[sb], (u - 1) & 1))) {
-            tc_fence_after();
-            const uint64_t bk = b_ring + s * kSlot;
-            const uint32_t tb = tmem + sb * G::SCORE_COLS;
-            umma_chain<KS, G::RES_PANEL, G::PAIR_PANEL, false>(tb + G::C_S, a_q, bk, id128, false);
-            umma_chain<KS, G::RES_PANEL, G::PAIR_PANEL, false>(tb + G::C_DDS, a_ddq, bk, id64, true);
-            umma_chain<KS, G::RES_PANEL, G::PAIR_PANEL, false>(tb + G::C_DP, a_do, bk + kPair, id128, false);
-            umma_commit(&bar_sc_full[sb]);
-            if (ns < n) umma_commit(&bar_empty[s]);  // stats sweep: slot free once scored
-            ++ns;
-            idle_since = 0;
-            continue;
-          }
+        if (u > 0 && !mbar_wait(&bar_sc_empty[sb], (u - 1) & 1, &abort_flag)) {
+          raise_error(a.status, &abort_flag, kDevTimeoutEpilogue);
+          break;
         }
-        if (!issuer_idle(idle_since, &abort_flag)) {
+        tc_fence_after();
+        const uint64_t bk = b_ring + s * kSlot;
+        const uint32_t tb = tmem + sb * G::SCORE_COLS;
+        umma_chain<KS, G::RES_PANEL, G::PAIR_PANEL, false>(tb + G::C_S, a_q, bk, id128, false);
+        umma_chain<KS, G::RES_PANEL, G::PAIR_PANEL, false>(tb + G::C_DDS, a_ddq, bk, id64, true);
+        umma_chain<KS, G::RES_PANEL, G::PAIR_PANEL, false>(tb + G::C_DP, a_do, bk + kPair, id128, false);
+        umma_commit(&bar_sc_full[sb]);
+        if (it < n) umma_commit(&bar_empty[s]);  // stats sweep: slot free once scored
+      }
+    }
+  } else if (warp == kBBWarpMmaOut) {
+    // ----------------------------- operand MMA issuer -----------------------------
+    // Second-sweep tile j, A in TMEM:  dQ'/scale += dS ddK + dS2 K,  ddO += ddP V + P ddV
+    if (lane == 0) {
+      constexpr int KO = BN / 16, OC = G::OPS_COLS;
+      const uint32_t id_out = idesc_bf16_f32(kBM, HD, false, true);
+      const uint64_t mn_ring = mndesc(s_ring, G::PAIR_PANEL);  // K of slot 0, MN-major
+      constexpr uint64_t kSlot = G::SLOT >> 4, kPair = G::PAIR >> 4, kHalf = (BN * 128) >> 4;
+      const uint32_t t_ops = tmem + G::C_OPS;
+      bool ok = true;
+      for (int j = 0; j < n; ++j) {
+        if (!mbar_wait(&bar_ops_full, j & 1, &abort_flag)) {
           raise_error(a.status, &abort_flag, kDevTimeoutEpilogue);
           ok = false;
+          break;
         }
+        tc_fence_after();
+        const int sp = (n + j) % ST;
+        const uint64_t mk = mn_ring + sp * kSlot;  // K; ddK = +kHalf; V = +kPair; ddV = +kPair+kHalf
+        const bool acc = j > 0;
+        umma_chain_ts<KO>(tmem + G::C_DQ, t_ops, mk + kHalf, id_out, acc);
+        umma_chain_ts<KO>(tmem + G::C_DQ, t_ops + OC, mk, id_out, true);
+        umma_chain_ts<KO>(tmem + G::C_DDO, t_ops + 2 * OC, mk + kPair, id_out, acc);
+        umma_chain_ts<KO>(tmem + G::C_DDO, t_ops + 3 * OC, mk + kPair + kHalf, id_out, true);
+        umma_commit(&bar_ops_empty);
+        umma_commit(&bar_empty[sp]);
       }
       if (ok) umma_commit(&bar_acc);
     }
@@ -579,59 +576,63 @@ __global__ void __launch_bounds__(kBBThreads, 1)
       if (!drained) raise_error(a.status, &abort_flag, kDevTimeoutDrain);
     }
   } else if (warp == kBBWarpMma) {
-    // --------------------------- event-driven MMA issuer --------------------------
+    // ------------------------------ score MMA issuer ------------------------------
     //   [S^T | K ddQ^T] = K [Q ; ddQ]^T,  ddS^T += ddK Q^T,  dP^T = V dO^T,  dPa^T = ddV dO^T
-    //   dK'/scale += dS^T ddQ + dS2^T Q,  dV' += ddP^T dO   (A in TMEM)
     if (lane == 0 && n > 0) {
-      constexpr int KS = HD / 16, KO = BN / 16, OC = G::OPS_COLS;
+      constexpr int KS = HD / 16;
       const uint32_t id128 = idesc_bf16_f32(kBM, 2 * BN, false, false);
       const uint32_t id64 = idesc_bf16_f32(kBM, BN, false, false);
-      const uint32_t id_out = idesc_bf16_f32(kBM, HD, false, true);
       const uint64_t a_k = kdesc(s_k), a_v = kdesc(s_v), a_ddk = kdesc(s_ddk), a_ddv = kdesc(s_ddv);
-      const uint64_t b_ring = kdesc(s_ring);                          // pair (Q | ddQ) of slot 0
-      const uint64_t b_do = kdesc(s_ring + G::PAIR);                  // dO of slot 0
-      const uint64_t mn_ring = mndesc(s_ring, G::PAIR_PANEL);         // Q of slot 0, MN-major
-      const uint64_t mn_do = mndesc(s_ring + G::PAIR, BN * 128);      // dO of slot 0, MN-major
-      constexpr uint64_t kSlot = G::SLOT >> 4, kHalf = (BN * 128) >> 4;
-      const uint32_t t_ops = tmem + G::C_OPS;
+      const uint64_t b_ring = kdesc(s_ring);          // pair (Q | ddQ) of slot 0
+      const uint64_t b_do = kdesc(s_ring + G::PAIR);  // dO of slot 0
+      constexpr uint64_t kSlot = G::SLOT >> 4;
       bool ok = mbar_wait(&bar_res, 0, &abort_flag);
       if (!ok) raise_error(a.status, &abort_flag, kDevTimeoutTmaFull);
-      int ns = 0, np = 0;  // next tile to score, next tile to multiply out
-      unsigned long long idle_since = 0;
-      while (ok && np < n) {
-        if (np < ns && mbar_test(&bar_ops_full, np & 1)) {
-          tc_fence_after();
-          const int sp = np % ST;
-          const uint64_t mq = mn_ring + sp * kSlot, mo = mn_do + sp * kSlot;
-          const bool acc = np > 0;
-          umma_chain_ts<KO>(tmem + G::C_DK, t_ops, mq + kHalf, id_out, acc);
-          umma_chain_ts<KO>(tmem + G::C_DK, t_ops + OC, mq, id_out, true);
-          umma_chain_ts<KO>(tmem + G::C_DV, t_ops + 2 * OC, mo, id_out, acc);
-          umma_commit(&bar_ops_empty);
-          umma_commit(&bar_empty[sp]);
-          ++np;
-          idle_since = 0;
-          continue;
+      for (int it = 0; ok && it < n; ++it) {
+        const int s = it % ST;
+        if (!mbar_wait(&bar_full[s], (it / ST) & 1, &abort_flag)) {
+          raise_error(a.status, &abort_flag, kDevTimeoutTmaFull);
+          break;
         }
-        if (ns < n) {
-          const int s = ns % ST;
-          if (mbar_test(&bar_full[s], (ns / ST) & 1) && (ns == 0 || mbar_test(&bar_sc_empty, (ns - 1) & 1))) {
-            tc_fence_after();
-            const uint64_t bq = b_ring + s * kSlot, bo = b_do + s * kSlot;
-            umma_chain<KS, G::RES_PANEL, G::PAIR_PANEL, false>(tmem + G::C_S, a_k, bq, id128, false);
-            umma_chain<KS, G::RES_PANEL, G::PAIR_PANEL, false>(tmem + G::C_DDS, a_ddk, bq, id64, true);
-            umma_chain<KS, G::RES_PANEL, BN * 128, false>(tmem + G::C_DP, a_v, bo, id64, false);
-            umma_chain<KS, G::RES_PANEL, BN * 128, false>(tmem + G::C_DPA, a_ddv, bo, id64, false);
-            umma_commit(&bar_sc_full);
-            ++ns;
-            idle_since = 0;
-            continue;
-          }
+        if (it > 0 && !mbar_wait(&bar_sc_empty, (it - 1) & 1, &abort_flag)) {
+          raise_error(a.status, &abort_flag, kDevTimeoutEpilogue);
+          break;
         }
-        if (!issuer_idle(idle_since, &abort_flag)) {
+        tc_fence_after();
+        const uint64_t bq = b_ring + s * kSlot, bo = b_do + s * kSlot;
+        umma_chain<KS, G::RES_PANEL, G::PAIR_PANEL, false>(tmem + G::C_S, a_k, bq, id128, false);
+        umma_chain<KS, G::RES_PANEL, G::PAIR_PANEL, false>(tmem + G::C_DDS, a_ddk, bq, id64, true);
+        umma_chain<KS, G::RES_PANEL, BN * 128, false>(tmem + G::C_DP, a_v, bo, id64, false);
+        umma_chain<KS, G::RES_PANEL, BN * 128, false>(tmem + G::C_DPA, a_ddv, bo, id64, false);
+        umma_commit(&bar_sc_full);
+      }
+    }
+  } else if (warp == kBBWarpMmaOut) {
+    // ----------------------------- operand MMA issuer -----------------------------
+    //   dK'/scale += dS^T ddQ + dS2^T Q,  dV' += ddP^T dO   (A in TMEM)
+    if (lane == 0 && n > 0) {
+      constexpr int KO = BN / 16, OC = G::OPS_COLS;
+      const uint32_t id_out = idesc_bf16_f32(kBM, HD, false, true);
+      const uint64_t mn_ring = mndesc(s_ring, G::PAIR_PANEL);     // Q of slot 0, MN-major
+      const uint64_t mn_do = mndesc(s_ring + G::PAIR, BN * 128);  // dO of slot 0, MN-major
+      constexpr uint64_t kSlot = G::SLOT >> 4, kHalf = (BN * 128) >> 4;
+      const uint32_t t_ops = tmem + G::C_OPS;
+      bool ok = true;
+      for (int it = 0; it < n; ++it) {
+        if (!mbar_wait(&bar_ops_full, it & 1, &abort_flag)) {
           raise_error(a.status, &abort_flag, kDevTimeoutEpilogue);
           ok = false;
+          break;
         }
+        tc_fence_after();
+        const int sp = it % ST;
+        const uint64_t mq = mn_ring + sp * kSlot, mo = mn_do + sp * kSlot;
+        const bool acc = it > 0;
+        umma_chain_ts<KO>(tmem + G::C_DK, t_ops, mq + kHalf, id_out, acc);
+        umma_chain_ts<KO>(tmem + G::C_DK, t_ops + OC, mq, id_out, true);
+        umma_chain_ts<KO>(tmem + G::C_DV, t_ops + 2 * OC, mo, id_out, acc);
+        umma_commit(&bar_ops_empty);
+        umma_commit(&bar_empty[sp]);
       }
       if (ok) umma_commit(&bar_acc);
     }
