@@ -141,6 +141,22 @@ __device__ __forceinline__ void umma_chain_ts(uint32_t d, uint32_t a_tmem, uint6
     umma_bf16_ts(d, a_tmem + 8 * ks, b0 + mnoff(ks), idesc, (acc || ks > 0) ? 1u : 0u);
 }
 
+// Warp-convergent forms of the two chains (the whole warp calls them).
+template <int KSTEPS, int A_PANEL, int B_PANEL, bool B_MN>
+__device__ __forceinline__ void umma_chain_w(uint32_t d, uint64_t a0, uint64_t b0, uint32_t idesc, bool acc) {
+#pragma unroll
+  for (int ks = 0; ks < KSTEPS; ++ks)
+    umma_bf16_w(d, a0 + koff<A_PANEL>(ks), b0 + (B_MN ? mnoff(ks) : koff<B_PANEL>(ks)), idesc,
+                (acc || ks > 0) ? 1u : 0u);
+}
+
+template <int KSTEPS>
+__device__ __forceinline__ void umma_chain_ts_w(uint32_t d, uint32_t a_tmem, uint64_t b0, uint32_t idesc, bool acc) {
+#pragma unroll
+  for (int ks = 0; ks < KSTEPS; ++ks)
+    umma_bf16_ts_w(d, a_tmem + 8 * ks, b0 + mnoff(ks), idesc, (acc || ks > 0) ? 1u : 0u);
+}
+
 // Loads a pair of BN-row tiles (X then Y) of HD columns into "pair" panels:
 // panel p holds X's rows then Y's rows (2*BN rows of 128 bytes), so the pair is
 // one 2*BN-row K-major operand and each half is an MN-major operand with panel

@@ -257,39 +257,39 @@ __global__ void __launch_bounds__(kBBThreads, 1)
     // ------------------------------ score MMA issuer ------------------------------
     // Products sharing an A operand are one N=128 MMA:
     //   [S | Q ddK^T] = Q [K ; ddK]^T,  ddS += ddQ K^T,  [dP | dPa] = dO [V ; ddV]^T
-    if (lane == 0) {
+    {
       constexpr int KS = HD / 16;
       const uint32_t id128 = idesc_bf16_f32(kBM, 2 * BN, false, false);
       const uint32_t id64 = idesc_bf16_f32(kBM, BN, false, false);
       const uint64_t a_q = kdesc(s_q), a_do = kdesc(s_do), a_ddq = kdesc(s_ddq);
       const uint64_t b_ring = kdesc(s_ring);  // pair (K | ddK) of slot 0, K-major
       constexpr uint64_t kSlot = G::SLOT >> 4, kPair = G::PAIR >> 4;
-      bool ok = mbar_wait(&bar_res, 0, &abort_flag);
-      if (!ok) raise_error(a.status, &abort_flag, kDevTimeoutTmaFull);
+      bool ok = __all_sync(0xffffffffu, mbar_wait(&bar_res, 0, &abort_flag));
+      if (!ok && lane == 0) raise_error(a.status, &abort_flag, kDevTimeoutTmaFull);
       for (int it = 0; ok && it < total; ++it) {
         const int s = it % ST, sb = buf_of(it), u = use_of(it);
-        if (!mbar_wait(&bar_full[s], (it / ST) & 1, &abort_flag)) {
-          raise_error(a.status, &abort_flag, kDevTimeoutTmaFull);
+        if (!__all_sync(0xffffffffu, mbar_wait(&bar_full[s], (it / ST) & 1, &abort_flag))) {
+          if (lane == 0) raise_error(a.status, &abort_flag, kDevTimeoutTmaFull);
           break;
         }
-        if (u > 0 && !mbar_wait(&bar_sc_empty[sb], (u - 1) & 1, &abort_flag)) {
-          raise_error(a.status, &abort_flag, kDevTimeoutEpilogue);
+        if (u > 0 && !__all_sync(0xffffffffu, mbar_wait(&bar_sc_empty[sb], (u - 1) & 1, &abort_flag))) {
+          if (lane == 0) raise_error(a.status, &abort_flag, kDevTimeoutEpilogue);
           break;
         }
         tc_fence_after();
         const uint64_t bk = b_ring + s * kSlot;
         const uint32_t tb = tmem + sb * G::SCORE_COLS;
-        umma_chain<KS, G::RES_PANEL, G::PAIR_PANEL, false>(tb + G::C_S, a_q, bk, id128, false);
-        umma_chain<KS, G::RES_PANEL, G::PAIR_PANEL, false>(tb + G::C_DDS, a_ddq, bk, id64, true);
-        umma_chain<KS, G::RES_PANEL, G::PAIR_PANEL, false>(tb + G::C_DP, a_do, bk + kPair, id128, false);
-        umma_commit(&bar_sc_full[sb]);
-        if (it < n) umma_commit(&bar_empty[s]);  // stats sweep: slot free once scored
+        umma_chain_w<KS, G::RES_PANEL, G::PAIR_PANEL, false>(tb + G::C_S, a_q, bk, id128, false);
+        umma_chain_w<KS, G::RES_PANEL, G::PAIR_PANEL, false>(tb + G::C_DDS, a_ddq, bk, id64, true);
+        umma_chain_w<KS, G::RES_PANEL, G::PAIR_PANEL, false>(tb + G::C_DP, a_do, bk + kPair, id128, false);
+        umma_commit_w(&bar_sc_full[sb]);
+        if (it < n) umma_commit_w(&bar_empty[s]);  // stats sweep: slot free once scored
       }
     }
   } else if (warp == kBBWarpMmaOut) {
     // ----------------------------- operand MMA issuer -----------------------------
     // Second-sweep tile j, A in TMEM:  dQ'/scale += dS ddK + dS2 K,  ddO += ddP V + P ddV
-    if (lane == 0) {
+    {
       constexpr int KO = BN / 16, OC = G::OPS_COLS;
       const uint32_t id_out = idesc_bf16_f32(kBM, HD, false, true);
       const uint64_t mn_ring = mndesc(s_ring, G::PAIR_PANEL);  // K of slot 0, MN-major
@@ -297,8 +297,8 @@ __global__ void __launch_bounds__(kBBThreads, 1)
       const uint32_t t_ops = tmem + G::C_OPS;
       bool ok = true;
       for (int j = 0; j < n; ++j) {
-        if (!mbar_wait(&bar_ops_full, j & 1, &abort_flag)) {
-          raise_error(a.status, &abort_flag, kDevTimeoutEpilogue);
+        if (!__all_sync(0xffffffffu, mbar_wait(&bar_ops_full, j & 1, &abort_flag))) {
+          if (lane == 0) raise_error(a.status, &abort_flag, kDevTimeoutEpilogue);
           ok = false;
           break;
         }
@@ -306,14 +306,14 @@ __global__ void __launch_bounds__(kBBThreads, 1)
         const int sp = (n + j) % ST;
         const uint64_t mk = mn_ring + sp * kSlot;  // K; ddK = +kHalf; V = +kPair; ddV = +kPair+kHalf
         const bool acc = j > 0;
-        umma_chain_ts<KO>(tmem + G::C_DQ, t_ops, mk + kHalf, id_out, acc);
-        umma_chain_ts<KO>(tmem + G::C_DQ, t_ops + OC, mk, id_out, true);
-        umma_chain_ts<KO>(tmem + G::C_DDO, t_ops + 2 * OC, mk + kPair, id_out, acc);
-        umma_chain_ts<KO>(tmem + G::C_DDO, t_ops + 3 * OC, mk + kPair + kHalf, id_out, true);
-        umma_commit(&bar_ops_empty);
-        umma_commit(&bar_empty[sp]);
+        umma_chain_ts_w<KO>(tmem + G::C_DQ, t_ops, mk + kHalf, id_out, acc);
+        umma_chain_ts_w<KO>(tmem + G::C_DQ, t_ops + OC, mk, id_out, true);
+        umma_chain_ts_w<KO>(tmem + G::C_DDO, t_ops + 2 * OC, mk + kPair, id_out, acc);
+        umma_chain_ts_w<KO>(tmem + G::C_DDO, t_ops + 3 * OC, mk + kPair + kHalf, id_out, true);
+        umma_commit_w(&bar_ops_empty);
+        umma_commit_w(&bar_empty[sp]);
       }
-      if (ok) umma_commit(&bar_acc);
+      if (ok) umma_commit_w(&bar_acc);
     }
   } else {
     // --------------------------- elementwise warps ----------------------------
@@ -578,7 +578,7 @@ __global__ void __launch_bounds__(kBBThreads, 1)
   } else if (warp == kBBWarpMma) {
     // ------------------------------ score MMA issuer ------------------------------
     //   [S^T | K ddQ^T] = K [Q ; ddQ]^T,  ddS^T += ddK Q^T,  dP^T = V dO^T,  dPa^T = ddV dO^T
-    if (lane == 0 && n > 0) {
+    if (n > 0) {
       constexpr int KS = HD / 16;
       const uint32_t id128 = idesc_bf16_f32(kBM, 2 * BN, false, false);
       const uint32_t id64 = idesc_bf16_f32(kBM, BN, false, false);
@@ -586,31 +586,31 @@ __global__ void __launch_bounds__(kBBThreads, 1)
       const uint64_t b_ring = kdesc(s_ring);          // pair (Q | ddQ) of slot 0
       const uint64_t b_do = kdesc(s_ring + G::PAIR);  // dO of slot 0
       constexpr uint64_t kSlot = G::SLOT >> 4;
-      bool ok = mbar_wait(&bar_res, 0, &abort_flag);
-      if (!ok) raise_error(a.status, &abort_flag, kDevTimeoutTmaFull);
+      bool ok = __all_sync(0xffffffffu, mbar_wait(&bar_res, 0, &abort_flag));
+      if (!ok && lane == 0) raise_error(a.status, &abort_flag, kDevTimeoutTmaFull);
       for (int it = 0; ok && it < n; ++it) {
         const int s = it % ST;
-        if (!mbar_wait(&bar_full[s], (it / ST) & 1, &abort_flag)) {
-          raise_error(a.status, &abort_flag, kDevTimeoutTmaFull);
+        if (!__all_sync(0xffffffffu, mbar_wait(&bar_full[s], (it / ST) & 1, &abort_flag))) {
+          if (lane == 0) raise_error(a.status, &abort_flag, kDevTimeoutTmaFull);
           break;
         }
-        if (it > 0 && !mbar_wait(&bar_sc_empty, (it - 1) & 1, &abort_flag)) {
-          raise_error(a.status, &abort_flag, kDevTimeoutEpilogue);
+        if (it > 0 && !__all_sync(0xffffffffu, mbar_wait(&bar_sc_empty, (it - 1) & 1, &abort_flag))) {
+          if (lane == 0) raise_error(a.status, &abort_flag, kDevTimeoutEpilogue);
           break;
         }
         tc_fence_after();
         const uint64_t bq = b_ring + s * kSlot, bo = b_do + s * kSlot;
-        umma_chain<KS, G::RES_PANEL, G::PAIR_PANEL, false>(tmem + G::C_S, a_k, bq, id128, false);
-        umma_chain<KS, G::RES_PANEL, G::PAIR_PANEL, false>(tmem + G::C_DDS, a_ddk, bq, id64, true);
-        umma_chain<KS, G::RES_PANEL, BN * 128, false>(tmem + G::C_DP, a_v, bo, id64, false);
-        umma_chain<KS, G::RES_PANEL, BN * 128, false>(tmem + G::C_DPA, a_ddv, bo, id64, false);
-        umma_commit(&bar_sc_full);
+        umma_chain_w<KS, G::RES_PANEL, G::PAIR_PANEL, false>(tmem + G::C_S, a_k, bq, id128, false);
+        umma_chain_w<KS, G::RES_PANEL, G::PAIR_PANEL, false>(tmem + G::C_DDS, a_ddk, bq, id64, true);
+        umma_chain_w<KS, G::RES_PANEL, BN * 128, false>(tmem + G::C_DP, a_v, bo, id64, false);
+        umma_chain_w<KS, G::RES_PANEL, BN * 128, false>(tmem + G::C_DPA, a_ddv, bo, id64, false);
+        umma_commit_w(&bar_sc_full);
       }
     }
   } else if (warp == kBBWarpMmaOut) {
     // ----------------------------- operand MMA issuer -----------------------------
     //   dK'/scale += dS^T ddQ + dS2^T Q,  dV' += ddP^T dO   (A in TMEM)
-    if (lane == 0 && n > 0) {
+    if (n > 0) {
       constexpr int KO = BN / 16, OC = G::OPS_COLS;
       const uint32_t id_out = idesc_bf16_f32(kBM, HD, false, true);
       const uint64_t mn_ring = mndesc(s_ring, G::PAIR_PANEL);     // Q of slot 0, MN-major
@@ -619,8 +619,8 @@ __global__ void __launch_bounds__(kBBThreads, 1)
       const uint32_t t_ops = tmem + G::C_OPS;
       bool ok = true;
       for (int it = 0; it < n; ++it) {
-        if (!mbar_wait(&bar_ops_full, it & 1, &abort_flag)) {
-          raise_error(a.status, &abort_flag, kDevTimeoutEpilogue);
+        if (!__all_sync(0xffffffffu, mbar_wait(&bar_ops_full, it & 1, &abort_flag))) {
+          if (lane == 0) raise_error(a.status, &abort_flag, kDevTimeoutEpilogue);
           ok = false;
           break;
         }
@@ -628,13 +628,13 @@ __global__ void __launch_bounds__(kBBThreads, 1)
         const int sp = it % ST;
         const uint64_t mq = mn_ring + sp * kSlot, mo = mn_do + sp * kSlot;
         const bool acc = it > 0;
-        umma_chain_ts<KO>(tmem + G::C_DK, t_ops, mq + kHalf, id_out, acc);
-        umma_chain_ts<KO>(tmem + G::C_DK, t_ops + OC, mq, id_out, true);
-        umma_chain_ts<KO>(tmem + G::C_DV, t_ops + 2 * OC, mo, id_out, acc);
-        umma_commit(&bar_ops_empty);
-        umma_commit(&bar_empty[sp]);
+        umma_chain_ts_w<KO>(tmem + G::C_DK, t_ops, mq + kHalf, id_out, acc);
+        umma_chain_ts_w<KO>(tmem + G::C_DK, t_ops + OC, mq, id_out, true);
+        umma_chain_ts_w<KO>(tmem + G::C_DV, t_ops + 2 * OC, mo, id_out, acc);
+        umma_commit_w(&bar_ops_empty);
+        umma_commit_w(&bar_empty[sp]);
       }
-      if (ok) umma_commit(&bar_acc);
+      if (ok) umma_commit_w(&bar_acc);
     }
   } else {
     // --------------------------- elementwise warps ----------------------------
