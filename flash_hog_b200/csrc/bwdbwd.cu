@@ -114,7 +114,9 @@ struct QPass {
   static_assert(BN == 64, "two warpgroups x 32 columns");
 };
 
-// Stats sweep: row partial sums over this thread's 32 columns.
+// Stats sweep: row partial sums over this thread's 32 columns. dD and r3 are
+// accumulated without the softmax scale of ddS (applied once per row after the
+// sweep): dD/scale += P ddS', r1 += P dPa, r2 += P dP, r3/scale += P ddS' dP.
 template <bool MASK>
 __device__ __forceinline__ void q_stats32(const uint32_t (&vs)[32], const uint32_t (&vdds)[32],
                                           const uint32_t (&vdp)[32], const uint32_t (&vdpa)[32], int kc, int row,
@@ -125,7 +127,7 @@ __device__ __forceinline__ void q_stats32(const uint32_t (&vs)[32], const uint32
     float s = fmaf(__uint_as_float(vs[i]), sc2, -lg);
     if (MASK && (kc + i >= tk || (causal && kc + i > row))) s = -INFINITY;
     const float p = ex2(s);
-    const float t = __uint_as_float(vdds[i]) * sc * p;
+    const float t = __uint_as_float(vdds[i]) * p;
     const float dp = __uint_as_float(vdp[i]);
     dD += t;
     r3 = fmaf(t, dp, r3);
@@ -136,14 +138,15 @@ __device__ __forceinline__ void q_stats32(const uint32_t (&vs)[32], const uint32
 
 // Second sweep: packed bf16 pairs of dS/scale, dS2/scale, ddP and P for this
 // thread's 32 columns (the softmax scale of dS and dS2 is applied to dQ' in
-// the epilogue instead of per element).
+// the epilogue instead of per element). With u = ddS - dD and c = dD D + B,
+//   ddP = P u,  dS/scale = P (dP - D),
+//   dS2/scale = P (dPa + dP u - ddS D - B) = P (dPa - c) + ddP (dP - D).
 template <bool MASK>
 __device__ __forceinline__ void q_ops32(const uint32_t (&vs)[32], const uint32_t (&vdds)[32],
                                         const uint32_t (&vdp)[32], const uint32_t (&vdpa)[32], int kc, int row, int tk,
-                                        int causal, float sc, float sc2, float lg, float dv, float dD, float Bv,
+                                        int causal, float sc, float sc2, float lg, float dv, float dD, float cq,
                                         uint32_t (&o_ds)[16], uint32_t (&o_ds2)[16], uint32_t (&o_ddp)[16],
                                         uint32_t (&o_p)[16]) {
-  const float nscdv = -sc * dv;
 #pragma unroll
   for (int i = 0; i < 32; i += 2) {
     float pp[2], ddp[2], ds[2], ds2[2];
@@ -153,14 +156,12 @@ __device__ __forceinline__ void q_ops32(const uint32_t (&vs)[32], const uint32_t
       float s = fmaf(__uint_as_float(vs[c]), sc2, -lg);
       if (MASK && (kc + c >= tk || (causal && kc + c > row))) s = -INFINITY;
       const float p = ex2(s);
-      const float vd = __uint_as_float(vdds[c]);
-      const float dp = __uint_as_float(vdp[c]);
-      const float u = fmaf(vd, sc, -dD);                                            // ddS - dD
+      const float u = fmaf(__uint_as_float(vdds[c]), sc, -dD);  // ddS - dD
+      const float dpd = __uint_as_float(vdp[c]) - dv;            // dP - D
       pp[e] = p;
       ddp[e] = p * u;
-      ds[e] = p * (dp - dv);
-      const float dp2 = fmaf(vd, nscdv, fmaf(dp, u, __uint_as_float(vdpa[c])));   // dPa + dP(ddS-dD) - ddS D
-      ds2[e] = p * (dp2 - Bv);
+      ds[e] = p * dpd;
+      ds2[e] = fmaf(ddp[e], dpd, p * (__uint_as_float(vdpa[c]) - cq));
     }
     o_p[i / 2] = pack_bf16(pp[0], pp[1]);
     o_ddp[i / 2] = pack_bf16(ddp[0], ddp[1]);
@@ -326,7 +327,7 @@ __global__ void __launch_bounds__(kBBThreads, 1)
     const float lg = row_ok ? a.lse[vi] * kLog2e : 0.f;
     const float dv = row_ok ? a.delta[vi] : 0.f;
     const float sc = sh.scale, sc2 = sh.scale * kLog2e;
-    float dD = 0.f, r1 = 0.f, r2 = 0.f, r3 = 0.f, Bv = 0.f;
+    float dD = 0.f, r1 = 0.f, r2 = 0.f, r3 = 0.f, Bv = 0.f, cq = 0.f;
     bool ok = true;
     for (int it = 0; it < total; ++it) {
       const int j = it % n;
@@ -363,19 +364,20 @@ __global__ void __launch_bounds__(kBBThreads, 1)
           warp_arrive(&bar_red);
           ok = __all_sync(0xffffffffu, mbar_wait(&bar_red, 0, &abort_flag));
           if (!ok) break;
-          dD = red[0][0][r] + red[0][1][r];
+          dD = (red[0][0][r] + red[0][1][r]) * sc;
           r1 = red[1][0][r] + red[1][1][r];
           r2 = red[2][0][r] + red[2][1][r];
-          r3 = red[3][0][r] + red[3][1][r];
+          r3 = (red[3][0][r] + red[3][1][r]) * sc;
           Bv = r1 - dD * r2 - dv * dD + r3;
+          cq = r1 - dD * r2 + r3;  // dD D + B
         }
       } else {
         uint32_t o_ds[16], o_ds2[16], o_ddp[16], o_p[16];
         if (need_mask)
-          q_ops32<true>(vs, vdds, vdp, vdpa, kc, row, sh.Tk, sh.causal, sc, sc2, lg, dv, dD, Bv, o_ds, o_ds2, o_ddp,
+          q_ops32<true>(vs, vdds, vdp, vdpa, kc, row, sh.Tk, sh.causal, sc, sc2, lg, dv, dD, cq, o_ds, o_ds2, o_ddp,
                         o_p);
         else
-          q_ops32<false>(vs, vdds, vdp, vdpa, kc, row, sh.Tk, sh.causal, sc, sc2, lg, dv, dD, Bv, o_ds, o_ds2,
+          q_ops32<false>(vs, vdds, vdp, vdpa, kc, row, sh.Tk, sh.causal, sc, sc2, lg, dv, dD, cq, o_ds, o_ds2,
                          o_ddp, o_p);
         if (j > 0) ok = __all_sync(0xffffffffu, mbar_wait(&bar_ops_empty, (j - 1) & 1, &abort_flag));
         if (!ok) break;
@@ -427,7 +429,7 @@ struct KPass {
   static constexpr int PAIR = 2 * STR;
   static constexpr int PAIR_PANEL = 2 * BN * 128;
   static constexpr int VEC = BN * 4;               // one fp32 statistic per streamed query
-  static constexpr int SLOT = PAIR + STR + 4 * VEC;  // (Q | ddQ) pair, dO, then L, D, dD, B
+  static constexpr int SLOT = PAIR + STR + 4 * VEC;  // (Q | ddQ) pair, dO, then L, D, dD, c = dD D + B
   static constexpr int SMEM = 1024 + 4 * RES + ST * SLOT;
   // TMEM: scores, accumulators dK', dV', bf16 operands dS^T, dS2^T, ddP^T (A of the MMAs).
   static constexpr int C_S = 0, C_DDS = BN, C_DP = 2 * BN, C_DPA = 3 * BN;
@@ -441,7 +443,9 @@ struct KPass {
 };
 
 // Packed bf16 pairs of dS^T/scale, dS2^T/scale and ddP^T for this thread's 32
-// query columns (the scale of dS, dS2 is applied to dK' in the epilogue).
+// query columns (the scale of dS, dS2 is applied to dK' in the epilogue), by
+// the same identities as the query pass; sv holds per query L log2(e), D, dD
+// and c = dD D + B.
 template <bool MASK>
 __device__ __forceinline__ void k_ops32(const uint32_t (&vs)[32], const uint32_t (&vdds)[32],
                                         const uint32_t (&vdp)[32], const uint32_t (&vdpa)[32], const float* sv,
@@ -457,14 +461,11 @@ __device__ __forceinline__ void k_ops32(const uint32_t (&vs)[32], const uint32_t
       float s = fmaf(__uint_as_float(vs[c]), sc2, -sv[c]);
       if (MASK && (qc + c >= tq || (causal && qc + c < key))) s = -INFINITY;
       const float p = ex2(s);
-      const float dq = sv[BN + c];
-      const float vd = __uint_as_float(vdds[c]);
-      const float dp = __uint_as_float(vdp[c]);
-      const float u = fmaf(vd, sc, -sv[2 * BN + c]);
+      const float u = fmaf(__uint_as_float(vdds[c]), sc, -sv[2 * BN + c]);  // ddS - dD
+      const float dpd = __uint_as_float(vdp[c]) - sv[BN + c];              // dP - D
       ddp[e] = p * u;
-      ds[e] = p * (dp - dq);
-      const float dp2 = fmaf(-vd * sc, dq, fmaf(dp, u, __uint_as_float(vdpa[c])));
-      ds2[e] = p * (dp2 - sv[3 * BN + c]);
+      ds[e] = p * dpd;
+      ds2[e] = fmaf(ddp[e], dpd, p * (__uint_as_float(vdpa[c]) - sv[3 * BN + c]));
     }
     o_ddp[i / 2] = pack_bf16(ddp[0], ddp[1]);
     o_ds[i / 2] = pack_bf16(ds[0], ds[1]);
@@ -546,7 +547,7 @@ __global__ void __launch_bounds__(kBBThreads, 1)
         st[k][0] = v ? a.lse[idx] * kLog2e : 0.f;
         st[k][1] = v ? a.delta[idx] : 0.f;
         st[k][2] = v ? a.dd[idx] : 0.f;
-        st[k][3] = v ? a.bv[idx] : 0.f;
+        st[k][3] = v ? fmaf(st[k][2], st[k][1], a.bv[idx]) : 0.f;  // c = dD D + B
       }
       bool ok = true;
       if (it >= ST) ok = mbar_wait(&bar_empty[s], ((it / ST) - 1) & 1, &abort_flag);
