@@ -444,32 +444,40 @@ struct KPass {
 
 // Packed bf16 pairs of dS^T/scale, dS2^T/scale and ddP^T for this thread's 32
 // query columns (the scale of dS, dS2 is applied to dK' in the epilogue), by
-// the same identities as the query pass; sv holds per query L log2(e), D, dD
-// and c = dD D + B.
+// the same identities as the query pass. sv points at this thread's first
+// column of the slot's statistics block [L log2(e) | D | dD | c = dD D + B]
+// (BN floats each, 16-byte aligned), read four columns per load.
 template <bool MASK>
 __device__ __forceinline__ void k_ops32(const uint32_t (&vs)[32], const uint32_t (&vdds)[32],
                                         const uint32_t (&vdp)[32], const uint32_t (&vdpa)[32], const float* sv,
                                         int qc, int key, int tq, int causal, float sc, float sc2,
                                         uint32_t (&o_ds)[16], uint32_t (&o_ds2)[16], uint32_t (&o_ddp)[16]) {
   constexpr int BN = 64;
+  const float4* sv4 = reinterpret_cast<const float4*>(sv);
 #pragma unroll
-  for (int i = 0; i < 32; i += 2) {
-    float ddp[2], ds[2], ds2[2];
+  for (int i = 0; i < 32; i += 4) {
+    const float4 l4 = sv4[i / 4], d4 = sv4[(BN + i) / 4], dd4 = sv4[(2 * BN + i) / 4], c4 = sv4[(3 * BN + i) / 4];
+    const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dv[4] = {d4.x, d4.y, d4.z, d4.w};
+    const float ddv[4] = {dd4.x, dd4.y, dd4.z, dd4.w}, cv[4] = {c4.x, c4.y, c4.z, c4.w};
+    float ddp[4], ds[4], ds2[4];
 #pragma unroll
-    for (int e = 0; e < 2; ++e) {
+    for (int e = 0; e < 4; ++e) {
       const int c = i + e;
-      float s = fmaf(__uint_as_float(vs[c]), sc2, -sv[c]);
+      float s = fmaf(__uint_as_float(vs[c]), sc2, -lv[e]);
       if (MASK && (qc + c >= tq || (causal && qc + c < key))) s = -INFINITY;
       const float p = ex2(s);
-      const float u = fmaf(__uint_as_float(vdds[c]), sc, -sv[2 * BN + c]);  // ddS - dD
-      const float dpd = __uint_as_float(vdp[c]) - sv[BN + c];              // dP - D
+      const float u = fmaf(__uint_as_float(vdds[c]), sc, -ddv[e]);  // ddS - dD
+      const float dpd = __uint_as_float(vdp[c]) - dv[e];           // dP - D
       ddp[e] = p * u;
       ds[e] = p * dpd;
-      ds2[e] = fmaf(ddp[e], dpd, p * (__uint_as_float(vdpa[c]) - sv[3 * BN + c]));
+      ds2[e] = fmaf(ddp[e], dpd, p * (__uint_as_float(vdpa[c]) - cv[e]));
     }
-    o_ddp[i / 2] = pack_bf16(ddp[0], ddp[1]);
-    o_ds[i / 2] = pack_bf16(ds[0], ds[1]);
-    o_ds2[i / 2] = pack_bf16(ds2[0], ds2[1]);
+#pragma unroll
+    for (int e = 0; e < 4; e += 2) {
+      o_ddp[(i + e) / 2] = pack_bf16(ddp[e], ddp[e + 1]);
+      o_ds[(i + e) / 2] = pack_bf16(ds[e], ds[e + 1]);
+      o_ds2[(i + e) / 2] = pack_bf16(ds2[e], ds2[e + 1]);
+    }
   }
 }
 

@@ -74,19 +74,18 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                : "memory");
 }
 
-// One bounded wait attempt: the thread may sleep in the hardware until the
-// phase completes or kSuspendHintNs elapses, so waiting warps do not take
-// issue slots from the warps sharing their scheduler.
-constexpr uint32_t kSuspendHintNs = 200000;
-
+// One wait attempt: the thread may sleep in the hardware until the phase
+// completes or a system-dependent time limit passes, so waiting warps do not
+// take issue slots from the warps sharing their scheduler. (An explicit long
+// suspend-time hint delayed the wake-up after the phase completed.)
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(bar), "r"(parity), "n"(kSuspendHintNs)
+      : "r"(bar), "r"(parity)
       : "memory");
   return ok != 0;
 }
