@@ -141,20 +141,27 @@ __device__ __forceinline__ void umma_chain_ts(uint32_t d, uint32_t a_tmem, uint6
     umma_bf16_ts(d, a_tmem + 8 * ks, b0 + mnoff(ks), idesc, (acc || ks > 0) ? 1u : 0u);
 }
 
-// Warp-convergent forms of the two chains (the whole warp calls them).
+// Warp-convergent forms of the two chains (the whole warp calls them), issued
+// four k-steps per elected asm block.
 template <int KSTEPS, int A_PANEL, int B_PANEL, bool B_MN>
 __device__ __forceinline__ void umma_chain_w(uint32_t d, uint64_t a0, uint64_t b0, uint32_t idesc, bool acc) {
+  static_assert(KSTEPS % 4 == 0, "chains are issued four k-steps at a time");
 #pragma unroll
-  for (int ks = 0; ks < KSTEPS; ++ks)
-    umma_bf16_w(d, a0 + koff<A_PANEL>(ks), b0 + (B_MN ? mnoff(ks) : koff<B_PANEL>(ks)), idesc,
-                (acc || ks > 0) ? 1u : 0u);
+  for (int ks = 0; ks < KSTEPS; ks += 4) {
+    auto bo = [&](int k) { return b0 + (B_MN ? mnoff(k) : koff<B_PANEL>(k)); };
+    umma_bf16_x4_w(d, a0 + koff<A_PANEL>(ks), a0 + koff<A_PANEL>(ks + 1), a0 + koff<A_PANEL>(ks + 2),
+                   a0 + koff<A_PANEL>(ks + 3), bo(ks), bo(ks + 1), bo(ks + 2), bo(ks + 3), idesc,
+                   (acc || ks > 0) ? 1u : 0u);
+  }
 }
 
 template <int KSTEPS>
 __device__ __forceinline__ void umma_chain_ts_w(uint32_t d, uint32_t a_tmem, uint64_t b0, uint32_t idesc, bool acc) {
+  static_assert(KSTEPS % 4 == 0, "chains are issued four k-steps at a time");
 #pragma unroll
-  for (int ks = 0; ks < KSTEPS; ++ks)
-    umma_bf16_ts_w(d, a_tmem + 8 * ks, b0 + mnoff(ks), idesc, (acc || ks > 0) ? 1u : 0u);
+  for (int ks = 0; ks < KSTEPS; ks += 4)
+    umma_bf16_ts_x4_w(d, a_tmem + 8 * ks, b0 + mnoff(ks), b0 + mnoff(ks + 1), b0 + mnoff(ks + 2),
+                      b0 + mnoff(ks + 3), idesc, (acc || ks > 0) ? 1u : 0u);
 }
 
 // Loads a pair of BN-row tiles (X then Y) of HD columns into "pair" panels:

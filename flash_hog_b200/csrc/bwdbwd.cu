@@ -265,15 +265,15 @@ __global__ void __launch_bounds__(kBBThreads, 1)
       const uint64_t a_q = kdesc(s_q), a_do = kdesc(s_do), a_ddq = kdesc(s_ddq);
       const uint64_t b_ring = kdesc(s_ring);  // pair (K | ddK) of slot 0, K-major
       constexpr uint64_t kSlot = G::SLOT >> 4, kPair = G::PAIR >> 4;
-      bool ok = __all_sync(0xffffffffu, mbar_wait(&bar_res, 0, &abort_flag));
+      bool ok = mbar_wait_warp(&bar_res, 0, &abort_flag);
       if (!ok && lane == 0) raise_error(a.status, &abort_flag, kDevTimeoutTmaFull);
       for (int it = 0; ok && it < total; ++it) {
         const int s = it % ST, sb = buf_of(it), u = use_of(it);
-        if (!__all_sync(0xffffffffu, mbar_wait(&bar_full[s], (it / ST) & 1, &abort_flag))) {
+        if (!mbar_wait_warp(&bar_full[s], (it / ST) & 1, &abort_flag)) {
           if (lane == 0) raise_error(a.status, &abort_flag, kDevTimeoutTmaFull);
           break;
         }
-        if (u > 0 && !__all_sync(0xffffffffu, mbar_wait(&bar_sc_empty[sb], (u - 1) & 1, &abort_flag))) {
+        if (u > 0 && !mbar_wait_warp(&bar_sc_empty[sb], (u - 1) & 1, &abort_flag)) {
           if (lane == 0) raise_error(a.status, &abort_flag, kDevTimeoutEpilogue);
           break;
         }
@@ -298,7 +298,7 @@ __global__ void __launch_bounds__(kBBThreads, 1)
       const uint32_t t_ops = tmem + G::C_OPS;
       bool ok = true;
       for (int j = 0; j < n; ++j) {
-        if (!__all_sync(0xffffffffu, mbar_wait(&bar_ops_full, j & 1, &abort_flag))) {
+        if (!mbar_wait_warp(&bar_ops_full, j & 1, &abort_flag)) {
           if (lane == 0) raise_error(a.status, &abort_flag, kDevTimeoutEpilogue);
           ok = false;
           break;
@@ -334,7 +334,7 @@ __global__ void __launch_bounds__(kBBThreads, 1)
       const bool sweep2 = it >= n;
       const int kc = j * BN + cb;  // first key of this thread's columns
       const int sb = buf_of(it);
-      ok = __all_sync(0xffffffffu, mbar_wait(&bar_sc_full[sb], use_of(it) & 1, &abort_flag));
+      ok = mbar_wait_warp(&bar_sc_full[sb], use_of(it) & 1, &abort_flag);
       if (!ok) break;
       tc_fence_after();
       const uint32_t tb = tmem + sb * G::SCORE_COLS;
@@ -362,7 +362,7 @@ __global__ void __launch_bounds__(kBBThreads, 1)
           red[2][wg][r] = r2;
           red[3][wg][r] = r3;
           warp_arrive(&bar_red);
-          ok = __all_sync(0xffffffffu, mbar_wait(&bar_red, 0, &abort_flag));
+          ok = mbar_wait_warp(&bar_red, 0, &abort_flag);
           if (!ok) break;
           dD = (red[0][0][r] + red[0][1][r]) * sc;
           r1 = red[1][0][r] + red[1][1][r];
@@ -379,7 +379,7 @@ __global__ void __launch_bounds__(kBBThreads, 1)
         else
           q_ops32<false>(vs, vdds, vdp, vdpa, kc, row, sh.Tk, sh.causal, sc, sc2, lg, dv, dD, cq, o_ds, o_ds2,
                          o_ddp, o_p);
-        if (j > 0) ok = __all_sync(0xffffffffu, mbar_wait(&bar_ops_empty, (j - 1) & 1, &abort_flag));
+        if (j > 0) ok = mbar_wait_warp(&bar_ops_empty, (j - 1) & 1, &abort_flag);
         if (!ok) break;
         tc_fence_after();
         // This warpgroup's 32 keys are packed columns [16 wg, 16 wg + 16) of each operand.
@@ -392,7 +392,7 @@ __global__ void __launch_bounds__(kBBThreads, 1)
         warp_arrive(&bar_ops_full);
       }
     }
-    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&bar_acc, 0, &abort_flag));
+    if (ok) ok = mbar_wait_warp(&bar_acc, 0, &abort_flag);
     if (ok) {
       tc_fence_after();
       const int srow = row_ok ? row : 0;
@@ -557,9 +557,7 @@ __global__ void __launch_bounds__(kBBThreads, 1)
         st[k][2] = v ? a.dd[idx] : 0.f;
         st[k][3] = v ? fmaf(st[k][2], st[k][1], a.bv[idx]) : 0.f;  // c = dD D + B
       }
-      bool ok = true;
-      if (it >= ST) ok = mbar_wait(&bar_empty[s], ((it / ST) - 1) & 1, &abort_flag);
-      if (!__all_sync(0xffffffffu, ok)) {
+      if (it >= ST && !mbar_wait_warp(&bar_empty[s], ((it / ST) - 1) & 1, &abort_flag)) {
         if (lane == 0) raise_error(a.status, &abort_flag, kDevTimeoutSlotEmpty);
         break;
       }
@@ -595,15 +593,15 @@ __global__ void __launch_bounds__(kBBThreads, 1)
       const uint64_t b_ring = kdesc(s_ring);          // pair (Q | ddQ) of slot 0
       const uint64_t b_do = kdesc(s_ring + G::PAIR);  // dO of slot 0
       constexpr uint64_t kSlot = G::SLOT >> 4;
-      bool ok = __all_sync(0xffffffffu, mbar_wait(&bar_res, 0, &abort_flag));
+      bool ok = mbar_wait_warp(&bar_res, 0, &abort_flag);
       if (!ok && lane == 0) raise_error(a.status, &abort_flag, kDevTimeoutTmaFull);
       for (int it = 0; ok && it < n; ++it) {
         const int s = it % ST;
-        if (!__all_sync(0xffffffffu, mbar_wait(&bar_full[s], (it / ST) & 1, &abort_flag))) {
+        if (!mbar_wait_warp(&bar_full[s], (it / ST) & 1, &abort_flag)) {
           if (lane == 0) raise_error(a.status, &abort_flag, kDevTimeoutTmaFull);
           break;
         }
-        if (it > 0 && !__all_sync(0xffffffffu, mbar_wait(&bar_sc_empty, (it - 1) & 1, &abort_flag))) {
+        if (it > 0 && !mbar_wait_warp(&bar_sc_empty, (it - 1) & 1, &abort_flag)) {
           if (lane == 0) raise_error(a.status, &abort_flag, kDevTimeoutEpilogue);
           break;
         }
@@ -628,7 +626,7 @@ __global__ void __launch_bounds__(kBBThreads, 1)
       const uint32_t t_ops = tmem + G::C_OPS;
       bool ok = true;
       for (int it = 0; it < n; ++it) {
-        if (!__all_sync(0xffffffffu, mbar_wait(&bar_ops_full, it & 1, &abort_flag))) {
+        if (!mbar_wait_warp(&bar_ops_full, it & 1, &abort_flag)) {
           if (lane == 0) raise_error(a.status, &abort_flag, kDevTimeoutEpilogue);
           ok = false;
           break;
@@ -657,7 +655,7 @@ __global__ void __launch_bounds__(kBBThreads, 1)
     for (int it = 0; it < n; ++it) {
       const int s = it % ST;
       const int qc = (qt_begin + it) * BN + cb;  // first query of this thread's columns
-      ok = __all_sync(0xffffffffu, mbar_wait(&bar_sc_full, it & 1, &abort_flag));
+      ok = mbar_wait_warp(&bar_sc_full, it & 1, &abort_flag);
       if (!ok) break;
       tc_fence_after();
       uint32_t vs[32], vdds[32], vdp[32], vdpa[32];
@@ -678,7 +676,7 @@ __global__ void __launch_bounds__(kBBThreads, 1)
         k_ops32<true>(vs, vdds, vdp, vdpa, sv, qc, key, sh.Tq, sh.causal, sc, sc2, o_ds, o_ds2, o_ddp);
       else
         k_ops32<false>(vs, vdds, vdp, vdpa, sv, qc, key, sh.Tq, sh.causal, sc, sc2, o_ds, o_ds2, o_ddp);
-      if (it > 0) ok = __all_sync(0xffffffffu, mbar_wait(&bar_ops_empty, (it - 1) & 1, &abort_flag));
+      if (it > 0) ok = mbar_wait_warp(&bar_ops_empty, (it - 1) & 1, &abort_flag);
       if (!ok) break;
       tc_fence_after();
       const uint32_t to = tmem + tmem_lane_base(warp & 3) + G::C_OPS + 16 * wg;
@@ -694,7 +692,7 @@ __global__ void __launch_bounds__(kBBThreads, 1)
       // No query sees these keys (causal with Tk > Tq): the gradients are zero.
       if (key_ok) zero_row_global<HD>(dst);
     } else {
-      if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&bar_acc, 0, &abort_flag));
+      if (ok) ok = mbar_wait_warp(&bar_acc, 0, &abort_flag);
       if (ok) {
         tc_fence_after();
         tmem_row_to_global<HD>(tmem, warp, wg == 0 ? G::C_DK : G::C_DV, dst, key_ok, wg == 0 ? sc : 1.f);

@@ -117,6 +117,22 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+// Warp-wide form of mbar_wait: every lane of the warp calls it and all lanes
+// leave together as soon as any lane sees the phase complete. Each exit test is
+// voted across the warp, so lanes that time out of one try_wait never diverge
+// from lanes that saw the phase (a diverged warp waited for its last lane to
+// wake). Same limits as mbar_wait.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+  const uint32_t a = smem_u32(bar);
+  if (__any_sync(0xffffffffu, mbar_try_wait(a, parity))) return true;
+  const unsigned long long t0 = global_timer_ns();
+  while (true) {
+    if (__any_sync(0xffffffffu, mbar_try_wait(a, parity))) return true;
+    const bool stop = (abort_flag && *abort_flag) || (global_timer_ns() - t0 > kWaitLimitNs);
+    if (__any_sync(0xffffffffu, stop)) return false;
+  }
+}
+
 // ------------------------------------------------------------------------------------
 // TMA
 // ------------------------------------------------------------------------------------
@@ -309,6 +325,39 @@ __device__ __forceinline__ void umma_bf16_ts_w(uint32_t d_tmem, uint32_t a_tmem,
       "setp.ne.b32 p, %4, 0;\n\t"
       "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
       "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Four chained MMAs into one accumulator from one elected lane (the whole warp
+// executes it): one elect.sync and one predicate for the chain instead of per
+// instruction, so the issuing warp spends fewer issue slots per MMA.
+__device__ __forceinline__ void umma_bf16_x4_w(uint32_t d_tmem, uint64_t a0, uint64_t a1, uint64_t a2, uint64_t a3,
+                                               uint64_t b0, uint64_t b1, uint64_t b2, uint64_t b3, uint32_t idesc,
+                                               uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "setp.ne.b32 p, %10, 0;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %5, %9, p;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %2, %6, %9, 1;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %3, %7, %9, 1;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %4, %8, %9, 1;\n\t}" ::"r"(d_tmem),
+      "l"(a0), "l"(a1), "l"(a2), "l"(a3), "l"(b0), "l"(b1), "l"(b2), "l"(b3), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_bf16_ts_x4_w(uint32_t d_tmem, uint32_t a_tmem, uint64_t b0, uint64_t b1,
+                                                  uint64_t b2, uint64_t b3, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\t.reg .b32 t1, t2, t3;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "setp.ne.b32 p, %7, 0;\n\t"
+      "add.u32 t1, %1, 8;\n\tadd.u32 t2, %1, 16;\n\tadd.u32 t3, %1, 24;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %6, p;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [t1], %3, %6, 1;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [t2], %4, %6, 1;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [t3], %5, %6, 1;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b0), "l"(b1), "l"(b2), "l"(b3), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 
