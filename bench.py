@@ -2,8 +2,8 @@
 
 Workload (per GPU, weak scaling): causal bf16 B4 H16 S2048 D64 -- BASELINE.json's
 ``configs[1]``. One step = one double-backward pass over one batch: the
-D = rowsum(dO o O) pre-pass, the query-tiled pass (dQ', ddO, dD, B) and the
-key-tiled pass (dK', dV'), i.e. the work of the reference's
+query-tiled pass (D = rowsum(dO o O), dQ', ddO, dD, B) and the key-tiled pass
+(dK', dV'), i.e. the work of the reference's
 ``dot_product_attention_bwd_rule_bwd_rule``. Credited FLOPs are
 22 GEMM-equivalents x 2 x D per kept (query, key) pair (378.1 GFLOP per step).
 
@@ -229,17 +229,14 @@ def main():
         s, (dq2, ddo, dk2, dv2), st = sets[i], outs[i], stats[i]
         if ev is not None:
             ev[0].record()
-        _capi.attn_rowdot(s["o"], s["do"], st[0])
+        _capi.attn_bwdbwd_o(s["q"], s["k"], s["v"], s["o"], s["do"], s["ddq"], s["ddk"], s["ddv"], s["lse"],
+                            dq2, ddo, dk2, dv2, st[0], st[1], st[2], SCALE, CAUSAL, _capi.PASS_QUERY)
         if ev is not None:
             ev[1].record()
-        _capi.attn_bwdbwd_pass(s["q"], s["k"], s["v"], s["do"], s["ddq"], s["ddk"], s["ddv"], s["lse"], st[0],
-                               dq2, ddo, dk2, dv2, st[1], st[2], SCALE, CAUSAL, _capi.PASS_QUERY)
+        _capi.attn_bwdbwd_o(s["q"], s["k"], s["v"], s["o"], s["do"], s["ddq"], s["ddk"], s["ddv"], s["lse"],
+                            dq2, ddo, dk2, dv2, st[0], st[1], st[2], SCALE, CAUSAL, _capi.PASS_KEY)
         if ev is not None:
             ev[2].record()
-        _capi.attn_bwdbwd_pass(s["q"], s["k"], s["v"], s["do"], s["ddq"], s["ddk"], s["ddv"], s["lse"], st[0],
-                               dq2, ddo, dk2, dv2, st[1], st[2], SCALE, CAUSAL, _capi.PASS_KEY)
-        if ev is not None:
-            ev[3].record()
 
     def barrier():
         if dist is not None:
@@ -251,7 +248,7 @@ def main():
     if _capi.device_status() != 0:
         raise RuntimeError("device-side error during warm-up")
 
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(list(range(world)) if rank == 0 else []) as clocks:
         barrier()
@@ -265,9 +262,8 @@ def main():
     if _capi.device_status() != 0:
         raise RuntimeError("device-side error during the timed region")
     ms = start.elapsed_time(stop) / args.steps
-    t_rowdot = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
-    t_q = statistics.mean(e[1].elapsed_time(e[2]) for e in evs)
-    t_k = statistics.mean(e[2].elapsed_time(e[3]) for e in evs)
+    t_q = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
+    t_k = statistics.mean(e[1].elapsed_time(e[2]) for e in evs)
     if dist is not None:
         t = torch.tensor([ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -324,7 +320,7 @@ def main():
                 "achieved": achieved, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                 "frac": achieved / peaks["bf16_tflops"], "peak_source": f"{peak_kind} bf16 dense (burst)",
                 "traffic": None,
-                "per_launch_ms": {"rowdot": t_rowdot, "query_pass": t_q, "key_pass": t_k},
+                "per_launch_ms": {"query_pass": t_q, "key_pass": t_k},
                 "key_pass": {"achieved": credited_flops(B, H, S, gemms=8) / (t_k * 1e-3) / 1e12}}
     cpu = None
     if not args.skip_cpu:
@@ -340,7 +336,7 @@ def main():
                    "l2": f"{N_SETS} rotating input sets of ~136 MB each (> 126 MB L2)",
                    "credited_gflop_per_step_per_gpu": credited_flops(B, H, S) / 1e9},
         "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks.summary(),
-        "gpu_launches": 3 * args.steps,
+        "gpu_launches": 2 * args.steps,
     }
     print(json.dumps(line), flush=True)
     return 0

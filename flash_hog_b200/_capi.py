@@ -37,6 +37,7 @@ EXPORTED_SYMBOLS = (
     "fh_attn_bwd",
     "fh_attn_bwdbwd",
     "fh_attn_bwdbwd_pass",
+    "fh_attn_bwdbwd_o",
     "fh_attn_bwdbwd_noalloc",
     "fh_device_status",
     "fh_status_string",
@@ -89,6 +90,7 @@ def lib() -> ctypes.CDLL:
     h.fh_attn_bwd.argtypes = [vp, dims, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, f32, i32]
     h.fh_attn_bwdbwd.argtypes = [vp, dims] + [vp] * 15 + [f32, i32]
     h.fh_attn_bwdbwd_pass.argtypes = [vp, dims] + [vp] * 15 + [f32, i32, i32]
+    h.fh_attn_bwdbwd_o.argtypes = [vp, dims] + [vp] * 16 + [f32, i32, i32]
     h.fh_attn_bwdbwd_noalloc.argtypes = [vp, dims] + [vp] * 13 + [f32, i32, vp]
     h.fh_device_status.argtypes = [vp, ctypes.POINTER(ctypes.c_int)]
     h.fh_status_string.argtypes = [i32]
@@ -97,7 +99,7 @@ def lib() -> ctypes.CDLL:
     h.fh_last_error.argtypes = []
     h.fh_last_error.restype = ctypes.c_char_p
     for name in ("fh_attn_fwd", "fh_attn_rowdot", "fh_attn_bwd", "fh_attn_bwdbwd", "fh_attn_bwdbwd_pass",
-                 "fh_attn_bwdbwd_noalloc", "fh_device_status", "fh_abi_version"):
+                 "fh_attn_bwdbwd_o", "fh_attn_bwdbwd_noalloc", "fh_device_status", "fh_abi_version"):
         getattr(h, name).restype = i32
     if h.fh_abi_version() != ABI_VERSION:
         raise RuntimeError(f"flash_hog_b200 ABI mismatch: library {h.fh_abi_version()}, binding {ABI_VERSION}")
@@ -196,6 +198,18 @@ def attn_bwdbwd_pass(q, k, v, dO, ddq, ddk, ddv, lse, delta, dq2, ddo, dk2, dv2,
         _stream(q.device), ctypes.byref(dims), _ptr(q), _ptr(k), _ptr(v), _ptr(dO), _ptr(ddq), _ptr(ddk),
         _ptr(ddv), _ptr(lse), _ptr(delta), _ptr(dq2), _ptr(ddo), _ptr(dk2), _ptr(dv2), _ptr(dd), _ptr(bvec),
         float(scale), int(causal), int(which)))
+
+
+def attn_bwdbwd_o(q, k, v, o, dO, ddq, ddk, ddv, lse, dq2, ddo, dk2, dv2, delta, dd, bvec, scale: float,
+                  causal: bool, which: int = PASS_QUERY | PASS_KEY) -> None:
+    """Double backward from the forward output: the query pass computes delta itself."""
+    _same_layout(q, o, dO, ddq, dq2, ddo)
+    _same_layout(k, v, ddk, ddv, dk2, dv2)
+    dims = make_dims(q, k)
+    _check("fh_attn_bwdbwd_o", lib().fh_attn_bwdbwd_o(
+        _stream(q.device), ctypes.byref(dims), _ptr(q), _ptr(k), _ptr(v), _ptr(o), _ptr(dO), _ptr(ddq),
+        _ptr(ddk), _ptr(ddv), _ptr(lse), _ptr(dq2), _ptr(ddo), _ptr(dk2), _ptr(dv2), _ptr(delta), _ptr(dd),
+        _ptr(bvec), float(scale), int(causal), int(which)))
 
 
 def device_status(device=None) -> int:

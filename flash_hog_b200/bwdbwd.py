@@ -62,10 +62,10 @@ def flash_bwdbwd(Q, K, V, O, dO, ddQ, ddK, ddV, L, mask_type: MaskType = MaskTyp
     lse = L.reshape(b, n, t).float().contiguous()
     stats = torch.empty((3, b, n, t), dtype=torch.float32, device=q.device)
     delta, dd, bvec = stats[0], stats[1], stats[2]
-    _capi.attn_rowdot(o, do, delta)
     dq2, ddo = torch.empty_like(q), torch.empty_like(q)
     dk2, dv2 = torch.empty_like(k), torch.empty_like(k)
-    _capi.attn_bwdbwd(q, k, v, do, ddq, ddk, ddv, lse, delta, dq2, ddo, dk2, dv2, dd, bvec, scale, causal)
+    # D = rowsum(dO * O) is computed by the query-tiled pass itself.
+    _capi.attn_bwdbwd_o(q, k, v, o, do, ddq, ddk, ddv, lse, dq2, ddo, dk2, dv2, delta, dd, bvec, scale, causal)
     outs = (dq2.to(Q.dtype), dk2.to(K.dtype), dv2.to(V.dtype), ddo.to(dO.dtype))
     if return_stats:
         return outs, (delta, dd, bvec)

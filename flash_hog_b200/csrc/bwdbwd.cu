@@ -34,7 +34,8 @@ namespace {
 struct BBArgs {
   AttnShape sh;
   const float* lse;
-  const float* delta;
+  const float* delta;  // D = rowsum(dO o): read by both passes
+  float* delta_out;    // non-null: the query pass computes D from o and writes it here (= delta)
   float* dd;
   float* bv;
   __nv_bfloat16* dq2;
@@ -100,7 +101,7 @@ struct QPass {
   static constexpr int PAIR = 2 * STR;             // two streamed tiles as pair panels
   static constexpr int PAIR_PANEL = 2 * BN * 128;
   static constexpr int SLOT = 2 * PAIR;            // (K | ddK) pair, (V | ddV) pair
-  static constexpr int SMEM = 1024 + 3 * RES + ST * SLOT;
+  static constexpr int SMEM = 1024 + 3 * RES + ST * SLOT;  // Q, dO, ddQ, ring (O borrows the last slot)
   // TMEM: score buffer 0 [0, 256); accumulators dQ', ddO; bf16 operands dS,
   // dS2, ddP, P (BN/2 packed columns each). During the stats sweep the
   // accumulator and operand columns hold score buffer 1.
@@ -113,6 +114,31 @@ struct QPass {
   static_assert(SMEM <= 232448, "shared memory budget");
   static_assert(BN == 64, "two warpgroups x 32 columns");
 };
+
+// Partial rowsum(dO o) over columns [32 wg, 32 wg + 32) of row r of two
+// resident 128-row tiles (128B-swizzled 64-column panels, as loaded by TMA).
+template <int HD>
+__device__ __forceinline__ float rowdot_share(const uint8_t* s_o, const uint8_t* s_do, int r, int wg) {
+  float acc = 0.f;
+#pragma unroll
+  for (int c = 0; c < HD / 16; ++c) {  // 16-byte chunks: HD/8 per row, half of them per warpgroup
+    const int chunk = wg * (HD / 16) + c;
+    const int panel = chunk >> 3;
+    const uint32_t off = panel * kBM * 128 + sw128_offset(r, chunk & 7);
+    const uint4 x = *reinterpret_cast<const uint4*>(s_o + off);
+    const uint4 y = *reinterpret_cast<const uint4*>(s_do + off);
+    const __nv_bfloat162* xa = reinterpret_cast<const __nv_bfloat162*>(&x);
+    const __nv_bfloat162* ya = reinterpret_cast<const __nv_bfloat162*>(&y);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 xf = __bfloat1622float2(xa[i]);
+      const float2 yf = __bfloat1622float2(ya[i]);
+      acc = fmaf(xf.x, yf.x, acc);
+      acc = fmaf(xf.y, yf.y, acc);
+    }
+  }
+  return acc;
+}
 
 // Stats sweep: row partial sums over this thread's 32 columns. dD and r3 are
 // accumulated without the softmax scale of ddS (applied once per row after the
@@ -175,7 +201,8 @@ __global__ void __launch_bounds__(kBBThreads, 1)
     bwdbwd_q_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
                     const __grid_constant__ CUtensorMap tm_ddq, const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_ddk,
-                    const __grid_constant__ CUtensorMap tm_ddv, const BBArgs a) {
+                    const __grid_constant__ CUtensorMap tm_ddv, const __grid_constant__ CUtensorMap tm_o,
+                    const BBArgs a) {
   using G = QPass<HD>;
   constexpr int BN = G::BN, ST = G::ST;
   extern __shared__ uint8_t smem_raw[];
@@ -184,9 +211,15 @@ __global__ void __launch_bounds__(kBBThreads, 1)
   uint8_t* s_do = s_q + G::RES;
   uint8_t* s_ddq = s_do + G::RES;
   uint8_t* s_ring = s_ddq + G::RES;
+  // When D is computed here, O is staged in the last ring slot, which the
+  // first ST-1 key tiles do not use; the producer refills that slot only once
+  // every elementwise warp has read O (bar_ofree).
+  uint8_t* s_o = s_ring + (ST - 1) * G::SLOT;
+  static_assert(G::RES <= G::SLOT, "O fits in one ring slot");
   __shared__ uint64_t bar_res, bar_full[ST], bar_empty[ST];
-  __shared__ uint64_t bar_sc_full[2], bar_sc_empty[2], bar_ops_full, bar_ops_empty, bar_acc, bar_red;
+  __shared__ uint64_t bar_sc_full[2], bar_sc_empty[2], bar_ops_full, bar_ops_empty, bar_acc, bar_red, bar_ofree;
   __shared__ float red[4][2][kBM];  // stats-sweep partial sums: statistic, warpgroup, row
+  __shared__ float dred[2][kBM];    // partial rowsum(dO o): warpgroup, row
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
 
@@ -218,6 +251,7 @@ __global__ void __launch_bounds__(kBBThreads, 1)
     mbar_init(&bar_ops_empty, 1);
     mbar_init(&bar_acc, 1);
     mbar_init(&bar_red, kBBEwWarps);
+    mbar_init(&bar_ofree, kBBEwWarps);
     mbar_fence_init();
   }
   if (warp == kBBWarpMma) tmem_alloc(&tmem_base, G::TMEM_COLS);
@@ -230,14 +264,20 @@ __global__ void __launch_bounds__(kBBThreads, 1)
     if (lane == 0) {
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
-      mbar_arrive_expect_tx(&bar_res, 3 * G::RES);
+      const bool fuse_d = a.delta_out != nullptr;
+      mbar_arrive_expect_tx(&bar_res, (fuse_d ? 4 : 3) * G::RES);
       tma_rows<HD>(s_q, &tm_q, &bar_res, q0, kBM, h, b);
       tma_rows<HD>(s_do, &tm_do, &bar_res, q0, kBM, h, b);
       tma_rows<HD>(s_ddq, &tm_ddq, &bar_res, q0, kBM, h, b);
+      if (fuse_d) tma_rows<HD>(s_o, &tm_o, &bar_res, q0, kBM, h, b);
       int issued = 0;
       for (int it = 0; it < total; ++it) {
         const int s = it % ST;
         if (it >= ST && !mbar_wait(&bar_empty[s], ((it / ST) - 1) & 1, &abort_flag)) {
+          raise_error(a.status, &abort_flag, kDevTimeoutSlotEmpty);
+          break;
+        }
+        if (fuse_d && it == ST - 1 && !mbar_wait(&bar_ofree, 0, &abort_flag)) {
           raise_error(a.status, &abort_flag, kDevTimeoutSlotEmpty);
           break;
         }
@@ -325,11 +365,24 @@ __global__ void __launch_bounds__(kBBThreads, 1)
     const bool row_ok = row < sh.Tq;
     const size_t vi = stat_index(b, h, row_ok ? row : 0, sh.H, sh.Tq);
     const float lg = row_ok ? a.lse[vi] * kLog2e : 0.f;
-    const float dv = row_ok ? a.delta[vi] : 0.f;
     const float sc = sh.scale, sc2 = sh.scale * kLog2e;
     float dD = 0.f, r1 = 0.f, r2 = 0.f, r3 = 0.f, Bv = 0.f, cq = 0.f;
     bool ok = true;
-    for (int it = 0; it < total; ++it) {
+    float dv = 0.f;
+    if (a.delta_out == nullptr) {
+      dv = row_ok ? a.delta[vi] : 0.f;
+    } else {
+      // D = rowsum(dO o) of this row from the resident tiles, while the first
+      // scores are computed: each warpgroup sums its 32 columns.
+      ok = mbar_wait_warp(&bar_res, 0, &abort_flag);
+      dv = ok ? rowdot_share<HD>(s_o, s_do, r, wg) : 0.f;
+      dred[wg][r] = dv;
+      warp_arrive(&bar_ofree);  // O has been read: its ring slot may be refilled
+      named_bar_sync(1, kBBEwWarps * 32);
+      dv = dred[0][r] + dred[1][r];
+      if (wg == 0 && row_ok) a.delta_out[vi] = dv;
+    }
+    for (int it = 0; ok && it < total; ++it) {
       const int j = it % n;
       const bool sweep2 = it >= n;
       const int kc = j * BN + cb;  // first key of this thread's columns
@@ -711,7 +764,7 @@ template <int HD>
 int launch_bwdbwd_hd(const AttnShape& s, const BwdBwdPtrs& p, int passes, int* status, cudaStream_t stream) {
   using GQ = QPass<HD>;
   using GK = KPass<HD>;
-  CUtensorMap mq[7], mk[7];
+  CUtensorMap mq[8], mk[7];
   // Query-tiled pass: 128-row query tiles, 64-row key tiles.
   bool ok = make_seq_map(&mq[0], p.q, HD, s.Tq, s.H, s.B, s.sq, kBM) &&
             make_seq_map(&mq[1], p.dO, HD, s.Tq, s.H, s.B, s.sq, kBM) &&
@@ -719,7 +772,8 @@ int launch_bwdbwd_hd(const AttnShape& s, const BwdBwdPtrs& p, int passes, int* s
             make_seq_map(&mq[3], p.k, HD, s.Tk, s.H, s.B, s.sk, GQ::BN) &&
             make_seq_map(&mq[4], p.v, HD, s.Tk, s.H, s.B, s.sk, GQ::BN) &&
             make_seq_map(&mq[5], p.ddk, HD, s.Tk, s.H, s.B, s.sk, GQ::BN) &&
-            make_seq_map(&mq[6], p.ddv, HD, s.Tk, s.H, s.B, s.sk, GQ::BN);
+            make_seq_map(&mq[6], p.ddv, HD, s.Tk, s.H, s.B, s.sk, GQ::BN) &&
+            make_seq_map(&mq[7], p.o ? p.o : p.q, HD, s.Tq, s.H, s.B, s.sq, kBM);  // O: only read when D is fused
   // Key-tiled pass: 128-row key tiles, 64-row query tiles.
   ok = ok && make_seq_map(&mk[0], p.k, HD, s.Tk, s.H, s.B, s.sk, kBM) &&
        make_seq_map(&mk[1], p.v, HD, s.Tk, s.H, s.B, s.sk, kBM) &&
@@ -732,9 +786,11 @@ int launch_bwdbwd_hd(const AttnShape& s, const BwdBwdPtrs& p, int passes, int* s
   if (ensure_smem_limit(reinterpret_cast<const void*>(&bwdbwd_q_kernel<HD>), GQ::SMEM) != kOk ||
       ensure_smem_limit(reinterpret_cast<const void*>(&bwdbwd_k_kernel<HD>), GK::SMEM) != kOk)
     return kLaunchFailed;
+  // With `o`, the query pass computes D into delta_out and the key pass reads it there.
   BBArgs args{s,
               p.lse,
-              p.delta,
+              p.o ? p.delta_out : p.delta,
+              p.o ? p.delta_out : nullptr,
               p.dd,
               p.bv,
               static_cast<__nv_bfloat16*>(p.dq2),
@@ -744,7 +800,8 @@ int launch_bwdbwd_hd(const AttnShape& s, const BwdBwdPtrs& p, int passes, int* s
               status};
   if (passes & kPassQuery) {
     const dim3 gq(s.H, s.B, (s.Tq + kBM - 1) / kBM);
-    bwdbwd_q_kernel<HD><<<gq, kBBThreads, GQ::SMEM, stream>>>(mq[0], mq[1], mq[2], mq[3], mq[4], mq[5], mq[6], args);
+    bwdbwd_q_kernel<HD><<<gq, kBBThreads, GQ::SMEM, stream>>>(mq[0], mq[1], mq[2], mq[3], mq[4], mq[5], mq[6],
+                                                              mq[7], args);
     if (cudaGetLastError() != cudaSuccess) return kLaunchFailed;
   }
   if (passes & kPassKey) {

@@ -220,42 +220,54 @@ int fh_attn_bwd(void* stream, const fh_attn_dims* dims, const void* q, const voi
   return launch_bwd(s, dims->head_dim, BwdPtrs{q, k, v, o, dO, lse, dq, dk, dv, delta}, status, st);
 }
 
+// `o` null: `delta` is an input. `o` set: the query pass computes D into
+// `delta_out`, which the key pass reads.
 static int bwdbwd_entry(const char* entry, void* stream, const fh_attn_dims* dims, const void* q, const void* k,
-                        const void* v, const void* dO, const void* ddq, const void* ddk, const void* ddv,
-                        const float* lse, const float* delta, void* dq2, void* ddo, void* dk2, void* dv2, float* dd,
-                        float* bvec, float scale, int causal, int passes) {
+                        const void* v, const void* o, const void* dO, const void* ddq, const void* ddk,
+                        const void* ddv, const float* lse, const float* delta, float* delta_out, void* dq2, void* ddo,
+                        void* dk2, void* dv2, float* dd, float* bvec, float scale, int causal, int passes) {
   if (injected(entry)) return FH_ERR_INJECTED;
   AttnShape s;
   int rc = validate(dims, &s, scale, causal);
   if (rc != kOk) return rc;
   if (passes < 1 || passes > 3) return fail(FH_ERR_INVALID_ARGUMENT, "pass must be 1, 2 or 3");
-  if (!all_aligned(q, k, v, dO, ddq, ddk, ddv) || !lse || !delta || !dd || !bvec)
+  if (!all_aligned(q, k, v, dO, ddq, ddk, ddv) || !lse || !dd || !bvec)
     return fail(FH_ERR_INVALID_ARGUMENT, kAlignMsg);
+  if (o ? (!all_aligned(o) || !delta_out) : !delta) return fail(FH_ERR_INVALID_ARGUMENT, kAlignMsg);
   if ((passes & kPassQuery) && !all_aligned(dq2, ddo)) return fail(FH_ERR_INVALID_ARGUMENT, kAlignMsg);
   if ((passes & kPassKey) && !all_aligned(dk2, dv2)) return fail(FH_ERR_INVALID_ARGUMENT, kAlignMsg);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if ((rc = select_stream_device(st)) != kOk) return rc;
   int* status = status_word();
   if (!status) return FH_ERR_NO_DEVICE;
-  return launch_bwdbwd(s, dims->head_dim,
-                       BwdBwdPtrs{q, k, v, dO, ddq, ddk, ddv, lse, delta, dq2, ddo, dk2, dv2, dd, bvec}, passes,
-                       status, st);
+  return launch_bwdbwd(
+      s, dims->head_dim,
+      BwdBwdPtrs{q, k, v, dO, ddq, ddk, ddv, lse, delta, dq2, ddo, dk2, dv2, dd, bvec, o, delta_out}, passes,
+      status, st);
 }
 
 int fh_attn_bwdbwd(void* stream, const fh_attn_dims* dims, const void* q, const void* k, const void* v,
                    const void* dO, const void* ddq, const void* ddk, const void* ddv, const float* lse,
                    const float* delta, void* dq2, void* ddo, void* dk2, void* dv2, float* dd, float* bvec,
                    float scale, int causal) {
-  return bwdbwd_entry("fh_attn_bwdbwd", stream, dims, q, k, v, dO, ddq, ddk, ddv, lse, delta, dq2, ddo, dk2, dv2,
-                      dd, bvec, scale, causal, kPassQuery | kPassKey);
+  return bwdbwd_entry("fh_attn_bwdbwd", stream, dims, q, k, v, nullptr, dO, ddq, ddk, ddv, lse, delta, nullptr, dq2,
+                      ddo, dk2, dv2, dd, bvec, scale, causal, kPassQuery | kPassKey);
 }
 
 int fh_attn_bwdbwd_pass(void* stream, const fh_attn_dims* dims, const void* q, const void* k, const void* v,
                         const void* dO, const void* ddq, const void* ddk, const void* ddv, const float* lse,
                         const float* delta, void* dq2, void* ddo, void* dk2, void* dv2, float* dd, float* bvec,
                         float scale, int causal, int pass) {
-  return bwdbwd_entry("fh_attn_bwdbwd_pass", stream, dims, q, k, v, dO, ddq, ddk, ddv, lse, delta, dq2, ddo, dk2,
-                      dv2, dd, bvec, scale, causal, pass);
+  return bwdbwd_entry("fh_attn_bwdbwd_pass", stream, dims, q, k, v, nullptr, dO, ddq, ddk, ddv, lse, delta, nullptr,
+                      dq2, ddo, dk2, dv2, dd, bvec, scale, causal, pass);
+}
+
+int fh_attn_bwdbwd_o(void* stream, const fh_attn_dims* dims, const void* q, const void* k, const void* v,
+                     const void* o, const void* dO, const void* ddq, const void* ddk, const void* ddv,
+                     const float* lse, void* dq2, void* ddo, void* dk2, void* dv2, float* delta, float* dd,
+                     float* bvec, float scale, int causal, int passes) {
+  return bwdbwd_entry("fh_attn_bwdbwd_o", stream, dims, q, k, v, o, dO, ddq, ddk, ddv, lse, nullptr, delta, dq2, ddo,
+                      dk2, dv2, dd, bvec, scale, causal, passes);
 }
 
 int fh_device_status(void* stream, int* code) {

@@ -37,6 +37,10 @@ struct BwdBwdPtrs {
   const float *lse, *delta;
   void *dq2, *ddo, *dk2, *dv2;
   float *dd, *bv;  // scratch written by the query-tiled pass, read by the key-tiled pass
+  // Optional: with `o` set, D = rowsum(dO o) is computed by the query-tiled pass
+  // into `delta_out` (which the key-tiled pass then reads) and `delta` is unused.
+  const void* o = nullptr;
+  float* delta_out = nullptr;
 };
 
 int launch_fwd(const AttnShape& s, int hd, const FwdPtrs& p, int* status, cudaStream_t stream);

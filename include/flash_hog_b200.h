@@ -121,6 +121,21 @@ int fh_attn_bwdbwd_pass(void* stream, const fh_attn_dims* dims, const void* q, c
                         const float* delta, void* dq2, void* ddo, void* dk2, void* dv2, float* dd, float* bvec,
                         float scale, int causal, int pass);
 
+/* Double backward from the forward output o instead of a precomputed delta:
+ * the query-tiled pass computes D = rowsum(dO * o) for its rows itself and
+ * writes it to `delta` (caller scratch of batch*heads*seq_q floats), which the
+ * key-tiled pass reads -- one kernel launch fewer than fh_attn_rowdot followed
+ * by fh_attn_bwdbwd, same results up to the summation order of D.
+ * Replaces the reference's flash_bwdbwd (flash_hog/jax/_tk_gpu.py:83-103, which
+ * computes D with an XLA einsum at _tk_gpu.py:93 before calling TkBwdBwd;
+ * the Pallas rule does the same at _pallas_gpu_kernel.py:110).
+ * `passes`: FH_PASS_QUERY, FH_PASS_KEY (after a query pass on the same
+ * buffers) or both (3). */
+int fh_attn_bwdbwd_o(void* stream, const fh_attn_dims* dims, const void* q, const void* k, const void* v,
+                     const void* o, const void* dO, const void* ddq, const void* ddk, const void* ddv,
+                     const float* lse, void* dq2, void* ddo, void* dk2, void* dv2, float* delta, float* dd,
+                     float* bvec, float scale, int causal, int passes);
+
 /* Allocation-free double backward. No counterpart in the reference: it exists
  * for callers that cannot allocate device memory while they run -- an XLA FFI
  * handler only gets the buffers XLA assigned up front (and JAX reserves most of

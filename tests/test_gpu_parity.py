@@ -116,12 +116,22 @@ def test_unbatched_and_bhtd_layouts():
     dd, bv = torch.empty_like(delta), torch.empty_like(delta)
     dq2, ddo = torch.empty_like(q), torch.empty_like(q)
     dk2, dv2 = torch.empty_like(k), torch.empty_like(k)
-    _capi.attn_rowdot(o, do, delta)
-    _capi.attn_bwdbwd(q, k, v, do, ddq, ddk, ddv, x["lse"], delta, dq2, ddo, dk2, dv2, dd, bv, 0.125, True)
+    _capi.attn_bwdbwd_o(q, k, v, o, do, ddq, ddk, ddv, x["lse"], dq2, ddo, dk2, dv2, delta, dd, bv, 0.125, True)
+    # The delta-input entry (D from fh_attn_rowdot) sums D in another order: equal
+    # up to bf16 rounding of the outputs.
+    delta_r, dd_r, bv_r = (torch.empty_like(delta) for _ in range(3))
+    r2 = [torch.empty_like(t) for t in (dq2, ddo, dk2, dv2)]
+    _capi.attn_rowdot(o, do, delta_r)
+    _capi.attn_bwdbwd(q, k, v, do, ddq, ddk, ddv, x["lse"], delta_r, r2[0], r2[1], r2[2], r2[3], dd_r, bv_r,
+                      0.125, True)
     torch.cuda.synchronize()
     for a, u, s in zip(full, unb, (dq2, dk2, dv2, ddo)):
         assert torch.equal(a[0], u)
         assert torch.equal(a, s)
+    assert torch.allclose(delta_r, delta, rtol=1e-5, atol=1e-5)
+    for got, ref in zip(r2, (dq2, ddo, dk2, dv2)):
+        err = (got.float() - ref.float()).abs().max().item() / ref.float().abs().max().item()
+        assert err < 1e-2, err
 
 
 def test_headline_config_full_size_sampled_heads():
