@@ -481,57 +481,70 @@ struct KPass {
   static constexpr int STR = BN * HD * 2;
   static constexpr int PAIR = 2 * STR;
   static constexpr int PAIR_PANEL = 2 * BN * 128;
-  static constexpr int VEC = BN * 4;               // one fp32 statistic per streamed query
-  static constexpr int SLOT = PAIR + STR + 4 * VEC;  // (Q | ddQ) pair, dO, then L, D, dD, c = dD D + B
-  static constexpr int SMEM = 1024 + 4 * RES + ST * SLOT;
+  // Per-query biases of the four score products as a K = 16 bf16 operand
+  // (32-byte rows, 32B swizzle): rows [64 m, 64 m + 64) hold product m's bias
+  // for each streamed query as a (hi, lo) bf16 pair in columns 0-1, zeros after.
+  static constexpr int BIAS_ROW = 32;
+  static constexpr int BIAS = 4 * BN * BIAS_ROW;
+  static constexpr int ONES = kBM * BIAS_ROW;      // resident A operand: (1, 1, 0, ...) per key row
+  static constexpr int SLOT = PAIR + STR + BIAS;   // (Q | ddQ) pair, dO, biases
+  static constexpr int SMEM = 1024 + 4 * RES + ONES + ST * SLOT;
   // TMEM: scores, accumulators dK', dV', bf16 operands dS^T, dS2^T, ddP^T (A of the MMAs).
   static constexpr int C_S = 0, C_DDS = BN, C_DP = 2 * BN, C_DPA = 3 * BN;
   static constexpr int C_DK = 4 * BN, C_DV = 4 * BN + HD, C_OPS = 4 * BN + 2 * HD;
   static constexpr int OPS_COLS = BN / 2;
   static constexpr int TMEM_COLS = 512;
-  static_assert(SLOT % 1024 == 0, "slots must keep panels 1024-byte aligned");
+  static_assert(SLOT % 1024 == 0 && (4 * RES + ONES) % 1024 == 0, "slots must keep panels 1024-byte aligned");
   static_assert(C_OPS + 3 * OPS_COLS <= TMEM_COLS, "TMEM budget");
+  static_assert(C_DDS == C_S + BN && C_DP == C_S + 2 * BN && C_DPA == C_S + 3 * BN, "one bias MMA covers 4 products");
   static_assert(SMEM <= 232448, "shared memory budget");
   static_assert(BN == 64, "two warpgroups x 32 columns");
 };
 
 // Packed bf16 pairs of dS^T/scale, dS2^T/scale and ddP^T for this thread's 32
 // query columns (the scale of dS, dS2 is applied to dK' in the epilogue), by
-// the same identities as the query pass. sv points at this thread's first
-// column of the slot's statistics block [L log2(e) | D | dD | c = dD D + B]
-// (BN floats each, 16-byte aligned), read four columns per load.
+// the same identities as the query pass. The per-query statistics arrive
+// already folded into the score products by the bias MMA:
+//   vs = S - L/scale,  vdds = ddS/scale - dD/scale,  vdp = dP - D,  vdpa = dPa - c.
 template <bool MASK>
 __device__ __forceinline__ void k_ops32(const uint32_t (&vs)[32], const uint32_t (&vdds)[32],
-                                        const uint32_t (&vdp)[32], const uint32_t (&vdpa)[32], const float* sv,
-                                        int qc, int key, int tq, int causal, float sc, float sc2,
-                                        uint32_t (&o_ds)[16], uint32_t (&o_ds2)[16], uint32_t (&o_ddp)[16]) {
-  constexpr int BN = 64;
-  const float4* sv4 = reinterpret_cast<const float4*>(sv);
+                                        const uint32_t (&vdp)[32], const uint32_t (&vdpa)[32], int qc, int key,
+                                        int tq, int causal, float sc, float sc2, uint32_t (&o_ds)[16],
+                                        uint32_t (&o_ds2)[16], uint32_t (&o_ddp)[16]) {
 #pragma unroll
-  for (int i = 0; i < 32; i += 4) {
-    const float4 l4 = sv4[i / 4], d4 = sv4[(BN + i) / 4], dd4 = sv4[(2 * BN + i) / 4], c4 = sv4[(3 * BN + i) / 4];
-    const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dv[4] = {d4.x, d4.y, d4.z, d4.w};
-    const float ddv[4] = {dd4.x, dd4.y, dd4.z, dd4.w}, cv[4] = {c4.x, c4.y, c4.z, c4.w};
-    float ddp[4], ds[4], ds2[4];
+  for (int i = 0; i < 32; i += 2) {
+    float ddp[2], ds[2], ds2[2];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
+    for (int e = 0; e < 2; ++e) {
       const int c = i + e;
-      float s = fmaf(__uint_as_float(vs[c]), sc2, -lv[e]);
+      float s = __uint_as_float(vs[c]) * sc2;
       if (MASK && (qc + c >= tq || (causal && qc + c < key))) s = -INFINITY;
       const float p = ex2(s);
-      const float u = fmaf(__uint_as_float(vdds[c]), sc, -ddv[e]);  // ddS - dD
-      const float dpd = __uint_as_float(vdp[c]) - dv[e];           // dP - D
+      const float u = __uint_as_float(vdds[c]) * sc;  // ddS - dD
+      const float dpd = __uint_as_float(vdp[c]);      // dP - D
       ddp[e] = p * u;
       ds[e] = p * dpd;
-      ds2[e] = fmaf(ddp[e], dpd, p * (__uint_as_float(vdpa[c]) - cv[e]));
+      ds2[e] = fmaf(ddp[e], dpd, p * __uint_as_float(vdpa[c]));
     }
-#pragma unroll
-    for (int e = 0; e < 4; e += 2) {
-      o_ddp[(i + e) / 2] = pack_bf16(ddp[e], ddp[e + 1]);
-      o_ds[(i + e) / 2] = pack_bf16(ds[e], ds[e + 1]);
-      o_ds2[(i + e) / 2] = pack_bf16(ds2[e], ds2[e + 1]);
-    }
+    o_ddp[i / 2] = pack_bf16(ddp[0], ddp[1]);
+    o_ds[i / 2] = pack_bf16(ds[0], ds[1]);
+    o_ds2[i / 2] = pack_bf16(ds2[0], ds2[1]);
   }
+}
+
+// One 16-byte chunk of a 32B-swizzled K = 16 bf16 operand row (tiles 256-byte aligned).
+__device__ __forceinline__ uint32_t sw32_offset(int r, int c) {
+  return static_cast<uint32_t>(r * 32 + ((c ^ ((r >> 2) & 1)) << 4));
+}
+
+// Writes (hi, lo) with hi + lo = x to within 2^-16 |x| as row r of a bias operand.
+__device__ __forceinline__ void store_bias_row(uint32_t tile, int r, float x) {
+  const __nv_bfloat16 hi = __float2bfloat16_rn(x);
+  const __nv_bfloat16 lo = __float2bfloat16_rn(x - __bfloat162float(hi));
+  const uint32_t pair = static_cast<uint32_t>(__bfloat16_as_ushort(hi)) |
+                        (static_cast<uint32_t>(__bfloat16_as_ushort(lo)) << 16);
+  st_shared_v4(tile + sw32_offset(r, 0), pair, 0u, 0u, 0u);
+  st_shared_v4(tile + sw32_offset(r, 1), 0u, 0u, 0u, 0u);
 }
 
 template <int HD>
@@ -548,7 +561,8 @@ __global__ void __launch_bounds__(kBBThreads, 1)
   uint8_t* s_v = s_k + G::RES;
   uint8_t* s_ddk = s_v + G::RES;
   uint8_t* s_ddv = s_ddk + G::RES;
-  uint8_t* s_ring = s_ddv + G::RES;
+  uint8_t* s_ones = s_ddv + G::RES;
+  uint8_t* s_ring = s_ones + G::ONES;
   __shared__ uint64_t bar_res, bar_full[ST], bar_empty[ST];
   __shared__ uint64_t bar_sc_full, bar_sc_empty, bar_ops_full, bar_ops_empty, bar_acc;
   __shared__ uint32_t tmem_base;
@@ -577,6 +591,14 @@ __global__ void __launch_bounds__(kBBThreads, 1)
     mbar_init(&bar_acc, 1);
     mbar_fence_init();
   }
+  if (threadIdx.x < kBM) {
+    // The resident ones operand: row r = (1, 1, 0, ..., 0), so ones x biases^T
+    // adds hi + lo of each query's bias to every key row.
+    const uint32_t t = smem_u32(s_ones);
+    st_shared_v4(t + sw32_offset(threadIdx.x, 0), 0x3F803F80u, 0u, 0u, 0u);
+    st_shared_v4(t + sw32_offset(threadIdx.x, 1), 0u, 0u, 0u, 0u);
+    fence_async_smem();
+  }
   if (warp == kBBWarpMma) tmem_alloc(&tmem_base, G::TMEM_COLS);
   __syncthreads();
   tc_fence_after();
@@ -594,6 +616,7 @@ __global__ void __launch_bounds__(kBBThreads, 1)
       tma_rows<HD>(s_ddv, &tm_ddv, &bar_res, k0, kBM, h, b);
     }
     int issued = 0;
+    const float inv_scale = 1.f / sh.scale;
     for (int it = 0; it < n; ++it) {
       const int s = it % ST;
       const int q0 = (qt_begin + it) * BN;
@@ -605,21 +628,23 @@ __global__ void __launch_bounds__(kBBThreads, 1)
         const int q = q0 + lane + 32 * k;
         const bool v = q < sh.Tq;
         const size_t idx = stat_index(b, h, v ? q : 0, sh.H, sh.Tq);
-        st[k][0] = v ? a.lse[idx] * kLog2e : 0.f;
-        st[k][1] = v ? a.delta[idx] : 0.f;
-        st[k][2] = v ? a.dd[idx] : 0.f;
-        st[k][3] = v ? fmaf(st[k][2], st[k][1], a.bv[idx]) : 0.f;  // c = dD D + B
+        const float lse = v ? a.lse[idx] : 0.f, dl = v ? a.delta[idx] : 0.f, ddl = v ? a.dd[idx] : 0.f;
+        st[k][0] = -lse * inv_scale;                            // S - L/scale
+        st[k][1] = -ddl * inv_scale;                            // ddS/scale - dD/scale
+        st[k][2] = -dl;                                         // dP - D
+        st[k][3] = v ? -fmaf(ddl, dl, a.bv[idx]) : 0.f;         // dPa - c, c = dD D + B
       }
       if (it >= ST && !mbar_wait_warp(&bar_empty[s], ((it / ST) - 1) & 1, &abort_flag)) {
         if (lane == 0) raise_error(a.status, &abort_flag, kDevTimeoutSlotEmpty);
         break;
       }
       uint8_t* slot = s_ring + s * G::SLOT;
-      float* sv = reinterpret_cast<float*>(slot + G::PAIR + G::STR);
+      const uint32_t bias = smem_u32(slot + G::PAIR + G::STR);
 #pragma unroll
       for (int k = 0; k < 2; ++k)
 #pragma unroll
-        for (int m = 0; m < 4; ++m) sv[m * BN + lane + 32 * k] = st[k][m];
+        for (int m = 0; m < 4; ++m) store_bias_row(bias, m * BN + lane + 32 * k, st[k][m]);
+      fence_async_smem();  // the tensor core reads the biases through the async proxy
       __syncwarp();
       if (lane == 0) {
         mbar_arrive_expect_tx(&bar_full[s], G::PAIR + G::STR);
@@ -645,6 +670,9 @@ __global__ void __launch_bounds__(kBBThreads, 1)
       const uint64_t a_k = kdesc(s_k), a_v = kdesc(s_v), a_ddk = kdesc(s_ddk), a_ddv = kdesc(s_ddv);
       const uint64_t b_ring = kdesc(s_ring);          // pair (Q | ddQ) of slot 0
       const uint64_t b_do = kdesc(s_ring + G::PAIR);  // dO of slot 0
+      const uint32_t id_bias = idesc_bf16_f32(kBM, 4 * BN, false, false);
+      const uint64_t a_ones = smem_desc(smem_u32(s_ones), 16, 8 * G::BIAS_ROW, kSwizzle32B);
+      const uint64_t b_bias = smem_desc(smem_u32(s_ring + G::PAIR + G::STR), 16, 8 * G::BIAS_ROW, kSwizzle32B);
       constexpr uint64_t kSlot = G::SLOT >> 4;
       bool ok = mbar_wait_warp(&bar_res, 0, &abort_flag);
       if (!ok && lane == 0) raise_error(a.status, &abort_flag, kDevTimeoutTmaFull);
@@ -660,10 +688,12 @@ __global__ void __launch_bounds__(kBBThreads, 1)
         }
         tc_fence_after();
         const uint64_t bq = b_ring + s * kSlot, bo = b_do + s * kSlot;
-        umma_chain_w<KS, G::RES_PANEL, G::PAIR_PANEL, false>(tmem + G::C_S, a_k, bq, id128, false);
+        // Biases first (one N = 4 BN MMA over all four products), then the products accumulate.
+        umma_bf16_w(tmem + G::C_S, a_ones, b_bias + s * kSlot, id_bias, 0u);
+        umma_chain_w<KS, G::RES_PANEL, G::PAIR_PANEL, false>(tmem + G::C_S, a_k, bq, id128, true);
         umma_chain_w<KS, G::RES_PANEL, G::PAIR_PANEL, false>(tmem + G::C_DDS, a_ddk, bq, id64, true);
-        umma_chain_w<KS, G::RES_PANEL, BN * 128, false>(tmem + G::C_DP, a_v, bo, id64, false);
-        umma_chain_w<KS, G::RES_PANEL, BN * 128, false>(tmem + G::C_DPA, a_ddv, bo, id64, false);
+        umma_chain_w<KS, G::RES_PANEL, BN * 128, false>(tmem + G::C_DP, a_v, bo, id64, true);
+        umma_chain_w<KS, G::RES_PANEL, BN * 128, false>(tmem + G::C_DPA, a_ddv, bo, id64, true);
         umma_commit_w(&bar_sc_full);
       }
     }
@@ -722,13 +752,12 @@ __global__ void __launch_bounds__(kBBThreads, 1)
       reg_fence32(vdp);
       reg_fence32(vdpa);
       warp_arrive(&bar_sc_empty);
-      const float* sv = reinterpret_cast<const float*>(s_ring + s * G::SLOT + G::PAIR + G::STR) + cb;
       const bool need_mask = (qc + 32 > sh.Tq) || (sh.causal && qc < key);
       uint32_t o_ds[16], o_ds2[16], o_ddp[16];
       if (need_mask)
-        k_ops32<true>(vs, vdds, vdp, vdpa, sv, qc, key, sh.Tq, sh.causal, sc, sc2, o_ds, o_ds2, o_ddp);
+        k_ops32<true>(vs, vdds, vdp, vdpa, qc, key, sh.Tq, sh.causal, sc, sc2, o_ds, o_ds2, o_ddp);
       else
-        k_ops32<false>(vs, vdds, vdp, vdpa, sv, qc, key, sh.Tq, sh.causal, sc, sc2, o_ds, o_ds2, o_ddp);
+        k_ops32<false>(vs, vdds, vdp, vdpa, qc, key, sh.Tq, sh.causal, sc, sc2, o_ds, o_ds2, o_ddp);
       if (it > 0) ok = mbar_wait_warp(&bar_ops_empty, (it - 1) & 1, &abort_flag);
       if (!ok) break;
       tc_fence_after();
