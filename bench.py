@@ -41,6 +41,7 @@ CAUSAL = True
 SCALE = D ** -0.5
 N_SETS = 3  # rotating input sets, each larger than the 126 MB L2
 PEAKS_FILE = os.path.join(ROOT, "MEASURED_PEAKS.json")
+QPASS_DRAM_BYTES = 214.9e6  # ncu dram read + write of one query-pass launch (profiles/)
 FALLBACK_PEAKS = {"bf16_tflops": 1590.0, "hbm_gbs": 6650.0}
 
 
@@ -319,7 +320,9 @@ def main():
     roofline = {"bound": "tensor", "kernel": "bwdbwd_q_kernel (query-tiled pass, 14 of 22 GEMM-eq)",
                 "achieved": achieved, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                 "frac": achieved / peaks["bf16_tflops"], "peak_source": f"{peak_kind} bf16 dense (burst)",
-                "traffic": None,
+                # dram__bytes_read.sum + dram__bytes_write.sum of one query-pass launch of this
+                # workload, from the ncu capture summarised in profiles/bwdbwd_b4h16s2048d64_causal.md
+                "traffic": QPASS_DRAM_BYTES, "traffic_unit": "bytes per launch (ncu)",
                 "per_launch_ms": {"query_pass": t_q, "key_pass": t_k},
                 "key_pass": {"achieved": credited_flops(B, H, S, gemms=8) / (t_k * 1e-3) / 1e12}}
     cpu = None
