@@ -214,7 +214,7 @@ struct DkvPass {
   static constexpr int OPS = kBM * BN * 2;
   static constexpr int SMEM = 1024 + 2 * RES + ST * SLOT + 2 * OPS;
   static constexpr int C_S = 0, C_DP = BN, C_DK = 2 * BN, C_DV = 2 * BN + HD;
-  static constexpr int TMEM_COLS = 256;
+  static constexpr int TMEM_COLS = C_DV + HD <= 256 ? 256 : 512;
   static_assert(C_DV + HD <= TMEM_COLS, "TMEM budget");
 };
 
@@ -452,6 +452,7 @@ int launch_bwd_hd(const AttnShape& s, const BwdPtrs& p, int* status, cudaStream_
 
 int launch_bwd(const AttnShape& s, int hd, const BwdPtrs& p, int* status, cudaStream_t stream) {
   if (hd == 64) return launch_bwd_hd<64>(s, p, status, stream);
+  if (hd == 128) return launch_bwd_hd<128>(s, p, status, stream);
   return kUnsupported;
 }
 

@@ -101,7 +101,7 @@ int validate(const fh_attn_dims* d, AttnShape* out, float scale, int causal) {
   if (!d) return fail(kInvalidArgument, "dims is NULL");
   if (d->batch < 1 || d->heads < 1 || d->seq_q < 1 || d->seq_k < 1)
     return fail(kInvalidArgument, "batch, heads, seq_q and seq_k must be >= 1");
-  if (d->head_dim != 64) return fail(kUnsupported, "head_dim must be 64");
+  if (d->head_dim != 64 && d->head_dim != 128) return fail(kUnsupported, "head_dim must be 64 or 128");
   if (!strides_ok(d->q) || !strides_ok(d->k))
     return fail(kInvalidArgument, "strides must be non-negative multiples of 8 elements (seq stride > 0)");
   if (!(scale == scale)) return fail(kInvalidArgument, "scale is NaN");
@@ -231,6 +231,7 @@ static int bwdbwd_entry(const char* entry, void* stream, const fh_attn_dims* dim
   int rc = validate(dims, &s, scale, causal);
   if (rc != kOk) return rc;
   if (passes < 1 || passes > 3) return fail(FH_ERR_INVALID_ARGUMENT, "pass must be 1, 2 or 3");
+  if (dims->head_dim != 64) return fail(FH_ERR_UNSUPPORTED, "the double backward supports head_dim 64");
   if (!all_aligned(q, k, v, dO, ddq, ddk, ddv) || !lse || !dd || !bvec)
     return fail(FH_ERR_INVALID_ARGUMENT, kAlignMsg);
   if (o ? (!all_aligned(o) || !delta_out) : !delta) return fail(FH_ERR_INVALID_ARGUMENT, kAlignMsg);
@@ -348,6 +349,7 @@ extern "C" int fh_attn_bwdbwd_noalloc(void* stream, const fh_attn_dims* dims, co
   int rc = validate(dims, &s, scale, causal);
   if (rc != kOk) return rc;
   const long long rows = static_cast<long long>(s.B) * s.H * s.Tq;
+  if (dims->head_dim != 64) return fail(FH_ERR_UNSUPPORTED, "the double backward supports head_dim 64");
   if (rows > kNoAllocMaxRows) {
     char msg[240];
     std::snprintf(msg, sizeof(msg),

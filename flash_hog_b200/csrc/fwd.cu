@@ -28,7 +28,7 @@ struct FwdArgs {
 template <int HD>
 struct FPass {
   static constexpr int BN = 128;
-  static constexpr int ST = 3;
+  static constexpr int ST = HD == 128 ? 2 : 3;  // K|V slots: 64 KB each at head_dim 128
   static constexpr int RES = kBM * HD * 2;
   static constexpr int STR = BN * HD * 2;
   static constexpr int SLOT = 2 * STR;       // K | V
@@ -285,6 +285,7 @@ int launch_fwd_hd(const AttnShape& s, const FwdPtrs& p, int* status, cudaStream_
 
 int launch_fwd(const AttnShape& s, int hd, const FwdPtrs& p, int* status, cudaStream_t stream) {
   if (hd == 64) return launch_fwd_hd<64>(s, p, status, stream);
+  if (hd == 128) return launch_fwd_hd<128>(s, p, status, stream);
   return kUnsupported;
 }
 

@@ -83,6 +83,43 @@ def test_fwd_bwd_match_oracle(b, h, tq, tk, causal):
     assert_close("dV", np64(dv), rv)
 
 
+HD128_CASES = [
+    # b, h, tq, tk, causal -- head_dim 128 (the long-sequence and cross-attention configs)
+    (1, 2, 128, 128, True),
+    (1, 2, 256, 384, False),
+    (1, 1, 200, 200, True),
+    (1, 2, 72, 136, False),
+    (2, 2, 512, 512, True),
+]
+
+
+@pytest.mark.parametrize("b,h,tq,tk,causal", HD128_CASES)
+def test_fwd_bwd_match_oracle_hd128(b, h, tq, tk, causal):
+    from flash_hog_b200 import MaskType
+    from flash_hog_b200 import _attention_impl as impl
+    from flash_hog_b200._capi import device_status
+
+    x = case_inputs(b, h, tq, tk, d=128, seed=5 * tq + tk, causal=causal)
+    g = _cuda(x)
+    mask = MaskType.CAUSAL if causal else MaskType.NO_MASK
+    scale = 128 ** -0.5
+    out, lse = impl.cuda_dot_product_attention(g["q"], g["k"], g["v"], mask, scale, return_residual=True)
+    torch.cuda.synchronize()
+    assert device_status() == 0
+    ro, rl = ora.attention_fwd(np64(x["q"]), np64(x["k"]), np64(x["v"]), causal=causal)
+    assert_close("O", np64(out), ro)
+    assert ora.max_abs(np64(lse), rl) <= 2e-3
+    dq, dk, dv = impl.dot_product_attention_bwd_rule(mask, scale, (g["q"], g["k"], g["v"], g["lse"], g["o"]),
+                                                     g["do"])
+    torch.cuda.synchronize()
+    assert device_status() == 0
+    rq, rk, rv = ora.attention_bwd(np64(x["q"]), np64(x["k"]), np64(x["v"]), np64(x["o"]), np64(x["lse"]),
+                                   np64(x["do"]), causal=causal)
+    assert_close("dQ", np64(dq), rq)
+    assert_close("dK", np64(dk), rk)
+    assert_close("dV", np64(dv), rv)
+
+
 @pytest.mark.parametrize("causal", [True, False])
 def test_nested_autograd_matches_double_autograd(causal):
     """grad-of-grad through the public API vs torch double autograd of naive attention."""
