@@ -157,11 +157,15 @@ __device__ __forceinline__ void umma_chain_w(uint32_t d, uint64_t a0, uint64_t b
 
 template <int KSTEPS>
 __device__ __forceinline__ void umma_chain_ts_w(uint32_t d, uint32_t a_tmem, uint64_t b0, uint32_t idesc, bool acc) {
-  static_assert(KSTEPS % 4 == 0, "chains are issued four k-steps at a time");
+  static_assert(KSTEPS % 4 == 0 || KSTEPS == 2, "chains are issued four (or two) k-steps at a time");
+  if constexpr (KSTEPS == 2) {
+    umma_bf16_ts_x2_w(d, a_tmem, b0 + mnoff(0), b0 + mnoff(1), idesc, acc ? 1u : 0u);
+  } else {
 #pragma unroll
-  for (int ks = 0; ks < KSTEPS; ks += 4)
-    umma_bf16_ts_x4_w(d, a_tmem + 8 * ks, b0 + mnoff(ks), b0 + mnoff(ks + 1), b0 + mnoff(ks + 2),
-                      b0 + mnoff(ks + 3), idesc, (acc || ks > 0) ? 1u : 0u);
+    for (int ks = 0; ks < KSTEPS; ks += 4)
+      umma_bf16_ts_x4_w(d, a_tmem + 8 * ks, b0 + mnoff(ks), b0 + mnoff(ks + 1), b0 + mnoff(ks + 2),
+                        b0 + mnoff(ks + 3), idesc, (acc || ks > 0) ? 1u : 0u);
+  }
 }
 
 // Loads a pair of BN-row tiles (X then Y) of HD columns into "pair" panels:

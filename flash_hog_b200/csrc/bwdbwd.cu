@@ -52,13 +52,13 @@ struct BBArgs {
 // 11 warps. Warp 0 allocates TMEM and issues the score MMAs, warp 1 issues the
 // accumulating (operand) MMAs, warp 2 is the TMA producer, warps 3-10 are two
 // elementwise warpgroups: thread (warp, lane) owns TMEM lane 32*(warp%4)+lane
-// (one resident row) and warpgroup w = (warp-3)/4 owns columns [32w, 32w+32)
-// of every 64-row streamed tile. TMEM lane quadrants pin the elementwise warps
+// (one resident row) and warpgroup w = (warp-3)/4 owns columns [CW w, CW w + CW)
+// of every BN-row streamed tile (CW = BN/2: 32 at head_dim 64, 16 at 128). TMEM lane quadrants pin the elementwise warps
 // to all four schedulers, and their arithmetic starves a co-resident issuing
 // thread; two issuers on different schedulers halve that exposure and let the
 // score MMAs of the next tile and the operand MMAs of this tile be issued
 // independently, each as soon as its inputs are ready.
-// Each elementwise thread loads its 32-column share of all four score tiles
+// Each elementwise thread loads its CW-column share of all four score tiles
 // into registers and releases the score buffer at once. The bf16 operands it
 // produces (dS, dS2, ddP, P) go back to TMEM with tcgen05.st and are read there
 // as the A operand of the accumulating MMAs.
@@ -76,15 +76,27 @@ __device__ __forceinline__ void warp_arrive(uint64_t* bar) {
   if ((threadIdx.x & 31) == 0) mbar_arrive(bar);
 }
 
-// This thread's 32-column share of a score tile (two x16 loads).
-__device__ __forceinline__ void tmem_share32(uint32_t tmem, int warp, int col, uint32_t (&r)[32]) {
-  tmem_ld16(tmem + tmem_lane_base(warp & 3) + col, *reinterpret_cast<uint32_t(*)[16]>(&r[0]));
-  tmem_ld16(tmem + tmem_lane_base(warp & 3) + col + 16, *reinterpret_cast<uint32_t(*)[16]>(&r[16]));
+// This thread's CW-column share of a score tile (x16 loads).
+template <int CW>
+__device__ __forceinline__ void tmem_share(uint32_t tmem, int warp, int col, uint32_t (&r)[CW]) {
+  static_assert(CW % 16 == 0, "shares are whole x16 loads");
+#pragma unroll
+  for (int c = 0; c < CW; c += 16)
+    tmem_ld16(tmem + tmem_lane_base(warp & 3) + col + c, *reinterpret_cast<uint32_t(*)[16]>(&r[c]));
 }
 
-__device__ __forceinline__ void reg_fence32(uint32_t (&r)[32]) {
+template <int N>
+__device__ __forceinline__ void reg_fence(uint32_t (&r)[N]) {
 #pragma unroll
-  for (int i = 0; i < 32; ++i) asm volatile("" : "+r"(r[i])::"memory");
+  for (int i = 0; i < N; ++i) asm volatile("" : "+r"(r[i])::"memory");
+}
+
+// Stores a thread's N packed bf16 operand columns (N = 16 or 8) to TMEM.
+template <int N>
+__device__ __forceinline__ void tmem_st_ops(uint32_t taddr, const uint32_t (&r)[N]) {
+  static_assert(N == 16 || N == 8, "operand shares are 16 or 8 packed columns");
+  if constexpr (N == 16) tmem_st16(taddr, r);
+  else tmem_st8(taddr, r);
 }
 
 // ----------------------------------------------------------------------------------
@@ -93,8 +105,11 @@ __device__ __forceinline__ void reg_fence32(uint32_t (&r)[32]) {
 
 template <int HD>
 struct QPass {
-  static constexpr int BN = 64;                    // key rows per streamed tile
-  static constexpr int ST = 4;                     // ring depth
+  // Key rows per streamed tile and ring depth: 64 x 4 at head_dim 64; 32 x 3 at
+  // 128, where accumulators of 2 x 128 columns leave TMEM room for 32-key scores.
+  static constexpr int BN = HD == 64 ? 64 : 32;
+  static constexpr int ST = HD == 64 ? 4 : 3;
+  static constexpr int CW = BN / 2;                // columns of a tile per elementwise thread
   static constexpr int RES = kBM * HD * 2;         // one resident bf16 tile (panels of 128 rows)
   static constexpr int RES_PANEL = kBM * 128;
   static constexpr int STR = BN * HD * 2;          // one streamed bf16 tile
@@ -112,10 +127,10 @@ struct QPass {
   static_assert(C_OPS + 4 * OPS_COLS <= TMEM_COLS, "TMEM budget");
   static_assert(2 * SCORE_COLS <= TMEM_COLS, "stats sweep double-buffers the scores");
   static_assert(SMEM <= 232448, "shared memory budget");
-  static_assert(BN == 64, "two warpgroups x 32 columns");
+  static_assert(CW % 16 == 0 && HD % 64 == 0, "tile shapes");
 };
 
-// Partial rowsum(dO o) over columns [32 wg, 32 wg + 32) of row r of two
+// Partial rowsum(dO o) over head_dim columns [HD/2 wg, HD/2 wg + HD/2) of row r of two
 // resident 128-row tiles (128B-swizzled 64-column panels, as loaded by TMA).
 template <int HD>
 __device__ __forceinline__ float rowdot_share(const uint8_t* s_o, const uint8_t* s_do, int r, int wg) {
@@ -140,16 +155,16 @@ __device__ __forceinline__ float rowdot_share(const uint8_t* s_o, const uint8_t*
   return acc;
 }
 
-// Stats sweep: row partial sums over this thread's 32 columns. dD and r3 are
+// Stats sweep: row partial sums over this thread's CW columns. dD and r3 are
 // accumulated without the softmax scale of ddS (applied once per row after the
 // sweep): dD/scale += P ddS', r1 += P dPa, r2 += P dP, r3/scale += P ddS' dP.
-template <bool MASK>
-__device__ __forceinline__ void q_stats32(const uint32_t (&vs)[32], const uint32_t (&vdds)[32],
-                                          const uint32_t (&vdp)[32], const uint32_t (&vdpa)[32], int kc, int row,
+template <int CW, bool MASK>
+__device__ __forceinline__ void q_stats(const uint32_t (&vs)[CW], const uint32_t (&vdds)[CW],
+                                        const uint32_t (&vdp)[CW], const uint32_t (&vdpa)[CW], int kc, int row,
                                           int tk, int causal, float sc, float sc2, float lg, float& dD, float& r1,
                                           float& r2, float& r3) {
 #pragma unroll
-  for (int i = 0; i < 32; ++i) {
+  for (int i = 0; i < CW; ++i) {
     float s = fmaf(__uint_as_float(vs[i]), sc2, -lg);
     if (MASK && (kc + i >= tk || (causal && kc + i > row))) s = -INFINITY;
     const float p = ex2(s);
@@ -163,18 +178,18 @@ __device__ __forceinline__ void q_stats32(const uint32_t (&vs)[32], const uint32
 }
 
 // Second sweep: packed bf16 pairs of dS/scale, dS2/scale, ddP and P for this
-// thread's 32 columns (the softmax scale of dS and dS2 is applied to dQ' in
+// thread's CW columns (the softmax scale of dS and dS2 is applied to dQ' in
 // the epilogue instead of per element). With u = ddS - dD and c = dD D + B,
 //   ddP = P u,  dS/scale = P (dP - D),
 //   dS2/scale = P (dPa + dP u - ddS D - B) = P (dPa - c) + ddP (dP - D).
-template <bool MASK>
-__device__ __forceinline__ void q_ops32(const uint32_t (&vs)[32], const uint32_t (&vdds)[32],
-                                        const uint32_t (&vdp)[32], const uint32_t (&vdpa)[32], int kc, int row, int tk,
-                                        int causal, float sc, float sc2, float lg, float dv, float dD, float cq,
-                                        uint32_t (&o_ds)[16], uint32_t (&o_ds2)[16], uint32_t (&o_ddp)[16],
-                                        uint32_t (&o_p)[16]) {
+template <int CW, bool MASK>
+__device__ __forceinline__ void q_ops(const uint32_t (&vs)[CW], const uint32_t (&vdds)[CW],
+                                      const uint32_t (&vdp)[CW], const uint32_t (&vdpa)[CW], int kc, int row, int tk,
+                                      int causal, float sc, float sc2, float lg, float dv, float dD, float cq,
+                                      uint32_t (&o_ds)[CW / 2], uint32_t (&o_ds2)[CW / 2], uint32_t (&o_ddp)[CW / 2],
+                                      uint32_t (&o_p)[CW / 2]) {
 #pragma unroll
-  for (int i = 0; i < 32; i += 2) {
+  for (int i = 0; i < CW; i += 2) {
     float pp[2], ddp[2], ds[2], ds2[2];
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
@@ -360,7 +375,8 @@ __global__ void __launch_bounds__(kBBThreads, 1)
     // --------------------------- elementwise warps ----------------------------
     const int wg = (warp - kBBFirstEwWarp) >> 2;  // column half of every tile
     const int r = (warp & 3) * 32 + lane;         // TMEM lane = query row inside the tile
-    const int cb = wg * 32;
+    constexpr int CW = G::CW;
+    const int cb = wg * CW;
     const int row = q0 + r;
     const bool row_ok = row < sh.Tq;
     const size_t vi = stat_index(b, h, row_ok ? row : 0, sh.H, sh.Tq);
@@ -373,7 +389,7 @@ __global__ void __launch_bounds__(kBBThreads, 1)
       dv = row_ok ? a.delta[vi] : 0.f;
     } else {
       // D = rowsum(dO o) of this row from the resident tiles, while the first
-      // scores are computed: each warpgroup sums its 32 columns.
+      // scores are computed: each warpgroup sums half of the head_dim columns.
       ok = mbar_wait_warp(&bar_res, 0, &abort_flag);
       dv = ok ? rowdot_share<HD>(s_o, s_do, r, wg) : 0.f;
       dred[wg][r] = dv;
@@ -391,23 +407,23 @@ __global__ void __launch_bounds__(kBBThreads, 1)
       if (!ok) break;
       tc_fence_after();
       const uint32_t tb = tmem + sb * G::SCORE_COLS;
-      uint32_t vs[32], vdds[32], vdp[32], vdpa[32];
-      tmem_share32(tb, warp, G::C_S + cb, vs);
-      tmem_share32(tb, warp, G::C_DDS + cb, vdds);
-      tmem_share32(tb, warp, G::C_DP + cb, vdp);
-      tmem_share32(tb, warp, G::C_DPA + cb, vdpa);
+      uint32_t vs[CW], vdds[CW], vdp[CW], vdpa[CW];
+      tmem_share<CW>(tb, warp, G::C_S + cb, vs);
+      tmem_share<CW>(tb, warp, G::C_DDS + cb, vdds);
+      tmem_share<CW>(tb, warp, G::C_DP + cb, vdp);
+      tmem_share<CW>(tb, warp, G::C_DPA + cb, vdpa);
       tmem_wait_ld();
-      reg_fence32(vs);
-      reg_fence32(vdds);
-      reg_fence32(vdp);
-      reg_fence32(vdpa);
+      reg_fence(vs);
+      reg_fence(vdds);
+      reg_fence(vdp);
+      reg_fence(vdpa);
       warp_arrive(&bar_sc_empty[sb]);  // the tensor core may reuse this score buffer now
-      const bool need_mask = (kc + 32 > sh.Tk) || (sh.causal && kc + 31 > row);
+      const bool need_mask = (kc + CW > sh.Tk) || (sh.causal && kc + CW - 1 > row);
       if (!sweep2) {
         if (need_mask)
-          q_stats32<true>(vs, vdds, vdp, vdpa, kc, row, sh.Tk, sh.causal, sc, sc2, lg, dD, r1, r2, r3);
+          q_stats<CW, true>(vs, vdds, vdp, vdpa, kc, row, sh.Tk, sh.causal, sc, sc2, lg, dD, r1, r2, r3);
         else
-          q_stats32<false>(vs, vdds, vdp, vdpa, kc, row, sh.Tk, sh.causal, sc, sc2, lg, dD, r1, r2, r3);
+          q_stats<CW, false>(vs, vdds, vdp, vdpa, kc, row, sh.Tk, sh.causal, sc, sc2, lg, dD, r1, r2, r3);
         if (it == n - 1) {
           // Combine the two warpgroups' column halves (same order on both sides).
           red[0][wg][r] = dD;
@@ -425,22 +441,22 @@ __global__ void __launch_bounds__(kBBThreads, 1)
           cq = r1 - dD * r2 + r3;  // dD D + B
         }
       } else {
-        uint32_t o_ds[16], o_ds2[16], o_ddp[16], o_p[16];
+        uint32_t o_ds[CW / 2], o_ds2[CW / 2], o_ddp[CW / 2], o_p[CW / 2];
         if (need_mask)
-          q_ops32<true>(vs, vdds, vdp, vdpa, kc, row, sh.Tk, sh.causal, sc, sc2, lg, dv, dD, cq, o_ds, o_ds2, o_ddp,
-                        o_p);
+          q_ops<CW, true>(vs, vdds, vdp, vdpa, kc, row, sh.Tk, sh.causal, sc, sc2, lg, dv, dD, cq, o_ds, o_ds2,
+                          o_ddp, o_p);
         else
-          q_ops32<false>(vs, vdds, vdp, vdpa, kc, row, sh.Tk, sh.causal, sc, sc2, lg, dv, dD, cq, o_ds, o_ds2,
-                         o_ddp, o_p);
+          q_ops<CW, false>(vs, vdds, vdp, vdpa, kc, row, sh.Tk, sh.causal, sc, sc2, lg, dv, dD, cq, o_ds, o_ds2,
+                           o_ddp, o_p);
         if (j > 0) ok = mbar_wait_warp(&bar_ops_empty, (j - 1) & 1, &abort_flag);
         if (!ok) break;
         tc_fence_after();
-        // This warpgroup's 32 keys are packed columns [16 wg, 16 wg + 16) of each operand.
-        const uint32_t to = tmem + tmem_lane_base(warp & 3) + G::C_OPS + 16 * wg;
-        tmem_st16(to, o_ds);
-        tmem_st16(to + G::OPS_COLS, o_ds2);
-        tmem_st16(to + 2 * G::OPS_COLS, o_ddp);
-        tmem_st16(to + 3 * G::OPS_COLS, o_p);
+        // This warpgroup's CW keys are packed columns [CW/2 wg, CW/2 wg + CW/2) of each operand.
+        const uint32_t to = tmem + tmem_lane_base(warp & 3) + G::C_OPS + (CW / 2) * wg;
+        tmem_st_ops(to, o_ds);
+        tmem_st_ops(to + G::OPS_COLS, o_ds2);
+        tmem_st_ops(to + 2 * G::OPS_COLS, o_ddp);
+        tmem_st_ops(to + 3 * G::OPS_COLS, o_p);
         tmem_wait_st();
         warp_arrive(&bar_ops_full);
       }
@@ -474,15 +490,18 @@ __global__ void __launch_bounds__(kBBThreads, 1)
 
 template <int HD>
 struct KPass {
-  static constexpr int BN = 64;                    // query rows per streamed tile
-  static constexpr int ST = 4;
+  // Query rows per streamed tile and ring depth: 64 x 4 at head_dim 64; 32 x 3 at
+  // 128 (four 32 KB resident key-side tiles leave room for three 28 KB slots).
+  static constexpr int BN = HD == 64 ? 64 : 32;
+  static constexpr int ST = HD == 64 ? 4 : 3;
+  static constexpr int CW = BN / 2;
   static constexpr int RES = kBM * HD * 2;
   static constexpr int RES_PANEL = kBM * 128;
   static constexpr int STR = BN * HD * 2;
   static constexpr int PAIR = 2 * STR;
   static constexpr int PAIR_PANEL = 2 * BN * 128;
   // Per-query biases of the four score products as a K = 16 bf16 operand
-  // (32-byte rows, 32B swizzle): rows [64 m, 64 m + 64) hold product m's bias
+  // (32-byte rows, 32B swizzle): rows [BN m, BN m + BN) hold product m's bias
   // for each streamed query as a (hi, lo) bf16 pair in columns 0-1, zeros after.
   static constexpr int BIAS_ROW = 32;
   static constexpr int BIAS = 4 * BN * BIAS_ROW;
@@ -498,21 +517,21 @@ struct KPass {
   static_assert(C_OPS + 3 * OPS_COLS <= TMEM_COLS, "TMEM budget");
   static_assert(C_DDS == C_S + BN && C_DP == C_S + 2 * BN && C_DPA == C_S + 3 * BN, "one bias MMA covers 4 products");
   static_assert(SMEM <= 232448, "shared memory budget");
-  static_assert(BN == 64, "two warpgroups x 32 columns");
+  static_assert(CW % 16 == 0 && BN % 32 == 0, "tile shapes");
 };
 
-// Packed bf16 pairs of dS^T/scale, dS2^T/scale and ddP^T for this thread's 32
+// Packed bf16 pairs of dS^T/scale, dS2^T/scale and ddP^T for this thread's CW
 // query columns (the scale of dS, dS2 is applied to dK' in the epilogue), by
 // the same identities as the query pass. The per-query statistics arrive
 // already folded into the score products by the bias MMA:
 //   vs = S - L/scale,  vdds = ddS/scale - dD/scale,  vdp = dP - D,  vdpa = dPa - c.
-template <bool MASK>
-__device__ __forceinline__ void k_ops32(const uint32_t (&vs)[32], const uint32_t (&vdds)[32],
-                                        const uint32_t (&vdp)[32], const uint32_t (&vdpa)[32], int qc, int key,
-                                        int tq, int causal, float sc, float sc2, uint32_t (&o_ds)[16],
-                                        uint32_t (&o_ds2)[16], uint32_t (&o_ddp)[16]) {
+template <int CW, bool MASK>
+__device__ __forceinline__ void k_ops(const uint32_t (&vs)[CW], const uint32_t (&vdds)[CW],
+                                      const uint32_t (&vdp)[CW], const uint32_t (&vdpa)[CW], int qc, int key, int tq,
+                                      int causal, float sc, float sc2, uint32_t (&o_ds)[CW / 2],
+                                      uint32_t (&o_ds2)[CW / 2], uint32_t (&o_ddp)[CW / 2]) {
 #pragma unroll
-  for (int i = 0; i < 32; i += 2) {
+  for (int i = 0; i < CW; i += 2) {
     float ddp[2], ds[2], ds2[2];
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
@@ -620,11 +639,12 @@ __global__ void __launch_bounds__(kBBThreads, 1)
     for (int it = 0; it < n; ++it) {
       const int s = it % ST;
       const int q0 = (qt_begin + it) * BN;
-      // Per-query statistics of this tile (two rows per lane), fetched before
+      // Per-query statistics of this tile (BN/32 rows per lane), fetched before
       // waiting for the slot so their latency overlaps the wait.
-      float st[2][4];
+      constexpr int RPL = BN / 32;
+      float st[RPL][4];
 #pragma unroll
-      for (int k = 0; k < 2; ++k) {
+      for (int k = 0; k < RPL; ++k) {
         const int q = q0 + lane + 32 * k;
         const bool v = q < sh.Tq;
         const size_t idx = stat_index(b, h, v ? q : 0, sh.H, sh.Tq);
@@ -641,7 +661,7 @@ __global__ void __launch_bounds__(kBBThreads, 1)
       uint8_t* slot = s_ring + s * G::SLOT;
       const uint32_t bias = smem_u32(slot + G::PAIR + G::STR);
 #pragma unroll
-      for (int k = 0; k < 2; ++k)
+      for (int k = 0; k < RPL; ++k)
 #pragma unroll
         for (int m = 0; m < 4; ++m) store_bias_row(bias, m * BN + lane + 32 * k, st[k][m]);
       fence_async_smem();  // the tensor core reads the biases through the async proxy
@@ -730,7 +750,8 @@ __global__ void __launch_bounds__(kBBThreads, 1)
     // --------------------------- elementwise warps ----------------------------
     const int wg = (warp - kBBFirstEwWarp) >> 2;
     const int r = (warp & 3) * 32 + lane;  // TMEM lane = key row inside the tile
-    const int cb = wg * 32;
+    constexpr int CW = G::CW;
+    const int cb = wg * CW;
     const int key = k0 + r;
     const bool key_ok = key < sh.Tk;
     const float sc = sh.scale, sc2 = sh.scale * kLog2e;
@@ -741,30 +762,30 @@ __global__ void __launch_bounds__(kBBThreads, 1)
       ok = mbar_wait_warp(&bar_sc_full, it & 1, &abort_flag);
       if (!ok) break;
       tc_fence_after();
-      uint32_t vs[32], vdds[32], vdp[32], vdpa[32];
-      tmem_share32(tmem, warp, G::C_S + cb, vs);
-      tmem_share32(tmem, warp, G::C_DDS + cb, vdds);
-      tmem_share32(tmem, warp, G::C_DP + cb, vdp);
-      tmem_share32(tmem, warp, G::C_DPA + cb, vdpa);
+      uint32_t vs[CW], vdds[CW], vdp[CW], vdpa[CW];
+      tmem_share<CW>(tmem, warp, G::C_S + cb, vs);
+      tmem_share<CW>(tmem, warp, G::C_DDS + cb, vdds);
+      tmem_share<CW>(tmem, warp, G::C_DP + cb, vdp);
+      tmem_share<CW>(tmem, warp, G::C_DPA + cb, vdpa);
       tmem_wait_ld();
-      reg_fence32(vs);
-      reg_fence32(vdds);
-      reg_fence32(vdp);
-      reg_fence32(vdpa);
+      reg_fence(vs);
+      reg_fence(vdds);
+      reg_fence(vdp);
+      reg_fence(vdpa);
       warp_arrive(&bar_sc_empty);
-      const bool need_mask = (qc + 32 > sh.Tq) || (sh.causal && qc < key);
-      uint32_t o_ds[16], o_ds2[16], o_ddp[16];
+      const bool need_mask = (qc + CW > sh.Tq) || (sh.causal && qc < key);
+      uint32_t o_ds[CW / 2], o_ds2[CW / 2], o_ddp[CW / 2];
       if (need_mask)
-        k_ops32<true>(vs, vdds, vdp, vdpa, qc, key, sh.Tq, sh.causal, sc, sc2, o_ds, o_ds2, o_ddp);
+        k_ops<CW, true>(vs, vdds, vdp, vdpa, qc, key, sh.Tq, sh.causal, sc, sc2, o_ds, o_ds2, o_ddp);
       else
-        k_ops32<false>(vs, vdds, vdp, vdpa, qc, key, sh.Tq, sh.causal, sc, sc2, o_ds, o_ds2, o_ddp);
+        k_ops<CW, false>(vs, vdds, vdp, vdpa, qc, key, sh.Tq, sh.causal, sc, sc2, o_ds, o_ds2, o_ddp);
       if (it > 0) ok = mbar_wait_warp(&bar_ops_empty, (it - 1) & 1, &abort_flag);
       if (!ok) break;
       tc_fence_after();
-      const uint32_t to = tmem + tmem_lane_base(warp & 3) + G::C_OPS + 16 * wg;
-      tmem_st16(to, o_ds);
-      tmem_st16(to + G::OPS_COLS, o_ds2);
-      tmem_st16(to + 2 * G::OPS_COLS, o_ddp);
+      const uint32_t to = tmem + tmem_lane_base(warp & 3) + G::C_OPS + (CW / 2) * wg;
+      tmem_st_ops(to, o_ds);
+      tmem_st_ops(to + G::OPS_COLS, o_ds2);
+      tmem_st_ops(to + 2 * G::OPS_COLS, o_ddp);
       tmem_wait_st();
       warp_arrive(&bar_ops_full);
     }
@@ -845,6 +866,7 @@ int launch_bwdbwd_hd(const AttnShape& s, const BwdBwdPtrs& p, int passes, int* s
 
 int launch_bwdbwd(const AttnShape& s, int hd, const BwdBwdPtrs& p, int passes, int* status, cudaStream_t stream) {
   if (hd == 64) return launch_bwdbwd_hd<64>(s, p, passes, status, stream);
+  if (hd == 128) return launch_bwdbwd_hd<128>(s, p, passes, status, stream);
   return kUnsupported;
 }
 

@@ -231,7 +231,6 @@ static int bwdbwd_entry(const char* entry, void* stream, const fh_attn_dims* dim
   int rc = validate(dims, &s, scale, causal);
   if (rc != kOk) return rc;
   if (passes < 1 || passes > 3) return fail(FH_ERR_INVALID_ARGUMENT, "pass must be 1, 2 or 3");
-  if (dims->head_dim != 64) return fail(FH_ERR_UNSUPPORTED, "the double backward supports head_dim 64");
   if (!all_aligned(q, k, v, dO, ddq, ddk, ddv) || !lse || !dd || !bvec)
     return fail(FH_ERR_INVALID_ARGUMENT, kAlignMsg);
   if (o ? (!all_aligned(o) || !delta_out) : !delta) return fail(FH_ERR_INVALID_ARGUMENT, kAlignMsg);
@@ -349,7 +348,6 @@ extern "C" int fh_attn_bwdbwd_noalloc(void* stream, const fh_attn_dims* dims, co
   int rc = validate(dims, &s, scale, causal);
   if (rc != kOk) return rc;
   const long long rows = static_cast<long long>(s.B) * s.H * s.Tq;
-  if (dims->head_dim != 64) return fail(FH_ERR_UNSUPPORTED, "the double backward supports head_dim 64");
   if (rows > kNoAllocMaxRows) {
     char msg[240];
     std::snprintf(msg, sizeof(msg),

@@ -219,6 +219,12 @@ __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.
 
 // 32 lanes x 16 consecutive 32-bit columns from registers (the store twin of
 // tmem_ld16). Visible to tcgen05.mma only after tmem_wait_st().
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
+               "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+               : "memory");
+}
+
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
@@ -358,6 +364,19 @@ __device__ __forceinline__ void umma_bf16_ts_x4_w(uint32_t d_tmem, uint32_t a_tm
       "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [t2], %4, %6, 1;\n\t"
       "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [t3], %5, %6, 1;\n\t}" ::"r"(d_tmem),
       "r"(a_tmem), "l"(b0), "l"(b1), "l"(b2), "l"(b3), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_bf16_ts_x2_w(uint32_t d_tmem, uint32_t a_tmem, uint64_t b0, uint64_t b1,
+                                                  uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\t.reg .b32 t1;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "setp.ne.b32 p, %5, 0;\n\t"
+      "add.u32 t1, %1, 8;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %4, p;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [t1], %3, %4, 1;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b0), "l"(b1), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 

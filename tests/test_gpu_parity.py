@@ -94,6 +94,28 @@ HD128_CASES = [
 
 
 @pytest.mark.parametrize("b,h,tq,tk,causal", HD128_CASES)
+def test_bwdbwd_matches_oracle_hd128(b, h, tq, tk, causal):
+    from flash_hog_b200 import MaskType, flash_bwdbwd
+    from flash_hog_b200._capi import device_status
+
+    x = case_inputs(b, h, tq, tk, d=128, seed=13 * tq + tk, causal=causal)
+    (rq2, rk2, rv2, rdo), (rd, rdd, rb) = oracle_bwdbwd(x, causal)
+    g = _cuda(x)
+    mask = MaskType.CAUSAL if causal else MaskType.NO_MASK
+    (dq2, dk2, dv2, ddo), (d, dd, bv) = flash_bwdbwd(g["q"], g["k"], g["v"], g["o"], g["do"], g["ddq"], g["ddk"],
+                                                     g["ddv"], g["lse"], mask_type=mask, return_stats=True)
+    torch.cuda.synchronize()
+    assert device_status() == 0
+    assert_close("D", np64(d), rd)
+    assert_close("dD", np64(dd), rdd)
+    assert_close("B", np64(bv), rb)
+    assert_close("dQ2", np64(dq2), rq2)
+    assert_close("dK2", np64(dk2), rk2)
+    assert_close("dV2", np64(dv2), rv2)
+    assert_close("ddO", np64(ddo), rdo)
+
+
+@pytest.mark.parametrize("b,h,tq,tk,causal", HD128_CASES)
 def test_fwd_bwd_match_oracle_hd128(b, h, tq, tk, causal):
     from flash_hog_b200 import MaskType
     from flash_hog_b200 import _attention_impl as impl
