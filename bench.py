@@ -7,7 +7,12 @@ query-tiled pass (D = rowsum(dO o O), dQ', ddO, dD, B) and the key-tiled pass
 ``dot_product_attention_bwd_rule_bwd_rule``. Credited FLOPs are
 22 GEMM-equivalents x 2 x D per kept (query, key) pair (378.1 GFLOP per step).
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload cfg2|cfg3|cfg4]
+
+``--workload`` (default cfg2, the headline) also measures BASELINE.json's other
+GPU configs with the same kernels: cfg3 = causal B2 H32 S8192 D128 (plus peak
+device memory against the sequence length), cfg4 = non-causal B8 H16 Sq4096
+Sk2048 D128. Those lines are reported measurements, not the headline.
 
 Under torchrun every rank runs the workload on its own GPU (batch x heads of a
 global batch 4N; no collective on the data path) and rank 0 prints one JSON line
@@ -36,21 +41,45 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "bwd-of-bwd TFLOP/s/GPU, causal bf16 B4 H16 S2048 D64, at 1/2/4/8 B200"
-B, H, S, D = 4, 16, 2048, 64
-CAUSAL = True
+# name: (batch, heads, seq_q, seq_k, head_dim, causal)
+WORKLOADS = {
+    "cfg2": (4, 16, 2048, 2048, 64, True),
+    "cfg3": (2, 32, 8192, 8192, 128, True),
+    "cfg4": (8, 16, 4096, 2048, 128, False),
+}
+B, H, SQ, SK, D, CAUSAL = WORKLOADS["cfg2"]
+S = SQ
 SCALE = D ** -0.5
+
+
+def set_workload(name):
+    global B, H, SQ, SK, S, D, CAUSAL, SCALE, METRIC
+    B, H, SQ, SK, D, CAUSAL = WORKLOADS[name]
+    S, SCALE = SQ, D ** -0.5
+    if name != "cfg2":
+        METRIC = f"bwd-of-bwd TFLOP/s/GPU, {describe()}"
+
+
+def describe():
+    seq = f"S{SQ}" if SQ == SK else f"Sq{SQ} Sk{SK}"
+    return f"{'causal' if CAUSAL else 'non-causal'} bf16 B{B} H{H} {seq} D{D}"
 N_SETS = 3  # rotating input sets, each larger than the 126 MB L2
 PEAKS_FILE = os.path.join(ROOT, "MEASURED_PEAKS.json")
 QPASS_DRAM_BYTES = 214.9e6  # ncu dram read + write of one query-pass launch (profiles/)
 FALLBACK_PEAKS = {"bf16_tflops": 1590.0, "hbm_gbs": 6650.0}
 
 
-def pairs(b, h, s, causal):
-    return b * h * (s * (s + 1) // 2 if causal else s * s)
+def pairs(b, h, sq, sk, causal):
+    """Kept (query, key) pairs; the causal mask is top-left (key <= query)."""
+    if not causal:
+        return b * h * sq * sk
+    if sq <= sk:
+        return b * h * sq * (sq + 1) // 2
+    return b * h * (sk * (sk + 1) // 2 + (sq - sk) * sk)
 
 
-def credited_flops(b, h, s, gemms=22):
-    return gemms * 2 * D * pairs(b, h, s, CAUSAL)
+def credited_flops(b, h, gemms=22):
+    return gemms * 2 * D * pairs(b, h, SQ, SK, CAUSAL)
 
 
 def load_peaks():
@@ -145,7 +174,7 @@ def cpu_baseline_sample(steps=1, heads=1, threads=None):
         ora.autograd_all(*args, scale=SCALE, causal=CAUSAL)
         times.append(time.perf_counter() - t0)
     t = statistics.median(times)
-    value = credited_flops(1, heads, S) / t / 1e12
+    value = credited_flops(1, heads) / t / 1e12
     return {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "port",
             "sample": f"{heads} of {B * H} heads of the workload per step (B1 H{heads} S{S} D{D} causal fp32, "
                       f"torch double autograd of naive attention), median of {steps}"}, t
@@ -184,11 +213,36 @@ def make_set(seed, device):
     from flash_hog_b200 import _attention_impl as impl
     from oracle.attention_oracle import make_inputs
 
-    x = make_inputs(B, H, S, S, D, seed=seed)
+    x = make_inputs(B, H, SQ, SK, D, seed=seed)
     g = {k: v.to(device) for k, v in x.items()}
-    o, lse = impl.cuda_dot_product_attention(g["q"], g["k"], g["v"], MaskType.CAUSAL, SCALE, return_residual=True)
+    mask = MaskType.CAUSAL if CAUSAL else MaskType.NO_MASK
+    o, lse = impl.cuda_dot_product_attention(g["q"], g["k"], g["v"], mask, SCALE, return_residual=True)
     g["o"], g["lse"] = o, lse
     return g
+
+
+def memory_vs_seq(dev, seqs=(1024, 2048, 4096, 8192)):
+    """Device memory of one double backward (inputs + outputs + scratch) against the
+    sequence length, at the workload's batch, heads and head_dim: linear in S since
+    no (Sq, Sk) array is ever allocated."""
+    from flash_hog_b200 import MaskType, flash_bwdbwd
+
+    rows = []
+    for s in seqs:
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+        base = torch.cuda.memory_allocated(dev)
+        torch.cuda.reset_peak_memory_stats(dev)
+        g = torch.Generator(device="cpu").manual_seed(s)
+        shape = (B, s, H, D)
+        x = [torch.randn(shape, generator=g).to(dev, torch.bfloat16) for _ in range(8)]
+        lse = torch.randn((B, H, s), generator=g).to(dev) + 8.0
+        flash_bwdbwd(*x, lse, mask_type=MaskType.CAUSAL if CAUSAL else MaskType.NO_MASK, scale=SCALE)
+        torch.cuda.synchronize()
+        rows.append({"seq_len": s, "peak_bytes": torch.cuda.max_memory_allocated(dev) - base,
+                     "input_bytes": sum(t.numel() * t.element_size() for t in x) + lse.numel() * 4})
+        del x, lse
+    return rows
 
 
 def main():
@@ -199,7 +253,11 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--skip-e2e", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg2")
     args = ap.parse_args()
+    set_workload(args.workload)
+    if args.workload != "cfg2":
+        args.skip_cpu = True  # the CPU baseline samples the headline workload only
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
     if args.impl == "reference":
@@ -222,7 +280,7 @@ def main():
 
     # Rank r holds batch rows [4r, 4r+4) of the global batch: distinct seeds.
     sets = [make_set(1000 * rank + i, dev) for i in range(N_SETS)]
-    stats = torch.empty((N_SETS, 3, B, H, S), dtype=torch.float32, device=dev)
+    stats = torch.empty((N_SETS, 3, B, H, SQ), dtype=torch.float32, device=dev)
     outs = [(torch.empty_like(s["q"]), torch.empty_like(s["q"]), torch.empty_like(s["k"]), torch.empty_like(s["k"]))
             for s in sets]
 
@@ -262,6 +320,7 @@ def main():
         barrier()
     if _capi.device_status() != 0:
         raise RuntimeError("device-side error during the timed region")
+    peak_bytes = torch.cuda.max_memory_allocated(dev)
     ms = start.elapsed_time(stop) / args.steps
     t_q = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
     t_k = statistics.mean(e[1].elapsed_time(e[2]) for e in evs)
@@ -276,14 +335,14 @@ def main():
         host = {k: v.cpu().pin_memory() for k, v in sets[0].items()}
         names = ("q", "k", "v", "o", "do", "ddq", "ddk", "ddv", "lse")
         h2d = sum(host[n].numel() * host[n].element_size() for n in names)
-        res_host = [torch.empty(host["q"].shape, dtype=torch.bfloat16).pin_memory() for _ in range(2)] + \
-                   [torch.empty(host["k"].shape, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+        # flash_bwdbwd returns (dQ2, dK2, dV2, ddO)
+        res_host = [torch.empty(host[n].shape, dtype=torch.bfloat16).pin_memory() for n in ("q", "k", "k", "q")]
         d2h = sum(t.numel() * t.element_size() for t in res_host)
 
         def e2e_step():
             d = {n: host[n].to(dev, non_blocking=True) for n in names}
             r = flash_bwdbwd(d["q"], d["k"], d["v"], d["o"], d["do"], d["ddq"], d["ddk"], d["ddv"], d["lse"],
-                             mask_type=MaskType.CAUSAL, scale=SCALE)
+                             mask_type=MaskType.CAUSAL if CAUSAL else MaskType.NO_MASK, scale=SCALE)
             for dst, src in zip(res_host, r):
                 dst.copy_(src, non_blocking=True)
 
@@ -305,40 +364,45 @@ def main():
             t = torch.tensor([e2e_ms], device=dev)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             e2e_ms = float(t.item())
-        e2e = {"value": world * credited_flops(B, H, S) / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+        e2e = {"value": world * credited_flops(B, H) / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
                "api": "flash_hog_b200.flash_bwdbwd"}
 
+    mem_rows = memory_vs_seq(dev) if args.workload == "cfg3" and rank == 0 else None
     if dist is not None:
         dist.destroy_process_group()
     if rank != 0:
         return 0
 
     peaks, peak_kind = load_peaks()
-    flops_q = credited_flops(B, H, S, gemms=14)
+    flops_q = credited_flops(B, H, gemms=14)
     achieved = flops_q / (t_q * 1e-3) / 1e12
     roofline = {"bound": "tensor", "kernel": "bwdbwd_q_kernel (query-tiled pass, 14 of 22 GEMM-eq)",
                 "achieved": achieved, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                 "frac": achieved / peaks["bf16_tflops"], "peak_source": f"{peak_kind} bf16 dense (burst)",
                 # dram__bytes_read.sum + dram__bytes_write.sum of one query-pass launch of this
                 # workload, from the ncu capture summarised in profiles/bwdbwd_b4h16s2048d64_causal.md
-                "traffic": QPASS_DRAM_BYTES, "traffic_unit": "bytes per launch (ncu)",
+                "traffic": QPASS_DRAM_BYTES if args.workload == "cfg2" else None,
+                "traffic_unit": "bytes per launch (ncu)",
                 "per_launch_ms": {"query_pass": t_q, "key_pass": t_k},
-                "key_pass": {"achieved": credited_flops(B, H, S, gemms=8) / (t_k * 1e-3) / 1e12}}
+                "key_pass": {"achieved": credited_flops(B, H, gemms=8) / (t_k * 1e-3) / 1e12}}
     cpu = None
     if not args.skip_cpu:
         cpu, _ = cpu_baseline_sample(steps=1, heads=4)
-    value = world * credited_flops(B, H, S) / (ms * 1e-3) / 1e12
+    value = world * credited_flops(B, H) / (ms * 1e-3) / 1e12
     line = {
         "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": f"bwdbwd causal B{B} H{H} S{S} D{D} per GPU", "global_batch": B * world,
-                   "heads": H, "seq_len": S, "head_dim": D, "causal": True,
+        "config": {"workload": f"bwdbwd {describe()} per GPU", "name": args.workload,
+                   "global_batch": B * world, "heads": H, "seq_len": SQ, "seq_len_k": SK, "head_dim": D,
+                   "causal": CAUSAL,
                    "parallelism": f"dp{world} (batch x heads sharded, no collective)",
                    "l2": f"{N_SETS} rotating input sets of ~136 MB each (> 126 MB L2)",
-                   "credited_gflop_per_step_per_gpu": credited_flops(B, H, S) / 1e9},
+                   "credited_gflop_per_step_per_gpu": credited_flops(B, H) / 1e9,
+                   "peak_device_bytes": peak_bytes},
         "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks.summary(),
+        **({"memory_vs_seq": mem_rows} if mem_rows else {}),
         "gpu_launches": 2 * args.steps,
     }
     print(json.dumps(line), flush=True)
