@@ -387,7 +387,7 @@ def main():
                 "per_launch_ms": {"query_pass": t_q, "key_pass": t_k},
                 "key_pass": {"achieved": credited_flops(B, H, gemms=8) / (t_k * 1e-3) / 1e12}}
     cpu = None
-    if not args.skip_cpu:
+    if not args.skip_cpu and world == 1:  # the CPU baseline is reported at N=1 only
         cpu, _ = cpu_baseline_sample(steps=1, heads=4)
     value = world * credited_flops(B, H) / (ms * 1e-3) / 1e12
     line = {
