@@ -50,8 +50,8 @@ def _check_inputs(query, key, value):
         raise ValueError("flash_hog_b200 runs on CUDA tensors only")
     if key.shape != value.shape or query.shape[0] != key.shape[0] or query.shape[3] != key.shape[3]:
         raise ValueError(f"incompatible shapes q{tuple(query.shape)} k{tuple(key.shape)} v{tuple(value.shape)}")
-    if query.shape[2] != key.shape[2]:
-        raise NotImplementedError("grouped-query attention (q_heads != kv_heads) is not supported yet")
+    if query.shape[2] % key.shape[2] != 0:
+        raise ValueError(f"q_heads ({query.shape[2]}) must be a multiple of kv_heads ({key.shape[2]})")
 
 
 def cuda_dot_product_attention(query, key, value, mask_type: MaskType, scale: float, return_residual=False):

@@ -44,7 +44,7 @@ EXPORTED_SYMBOLS = (
     "fh_last_error",
     "fh_abi_version",
 )
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 
 class FlashHogError(RuntimeError):
@@ -69,6 +69,7 @@ class FhAttnDims(ctypes.Structure):
         ("head_dim", ctypes.c_int32),
         ("q", FhStrides),
         ("k", FhStrides),
+        ("kv_heads", ctypes.c_int32),
     ]
 
 
@@ -136,10 +137,10 @@ def _layout_key(t: torch.Tensor):
 
 
 def make_dims(q: torch.Tensor, k: torch.Tensor) -> FhAttnDims:
-    """Dims for BTNH tensors: q (B, Tq, H, D), k (B, Tk, H, D)."""
+    """Dims for BTNH tensors: q (B, Tq, H, D), k (B, Tk, Hkv, D) with H a multiple of Hkv."""
     b, tq, h, d = q.shape
-    tk = k.shape[1]
-    return FhAttnDims(b, h, tq, tk, d, _strides(q), _strides(k))
+    tk, hkv = k.shape[1], k.shape[2]
+    return FhAttnDims(b, h, tq, tk, d, _strides(q), _strides(k), hkv)
 
 
 def _same_layout(ref: torch.Tensor, *others: torch.Tensor) -> None:

@@ -54,8 +54,8 @@ def flash_bwdbwd(Q, K, V, O, dO, ddQ, ddK, ddV, L, mask_type: MaskType = MaskTyp
         return outs
     if scale is None:
         scale = Q.shape[-1] ** -0.5
-    if Q.shape[2] != K.shape[2]:
-        raise NotImplementedError("grouped-query attention (q_heads != kv_heads) is not supported yet")
+    if Q.shape[2] % K.shape[2] != 0:
+        raise ValueError(f"q_heads ({Q.shape[2]}) must be a multiple of kv_heads ({K.shape[2]})")
     causal = _is_causal(mask_type)
     q, k, v, o, do, ddq, ddk, ddv = (_bf16(x) for x in (Q, K, V, O, dO, ddQ, ddK, ddV))
     b, t, n, _ = q.shape

@@ -38,7 +38,8 @@ struct Strides3 {
 };
 
 struct AttnShape {
-  int B, H, Tq, Tk;
+  int B, H, Tq, Tk;  // H: query heads
+  int Hk, G;         // key/value heads and the group size H / Hk (query head h uses key head h / G)
   Strides3 sq;   // query-side tensors
   Strides3 sk;   // key-side tensors
   float scale;

@@ -104,8 +104,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         uint8_t* slot = s_ring + s * G::SLOT;
         mbar_arrive_expect_tx(&bar_full[s], G::SLOT);
-        tma_rows<HD>(slot, &tm_k, &bar_full[s], it * BN, BN, h, b);
-        tma_rows<HD>(slot + G::STR, &tm_v, &bar_full[s], it * BN, BN, h, b);
+        tma_rows<HD>(slot, &tm_k, &bar_full[s], it * BN, BN, h / sh.G, b);
+        tma_rows<HD>(slot + G::STR, &tm_v, &bar_full[s], it * BN, BN, h / sh.G, b);
         issued = it + 1;
       }
       bool drained = mbar_wait(&bar_res, 0, nullptr);
@@ -238,12 +238,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const AttnShape& sh = a.sh;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int h = blockIdx.x, b = blockIdx.y;
+  const int hk = blockIdx.x, b = blockIdx.y;  // key/value head
   const int kt = blockIdx.z;
   const int k0 = kt * kBM;
   const int nq_tiles = (sh.Tq + BN - 1) / BN;
   const int qt_begin = sh.causal ? k0 / BN : 0;
-  const int n = nq_tiles > qt_begin ? nq_tiles - qt_begin : 0;
+  const int n = nq_tiles > qt_begin ? nq_tiles - qt_begin : 0;  // query tiles per query head
+  // Streamed tile `it` is query tile qt_begin + it % n of query head hk*G + it / n:
+  // the G query heads sharing this key head accumulate into the same dK, dV.
+  const int total = n * sh.G;
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
@@ -269,13 +272,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_q);
       mbar_arrive_expect_tx(&bar_res, 2 * G::RES);
-      tma_rows<HD>(s_k, &tm_k, &bar_res, k0, kBM, h, b);
-      tma_rows<HD>(s_v, &tm_v, &bar_res, k0, kBM, h, b);
+      tma_rows<HD>(s_k, &tm_k, &bar_res, k0, kBM, hk, b);
+      tma_rows<HD>(s_v, &tm_v, &bar_res, k0, kBM, hk, b);
     }
     int issued = 0;
-    for (int it = 0; it < n; ++it) {
+    for (int it = 0; it < total; ++it) {
       const int s = it % ST;
-      const int q0 = (qt_begin + it) * BN;
+      const int q0 = (qt_begin + it % n) * BN;
+      const int h = hk * sh.G + it / n;
       float st[2][2];
 #pragma unroll
       for (int k = 0; k < 2; ++k) {
@@ -319,8 +323,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t id_out = idesc_bf16_f32(kBM, HD, false, true);
       bool ok = mbar_wait(&bar_res, 0, &abort_flag);
       if (!ok) raise_error(a.status, &abort_flag, kDevTimeoutTmaFull);
-      for (int it = 0; ok && it <= n; ++it) {
-        if (it < n) {
+      for (int it = 0; ok && it <= total; ++it) {
+        if (it < total) {
           const int s = it % ST;
           if (!mbar_wait(&bar_full[s], (it / ST) & 1, &abort_flag) ||
               (it > 0 && !mbar_wait(&bar_sc_empty, (it - 1) & 1, &abort_flag))) {
@@ -358,9 +362,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool key_ok = key < sh.Tk;
     const float sc = sh.scale, sc2 = sh.scale * kLog2e;
     bool ok = true;
-    for (int it = 0; it < n; ++it) {
+    for (int it = 0; it < total; ++it) {
       const int s = it % ST;
-      const int q0 = (qt_begin + it) * BN;
+      const int q0 = (qt_begin + it % n) * BN;
       ok = __all_sync(0xffffffffu, mbar_wait(&bar_sc_full, it & 1, &abort_flag));
       if (ok && it > 0) ok = __all_sync(0xffffffffu, mbar_wait(&bar_ops_empty, (it - 1) & 1, &abort_flag));
       if (!ok) break;
@@ -395,8 +399,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_arrive(&bar_ops_full);
     }
     const int skey = key_ok ? key : 0;
-    __nv_bfloat16* dk_row = a.dk + row_offset(sh.sk, b, skey, h);
-    __nv_bfloat16* dv_row = a.dv + row_offset(sh.sk, b, skey, h);
+    __nv_bfloat16* dk_row = a.dk + row_offset(sh.sk, b, skey, hk);
+    __nv_bfloat16* dv_row = a.dv + row_offset(sh.sk, b, skey, hk);
     if (n == 0) {
       if (key_ok) {
         zero_row_global<HD>(dk_row);
@@ -426,10 +430,10 @@ int launch_bwd_hd(const AttnShape& s, const BwdPtrs& p, int* status, cudaStream_
   CUtensorMap mq[4], mk[4];
   bool ok = make_seq_map(&mq[0], p.q, HD, s.Tq, s.H, s.B, s.sq, kBM) &&
             make_seq_map(&mq[1], p.dO, HD, s.Tq, s.H, s.B, s.sq, kBM) &&
-            make_seq_map(&mq[2], p.k, HD, s.Tk, s.H, s.B, s.sk, GQ::BN) &&
-            make_seq_map(&mq[3], p.v, HD, s.Tk, s.H, s.B, s.sk, GQ::BN) &&
-            make_seq_map(&mk[0], p.k, HD, s.Tk, s.H, s.B, s.sk, kBM) &&
-            make_seq_map(&mk[1], p.v, HD, s.Tk, s.H, s.B, s.sk, kBM) &&
+            make_seq_map(&mq[2], p.k, HD, s.Tk, s.Hk, s.B, s.sk, GQ::BN) &&
+            make_seq_map(&mq[3], p.v, HD, s.Tk, s.Hk, s.B, s.sk, GQ::BN) &&
+            make_seq_map(&mk[0], p.k, HD, s.Tk, s.Hk, s.B, s.sk, kBM) &&
+            make_seq_map(&mk[1], p.v, HD, s.Tk, s.Hk, s.B, s.sk, kBM) &&
             make_seq_map(&mk[2], p.q, HD, s.Tq, s.H, s.B, s.sq, GK::BN) &&
             make_seq_map(&mk[3], p.dO, HD, s.Tq, s.H, s.B, s.sq, GK::BN);
   if (!ok) return kInvalidArgument;
@@ -443,7 +447,7 @@ int launch_bwd_hd(const AttnShape& s, const BwdPtrs& p, int* status, cudaStream_
   bwd_dq_kernel<HD><<<dim3(s.H, s.B, (s.Tq + kBM - 1) / kBM), kThreads, GQ::SMEM, stream>>>(mq[0], mq[1], mq[2],
                                                                                           mq[3], args);
   if (cudaGetLastError() != cudaSuccess) return kLaunchFailed;
-  bwd_dkdv_kernel<HD><<<dim3(s.H, s.B, (s.Tk + kBM - 1) / kBM), kThreads, GK::SMEM, stream>>>(mk[0], mk[1], mk[2],
+  bwd_dkdv_kernel<HD><<<dim3(s.Hk, s.B, (s.Tk + kBM - 1) / kBM), kThreads, GK::SMEM, stream>>>(mk[0], mk[1], mk[2],
                                                                                             mk[3], args);
   return cudaGetLastError() == cudaSuccess ? kOk : kLaunchFailed;
 }

@@ -299,8 +299,8 @@ __global__ void __launch_bounds__(kBBThreads, 1)
         const int k0 = (it % n) * BN;
         uint8_t* slot = s_ring + s * G::SLOT;
         mbar_arrive_expect_tx(&bar_full[s], G::SLOT);
-        tma_pair<HD>(slot, &tm_k, &tm_ddk, &bar_full[s], k0, BN, h, b);
-        tma_pair<HD>(slot + G::PAIR, &tm_v, &tm_ddv, &bar_full[s], k0, BN, h, b);
+        tma_pair<HD>(slot, &tm_k, &tm_ddk, &bar_full[s], k0, BN, h / sh.G, b);
+        tma_pair<HD>(slot + G::PAIR, &tm_v, &tm_ddv, &bar_full[s], k0, BN, h / sh.G, b);
         issued = it + 1;
       }
       // Every issued copy must land before this CTA's shared memory is released.
@@ -589,12 +589,15 @@ __global__ void __launch_bounds__(kBBThreads, 1)
 
   const AttnShape& sh = a.sh;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int h = blockIdx.x, b = blockIdx.y;
+  const int hk = blockIdx.x, b = blockIdx.y;  // key/value head
   const int kt = blockIdx.z;  // key tile 0 carries the most causal work
   const int k0 = kt * kBM;
   const int nq_tiles = (sh.Tq + BN - 1) / BN;
   const int qt_begin = sh.causal ? k0 / BN : 0;
-  const int n = nq_tiles > qt_begin ? nq_tiles - qt_begin : 0;
+  const int n = nq_tiles > qt_begin ? nq_tiles - qt_begin : 0;  // query tiles per query head
+  // Streamed tile `it` is query tile qt_begin + it % n of query head hk*G + it / n:
+  // the G query heads sharing this key head accumulate into the same dK', dV'.
+  const int total = n * sh.G;
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
@@ -629,16 +632,17 @@ __global__ void __launch_bounds__(kBBThreads, 1)
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_q);
       mbar_arrive_expect_tx(&bar_res, 4 * G::RES);
-      tma_rows<HD>(s_k, &tm_k, &bar_res, k0, kBM, h, b);
-      tma_rows<HD>(s_v, &tm_v, &bar_res, k0, kBM, h, b);
-      tma_rows<HD>(s_ddk, &tm_ddk, &bar_res, k0, kBM, h, b);
-      tma_rows<HD>(s_ddv, &tm_ddv, &bar_res, k0, kBM, h, b);
+      tma_rows<HD>(s_k, &tm_k, &bar_res, k0, kBM, hk, b);
+      tma_rows<HD>(s_v, &tm_v, &bar_res, k0, kBM, hk, b);
+      tma_rows<HD>(s_ddk, &tm_ddk, &bar_res, k0, kBM, hk, b);
+      tma_rows<HD>(s_ddv, &tm_ddv, &bar_res, k0, kBM, hk, b);
     }
     int issued = 0;
     const float inv_scale = 1.f / sh.scale;
-    for (int it = 0; it < n; ++it) {
+    for (int it = 0; it < total; ++it) {
       const int s = it % ST;
-      const int q0 = (qt_begin + it) * BN;
+      const int q0 = (qt_begin + it % n) * BN;
+      const int h = hk * sh.G + it / n;  // query head of this tile
       // Per-query statistics of this tile (BN/32 rows per lane), fetched before
       // waiting for the slot so their latency overlaps the wait.
       constexpr int RPL = BN / 32;
@@ -696,7 +700,7 @@ __global__ void __launch_bounds__(kBBThreads, 1)
       constexpr uint64_t kSlot = G::SLOT >> 4;
       bool ok = mbar_wait_warp(&bar_res, 0, &abort_flag);
       if (!ok && lane == 0) raise_error(a.status, &abort_flag, kDevTimeoutTmaFull);
-      for (int it = 0; ok && it < n; ++it) {
+      for (int it = 0; ok && it < total; ++it) {
         const int s = it % ST;
         if (!mbar_wait_warp(&bar_full[s], (it / ST) & 1, &abort_flag)) {
           if (lane == 0) raise_error(a.status, &abort_flag, kDevTimeoutTmaFull);
@@ -728,7 +732,7 @@ __global__ void __launch_bounds__(kBBThreads, 1)
       constexpr uint64_t kSlot = G::SLOT >> 4, kHalf = (BN * 128) >> 4;
       const uint32_t t_ops = tmem + G::C_OPS;
       bool ok = true;
-      for (int it = 0; it < n; ++it) {
+      for (int it = 0; it < total; ++it) {
         if (!mbar_wait_warp(&bar_ops_full, it & 1, &abort_flag)) {
           if (lane == 0) raise_error(a.status, &abort_flag, kDevTimeoutEpilogue);
           ok = false;
@@ -756,9 +760,8 @@ __global__ void __launch_bounds__(kBBThreads, 1)
     const bool key_ok = key < sh.Tk;
     const float sc = sh.scale, sc2 = sh.scale * kLog2e;
     bool ok = true;
-    for (int it = 0; it < n; ++it) {
-      const int s = it % ST;
-      const int qc = (qt_begin + it) * BN + cb;  // first query of this thread's columns
+    for (int it = 0; it < total; ++it) {
+      const int qc = (qt_begin + it % n) * BN + cb;  // first query of this thread's columns
       ok = mbar_wait_warp(&bar_sc_full, it & 1, &abort_flag);
       if (!ok) break;
       tc_fence_after();
@@ -790,7 +793,7 @@ __global__ void __launch_bounds__(kBBThreads, 1)
       warp_arrive(&bar_ops_full);
     }
     const int skey = key_ok ? key : 0;
-    __nv_bfloat16* dst = (wg == 0 ? a.dk2 : a.dv2) + row_offset(sh.sk, b, skey, h);
+    __nv_bfloat16* dst = (wg == 0 ? a.dk2 : a.dv2) + row_offset(sh.sk, b, skey, hk);
     if (n == 0) {
       // No query sees these keys (causal with Tk > Tq): the gradients are zero.
       if (key_ok) zero_row_global<HD>(dst);
@@ -819,16 +822,16 @@ int launch_bwdbwd_hd(const AttnShape& s, const BwdBwdPtrs& p, int passes, int* s
   bool ok = make_seq_map(&mq[0], p.q, HD, s.Tq, s.H, s.B, s.sq, kBM) &&
             make_seq_map(&mq[1], p.dO, HD, s.Tq, s.H, s.B, s.sq, kBM) &&
             make_seq_map(&mq[2], p.ddq, HD, s.Tq, s.H, s.B, s.sq, kBM) &&
-            make_seq_map(&mq[3], p.k, HD, s.Tk, s.H, s.B, s.sk, GQ::BN) &&
-            make_seq_map(&mq[4], p.v, HD, s.Tk, s.H, s.B, s.sk, GQ::BN) &&
-            make_seq_map(&mq[5], p.ddk, HD, s.Tk, s.H, s.B, s.sk, GQ::BN) &&
-            make_seq_map(&mq[6], p.ddv, HD, s.Tk, s.H, s.B, s.sk, GQ::BN) &&
+            make_seq_map(&mq[3], p.k, HD, s.Tk, s.Hk, s.B, s.sk, GQ::BN) &&
+            make_seq_map(&mq[4], p.v, HD, s.Tk, s.Hk, s.B, s.sk, GQ::BN) &&
+            make_seq_map(&mq[5], p.ddk, HD, s.Tk, s.Hk, s.B, s.sk, GQ::BN) &&
+            make_seq_map(&mq[6], p.ddv, HD, s.Tk, s.Hk, s.B, s.sk, GQ::BN) &&
             make_seq_map(&mq[7], p.o ? p.o : p.q, HD, s.Tq, s.H, s.B, s.sq, kBM);  // O: only read when D is fused
   // Key-tiled pass: 128-row key tiles, 64-row query tiles.
-  ok = ok && make_seq_map(&mk[0], p.k, HD, s.Tk, s.H, s.B, s.sk, kBM) &&
-       make_seq_map(&mk[1], p.v, HD, s.Tk, s.H, s.B, s.sk, kBM) &&
-       make_seq_map(&mk[2], p.ddk, HD, s.Tk, s.H, s.B, s.sk, kBM) &&
-       make_seq_map(&mk[3], p.ddv, HD, s.Tk, s.H, s.B, s.sk, kBM) &&
+  ok = ok && make_seq_map(&mk[0], p.k, HD, s.Tk, s.Hk, s.B, s.sk, kBM) &&
+       make_seq_map(&mk[1], p.v, HD, s.Tk, s.Hk, s.B, s.sk, kBM) &&
+       make_seq_map(&mk[2], p.ddk, HD, s.Tk, s.Hk, s.B, s.sk, kBM) &&
+       make_seq_map(&mk[3], p.ddv, HD, s.Tk, s.Hk, s.B, s.sk, kBM) &&
        make_seq_map(&mk[4], p.q, HD, s.Tq, s.H, s.B, s.sq, GK::BN) &&
        make_seq_map(&mk[5], p.dO, HD, s.Tq, s.H, s.B, s.sq, GK::BN) &&
        make_seq_map(&mk[6], p.ddq, HD, s.Tq, s.H, s.B, s.sq, GK::BN);
@@ -855,7 +858,7 @@ int launch_bwdbwd_hd(const AttnShape& s, const BwdBwdPtrs& p, int passes, int* s
     if (cudaGetLastError() != cudaSuccess) return kLaunchFailed;
   }
   if (passes & kPassKey) {
-    const dim3 gk(s.H, s.B, (s.Tk + kBM - 1) / kBM);
+    const dim3 gk(s.Hk, s.B, (s.Tk + kBM - 1) / kBM);
     bwdbwd_k_kernel<HD><<<gk, kBBThreads, GK::SMEM, stream>>>(mk[0], mk[1], mk[2], mk[3], mk[4], mk[5], mk[6], args);
     if (cudaGetLastError() != cudaSuccess) return kLaunchFailed;
   }

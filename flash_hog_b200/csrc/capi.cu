@@ -105,8 +105,12 @@ int validate(const fh_attn_dims* d, AttnShape* out, float scale, int causal) {
   if (!strides_ok(d->q) || !strides_ok(d->k))
     return fail(kInvalidArgument, "strides must be non-negative multiples of 8 elements (seq stride > 0)");
   if (!(scale == scale)) return fail(kInvalidArgument, "scale is NaN");
+  const int kv = d->kv_heads ? d->kv_heads : d->heads;
+  if (kv < 1 || d->heads % kv != 0) return fail(kInvalidArgument, "heads must be a multiple of kv_heads");
   out->B = d->batch;
   out->H = d->heads;
+  out->Hk = kv;
+  out->G = d->heads / kv;
   out->Tq = d->seq_q;
   out->Tk = d->seq_k;
   out->sq = Strides3{d->q.batch, d->q.seq, d->q.head};

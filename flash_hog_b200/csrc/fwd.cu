@@ -102,8 +102,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         uint8_t* slot = s_ring + s * G::SLOT;
         mbar_arrive_expect_tx(&bar_full[s], G::SLOT);
-        tma_rows<HD>(slot, &tm_k, &bar_full[s], it * BN, BN, h, b);
-        tma_rows<HD>(slot + G::STR, &tm_v, &bar_full[s], it * BN, BN, h, b);
+        tma_rows<HD>(slot, &tm_k, &bar_full[s], it * BN, BN, h / sh.G, b);
+        tma_rows<HD>(slot + G::STR, &tm_v, &bar_full[s], it * BN, BN, h / sh.G, b);
         issued = it + 1;
       }
       bool drained = mbar_wait(&bar_res, 0, nullptr);
@@ -271,8 +271,8 @@ int launch_fwd_hd(const AttnShape& s, const FwdPtrs& p, int* status, cudaStream_
   using G = FPass<HD>;
   CUtensorMap mq, mk, mv;
   if (!make_seq_map(&mq, p.q, HD, s.Tq, s.H, s.B, s.sq, kBM) ||
-      !make_seq_map(&mk, p.k, HD, s.Tk, s.H, s.B, s.sk, G::BN) ||
-      !make_seq_map(&mv, p.v, HD, s.Tk, s.H, s.B, s.sk, G::BN))
+      !make_seq_map(&mk, p.k, HD, s.Tk, s.Hk, s.B, s.sk, G::BN) ||
+      !make_seq_map(&mv, p.v, HD, s.Tk, s.Hk, s.B, s.sk, G::BN))
     return kInvalidArgument;
   if (ensure_smem_limit(reinterpret_cast<const void*>(&fwd_kernel<HD>), G::SMEM) != kOk) return kLaunchFailed;
   FwdArgs args{s, static_cast<__nv_bfloat16*>(p.o), p.lse, status};

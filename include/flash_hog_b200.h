@@ -24,8 +24,9 @@
  *    log-sum-exp of the scaled, masked scores.
  *  - causal != 0 applies the top-left mask (query i sees keys j <= i), the mask
  *    of flash_hog/jax/_pallas_gpu_kernel.py:37-41.
- *  - head_dim must be 64 in this version; seq_q, seq_k >= 1 (no divisibility
- *    requirement: ragged edges are masked).
+ *  - head_dim is 64 or 128; seq_q, seq_k >= 1 (no divisibility requirement:
+ *    ragged edges are masked); heads a multiple of kv_heads (grouped-query
+ *    attention; key-side tensors and dk, dv, dk2, dv2 have kv_heads heads).
  *  - Calls are asynchronous on `stream` (a cudaStream_t, may be NULL for the
  *    legacy default stream) and never allocate device memory except a 4-byte
  *    status word per device on first use. Scratch buffers are the caller's, as
@@ -71,6 +72,10 @@ typedef struct fh_attn_dims {
   int32_t head_dim;
   fh_strides q; /* Q, O, dO, ddQ and the query-side outputs dQ, dQ', ddO */
   fh_strides k; /* K, V, ddK, ddV and the key-side outputs dK, dV, dK', dV' */
+  /* Key/value heads for grouped-query attention: 0 (= heads) or a divisor of
+   * heads; query head n attends with key/value head n / (heads / kv_heads), the
+   * reference's "(kv_heads group)" grouping (flash_hog/jax/_pallas_gpu_kernel.py:106-107). */
+  int32_t kv_heads;
 } fh_attn_dims;
 
 /* Forward: o = softmax(scale * q k^T + mask) v, lse = logsumexp(scale * q k^T + mask).
@@ -180,7 +185,7 @@ const char* fh_status_string(int status);
 /* ABI version of this header (bumped on any signature change). */
 int fh_abi_version(void);
 
-#define FH_ABI_VERSION 1
+#define FH_ABI_VERSION 2
 
 #ifdef __cplusplus
 }

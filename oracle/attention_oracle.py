@@ -63,6 +63,27 @@ def _btnh(x: np.ndarray) -> np.ndarray:
     return np.ascontiguousarray(np.transpose(x, (0, 2, 1, 3)))
 
 
+def _expand(xh: np.ndarray, group: int) -> np.ndarray:
+    """Key-side heads (B, Hkv, T, D) repeated for grouped-query attention: query
+    head n uses key head n // group, the reference's "(kv_heads group)" split
+    (``flash_hog/jax/_pallas_gpu_kernel.py:106-107``)."""
+    return xh if group == 1 else np.repeat(xh, group, axis=1)
+
+
+def _group_sum(xh: np.ndarray, group: int) -> np.ndarray:
+    """Sums a key-side gradient computed per query head back onto its key head."""
+    if group == 1:
+        return xh
+    b, h, t, d = xh.shape
+    return xh.reshape(b, h // group, group, t, d).sum(axis=2)
+
+
+def _group(q, k) -> int:
+    if q.shape[2] % k.shape[2]:
+        raise ValueError("q_heads must be a multiple of kv_heads")
+    return q.shape[2] // k.shape[2]
+
+
 def _scores(q, k, scale, causal):
     s = np.einsum("bhqd,bhkd->bhqk", q, k) * scale
     if causal:
@@ -83,7 +104,8 @@ def attention_fwd(q, k, v, scale=None, causal=False):
     Returns (O BTNH, L (B,N,T)).
     """
     scale = default_scale(q.shape[-1]) if scale is None else scale
-    qh, kh, vh = _heads(q), _heads(k), _heads(v)
+    g = _group(q, k)
+    qh, kh, vh = _heads(q), _expand(_heads(k), g), _expand(_heads(v), g)
     s = _scores(qh, kh, scale, causal)
     m = s.max(axis=-1, keepdims=True)
     e = np.exp(s - m)
@@ -102,15 +124,17 @@ def attention_bwd(q, k, v, o, lse, do, scale=None, causal=False):
     cuDNN backward uses (``flash_hog/jax/_attention_impl.py:242-261``).
     """
     scale = default_scale(q.shape[-1]) if scale is None else scale
-    qh, kh, vh, oh, doh = map(_heads, (q, k, v, o, do))
+    g = _group(q, k)
+    qh, oh, doh = map(_heads, (q, o, do))
+    kh, vh = (_expand(_heads(x), g) for x in (k, v))
     s = _scores(qh, kh, scale, causal)
     p = np.exp(s - np.asarray(lse, np.float64)[..., None])
     dp = np.einsum("bhqd,bhkd->bhqk", doh, vh)
     d = np.einsum("bhqd,bhqd->bhq", doh, oh)[..., None]
     ds = scale * p * (dp - d)
     dq = np.einsum("bhqk,bhkd->bhqd", ds, kh)
-    dk = np.einsum("bhqk,bhqd->bhkd", ds, qh)
-    dv = np.einsum("bhqk,bhqd->bhkd", p, doh)
+    dk = _group_sum(np.einsum("bhqk,bhqd->bhkd", ds, qh), g)
+    dv = _group_sum(np.einsum("bhqk,bhqd->bhkd", p, doh), g)
     return _btnh(dq), _btnh(dk), _btnh(dv)
 
 
@@ -180,10 +204,14 @@ def bwdbwd_stats(q, k, v, o, lse, do, ddq, ddk, ddv, scale=None, causal=False, r
         dQ' = dS ddK + dS2 K             dK' = dS^T ddQ + dS2^T Q
         dV' = ddP^T dO                   ddO = P ddV + ddP V
 
-    With ``return_stats`` also returns (D, dD, B), each (B, N, T).
+    With ``return_stats`` also returns (D, dD, B), each (B, N, T). Grouped-query
+    inputs (fewer key heads) use key head n // group for query head n, and
+    dK', dV' are summed over each group.
     """
     scale = default_scale(q.shape[-1]) if scale is None else scale
-    qh, kh, vh, oh, doh, ddqh, ddkh, ddvh = map(_heads, (q, k, v, o, do, ddq, ddk, ddv))
+    g = _group(q, k)
+    qh, oh, doh, ddqh = map(_heads, (q, o, do, ddq))
+    kh, vh, ddkh, ddvh = (_expand(_heads(x), g) for x in (k, v, ddk, ddv))
     s = _scores(qh, kh, scale, causal)
     p = np.exp(s - np.asarray(lse, np.float64)[..., None])
     dp = np.einsum("bhqd,bhkd->bhqk", doh, vh)
@@ -196,8 +224,8 @@ def bwdbwd_stats(q, k, v, o, lse, do, ddq, ddk, ddv, scale=None, causal=False, r
     ds2 = scale * p * (dp2 - bb)
     ds = scale * p * (dp - d)
     dq2 = np.einsum("bhqk,bhkd->bhqd", ds, ddkh) + np.einsum("bhqk,bhkd->bhqd", ds2, kh)
-    dk2 = np.einsum("bhqk,bhqd->bhkd", ds, ddqh) + np.einsum("bhqk,bhqd->bhkd", ds2, qh)
-    dv2 = np.einsum("bhqk,bhqd->bhkd", ddp, doh)
+    dk2 = _group_sum(np.einsum("bhqk,bhqd->bhkd", ds, ddqh) + np.einsum("bhqk,bhqd->bhkd", ds2, qh), g)
+    dv2 = _group_sum(np.einsum("bhqk,bhqd->bhkd", ddp, doh), g)
     ddo = np.einsum("bhqk,bhkd->bhqd", p, ddvh) + np.einsum("bhqk,bhkd->bhqd", ddp, vh)
     out = (_btnh(dq2), _btnh(dk2), _btnh(dv2), _btnh(ddo))
     if return_stats:
@@ -295,6 +323,9 @@ def bwdbwd_4pass(q, k, v, o, lse, do, ddq, ddk, ddv, scale=None, causal=False,
 # --------------------------------------------------------------------------------------
 
 def _torch_attention(q, k, v, scale, causal):
+    group = q.shape[2] // k.shape[2]
+    if group > 1:  # query head n uses key head n // group; autograd sums the group
+        k, v = k.repeat_interleave(group, dim=2), v.repeat_interleave(group, dim=2)
     s = torch.einsum("bqhd,bkhd->bhqk", q, k) * scale
     if causal:
         keep = torch.ones(q.shape[1], k.shape[1], dtype=torch.bool).tril()
@@ -328,17 +359,18 @@ def autograd_all(q, k, v, do, ddq, ddk, ddv, scale=None, causal=False):
 # seeded inputs and credited work
 # --------------------------------------------------------------------------------------
 
-def make_inputs(batch, heads, seq_q, seq_k, head_dim, seed=0, dtype=None):
+def make_inputs(batch, heads, seq_q, seq_k, head_dim, seed=0, dtype=None, kv_heads=None):
     """Seeded N(0,1) Q, K, V, dO, ddQ, ddK, ddV (BTNH) as torch tensors.
 
     Draw order and shapes follow the reference tests
     (``tests/test_jax_fhog.py:125-132``: q, k, v, do, ddq, ddk, ddv); the
-    generator is torch's, seeded with ``seed``. ``dtype`` defaults to bf16.
+    generator is torch's, seeded with ``seed``. ``dtype`` defaults to bf16;
+    ``kv_heads`` (default ``heads``) sets the key-side head count.
     """
     dtype = torch.bfloat16 if dtype is None else dtype
     g = torch.Generator().manual_seed(seed)
     qs = (batch, seq_q, heads, head_dim)
-    ks = (batch, seq_k, heads, head_dim)
+    ks = (batch, seq_k, heads if kv_heads is None else kv_heads, head_dim)
     shapes = dict(q=qs, k=ks, v=ks, do=qs, ddq=qs, ddk=ks, ddv=ks)
     return {n: torch.randn(s, generator=g, dtype=torch.float32).to(dtype) for n, s in shapes.items()}
 

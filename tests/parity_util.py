@@ -15,9 +15,9 @@ def np64(t: torch.Tensor) -> np.ndarray:
     return t.detach().float().cpu().numpy().astype(np.float64)
 
 
-def case_inputs(b, h, tq, tk, d=64, seed=0, causal=False):
+def case_inputs(b, h, tq, tk, d=64, seed=0, causal=False, kv_heads=None):
     """Seeded bf16 inputs plus the oracle forward (O rounded to bf16, L fp32)."""
-    x = ora.make_inputs(b, h, tq, tk, d, seed=seed)
+    x = ora.make_inputs(b, h, tq, tk, d, seed=seed, kv_heads=kv_heads)
     o, lse = ora.attention_fwd(np64(x["q"]), np64(x["k"]), np64(x["v"]), causal=causal)
     x["o"] = torch.from_numpy(o).to(torch.bfloat16)
     x["lse"] = torch.from_numpy(lse).float()

@@ -83,6 +83,53 @@ def test_fwd_bwd_match_oracle(b, h, tq, tk, causal):
     assert_close("dV", np64(dv), rv)
 
 
+GQA_CASES = [
+    # b, q_heads, kv_heads, tq, tk, causal, head_dim -- grouped-query attention
+    (1, 4, 2, 128, 128, True, 64),
+    (2, 4, 1, 256, 384, False, 64),
+    (1, 8, 2, 200, 200, True, 64),
+    (1, 4, 2, 256, 256, True, 128),
+    (1, 6, 3, 72, 136, False, 128),
+]
+
+
+@pytest.mark.parametrize("b,h,hk,tq,tk,causal,d", GQA_CASES)
+def test_gqa_matches_oracle(b, h, hk, tq, tk, causal, d):
+    """q_heads a multiple of kv_heads: forward, backward and double backward."""
+    from flash_hog_b200 import MaskType, flash_bwdbwd
+    from flash_hog_b200 import _attention_impl as impl
+    from flash_hog_b200._capi import device_status
+
+    x = case_inputs(b, h, tq, tk, d=d, seed=17 * tq + tk + h, causal=causal, kv_heads=hk)
+    g = _cuda(x)
+    mask = MaskType.CAUSAL if causal else MaskType.NO_MASK
+    scale = d ** -0.5
+    out, lse = impl.cuda_dot_product_attention(g["q"], g["k"], g["v"], mask, scale, return_residual=True)
+    dq, dk, dv = impl.dot_product_attention_bwd_rule(mask, scale, (g["q"], g["k"], g["v"], g["lse"], g["o"]),
+                                                     g["do"])
+    (dq2, dk2, dv2, ddo), (dd_, dd, bv) = flash_bwdbwd(g["q"], g["k"], g["v"], g["o"], g["do"], g["ddq"],
+                                                       g["ddk"], g["ddv"], g["lse"], mask_type=mask,
+                                                       return_stats=True)
+    torch.cuda.synchronize()
+    assert device_status() == 0
+    assert dk.shape == x["k"].shape and dk2.shape == x["k"].shape and dv2.shape == x["v"].shape
+    ro, rl = ora.attention_fwd(np64(x["q"]), np64(x["k"]), np64(x["v"]), causal=causal)
+    assert_close("O", np64(out), ro)
+    assert ora.max_abs(np64(lse), rl) <= 2e-3
+    rq, rk, rv = ora.attention_bwd(np64(x["q"]), np64(x["k"]), np64(x["v"]), np64(x["o"]), np64(x["lse"]),
+                                   np64(x["do"]), causal=causal)
+    assert_close("dQ", np64(dq), rq)
+    assert_close("dK", np64(dk), rk)
+    assert_close("dV", np64(dv), rv)
+    (rq2, rk2, rv2, rdo), (rd, rdd, rb) = oracle_bwdbwd(x, causal)
+    assert_close("dD", np64(dd), rdd)
+    assert_close("B", np64(bv), rb)
+    assert_close("dQ2", np64(dq2), rq2)
+    assert_close("dK2", np64(dk2), rk2)
+    assert_close("dV2", np64(dv2), rv2)
+    assert_close("ddO", np64(ddo), rdo)
+
+
 HD128_CASES = [
     # b, h, tq, tk, causal -- head_dim 128 (the long-sequence and cross-attention configs)
     (1, 2, 128, 128, True),
@@ -142,12 +189,13 @@ def test_fwd_bwd_match_oracle_hd128(b, h, tq, tk, causal):
     assert_close("dV", np64(dv), rv)
 
 
-@pytest.mark.parametrize("causal", [True, False])
-def test_nested_autograd_matches_double_autograd(causal):
-    """grad-of-grad through the public API vs torch double autograd of naive attention."""
+@pytest.mark.parametrize("causal,kv_heads,d", [(True, 2, 64), (False, 2, 64), (True, 1, 64), (True, 2, 128)])
+def test_nested_autograd_matches_double_autograd(causal, kv_heads, d):
+    """grad-of-grad through the public API vs torch double autograd of naive
+    attention (kv_heads < 2: grouped-query attention)."""
     import flash_hog_b200 as fhb
 
-    x = ora.make_inputs(2, 2, 256, 256, 64, seed=5)
+    x = ora.make_inputs(2, 2, 256, 256, d, seed=5, kv_heads=kv_heads)
     ref = ora.autograd_all(*(x[n].double() for n in ("q", "k", "v", "do", "ddq", "ddk", "ddv")), causal=causal)
     q, k, v, do = (x[n].cuda().requires_grad_(True) for n in ("q", "k", "v", "do"))
     out = fhb.dot_product_attention(q, k, v, is_causal=causal)

@@ -83,3 +83,22 @@ def test_credited_flops_headline():
     # B4 H16 S2048 D64 causal: 22 GEMM-equivalents x 2 x D per kept pair.
     assert ora.causal_pairs(4, 16, 2048, 2048, True) == 134_283_264
     assert abs(ora.bwdbwd_flops(4, 16, 2048, 2048, 64, True) / 1e9 - 378.1) < 0.1
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_oracle_grouped_query_heads(causal):
+    """Grouped-query attention (4 query heads on 2 key heads): the explicit
+    formulas, with key head n // group for query head n and key-side gradients
+    summed over each group, agree with torch double autograd of naive attention
+    whose key/value heads are repeated the same way."""
+    x = ora.make_inputs(2, 4, 48, 48 if causal else 64, 16, seed=3, dtype=torch.float64, kv_heads=2)
+    a = ora.autograd_all(*(x[n] for n in ("q", "k", "v", "do", "ddq", "ddk", "ddv")), causal=causal)
+    q, k, v, do, ddq, ddk, ddv = (x[n].numpy() for n in ("q", "k", "v", "do", "ddq", "ddk", "ddv"))
+    o, lse = ora.attention_fwd(q, k, v, causal=causal)
+    assert np.abs(o - a["o"].numpy()).max() < 1e-12
+    for got, name in zip(ora.attention_bwd(q, k, v, o, lse, do, causal=causal), ("dq", "dk", "dv")):
+        assert np.abs(got - a[name].numpy()).max() < 1e-12, name
+    for got, name in zip(ora.bwdbwd_stats(q, k, v, o, lse, do, ddq, ddk, ddv, causal=causal),
+                         ("dq2", "dk2", "dv2", "ddo")):
+        assert got.shape == a[name].shape
+        assert np.abs(got - a[name].numpy()).max() < 1e-12, name
