@@ -9,10 +9,12 @@ query-tiled pass (D = rowsum(dO o O), dQ', ddO, dD, B) and the key-tiled pass
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload cfg2|cfg3|cfg4]
 
-``--workload`` (default cfg2, the headline) also measures BASELINE.json's other
-GPU configs with the same kernels: cfg3 = causal B2 H32 S8192 D128 (plus peak
+``--workload`` (default cfg2, the headline) also measures the other GPU
+configurations with the same kernels: cfg3 = causal B2 H32 S8192 D128 (plus peak
 device memory against the sequence length), cfg4 = non-causal B8 H16 Sq4096
-Sk2048 D128. Those lines are reported measurements, not the headline.
+Sk2048 D128, gpt = the grad-norm-penalty training step of a 12-layer GPT (tokens/s,
+NCCL gradient all-reduce under torchrun). Those lines are reported measurements, not
+the headline.
 
 Under torchrun every rank runs the workload on its own GPU (batch x heads of a
 global batch 4N; no collective on the data path) and rank 0 prints one JSON line
@@ -245,6 +247,93 @@ def memory_vs_seq(dev, seqs=(1024, 2048, 4096, 8192)):
     return rows
 
 
+def run_gpt(args):
+    """The grad-norm-penalty GPT training step (12 layers, d768, 12 heads of 64, MLP
+    3072, vocab 32000, sequence 1024, 4 sequences per GPU; tokens uniform in
+    [0, 32000)), data-parallel over the ranks with an NCCL gradient all-reduce.
+    Metric: tokens per second of the whole job."""
+    import datetime
+    from flash_hog_b200 import _capi
+    from flash_hog_b200.gpt import GPT, GPTConfig, train_step
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    cfg, batch, lam = GPTConfig(), 4, 1e-2
+    torch.manual_seed(0)  # the same initial weights on every rank
+    model = GPT(cfg).to(dev)
+    opt = torch.optim.SGD(model.parameters(), lr=1e-4)
+    g = torch.Generator().manual_seed(1000 + rank)
+    host = [torch.randint(0, cfg.vocab, (batch, cfg.seq_len + 1), generator=g).pin_memory() for _ in range(2)]
+    resident = [t.to(dev) for t in host]
+
+    def barrier():
+        if dist is not None:
+            dist.barrier(device_ids=[local])
+
+    def timed(step_fn, steps):
+        barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n0 = _capi.launch_count()
+        e0.record()
+        for i in range(steps):
+            step_fn(i)
+        e1.record()
+        torch.cuda.synchronize()
+        barrier()
+        ms = e0.elapsed_time(e1) / steps
+        if dist is not None:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms, _capi.launch_count() - n0
+
+    def device_step(i):
+        train_step(model, resident[i % 2], lam, optimizer=opt, distributed=dist is not None)
+
+    loss_host = torch.empty((), dtype=torch.float32).pin_memory()
+
+    def e2e_step(i):
+        tokens = host[i % 2].to(dev, non_blocking=True)
+        loss, _ = train_step(model, tokens, lam, optimizer=opt, distributed=dist is not None)
+        loss_host.copy_(loss, non_blocking=True)
+
+    for i in range(args.warmup):
+        device_step(i)
+    with ClockSampler(list(range(world)) if rank == 0 else []) as clocks:
+        ms, launches = timed(device_step, args.steps)
+    e2e_ms, _ = timed(e2e_step, max(3, min(args.steps, 10)))
+    if _capi.device_status() != 0:
+        raise RuntimeError("device-side error in the GPT step")
+    if dist is not None:
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    tokens_step = world * batch * cfg.seq_len
+    print(json.dumps({
+        "metric": "grad-norm-penalty GPT training step, tokens/s (12L d768 h12 D64 causal, seq 1024, 4 seq/GPU)",
+        "value": tokens_step / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (tokens uniform in [0, 32000), random init)",
+        "config": {"workload": "gpt grad-norm penalty L + 0.01 ||dL/dtheta||^2, SGD update", "name": "gpt",
+                   "layers": cfg.n_layer, "d_model": cfg.d_model, "heads": cfg.n_head, "seq_len": cfg.seq_len,
+                   "global_batch": world * batch, "parallelism": f"dp{world} (NCCL all-reduce of gradients)",
+                   "peak_device_bytes": torch.cuda.max_memory_allocated(dev)},
+        "roofline": None, "cpu_baseline": None,
+        "e2e": {"value": tokens_step / (e2e_ms * 1e-3), "unit": "tokens/s",
+                "h2d_bytes_per_step": host[0].numel() * host[0].element_size(), "d2h_bytes_per_step": 4},
+        "clocks": clocks.summary(), "gpu_launches": launches,
+    }), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -253,8 +342,12 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--skip-e2e", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg2")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["gpt"], default="cfg2")
     args = ap.parse_args()
+    if args.workload == "gpt":
+        if args.warmup < 3:
+            args.warmup = 3
+        return run_gpt(args)
     set_workload(args.workload)
     if args.workload != "cfg2":
         args.skip_cpu = True  # the CPU baseline samples the headline workload only
@@ -312,10 +405,12 @@ def main():
     with ClockSampler(list(range(world)) if rank == 0 else []) as clocks:
         barrier()
         torch.cuda.synchronize()
+        launches0 = _capi.launch_count()
         start.record()
         for i in range(args.steps):
             launch(i % N_SETS, evs[i])
         stop.record()
+        launches = _capi.launch_count() - launches0
         torch.cuda.synchronize()
         barrier()
     if _capi.device_status() != 0:
@@ -403,7 +498,7 @@ def main():
                    "peak_device_bytes": peak_bytes},
         "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks.summary(),
         **({"memory_vs_seq": mem_rows} if mem_rows else {}),
-        "gpu_launches": 2 * args.steps,
+        "gpu_launches": launches,  # counted by the library (fh_launch_count) over the timed region
     }
     print(json.dumps(line), flush=True)
     return 0

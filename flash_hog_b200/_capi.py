@@ -43,6 +43,7 @@ EXPORTED_SYMBOLS = (
     "fh_status_string",
     "fh_last_error",
     "fh_abi_version",
+    "fh_launch_count",
 )
 ABI_VERSION = 2
 
@@ -97,6 +98,8 @@ def lib() -> ctypes.CDLL:
     h.fh_status_string.argtypes = [i32]
     h.fh_status_string.restype = ctypes.c_char_p
     h.fh_abi_version.argtypes = []
+    h.fh_launch_count.argtypes = []
+    h.fh_launch_count.restype = ctypes.c_ulonglong
     h.fh_last_error.argtypes = []
     h.fh_last_error.restype = ctypes.c_char_p
     for name in ("fh_attn_fwd", "fh_attn_rowdot", "fh_attn_bwd", "fh_attn_bwdbwd", "fh_attn_bwdbwd_pass",
@@ -211,6 +214,11 @@ def attn_bwdbwd_o(q, k, v, o, dO, ddq, ddk, ddv, lse, dq2, ddo, dk2, dv2, delta,
         _stream(q.device), ctypes.byref(dims), _ptr(q), _ptr(k), _ptr(v), _ptr(o), _ptr(dO), _ptr(ddq),
         _ptr(ddk), _ptr(ddv), _ptr(lse), _ptr(dq2), _ptr(ddo), _ptr(dk2), _ptr(dv2), _ptr(delta), _ptr(dd),
         _ptr(bvec), float(scale), int(causal), int(which)))
+
+
+def launch_count() -> int:
+    """Kernels launched by the library in this process so far."""
+    return int(lib().fh_launch_count())
 
 
 def device_status(device=None) -> int:

@@ -446,10 +446,10 @@ int launch_bwd_hd(const AttnShape& s, const BwdPtrs& p, int* status, cudaStream_
                static_cast<__nv_bfloat16*>(p.dv), status};
   bwd_dq_kernel<HD><<<dim3(s.H, s.B, (s.Tq + kBM - 1) / kBM), kThreads, GQ::SMEM, stream>>>(mq[0], mq[1], mq[2],
                                                                                           mq[3], args);
-  if (cudaGetLastError() != cudaSuccess) return kLaunchFailed;
+  if (after_launch() != kOk) return kLaunchFailed;
   bwd_dkdv_kernel<HD><<<dim3(s.Hk, s.B, (s.Tk + kBM - 1) / kBM), kThreads, GK::SMEM, stream>>>(mk[0], mk[1], mk[2],
                                                                                             mk[3], args);
-  return cudaGetLastError() == cudaSuccess ? kOk : kLaunchFailed;
+  return after_launch();
 }
 
 }  // namespace

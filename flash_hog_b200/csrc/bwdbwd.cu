@@ -855,12 +855,12 @@ int launch_bwdbwd_hd(const AttnShape& s, const BwdBwdPtrs& p, int passes, int* s
     const dim3 gq(s.H, s.B, (s.Tq + kBM - 1) / kBM);
     bwdbwd_q_kernel<HD><<<gq, kBBThreads, GQ::SMEM, stream>>>(mq[0], mq[1], mq[2], mq[3], mq[4], mq[5], mq[6],
                                                               mq[7], args);
-    if (cudaGetLastError() != cudaSuccess) return kLaunchFailed;
+    if (after_launch() != kOk) return kLaunchFailed;
   }
   if (passes & kPassKey) {
     const dim3 gk(s.Hk, s.B, (s.Tk + kBM - 1) / kBM);
     bwdbwd_k_kernel<HD><<<gk, kBBThreads, GK::SMEM, stream>>>(mk[0], mk[1], mk[2], mk[3], mk[4], mk[5], mk[6], args);
-    if (cudaGetLastError() != cudaSuccess) return kLaunchFailed;
+    if (after_launch() != kOk) return kLaunchFailed;
   }
   return kOk;
 }

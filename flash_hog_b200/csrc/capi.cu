@@ -4,6 +4,7 @@
 
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -129,6 +130,14 @@ bool all_aligned(P... ptrs) {
 
 }  // namespace
 
+std::atomic<unsigned long long> g_launches{0};
+
+int after_launch() {
+  if (cudaGetLastError() != cudaSuccess) return kLaunchFailed;
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return kOk;
+}
+
 int ensure_smem_limit(const void* func, int bytes) {
   const int dev = current_device();
   std::lock_guard<std::mutex> lock(g_mutex);
@@ -168,6 +177,8 @@ using namespace fh;
 extern "C" {
 
 int fh_abi_version(void) { return FH_ABI_VERSION; }
+
+unsigned long long fh_launch_count(void) { return fh::g_launches.load(std::memory_order_relaxed); }
 
 const char* fh_last_error(void) { return g_last_error; }
 

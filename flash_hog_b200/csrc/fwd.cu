@@ -278,7 +278,7 @@ int launch_fwd_hd(const AttnShape& s, const FwdPtrs& p, int* status, cudaStream_
   FwdArgs args{s, static_cast<__nv_bfloat16*>(p.o), p.lse, status};
   const dim3 grid(s.H, s.B, (s.Tq + kBM - 1) / kBM);
   fwd_kernel<HD><<<grid, kThreads, G::SMEM, stream>>>(mq, mk, mv, args);
-  return cudaGetLastError() == cudaSuccess ? kOk : kLaunchFailed;
+  return after_launch();
 }
 
 }  // namespace

@@ -50,6 +50,10 @@ int launch_bwd(const AttnShape& s, int hd, const BwdPtrs& p, int* status, cudaSt
 enum BwdBwdPass : int { kPassQuery = 1, kPassKey = 2 };
 int launch_bwdbwd(const AttnShape& s, int hd, const BwdBwdPtrs& p, int passes, int* status, cudaStream_t stream);
 
+// Checks the kernel launch just made (cudaGetLastError) and, if it was queued,
+// counts it for fh_launch_count(). Returns kOk or kLaunchFailed.
+int after_launch();
+
 // Sets the dynamic shared memory limit of `func` on the current device once.
 int ensure_smem_limit(const void* func, int bytes);
 

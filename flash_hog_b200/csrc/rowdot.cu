@@ -52,7 +52,7 @@ int launch_rowdot_hd(const AttnShape& s, const void* o, const void* dO, float* d
   if (grid > 0x7fffffffLL) return kInvalidArgument;
   rowdot_kernel<HD><<<static_cast<unsigned>(grid), block, 0, stream>>>(
       static_cast<const __nv_bfloat16*>(o), static_cast<const __nv_bfloat16*>(dO), delta, s);
-  return cudaGetLastError() == cudaSuccess ? kOk : kLaunchFailed;
+  return after_launch();
 }
 
 }  // namespace

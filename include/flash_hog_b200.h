@@ -185,6 +185,11 @@ const char* fh_status_string(int status);
 /* ABI version of this header (bumped on any signature change). */
 int fh_abi_version(void);
 
+/* Number of kernels this library has launched in the process so far (all
+ * devices, every entry point). No counterpart in the reference; a benchmark
+ * reads it before and after a timed region to report its kernel launches. */
+unsigned long long fh_launch_count(void);
+
 #define FH_ABI_VERSION 2
 
 #ifdef __cplusplus
