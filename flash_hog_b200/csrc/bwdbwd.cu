@@ -639,43 +639,64 @@ __global__ void __launch_bounds__(kBBThreads, 1)
     }
     int issued = 0;
     const float inv_scale = 1.f / sh.scale;
+    // Per-query statistics of tile `it` (BN/32 rows per lane), loaded one tile
+    // ahead into registers and only turned into biases when the tile is written,
+    // so the global-load latency overlaps the previous tile's work.
+    constexpr int RPL = BN / 32;
+    auto load_stats = [&](int it, float (&raw)[RPL][4]) {
+      const int q0 = (qt_begin + it % n) * BN;
+      const int h = hk * sh.G + it / n;
+#pragma unroll
+      for (int k = 0; k < RPL; ++k) {
+        const int q = q0 + lane + 32 * k;
+        const size_t idx = stat_index(b, h, q < sh.Tq ? q : 0, sh.H, sh.Tq);
+        raw[k][0] = a.lse[idx];
+        raw[k][1] = a.delta[idx];
+        raw[k][2] = a.dd[idx];
+        raw[k][3] = a.bv[idx];
+      }
+    };
+    float raw_next[RPL][4];
+    if (total > 0) load_stats(0, raw_next);
     for (int it = 0; it < total; ++it) {
       const int s = it % ST;
       const int q0 = (qt_begin + it % n) * BN;
       const int h = hk * sh.G + it / n;  // query head of this tile
-      // Per-query statistics of this tile (BN/32 rows per lane), fetched before
-      // waiting for the slot so their latency overlaps the wait.
-      constexpr int RPL = BN / 32;
-      float st[RPL][4];
-#pragma unroll
-      for (int k = 0; k < RPL; ++k) {
-        const int q = q0 + lane + 32 * k;
-        const bool v = q < sh.Tq;
-        const size_t idx = stat_index(b, h, v ? q : 0, sh.H, sh.Tq);
-        const float lse = v ? a.lse[idx] : 0.f, dl = v ? a.delta[idx] : 0.f, ddl = v ? a.dd[idx] : 0.f;
-        st[k][0] = -lse * inv_scale;                            // S - L/scale
-        st[k][1] = -ddl * inv_scale;                            // ddS/scale - dD/scale
-        st[k][2] = -dl;                                         // dP - D
-        st[k][3] = v ? -fmaf(ddl, dl, a.bv[idx]) : 0.f;         // dPa - c, c = dD D + B
-      }
       if (it >= ST && !mbar_wait_warp(&bar_empty[s], ((it / ST) - 1) & 1, &abort_flag)) {
         if (lane == 0) raise_error(a.status, &abort_flag, kDevTimeoutSlotEmpty);
         break;
       }
       uint8_t* slot = s_ring + s * G::SLOT;
-      const uint32_t bias = smem_u32(slot + G::PAIR + G::STR);
-#pragma unroll
-      for (int k = 0; k < RPL; ++k)
-#pragma unroll
-        for (int m = 0; m < 4; ++m) store_bias_row(bias, m * BN + lane + 32 * k, st[k][m]);
-      fence_async_smem();  // the tensor core reads the biases through the async proxy
-      __syncwarp();
+      // Copies first (their bytes are expected without arriving), then the biases;
+      // the single arrive after the biases completes the slot's phase together
+      // with the copies.
       if (lane == 0) {
-        mbar_arrive_expect_tx(&bar_full[s], G::PAIR + G::STR);
+        mbar_expect_tx(&bar_full[s], G::PAIR + G::STR);
         tma_pair<HD>(slot, &tm_q, &tm_ddq, &bar_full[s], q0, BN, h, b);
         tma_rows<HD>(slot + G::PAIR, &tm_do, &bar_full[s], q0, BN, h, b);
       }
+      float raw[RPL][4];  // first use of this tile's statistics: after its copies are issued
+#pragma unroll
+      for (int k = 0; k < RPL; ++k)
+#pragma unroll
+        for (int m = 0; m < 4; ++m) raw[k][m] = raw_next[k][m];
+      const uint32_t bias = smem_u32(slot + G::PAIR + G::STR);
+#pragma unroll
+      for (int k = 0; k < RPL; ++k) {
+        const bool v = q0 + lane + 32 * k < sh.Tq;
+        const float lse = raw[k][0], dl = raw[k][1], ddl = raw[k][2];
+        const int r = lane + 32 * k;
+        store_bias_row(bias, r, v ? -lse * inv_scale : 0.f);                   // S - L/scale
+        store_bias_row(bias, BN + r, v ? -ddl * inv_scale : 0.f);              // ddS/scale - dD/scale
+        store_bias_row(bias, 2 * BN + r, v ? -dl : 0.f);                       // dP - D
+        store_bias_row(bias, 3 * BN + r, v ? -fmaf(ddl, dl, raw[k][3]) : 0.f); // dPa - c, c = dD D + B
+      }
+      fence_async_smem();  // the tensor core reads the biases through the async proxy
       __syncwarp();
+      if (lane == 0) mbar_arrive(&bar_full[s]);
+      // Next tile's statistics: issued after the proxy fence, which would
+      // otherwise wait for these loads too.
+      if (it + 1 < total) load_stats(it + 1, raw_next);
       issued = it + 1;
     }
     if (lane == 0) {
