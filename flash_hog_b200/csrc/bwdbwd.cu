@@ -566,6 +566,38 @@ __device__ __forceinline__ void store_bias_row(uint32_t tile, int r, float x) {
   st_shared_v4(tile + sw32_offset(r, 1), 0u, 0u, 0u, 0u);
 }
 
+// A unit of key-pass work: one 128-row key tile of one (key head, batch).
+struct KItem {
+  int hk, b, k0, qt_begin, n, total;  // n query tiles per query head; total = n * G streamed tiles
+};
+
+// Work item w in heaviest-first order (key tile 0 first: the most causal query
+// tiles), key heads fastest.
+__device__ __forceinline__ KItem k_item(const AttnShape& sh, int w, int bn) {
+  const int per_kt = sh.Hk * sh.B;
+  const int kt = w / per_kt, rem = w - kt * per_kt;
+  KItem it;
+  it.hk = rem % sh.Hk;
+  it.b = rem / sh.Hk;
+  it.k0 = kt * kBM;
+  const int nq_tiles = (sh.Tq + bn - 1) / bn;
+  it.qt_begin = sh.causal ? it.k0 / bn : 0;
+  it.n = nq_tiles > it.qt_begin ? nq_tiles - it.qt_begin : 0;
+  it.total = it.n * sh.G;
+  return it;
+}
+
+// The j-th item of persistent CTA c out of P: a "snake" over the heaviest-first
+// order (c, then 2P-1-c, ...), which balances the causal work to within a few
+// percent without a global counter.
+__device__ __forceinline__ int snake_item(int j, int c, int P) { return j * P + ((j & 1) ? P - 1 - c : c); }
+
+// Persistent key-tiled pass: gridDim.x CTAs (one per SM) each run a sequence of
+// work items. The ring and the per-tile barriers run on one tile counter (gt)
+// across items; per item the producer reloads the resident tiles once the score
+// MMAs of the previous item are done (bar_res_empty), so the reload overlaps the
+// previous item's last tile and epilogue, and the operand MMAs of an item start
+// only once the previous item's accumulators were read out (bar_acc_empty).
 template <int HD>
 __global__ void __launch_bounds__(kBBThreads, 1)
     bwdbwd_k_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
@@ -582,26 +614,20 @@ __global__ void __launch_bounds__(kBBThreads, 1)
   uint8_t* s_ddv = s_ddk + G::RES;
   uint8_t* s_ones = s_ddv + G::RES;
   uint8_t* s_ring = s_ones + G::ONES;
-  __shared__ uint64_t bar_res, bar_full[ST], bar_empty[ST];
-  __shared__ uint64_t bar_sc_full, bar_sc_empty, bar_ops_full, bar_ops_empty, bar_acc;
+  __shared__ uint64_t bar_res, bar_res_empty, bar_full[ST], bar_empty[ST];
+  __shared__ uint64_t bar_sc_full, bar_sc_empty, bar_ops_full, bar_ops_empty, bar_acc, bar_acc_empty;
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
 
   const AttnShape& sh = a.sh;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int hk = blockIdx.x, b = blockIdx.y;  // key/value head
-  const int kt = blockIdx.z;  // key tile 0 carries the most causal work
-  const int k0 = kt * kBM;
-  const int nq_tiles = (sh.Tq + BN - 1) / BN;
-  const int qt_begin = sh.causal ? k0 / BN : 0;
-  const int n = nq_tiles > qt_begin ? nq_tiles - qt_begin : 0;  // query tiles per query head
-  // Streamed tile `it` is query tile qt_begin + it % n of query head hk*G + it / n:
-  // the G query heads sharing this key head accumulate into the same dK', dV'.
-  const int total = n * sh.G;
+  const int n_items = sh.Hk * sh.B * ((sh.Tk + kBM - 1) / kBM);
+  const int P = gridDim.x, c = blockIdx.x;
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
     mbar_init(&bar_res, 1);
+    mbar_init(&bar_res_empty, 1);
     for (int s = 0; s < ST; ++s) {
       mbar_init(&bar_full[s], 1);
       mbar_init(&bar_empty[s], 1);
@@ -611,6 +637,7 @@ __global__ void __launch_bounds__(kBBThreads, 1)
     mbar_init(&bar_ops_full, kBBEwWarps);
     mbar_init(&bar_ops_empty, 1);
     mbar_init(&bar_acc, 1);
+    mbar_init(&bar_acc_empty, kBBEwWarps);
     mbar_fence_init();
   }
   if (threadIdx.x < kBM) {
@@ -631,104 +658,127 @@ __global__ void __launch_bounds__(kBBThreads, 1)
     if (lane == 0) {
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_q);
-      mbar_arrive_expect_tx(&bar_res, 4 * G::RES);
-      tma_rows<HD>(s_k, &tm_k, &bar_res, k0, kBM, hk, b);
-      tma_rows<HD>(s_v, &tm_v, &bar_res, k0, kBM, hk, b);
-      tma_rows<HD>(s_ddk, &tm_ddk, &bar_res, k0, kBM, hk, b);
-      tma_rows<HD>(s_ddv, &tm_ddv, &bar_res, k0, kBM, hk, b);
     }
-    int issued = 0;
     const float inv_scale = 1.f / sh.scale;
-    // Per-query statistics of tile `it` (BN/32 rows per lane), loaded one tile
-    // ahead into registers and only turned into biases when the tile is written,
-    // so the global-load latency overlaps the previous tile's work.
     constexpr int RPL = BN / 32;
-    auto load_stats = [&](int it, float (&raw)[RPL][4]) {
-      const int q0 = (qt_begin + it % n) * BN;
-      const int h = hk * sh.G + it / n;
+    // Per-query statistics of streamed tile `it` of item `w`, into registers.
+    auto load_stats = [&](const KItem& w, int it, float (&raw)[RPL][4]) {
+      const int q0 = (w.qt_begin + it % w.n) * BN;
+      const int h = w.hk * sh.G + it / w.n;
 #pragma unroll
       for (int k = 0; k < RPL; ++k) {
         const int q = q0 + lane + 32 * k;
-        const size_t idx = stat_index(b, h, q < sh.Tq ? q : 0, sh.H, sh.Tq);
+        const size_t idx = stat_index(w.b, h, q < sh.Tq ? q : 0, sh.H, sh.Tq);
         raw[k][0] = a.lse[idx];
         raw[k][1] = a.delta[idx];
         raw[k][2] = a.dd[idx];
         raw[k][3] = a.bv[idx];
       }
     };
-    float raw_next[RPL][4];
-    if (total > 0) load_stats(0, raw_next);
-    for (int it = 0; it < total; ++it) {
-      const int s = it % ST;
-      const int q0 = (qt_begin + it % n) * BN;
-      const int h = hk * sh.G + it / n;  // query head of this tile
-      if (it >= ST && !mbar_wait_warp(&bar_empty[s], ((it / ST) - 1) & 1, &abort_flag)) {
+    int gt = 0, ai = 0;  // tiles and active items issued so far
+    bool ok = true;
+    for (int j = 0; ok; ++j) {
+      const int wi = snake_item(j, c, P);
+      if (wi >= n_items) break;
+      const KItem w = k_item(sh, wi, BN);
+      if (w.total == 0) continue;
+      // The previous item's score MMAs no longer read the resident tiles.
+      if (ai > 0 && !mbar_wait_warp(&bar_res_empty, (ai - 1) & 1, &abort_flag)) {
         if (lane == 0) raise_error(a.status, &abort_flag, kDevTimeoutSlotEmpty);
         break;
       }
-      uint8_t* slot = s_ring + s * G::SLOT;
-      // Copies first (their bytes are expected without arriving), then the biases;
-      // the single arrive after the biases completes the slot's phase together
-      // with the copies.
       if (lane == 0) {
-        mbar_expect_tx(&bar_full[s], G::PAIR + G::STR);
-        tma_pair<HD>(slot, &tm_q, &tm_ddq, &bar_full[s], q0, BN, h, b);
-        tma_rows<HD>(slot + G::PAIR, &tm_do, &bar_full[s], q0, BN, h, b);
+        mbar_arrive_expect_tx(&bar_res, 4 * G::RES);
+        tma_rows<HD>(s_k, &tm_k, &bar_res, w.k0, kBM, w.hk, w.b);
+        tma_rows<HD>(s_v, &tm_v, &bar_res, w.k0, kBM, w.hk, w.b);
+        tma_rows<HD>(s_ddk, &tm_ddk, &bar_res, w.k0, kBM, w.hk, w.b);
+        tma_rows<HD>(s_ddv, &tm_ddv, &bar_res, w.k0, kBM, w.hk, w.b);
       }
-      float raw[RPL][4];  // first use of this tile's statistics: after its copies are issued
+      ++ai;
+      float raw_next[RPL][4];
+      load_stats(w, 0, raw_next);
+      for (int it = 0; it < w.total; ++it, ++gt) {
+        const int s = gt % ST;
+        const int q0 = (w.qt_begin + it % w.n) * BN;
+        const int h = w.hk * sh.G + it / w.n;  // query head of this tile
+        if (gt >= ST && !mbar_wait_warp(&bar_empty[s], ((gt / ST) - 1) & 1, &abort_flag)) {
+          if (lane == 0) raise_error(a.status, &abort_flag, kDevTimeoutSlotEmpty);
+          ok = false;
+          break;
+        }
+        uint8_t* slot = s_ring + s * G::SLOT;
+        // Copies first (their bytes are expected without arriving), then the
+        // biases; the single arrive after the biases completes the slot's phase
+        // together with the copies.
+        if (lane == 0) {
+          mbar_expect_tx(&bar_full[s], G::PAIR + G::STR);
+          tma_pair<HD>(slot, &tm_q, &tm_ddq, &bar_full[s], q0, BN, h, w.b);
+          tma_rows<HD>(slot + G::PAIR, &tm_do, &bar_full[s], q0, BN, h, w.b);
+        }
+        float raw[RPL][4];  // first use of this tile's statistics: after its copies are issued
 #pragma unroll
-      for (int k = 0; k < RPL; ++k)
+        for (int k = 0; k < RPL; ++k)
 #pragma unroll
-        for (int m = 0; m < 4; ++m) raw[k][m] = raw_next[k][m];
-      const uint32_t bias = smem_u32(slot + G::PAIR + G::STR);
+          for (int m = 0; m < 4; ++m) raw[k][m] = raw_next[k][m];
+        const uint32_t bias = smem_u32(slot + G::PAIR + G::STR);
 #pragma unroll
-      for (int k = 0; k < RPL; ++k) {
-        const bool v = q0 + lane + 32 * k < sh.Tq;
-        const float lse = raw[k][0], dl = raw[k][1], ddl = raw[k][2];
-        const int r = lane + 32 * k;
-        store_bias_row(bias, r, v ? -lse * inv_scale : 0.f);                   // S - L/scale
-        store_bias_row(bias, BN + r, v ? -ddl * inv_scale : 0.f);              // ddS/scale - dD/scale
-        store_bias_row(bias, 2 * BN + r, v ? -dl : 0.f);                       // dP - D
-        store_bias_row(bias, 3 * BN + r, v ? -fmaf(ddl, dl, raw[k][3]) : 0.f); // dPa - c, c = dD D + B
+        for (int k = 0; k < RPL; ++k) {
+          const bool v = q0 + lane + 32 * k < sh.Tq;
+          const float lse = raw[k][0], dl = raw[k][1], ddl = raw[k][2];
+          const int r = lane + 32 * k;
+          store_bias_row(bias, r, v ? -lse * inv_scale : 0.f);                   // S - L/scale
+          store_bias_row(bias, BN + r, v ? -ddl * inv_scale : 0.f);              // ddS/scale - dD/scale
+          store_bias_row(bias, 2 * BN + r, v ? -dl : 0.f);                       // dP - D
+          store_bias_row(bias, 3 * BN + r, v ? -fmaf(ddl, dl, raw[k][3]) : 0.f); // dPa - c, c = dD D + B
+        }
+        fence_async_smem();  // the tensor core reads the biases through the async proxy
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar_full[s]);
+        // Next tile's statistics: issued after the proxy fence, which would
+        // otherwise wait for these loads too.
+        if (it + 1 < w.total) load_stats(w, it + 1, raw_next);
       }
-      fence_async_smem();  // the tensor core reads the biases through the async proxy
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bar_full[s]);
-      // Next tile's statistics: issued after the proxy fence, which would
-      // otherwise wait for these loads too.
-      if (it + 1 < total) load_stats(it + 1, raw_next);
-      issued = it + 1;
     }
     if (lane == 0) {
-      bool drained = mbar_wait(&bar_res, 0, nullptr);
-      for (int it = issued > ST ? issued - ST : 0; it < issued; ++it)
-        drained &= mbar_wait(&bar_full[it % ST], (it / ST) & 1, nullptr);
+      // Every issued copy must land before this CTA's shared memory is released.
+      bool drained = ai == 0 || mbar_wait(&bar_res, (ai - 1) & 1, nullptr);
+      for (int t = gt > ST ? gt - ST : 0; t < gt; ++t) drained &= mbar_wait(&bar_full[t % ST], (t / ST) & 1, nullptr);
       if (!drained) raise_error(a.status, &abort_flag, kDevTimeoutDrain);
     }
   } else if (warp == kBBWarpMma) {
     // ------------------------------ score MMA issuer ------------------------------
     //   [S^T | K ddQ^T] = K [Q ; ddQ]^T,  ddS^T += ddK Q^T,  dP^T = V dO^T,  dPa^T = ddV dO^T
-    if (n > 0) {
-      constexpr int KS = HD / 16;
-      const uint32_t id128 = idesc_bf16_f32(kBM, 2 * BN, false, false);
-      const uint32_t id64 = idesc_bf16_f32(kBM, BN, false, false);
-      const uint64_t a_k = kdesc(s_k), a_v = kdesc(s_v), a_ddk = kdesc(s_ddk), a_ddv = kdesc(s_ddv);
-      const uint64_t b_ring = kdesc(s_ring);          // pair (Q | ddQ) of slot 0
-      const uint64_t b_do = kdesc(s_ring + G::PAIR);  // dO of slot 0
-      const uint32_t id_bias = idesc_bf16_f32(kBM, 4 * BN, false, false);
-      const uint64_t a_ones = smem_desc(smem_u32(s_ones), 16, 8 * G::BIAS_ROW, kSwizzle32B);
-      const uint64_t b_bias = smem_desc(smem_u32(s_ring + G::PAIR + G::STR), 16, 8 * G::BIAS_ROW, kSwizzle32B);
-      constexpr uint64_t kSlot = G::SLOT >> 4;
-      bool ok = mbar_wait_warp(&bar_res, 0, &abort_flag);
-      if (!ok && lane == 0) raise_error(a.status, &abort_flag, kDevTimeoutTmaFull);
-      for (int it = 0; ok && it < total; ++it) {
-        const int s = it % ST;
-        if (!mbar_wait_warp(&bar_full[s], (it / ST) & 1, &abort_flag)) {
+    constexpr int KS = HD / 16;
+    const uint32_t id128 = idesc_bf16_f32(kBM, 2 * BN, false, false);
+    const uint32_t id64 = idesc_bf16_f32(kBM, BN, false, false);
+    const uint64_t a_k = kdesc(s_k), a_v = kdesc(s_v), a_ddk = kdesc(s_ddk), a_ddv = kdesc(s_ddv);
+    const uint64_t b_ring = kdesc(s_ring);          // pair (Q | ddQ) of slot 0
+    const uint64_t b_do = kdesc(s_ring + G::PAIR);  // dO of slot 0
+    const uint32_t id_bias = idesc_bf16_f32(kBM, 4 * BN, false, false);
+    const uint64_t a_ones = smem_desc(smem_u32(s_ones), 16, 8 * G::BIAS_ROW, kSwizzle32B);
+    const uint64_t b_bias = smem_desc(smem_u32(s_ring + G::PAIR + G::STR), 16, 8 * G::BIAS_ROW, kSwizzle32B);
+    constexpr uint64_t kSlot = G::SLOT >> 4;
+    int gt = 0, ai = 0;
+    bool ok = true;
+    for (int j = 0; ok; ++j) {
+      const int wi = snake_item(j, c, P);
+      if (wi >= n_items) break;
+      const KItem w = k_item(sh, wi, BN);
+      if (w.total == 0) continue;
+      if (!mbar_wait_warp(&bar_res, ai & 1, &abort_flag)) {
+        if (lane == 0) raise_error(a.status, &abort_flag, kDevTimeoutTmaFull);
+        break;
+      }
+      for (int it = 0; it < w.total; ++it, ++gt) {
+        const int s = gt % ST;
+        if (!mbar_wait_warp(&bar_full[s], (gt / ST) & 1, &abort_flag)) {
           if (lane == 0) raise_error(a.status, &abort_flag, kDevTimeoutTmaFull);
+          ok = false;
           break;
         }
-        if (it > 0 && !mbar_wait_warp(&bar_sc_empty, (it - 1) & 1, &abort_flag)) {
+        if (gt > 0 && !mbar_wait_warp(&bar_sc_empty, (gt - 1) & 1, &abort_flag)) {
           if (lane == 0) raise_error(a.status, &abort_flag, kDevTimeoutEpilogue);
+          ok = false;
           break;
         }
         tc_fence_after();
@@ -741,26 +791,41 @@ __global__ void __launch_bounds__(kBBThreads, 1)
         umma_chain_w<KS, G::RES_PANEL, BN * 128, false>(tmem + G::C_DPA, a_ddv, bo, id64, true);
         umma_commit_w(&bar_sc_full);
       }
+      if (!ok) break;
+      umma_commit_w(&bar_res_empty);  // once these MMAs finish, the residents may be reloaded
+      ++ai;
     }
   } else if (warp == kBBWarpMmaOut) {
     // ----------------------------- operand MMA issuer -----------------------------
     //   dK'/scale += dS^T ddQ + dS2^T Q,  dV' += ddP^T dO   (A in TMEM)
-    if (n > 0) {
-      constexpr int KO = BN / 16, OC = G::OPS_COLS;
-      const uint32_t id_out = idesc_bf16_f32(kBM, HD, false, true);
-      const uint64_t mn_ring = mndesc(s_ring, G::PAIR_PANEL);     // Q of slot 0, MN-major
-      const uint64_t mn_do = mndesc(s_ring + G::PAIR, BN * 128);  // dO of slot 0, MN-major
-      constexpr uint64_t kSlot = G::SLOT >> 4, kHalf = (BN * 128) >> 4;
-      const uint32_t t_ops = tmem + G::C_OPS;
-      bool ok = true;
-      for (int it = 0; it < total; ++it) {
-        if (!mbar_wait_warp(&bar_ops_full, it & 1, &abort_flag)) {
+    constexpr int KO = BN / 16, OC = G::OPS_COLS;
+    const uint32_t id_out = idesc_bf16_f32(kBM, HD, false, true);
+    const uint64_t mn_ring = mndesc(s_ring, G::PAIR_PANEL);     // Q of slot 0, MN-major
+    const uint64_t mn_do = mndesc(s_ring + G::PAIR, BN * 128);  // dO of slot 0, MN-major
+    constexpr uint64_t kSlot = G::SLOT >> 4, kHalf = (BN * 128) >> 4;
+    const uint32_t t_ops = tmem + G::C_OPS;
+    int gt = 0, ai = 0;
+    bool ok = true;
+    for (int j = 0; ok; ++j) {
+      const int wi = snake_item(j, c, P);
+      if (wi >= n_items) break;
+      const KItem w = k_item(sh, wi, BN);
+      if (w.total == 0) continue;
+      for (int it = 0; it < w.total; ++it, ++gt) {
+        if (!mbar_wait_warp(&bar_ops_full, gt & 1, &abort_flag)) {
+          if (lane == 0) raise_error(a.status, &abort_flag, kDevTimeoutEpilogue);
+          ok = false;
+          break;
+        }
+        // The first product of an item overwrites the accumulators: the previous
+        // item's epilogue must have read them.
+        if (it == 0 && ai > 0 && !mbar_wait_warp(&bar_acc_empty, (ai - 1) & 1, &abort_flag)) {
           if (lane == 0) raise_error(a.status, &abort_flag, kDevTimeoutEpilogue);
           ok = false;
           break;
         }
         tc_fence_after();
-        const int sp = it % ST;
+        const int sp = gt % ST;
         const uint64_t mq = mn_ring + sp * kSlot, mo = mn_do + sp * kSlot;
         const bool acc = it > 0;
         umma_chain_ts_w<KO>(tmem + G::C_DK, t_ops, mq + kHalf, id_out, acc);
@@ -769,7 +834,9 @@ __global__ void __launch_bounds__(kBBThreads, 1)
         umma_commit_w(&bar_ops_empty);
         umma_commit_w(&bar_empty[sp]);
       }
-      if (ok) umma_commit_w(&bar_acc);
+      if (!ok) break;
+      umma_commit_w(&bar_acc);
+      ++ai;
     }
   } else {
     // --------------------------- elementwise warps ----------------------------
@@ -777,55 +844,63 @@ __global__ void __launch_bounds__(kBBThreads, 1)
     const int r = (warp & 3) * 32 + lane;  // TMEM lane = key row inside the tile
     constexpr int CW = G::CW;
     const int cb = wg * CW;
-    const int key = k0 + r;
-    const bool key_ok = key < sh.Tk;
     const float sc = sh.scale, sc2 = sh.scale * kLog2e;
+    int gt = 0, ai = 0;
     bool ok = true;
-    for (int it = 0; it < total; ++it) {
-      const int qc = (qt_begin + it % n) * BN + cb;  // first query of this thread's columns
-      ok = mbar_wait_warp(&bar_sc_full, it & 1, &abort_flag);
-      if (!ok) break;
-      tc_fence_after();
-      uint32_t vs[CW], vdds[CW], vdp[CW], vdpa[CW];
-      tmem_share<CW>(tmem, warp, G::C_S + cb, vs);
-      tmem_share<CW>(tmem, warp, G::C_DDS + cb, vdds);
-      tmem_share<CW>(tmem, warp, G::C_DP + cb, vdp);
-      tmem_share<CW>(tmem, warp, G::C_DPA + cb, vdpa);
-      tmem_wait_ld();
-      reg_fence(vs);
-      reg_fence(vdds);
-      reg_fence(vdp);
-      reg_fence(vdpa);
-      warp_arrive(&bar_sc_empty);
-      const bool need_mask = (qc + CW > sh.Tq) || (sh.causal && qc < key);
-      uint32_t o_ds[CW / 2], o_ds2[CW / 2], o_ddp[CW / 2];
-      if (need_mask)
-        k_ops<CW, true>(vs, vdds, vdp, vdpa, qc, key, sh.Tq, sh.causal, sc, sc2, o_ds, o_ds2, o_ddp);
-      else
-        k_ops<CW, false>(vs, vdds, vdp, vdpa, qc, key, sh.Tq, sh.causal, sc, sc2, o_ds, o_ds2, o_ddp);
-      if (it > 0) ok = mbar_wait_warp(&bar_ops_empty, (it - 1) & 1, &abort_flag);
-      if (!ok) break;
-      tc_fence_after();
-      const uint32_t to = tmem + tmem_lane_base(warp & 3) + G::C_OPS + (CW / 2) * wg;
-      tmem_st_ops(to, o_ds);
-      tmem_st_ops(to + G::OPS_COLS, o_ds2);
-      tmem_st_ops(to + 2 * G::OPS_COLS, o_ddp);
-      tmem_wait_st();
-      warp_arrive(&bar_ops_full);
-    }
-    const int skey = key_ok ? key : 0;
-    __nv_bfloat16* dst = (wg == 0 ? a.dk2 : a.dv2) + row_offset(sh.sk, b, skey, hk);
-    if (n == 0) {
-      // No query sees these keys (causal with Tk > Tq): the gradients are zero.
-      if (key_ok) zero_row_global<HD>(dst);
-    } else {
-      if (ok) ok = mbar_wait_warp(&bar_acc, 0, &abort_flag);
-      if (ok) {
-        tc_fence_after();
-        tmem_row_to_global<HD>(tmem, warp, wg == 0 ? G::C_DK : G::C_DV, dst, key_ok, wg == 0 ? sc : 1.f);
-      } else if (threadIdx.x == kBBFirstEwWarp * 32) {
-        raise_error(a.status, &abort_flag, kDevTimeoutMma);
+    for (int j = 0; ok; ++j) {
+      const int wi = snake_item(j, c, P);
+      if (wi >= n_items) break;
+      const KItem w = k_item(sh, wi, BN);
+      const int key = w.k0 + r;
+      const bool key_ok = key < sh.Tk;
+      const int skey = key_ok ? key : 0;
+      __nv_bfloat16* dst = (wg == 0 ? a.dk2 : a.dv2) + row_offset(sh.sk, w.b, skey, w.hk);
+      if (w.total == 0) {
+        // No query sees these keys (causal with Tk > Tq): the gradients are zero.
+        if (key_ok) zero_row_global<HD>(dst);
+        continue;
       }
+      for (int it = 0; it < w.total; ++it, ++gt) {
+        const int qc = (w.qt_begin + it % w.n) * BN + cb;  // first query of this thread's columns
+        ok = mbar_wait_warp(&bar_sc_full, gt & 1, &abort_flag);
+        if (!ok) break;
+        tc_fence_after();
+        uint32_t vs[CW], vdds[CW], vdp[CW], vdpa[CW];
+        tmem_share<CW>(tmem, warp, G::C_S + cb, vs);
+        tmem_share<CW>(tmem, warp, G::C_DDS + cb, vdds);
+        tmem_share<CW>(tmem, warp, G::C_DP + cb, vdp);
+        tmem_share<CW>(tmem, warp, G::C_DPA + cb, vdpa);
+        tmem_wait_ld();
+        reg_fence(vs);
+        reg_fence(vdds);
+        reg_fence(vdp);
+        reg_fence(vdpa);
+        warp_arrive(&bar_sc_empty);
+        const bool need_mask = (qc + CW > sh.Tq) || (sh.causal && qc < key);
+        uint32_t o_ds[CW / 2], o_ds2[CW / 2], o_ddp[CW / 2];
+        if (need_mask)
+          k_ops<CW, true>(vs, vdds, vdp, vdpa, qc, key, sh.Tq, sh.causal, sc, sc2, o_ds, o_ds2, o_ddp);
+        else
+          k_ops<CW, false>(vs, vdds, vdp, vdpa, qc, key, sh.Tq, sh.causal, sc, sc2, o_ds, o_ds2, o_ddp);
+        if (gt > 0) ok = mbar_wait_warp(&bar_ops_empty, (gt - 1) & 1, &abort_flag);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t to = tmem + tmem_lane_base(warp & 3) + G::C_OPS + (CW / 2) * wg;
+        tmem_st_ops(to, o_ds);
+        tmem_st_ops(to + G::OPS_COLS, o_ds2);
+        tmem_st_ops(to + 2 * G::OPS_COLS, o_ddp);
+        tmem_wait_st();
+        warp_arrive(&bar_ops_full);
+      }
+      if (ok) ok = mbar_wait_warp(&bar_acc, ai & 1, &abort_flag);
+      if (!ok) {
+        if (threadIdx.x == kBBFirstEwWarp * 32) raise_error(a.status, &abort_flag, kDevTimeoutMma);
+        break;
+      }
+      tc_fence_after();
+      tmem_row_to_global<HD>(tmem, warp, wg == 0 ? G::C_DK : G::C_DV, dst, key_ok, wg == 0 ? sc : 1.f);
+      warp_arrive(&bar_acc_empty);  // the accumulators may be overwritten by the next item
+      ++ai;
     }
   }
 
@@ -879,7 +954,9 @@ int launch_bwdbwd_hd(const AttnShape& s, const BwdBwdPtrs& p, int passes, int* s
     if (after_launch() != kOk) return kLaunchFailed;
   }
   if (passes & kPassKey) {
-    const dim3 gk(s.Hk, s.B, (s.Tk + kBM - 1) / kBM);
+    // Persistent: one CTA per SM (at most one per work item).
+    const int items = s.Hk * s.B * ((s.Tk + kBM - 1) / kBM);
+    const dim3 gk(static_cast<unsigned>(items < sm_count() ? items : sm_count()));
     bwdbwd_k_kernel<HD><<<gk, kBBThreads, GK::SMEM, stream>>>(mk[0], mk[1], mk[2], mk[3], mk[4], mk[5], mk[6], args);
     if (after_launch() != kOk) return kLaunchFailed;
   }

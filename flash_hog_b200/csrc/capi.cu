@@ -131,6 +131,18 @@ bool all_aligned(P... ptrs) {
 }  // namespace
 
 std::atomic<unsigned long long> g_launches{0};
+std::atomic<int> g_sm_count[kMaxDevices];
+
+int sm_count() {
+  const int dev = current_device();
+  if (dev < 0 || dev >= kMaxDevices) return 1;
+  int n = g_sm_count[dev].load(std::memory_order_relaxed);
+  if (n <= 0) {
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 1;
+    g_sm_count[dev].store(n, std::memory_order_relaxed);
+  }
+  return n;
+}
 
 int after_launch() {
   if (cudaGetLastError() != cudaSuccess) return kLaunchFailed;

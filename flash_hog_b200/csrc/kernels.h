@@ -54,6 +54,10 @@ int launch_bwdbwd(const AttnShape& s, int hd, const BwdBwdPtrs& p, int passes, i
 // counts it for fh_launch_count(). Returns kOk or kLaunchFailed.
 int after_launch();
 
+// Streaming multiprocessors of the current device (cached per device): the
+// grid size of the persistent kernels.
+int sm_count();
+
 // Sets the dynamic shared memory limit of `func` on the current device once.
 int ensure_smem_limit(const void* func, int bytes);
 
