@@ -186,14 +186,23 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 #pragma unroll
       for (int i = 0; i < BN; ++i) asm volatile("" : "+r"(v[i])::"memory");
       const bool need_mask = (k0 + BN > sh.Tk) || (sh.causal && k0 + BN - 1 > row);
-      float tmax = -INFINITY;
+      if (need_mask) {
+        const int lim = sh.causal ? min(sh.Tk, row + 1) : sh.Tk;  // keys [k0, lim) are visible
 #pragma unroll
-      for (int i = 0; i < BN; ++i) {
-        float s = __uint_as_float(v[i]) * sc2;
-        if (need_mask && (k0 + i >= sh.Tk || (sh.causal && k0 + i > row))) s = -INFINITY;
-        v[i] = __float_as_uint(s);
-        tmax = fmaxf(tmax, s);
+        for (int i = 0; i < BN; ++i)
+          if (k0 + i >= lim) v[i] = __float_as_uint(-INFINITY);
       }
+      // Row maximum of the raw scores (the scale is positive), eight independent chains.
+      float mx[8];
+#pragma unroll
+      for (int c = 0; c < 8; ++c) mx[c] = __uint_as_float(v[c]);
+#pragma unroll
+      for (int i = 8; i < BN; ++i) mx[i & 7] = fmaxf(mx[i & 7], __uint_as_float(v[i]));
+#pragma unroll
+      for (int c = 4; c > 0; c >>= 1)
+#pragma unroll
+        for (int k = 0; k < c; ++k) mx[k] = fmaxf(mx[k], mx[k + c]);
+      const float tmax = mx[0] * sc2;  // log2 domain
       // O is stable once the previous O update is done (needed for a rescale).
       if (j > 0) {
         ok = mbar_wait_warp(&bar_pv, (j - 1) & 1, &abort_flag);
@@ -221,12 +230,15 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       const float base = (m_used == -INFINITY) ? 0.f : m_used;
       uint32_t pk[BN / 2];
       float psum = 0.f;
+      float ps[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int i = 0; i < BN; i += 2) {
-        const float p0 = ex2(__uint_as_float(v[i]) - base), p1 = ex2(__uint_as_float(v[i + 1]) - base);
-        psum += p0 + p1;
+        const float p0 = ex2(fmaf(__uint_as_float(v[i]), sc2, -base));
+        const float p1 = ex2(fmaf(__uint_as_float(v[i + 1]), sc2, -base));
+        ps[(i >> 1) & 3] += p0 + p1;
         pk[i / 2] = pack_bf16(p0, p1);
       }
+      psum = (ps[0] + ps[1]) + (ps[2] + ps[3]);
       l += psum;
 #pragma unroll
       for (int c = 0; c < BN / 2; c += 16) tmem_st16(tcol + c, *reinterpret_cast<const uint32_t(*)[16]>(&pk[c]));
