@@ -1,0 +1,85 @@
+// Pieces shared by the warp-specialised attention kernels (double backward and
+// first-order backward): the 11-warp CTA layout, TMEM operand shares, bias
+// operands for the tensor core, and the persistent work-item order.
+
+#pragma once
+
+#include "attn_common.cuh"
+
+namespace fh {
+
+// ----------------------------------------------------------------------------------
+// CTA layout shared by the warp-specialised kernels
+// ----------------------------------------------------------------------------------
+//
+// 11 warps. Warp 0 allocates TMEM and issues the score MMAs, warp 1 issues the
+// accumulating (operand) MMAs, warp 2 is the TMA producer, warps 3-10 are two
+// elementwise warpgroups: thread (warp, lane) owns TMEM lane 32*(warp%4)+lane
+// (one resident row) and warpgroup w = (warp-3)/4 owns columns [CW w, CW w + CW)
+// of every BN-row streamed tile (CW = BN/2: 32 at head_dim 64, 16 at 128). TMEM lane quadrants pin the elementwise warps
+// to all four schedulers, and their arithmetic starves a co-resident issuing
+// thread; two issuers on different schedulers halve that exposure and let the
+// score MMAs of the next tile and the operand MMAs of this tile be issued
+// independently, each as soon as its inputs are ready.
+// Each elementwise thread loads its CW-column share of all four score tiles
+// into registers and releases the score buffer at once. The bf16 operands it
+// produces (dS, dS2, ddP, P) go back to TMEM with tcgen05.st and are read there
+// as the A operand of the accumulating MMAs.
+constexpr int kBBThreads = 352;
+constexpr int kBBEwWarps = 8;  // elementwise arrivals are one per warp
+constexpr int kBBWarpMma = 0;      // score MMAs; TMEM allocation
+constexpr int kBBWarpMmaOut = 1;   // operand (accumulating) MMAs
+constexpr int kBBWarpProducer = 2;
+constexpr int kBBFirstEwWarp = 3;
+
+// All lanes of the warp have finished their TMEM / shared-memory accesses; one lane arrives.
+__device__ __forceinline__ void warp_arrive(uint64_t* bar) {
+  tc_fence_before();
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) mbar_arrive(bar);
+}
+
+// This thread's CW-column share of a score tile (x16 loads).
+template <int CW>
+__device__ __forceinline__ void tmem_share(uint32_t tmem, int warp, int col, uint32_t (&r)[CW]) {
+  static_assert(CW % 16 == 0, "shares are whole x16 loads");
+#pragma unroll
+  for (int c = 0; c < CW; c += 16)
+    tmem_ld16(tmem + tmem_lane_base(warp & 3) + col + c, *reinterpret_cast<uint32_t(*)[16]>(&r[c]));
+}
+
+template <int N>
+__device__ __forceinline__ void reg_fence(uint32_t (&r)[N]) {
+#pragma unroll
+  for (int i = 0; i < N; ++i) asm volatile("" : "+r"(r[i])::"memory");
+}
+
+// Stores a thread's N packed bf16 operand columns (N = 16 or 8) to TMEM.
+template <int N>
+__device__ __forceinline__ void tmem_st_ops(uint32_t taddr, const uint32_t (&r)[N]) {
+  static_assert(N == 16 || N == 8, "operand shares are 16 or 8 packed columns");
+  if constexpr (N == 16) tmem_st16(taddr, r);
+  else tmem_st8(taddr, r);
+}
+
+// One 16-byte chunk of a 32B-swizzled K = 16 bf16 operand row (tiles 256-byte aligned).
+__device__ __forceinline__ uint32_t sw32_offset(int r, int c) {
+  return static_cast<uint32_t>(r * 32 + ((c ^ ((r >> 2) & 1)) << 4));
+}
+
+// Writes (hi, lo) with hi + lo = x to within 2^-16 |x| as row r of a bias operand.
+__device__ __forceinline__ void store_bias_row(uint32_t tile, int r, float x) {
+  const __nv_bfloat16 hi = __float2bfloat16_rn(x);
+  const __nv_bfloat16 lo = __float2bfloat16_rn(x - __bfloat162float(hi));
+  const uint32_t pair = static_cast<uint32_t>(__bfloat16_as_ushort(hi)) |
+                        (static_cast<uint32_t>(__bfloat16_as_ushort(lo)) << 16);
+  st_shared_v4(tile + sw32_offset(r, 0), pair, 0u, 0u, 0u);
+  st_shared_v4(tile + sw32_offset(r, 1), 0u, 0u, 0u, 0u);
+}
+
+// The j-th item of persistent CTA c out of P: a "snake" over the heaviest-first
+// order (c, then 2P-1-c, ...), which balances the causal work to within a few
+// percent without a global counter.
+__device__ __forceinline__ int snake_item(int j, int c, int P) { return j * P + ((j & 1) ? P - 1 - c : c); }
+
+}  // namespace fh
