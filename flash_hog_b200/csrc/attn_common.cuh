@@ -169,6 +169,17 @@ __device__ __forceinline__ void umma_chain_ts_w(uint32_t d, uint32_t a_tmem, uin
   }
 }
 
+// KSTEPS chained tcgen05.mma with A in TMEM and B a K-major shared-memory
+// operand whose 64-column K panels are B_PANEL bytes apart.
+template <int KSTEPS, int B_PANEL>
+__device__ __forceinline__ void umma_chain_tsk_w(uint32_t d, uint32_t a_tmem, uint64_t b0, uint32_t idesc, bool acc) {
+  static_assert(KSTEPS % 4 == 0, "chains are issued four k-steps at a time");
+#pragma unroll
+  for (int ks = 0; ks < KSTEPS; ks += 4)
+    umma_bf16_ts_x4_w(d, a_tmem + 8 * ks, b0 + koff<B_PANEL>(ks), b0 + koff<B_PANEL>(ks + 1),
+                      b0 + koff<B_PANEL>(ks + 2), b0 + koff<B_PANEL>(ks + 3), idesc, (acc || ks > 0) ? 1u : 0u);
+}
+
 // Loads a pair of BN-row tiles (X then Y) of HD columns into "pair" panels:
 // panel p holds X's rows then Y's rows (2*BN rows of 128 bytes), so the pair is
 // one 2*BN-row K-major operand and each half is an MN-major operand with panel

@@ -3,17 +3,29 @@
 // (flash_hog/jax/_attention_impl.py:242-261; formulas of
 // flash_hog/_jax_refs/jax_impl.py:142-191).
 //
-// Atomic-free split into two launches after the D = rowsum(dO o O) pre-pass:
-//  * `bwd_dq_kernel`, query-tiled: S = Q K^T, dP = dO V^T,
-//    dS = scale P o (dP - D), dQ += dS K;
-//  * `bwd_dkdv_kernel`, key-tiled on transposed scores: S^T = K Q^T,
-//    dP^T = V dO^T, dV += P^T dO, dK += dS^T Q.
+// Two launches, no atomics, no (Nq, Nk) intermediate in global memory:
+//  * `bwd_dq_kernel`, query-tiled: one CTA per 128 query rows. It computes
+//    D = rowsum(dO o O) for its rows (written out for the second launch), then
+//    streams 64-key tiles of K, V:  S = Q K^T, dP = dO V^T,
+//    dS/scale = P o (dP - D), dQ/scale += dS K;
+//  * `bwd_dkdv_kernel`, key-tiled on transposed scores: one CTA per 128 key
+//    rows; it streams 64-query tiles of Q, dO with their L and D:
+//    S^T = K Q^T, dP^T = V dO^T, dV += P^T dO, dK/scale += dS^T Q.
+//
+// Both use the 11-warp layout of the double backward (two MMA issuers, a TMA
+// producer, two elementwise warpgroups). The resident operand of every score
+// product (Q and dO, or K and V) is copied into TMEM once per CTA, so the score
+// MMAs read only the streamed tile from shared memory and run at the tensor
+// core's math rate; the key-tiled pass folds -L/scale and -D into its score
+// accumulators with one bias MMA per tile, so its elementwise warps read no
+// per-query statistics.
 
 #include <cuda_runtime.h>
 
 #include <cmath>
 
 #include "kernels.h"
+#include "ws_common.cuh"
 
 namespace fh {
 namespace {
@@ -21,84 +33,129 @@ namespace {
 struct BwdArgs {
   AttnShape sh;
   const float* lse;
-  const float* delta;
+  float* delta;  // D = rowsum(dO o O): written by the query-tiled pass, read by the key-tiled pass
   __nv_bfloat16* dq;
   __nv_bfloat16* dk;
   __nv_bfloat16* dv;
   int* status;
 };
 
-constexpr int round_up_1024(int x) { return (x + 1023) / 1024 * 1024; }
+// ----------------------------------------------------------------------------------
+// query-tiled pass: dQ (and D)
+// ----------------------------------------------------------------------------------
 
 template <int HD>
 struct DqPass {
-  static constexpr int BN = 64, ST = 3;
+  static constexpr int BN = 64;  // keys per streamed tile
+  static constexpr int ST = 4;   // ring depth
+  static constexpr int CW = BN / 2;
   static constexpr int RES = kBM * HD * 2;
+  static constexpr int RES_PANEL = kBM * 128;
   static constexpr int STR = BN * HD * 2;
-  static constexpr int SLOT = 2 * STR;  // K | V
-  static constexpr int OPS = kBM * BN * 2;
-  static constexpr int SMEM = 1024 + 2 * RES + ST * SLOT + OPS;
-  static constexpr int C_S = 0, C_DP = BN, C_DQ = 2 * BN;
-  static constexpr int TMEM_COLS = 256;
-  static_assert(C_DQ + HD <= TMEM_COLS, "TMEM budget");
+  static constexpr int STR_PANEL = BN * 128;
+  static constexpr int SLOT = 2 * STR;                     // K, V
+  static constexpr int SMEM = 1024 + 2 * RES + ST * SLOT;  // Q, dO, ring (O borrows the last slot)
+  // TMEM: two score buffers [S | dP], the dQ accumulator, the bf16 dS operand
+  // (BN/2 packed columns), then Q -- and dO at head_dim 64, where it fits --
+  // as packed bf16 A operands of the score MMAs.
+  static constexpr bool DO_TMEM = HD == 64;
+  static constexpr int C_S = 0, C_DP = BN, SCORE_COLS = 2 * BN;
+  static constexpr int C_DQ = 2 * SCORE_COLS, C_OPS = C_DQ + HD, C_QT = C_OPS + BN / 2, C_DOT = C_QT + HD / 2;
+  static constexpr int TMEM_COLS = 512;
+  static_assert(C_DOT + (DO_TMEM ? HD / 2 : 0) <= TMEM_COLS, "TMEM budget");
+  static_assert(RES <= SLOT, "O fits in one ring slot");
+  static_assert(SMEM <= 232448, "shared memory budget");
+  static_assert(CW % 16 == 0 && HD % 64 == 0, "tile shapes");
 };
 
+// Packed bf16 pairs of dS/scale = P (dP - D) for this thread's CW key columns.
+template <int CW, bool MASK>
+__device__ __forceinline__ void dq_ops(const uint32_t (&vs)[CW], const uint32_t (&vdp)[CW], int kc, int row, int tk,
+                                       int causal, float sc2, float lg, float dv, uint32_t (&o_ds)[CW / 2]) {
+#pragma unroll
+  for (int i = 0; i < CW; i += 2) {
+    float ds[2];
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int c = i + e;
+      float s = fmaf(__uint_as_float(vs[c]), sc2, -lg);
+      if (MASK && (kc + c >= tk || (causal && kc + c > row))) s = -INFINITY;
+      ds[e] = ex2(s) * (__uint_as_float(vdp[c]) - dv);
+    }
+    o_ds[i / 2] = pack_bf16(ds[0], ds[1]);
+  }
+}
+
 template <int HD>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kBBThreads, 1)
     bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
                   const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
-                  const BwdArgs a) {
+                  const __grid_constant__ CUtensorMap tm_o, const BwdArgs a) {
   using G = DqPass<HD>;
-  constexpr int BN = G::BN, ST = G::ST;
+  constexpr int BN = G::BN, ST = G::ST, CW = G::CW;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = align1024(smem_raw);
   uint8_t* s_q = sm;
   uint8_t* s_do = s_q + G::RES;
   uint8_t* s_ring = s_do + G::RES;
-  uint8_t* s_ops = s_ring + ST * G::SLOT;
-  __shared__ uint64_t bar_res, bar_full[ST], bar_empty[ST];
-  __shared__ uint64_t bar_sc_full, bar_sc_empty, bar_ops_full, bar_ops_empty, bar_acc;
+  // O is staged in the last ring slot, which the first ST-1 key tiles do not
+  // use; the producer refills it only once every elementwise warp has read O.
+  uint8_t* s_o = s_ring + (ST - 1) * G::SLOT;
+  __shared__ uint64_t bar_res, bar_tres, bar_ofree, bar_dred, bar_full[ST], bar_empty[ST];
+  __shared__ uint64_t bar_sc_full[2], bar_sc_empty[2], bar_ops_full, bar_ops_empty, bar_acc;
+  __shared__ float dred[2][kBM];  // partial rowsum(dO o O): warpgroup, row
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
 
   const AttnShape& sh = a.sh;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int h = blockIdx.x, b = blockIdx.y;
-  const int qt = gridDim.z - 1 - blockIdx.z;
+  const int qt = gridDim.z - 1 - blockIdx.z;  // longest causal rows first
   const int q0 = qt * kBM;
   const int kv_end = sh.causal ? min(sh.Tk, q0 + kBM) : sh.Tk;
-  const int n = (kv_end + BN - 1) / BN;
+  const int n = (kv_end + BN - 1) / BN;  // key tiles (>= 1)
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
     mbar_init(&bar_res, 1);
+    mbar_init(&bar_tres, kBBEwWarps);
+    mbar_init(&bar_ofree, kBBEwWarps);
+    mbar_init(&bar_dred, kBBEwWarps);
     for (int s = 0; s < ST; ++s) {
       mbar_init(&bar_full[s], 1);
       mbar_init(&bar_empty[s], 1);
     }
-    mbar_init(&bar_sc_full, 1);
-    mbar_init(&bar_sc_empty, kEwThreads);
-    mbar_init(&bar_ops_full, kEwThreads);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bar_sc_full[i], 1);
+      mbar_init(&bar_sc_empty[i], kBBEwWarps);
+    }
+    mbar_init(&bar_ops_full, kBBEwWarps);
     mbar_init(&bar_ops_empty, 1);
     mbar_init(&bar_acc, 1);
     mbar_fence_init();
   }
-  if (warp == kWarpMma) tmem_alloc(&tmem_base, G::TMEM_COLS);
+  if (warp == kBBWarpMma) tmem_alloc(&tmem_base, G::TMEM_COLS);
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_base;
 
-  if (warp == kWarpProducer) {
+  if (warp == kBBWarpProducer) {
+    // ------------------------------ TMA producer ------------------------------
     if (lane == 0) {
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
-      mbar_arrive_expect_tx(&bar_res, 2 * G::RES);
+      mbar_arrive_expect_tx(&bar_res, 3 * G::RES);
       tma_rows<HD>(s_q, &tm_q, &bar_res, q0, kBM, h, b);
       tma_rows<HD>(s_do, &tm_do, &bar_res, q0, kBM, h, b);
+      tma_rows<HD>(s_o, &tm_o, &bar_res, q0, kBM, h, b);
       int issued = 0;
       for (int it = 0; it < n; ++it) {
         const int s = it % ST;
         if (it >= ST && !mbar_wait(&bar_empty[s], ((it / ST) - 1) & 1, &abort_flag)) {
+          raise_error(a.status, &abort_flag, kDevTimeoutSlotEmpty);
+          break;
+        }
+        if (it == ST - 1 && !mbar_wait(&bar_ofree, 0, &abort_flag)) {
           raise_error(a.status, &abort_flag, kDevTimeoutSlotEmpty);
           break;
         }
@@ -108,166 +165,257 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_rows<HD>(slot + G::STR, &tm_v, &bar_full[s], it * BN, BN, h / sh.G, b);
         issued = it + 1;
       }
+      // Every issued copy must land before this CTA's shared memory is released.
       bool drained = mbar_wait(&bar_res, 0, nullptr);
       for (int it = issued > ST ? issued - ST : 0; it < issued; ++it)
         drained &= mbar_wait(&bar_full[it % ST], (it / ST) & 1, nullptr);
       if (!drained) raise_error(a.status, &abort_flag, kDevTimeoutDrain);
     }
-  } else if (warp == kWarpMma) {
-    if (lane == 0) {
-      const uint32_t id_sc = idesc_bf16_f32(kBM, BN, false, false);
-      const uint32_t id_out = idesc_bf16_f32(kBM, HD, false, true);
-      bool ok = mbar_wait(&bar_res, 0, &abort_flag);
-      if (!ok) raise_error(a.status, &abort_flag, kDevTimeoutTmaFull);
-      for (int it = 0; ok && it <= n; ++it) {
-        if (it < n) {
-          const int s = it % ST;
-          if (!mbar_wait(&bar_full[s], (it / ST) & 1, &abort_flag) ||
-              (it > 0 && !mbar_wait(&bar_sc_empty, (it - 1) & 1, &abort_flag))) {
-            raise_error(a.status, &abort_flag, kDevTimeoutTmaFull);
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint8_t* slot = s_ring + s * G::SLOT;
-          gemm_abt(tmem + G::C_S, s_q, slot, BN, HD / 16, id_sc, false);              // S  = Q K^T
-          gemm_abt(tmem + G::C_DP, s_do, slot + G::STR, BN, HD / 16, id_sc, false);   // dP = dO V^T
-          umma_commit(&bar_sc_full);
-        }
-        const int t = it - 1;
-        if (t >= 0) {
-          if (!mbar_wait(&bar_ops_full, t & 1, &abort_flag)) {
-            raise_error(a.status, &abort_flag, kDevTimeoutEpilogue);
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const int sp = t % ST;
-          gemm_ab(tmem + G::C_DQ, s_ops, s_ring + sp * G::SLOT, BN, BN / 16, id_out, t > 0);  // dQ += dS K
-          umma_commit(&bar_ops_empty);
-          umma_commit(&bar_empty[sp]);
-        }
+  } else if (warp == kBBWarpMma) {
+    // ------------------------------ score MMA issuer ------------------------------
+    //   S = Q K^T,  dP = dO V^T   (Q, dO in TMEM; K, V K-major in the ring)
+    constexpr int KS = HD / 16;
+    const uint32_t id_s = idesc_bf16_f32(kBM, BN, false, false);
+    const uint64_t b_ring = kdesc(s_ring);  // K of slot 0
+    const uint64_t a_do = kdesc(s_do);
+    constexpr uint64_t kSlot = G::SLOT >> 4, kStr = G::STR >> 4;
+    bool ok = mbar_wait_warp(&bar_res, 0, &abort_flag) && mbar_wait_warp(&bar_tres, 0, &abort_flag);
+    if (!ok && lane == 0) raise_error(a.status, &abort_flag, kDevTimeoutTmaFull);
+    for (int it = 0; ok && it < n; ++it) {
+      const int s = it % ST, sb = it & 1, u = it >> 1;
+      if (!mbar_wait_warp(&bar_full[s], (it / ST) & 1, &abort_flag)) {
+        if (lane == 0) raise_error(a.status, &abort_flag, kDevTimeoutTmaFull);
+        break;
       }
-      if (ok) umma_commit(&bar_acc);
+      if (u > 0 && !mbar_wait_warp(&bar_sc_empty[sb], (u - 1) & 1, &abort_flag)) {
+        if (lane == 0) raise_error(a.status, &abort_flag, kDevTimeoutEpilogue);
+        break;
+      }
+      tc_fence_after();
+      const uint64_t bk = b_ring + s * kSlot;
+      const uint32_t tb = tmem + sb * G::SCORE_COLS;
+      umma_chain_tsk_w<KS, G::STR_PANEL>(tb + G::C_S, tmem + G::C_QT, bk, id_s, false);
+      if constexpr (G::DO_TMEM)
+        umma_chain_tsk_w<KS, G::STR_PANEL>(tb + G::C_DP, tmem + G::C_DOT, bk + kStr, id_s, false);
+      else
+        umma_chain_w<KS, G::RES_PANEL, G::STR_PANEL, false>(tb + G::C_DP, a_do, bk + kStr, id_s, false);
+      umma_commit_w(&bar_sc_full[sb]);
     }
+  } else if (warp == kBBWarpMmaOut) {
+    // ----------------------------- operand MMA issuer -----------------------------
+    //   dQ/scale += dS K   (dS in TMEM, K MN-major in the ring)
+    const uint32_t id_dq = idesc_bf16_f32(kBM, HD, false, true);
+    const uint64_t mn_ring = mndesc(s_ring, G::STR_PANEL);
+    constexpr uint64_t kSlot = G::SLOT >> 4;
+    bool ok = true;
+    for (int j = 0; j < n; ++j) {
+      if (!mbar_wait_warp(&bar_ops_full, j & 1, &abort_flag)) {
+        if (lane == 0) raise_error(a.status, &abort_flag, kDevTimeoutEpilogue);
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const int s = j % ST;
+      umma_chain_ts_w<BN / 16>(tmem + G::C_DQ, tmem + G::C_OPS, mn_ring + s * kSlot, id_dq, j > 0);
+      umma_commit_w(&bar_ops_empty);
+      umma_commit_w(&bar_empty[s]);
+    }
+    if (ok) umma_commit_w(&bar_acc);
   } else {
-    const int r = threadIdx.x;
+    // --------------------------- elementwise warps ----------------------------
+    const int wg = (warp - kBBFirstEwWarp) >> 2;  // column half of every tile
+    const int r = (warp & 3) * 32 + lane;         // TMEM lane = query row inside the tile
+    const uint32_t lane_t = tmem + tmem_lane_base(warp & 3);
+    const int cb = wg * CW;
     const int row = q0 + r;
     const bool row_ok = row < sh.Tq;
     const size_t vi = stat_index(b, h, row_ok ? row : 0, sh.H, sh.Tq);
     const float lg = row_ok ? a.lse[vi] * kLog2e : 0.f;
-    const float dv = row_ok ? a.delta[vi] : 0.f;
-    const float sc = sh.scale, sc2 = sh.scale * kLog2e;
-    bool ok = true;
-    for (int it = 0; it < n; ++it) {
-      const int k0 = it * BN;
-      ok = __all_sync(0xffffffffu, mbar_wait(&bar_sc_full, it & 1, &abort_flag));
-      if (ok && it > 0) ok = __all_sync(0xffffffffu, mbar_wait(&bar_ops_empty, (it - 1) & 1, &abort_flag));
+    const float sc2 = sh.scale * kLog2e;
+    bool ok = mbar_wait_warp(&bar_res, 0, &abort_flag);
+    float dv = 0.f;
+    if (ok) {
+      // This warpgroup's half of the head_dim columns of Q (and dO) into TMEM.
+      row_to_tmem<HD / 2>(s_q, r, wg * (HD / 2), lane_t + G::C_QT);
+      if constexpr (G::DO_TMEM) row_to_tmem<HD / 2>(s_do, r, wg * (HD / 2), lane_t + G::C_DOT);
+      tmem_wait_st();
+      warp_arrive(&bar_tres);
+      // D = rowsum(dO o O) of this row: each warpgroup sums half the columns.
+      dred[wg][r] = rowdot_share<HD>(s_o, s_do, r, wg);
+      warp_arrive(&bar_ofree);  // O has been read: its ring slot may be refilled
+      warp_arrive(&bar_dred);
+      ok = mbar_wait_warp(&bar_dred, 0, &abort_flag);
+      dv = dred[0][r] + dred[1][r];
+      if (ok && wg == 0 && row_ok) a.delta[vi] = dv;
+    }
+    for (int j = 0; ok && j < n; ++j) {
+      const int sb = j & 1;
+      ok = mbar_wait_warp(&bar_sc_full[sb], (j >> 1) & 1, &abort_flag);
       if (!ok) break;
       tc_fence_after();
-      const bool need_mask = (k0 + BN > sh.Tk) || (sh.causal && k0 + BN - 1 > q0);
-#pragma unroll 1
-      for (int c = 0; c < BN / 16; ++c) {
-        uint32_t vs[16], vdp[16];
-        tmem_row16(tmem, warp, G::C_S + c * 16, vs);
-        tmem_row16(tmem, warp, G::C_DP + c * 16, vdp);
-        tmem_wait_ld();
-        reg_fence16(vs);
-        reg_fence16(vdp);
-        float o_ds[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int key = k0 + c * 16 + i;
-          float s = fmaf(__uint_as_float(vs[i]), sc2, -lg);
-          if (need_mask && (key >= sh.Tk || (sh.causal && key > row))) s = -INFINITY;
-          const float p = ex2(s);
-          o_ds[i] = p * sc * (__uint_as_float(vdp[i]) - dv);
-        }
-        stage_bf16x16(s_ops, r, c, o_ds);
-      }
-      tc_fence_before();
-      mbar_arrive(&bar_sc_empty);
-      fence_async_smem();
-      mbar_arrive(&bar_ops_full);
+      const uint32_t tb = tmem + sb * G::SCORE_COLS;
+      uint32_t vs[CW], vdp[CW];
+      tmem_share<CW>(tb, warp, G::C_S + cb, vs);
+      tmem_share<CW>(tb, warp, G::C_DP + cb, vdp);
+      tmem_wait_ld();
+      reg_fence(vs);
+      reg_fence(vdp);
+      warp_arrive(&bar_sc_empty[sb]);  // the tensor core may reuse this score buffer now
+      const int kc = j * BN + cb;      // first key of this thread's columns
+      const bool need_mask = (kc + CW > sh.Tk) || (sh.causal && kc + CW - 1 > row);
+      uint32_t o_ds[CW / 2];
+      if (need_mask)
+        dq_ops<CW, true>(vs, vdp, kc, row, sh.Tk, sh.causal, sc2, lg, dv, o_ds);
+      else
+        dq_ops<CW, false>(vs, vdp, kc, row, sh.Tk, sh.causal, sc2, lg, dv, o_ds);
+      if (j > 0) ok = mbar_wait_warp(&bar_ops_empty, (j - 1) & 1, &abort_flag);
+      if (!ok) break;
+      tc_fence_after();
+      tmem_st_ops(lane_t + G::C_OPS + (CW / 2) * wg, o_ds);
+      tmem_wait_st();
+      warp_arrive(&bar_ops_full);
     }
-    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&bar_acc, 0, &abort_flag));
+    if (ok) ok = mbar_wait_warp(&bar_acc, 0, &abort_flag);
     if (ok) {
       tc_fence_after();
-      tmem_row_to_global<HD>(tmem, warp, G::C_DQ, a.dq + row_offset(sh.sq, b, row_ok ? row : 0, h), row_ok);
-    } else if (threadIdx.x == 0) {
+      const int srow = row_ok ? row : 0;
+      tmem_row_to_global<HD / 2>(tmem, warp, G::C_DQ + wg * (HD / 2),
+                                 a.dq + row_offset(sh.sq, b, srow, h) + wg * (HD / 2), row_ok, sh.scale);
+    } else if (threadIdx.x == kBBFirstEwWarp * 32) {
       raise_error(a.status, &abort_flag, kDevTimeoutMma);
     }
   }
 
   tc_fence_before();
   __syncthreads();
-  if (warp == kWarpMma) tmem_dealloc(tmem, G::TMEM_COLS);
+  if (warp == kBBWarpMma) tmem_dealloc(tmem, G::TMEM_COLS);
 }
+
+// ----------------------------------------------------------------------------------
+// key-tiled pass: dK, dV
+// ----------------------------------------------------------------------------------
 
 template <int HD>
 struct DkvPass {
-  static constexpr int BN = 64, ST = 3;
+  static constexpr int BN = 64;  // queries per streamed tile
+  static constexpr int ST = 4;
+  static constexpr int CW = BN / 2;
   static constexpr int RES = kBM * HD * 2;
+  static constexpr int RES_PANEL = kBM * 128;
   static constexpr int STR = BN * HD * 2;
-  static constexpr int VEC = BN * 4;
-  static constexpr int SLOT = round_up_1024(2 * STR + 2 * VEC);  // Q | dO | L, D
-  static constexpr int OPS = kBM * BN * 2;
-  static constexpr int SMEM = 1024 + 2 * RES + ST * SLOT + 2 * OPS;
-  static constexpr int C_S = 0, C_DP = BN, C_DK = 2 * BN, C_DV = 2 * BN + HD;
-  static constexpr int TMEM_COLS = C_DV + HD <= 256 ? 256 : 512;
-  static_assert(C_DV + HD <= TMEM_COLS, "TMEM budget");
+  static constexpr int STR_PANEL = BN * 128;
+  // Per-query biases of the two score products as a K = 16 bf16 operand (32-byte
+  // rows, 32B swizzle): rows [0, BN) hold -L/scale, rows [BN, 2 BN) hold -D, each
+  // a (hi, lo) bf16 pair in columns 0-1, zeros after.
+  static constexpr int BIAS_ROW = 32;
+  static constexpr int BIAS = 2 * BN * BIAS_ROW;
+  static constexpr int ONES = kBM * BIAS_ROW;  // resident A operand: (1, 1, 0, ...) per key row
+  static constexpr int SLOT = 2 * STR + BIAS;  // Q, dO, biases
+  static constexpr int SMEM = 1024 + 2 * RES + ONES + ST * SLOT;
+  // TMEM: score buffers [S^T | dP^T] (two at head_dim 64, one at 128), the dK
+  // and dV accumulators, the bf16 operands P^T and dS^T, then K -- and V at
+  // head_dim 64 -- as packed bf16 A operands of the score MMAs.
+  static constexpr bool V_TMEM = HD == 64;
+  static constexpr int NB = HD == 64 ? 2 : 1;
+  static constexpr int C_S = 0, C_DP = BN, SCORE_COLS = 2 * BN;
+  static constexpr int C_DK = NB * SCORE_COLS, C_DV = C_DK + HD, C_OPS = C_DV + HD, OPS_COLS = BN / 2;
+  static constexpr int C_KT = C_OPS + 2 * OPS_COLS, C_VT = C_KT + HD / 2;
+  static constexpr int TMEM_COLS = 512;
+  static_assert(C_VT + (V_TMEM ? HD / 2 : 0) <= TMEM_COLS, "TMEM budget");
+  static_assert(C_DP == C_S + BN, "one bias MMA covers both products");
+  static_assert(SLOT % 1024 == 0 && (2 * RES + ONES) % 1024 == 0, "slots must keep panels 1024-byte aligned");
+  static_assert(SMEM <= 232448, "shared memory budget");
+  static_assert(CW % 16 == 0 && HD % 64 == 0, "tile shapes");
 };
 
+// Packed bf16 pairs of P^T and dS^T/scale = P^T (dP^T - D) for this thread's CW
+// query columns; the statistics arrive folded into the scores by the bias MMA:
+//   vs = S - L/scale,  vdp = dP - D.
+template <int CW, bool MASK>
+__device__ __forceinline__ void dkv_ops(const uint32_t (&vs)[CW], const uint32_t (&vdp)[CW], int qc, int key, int tq,
+                                        int causal, float sc2, uint32_t (&o_p)[CW / 2], uint32_t (&o_ds)[CW / 2]) {
+#pragma unroll
+  for (int i = 0; i < CW; i += 2) {
+    float pp[2], ds[2];
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int c = i + e;
+      float s = __uint_as_float(vs[c]) * sc2;
+      if (MASK && (qc + c >= tq || (causal && qc + c < key))) s = -INFINITY;
+      pp[e] = ex2(s);
+      ds[e] = pp[e] * __uint_as_float(vdp[c]);
+    }
+    o_p[i / 2] = pack_bf16(pp[0], pp[1]);
+    o_ds[i / 2] = pack_bf16(ds[0], ds[1]);
+  }
+}
+
 template <int HD>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kBBThreads, 1)
     bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                     const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
                     const BwdArgs a) {
   using G = DkvPass<HD>;
-  constexpr int BN = G::BN, ST = G::ST;
+  constexpr int BN = G::BN, ST = G::ST, CW = G::CW, NB = G::NB;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = align1024(smem_raw);
   uint8_t* s_k = sm;
   uint8_t* s_v = s_k + G::RES;
-  uint8_t* s_ring = s_v + G::RES;
-  uint8_t* s_ops = s_ring + ST * G::SLOT;  // P^T | dS^T
-  __shared__ uint64_t bar_res, bar_full[ST], bar_empty[ST];
-  __shared__ uint64_t bar_sc_full, bar_sc_empty, bar_ops_full, bar_ops_empty, bar_acc;
+  uint8_t* s_ones = s_v + G::RES;
+  uint8_t* s_ring = s_ones + G::ONES;
+  __shared__ uint64_t bar_res, bar_tres, bar_full[ST], bar_empty[ST];
+  __shared__ uint64_t bar_sc_full[NB], bar_sc_empty[NB], bar_ops_full, bar_ops_empty, bar_acc;
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
 
   const AttnShape& sh = a.sh;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int hk = blockIdx.x, b = blockIdx.y;  // key/value head
-  const int kt = blockIdx.z;
-  const int k0 = kt * kBM;
+  const int hk = blockIdx.x, b = blockIdx.y;
+  const int k0 = blockIdx.z * kBM;  // key tile 0 first: the most causal query tiles
   const int nq_tiles = (sh.Tq + BN - 1) / BN;
-  const int qt_begin = sh.causal ? k0 / BN : 0;
-  const int n = nq_tiles > qt_begin ? nq_tiles - qt_begin : 0;  // query tiles per query head
-  // Streamed tile `it` is query tile qt_begin + it % n of query head hk*G + it / n:
-  // the G query heads sharing this key head accumulate into the same dK, dV.
-  const int total = n * sh.G;
+  const int qt_begin = sh.causal ? k0 / BN : 0;  // earlier queries see none of these keys
+  const int n = nq_tiles > qt_begin ? nq_tiles - qt_begin : 0;
+  const int total = n * sh.G;  // streamed tiles: n per query head of the group
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
     mbar_init(&bar_res, 1);
+    mbar_init(&bar_tres, kBBEwWarps);
     for (int s = 0; s < ST; ++s) {
       mbar_init(&bar_full[s], 1);
       mbar_init(&bar_empty[s], 1);
     }
-    mbar_init(&bar_sc_full, 1);
-    mbar_init(&bar_sc_empty, kEwThreads);
-    mbar_init(&bar_ops_full, kEwThreads);
+    for (int i = 0; i < NB; ++i) {
+      mbar_init(&bar_sc_full[i], 1);
+      mbar_init(&bar_sc_empty[i], kBBEwWarps);
+    }
+    mbar_init(&bar_ops_full, kBBEwWarps);
     mbar_init(&bar_ops_empty, 1);
     mbar_init(&bar_acc, 1);
     mbar_fence_init();
   }
-  if (warp == kWarpMma) tmem_alloc(&tmem_base, G::TMEM_COLS);
+  if (threadIdx.x < kBM) {
+    // The resident ones operand: row r = (1, 1, 0, ..., 0), so ones x biases^T
+    // adds hi + lo of each query's bias to every key row.
+    const uint32_t t = smem_u32(s_ones);
+    st_shared_v4(t + sw32_offset(threadIdx.x, 0), 0x3F803F80u, 0u, 0u, 0u);
+    st_shared_v4(t + sw32_offset(threadIdx.x, 1), 0u, 0u, 0u, 0u);
+    fence_async_smem();
+  }
+  if (warp == kBBWarpMma) tmem_alloc(&tmem_base, G::TMEM_COLS);
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_base;
 
-  if (warp == kWarpProducer) {
+  if (total == 0) {
+    // No query sees these keys (causal with Tk > Tq): the gradients are zero.
+    if (warp >= kBBFirstEwWarp) {
+      const int wg = (warp - kBBFirstEwWarp) >> 2;
+      const int key = k0 + (warp & 3) * 32 + lane;
+      if (key < sh.Tk) zero_row_global<HD>((wg == 0 ? a.dk : a.dv) + row_offset(sh.sk, b, key, hk));
+    }
+  } else if (warp == kBBWarpProducer) {
+    // ---------------------- TMA producer (whole warp) -----------------------
     if (lane == 0) {
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_q);
@@ -275,163 +423,195 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_rows<HD>(s_k, &tm_k, &bar_res, k0, kBM, hk, b);
       tma_rows<HD>(s_v, &tm_v, &bar_res, k0, kBM, hk, b);
     }
+    const float inv_scale = 1.f / sh.scale;
+    constexpr int RPL = BN / 32;
+    // L and D of the queries of streamed tile `it`, into registers.
+    auto load_stats = [&](int it, float (&raw)[RPL][2]) {
+      const int q0 = (qt_begin + it % n) * BN;
+      const int h = hk * sh.G + it / n;
+#pragma unroll
+      for (int k = 0; k < RPL; ++k) {
+        const int q = q0 + lane + 32 * k;
+        const size_t idx = stat_index(b, h, q < sh.Tq ? q : 0, sh.H, sh.Tq);
+        raw[k][0] = a.lse[idx];
+        raw[k][1] = a.delta[idx];
+      }
+    };
+    float raw_next[RPL][2];
+    load_stats(0, raw_next);
     int issued = 0;
     for (int it = 0; it < total; ++it) {
       const int s = it % ST;
       const int q0 = (qt_begin + it % n) * BN;
-      const int h = hk * sh.G + it / n;
-      float st[2][2];
-#pragma unroll
-      for (int k = 0; k < 2; ++k) {
-        const int q = q0 + lane + 32 * k;
-        const bool v = q < sh.Tq;
-        const size_t idx = stat_index(b, h, v ? q : 0, sh.H, sh.Tq);
-        st[k][0] = v ? a.lse[idx] : 0.f;
-        st[k][1] = v ? a.delta[idx] : 0.f;
-      }
-      bool ok = true;
-      if (it >= ST) ok = mbar_wait(&bar_empty[s], ((it / ST) - 1) & 1, &abort_flag);
-      if (!__all_sync(0xffffffffu, ok)) {
+      const int h = hk * sh.G + it / n;  // query head of this tile
+      if (it >= ST && !mbar_wait_warp(&bar_empty[s], ((it / ST) - 1) & 1, &abort_flag)) {
         if (lane == 0) raise_error(a.status, &abort_flag, kDevTimeoutSlotEmpty);
         break;
       }
       uint8_t* slot = s_ring + s * G::SLOT;
-      float* sv = reinterpret_cast<float*>(slot + 2 * G::STR);
-#pragma unroll
-      for (int k = 0; k < 2; ++k) {
-        sv[lane + 32 * k] = st[k][0];
-        sv[BN + lane + 32 * k] = st[k][1];
-      }
-      __syncwarp();
+      // Copies first (their bytes are expected without arriving), then the
+      // biases; the single arrive after the biases completes the slot's phase
+      // together with the copies.
       if (lane == 0) {
-        mbar_arrive_expect_tx(&bar_full[s], 2 * G::STR);
+        mbar_expect_tx(&bar_full[s], 2 * G::STR);
         tma_rows<HD>(slot, &tm_q, &bar_full[s], q0, BN, h, b);
         tma_rows<HD>(slot + G::STR, &tm_do, &bar_full[s], q0, BN, h, b);
       }
+      float raw[RPL][2];
+#pragma unroll
+      for (int k = 0; k < RPL; ++k) {
+        raw[k][0] = raw_next[k][0];
+        raw[k][1] = raw_next[k][1];
+      }
+      const uint32_t bias = smem_u32(slot + 2 * G::STR);
+#pragma unroll
+      for (int k = 0; k < RPL; ++k) {
+        const bool v = q0 + lane + 32 * k < sh.Tq;
+        const int r = lane + 32 * k;
+        store_bias_row(bias, r, v ? -raw[k][0] * inv_scale : 0.f);  // S - L/scale
+        store_bias_row(bias, BN + r, v ? -raw[k][1] : 0.f);         // dP - D
+      }
+      fence_async_smem();  // the tensor core reads the biases through the async proxy
       __syncwarp();
+      if (lane == 0) mbar_arrive(&bar_full[s]);
       issued = it + 1;
+      if (it + 1 < total) load_stats(it + 1, raw_next);
     }
     if (lane == 0) {
+      // Every issued copy must land before this CTA's shared memory is released.
       bool drained = mbar_wait(&bar_res, 0, nullptr);
-      for (int it = issued > ST ? issued - ST : 0; it < issued; ++it)
-        drained &= mbar_wait(&bar_full[it % ST], (it / ST) & 1, nullptr);
+      for (int t = issued > ST ? issued - ST : 0; t < issued; ++t)
+        drained &= mbar_wait(&bar_full[t % ST], (t / ST) & 1, nullptr);
       if (!drained) raise_error(a.status, &abort_flag, kDevTimeoutDrain);
     }
-  } else if (warp == kWarpMma) {
-    if (lane == 0 && n > 0) {
-      const uint32_t id_sc = idesc_bf16_f32(kBM, BN, false, false);
-      const uint32_t id_out = idesc_bf16_f32(kBM, HD, false, true);
-      bool ok = mbar_wait(&bar_res, 0, &abort_flag);
-      if (!ok) raise_error(a.status, &abort_flag, kDevTimeoutTmaFull);
-      for (int it = 0; ok && it <= total; ++it) {
-        if (it < total) {
-          const int s = it % ST;
-          if (!mbar_wait(&bar_full[s], (it / ST) & 1, &abort_flag) ||
-              (it > 0 && !mbar_wait(&bar_sc_empty, (it - 1) & 1, &abort_flag))) {
-            raise_error(a.status, &abort_flag, kDevTimeoutTmaFull);
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint8_t* slot = s_ring + s * G::SLOT;
-          gemm_abt(tmem + G::C_S, s_k, slot, BN, HD / 16, id_sc, false);             // S^T  = K Q^T
-          gemm_abt(tmem + G::C_DP, s_v, slot + G::STR, BN, HD / 16, id_sc, false);   // dP^T = V dO^T
-          umma_commit(&bar_sc_full);
-        }
-        const int t = it - 1;
-        if (t >= 0) {
-          if (!mbar_wait(&bar_ops_full, t & 1, &abort_flag)) {
-            raise_error(a.status, &abort_flag, kDevTimeoutEpilogue);
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const int sp = t % ST;
-          const uint8_t* slot = s_ring + sp * G::SLOT;
-          gemm_ab(tmem + G::C_DV, s_ops, slot + G::STR, BN, BN / 16, id_out, t > 0);   // dV += P^T dO
-          gemm_ab(tmem + G::C_DK, s_ops + G::OPS, slot, BN, BN / 16, id_out, t > 0);   // dK += dS^T Q
-          umma_commit(&bar_ops_empty);
-          umma_commit(&bar_empty[sp]);
-        }
+  } else if (warp == kBBWarpMma) {
+    // ------------------------------ score MMA issuer ------------------------------
+    //   [S^T | dP^T] = ones [-L/scale ; -D]^T,  S^T += K Q^T,  dP^T += V dO^T
+    constexpr int KS = HD / 16;
+    const uint32_t id_s = idesc_bf16_f32(kBM, BN, false, false);
+    const uint32_t id_bias = idesc_bf16_f32(kBM, 2 * BN, false, false);
+    const uint64_t b_q = kdesc(s_ring);  // Q of slot 0; dO follows at +STR
+    const uint64_t a_v = kdesc(s_v);
+    const uint64_t a_ones = smem_desc(smem_u32(s_ones), 16, 8 * G::BIAS_ROW, kSwizzle32B);
+    const uint64_t b_bias = smem_desc(smem_u32(s_ring + 2 * G::STR), 16, 8 * G::BIAS_ROW, kSwizzle32B);
+    constexpr uint64_t kSlot = G::SLOT >> 4, kStr = G::STR >> 4;
+    bool ok = mbar_wait_warp(&bar_res, 0, &abort_flag) && mbar_wait_warp(&bar_tres, 0, &abort_flag);
+    if (!ok && lane == 0) raise_error(a.status, &abort_flag, kDevTimeoutTmaFull);
+    for (int it = 0; ok && it < total; ++it) {
+      const int s = it % ST, sb = it % NB, u = it / NB;
+      if (!mbar_wait_warp(&bar_full[s], (it / ST) & 1, &abort_flag)) {
+        if (lane == 0) raise_error(a.status, &abort_flag, kDevTimeoutTmaFull);
+        break;
       }
-      if (ok) umma_commit(&bar_acc);
+      if (u > 0 && !mbar_wait_warp(&bar_sc_empty[sb], (u - 1) & 1, &abort_flag)) {
+        if (lane == 0) raise_error(a.status, &abort_flag, kDevTimeoutEpilogue);
+        break;
+      }
+      tc_fence_after();
+      const uint64_t bq = b_q + s * kSlot;
+      const uint32_t tb = tmem + sb * G::SCORE_COLS;
+      umma_bf16_w(tb + G::C_S, a_ones, b_bias + s * kSlot, id_bias, 0u);
+      umma_chain_tsk_w<KS, G::STR_PANEL>(tb + G::C_S, tmem + G::C_KT, bq, id_s, true);
+      if constexpr (G::V_TMEM)
+        umma_chain_tsk_w<KS, G::STR_PANEL>(tb + G::C_DP, tmem + G::C_VT, bq + kStr, id_s, true);
+      else
+        umma_chain_w<KS, G::RES_PANEL, G::STR_PANEL, false>(tb + G::C_DP, a_v, bq + kStr, id_s, true);
+      umma_commit_w(&bar_sc_full[sb]);
     }
-  } else {
-    const int r = threadIdx.x;
-    const int key = k0 + r;
-    const bool key_ok = key < sh.Tk;
-    const float sc = sh.scale, sc2 = sh.scale * kLog2e;
+  } else if (warp == kBBWarpMmaOut) {
+    // ----------------------------- operand MMA issuer -----------------------------
+    //   dV += P^T dO,  dK/scale += dS^T Q   (A in TMEM, B MN-major in the ring)
+    constexpr int KO = BN / 16, OC = G::OPS_COLS;
+    const uint32_t id_o = idesc_bf16_f32(kBM, HD, false, true);
+    const uint64_t mn_q = mndesc(s_ring, G::STR_PANEL);
+    const uint64_t mn_do = mndesc(s_ring + G::STR, G::STR_PANEL);
+    constexpr uint64_t kSlot = G::SLOT >> 4;
     bool ok = true;
     for (int it = 0; it < total; ++it) {
+      if (!mbar_wait_warp(&bar_ops_full, it & 1, &abort_flag)) {
+        if (lane == 0) raise_error(a.status, &abort_flag, kDevTimeoutEpilogue);
+        ok = false;
+        break;
+      }
+      tc_fence_after();
       const int s = it % ST;
-      const int q0 = (qt_begin + it % n) * BN;
-      ok = __all_sync(0xffffffffu, mbar_wait(&bar_sc_full, it & 1, &abort_flag));
-      if (ok && it > 0) ok = __all_sync(0xffffffffu, mbar_wait(&bar_ops_empty, (it - 1) & 1, &abort_flag));
+      umma_chain_ts_w<KO>(tmem + G::C_DV, tmem + G::C_OPS, mn_do + s * kSlot, id_o, it > 0);
+      umma_chain_ts_w<KO>(tmem + G::C_DK, tmem + G::C_OPS + OC, mn_q + s * kSlot, id_o, it > 0);
+      umma_commit_w(&bar_ops_empty);
+      umma_commit_w(&bar_empty[s]);
+    }
+    if (ok) umma_commit_w(&bar_acc);
+  } else {
+    // --------------------------- elementwise warps ----------------------------
+    const int wg = (warp - kBBFirstEwWarp) >> 2;
+    const int r = (warp & 3) * 32 + lane;  // TMEM lane = key row inside the tile
+    const uint32_t lane_t = tmem + tmem_lane_base(warp & 3);
+    const int cb = wg * CW;
+    const int key = k0 + r;
+    const bool key_ok = key < sh.Tk;
+    const float sc2 = sh.scale * kLog2e;
+    bool ok = mbar_wait_warp(&bar_res, 0, &abort_flag);
+    if (ok) {
+      // This warpgroup's half of the head_dim columns of K (and V) into TMEM.
+      row_to_tmem<HD / 2>(s_k, r, wg * (HD / 2), lane_t + G::C_KT);
+      if constexpr (G::V_TMEM) row_to_tmem<HD / 2>(s_v, r, wg * (HD / 2), lane_t + G::C_VT);
+      tmem_wait_st();
+      warp_arrive(&bar_tres);
+    }
+    for (int it = 0; ok && it < total; ++it) {
+      const int sb = it % NB;
+      ok = mbar_wait_warp(&bar_sc_full[sb], (it / NB) & 1, &abort_flag);
       if (!ok) break;
       tc_fence_after();
-      const float* sv = reinterpret_cast<const float*>(s_ring + s * G::SLOT + 2 * G::STR);
-      const bool need_mask = (q0 + BN > sh.Tq) || (sh.causal && q0 < k0 + kBM - 1);
-#pragma unroll 1
-      for (int c = 0; c < BN / 16; ++c) {
-        uint32_t vs[16], vdp[16];
-        tmem_row16(tmem, warp, G::C_S + c * 16, vs);
-        tmem_row16(tmem, warp, G::C_DP + c * 16, vdp);
-        tmem_wait_ld();
-        reg_fence16(vs);
-        reg_fence16(vdp);
-        float o_p[16], o_ds[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int col = c * 16 + i;
-          const int q = q0 + col;
-          float s = fmaf(__uint_as_float(vs[i]), sc2, -sv[col] * kLog2e);
-          if (need_mask && (q >= sh.Tq || (sh.causal && q < key))) s = -INFINITY;
-          const float p = ex2(s);
-          o_p[i] = p;
-          o_ds[i] = p * sc * (__uint_as_float(vdp[i]) - sv[BN + col]);
-        }
-        stage_bf16x16(s_ops, r, c, o_p);
-        stage_bf16x16(s_ops + G::OPS, r, c, o_ds);
-      }
-      tc_fence_before();
-      mbar_arrive(&bar_sc_empty);
-      fence_async_smem();
-      mbar_arrive(&bar_ops_full);
+      const uint32_t tb = tmem + sb * G::SCORE_COLS;
+      uint32_t vs[CW], vdp[CW];
+      tmem_share<CW>(tb, warp, G::C_S + cb, vs);
+      tmem_share<CW>(tb, warp, G::C_DP + cb, vdp);
+      tmem_wait_ld();
+      reg_fence(vs);
+      reg_fence(vdp);
+      warp_arrive(&bar_sc_empty[sb]);
+      const int qc = (qt_begin + it % n) * BN + cb;  // first query of this thread's columns
+      const bool need_mask = (qc + CW > sh.Tq) || (sh.causal && qc < key);
+      uint32_t o_p[CW / 2], o_ds[CW / 2];
+      if (need_mask)
+        dkv_ops<CW, true>(vs, vdp, qc, key, sh.Tq, sh.causal, sc2, o_p, o_ds);
+      else
+        dkv_ops<CW, false>(vs, vdp, qc, key, sh.Tq, sh.causal, sc2, o_p, o_ds);
+      if (it > 0) ok = mbar_wait_warp(&bar_ops_empty, (it - 1) & 1, &abort_flag);
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t to = lane_t + G::C_OPS + (CW / 2) * wg;
+      tmem_st_ops(to, o_p);
+      tmem_st_ops(to + G::OPS_COLS, o_ds);
+      tmem_wait_st();
+      warp_arrive(&bar_ops_full);
     }
-    const int skey = key_ok ? key : 0;
-    __nv_bfloat16* dk_row = a.dk + row_offset(sh.sk, b, skey, hk);
-    __nv_bfloat16* dv_row = a.dv + row_offset(sh.sk, b, skey, hk);
-    if (n == 0) {
-      if (key_ok) {
-        zero_row_global<HD>(dk_row);
-        zero_row_global<HD>(dv_row);
-      }
-    } else {
-      if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&bar_acc, 0, &abort_flag));
-      if (ok) {
-        tc_fence_after();
-        tmem_row_to_global<HD>(tmem, warp, G::C_DK, dk_row, key_ok);
-        tmem_row_to_global<HD>(tmem, warp, G::C_DV, dv_row, key_ok);
-      } else if (threadIdx.x == 0) {
-        raise_error(a.status, &abort_flag, kDevTimeoutMma);
-      }
+    if (ok) ok = mbar_wait_warp(&bar_acc, 0, &abort_flag);
+    if (ok) {
+      tc_fence_after();
+      __nv_bfloat16* dst = (wg == 0 ? a.dk : a.dv) + row_offset(sh.sk, b, key_ok ? key : 0, hk);
+      tmem_row_to_global<HD>(tmem, warp, wg == 0 ? G::C_DK : G::C_DV, dst, key_ok, wg == 0 ? sh.scale : 1.f);
+    } else if (threadIdx.x == kBBFirstEwWarp * 32) {
+      raise_error(a.status, &abort_flag, kDevTimeoutMma);
     }
   }
 
   tc_fence_before();
   __syncthreads();
-  if (warp == kWarpMma) tmem_dealloc(tmem, G::TMEM_COLS);
+  if (warp == kBBWarpMma) tmem_dealloc(tmem, G::TMEM_COLS);
 }
 
 template <int HD>
 int launch_bwd_hd(const AttnShape& s, const BwdPtrs& p, int* status, cudaStream_t stream) {
   using GQ = DqPass<HD>;
   using GK = DkvPass<HD>;
-  CUtensorMap mq[4], mk[4];
+  CUtensorMap mq[5], mk[4];
   bool ok = make_seq_map(&mq[0], p.q, HD, s.Tq, s.H, s.B, s.sq, kBM) &&
             make_seq_map(&mq[1], p.dO, HD, s.Tq, s.H, s.B, s.sq, kBM) &&
             make_seq_map(&mq[2], p.k, HD, s.Tk, s.Hk, s.B, s.sk, GQ::BN) &&
             make_seq_map(&mq[3], p.v, HD, s.Tk, s.Hk, s.B, s.sk, GQ::BN) &&
+            make_seq_map(&mq[4], p.o, HD, s.Tq, s.H, s.B, s.sq, kBM) &&
             make_seq_map(&mk[0], p.k, HD, s.Tk, s.Hk, s.B, s.sk, kBM) &&
             make_seq_map(&mk[1], p.v, HD, s.Tk, s.Hk, s.B, s.sk, kBM) &&
             make_seq_map(&mk[2], p.q, HD, s.Tq, s.H, s.B, s.sq, GK::BN) &&
@@ -440,15 +620,13 @@ int launch_bwd_hd(const AttnShape& s, const BwdPtrs& p, int* status, cudaStream_
   if (ensure_smem_limit(reinterpret_cast<const void*>(&bwd_dq_kernel<HD>), GQ::SMEM) != kOk ||
       ensure_smem_limit(reinterpret_cast<const void*>(&bwd_dkdv_kernel<HD>), GK::SMEM) != kOk)
     return kLaunchFailed;
-  int rc = launch_rowdot(s, HD, p.o, p.dO, p.delta, stream);
-  if (rc != kOk) return rc;
   BwdArgs args{s, p.lse, p.delta, static_cast<__nv_bfloat16*>(p.dq), static_cast<__nv_bfloat16*>(p.dk),
                static_cast<__nv_bfloat16*>(p.dv), status};
-  bwd_dq_kernel<HD><<<dim3(s.H, s.B, (s.Tq + kBM - 1) / kBM), kThreads, GQ::SMEM, stream>>>(mq[0], mq[1], mq[2],
-                                                                                          mq[3], args);
+  bwd_dq_kernel<HD><<<dim3(s.H, s.B, (s.Tq + kBM - 1) / kBM), kBBThreads, GQ::SMEM, stream>>>(mq[0], mq[1], mq[2],
+                                                                                             mq[3], mq[4], args);
   if (after_launch() != kOk) return kLaunchFailed;
-  bwd_dkdv_kernel<HD><<<dim3(s.Hk, s.B, (s.Tk + kBM - 1) / kBM), kThreads, GK::SMEM, stream>>>(mk[0], mk[1], mk[2],
-                                                                                            mk[3], args);
+  bwd_dkdv_kernel<HD><<<dim3(s.Hk, s.B, (s.Tk + kBM - 1) / kBM), kBBThreads, GK::SMEM, stream>>>(mk[0], mk[1], mk[2],
+                                                                                               mk[3], args);
   return after_launch();
 }
 

@@ -77,31 +77,6 @@ struct QPass {
   static_assert(CW % 16 == 0 && HD % 64 == 0, "tile shapes");
 };
 
-// Partial rowsum(dO o) over head_dim columns [HD/2 wg, HD/2 wg + HD/2) of row r of two
-// resident 128-row tiles (128B-swizzled 64-column panels, as loaded by TMA).
-template <int HD>
-__device__ __forceinline__ float rowdot_share(const uint8_t* s_o, const uint8_t* s_do, int r, int wg) {
-  float acc = 0.f;
-#pragma unroll
-  for (int c = 0; c < HD / 16; ++c) {  // 16-byte chunks: HD/8 per row, half of them per warpgroup
-    const int chunk = wg * (HD / 16) + c;
-    const int panel = chunk >> 3;
-    const uint32_t off = panel * kBM * 128 + sw128_offset(r, chunk & 7);
-    const uint4 x = *reinterpret_cast<const uint4*>(s_o + off);
-    const uint4 y = *reinterpret_cast<const uint4*>(s_do + off);
-    const __nv_bfloat162* xa = reinterpret_cast<const __nv_bfloat162*>(&x);
-    const __nv_bfloat162* ya = reinterpret_cast<const __nv_bfloat162*>(&y);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float2 xf = __bfloat1622float2(xa[i]);
-      const float2 yf = __bfloat1622float2(ya[i]);
-      acc = fmaf(xf.x, yf.x, acc);
-      acc = fmaf(xf.y, yf.y, acc);
-    }
-  }
-  return acc;
-}
-
 // Stats sweep: row partial sums over this thread's CW columns. dD and r3 are
 // accumulated without the softmax scale of ddS (applied once per row after the
 // sweep): dD/scale += P ddS', r1 += P dPa, r2 += P dP, r3/scale += P ddS' dP.

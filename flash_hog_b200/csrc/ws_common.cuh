@@ -77,6 +77,55 @@ __device__ __forceinline__ void store_bias_row(uint32_t tile, int r, float x) {
   st_shared_v4(tile + sw32_offset(r, 1), 0u, 0u, 0u, 0u);
 }
 
+// Partial rowsum(dO o) over head_dim columns [HD/2 wg, HD/2 wg + HD/2) of row r of two
+// resident 128-row tiles (128B-swizzled 64-column panels, as loaded by TMA).
+template <int HD>
+__device__ __forceinline__ float rowdot_share(const uint8_t* s_o, const uint8_t* s_do, int r, int wg) {
+  float acc = 0.f;
+#pragma unroll
+  for (int c = 0; c < HD / 16; ++c) {  // 16-byte chunks: HD/8 per row, half of them per warpgroup
+    const int chunk = wg * (HD / 16) + c;
+    const int panel = chunk >> 3;
+    const uint32_t off = panel * kBM * 128 + sw128_offset(r, chunk & 7);
+    const uint4 x = *reinterpret_cast<const uint4*>(s_o + off);
+    const uint4 y = *reinterpret_cast<const uint4*>(s_do + off);
+    const __nv_bfloat162* xa = reinterpret_cast<const __nv_bfloat162*>(&x);
+    const __nv_bfloat162* ya = reinterpret_cast<const __nv_bfloat162*>(&y);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 xf = __bfloat1622float2(xa[i]);
+      const float2 yf = __bfloat1622float2(ya[i]);
+      acc = fmaf(xf.x, yf.x, acc);
+      acc = fmaf(xf.y, yf.y, acc);
+    }
+  }
+  return acc;
+}
+
+// Copies bf16 columns [c0, c0 + NC) of row r of a resident 128-row tile
+// (128B-swizzled 64-column panels, as loaded by TMA) into this thread's TMEM
+// lane as packed pairs -- the layout of a TMEM A operand: column j holds
+// elements 2j (low half) and 2j + 1 -- starting at TMEM address `t` + c0/2.
+template <int NC>
+__device__ __forceinline__ void row_to_tmem(const uint8_t* tile, int r, int c0, uint32_t t) {
+  static_assert(NC % 32 == 0, "whole x16 stores");
+#pragma unroll
+  for (int c = 0; c < NC; c += 32) {
+    uint32_t v[16];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int chunk = (c0 + c) / 8 + k;  // 16-byte chunk of the row
+      const uint4 x =
+          *reinterpret_cast<const uint4*>(tile + (chunk >> 3) * kBM * 128 + sw128_offset(r, chunk & 7));
+      v[4 * k] = x.x;
+      v[4 * k + 1] = x.y;
+      v[4 * k + 2] = x.z;
+      v[4 * k + 3] = x.w;
+    }
+    tmem_st16(t + (c0 + c) / 2, v);
+  }
+}
+
 // The j-th item of persistent CTA c out of P: a "snake" over the heaviest-first
 // order (c, then 2P-1-c, ...), which balances the causal work to within a few
 // percent without a global counter.
