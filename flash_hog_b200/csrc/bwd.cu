@@ -48,24 +48,23 @@ template <int HD>
 struct DqPass {
   static constexpr int BN = 64;  // keys per streamed tile
   static constexpr int ST = 4;   // ring depth
-  static constexpr int CW = BN / 2;
   static constexpr int RES = kBM * HD * 2;
   static constexpr int RES_PANEL = kBM * 128;
   static constexpr int STR = BN * HD * 2;
   static constexpr int STR_PANEL = BN * 128;
   static constexpr int SLOT = 2 * STR;                     // K, V
   static constexpr int SMEM = 1024 + 2 * RES + ST * SLOT;  // Q, dO, ring (O borrows the last slot)
-  // TMEM: two score buffers [S | dP], the dQ accumulator, the bf16 dS operand
-  // (BN/2 packed columns), then Q -- and dO at head_dim 64, where it fits --
-  // as packed bf16 A operands of the score MMAs.
+  // TMEM: one score buffer [S | dP] and one bf16 dS operand (BN/2 packed
+  // columns) per elementwise warpgroup, the dQ accumulator, then Q -- and dO at
+  // head_dim 64, where it fits -- as packed bf16 A operands of the score MMAs.
   static constexpr bool DO_TMEM = HD == 64;
-  static constexpr int C_S = 0, C_DP = BN, SCORE_COLS = 2 * BN;
-  static constexpr int C_DQ = 2 * SCORE_COLS, C_OPS = C_DQ + HD, C_QT = C_OPS + BN / 2, C_DOT = C_QT + HD / 2;
+  static constexpr int C_S = 0, C_DP = BN, SCORE_COLS = 2 * BN, OPS_COLS = BN / 2;
+  static constexpr int C_DQ = 2 * SCORE_COLS, C_OPS = C_DQ + HD, C_QT = C_OPS + 2 * OPS_COLS, C_DOT = C_QT + HD / 2;
   static constexpr int TMEM_COLS = 512;
   static_assert(C_DOT + (DO_TMEM ? HD / 2 : 0) <= TMEM_COLS, "TMEM budget");
   static_assert(RES <= SLOT, "O fits in one ring slot");
   static_assert(SMEM <= 232448, "shared memory budget");
-  static_assert(CW % 16 == 0 && HD % 64 == 0, "tile shapes");
+  static_assert(HD % 64 == 0, "tile shapes");
 };
 
 // Packed bf16 pairs of dS/scale = P (dP - D) for this thread's CW key columns.
@@ -92,7 +91,7 @@ __global__ void __launch_bounds__(kBBThreads, 1)
                   const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                   const __grid_constant__ CUtensorMap tm_o, const BwdArgs a) {
   using G = DqPass<HD>;
-  constexpr int BN = G::BN, ST = G::ST, CW = G::CW;
+  constexpr int BN = G::BN, ST = G::ST;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = align1024(smem_raw);
   uint8_t* s_q = sm;
@@ -102,7 +101,10 @@ __global__ void __launch_bounds__(kBBThreads, 1)
   // use; the producer refills it only once every elementwise warp has read O.
   uint8_t* s_o = s_ring + (ST - 1) * G::SLOT;
   __shared__ uint64_t bar_res, bar_tres, bar_ofree, bar_dred, bar_full[ST], bar_empty[ST];
-  __shared__ uint64_t bar_sc_full[2], bar_sc_empty[2], bar_ops_full, bar_ops_empty, bar_acc;
+  // Score buffer and dS operand w belong to elementwise warpgroup w, which
+  // takes key tiles w, w + 2, ...: the two warpgroups work on consecutive tiles
+  // independently, so one computes while the other waits for its scores.
+  __shared__ uint64_t bar_sc_full[2], bar_sc_empty[2], bar_ops_full[2], bar_ops_empty[2], bar_acc;
   __shared__ float dred[2][kBM];  // partial rowsum(dO o O): warpgroup, row
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
@@ -127,10 +129,10 @@ __global__ void __launch_bounds__(kBBThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bar_sc_full[i], 1);
-      mbar_init(&bar_sc_empty[i], kBBEwWarps);
+      mbar_init(&bar_sc_empty[i], kBBEwWarps / 2);
+      mbar_init(&bar_ops_full[i], kBBEwWarps / 2);
+      mbar_init(&bar_ops_empty[i], 1);
     }
-    mbar_init(&bar_ops_full, kBBEwWarps);
-    mbar_init(&bar_ops_empty, 1);
     mbar_init(&bar_acc, 1);
     mbar_fence_init();
   }
@@ -203,30 +205,30 @@ __global__ void __launch_bounds__(kBBThreads, 1)
     }
   } else if (warp == kBBWarpMmaOut) {
     // ----------------------------- operand MMA issuer -----------------------------
-    //   dQ/scale += dS K   (dS in TMEM, K MN-major in the ring)
+    //   dQ/scale += dS K   (dS in TMEM, K MN-major in the ring), tiles in order
     const uint32_t id_dq = idesc_bf16_f32(kBM, HD, false, true);
     const uint64_t mn_ring = mndesc(s_ring, G::STR_PANEL);
     constexpr uint64_t kSlot = G::SLOT >> 4;
     bool ok = true;
     for (int j = 0; j < n; ++j) {
-      if (!mbar_wait_warp(&bar_ops_full, j & 1, &abort_flag)) {
+      const int w = j & 1;
+      if (!mbar_wait_warp(&bar_ops_full[w], (j >> 1) & 1, &abort_flag)) {
         if (lane == 0) raise_error(a.status, &abort_flag, kDevTimeoutEpilogue);
         ok = false;
         break;
       }
       tc_fence_after();
       const int s = j % ST;
-      umma_chain_ts_w<BN / 16>(tmem + G::C_DQ, tmem + G::C_OPS, mn_ring + s * kSlot, id_dq, j > 0);
-      umma_commit_w(&bar_ops_empty);
+      umma_chain_ts_w<BN / 16>(tmem + G::C_DQ, tmem + G::C_OPS + w * G::OPS_COLS, mn_ring + s * kSlot, id_dq, j > 0);
+      umma_commit_w(&bar_ops_empty[w]);
       umma_commit_w(&bar_empty[s]);
     }
     if (ok) umma_commit_w(&bar_acc);
   } else {
     // --------------------------- elementwise warps ----------------------------
-    const int wg = (warp - kBBFirstEwWarp) >> 2;  // column half of every tile
+    const int wg = (warp - kBBFirstEwWarp) >> 2;  // takes key tiles wg, wg + 2, ...
     const int r = (warp & 3) * 32 + lane;         // TMEM lane = query row inside the tile
     const uint32_t lane_t = tmem + tmem_lane_base(warp & 3);
-    const int cb = wg * CW;
     const int row = q0 + r;
     const bool row_ok = row < sh.Tq;
     const size_t vi = stat_index(b, h, row_ok ? row : 0, sh.H, sh.Tq);
@@ -248,32 +250,34 @@ __global__ void __launch_bounds__(kBBThreads, 1)
       dv = dred[0][r] + dred[1][r];
       if (ok && wg == 0 && row_ok) a.delta[vi] = dv;
     }
-    for (int j = 0; ok && j < n; ++j) {
-      const int sb = j & 1;
-      ok = mbar_wait_warp(&bar_sc_full[sb], (j >> 1) & 1, &abort_flag);
+    const uint32_t tb = tmem + wg * G::SCORE_COLS;
+    const uint32_t to = lane_t + G::C_OPS + wg * G::OPS_COLS;
+    for (int j = wg; ok && j < n; j += 2) {
+      const int u = j >> 1;  // earlier tiles of this warpgroup
+      ok = mbar_wait_warp(&bar_sc_full[wg], u & 1, &abort_flag);
       if (!ok) break;
       tc_fence_after();
-      const uint32_t tb = tmem + sb * G::SCORE_COLS;
-      uint32_t vs[CW], vdp[CW];
-      tmem_share<CW>(tb, warp, G::C_S + cb, vs);
-      tmem_share<CW>(tb, warp, G::C_DP + cb, vdp);
+      uint32_t vs[BN], vdp[BN];
+      tmem_share<BN>(tb, warp, G::C_S, vs);
+      tmem_share<BN>(tb, warp, G::C_DP, vdp);
       tmem_wait_ld();
       reg_fence(vs);
       reg_fence(vdp);
-      warp_arrive(&bar_sc_empty[sb]);  // the tensor core may reuse this score buffer now
-      const int kc = j * BN + cb;      // first key of this thread's columns
-      const bool need_mask = (kc + CW > sh.Tk) || (sh.causal && kc + CW - 1 > row);
-      uint32_t o_ds[CW / 2];
+      warp_arrive(&bar_sc_empty[wg]);  // the tensor core may reuse this score buffer now
+      const int kc = j * BN;
+      const bool need_mask = (kc + BN > sh.Tk) || (sh.causal && kc + BN - 1 > row);
+      uint32_t o_ds[BN / 2];
       if (need_mask)
-        dq_ops<CW, true>(vs, vdp, kc, row, sh.Tk, sh.causal, sc2, lg, dv, o_ds);
+        dq_ops<BN, true>(vs, vdp, kc, row, sh.Tk, sh.causal, sc2, lg, dv, o_ds);
       else
-        dq_ops<CW, false>(vs, vdp, kc, row, sh.Tk, sh.causal, sc2, lg, dv, o_ds);
-      if (j > 0) ok = mbar_wait_warp(&bar_ops_empty, (j - 1) & 1, &abort_flag);
+        dq_ops<BN, false>(vs, vdp, kc, row, sh.Tk, sh.causal, sc2, lg, dv, o_ds);
+      if (u > 0) ok = mbar_wait_warp(&bar_ops_empty[wg], (u - 1) & 1, &abort_flag);
       if (!ok) break;
       tc_fence_after();
-      tmem_st_ops(lane_t + G::C_OPS + (CW / 2) * wg, o_ds);
+      tmem_st16(to, *reinterpret_cast<const uint32_t(*)[16]>(&o_ds[0]));
+      tmem_st16(to + 16, *reinterpret_cast<const uint32_t(*)[16]>(&o_ds[16]));
       tmem_wait_st();
-      warp_arrive(&bar_ops_full);
+      warp_arrive(&bar_ops_full[wg]);
     }
     if (ok) ok = mbar_wait_warp(&bar_acc, 0, &abort_flag);
     if (ok) {
