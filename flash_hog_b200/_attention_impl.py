@@ -97,6 +97,73 @@ def dot_product_attention_bwd_rule_fwd_rule(mask_type: MaskType, scale: float, r
     return grads, (query, key, value, out, activation, g)
 
 
+def _zeros_if_none(ts, like):
+    return tuple(torch.zeros_like(x) if t is None else t for t, x in zip(ts, like))
+
+
+def _require_plain(*ts) -> None:
+    """The forward-mode rules hand tensors to the C ABI by address. Under the
+    ``torch.func.jvp`` transform their saved tensors are functorch wrappers with
+    no storage, so that transform is refused with a clear message; forward mode
+    through ``torch.autograd.forward_ad`` (dual tensors) passes plain tensors."""
+    if any(t is not None and torch._C._functorch.is_functorch_wrapped_tensor(t) for t in ts):
+        raise NotImplementedError(
+            "flash_hog_b200 forward-mode rules run under torch.autograd.forward_ad (dual tensors), not under "
+            "the torch.func.jvp transform; torch.func.grad / vjp are supported")
+
+
+def dot_product_attention_fwd_jvp(mask_type: MaskType, scale: float, res, tangents):
+    """Forward-mode derivative of the forward: ``(t_out, t_activation)``.
+
+    No counterpart in the reference, which has reverse-mode rules only
+    (``flash_hog/jax/attention.py:52-60``). The tangents are the double
+    backward's query-pass outputs for dO = 0 and (ddQ, ddK, ddV) = (tQ, tK, tV):
+    with tS = scale (tQ K^T + Q tK^T) and tP = P o (tS - rowsum(P o tS)),
+    ddO = tP V + P tV = t_out and dD = rowsum(P o tS) = t_lse (the double
+    backward's formulas, ``flash_hog/_jax_refs/jax_impl.py:273-336``, at dO = 0).
+    """
+    query, key, value, activation, out = res
+    _require_plain(query, key, value, activation, out, *tangents)
+    tq, tk, tv = _zeros_if_none(tangents, (query, key, value))
+    q, k, v, o = _bf16(query), _bf16(key), _bf16(value), _bf16(out)
+    tq, tk, tv = _bf16(tq), _bf16(tk), _bf16(tv)
+    b, t, n, _ = q.shape
+    stats = torch.empty((3, b, n, t), dtype=torch.float32, device=q.device)
+    zero_do = torch.zeros_like(q)
+    dq2, t_out = torch.empty_like(q), torch.empty_like(q)
+    _capi.attn_bwdbwd_o(q, k, v, o, zero_do, tq, tk, tv, activation.float().contiguous(), dq2, t_out, None, None,
+                        stats[0], stats[1], stats[2], scale, _is_causal(mask_type), which=_capi.PASS_QUERY)
+    return t_out.to(out.dtype), stats[1].clone()
+
+
+def dot_product_attention_bwd_jvp(mask_type: MaskType, scale: float, res, g, tangents):
+    """Forward-mode derivative of the first-order backward: ``(tdQ, tdK, tdV)``.
+
+    ``res`` = (query, key, value, activation, out), ``g`` = dO, ``tangents`` =
+    (tQ, tK, tV, tdO) (None = zero). The backward is the gradient of
+    phi = <O, dO>, so its jvp is Hess(phi) (tQ, tK, tV) -- the double backward
+    with (ddQ, ddK, ddV) = (tQ, tK, tV), the Hessian being symmetric -- plus the
+    first-order backward of tdO (``fh_attn_jvp_bwd``). The tangents of the
+    residuals L and O are not used: they are functions of (Q, K, V), whose
+    tangents already carry them (the reference's bwd-of-bwd rule returns None
+    for them likewise, ``flash_hog/jax/_attention_impl.py:302-303``).
+    """
+    query, key, value, activation, out = res
+    _require_plain(query, key, value, activation, out, g, *tangents)
+    tq, tk, tv = _zeros_if_none(tangents[:3], (query, key, value))
+    tdo = tangents[3]
+    q, k, v, o, do = _bf16(query), _bf16(key), _bf16(value), _bf16(out), _bf16(g)
+    tq, tk, tv = _bf16(tq), _bf16(tk), _bf16(tv)
+    tdo = None if tdo is None else _bf16(tdo)
+    b, t, n, _ = q.shape
+    stats = torch.empty((3, b, n, t), dtype=torch.float32, device=q.device)
+    tdq, t_out = torch.empty_like(q), torch.empty_like(q)
+    tdk, tdv = torch.empty_like(k), torch.empty_like(v)
+    _capi.attn_jvp_bwd(q, k, v, o, do, activation.float().contiguous(), tq, tk, tv, tdo, tdq, tdk, tdv, t_out,
+                       stats[0], stats[1], stats[2], scale, _is_causal(mask_type))
+    return tdq.to(query.dtype), tdk.to(key.dtype), tdv.to(value.dtype)
+
+
 def dot_product_attention_bwd_rule_bwd_rule(mask_type: MaskType, scale: float, res, g):
     """Backward through the backward (``_attention_impl.py:278-303``).
 

@@ -39,13 +39,14 @@ EXPORTED_SYMBOLS = (
     "fh_attn_bwdbwd_pass",
     "fh_attn_bwdbwd_o",
     "fh_attn_bwdbwd_noalloc",
+    "fh_attn_jvp_bwd",
     "fh_device_status",
     "fh_status_string",
     "fh_last_error",
     "fh_abi_version",
     "fh_launch_count",
 )
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 
 class FlashHogError(RuntimeError):
@@ -94,6 +95,7 @@ def lib() -> ctypes.CDLL:
     h.fh_attn_bwdbwd_pass.argtypes = [vp, dims] + [vp] * 15 + [f32, i32, i32]
     h.fh_attn_bwdbwd_o.argtypes = [vp, dims] + [vp] * 16 + [f32, i32, i32]
     h.fh_attn_bwdbwd_noalloc.argtypes = [vp, dims] + [vp] * 13 + [f32, i32, vp]
+    h.fh_attn_jvp_bwd.argtypes = [vp, dims] + [vp] * 17 + [f32, i32]
     h.fh_device_status.argtypes = [vp, ctypes.POINTER(ctypes.c_int)]
     h.fh_status_string.argtypes = [i32]
     h.fh_status_string.restype = ctypes.c_char_p
@@ -103,7 +105,8 @@ def lib() -> ctypes.CDLL:
     h.fh_last_error.argtypes = []
     h.fh_last_error.restype = ctypes.c_char_p
     for name in ("fh_attn_fwd", "fh_attn_rowdot", "fh_attn_bwd", "fh_attn_bwdbwd", "fh_attn_bwdbwd_pass",
-                 "fh_attn_bwdbwd_o", "fh_attn_bwdbwd_noalloc", "fh_device_status", "fh_abi_version"):
+                 "fh_attn_bwdbwd_o", "fh_attn_bwdbwd_noalloc", "fh_attn_jvp_bwd", "fh_device_status",
+                 "fh_abi_version"):
         getattr(h, name).restype = i32
     if h.fh_abi_version() != ABI_VERSION:
         raise RuntimeError(f"flash_hog_b200 ABI mismatch: library {h.fh_abi_version()}, binding {ABI_VERSION}")
@@ -147,7 +150,11 @@ def make_dims(q: torch.Tensor, k: torch.Tensor) -> FhAttnDims:
 
 
 def _same_layout(ref: torch.Tensor, *others: torch.Tensor) -> None:
+    """Checks shape, strides, dtype and device against ``ref`` (None entries,
+    unused outputs, are skipped)."""
     for t in others:
+        if t is None:
+            continue
         if _layout_key(t) != _layout_key(ref):
             raise ValueError("tensors of one side must share shape and strides")
         if t.dtype != torch.bfloat16 or t.device != ref.device:
@@ -214,6 +221,18 @@ def attn_bwdbwd_o(q, k, v, o, dO, ddq, ddk, ddv, lse, dq2, ddo, dk2, dv2, delta,
         _stream(q.device), ctypes.byref(dims), _ptr(q), _ptr(k), _ptr(v), _ptr(o), _ptr(dO), _ptr(ddq),
         _ptr(ddk), _ptr(ddv), _ptr(lse), _ptr(dq2), _ptr(ddo), _ptr(dk2), _ptr(dv2), _ptr(delta), _ptr(dd),
         _ptr(bvec), float(scale), int(causal), int(which)))
+
+
+def attn_jvp_bwd(q, k, v, o, dO, lse, tq, tk, tv, tdO, tdq, tdk, tdv, to, delta, dd, bvec, scale: float,
+                 causal: bool) -> None:
+    """Forward-mode derivative of the first-order backward (``tdO`` may be None)."""
+    _same_layout(q, o, dO, tq, tdq, to, tdO)
+    _same_layout(k, v, tk, tv, tdk, tdv)
+    dims = make_dims(q, k)
+    _check("fh_attn_jvp_bwd", lib().fh_attn_jvp_bwd(
+        _stream(q.device), ctypes.byref(dims), _ptr(q), _ptr(k), _ptr(v), _ptr(o), _ptr(dO), _ptr(lse), _ptr(tq),
+        _ptr(tk), _ptr(tv), _ptr(tdO), _ptr(tdq), _ptr(tdk), _ptr(tdv), _ptr(to),
+        _ptr(delta), _ptr(dd), _ptr(bvec), float(scale), int(causal)))
 
 
 def launch_count() -> int:

@@ -15,6 +15,13 @@ here the same nesting is two ``torch.autograd.Function``s:
 So ``torch.autograd.grad(..., create_graph=True)`` followed by a second
 ``grad`` (grad-of-grad, Hessian-vector products) runs fwd -> bwd -> bwdbwd on
 the sm_100a kernels, as nested ``jax.grad`` does in the reference.
+
+Beyond the reference, both Functions also have forward-mode (``jvp``) rules
+and the ``setup_context`` form, so ``torch.func`` transforms compose over them:
+``torch.func.jvp(torch.func.grad(f), primals, tangents)`` -- forward-over-reverse
+Hessian-vector products -- runs fwd, bwd, the forward jvp (the double
+backward's query pass at dO = 0) and the backward's jvp (double backward plus
+first-order backward, ``fh_attn_jvp_bwd``) on the kernels.
 """
 
 from __future__ import annotations
@@ -39,36 +46,59 @@ def dot_product_attention(query, key, value, is_causal: bool = False, scale: flo
     unbatched = query.ndim == 3
     if unbatched:
         query, key, value = query.unsqueeze(0), key.unsqueeze(0), value.unsqueeze(0)
-    result = _DotProductAttention.apply(query, key, value, mask_type, float(scale))
+    result, _ = _DotProductAttention.apply(query, key, value, mask_type, float(scale))
     if unbatched:
         result = result.squeeze(0)
     return result
 
 
 class _DotProductAttention(torch.autograd.Function):
-    @staticmethod
-    def forward(ctx, query, key, value, mask_type, scale):
-        out, activation = attn_impl.cuda_dot_product_attention(query, key, value, mask_type=mask_type, scale=scale,
-                                                               return_residual=True)
-        ctx.save_for_backward(query, key, value, activation, out)
-        ctx.mask_type, ctx.scale = mask_type, scale
-        return out
+    """Forward (outputs O and the log-sum-exp L, the latter non-differentiable)."""
 
     @staticmethod
-    def backward(ctx, g):
+    def forward(query, key, value, mask_type, scale):
+        return attn_impl.cuda_dot_product_attention(query, key, value, mask_type=mask_type, scale=scale,
+                                                    return_residual=True)
+
+    @staticmethod
+    def setup_context(ctx, inputs, output):
+        query, key, value, mask_type, scale = inputs
+        out, activation = output
+        ctx.mark_non_differentiable(activation)
+        ctx.save_for_backward(query, key, value, activation, out)
+        ctx.save_for_forward(query, key, value, activation, out)
+        ctx.mask_type, ctx.scale = mask_type, scale
+
+    @staticmethod
+    def backward(ctx, g, _g_activation):
         query, key, value, activation, out = ctx.saved_tensors
         dq, dk, dv = _DotProductAttentionBwd.apply(query, key, value, activation, out, g, ctx.mask_type, ctx.scale)
         return dq, dk, dv, None, None
 
+    @staticmethod
+    def jvp(ctx, tq, tk, tv, _t_mask, _t_scale):
+        res = ctx.saved_tensors
+        t_out, _ = attn_impl.dot_product_attention_fwd_jvp(ctx.mask_type, ctx.scale, res, (tq, tk, tv))
+        return t_out, None
+
 
 class _DotProductAttentionBwd(torch.autograd.Function):
+    """First-order backward (dQ, dK, dV); reverse mode gives the double backward,
+    forward mode its jvp."""
+
     @staticmethod
-    def forward(ctx, query, key, value, activation, out, g, mask_type, scale):
-        (dq, dk, dv), residual = attn_impl.dot_product_attention_bwd_rule_fwd_rule(
+    def forward(query, key, value, activation, out, g, mask_type, scale):
+        (dq, dk, dv), _ = attn_impl.dot_product_attention_bwd_rule_fwd_rule(
             mask_type=mask_type, scale=scale, res=(query, key, value, activation, out), g=g)
-        ctx.save_for_backward(*residual)
-        ctx.mask_type, ctx.scale = mask_type, scale
         return dq, dk, dv
+
+    @staticmethod
+    def setup_context(ctx, inputs, output):
+        query, key, value, activation, out, g, mask_type, scale = inputs
+        # The residual order of the reference's bwd-of-bwd rule (_attention_impl.py:264-275).
+        ctx.save_for_backward(query, key, value, out, activation, g)
+        ctx.save_for_forward(query, key, value, activation, out, g)
+        ctx.mask_type, ctx.scale = mask_type, scale
 
     @staticmethod
     def backward(ctx, ddq, ddk, ddv):
@@ -77,3 +107,9 @@ class _DotProductAttentionBwd(torch.autograd.Function):
         (dq2, dk2, dv2, _, _), ddo = attn_impl.dot_product_attention_bwd_rule_bwd_rule(
             mask_type=ctx.mask_type, scale=ctx.scale, res=res, g=tuple(zeros))
         return dq2, dk2, dv2, None, None, ddo, None, None
+
+    @staticmethod
+    def jvp(ctx, tq, tk, tv, _t_activation, _t_out, tg, _t_mask, _t_scale):
+        query, key, value, activation, out, g = ctx.saved_tensors
+        return attn_impl.dot_product_attention_bwd_jvp(ctx.mask_type, ctx.scale, (query, key, value, activation, out),
+                                                      g, (tq, tk, tv, tg))

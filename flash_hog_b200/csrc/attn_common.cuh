@@ -232,10 +232,11 @@ __device__ __forceinline__ void stage_bf16x16(uint8_t* panel, int r, int c16, co
 }
 
 // Drains the TMEM accumulator columns [col, col+HD) of this thread's lane,
-// times `mult`, to a bf16 row in global memory.
+// times `mult`, plus the bf16 row `add` when it is not null (it may alias
+// `dst`: each element is read before it is written), to a bf16 row in global memory.
 template <int HD>
 __device__ __forceinline__ void tmem_row_to_global(uint32_t tmem, int warp, int col, __nv_bfloat16* dst,
-                                                   bool write, float mult = 1.f) {
+                                                   bool write, float mult = 1.f, const __nv_bfloat16* add = nullptr) {
 #pragma unroll
   for (int c = 0; c < HD; c += 16) {
     uint32_t r[16];
@@ -245,6 +246,18 @@ __device__ __forceinline__ void tmem_row_to_global(uint32_t tmem, int warp, int 
     float v[16];
 #pragma unroll
     for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]) * mult;
+    if (write && add) {
+      uint4 a[2];
+      a[0] = reinterpret_cast<const uint4*>(add + c)[0];
+      a[1] = reinterpret_cast<const uint4*>(add + c)[1];
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(a);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float2 f = __bfloat1622float2(h[i]);
+        v[2 * i] += f.x;
+        v[2 * i + 1] += f.y;
+      }
+    }
     if (write) store_bf16x16(dst + c, v);
   }
 }

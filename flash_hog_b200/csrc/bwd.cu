@@ -37,6 +37,9 @@ struct BwdArgs {
   __nv_bfloat16* dq;
   __nv_bfloat16* dk;
   __nv_bfloat16* dv;
+  const __nv_bfloat16* dq_acc;  // optional addends of dq, dk, dv (may alias them)
+  const __nv_bfloat16* dk_acc;
+  const __nv_bfloat16* dv_acc;
   int* status;
 };
 
@@ -283,8 +286,9 @@ __global__ void __launch_bounds__(kBBThreads, 1)
     if (ok) {
       tc_fence_after();
       const int srow = row_ok ? row : 0;
-      tmem_row_to_global<HD / 2>(tmem, warp, G::C_DQ + wg * (HD / 2),
-                                 a.dq + row_offset(sh.sq, b, srow, h) + wg * (HD / 2), row_ok, sh.scale);
+      const size_t off = row_offset(sh.sq, b, srow, h) + wg * (HD / 2);
+      tmem_row_to_global<HD / 2>(tmem, warp, G::C_DQ + wg * (HD / 2), a.dq + off, row_ok, sh.scale,
+                                 a.dq_acc ? a.dq_acc + off : nullptr);
     } else if (threadIdx.x == kBBFirstEwWarp * 32) {
       raise_error(a.status, &abort_flag, kDevTimeoutMma);
     }
@@ -416,7 +420,17 @@ __global__ void __launch_bounds__(kBBThreads, 1)
     if (warp >= kBBFirstEwWarp) {
       const int wg = (warp - kBBFirstEwWarp) >> 2;
       const int key = k0 + (warp & 3) * 32 + lane;
-      if (key < sh.Tk) zero_row_global<HD>((wg == 0 ? a.dk : a.dv) + row_offset(sh.sk, b, key, hk));
+      const size_t off = row_offset(sh.sk, b, key < sh.Tk ? key : 0, hk);
+      const __nv_bfloat16* add = wg == 0 ? a.dk_acc : a.dv_acc;
+      __nv_bfloat16* dst = (wg == 0 ? a.dk : a.dv) + off;
+      if (key < sh.Tk) {
+        if (add) {  // the outputs are the addends
+          for (int c = 0; c < HD; c += 8)
+            reinterpret_cast<uint4*>(dst + c)[0] = reinterpret_cast<const uint4*>(add + off + c)[0];
+        } else {
+          zero_row_global<HD>(dst);
+        }
+      }
     }
   } else if (warp == kBBWarpProducer) {
     // ---------------------- TMA producer (whole warp) -----------------------
@@ -594,8 +608,10 @@ __global__ void __launch_bounds__(kBBThreads, 1)
     if (ok) ok = mbar_wait_warp(&bar_acc, 0, &abort_flag);
     if (ok) {
       tc_fence_after();
-      __nv_bfloat16* dst = (wg == 0 ? a.dk : a.dv) + row_offset(sh.sk, b, key_ok ? key : 0, hk);
-      tmem_row_to_global<HD>(tmem, warp, wg == 0 ? G::C_DK : G::C_DV, dst, key_ok, wg == 0 ? sh.scale : 1.f);
+      const size_t off = row_offset(sh.sk, b, key_ok ? key : 0, hk);
+      const __nv_bfloat16* add = wg == 0 ? a.dk_acc : a.dv_acc;
+      tmem_row_to_global<HD>(tmem, warp, wg == 0 ? G::C_DK : G::C_DV, (wg == 0 ? a.dk : a.dv) + off, key_ok,
+                             wg == 0 ? sh.scale : 1.f, add ? add + off : nullptr);
     } else if (threadIdx.x == kBBFirstEwWarp * 32) {
       raise_error(a.status, &abort_flag, kDevTimeoutMma);
     }
@@ -624,8 +640,16 @@ int launch_bwd_hd(const AttnShape& s, const BwdPtrs& p, int* status, cudaStream_
   if (ensure_smem_limit(reinterpret_cast<const void*>(&bwd_dq_kernel<HD>), GQ::SMEM) != kOk ||
       ensure_smem_limit(reinterpret_cast<const void*>(&bwd_dkdv_kernel<HD>), GK::SMEM) != kOk)
     return kLaunchFailed;
-  BwdArgs args{s, p.lse, p.delta, static_cast<__nv_bfloat16*>(p.dq), static_cast<__nv_bfloat16*>(p.dk),
-               static_cast<__nv_bfloat16*>(p.dv), status};
+  BwdArgs args{s,
+               p.lse,
+               p.delta,
+               static_cast<__nv_bfloat16*>(p.dq),
+               static_cast<__nv_bfloat16*>(p.dk),
+               static_cast<__nv_bfloat16*>(p.dv),
+               static_cast<const __nv_bfloat16*>(p.dq_acc),
+               static_cast<const __nv_bfloat16*>(p.dk_acc),
+               static_cast<const __nv_bfloat16*>(p.dv_acc),
+               status};
   bwd_dq_kernel<HD><<<dim3(s.H, s.B, (s.Tq + kBM - 1) / kBM), kBBThreads, GQ::SMEM, stream>>>(mq[0], mq[1], mq[2],
                                                                                              mq[3], mq[4], args);
   if (after_launch() != kOk) return kLaunchFailed;

@@ -297,6 +297,34 @@ int fh_attn_bwdbwd_o(void* stream, const fh_attn_dims* dims, const void* q, cons
                       dk2, dv2, dd, bvec, scale, causal, passes);
 }
 
+int fh_attn_jvp_bwd(void* stream, const fh_attn_dims* dims, const void* q, const void* k, const void* v,
+                    const void* o, const void* dO, const float* lse, const void* tq, const void* tk, const void* tv,
+                    const void* tdO, void* tdq, void* tdk, void* tdv, void* to, float* delta, float* dd, float* bvec,
+                    float scale, int causal) {
+  if (injected("fh_attn_jvp_bwd")) return FH_ERR_INJECTED;
+  AttnShape s;
+  int rc = validate(dims, &s, scale, causal);
+  if (rc != kOk) return rc;
+  if (!all_aligned(q, k, v, o, dO, tq, tk, tv, tdq, tdk, tdv, to) || !lse || !delta || !dd || !bvec)
+    return fail(FH_ERR_INVALID_ARGUMENT, kAlignMsg);
+  if (tdO && !all_aligned(tdO)) return fail(FH_ERR_INVALID_ARGUMENT, kAlignMsg);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if ((rc = select_stream_device(st)) != kOk) return rc;
+  int* status = status_word();
+  if (!status) return FH_ERR_NO_DEVICE;
+  // Hessian term: the double backward with (ddq, ddk, ddv) = (tq, tk, tv).
+  rc = launch_bwdbwd(s, dims->head_dim,
+                     BwdBwdPtrs{q, k, v, dO, tq, tk, tv, lse, nullptr, tdq, to, tdk, tdv, dd, bvec, o, delta},
+                     kPassQuery | kPassKey, status, st);
+  if (rc != kOk || !tdO) return rc;
+  // Plus the first-order backward of the cotangent tangent tdO, added in place.
+  BwdPtrs p{q, k, v, o, tdO, lse, tdq, tdk, tdv, delta};
+  p.dq_acc = tdq;
+  p.dk_acc = tdk;
+  p.dv_acc = tdv;
+  return launch_bwd(s, dims->head_dim, p, status, st);
+}
+
 int fh_device_status(void* stream, int* code) {
   if (!code) return FH_ERR_INVALID_ARGUMENT;
   *code = 0;

@@ -30,6 +30,12 @@ struct BwdPtrs {
   const float* lse;
   void *dq, *dk, *dv;
   float* delta;  // scratch: rowsum(dO * O), written by the first kernel
+  // Optional addends (same layout as dq, dk, dv; may alias them): the outputs
+  // become dq_acc + dQ, ... -- how the forward-mode derivative of the backward
+  // adds its first-order term to the double-backward term.
+  const void* dq_acc = nullptr;
+  const void* dk_acc = nullptr;
+  const void* dv_acc = nullptr;
 };
 
 struct BwdBwdPtrs {

@@ -135,11 +135,34 @@ int fh_attn_bwdbwd_pass(void* stream, const fh_attn_dims* dims, const void* q, c
  * computes D with an XLA einsum at _tk_gpu.py:93 before calling TkBwdBwd;
  * the Pallas rule does the same at _pallas_gpu_kernel.py:110).
  * `passes`: FH_PASS_QUERY, FH_PASS_KEY (after a query pass on the same
- * buffers) or both (3). */
+ * buffers) or both (3).
+ * Forward tangent: with dO = 0 (a zero-filled buffer) and (ddq, ddk, ddv) =
+ * (tq, tk, tv), the query pass alone writes the jvp of the forward, to = d O
+ * into `ddo` and tlse = d lse into `dd` (dq2 is then zero). */
 int fh_attn_bwdbwd_o(void* stream, const fh_attn_dims* dims, const void* q, const void* k, const void* v,
                      const void* o, const void* dO, const void* ddq, const void* ddk, const void* ddv,
                      const float* lse, void* dq2, void* ddo, void* dk2, void* dv2, float* delta, float* dd,
                      float* bvec, float scale, int causal, int passes);
+
+/* Forward-mode derivative (jvp) of the first-order backward. No counterpart in
+ * the reference, which differentiates the backward in reverse mode only
+ * (flash_hog/jax/attention.py:100-130); this is the forward-over-reverse path
+ * of Hessian-vector products. The backward (dq, dk, dv) = grad_{q,k,v} <O, dO>
+ * is the gradient of phi = <O(q, k, v), dO>, so its jvp with tangents
+ * (tq, tk, tv, tdO) is
+ *   (tdq, tdk, tdv) = Hess(phi) (tq, tk, tv) + J_O^T tdO:
+ * the double backward with (ddq, ddk, ddv) = (tq, tk, tv) (a Hessian is
+ * symmetric, so its vjp is its jvp) plus the first-order backward of tdO, whose
+ * kernels add their results in place. The double backward's ddO output is the
+ * forward tangent of the attention output, returned in `to`.
+ *  - Inputs as for fh_attn_bwdbwd_o (q, k, v, o, dO, lse) plus the tangents
+ *    tq (query side), tk, tv (key side) and tdO (query side; NULL = zero).
+ *  - Outputs tdq, tdk, tdv, to. Scratch delta, dd, bvec: batch*heads*seq_q floats each.
+ *  - Two kernel launches, four with tdO. */
+int fh_attn_jvp_bwd(void* stream, const fh_attn_dims* dims, const void* q, const void* k, const void* v,
+                    const void* o, const void* dO, const float* lse, const void* tq, const void* tk, const void* tv,
+                    const void* tdO, void* tdq, void* tdk, void* tdv, void* to, float* delta, float* dd, float* bvec,
+                    float scale, int causal);
 
 /* Allocation-free double backward. No counterpart in the reference: it exists
  * for callers that cannot allocate device memory while they run -- an XLA FFI
@@ -190,7 +213,7 @@ int fh_abi_version(void);
  * reads it before and after a timed region to report its kernel launches. */
 unsigned long long fh_launch_count(void);
 
-#define FH_ABI_VERSION 2
+#define FH_ABI_VERSION 3
 
 #ifdef __cplusplus
 }

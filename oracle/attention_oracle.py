@@ -356,6 +356,71 @@ def autograd_all(q, k, v, do, ddq, ddk, ddv, scale=None, causal=False):
 
 
 # --------------------------------------------------------------------------------------
+# forward mode: jvp of the forward and of the first-order backward
+# --------------------------------------------------------------------------------------
+
+def jvp_fwd(q, k, v, o, lse, tq, tk, tv, scale=None, causal=False):
+    """Forward tangents (tO, tL) of (O, L) along (tQ, tK, tV), in float64.
+
+    No counterpart in the reference (reverse-mode rules only,
+    ``flash_hog/jax/attention.py:52-60``). With tS = scale (tQ K^T + Q tK^T):
+    tL = rowsum(P o tS), tP = P o (tS - tL), tO = tP V + P tV -- the ddO and dD
+    of ``bwdbwd_stats`` with (ddQ, ddK, ddV) = (tQ, tK, tV), which do not
+    depend on dO.
+    """
+    zero = np.zeros_like(np.asarray(q, np.float64))
+    (_, _, _, to), (_, tl, _) = bwdbwd_stats(q, k, v, o, lse, zero, tq, tk, tv, scale=scale, causal=causal,
+                                              return_stats=True)
+    return to, tl
+
+
+def jvp_bwd(q, k, v, o, lse, do, tq, tk, tv, tdo=None, scale=None, causal=False):
+    """Forward-mode derivative (tdQ, tdK, tdV) of the first-order backward, float64.
+
+    The backward is grad_{Q,K,V} phi with phi = <O(Q, K, V), dO>, so
+        jvp(tQ, tK, tV, tdO) = Hess(phi) (tQ, tK, tV) + J_O^T tdO,
+    and Hess(phi) being symmetric, its product with the tangent is the double
+    backward (``bwdbwd_stats``) with (ddQ, ddK, ddV) = (tQ, tK, tV); J_O^T tdO
+    is the first-order backward (``attention_bwd``) of tdO.
+    """
+    dq2, dk2, dv2, _ = bwdbwd_stats(q, k, v, o, lse, do, tq, tk, tv, scale=scale, causal=causal)
+    if tdo is None:
+        return dq2, dk2, dv2
+    dq, dk, dv = attention_bwd(q, k, v, o, lse, tdo, scale=scale, causal=causal)
+    return dq2 + dq, dk2 + dk, dv2 + dv
+
+
+def autograd_jvp(q, k, v, do, tq, tk, tv, tdo, scale=None, causal=False):
+    """Forward-over-reverse derivatives of naive softmax attention by ``torch.func``
+    (an independent statement of ``jvp_fwd`` / ``jvp_bwd``): returns
+    ``dict(o, to, tlse, dq, dk, dv, tdq, tdk, tdv)`` for torch inputs (BTNH)."""
+    import torch.func as tf
+
+    scale = default_scale(q.shape[-1]) if scale is None else scale
+
+    def attn(q_, k_, v_):
+        return _torch_attention(q_, k_, v_, scale, causal)
+
+    def lse_fn(q_, k_):
+        group = q_.shape[2] // k_.shape[2]
+        kk = k_.repeat_interleave(group, dim=2) if group > 1 else k_
+        s = torch.einsum("bqhd,bkhd->bhqk", q_, kk) * scale
+        if causal:
+            keep = torch.ones(q_.shape[1], kk.shape[1], dtype=torch.bool).tril()
+            s = s.masked_fill(~keep, float("-inf"))
+        return torch.logsumexp(s, dim=-1)
+
+    def bwd(q_, k_, v_, do_):
+        _, vjp = tf.vjp(attn, q_, k_, v_)
+        return vjp(do_)
+
+    o, to = tf.jvp(attn, (q, k, v), (tq, tk, tv))
+    _, tlse = tf.jvp(lse_fn, (q, k), (tq, tk))
+    (dq, dk, dv), (tdq, tdk, tdv) = tf.jvp(bwd, (q, k, v, do), (tq, tk, tv, tdo))
+    return dict(o=o, to=to, tlse=tlse, dq=dq, dk=dk, dv=dv, tdq=tdq, tdk=tdk, tdv=tdv)
+
+
+# --------------------------------------------------------------------------------------
 # seeded inputs and credited work
 # --------------------------------------------------------------------------------------
 

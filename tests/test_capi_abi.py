@@ -37,6 +37,26 @@ def test_library_exports_every_declared_symbol():
     assert h.fh_status_string(5) == b"injected error"
 
 
+def _arities():
+    """Parameter count of every function the header declares."""
+    text = re.sub(r"/\*.*?\*/", "", open(HEADER).read(), flags=re.S)
+    out = {}
+    for name, params in re.findall(r"(fh_\w+)\s*\(([^)]*)\)\s*;", text):
+        params = params.strip()
+        out[name] = 0 if params in ("", "void") else params.count(",") + 1
+    return out
+
+
+def test_binding_argtypes_match_the_header():
+    from flash_hog_b200 import _capi
+
+    h = _capi.lib()
+    arities = _arities()
+    assert sorted(arities) == sorted(_capi.EXPORTED_SYMBOLS)
+    for name, n in arities.items():
+        assert len(getattr(h, name).argtypes) == n, f"{name}: binding has {len(getattr(h, name).argtypes)}, header {n}"
+
+
 def _dims(**kw):
     from flash_hog_b200._capi import FhAttnDims, FhStrides
 
