@@ -67,7 +67,7 @@ struct DqPass {
   static_assert(C_DOT + (DO_TMEM ? HD / 2 : 0) <= TMEM_COLS, "TMEM budget");
   static_assert(RES <= SLOT, "O fits in one ring slot");
   static_assert(SMEM <= 232448, "shared memory budget");
-  static_assert(HD % 64 == 0, "tile shapes");
+  static_assert(HD % 64 == 0 && RES_PANEL == kBM * 128, "tile shapes");
 };
 
 // Packed bf16 pairs of dS/scale = P (dP - D) for this thread's CW key columns.
@@ -333,7 +333,7 @@ struct DkvPass {
   static_assert(C_DP == C_S + BN, "one bias MMA covers both products");
   static_assert(SLOT % 1024 == 0 && (2 * RES + ONES) % 1024 == 0, "slots must keep panels 1024-byte aligned");
   static_assert(SMEM <= 232448, "shared memory budget");
-  static_assert(CW % 16 == 0 && HD % 64 == 0, "tile shapes");
+  static_assert(CW % 16 == 0 && HD % 64 == 0 && RES_PANEL == kBM * 128, "tile shapes");
 };
 
 // Packed bf16 pairs of P^T and dS^T/scale = P^T (dP^T - D) for this thread's CW

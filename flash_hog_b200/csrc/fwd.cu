@@ -2,20 +2,22 @@
 // natural-log log-sum-exp L, the residuals the reference's forward rule saves
 // (flash_hog/jax/_attention_impl.py:224-239 -- there produced by cuDNN).
 //
-// One CTA per 128 query rows of one (batch, head); key/value tiles of 128 rows
-// stream through a TMA ring. Warp 0 allocates TMEM and issues every MMA
-// (warp-convergent, one elected lane), warp 1 is the TMA producer, warps 2-5
-// are the softmax warpgroup: thread (warp, lane) owns TMEM lane 32*(warp%4)+lane,
-// one query row.
+// One CTA per 256 query rows of one (batch, head), as two 128-row tiles A and B
+// that share every streamed 128-row K|V tile of a TMA ring. Warp 0 allocates
+// TMEM and issues every MMA (warp-convergent, one elected lane), warp 1 is the
+// TMA producer, warps 2-5 and 6-9 are the softmax warpgroups of tiles A and B:
+// thread (warp, lane) owns TMEM lane 32*(warp%4)+lane, one query row.
 //
-// TMEM: two score buffers S0, S1 (128 columns each) and the output accumulator
-// O. The tensor core computes S(j+1) = Q K_{j+1}^T while the softmax warps turn
-// S(j) into P(j), which they write back as packed bf16 over the first half of
-// S(j)'s own buffer; O += P(j) V_j then reads P from TMEM (A operand) and V from
-// shared memory. Online softmax with lazy rescaling: P = exp2(s - m) against a
-// running maximum m that is only raised -- and O, l rescaled in TMEM -- when a
-// row's maximum grows by more than 2^8, so P stays below 2^8 and most tiles need
-// no rescale at all.
+// TMEM per tile: a score buffer S (128 columns) and the output accumulator O.
+// The softmax warps turn S(j) into P(j), written back as packed bf16 over the
+// first half of S; O += P(j) V_j reads P from TMEM (A operand) and V from shared
+// memory; S(j+1) is issued right behind that product into the same buffer (the
+// tensor core runs in issue order). The two tiles alternate: while one
+// warpgroup waits for its next scores, the other computes, which keeps the
+// exponential units busy. Online softmax with lazy rescaling: P = exp2(s - m)
+// against a running maximum m that is only raised -- and O, l rescaled in TMEM --
+// when a row's maximum grows by more than 2^8, so P stays below 2^8 and most
+// tiles need no rescale at all.
 
 #include <cuda_runtime.h>
 
@@ -33,24 +35,26 @@ struct FwdArgs {
   int* status;
 };
 
-constexpr int kFwdThreads = 192;
+constexpr int kFwdThreads = 320;
 constexpr int kFwdWarpMma = 0;
 constexpr int kFwdWarpProducer = 1;
 constexpr int kFwdFirstEwWarp = 2;
-constexpr int kFwdEwWarps = 4;
+constexpr int kFwdEwWarps = 4;       // per query tile
+constexpr int kFwdRows = 2 * kBM;    // query rows per CTA
 constexpr float kRescaleLog2 = 8.f;  // P < 2^8 between rescales
 
 template <int HD>
 struct FPass {
   static constexpr int BN = 128;                 // key rows per streamed tile
   static constexpr int ST = HD == 128 ? 2 : 4;   // K|V slots: 32 KB at head_dim 64, 64 KB at 128
-  static constexpr int RES = kBM * HD * 2;
+  static constexpr int RES = kBM * HD * 2;       // one 128-row query tile
   static constexpr int STR = BN * HD * 2;
   static constexpr int SLOT = 2 * STR;  // K | V
-  static constexpr int SMEM = 1024 + RES + ST * SLOT;
-  static constexpr int C_O = 2 * BN;    // after the two score buffers
+  static constexpr int SMEM = 1024 + 2 * RES + ST * SLOT;
+  // TMEM: S of tile t at t*BN, O of tile t at 2*BN + t*HD.
+  static constexpr int C_O = 2 * BN;
   static constexpr int TMEM_COLS = 512;
-  static_assert(C_O + HD <= TMEM_COLS, "TMEM budget");
+  static_assert(C_O + 2 * HD <= TMEM_COLS, "TMEM budget");
   static_assert(SMEM <= 232448, "shared memory budget");
 };
 
@@ -69,9 +73,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   constexpr int BN = G::BN, ST = G::ST;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = align1024(smem_raw);
-  uint8_t* s_q = sm;
-  uint8_t* s_ring = s_q + G::RES;
-  __shared__ uint64_t bar_q, bar_full[ST], bar_empty[ST], bar_s_full[2], bar_p_full, bar_pv;
+  uint8_t* s_q = sm;  // tile A, then tile B
+  uint8_t* s_ring = s_q + 2 * G::RES;
+  // Per query tile t: scores ready, P written, last O update done.
+  __shared__ uint64_t bar_q, bar_full[ST], bar_empty[ST], bar_s_full[2], bar_p_full[2], bar_o_done[2];
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
 
@@ -79,9 +84,16 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int h = blockIdx.x, b = blockIdx.y;
   const int qt = gridDim.z - 1 - blockIdx.z;  // longest causal rows first
-  const int q0 = qt * kBM;
-  const int kv_end = sh.causal ? min(sh.Tk, q0 + kBM) : sh.Tk;
-  const int n = (kv_end + BN - 1) / BN;  // key tiles (>= 1)
+  const int q0 = qt * kFwdRows;
+  // Key tiles of each query tile (tile B may lie past the last query row).
+  int nt[2];
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    const int r0 = q0 + t * kBM;
+    const int kv_end = sh.causal ? min(sh.Tk, r0 + kBM) : sh.Tk;
+    nt[t] = r0 < sh.Tq ? (kv_end + BN - 1) / BN : 0;
+  }
+  const int n = max(nt[0], nt[1]);  // key tiles streamed (>= 1)
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
@@ -90,10 +102,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       mbar_init(&bar_full[s], 1);
       mbar_init(&bar_empty[s], 1);
     }
-    mbar_init(&bar_s_full[0], 1);
-    mbar_init(&bar_s_full[1], 1);
-    mbar_init(&bar_p_full, kFwdEwWarps);
-    mbar_init(&bar_pv, 1);
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&bar_s_full[t], 1);
+      mbar_init(&bar_p_full[t], kFwdEwWarps);
+      mbar_init(&bar_o_done[t], 1);
+    }
     mbar_fence_init();
   }
   if (warp == kFwdWarpMma) tmem_alloc(&tmem_base, G::TMEM_COLS);
@@ -107,8 +120,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
-      mbar_arrive_expect_tx(&bar_q, G::RES);
+      mbar_arrive_expect_tx(&bar_q, 2 * G::RES);
       tma_rows<HD>(s_q, &tm_q, &bar_q, q0, kBM, h, b);
+      tma_rows<HD>(s_q + G::RES, &tm_q, &bar_q, q0 + kBM, kBM, h, b);
       int issued = 0;
       for (int j = 0; j < n; ++j) {
         const int s = j % ST;
@@ -130,53 +144,65 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     }
   } else if (warp == kFwdWarpMma) {
     // -------------------------------- MMA issuer --------------------------------
-    // S(j) = Q K_j^T into buffer j&1; O += P(j) V_j with P(j) read from TMEM.
+    // Per key tile j and query tile t: O_t += P_t(j) V_j, then S_t(j+1) = Q_t K_{j+1}^T
+    // into the same TMEM columns (issue order keeps the product's reads first).
     constexpr int KS = HD / 16, KO = BN / 16;
     const uint32_t id_s = idesc_bf16_f32(kBM, BN, false, false);
     const uint32_t id_o = idesc_bf16_f32(kBM, HD, false, true);
     const uint64_t a_q = kdesc(s_q);
+    constexpr uint64_t kRes = G::RES >> 4;
     const uint64_t b_k = kdesc(s_ring);                      // K of slot 0, K-major
     const uint64_t b_v = mndesc(s_ring + G::STR, BN * 128);  // V of slot 0, MN-major
     constexpr uint64_t kSlot = G::SLOT >> 4;
-    auto issue_s = [&](int j) -> bool {
+    auto issue_s = [&](int t, int j) -> bool {
       const int s = j % ST;
       if (!mbar_wait_warp(&bar_full[s], (j / ST) & 1, &abort_flag)) return false;
       tc_fence_after();
-      umma_chain_w<KS, kBM * 128, BN * 128, false>(tmem + (j & 1) * BN, a_q, b_k + s * kSlot, id_s, false);
-      umma_commit_w(&bar_s_full[j & 1]);
+      umma_chain_w<KS, kBM * 128, BN * 128, false>(tmem + t * BN, a_q + t * kRes, b_k + s * kSlot, id_s, false);
+      umma_commit_w(&bar_s_full[t]);
       return true;
     };
-    bool ok = mbar_wait_warp(&bar_q, 0, &abort_flag) && issue_s(0);
+    bool ok = mbar_wait_warp(&bar_q, 0, &abort_flag);
+    for (int t = 0; ok && t < 2; ++t)
+      if (nt[t] > 0) ok = issue_s(t, 0);
     for (int j = 0; ok && j < n; ++j) {
-      // The next tile's scores go into the buffer whose P the previous O update
-      // has already been issued for (the tensor core runs in issue order).
-      if (j + 1 < n && !issue_s(j + 1)) {
-        ok = false;
-        break;
+#pragma unroll 1
+      for (int t = 0; t < 2; ++t) {
+        if (j >= nt[t]) continue;
+        if (!mbar_wait_warp(&bar_p_full[t], j & 1, &abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        umma_chain_ts_w<KO>(tmem + G::C_O + t * HD, tmem + t * BN, b_v + (j % ST) * kSlot, id_o, j > 0);
+        if (j + 1 < nt[t]) {
+          if (!issue_s(t, j + 1)) {
+            ok = false;
+            break;
+          }
+        } else {
+          umma_commit_w(&bar_o_done[t]);
+        }
       }
-      if (!mbar_wait_warp(&bar_p_full, j & 1, &abort_flag)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      umma_chain_ts_w<KO>(tmem + G::C_O, tmem + (j & 1) * BN, b_v + (j % ST) * kSlot, id_o, j > 0);
-      umma_commit_w(&bar_pv);
-      umma_commit_w(&bar_empty[j % ST]);
+      if (ok) umma_commit_w(&bar_empty[j % ST]);
     }
     if (!ok && lane == 0) raise_error(a.status, &abort_flag, kDevTimeoutTmaFull);
   } else {
-    // ------------------------------ softmax warpgroup ------------------------------
-    const int r = (warp & 3) * 32 + lane;  // TMEM lane = query row inside the tile
-    const int row = q0 + r;
+    // ------------------------------ softmax warpgroups ------------------------------
+    const int t = (warp - kFwdFirstEwWarp) >> 2;  // query tile of this warpgroup
+    const int r = (warp & 3) * 32 + lane;         // TMEM lane = query row inside the tile
+    const int row = q0 + t * kBM + r;
     const bool row_ok = row < sh.Tq;
+    const int nj = nt[t];
     const float sc2 = sh.scale * kLog2e;
     const uint32_t lane_base = tmem + tmem_lane_base(warp & 3);
+    const uint32_t tcol = lane_base + t * BN;
+    const uint32_t ocol = lane_base + G::C_O + t * HD;
     float m_used = -INFINITY, l = 0.f;  // running maximum (log2 domain) and the sum against it
     bool ok = true;
-    for (int j = 0; j < n; ++j) {
+    for (int j = 0; j < nj; ++j) {
       const int k0 = j * BN;
-      const uint32_t tcol = lane_base + (j & 1) * BN;
-      ok = mbar_wait_warp(&bar_s_full[j & 1], (j >> 1) & 1, &abort_flag);
+      ok = mbar_wait_warp(&bar_s_full[t], j & 1, &abort_flag);
       if (!ok) break;
       tc_fence_after();
       uint32_t v[BN];
@@ -203,25 +229,21 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 #pragma unroll
         for (int k = 0; k < c; ++k) mx[k] = fmaxf(mx[k], mx[k + c]);
       const float tmax = mx[0] * sc2;  // log2 domain
-      // O is stable once the previous O update is done (needed for a rescale).
-      if (j > 0) {
-        ok = mbar_wait_warp(&bar_pv, (j - 1) & 1, &abort_flag);
-        if (!ok) break;
-        tc_fence_after();
-      }
       const float m_new = fmaxf(m_used, tmax);
       if (j == 0) {
         m_used = m_new;
       } else if (m_new > m_used + kRescaleLog2) {
+        // O is stable: S(j) was issued after the update O += P(j-1) V_{j-1}, so
+        // its completion (just waited for) implies that update's.
         const float f = ex2(m_used - m_new);
 #pragma unroll
         for (int c = 0; c < HD; c += 16) {
           uint32_t o[16];
-          tmem_ld16(lane_base + G::C_O + c, o);
+          tmem_ld16(ocol + c, o);
           tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
-          tmem_st16(lane_base + G::C_O + c, o);
+          tmem_st16(ocol + c, o);
         }
         tmem_wait_st();
         l *= f;
@@ -229,7 +251,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       }
       const float base = (m_used == -INFINITY) ? 0.f : m_used;
       uint32_t pk[BN / 2];
-      float psum = 0.f;
       float ps[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int i = 0; i < BN; i += 2) {
@@ -238,22 +259,21 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         ps[(i >> 1) & 3] += p0 + p1;
         pk[i / 2] = pack_bf16(p0, p1);
       }
-      psum = (ps[0] + ps[1]) + (ps[2] + ps[3]);
-      l += psum;
+      l += (ps[0] + ps[1]) + (ps[2] + ps[3]);
 #pragma unroll
       for (int c = 0; c < BN / 2; c += 16) tmem_st16(tcol + c, *reinterpret_cast<const uint32_t(*)[16]>(&pk[c]));
       tmem_wait_st();
-      fwd_warp_arrive(&bar_p_full);  // P(j) is in TMEM
+      fwd_warp_arrive(&bar_p_full[t]);  // P(j) is in TMEM
     }
-    if (ok) ok = mbar_wait_warp(&bar_pv, (n - 1) & 1, &abort_flag);
-    if (ok) {
+    if (ok && nj > 0) ok = mbar_wait_warp(&bar_o_done[t], 0, &abort_flag);
+    if (ok && nj > 0) {
       tc_fence_after();
       const float inv = (l > 0.f) ? 1.f / l : 0.f;
       __nv_bfloat16* dst = a.o + row_offset(sh.sq, b, row_ok ? row : 0, h);
 #pragma unroll
       for (int c = 0; c < HD; c += 16) {
         uint32_t o[16];
-        tmem_ld16(lane_base + G::C_O + c, o);
+        tmem_ld16(ocol + c, o);
         tmem_wait_ld();
         float x[16];
 #pragma unroll
@@ -261,7 +281,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         if (row_ok) store_bf16x16(dst + c, x);
       }
       if (row_ok) a.lse[stat_index(b, h, row, sh.H, sh.Tq)] = (m_used + log2f(l)) * kLn2;
-    } else if (threadIdx.x == kFwdFirstEwWarp * 32) {
+    } else if (!ok && (threadIdx.x & 127) == 0) {
       raise_error(a.status, &abort_flag, kDevTimeoutMma);
     }
   }
@@ -281,7 +301,7 @@ int launch_fwd_hd(const AttnShape& s, const FwdPtrs& p, int* status, cudaStream_
     return kInvalidArgument;
   if (ensure_smem_limit(reinterpret_cast<const void*>(&fwd_kernel<HD>), G::SMEM) != kOk) return kLaunchFailed;
   FwdArgs args{s, static_cast<__nv_bfloat16*>(p.o), p.lse, status};
-  const dim3 grid(s.H, s.B, (s.Tq + kBM - 1) / kBM);
+  const dim3 grid(s.H, s.B, (s.Tq + kFwdRows - 1) / kFwdRows);
   fwd_kernel<HD><<<grid, kFwdThreads, G::SMEM, stream>>>(mq, mk, mv, args);
   return after_launch();
 }
