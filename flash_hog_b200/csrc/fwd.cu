@@ -8,13 +8,18 @@
 // TMA producer, warps 2-5 and 6-9 are the softmax warpgroups of tiles A and B:
 // thread (warp, lane) owns TMEM lane 32*(warp%4)+lane, one query row.
 //
-// TMEM per tile: a score buffer S (128 columns) and the output accumulator O.
-// The softmax warps turn S(j) into P(j), written back as packed bf16 over the
-// first half of S; O += P(j) V_j reads P from TMEM (A operand) and V from shared
-// memory; S(j+1) is issued right behind that product into the same buffer (the
-// tensor core runs in issue order). The two tiles alternate: while one
-// warpgroup waits for its next scores, the other computes, which keeps the
-// exponential units busy. Online softmax with lazy rescaling: P = exp2(s - m)
+// TMEM per tile: a score buffer S (128 columns) and the output accumulator O,
+// and at head_dim 64 a separate bf16 buffer for P (64 columns). The softmax
+// warps turn S(j) into P(j); O += P(j) V_j reads P from TMEM (A operand) and V
+// from shared memory.
+//  * head_dim 64: the softmax warps release S as soon as they have loaded it, so
+//    S(j+1) is computed while they exponentiate tile j; P(j) goes to its own
+//    buffer once the previous product has read it.
+//  * head_dim 128 (TMEM holds no extra P buffers): P(j) is written back over the
+//    first half of S(j), and S(j+1) is issued right behind O += P(j) V_j into the
+//    same buffer (the tensor core runs in issue order).
+// The two tiles share the exponential units; each warpgroup computes while the
+// other waits. Online softmax with lazy rescaling: P = exp2(s - m)
 // against a running maximum m that is only raised -- and O, l rescaled in TMEM --
 // when a row's maximum grows by more than 2^8, so P stays below 2^8 and most
 // tiles need no rescale at all.
@@ -51,8 +56,11 @@ struct FPass {
   static constexpr int STR = BN * HD * 2;
   static constexpr int SLOT = 2 * STR;  // K | V
   static constexpr int SMEM = 1024 + 2 * RES + ST * SLOT;
-  // TMEM: S of tile t at t*BN, O of tile t at 2*BN + t*HD.
-  static constexpr int C_O = 2 * BN;
+  // TMEM: S of tile t at t*BN; with separate P buffers (head_dim 64), P of tile
+  // t at 2*BN + t*BN/2; O of tile t at C_O + t*HD.
+  static constexpr bool SEP_P = HD == 64;
+  static constexpr int C_P = 2 * BN;
+  static constexpr int C_O = SEP_P ? 3 * BN : 2 * BN;
   static constexpr int TMEM_COLS = 512;
   static_assert(C_O + 2 * HD <= TMEM_COLS, "TMEM budget");
   static_assert(SMEM <= 232448, "shared memory budget");
@@ -71,12 +79,15 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                const __grid_constant__ CUtensorMap tm_v, const FwdArgs a) {
   using G = FPass<HD>;
   constexpr int BN = G::BN, ST = G::ST;
+  constexpr bool SEP_P = G::SEP_P;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = align1024(smem_raw);
   uint8_t* s_q = sm;  // tile A, then tile B
   uint8_t* s_ring = s_q + 2 * G::RES;
-  // Per query tile t: scores ready, P written, last O update done.
-  __shared__ uint64_t bar_q, bar_full[ST], bar_empty[ST], bar_s_full[2], bar_p_full[2], bar_o_done[2];
+  // Per query tile t: scores ready, scores loaded (separate P only), P written,
+  // P read by its product (separate P only), last O update done.
+  __shared__ uint64_t bar_q, bar_full[ST], bar_empty[ST], bar_s_full[2], bar_s_empty[2], bar_p_full[2],
+      bar_p_free[2], bar_o_done[2];
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
 
@@ -104,7 +115,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(&bar_s_full[t], 1);
+      mbar_init(&bar_s_empty[t], kFwdEwWarps);
       mbar_init(&bar_p_full[t], kFwdEwWarps);
+      mbar_init(&bar_p_free[t], 1);
       mbar_init(&bar_o_done[t], 1);
     }
     mbar_fence_init();
@@ -165,7 +178,29 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     bool ok = mbar_wait_warp(&bar_q, 0, &abort_flag);
     for (int t = 0; ok && t < 2; ++t)
       if (nt[t] > 0) ok = issue_s(t, 0);
-    for (int j = 0; ok && j < n; ++j) {
+    for (int j = 0; ok && SEP_P && j < n; ++j) {
+      // Separate P: S(j+1) as soon as S(j) has been loaded, then the products.
+#pragma unroll 1
+      for (int t = 0; ok && t < 2; ++t) {
+        if (j + 1 >= nt[t]) continue;
+        ok = mbar_wait_warp(&bar_s_empty[t], j & 1, &abort_flag) && issue_s(t, j + 1);
+      }
+#pragma unroll 1
+      for (int t = 0; ok && t < 2; ++t) {
+        if (j >= nt[t]) continue;
+        if (!mbar_wait_warp(&bar_p_full[t], j & 1, &abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        umma_chain_ts_w<KO>(tmem + G::C_O + t * HD, tmem + G::C_P + t * (BN / 2), b_v + (j % ST) * kSlot, id_o,
+                            j > 0);
+        umma_commit_w(&bar_p_free[t]);
+        if (j + 1 == nt[t]) umma_commit_w(&bar_o_done[t]);
+      }
+      if (ok) umma_commit_w(&bar_empty[j % ST]);
+    }
+    for (int j = 0; ok && !SEP_P && j < n; ++j) {
 #pragma unroll 1
       for (int t = 0; t < 2; ++t) {
         if (j >= nt[t]) continue;
@@ -211,6 +246,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       tmem_wait_ld();
 #pragma unroll
       for (int i = 0; i < BN; ++i) asm volatile("" : "+r"(v[i])::"memory");
+      if constexpr (G::SEP_P) fwd_warp_arrive(&bar_s_empty[t]);  // S(j+1) may be computed now
       const bool need_mask = (k0 + BN > sh.Tk) || (sh.causal && k0 + BN - 1 > row);
       if (need_mask) {
         const int lim = sh.causal ? min(sh.Tk, row + 1) : sh.Tk;  // keys [k0, lim) are visible
@@ -230,12 +266,14 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         for (int k = 0; k < c; ++k) mx[k] = fmaxf(mx[k], mx[k + c]);
       const float tmax = mx[0] * sc2;  // log2 domain
       const float m_new = fmaxf(m_used, tmax);
+      float f = 1.f;  // rescale factor of O and l, applied before this tile's P is added
       if (j == 0) {
         m_used = m_new;
       } else if (m_new > m_used + kRescaleLog2) {
-        // O is stable: S(j) was issued after the update O += P(j-1) V_{j-1}, so
-        // its completion (just waited for) implies that update's.
-        const float f = ex2(m_used - m_new);
+        f = ex2(m_used - m_new);
+        m_used = m_new;
+      }
+      auto rescale_o = [&]() {
 #pragma unroll
         for (int c = 0; c < HD; c += 16) {
           uint32_t o[16];
@@ -246,9 +284,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           tmem_st16(ocol + c, o);
         }
         tmem_wait_st();
-        l *= f;
-        m_used = m_new;
-      }
+      };
+      // P over S: O is stable now -- S(j) was issued after O += P(j-1) V_{j-1}, so
+      // its completion (just waited for) implies that update's.
+      if (!G::SEP_P && f != 1.f) rescale_o();
       const float base = (m_used == -INFINITY) ? 0.f : m_used;
       uint32_t pk[BN / 2];
       float ps[4] = {0.f, 0.f, 0.f, 0.f};
@@ -259,9 +298,20 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         ps[(i >> 1) & 3] += p0 + p1;
         pk[i / 2] = pack_bf16(p0, p1);
       }
-      l += (ps[0] + ps[1]) + (ps[2] + ps[3]);
+      uint32_t pcol = tcol;
+      if constexpr (G::SEP_P) {
+        // The P buffer and O are free once the previous product is done.
+        if (j > 0) {
+          ok = mbar_wait_warp(&bar_p_free[t], (j - 1) & 1, &abort_flag);
+          if (!ok) break;
+          tc_fence_after();
+          if (f != 1.f) rescale_o();
+        }
+        pcol = lane_base + G::C_P + t * (BN / 2);
+      }
+      l = l * f + ((ps[0] + ps[1]) + (ps[2] + ps[3]));
 #pragma unroll
-      for (int c = 0; c < BN / 2; c += 16) tmem_st16(tcol + c, *reinterpret_cast<const uint32_t(*)[16]>(&pk[c]));
+      for (int c = 0; c < BN / 2; c += 16) tmem_st16(pcol + c, *reinterpret_cast<const uint32_t(*)[16]>(&pk[c]));
       tmem_wait_st();
       fwd_warp_arrive(&bar_p_full[t]);  // P(j) is in TMEM
     }
