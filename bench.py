@@ -13,8 +13,9 @@ query-tiled pass (D = rowsum(dO o O), dQ', ddO, dD, B) and the key-tiled pass
 configurations with the same kernels: cfg3 = causal B2 H32 S8192 D128 (plus peak
 device memory against the sequence length), cfg4 = non-causal B8 H16 Sq4096
 Sk2048 D128, gpt = the grad-norm-penalty training step of a 12-layer GPT (tokens/s,
-NCCL gradient all-reduce under torchrun). Those lines are reported measurements, not
-the headline.
+NCCL gradient all-reduce under torchrun), fwdbwd / fwdbwd128 = the first-order forward
+and backward on the cfg2 / cfg3 shapes beside torch SDPA (cuDNN). Those lines are
+reported measurements, not the headline.
 
 Under torchrun every rank runs the workload on its own GPU (batch x heads of a
 global batch 4N; no collective on the data path) and rank 0 prints one JSON line
@@ -334,6 +335,74 @@ def run_gpt(args):
     return 0
 
 
+def run_fwdbwd(args):
+    """Diagnostic line, not the headline: the first-order forward and backward on the
+    cfg2 (``fwdbwd``) or cfg3 (``fwdbwd128``) shapes, beside torch's SDPA (cuDNN on
+    B200) on the same inputs -- the kernels the reference calls for these two rules
+    (flash_hog/jax/_attention_impl.py:224-261). Credited work: forward 2 and backward
+    5 GEMM-equivalents per kept pair; one step = forward + backward. 1 GPU."""
+    import torch.nn.functional as F
+    from flash_hog_b200 import _capi
+
+    set_workload("cfg2" if args.workload == "fwdbwd" else "cfg3")
+    dev = torch.device("cuda", 0)
+    sets = [make_set(i, dev) for i in range(N_SETS)]
+    outs = [(torch.empty_like(x["q"]), torch.empty((B, H, SQ), dtype=torch.float32, device=dev),
+             torch.empty_like(x["q"]), torch.empty_like(x["k"]), torch.empty_like(x["k"]),
+             torch.empty((B, H, SQ), dtype=torch.float32, device=dev)) for x in sets]
+
+    def ours(i, ev):
+        x, (o, lse, dq, dk, dv, delta) = sets[i % N_SETS], outs[i % N_SETS]
+        ev[0].record()
+        _capi.attn_fwd(x["q"], x["k"], x["v"], o, lse, SCALE, CAUSAL)
+        ev[1].record()
+        _capi.attn_bwd(x["q"], x["k"], x["v"], o, x["do"], lse, dq, dk, dv, delta, SCALE, CAUSAL)
+        ev[2].record()
+
+    bhtd = [{n: x[n].transpose(1, 2) for n in ("q", "k", "v", "do")} for x in sets]
+
+    def sdpa(i, ev):
+        x = bhtd[i % N_SETS]
+        q, k, v = (x[n].detach().requires_grad_(True) for n in ("q", "k", "v"))
+        ev[0].record()
+        out = F.scaled_dot_product_attention(q, k, v, is_causal=CAUSAL, scale=SCALE)
+        ev[1].record()
+        torch.autograd.grad(out, (q, k, v), x["do"])
+        ev[2].record()
+
+    def timed(fn, steps):
+        evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps)]
+        for i in range(args.warmup):
+            fn(i, evs[0])
+        torch.cuda.synchronize()
+        n0 = _capi.launch_count()
+        for i in range(steps):
+            fn(i, evs[i])
+        torch.cuda.synchronize()
+        f = statistics.median(e[0].elapsed_time(e[1]) for e in evs)
+        b = statistics.median(e[1].elapsed_time(e[2]) for e in evs)
+        return f, b, _capi.launch_count() - n0
+
+    with ClockSampler([0]) as clocks:
+        f, b, launches = timed(ours, args.steps)
+    fs, bs, _ = timed(sdpa, args.steps)
+    if _capi.device_status() != 0:
+        raise RuntimeError("device-side error in the forward/backward")
+    p = pairs(B, H, SQ, SK, CAUSAL)
+    tf = lambda gemms, ms: gemms * 2 * D * p / (ms * 1e-3) / 1e12
+    print(json.dumps({
+        "metric": f"attention forward + backward TFLOP/s ({describe()})", "value": tf(7, f + b),
+        "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": f + b,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"fwd + bwd {describe()}", "name": args.workload, "l2": "3 rotating input sets",
+                   "credited_gemm_eq": {"fwd": 2, "bwd": 5}},
+        "fwd": {"ms": f, "tflops": tf(2, f)}, "bwd": {"ms": b, "tflops": tf(5, b)},
+        "torch_sdpa": {"fwd_ms": fs, "fwd_tflops": tf(2, fs), "bwd_ms": bs, "bwd_tflops": tf(5, bs)},
+        "roofline": None, "cpu_baseline": None, "e2e": None, "clocks": clocks.summary(), "gpu_launches": launches,
+    }), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -342,8 +411,11 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--skip-e2e", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["gpt"], default="cfg2")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["gpt", "fwdbwd", "fwdbwd128"], default="cfg2")
     args = ap.parse_args()
+    if args.workload in ("fwdbwd", "fwdbwd128"):
+        args.warmup = max(args.warmup, 3)
+        return run_fwdbwd(args)
     if args.workload == "gpt":
         if args.warmup < 3:
             args.warmup = 3
