@@ -14,6 +14,7 @@ Residual tuples keep the reference's order:
 
 from __future__ import annotations
 
+import dataclasses
 import enum
 
 import torch
@@ -22,16 +23,40 @@ from flash_hog_b200 import _capi
 
 
 class MaskType(enum.Enum):
-    """The two masks of the reference path (``_pallas_gpu_kernel.py:100``)."""
+    """Masks: the two of the reference path (``_pallas_gpu_kernel.py:100``) and the
+    bottom-right alignment of the reference's JAX statements for seq_q != seq_k
+    (``flash_hog/_jax_refs/jax_impl.py:104-109``: query i sees keys j <= i + Tk - Tq).
+    The values are the C ABI's ``causal`` codes."""
 
     NO_MASK = 0
     CAUSAL = 1
+    CAUSAL_BOTTOM_RIGHT = 2
 
 
-def _is_causal(mask_type: MaskType) -> bool:
-    if mask_type not in (MaskType.NO_MASK, MaskType.CAUSAL):
-        raise ValueError(f"unsupported mask type {mask_type}")
-    return mask_type is MaskType.CAUSAL
+@dataclasses.dataclass(frozen=True)
+class SlidingWindow:
+    """A causal mask (``mask_type`` CAUSAL or CAUSAL_BOTTOM_RIGHT) limited to the
+    ``length`` keys ending at each query's diagonal -- ``get_mask_bottom_right``'s
+    ``qi - kj < sliding_window_length`` (``flash_hog/_jax_refs/jax_impl.py:104-109``).
+    Accepted wherever a ``MaskType`` is."""
+
+    mask_type: MaskType
+    length: int
+
+
+def _mask_args(mask) -> tuple[int, int]:
+    """(causal code, window length) of a MaskType or SlidingWindow, for the C ABI."""
+    if isinstance(mask, SlidingWindow):
+        if mask.mask_type not in (MaskType.CAUSAL, MaskType.CAUSAL_BOTTOM_RIGHT) or mask.length < 1:
+            raise ValueError(f"a sliding window needs a causal mask type and a length >= 1, got {mask}")
+        return mask.mask_type.value, int(mask.length)
+    if not isinstance(mask, MaskType):
+        raise ValueError(f"unsupported mask type {mask}")
+    return mask.value, 0
+
+
+def _is_causal(mask) -> bool:
+    return _mask_args(mask)[0] != 0
 
 
 def _bf16(x: torch.Tensor) -> torch.Tensor:
@@ -61,7 +86,7 @@ def cuda_dot_product_attention(query, key, value, mask_type: MaskType, scale: fl
     b, t, n, _ = q.shape
     out = torch.empty_like(q)
     lse = torch.empty((b, n, t), dtype=torch.float32, device=q.device)
-    _capi.attn_fwd(q, k, v, out, lse, scale, _is_causal(mask_type))
+    _capi.attn_fwd(q, k, v, out, lse, scale, *_mask_args(mask_type))
     out = out.to(query.dtype)
     return (out, lse) if return_residual else out
 
@@ -86,7 +111,7 @@ def dot_product_attention_bwd_rule(mask_type: MaskType, scale: float, res, g):
     dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
     delta = torch.empty((b, n, t), dtype=torch.float32, device=q.device)
     _capi.attn_bwd(q, k, v, o, do, activation.float().contiguous(), dq, dk, dv, delta, scale,
-                   _is_causal(mask_type))
+                   *_mask_args(mask_type))
     return dq.to(query.dtype), dk.to(key.dtype), dv.to(value.dtype)
 
 
@@ -132,7 +157,8 @@ def dot_product_attention_fwd_jvp(mask_type: MaskType, scale: float, res, tangen
     zero_do = torch.zeros_like(q)
     dq2, t_out = torch.empty_like(q), torch.empty_like(q)
     _capi.attn_bwdbwd_o(q, k, v, o, zero_do, tq, tk, tv, activation.float().contiguous(), dq2, t_out, None, None,
-                        stats[0], stats[1], stats[2], scale, _is_causal(mask_type), which=_capi.PASS_QUERY)
+                        stats[0], stats[1], stats[2], scale, _mask_args(mask_type)[0], which=_capi.PASS_QUERY,
+                        window=_mask_args(mask_type)[1])
     return t_out.to(out.dtype), stats[1].clone()
 
 
@@ -160,7 +186,7 @@ def dot_product_attention_bwd_jvp(mask_type: MaskType, scale: float, res, g, tan
     tdq, t_out = torch.empty_like(q), torch.empty_like(q)
     tdk, tdv = torch.empty_like(k), torch.empty_like(v)
     _capi.attn_jvp_bwd(q, k, v, o, do, activation.float().contiguous(), tq, tk, tv, tdo, tdq, tdk, tdv, t_out,
-                       stats[0], stats[1], stats[2], scale, _is_causal(mask_type))
+                       stats[0], stats[1], stats[2], scale, *_mask_args(mask_type))
     return tdq.to(query.dtype), tdk.to(key.dtype), tdv.to(value.dtype)
 
 

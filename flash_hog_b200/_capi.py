@@ -46,7 +46,7 @@ EXPORTED_SYMBOLS = (
     "fh_abi_version",
     "fh_launch_count",
 )
-ABI_VERSION = 3
+ABI_VERSION = 4
 
 
 class FlashHogError(RuntimeError):
@@ -72,6 +72,7 @@ class FhAttnDims(ctypes.Structure):
         ("q", FhStrides),
         ("k", FhStrides),
         ("kv_heads", ctypes.c_int32),
+        ("window", ctypes.c_int32),
     ]
 
 
@@ -142,11 +143,12 @@ def _layout_key(t: torch.Tensor):
     return tuple(t.shape), (s.batch, s.seq, s.head)
 
 
-def make_dims(q: torch.Tensor, k: torch.Tensor) -> FhAttnDims:
-    """Dims for BTNH tensors: q (B, Tq, H, D), k (B, Tk, Hkv, D) with H a multiple of Hkv."""
+def make_dims(q: torch.Tensor, k: torch.Tensor, window: int = 0) -> FhAttnDims:
+    """Dims for BTNH tensors: q (B, Tq, H, D), k (B, Tk, Hkv, D) with H a multiple of
+    Hkv; ``window`` is the sliding-window length of a causal mask (0 = unlimited)."""
     b, tq, h, d = q.shape
     tk, hkv = k.shape[1], k.shape[2]
-    return FhAttnDims(b, h, tq, tk, d, _strides(q), _strides(k), hkv)
+    return FhAttnDims(b, h, tq, tk, d, _strides(q), _strides(k), hkv, int(window))
 
 
 def _same_layout(ref: torch.Tensor, *others: torch.Tensor) -> None:
@@ -161,10 +163,10 @@ def _same_layout(ref: torch.Tensor, *others: torch.Tensor) -> None:
             raise ValueError("tensors must be bf16 on the same CUDA device")
 
 
-def attn_fwd(q, k, v, out, lse, scale: float, causal: bool) -> None:
+def attn_fwd(q, k, v, out, lse, scale: float, causal: int, window: int = 0) -> None:
     _same_layout(q, out)
     _same_layout(k, v)
-    dims = make_dims(q, k)
+    dims = make_dims(q, k, window)
     _check("fh_attn_fwd", lib().fh_attn_fwd(_stream(q.device), ctypes.byref(dims), _ptr(q), _ptr(k), _ptr(v),
                                            _ptr(out), _ptr(lse), float(scale), int(causal)))
 
@@ -176,20 +178,20 @@ def attn_rowdot(o, dO, delta) -> None:
                                                  _ptr(delta)))
 
 
-def attn_bwd(q, k, v, o, dO, lse, dq, dk, dv, delta, scale: float, causal: bool) -> None:
+def attn_bwd(q, k, v, o, dO, lse, dq, dk, dv, delta, scale: float, causal: int, window: int = 0) -> None:
     _same_layout(q, o, dO, dq)
     _same_layout(k, v, dk, dv)
-    dims = make_dims(q, k)
+    dims = make_dims(q, k, window)
     _check("fh_attn_bwd", lib().fh_attn_bwd(_stream(q.device), ctypes.byref(dims), _ptr(q), _ptr(k), _ptr(v),
                                            _ptr(o), _ptr(dO), _ptr(lse), _ptr(dq), _ptr(dk), _ptr(dv),
                                            _ptr(delta), float(scale), int(causal)))
 
 
 def attn_bwdbwd(q, k, v, dO, ddq, ddk, ddv, lse, delta, dq2, ddo, dk2, dv2, dd, bvec, scale: float,
-                causal: bool) -> None:
+                causal: int, window: int = 0) -> None:
     _same_layout(q, dO, ddq, dq2, ddo)
     _same_layout(k, v, ddk, ddv, dk2, dv2)
-    dims = make_dims(q, k)
+    dims = make_dims(q, k, window)
     _check("fh_attn_bwdbwd", lib().fh_attn_bwdbwd(
         _stream(q.device), ctypes.byref(dims), _ptr(q), _ptr(k), _ptr(v), _ptr(dO), _ptr(ddq), _ptr(ddk),
         _ptr(ddv), _ptr(lse), _ptr(delta), _ptr(dq2), _ptr(ddo), _ptr(dk2), _ptr(dv2), _ptr(dd), _ptr(bvec),
@@ -200,11 +202,11 @@ PASS_QUERY, PASS_KEY = 1, 2
 
 
 def attn_bwdbwd_pass(q, k, v, dO, ddq, ddk, ddv, lse, delta, dq2, ddo, dk2, dv2, dd, bvec, scale: float,
-                     causal: bool, which: int) -> None:
+                     causal: int, which: int, window: int = 0) -> None:
     """One pass of the double backward (PASS_QUERY, PASS_KEY or both)."""
     _same_layout(q, dO, ddq, dq2, ddo)
     _same_layout(k, v, ddk, ddv, dk2, dv2)
-    dims = make_dims(q, k)
+    dims = make_dims(q, k, window)
     _check("fh_attn_bwdbwd_pass", lib().fh_attn_bwdbwd_pass(
         _stream(q.device), ctypes.byref(dims), _ptr(q), _ptr(k), _ptr(v), _ptr(dO), _ptr(ddq), _ptr(ddk),
         _ptr(ddv), _ptr(lse), _ptr(delta), _ptr(dq2), _ptr(ddo), _ptr(dk2), _ptr(dv2), _ptr(dd), _ptr(bvec),
@@ -212,11 +214,11 @@ def attn_bwdbwd_pass(q, k, v, dO, ddq, ddk, ddv, lse, delta, dq2, ddo, dk2, dv2,
 
 
 def attn_bwdbwd_o(q, k, v, o, dO, ddq, ddk, ddv, lse, dq2, ddo, dk2, dv2, delta, dd, bvec, scale: float,
-                  causal: bool, which: int = PASS_QUERY | PASS_KEY) -> None:
+                  causal: int, which: int = PASS_QUERY | PASS_KEY, window: int = 0) -> None:
     """Double backward from the forward output: the query pass computes delta itself."""
     _same_layout(q, o, dO, ddq, dq2, ddo)
     _same_layout(k, v, ddk, ddv, dk2, dv2)
-    dims = make_dims(q, k)
+    dims = make_dims(q, k, window)
     _check("fh_attn_bwdbwd_o", lib().fh_attn_bwdbwd_o(
         _stream(q.device), ctypes.byref(dims), _ptr(q), _ptr(k), _ptr(v), _ptr(o), _ptr(dO), _ptr(ddq),
         _ptr(ddk), _ptr(ddv), _ptr(lse), _ptr(dq2), _ptr(ddo), _ptr(dk2), _ptr(dv2), _ptr(delta), _ptr(dd),
@@ -224,11 +226,11 @@ def attn_bwdbwd_o(q, k, v, o, dO, ddq, ddk, ddv, lse, dq2, ddo, dk2, dv2, delta,
 
 
 def attn_jvp_bwd(q, k, v, o, dO, lse, tq, tk, tv, tdO, tdq, tdk, tdv, to, delta, dd, bvec, scale: float,
-                 causal: bool) -> None:
+                 causal: int, window: int = 0) -> None:
     """Forward-mode derivative of the first-order backward (``tdO`` may be None)."""
     _same_layout(q, o, dO, tq, tdq, to, tdO)
     _same_layout(k, v, tk, tv, tdk, tdv)
-    dims = make_dims(q, k)
+    dims = make_dims(q, k, window)
     _check("fh_attn_jvp_bwd", lib().fh_attn_jvp_bwd(
         _stream(q.device), ctypes.byref(dims), _ptr(q), _ptr(k), _ptr(v), _ptr(o), _ptr(dO), _ptr(lse), _ptr(tq),
         _ptr(tk), _ptr(tv), _ptr(tdO), _ptr(tdq), _ptr(tdk), _ptr(tdv), _ptr(to),

@@ -29,20 +29,36 @@ from __future__ import annotations
 import torch
 
 from flash_hog_b200 import _attention_impl as attn_impl
-from flash_hog_b200._attention_impl import MaskType
+from flash_hog_b200._attention_impl import MaskType, SlidingWindow
 
 
-def dot_product_attention(query, key, value, is_causal: bool = False, scale: float | None = None):
+def dot_product_attention(query, key, value, is_causal: bool = False, scale: float | None = None, *,
+                          causal_alignment: str = "top_left", sliding_window_length: int | None = None):
     """softmax(scale * query key^T [+ causal mask]) value.
 
     Dimensions: T query length, S key/value length, N heads, H head dim.
     query (B, T, N, H) or (T, N H); key, value (B, S, N, H) or (S, N, H).
+
+    Keyword-only extensions of the reference signature, with ``is_causal``:
+    ``causal_alignment`` "top_left" (query i sees keys j <= i, the reference API's
+    mask) or "bottom_right" (j <= i + S - T, the alignment of the reference's JAX
+    statements, ``flash_hog/_jax_refs/jax_impl.py:104-109``), and
+    ``sliding_window_length`` W (each query sees the W keys ending at its diagonal).
+    A query that sees no key gets a zero output.
     """
     if scale is None:
         scale = query.shape[-1] ** -0.5
     if not (query.dtype == key.dtype == value.dtype):
         raise TypeError("query, key and value must share a dtype")
-    mask_type = MaskType.CAUSAL if is_causal else MaskType.NO_MASK
+    if causal_alignment not in ("top_left", "bottom_right"):
+        raise ValueError(f"causal_alignment must be 'top_left' or 'bottom_right', got {causal_alignment!r}")
+    if not is_causal and (sliding_window_length is not None or causal_alignment != "top_left"):
+        raise ValueError("causal_alignment and sliding_window_length apply to causal attention only")
+    mask_type = MaskType.NO_MASK
+    if is_causal:
+        mask_type = MaskType.CAUSAL if causal_alignment == "top_left" else MaskType.CAUSAL_BOTTOM_RIGHT
+        if sliding_window_length is not None:
+            mask_type = SlidingWindow(mask_type, int(sliding_window_length))
     unbatched = query.ndim == 3
     if unbatched:
         query, key, value = query.unsqueeze(0), key.unsqueeze(0), value.unsqueeze(0)

@@ -37,6 +37,10 @@ struct Strides3 {
   long long b, t, h;
 };
 
+// The mask is a band: with `causal`, query i sees key j iff j <= i + diag and,
+// when window > 0, j > i + diag - window (diag = 0: top-left causal; diag =
+// Tk - Tq: bottom-right; window: sliding-window length). Without `causal` every
+// key is visible.
 struct AttnShape {
   int B, H, Tq, Tk;  // H: query heads
   int Hk, G;         // key/value heads and the group size H / Hk (query head h uses key head h / G)
@@ -44,7 +48,46 @@ struct AttnShape {
   Strides3 sk;   // key-side tensors
   float scale;
   int causal;
+  int diag;
+  int window;
 };
+
+// Visible keys [key_lo, key_hi] of query row i (empty when key_hi < key_lo).
+__host__ __device__ __forceinline__ int key_hi(const AttnShape& s, int i) {
+  return s.causal ? min(s.Tk - 1, i + s.diag) : s.Tk - 1;
+}
+__host__ __device__ __forceinline__ int key_lo(const AttnShape& s, int i) {
+  return (s.causal && s.window > 0) ? max(0, i + s.diag - s.window + 1) : 0;
+}
+// Queries [query_lo, query_hi] that see key j (empty when query_hi < query_lo).
+__host__ __device__ __forceinline__ int query_lo(const AttnShape& s, int j) {
+  return s.causal ? max(0, j - s.diag) : 0;
+}
+__host__ __device__ __forceinline__ int query_hi(const AttnShape& s, int j) {
+  return (s.causal && s.window > 0) ? min(s.Tq - 1, j - s.diag + s.window - 1) : s.Tq - 1;
+}
+
+// Streamed tiles of `bn` rows that query rows [r0, r0 + rows) need: tiles
+// [*first, *first + return value) of the key sequence (0 tiles if none).
+__host__ __device__ __forceinline__ int key_tiles(const AttnShape& s, int r0, int rows, int bn, int* first) {
+  const int r1 = min(r0 + rows, s.Tq) - 1;
+  *first = 0;
+  if (r1 < r0) return 0;
+  const int lo = key_lo(s, r0), hi = key_hi(s, r1);
+  if (hi < lo) return 0;
+  *first = lo / bn;
+  return hi / bn + 1 - *first;
+}
+// Streamed tiles of `bn` query rows that key rows [k0, k0 + rows) need.
+__host__ __device__ __forceinline__ int query_tiles(const AttnShape& s, int k0, int rows, int bn, int* first) {
+  const int k1 = min(k0 + rows, s.Tk) - 1;
+  *first = 0;
+  if (k1 < k0) return 0;
+  const int lo = query_lo(s, k0), hi = query_hi(s, k1);
+  if (hi < lo) return 0;
+  *first = lo / bn;
+  return hi / bn + 1 - *first;
+}
 
 __device__ __forceinline__ size_t row_offset(const Strides3& s, int b, int t, int h) {
   return static_cast<size_t>(b) * s.b + static_cast<size_t>(t) * s.t + static_cast<size_t>(h) * s.h;

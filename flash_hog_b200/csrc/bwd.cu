@@ -72,8 +72,8 @@ struct DqPass {
 
 // Packed bf16 pairs of dS/scale = P (dP - D) for this thread's CW key columns.
 template <int CW, bool MASK>
-__device__ __forceinline__ void dq_ops(const uint32_t (&vs)[CW], const uint32_t (&vdp)[CW], int kc, int row, int tk,
-                                       int causal, float sc2, float lg, float dv, uint32_t (&o_ds)[CW / 2]) {
+__device__ __forceinline__ void dq_ops(const uint32_t (&vs)[CW], const uint32_t (&vdp)[CW], int kc, int klo, int khi,
+                                       float sc2, float lg, float dv, uint32_t (&o_ds)[CW / 2]) {
 #pragma unroll
   for (int i = 0; i < CW; i += 2) {
     float ds[2];
@@ -81,7 +81,7 @@ __device__ __forceinline__ void dq_ops(const uint32_t (&vs)[CW], const uint32_t 
     for (int e = 0; e < 2; ++e) {
       const int c = i + e;
       float s = fmaf(__uint_as_float(vs[c]), sc2, -lg);
-      if (MASK && (kc + c >= tk || (causal && kc + c > row))) s = -INFINITY;
+      if (MASK && (kc + c > khi || kc + c < klo)) s = -INFINITY;
       ds[e] = ex2(s) * (__uint_as_float(vdp[c]) - dv);
     }
     o_ds[i / 2] = pack_bf16(ds[0], ds[1]);
@@ -117,8 +117,8 @@ __global__ void __launch_bounds__(kBBThreads, 1)
   const int h = blockIdx.x, b = blockIdx.y;
   const int qt = gridDim.z - 1 - blockIdx.z;  // longest causal rows first
   const int q0 = qt * kBM;
-  const int kv_end = sh.causal ? min(sh.Tk, q0 + kBM) : sh.Tk;
-  const int n = (kv_end + BN - 1) / BN;  // key tiles (>= 1)
+  int j0;
+  const int n = key_tiles(sh, q0, kBM, BN, &j0);  // key tiles j0, j0 + 1, ... (0: no row sees a key)
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
@@ -166,8 +166,8 @@ __global__ void __launch_bounds__(kBBThreads, 1)
         }
         uint8_t* slot = s_ring + s * G::SLOT;
         mbar_arrive_expect_tx(&bar_full[s], G::SLOT);
-        tma_rows<HD>(slot, &tm_k, &bar_full[s], it * BN, BN, h / sh.G, b);
-        tma_rows<HD>(slot + G::STR, &tm_v, &bar_full[s], it * BN, BN, h / sh.G, b);
+        tma_rows<HD>(slot, &tm_k, &bar_full[s], (j0 + it) * BN, BN, h / sh.G, b);
+        tma_rows<HD>(slot + G::STR, &tm_v, &bar_full[s], (j0 + it) * BN, BN, h / sh.G, b);
         issued = it + 1;
       }
       // Every issued copy must land before this CTA's shared memory is released.
@@ -235,7 +235,9 @@ __global__ void __launch_bounds__(kBBThreads, 1)
     const int row = q0 + r;
     const bool row_ok = row < sh.Tq;
     const size_t vi = stat_index(b, h, row_ok ? row : 0, sh.H, sh.Tq);
-    const float lg = row_ok ? a.lse[vi] * kLog2e : 0.f;
+    const float lse = row_ok ? a.lse[vi] : 0.f;
+    const float lg = lse > -INFINITY ? lse * kLog2e : 0.f;  // -inf: the row sees no key (all masked)
+    const int khi = key_hi(sh, row), klo = key_lo(sh, row);
     const float sc2 = sh.scale * kLog2e;
     bool ok = mbar_wait_warp(&bar_res, 0, &abort_flag);
     float dv = 0.f;
@@ -267,13 +269,13 @@ __global__ void __launch_bounds__(kBBThreads, 1)
       reg_fence(vs);
       reg_fence(vdp);
       warp_arrive(&bar_sc_empty[wg]);  // the tensor core may reuse this score buffer now
-      const int kc = j * BN;
-      const bool need_mask = (kc + BN > sh.Tk) || (sh.causal && kc + BN - 1 > row);
+      const int kc = (j0 + j) * BN;
+      const bool need_mask = kc + BN - 1 > khi || kc < klo;
       uint32_t o_ds[BN / 2];
       if (need_mask)
-        dq_ops<BN, true>(vs, vdp, kc, row, sh.Tk, sh.causal, sc2, lg, dv, o_ds);
+        dq_ops<BN, true>(vs, vdp, kc, klo, khi, sc2, lg, dv, o_ds);
       else
-        dq_ops<BN, false>(vs, vdp, kc, row, sh.Tk, sh.causal, sc2, lg, dv, o_ds);
+        dq_ops<BN, false>(vs, vdp, kc, klo, khi, sc2, lg, dv, o_ds);
       if (u > 0) ok = mbar_wait_warp(&bar_ops_empty[wg], (u - 1) & 1, &abort_flag);
       if (!ok) break;
       tc_fence_after();
@@ -282,8 +284,16 @@ __global__ void __launch_bounds__(kBBThreads, 1)
       tmem_wait_st();
       warp_arrive(&bar_ops_full[wg]);
     }
-    if (ok) ok = mbar_wait_warp(&bar_acc, 0, &abort_flag);
-    if (ok) {
+    if (ok && n == 0) {
+      // No key tile: dQ = 0 (plus the addend).
+      const size_t off = row_offset(sh.sq, b, row_ok ? row : 0, h) + wg * (HD / 2);
+      for (int c = 0; row_ok && c < HD / 2; c += 8)
+        reinterpret_cast<uint4*>(a.dq + off + c)[0] =
+            a.dq_acc ? reinterpret_cast<const uint4*>(a.dq_acc + off + c)[0] : make_uint4(0, 0, 0, 0);
+    } else if (ok) {
+      ok = mbar_wait_warp(&bar_acc, 0, &abort_flag);
+    }
+    if (ok && n > 0) {
       tc_fence_after();
       const int srow = row_ok ? row : 0;
       const size_t off = row_offset(sh.sq, b, srow, h) + wg * (HD / 2);
@@ -340,8 +350,8 @@ struct DkvPass {
 // query columns; the statistics arrive folded into the scores by the bias MMA:
 //   vs = S - L/scale,  vdp = dP - D.
 template <int CW, bool MASK>
-__device__ __forceinline__ void dkv_ops(const uint32_t (&vs)[CW], const uint32_t (&vdp)[CW], int qc, int key, int tq,
-                                        int causal, float sc2, uint32_t (&o_p)[CW / 2], uint32_t (&o_ds)[CW / 2]) {
+__device__ __forceinline__ void dkv_ops(const uint32_t (&vs)[CW], const uint32_t (&vdp)[CW], int qc, int qlo, int qhi,
+                                        float sc2, uint32_t (&o_p)[CW / 2], uint32_t (&o_ds)[CW / 2]) {
 #pragma unroll
   for (int i = 0; i < CW; i += 2) {
     float pp[2], ds[2];
@@ -349,7 +359,7 @@ __device__ __forceinline__ void dkv_ops(const uint32_t (&vs)[CW], const uint32_t
     for (int e = 0; e < 2; ++e) {
       const int c = i + e;
       float s = __uint_as_float(vs[c]) * sc2;
-      if (MASK && (qc + c >= tq || (causal && qc + c < key))) s = -INFINITY;
+      if (MASK && (qc + c > qhi || qc + c < qlo)) s = -INFINITY;
       pp[e] = ex2(s);
       ds[e] = pp[e] * __uint_as_float(vdp[c]);
     }
@@ -380,9 +390,8 @@ __global__ void __launch_bounds__(kBBThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int hk = blockIdx.x, b = blockIdx.y;
   const int k0 = blockIdx.z * kBM;  // key tile 0 first: the most causal query tiles
-  const int nq_tiles = (sh.Tq + BN - 1) / BN;
-  const int qt_begin = sh.causal ? k0 / BN : 0;  // earlier queries see none of these keys
-  const int n = nq_tiles > qt_begin ? nq_tiles - qt_begin : 0;
+  int qt_begin;
+  const int n = query_tiles(sh, k0, kBM, BN, &qt_begin);  // query tiles that see any of these keys
   const int total = n * sh.G;  // streamed tiles: n per query head of the group
 
   if (threadIdx.x == 0) {
@@ -484,7 +493,9 @@ __global__ void __launch_bounds__(kBBThreads, 1)
       const uint32_t bias = smem_u32(slot + 2 * G::STR);
 #pragma unroll
       for (int k = 0; k < RPL; ++k) {
-        const bool v = q0 + lane + 32 * k < sh.Tq;
+        // Queries past the end, or with L = -inf (no visible key: every element of
+        // theirs is masked), get a zero bias.
+        const bool v = q0 + lane + 32 * k < sh.Tq && raw[k][0] > -INFINITY;
         const int r = lane + 32 * k;
         store_bias_row(bias, r, v ? -raw[k][0] * inv_scale : 0.f);  // S - L/scale
         store_bias_row(bias, BN + r, v ? -raw[k][1] : 0.f);         // dP - D
@@ -567,6 +578,7 @@ __global__ void __launch_bounds__(kBBThreads, 1)
     const int cb = wg * CW;
     const int key = k0 + r;
     const bool key_ok = key < sh.Tk;
+    const int qhi = query_hi(sh, key), qlo = query_lo(sh, key);  // queries that see this key
     const float sc2 = sh.scale * kLog2e;
     bool ok = mbar_wait_warp(&bar_res, 0, &abort_flag);
     if (ok) {
@@ -590,12 +602,12 @@ __global__ void __launch_bounds__(kBBThreads, 1)
       reg_fence(vdp);
       warp_arrive(&bar_sc_empty[sb]);
       const int qc = (qt_begin + it % n) * BN + cb;  // first query of this thread's columns
-      const bool need_mask = (qc + CW > sh.Tq) || (sh.causal && qc < key);
+      const bool need_mask = qc + CW - 1 > qhi || qc < qlo;
       uint32_t o_p[CW / 2], o_ds[CW / 2];
       if (need_mask)
-        dkv_ops<CW, true>(vs, vdp, qc, key, sh.Tq, sh.causal, sc2, o_p, o_ds);
+        dkv_ops<CW, true>(vs, vdp, qc, qlo, qhi, sc2, o_p, o_ds);
       else
-        dkv_ops<CW, false>(vs, vdp, qc, key, sh.Tq, sh.causal, sc2, o_p, o_ds);
+        dkv_ops<CW, false>(vs, vdp, qc, qlo, qhi, sc2, o_p, o_ds);
       if (it > 0) ok = mbar_wait_warp(&bar_ops_empty, (it - 1) & 1, &abort_flag);
       if (!ok) break;
       tc_fence_after();

@@ -82,13 +82,13 @@ struct QPass {
 // sweep): dD/scale += P ddS', r1 += P dPa, r2 += P dP, r3/scale += P ddS' dP.
 template <int CW, bool MASK>
 __device__ __forceinline__ void q_stats(const uint32_t (&vs)[CW], const uint32_t (&vdds)[CW],
-                                        const uint32_t (&vdp)[CW], const uint32_t (&vdpa)[CW], int kc, int row,
-                                          int tk, int causal, float sc, float sc2, float lg, float& dD, float& r1,
-                                          float& r2, float& r3) {
+                                        const uint32_t (&vdp)[CW], const uint32_t (&vdpa)[CW], int kc, int klo,
+                                        int khi, float sc, float sc2, float lg, float& dD, float& r1, float& r2,
+                                        float& r3) {
 #pragma unroll
   for (int i = 0; i < CW; ++i) {
     float s = fmaf(__uint_as_float(vs[i]), sc2, -lg);
-    if (MASK && (kc + i >= tk || (causal && kc + i > row))) s = -INFINITY;
+    if (MASK && (kc + i > khi || kc + i < klo)) s = -INFINITY;
     const float p = ex2(s);
     const float t = __uint_as_float(vdds[i]) * p;
     const float dp = __uint_as_float(vdp[i]);
@@ -106,8 +106,8 @@ __device__ __forceinline__ void q_stats(const uint32_t (&vs)[CW], const uint32_t
 //   dS2/scale = P (dPa + dP u - ddS D - B) = P (dPa - c) + ddP (dP - D).
 template <int CW, bool MASK>
 __device__ __forceinline__ void q_ops(const uint32_t (&vs)[CW], const uint32_t (&vdds)[CW],
-                                      const uint32_t (&vdp)[CW], const uint32_t (&vdpa)[CW], int kc, int row, int tk,
-                                      int causal, float sc, float sc2, float lg, float dv, float dD, float cq,
+                                      const uint32_t (&vdp)[CW], const uint32_t (&vdpa)[CW], int kc, int klo, int khi,
+                                      float sc, float sc2, float lg, float dv, float dD, float cq,
                                       uint32_t (&o_ds)[CW / 2], uint32_t (&o_ds2)[CW / 2], uint32_t (&o_ddp)[CW / 2],
                                       uint32_t (&o_p)[CW / 2]) {
 #pragma unroll
@@ -117,7 +117,7 @@ __device__ __forceinline__ void q_ops(const uint32_t (&vs)[CW], const uint32_t (
     for (int e = 0; e < 2; ++e) {
       const int c = i + e;
       float s = fmaf(__uint_as_float(vs[c]), sc2, -lg);
-      if (MASK && (kc + c >= tk || (causal && kc + c > row))) s = -INFINITY;
+      if (MASK && (kc + c > khi || kc + c < klo)) s = -INFINITY;
       const float p = ex2(s);
       const float u = fmaf(__uint_as_float(vdds[c]), sc, -dD);  // ddS - dD
       const float dpd = __uint_as_float(vdp[c]) - dv;            // dP - D
@@ -165,8 +165,8 @@ __global__ void __launch_bounds__(kBBThreads, 1)
   const int h = blockIdx.x, b = blockIdx.y;
   const int qt = gridDim.z - 1 - blockIdx.z;  // longest causal rows first
   const int q0 = qt * kBM;
-  const int kv_end = sh.causal ? min(sh.Tk, q0 + kBM) : sh.Tk;
-  const int n = (kv_end + BN - 1) / BN;  // key tiles per sweep (>= 1)
+  int j0;
+  const int n = key_tiles(sh, q0, kBM, BN, &j0);  // key tiles j0, j0 + 1, ... per sweep (0: no row sees a key)
   const int total = 2 * n;
   // Score buffer of tile `it` and how many earlier tiles used that buffer:
   // the stats sweep alternates buffers 0 and 1, the second sweep uses buffer 0.
@@ -218,7 +218,7 @@ __global__ void __launch_bounds__(kBBThreads, 1)
           raise_error(a.status, &abort_flag, kDevTimeoutSlotEmpty);
           break;
         }
-        const int k0 = (it % n) * BN;
+        const int k0 = (j0 + it % n) * BN;
         uint8_t* slot = s_ring + s * G::SLOT;
         mbar_arrive_expect_tx(&bar_full[s], G::SLOT);
         tma_pair<HD>(slot, &tm_k, &tm_ddk, &bar_full[s], k0, BN, h / sh.G, b);
@@ -302,7 +302,9 @@ __global__ void __launch_bounds__(kBBThreads, 1)
     const int row = q0 + r;
     const bool row_ok = row < sh.Tq;
     const size_t vi = stat_index(b, h, row_ok ? row : 0, sh.H, sh.Tq);
-    const float lg = row_ok ? a.lse[vi] * kLog2e : 0.f;
+    const float lse = row_ok ? a.lse[vi] : 0.f;
+    const float lg = lse > -INFINITY ? lse * kLog2e : 0.f;  // -inf: the row sees no key (all masked)
+    const int khi = key_hi(sh, row), klo = key_lo(sh, row);
     const float sc = sh.scale, sc2 = sh.scale * kLog2e;
     float dD = 0.f, r1 = 0.f, r2 = 0.f, r3 = 0.f, Bv = 0.f, cq = 0.f;
     bool ok = true;
@@ -323,7 +325,7 @@ __global__ void __launch_bounds__(kBBThreads, 1)
     for (int it = 0; ok && it < total; ++it) {
       const int j = it % n;
       const bool sweep2 = it >= n;
-      const int kc = j * BN + cb;  // first key of this thread's columns
+      const int kc = (j0 + j) * BN + cb;  // first key of this thread's columns
       const int sb = buf_of(it);
       ok = mbar_wait_warp(&bar_sc_full[sb], use_of(it) & 1, &abort_flag);
       if (!ok) break;
@@ -340,12 +342,12 @@ __global__ void __launch_bounds__(kBBThreads, 1)
       reg_fence(vdp);
       reg_fence(vdpa);
       warp_arrive(&bar_sc_empty[sb]);  // the tensor core may reuse this score buffer now
-      const bool need_mask = (kc + CW > sh.Tk) || (sh.causal && kc + CW - 1 > row);
+      const bool need_mask = kc + CW - 1 > khi || kc < klo;
       if (!sweep2) {
         if (need_mask)
-          q_stats<CW, true>(vs, vdds, vdp, vdpa, kc, row, sh.Tk, sh.causal, sc, sc2, lg, dD, r1, r2, r3);
+          q_stats<CW, true>(vs, vdds, vdp, vdpa, kc, klo, khi, sc, sc2, lg, dD, r1, r2, r3);
         else
-          q_stats<CW, false>(vs, vdds, vdp, vdpa, kc, row, sh.Tk, sh.causal, sc, sc2, lg, dD, r1, r2, r3);
+          q_stats<CW, false>(vs, vdds, vdp, vdpa, kc, klo, khi, sc, sc2, lg, dD, r1, r2, r3);
         if (it == n - 1) {
           // Combine the two warpgroups' column halves (same order on both sides).
           red[0][wg][r] = dD;
@@ -365,11 +367,9 @@ __global__ void __launch_bounds__(kBBThreads, 1)
       } else {
         uint32_t o_ds[CW / 2], o_ds2[CW / 2], o_ddp[CW / 2], o_p[CW / 2];
         if (need_mask)
-          q_ops<CW, true>(vs, vdds, vdp, vdpa, kc, row, sh.Tk, sh.causal, sc, sc2, lg, dv, dD, cq, o_ds, o_ds2,
-                          o_ddp, o_p);
+          q_ops<CW, true>(vs, vdds, vdp, vdpa, kc, klo, khi, sc, sc2, lg, dv, dD, cq, o_ds, o_ds2, o_ddp, o_p);
         else
-          q_ops<CW, false>(vs, vdds, vdp, vdpa, kc, row, sh.Tk, sh.causal, sc, sc2, lg, dv, dD, cq, o_ds, o_ds2,
-                           o_ddp, o_p);
+          q_ops<CW, false>(vs, vdds, vdp, vdpa, kc, klo, khi, sc, sc2, lg, dv, dD, cq, o_ds, o_ds2, o_ddp, o_p);
         if (j > 0) ok = mbar_wait_warp(&bar_ops_empty, (j - 1) & 1, &abort_flag);
         if (!ok) break;
         tc_fence_after();
@@ -383,8 +383,19 @@ __global__ void __launch_bounds__(kBBThreads, 1)
         warp_arrive(&bar_ops_full);
       }
     }
-    if (ok) ok = mbar_wait_warp(&bar_acc, 0, &abort_flag);
-    if (ok) {
+    if (ok && n == 0) {
+      // No key tile: every output of these rows is zero.
+      if (row_ok) {
+        zero_row_global<HD>((wg == 0 ? a.dq2 : a.ddo) + row_offset(sh.sq, b, row, h));
+        if (wg == 0) {
+          a.dd[vi] = 0.f;
+          a.bv[vi] = 0.f;
+        }
+      }
+    } else if (ok) {
+      ok = mbar_wait_warp(&bar_acc, 0, &abort_flag);
+    }
+    if (ok && n > 0) {
       tc_fence_after();
       const int srow = row_ok ? row : 0;
       if (wg == 0) {
@@ -449,8 +460,8 @@ struct KPass {
 //   vs = S - L/scale,  vdds = ddS/scale - dD/scale,  vdp = dP - D,  vdpa = dPa - c.
 template <int CW, bool MASK>
 __device__ __forceinline__ void k_ops(const uint32_t (&vs)[CW], const uint32_t (&vdds)[CW],
-                                      const uint32_t (&vdp)[CW], const uint32_t (&vdpa)[CW], int qc, int key, int tq,
-                                      int causal, float sc, float sc2, uint32_t (&o_ds)[CW / 2],
+                                      const uint32_t (&vdp)[CW], const uint32_t (&vdpa)[CW], int qc, int qlo, int qhi,
+                                      float sc, float sc2, uint32_t (&o_ds)[CW / 2],
                                       uint32_t (&o_ds2)[CW / 2], uint32_t (&o_ddp)[CW / 2]) {
 #pragma unroll
   for (int i = 0; i < CW; i += 2) {
@@ -459,7 +470,7 @@ __device__ __forceinline__ void k_ops(const uint32_t (&vs)[CW], const uint32_t (
     for (int e = 0; e < 2; ++e) {
       const int c = i + e;
       float s = __uint_as_float(vs[c]) * sc2;
-      if (MASK && (qc + c >= tq || (causal && qc + c < key))) s = -INFINITY;
+      if (MASK && (qc + c > qhi || qc + c < qlo)) s = -INFINITY;
       const float p = ex2(s);
       const float u = __uint_as_float(vdds[c]) * sc;  // ddS - dD
       const float dpd = __uint_as_float(vdp[c]);      // dP - D
@@ -488,9 +499,7 @@ __device__ __forceinline__ KItem k_item(const AttnShape& sh, int w, int bn) {
   it.hk = rem % sh.Hk;
   it.b = rem / sh.Hk;
   it.k0 = kt * kBM;
-  const int nq_tiles = (sh.Tq + bn - 1) / bn;
-  it.qt_begin = sh.causal ? it.k0 / bn : 0;
-  it.n = nq_tiles > it.qt_begin ? nq_tiles - it.qt_begin : 0;
+  it.n = query_tiles(sh, it.k0, kBM, bn, &it.qt_begin);  // query tiles that see any of these keys
   it.total = it.n * sh.G;
   return it;
 }
@@ -630,7 +639,8 @@ __global__ void __launch_bounds__(kBBThreads, 1)
           const bool v = q0 + lane + 32 * k < sh.Tq;
           const float lse = raw[k][0], dl = raw[k][1], ddl = raw[k][2];
           const int r = lane + 32 * k;
-          store_bias_row(bias, r, v ? -lse * inv_scale : 0.f);                   // S - L/scale
+          // L = -inf: the query sees no key and all its elements are masked.
+          store_bias_row(bias, r, (v && lse > -INFINITY) ? -lse * inv_scale : 0.f);  // S - L/scale
           store_bias_row(bias, BN + r, v ? -ddl * inv_scale : 0.f);              // ddS/scale - dD/scale
           store_bias_row(bias, 2 * BN + r, v ? -dl : 0.f);                       // dP - D
           store_bias_row(bias, 3 * BN + r, v ? -fmaf(ddl, dl, raw[k][3]) : 0.f); // dPa - c, c = dD D + B
@@ -757,6 +767,7 @@ __global__ void __launch_bounds__(kBBThreads, 1)
       const KItem w = k_item(sh, wi, BN);
       const int key = w.k0 + r;
       const bool key_ok = key < sh.Tk;
+      const int qhi = query_hi(sh, key), qlo = query_lo(sh, key);  // queries that see this key
       const int skey = key_ok ? key : 0;
       __nv_bfloat16* dst = (wg == 0 ? a.dk2 : a.dv2) + row_offset(sh.sk, w.b, skey, w.hk);
       if (w.total == 0) {
@@ -780,12 +791,12 @@ __global__ void __launch_bounds__(kBBThreads, 1)
         reg_fence(vdp);
         reg_fence(vdpa);
         warp_arrive(&bar_sc_empty);
-        const bool need_mask = (qc + CW > sh.Tq) || (sh.causal && qc < key);
+        const bool need_mask = qc + CW - 1 > qhi || qc < qlo;
         uint32_t o_ds[CW / 2], o_ds2[CW / 2], o_ddp[CW / 2];
         if (need_mask)
-          k_ops<CW, true>(vs, vdds, vdp, vdpa, qc, key, sh.Tq, sh.causal, sc, sc2, o_ds, o_ds2, o_ddp);
+          k_ops<CW, true>(vs, vdds, vdp, vdpa, qc, qlo, qhi, sc, sc2, o_ds, o_ds2, o_ddp);
         else
-          k_ops<CW, false>(vs, vdds, vdp, vdpa, qc, key, sh.Tq, sh.causal, sc, sc2, o_ds, o_ds2, o_ddp);
+          k_ops<CW, false>(vs, vdds, vdp, vdpa, qc, qlo, qhi, sc, sc2, o_ds, o_ds2, o_ddp);
         if (gt > 0) ok = mbar_wait_warp(&bar_ops_empty, (gt - 1) & 1, &abort_flag);
         if (!ok) break;
         tc_fence_after();

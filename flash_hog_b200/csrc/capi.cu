@@ -116,8 +116,14 @@ int validate(const fh_attn_dims* d, AttnShape* out, float scale, int causal) {
   out->Tk = d->seq_k;
   out->sq = Strides3{d->q.batch, d->q.seq, d->q.head};
   out->sk = Strides3{d->k.batch, d->k.seq, d->k.head};
+  if (causal < 0 || causal > 2)
+    return fail(kInvalidArgument, "causal must be 0 (no mask), 1 (top-left) or 2 (bottom-right)");
+  if (d->window < 0) return fail(kInvalidArgument, "window must be >= 0");
+  if (d->window > 0 && !causal) return fail(kInvalidArgument, "a sliding window needs a causal mask");
   out->scale = scale;
   out->causal = causal ? 1 : 0;
+  out->diag = causal == 2 ? d->seq_k - d->seq_q : 0;
+  out->window = d->window;
   return kOk;
 }
 

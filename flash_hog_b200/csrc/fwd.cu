@@ -96,15 +96,20 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   const int h = blockIdx.x, b = blockIdx.y;
   const int qt = gridDim.z - 1 - blockIdx.z;  // longest causal rows first
   const int q0 = qt * kFwdRows;
-  // Key tiles of each query tile (tile B may lie past the last query row).
-  int nt[2];
+  // Key tiles of each query tile: nt[t] tiles from key tile jt[t] (0 when the
+  // tile lies past the last query row or sees no key). The ring streams the
+  // union [jlo, jlo + n); tile t joins at ring position at[t].
+  int nt[2], jt[2], at[2];
+#pragma unroll
+  for (int t = 0; t < 2; ++t) nt[t] = key_tiles(sh, q0 + t * kBM, kBM, BN, &jt[t]);
+  const int jlo = nt[0] > 0 ? (nt[1] > 0 ? min(jt[0], jt[1]) : jt[0]) : jt[1];
+  int jhi = jlo;
 #pragma unroll
   for (int t = 0; t < 2; ++t) {
-    const int r0 = q0 + t * kBM;
-    const int kv_end = sh.causal ? min(sh.Tk, r0 + kBM) : sh.Tk;
-    nt[t] = r0 < sh.Tq ? (kv_end + BN - 1) / BN : 0;
+    if (nt[t] > 0) jhi = max(jhi, jt[t] + nt[t]);
+    at[t] = jt[t] - jlo;
   }
-  const int n = max(nt[0], nt[1]);  // key tiles streamed (>= 1)
+  const int n = jhi - jlo;  // key tiles streamed (0 if no row sees a key)
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
@@ -145,8 +150,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         }
         uint8_t* slot = s_ring + s * G::SLOT;
         mbar_arrive_expect_tx(&bar_full[s], G::SLOT);
-        tma_rows<HD>(slot, &tm_k, &bar_full[s], j * BN, BN, h / sh.G, b);
-        tma_rows<HD>(slot + G::STR, &tm_v, &bar_full[s], j * BN, BN, h / sh.G, b);
+        tma_rows<HD>(slot, &tm_k, &bar_full[s], (jlo + j) * BN, BN, h / sh.G, b);
+        tma_rows<HD>(slot + G::STR, &tm_v, &bar_full[s], (jlo + j) * BN, BN, h / sh.G, b);
         issued = j + 1;
       }
       // Every issued copy must land before this CTA's shared memory is released.
@@ -175,46 +180,52 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       umma_commit_w(&bar_s_full[t]);
       return true;
     };
+    // Ring position j holds key tile jlo + j; tile t's own step is u = j - at[t].
     bool ok = mbar_wait_warp(&bar_q, 0, &abort_flag);
     for (int t = 0; ok && t < 2; ++t)
-      if (nt[t] > 0) ok = issue_s(t, 0);
+      if (nt[t] > 0 && at[t] == 0) ok = issue_s(t, 0);
     for (int j = 0; ok && SEP_P && j < n; ++j) {
-      // Separate P: S(j+1) as soon as S(j) has been loaded, then the products.
-#pragma unroll 1
+      // Separate P: S(u+1) as soon as S(u) has been loaded, then the products.
+#pragma unroll
       for (int t = 0; ok && t < 2; ++t) {
-        if (j + 1 >= nt[t]) continue;
-        ok = mbar_wait_warp(&bar_s_empty[t], j & 1, &abort_flag) && issue_s(t, j + 1);
+        const int u = j - at[t];
+        if (u + 1 < 0 || u + 1 >= nt[t]) continue;
+        if (u >= 0) ok = mbar_wait_warp(&bar_s_empty[t], u & 1, &abort_flag);
+        ok = ok && issue_s(t, j + 1);
       }
-#pragma unroll 1
+#pragma unroll
       for (int t = 0; ok && t < 2; ++t) {
-        if (j >= nt[t]) continue;
-        if (!mbar_wait_warp(&bar_p_full[t], j & 1, &abort_flag)) {
+        const int u = j - at[t];
+        if (u < 0 || u >= nt[t]) continue;
+        if (!mbar_wait_warp(&bar_p_full[t], u & 1, &abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
         umma_chain_ts_w<KO>(tmem + G::C_O + t * HD, tmem + G::C_P + t * (BN / 2), b_v + (j % ST) * kSlot, id_o,
-                            j > 0);
+                            u > 0);
         umma_commit_w(&bar_p_free[t]);
-        if (j + 1 == nt[t]) umma_commit_w(&bar_o_done[t]);
+        if (u + 1 == nt[t]) umma_commit_w(&bar_o_done[t]);
       }
       if (ok) umma_commit_w(&bar_empty[j % ST]);
     }
     for (int j = 0; ok && !SEP_P && j < n; ++j) {
-#pragma unroll 1
-      for (int t = 0; t < 2; ++t) {
-        if (j >= nt[t]) continue;
-        if (!mbar_wait_warp(&bar_p_full[t], j & 1, &abort_flag)) {
+#pragma unroll
+      for (int t = 0; ok && t < 2; ++t) {
+        const int u = j - at[t];
+        if (u == -1 && nt[t] > 0) {  // the tile's first key tile is the next one
+          ok = issue_s(t, j + 1);
+          continue;
+        }
+        if (u < 0 || u >= nt[t]) continue;
+        if (!mbar_wait_warp(&bar_p_full[t], u & 1, &abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        umma_chain_ts_w<KO>(tmem + G::C_O + t * HD, tmem + t * BN, b_v + (j % ST) * kSlot, id_o, j > 0);
-        if (j + 1 < nt[t]) {
-          if (!issue_s(t, j + 1)) {
-            ok = false;
-            break;
-          }
+        umma_chain_ts_w<KO>(tmem + G::C_O + t * HD, tmem + t * BN, b_v + (j % ST) * kSlot, id_o, u > 0);
+        if (u + 1 < nt[t]) {
+          ok = issue_s(t, j + 1);
         } else {
           umma_commit_w(&bar_o_done[t]);
         }
@@ -228,7 +239,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     const int r = (warp & 3) * 32 + lane;         // TMEM lane = query row inside the tile
     const int row = q0 + t * kBM + r;
     const bool row_ok = row < sh.Tq;
-    const int nj = nt[t];
+    int jt0;  // first key tile of this warpgroup's query tile
+    const int nj = key_tiles(sh, q0 + t * kBM, kBM, BN, &jt0);
+    const int khi = key_hi(sh, row), klo = key_lo(sh, row);  // this row's visible keys
     const float sc2 = sh.scale * kLog2e;
     const uint32_t lane_base = tmem + tmem_lane_base(warp & 3);
     const uint32_t tcol = lane_base + t * BN;
@@ -236,7 +249,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     float m_used = -INFINITY, l = 0.f;  // running maximum (log2 domain) and the sum against it
     bool ok = true;
     for (int j = 0; j < nj; ++j) {
-      const int k0 = j * BN;
+      const int k0 = (jt0 + j) * BN;
       ok = mbar_wait_warp(&bar_s_full[t], j & 1, &abort_flag);
       if (!ok) break;
       tc_fence_after();
@@ -247,12 +260,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 #pragma unroll
       for (int i = 0; i < BN; ++i) asm volatile("" : "+r"(v[i])::"memory");
       if constexpr (G::SEP_P) fwd_warp_arrive(&bar_s_empty[t]);  // S(j+1) may be computed now
-      const bool need_mask = (k0 + BN > sh.Tk) || (sh.causal && k0 + BN - 1 > row);
-      if (need_mask) {
-        const int lim = sh.causal ? min(sh.Tk, row + 1) : sh.Tk;  // keys [k0, lim) are visible
+      if (k0 + BN - 1 > khi || k0 < klo) {
 #pragma unroll
         for (int i = 0; i < BN; ++i)
-          if (k0 + i >= lim) v[i] = __float_as_uint(-INFINITY);
+          if (k0 + i > khi || k0 + i < klo) v[i] = __float_as_uint(-INFINITY);
       }
       // Row maximum of the raw scores (the scale is positive), eight independent chains.
       float mx[8];
@@ -287,7 +298,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       };
       // P over S: O is stable now -- S(j) was issued after O += P(j-1) V_{j-1}, so
       // its completion (just waited for) implies that update's.
-      if (!G::SEP_P && f != 1.f) rescale_o();
+      // The TMEM loads and stores of a rescale are warp-collective: the warp rescales
+      // together when any of its rows needs it (the others multiply by f = 1).
+      const bool warp_rescale = __any_sync(0xffffffffu, f != 1.f);
+      if (!G::SEP_P && warp_rescale) rescale_o();
       const float base = (m_used == -INFINITY) ? 0.f : m_used;
       uint32_t pk[BN / 2];
       float ps[4] = {0.f, 0.f, 0.f, 0.f};
@@ -305,7 +319,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           ok = mbar_wait_warp(&bar_p_free[t], (j - 1) & 1, &abort_flag);
           if (!ok) break;
           tc_fence_after();
-          if (f != 1.f) rescale_o();
+          if (warp_rescale) rescale_o();
         }
         pcol = lane_base + G::C_P + t * (BN / 2);
       }
@@ -331,6 +345,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         if (row_ok) store_bf16x16(dst + c, x);
       }
       if (row_ok) a.lse[stat_index(b, h, row, sh.H, sh.Tq)] = (m_used + log2f(l)) * kLn2;
+    } else if (ok && row_ok) {
+      // No key tile for these rows: O = 0 and L = -inf (no visible key).
+      zero_row_global<HD>(a.o + row_offset(sh.sq, b, row, h));
+      a.lse[stat_index(b, h, row, sh.H, sh.Tq)] = -INFINITY;
     } else if (!ok && (threadIdx.x & 127) == 0) {
       raise_error(a.status, &abort_flag, kDevTimeoutMma);
     }

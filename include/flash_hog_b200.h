@@ -22,8 +22,14 @@
  *    contiguous, the layout of the cuDNN log-sum-exp the reference saves
  *    (flash_hog/jax/_attention_impl.py:114-139). lse is the natural-log
  *    log-sum-exp of the scaled, masked scores.
- *  - causal != 0 applies the top-left mask (query i sees keys j <= i), the mask
- *    of flash_hog/jax/_pallas_gpu_kernel.py:37-41.
+ *  - causal = 1 applies the top-left mask (query i sees keys j <= i), the mask
+ *    of flash_hog/jax/_pallas_gpu_kernel.py:37-41; causal = 2 the bottom-right
+ *    one (query i sees keys j <= i + seq_k - seq_q), the alignment of the
+ *    reference's JAX statements (flash_hog/_jax_refs/jax_impl.py:104-109), which
+ *    also take a sliding window: fh_attn_dims.window = W > 0 further limits
+ *    query i to the W keys ending at its diagonal. causal = 0: no mask (window
+ *    must be 0). A query that sees no key at all (bottom-right with seq_q >
+ *    seq_k) gets o = 0, lse = -inf and zero gradients.
  *  - head_dim is 64 or 128; seq_q, seq_k >= 1 (no divisibility requirement:
  *    ragged edges are masked); heads a multiple of kv_heads (grouped-query
  *    attention; key-side tensors and dk, dv, dk2, dv2 have kv_heads heads).
@@ -76,6 +82,11 @@ typedef struct fh_attn_dims {
    * heads; query head n attends with key/value head n / (heads / kv_heads), the
    * reference's "(kv_heads group)" grouping (flash_hog/jax/_pallas_gpu_kernel.py:106-107). */
   int32_t kv_heads;
+  /* Sliding-window length of a causal mask (0 = unlimited): query i sees keys j
+   * with diag_i - W < j <= diag_i, where diag_i = i (causal = 1) or
+   * i + seq_k - seq_q (causal = 2) -- get_mask_bottom_right's
+   * (qi >= kj) & (qi - kj < sliding_window_length), flash_hog/_jax_refs/jax_impl.py:104-109. */
+  int32_t window;
 } fh_attn_dims;
 
 /* Forward: o = softmax(scale * q k^T + mask) v, lse = logsumexp(scale * q k^T + mask).
@@ -213,7 +224,7 @@ int fh_abi_version(void);
  * reads it before and after a timed region to report its kernel launches. */
 unsigned long long fh_launch_count(void);
 
-#define FH_ABI_VERSION 3
+#define FH_ABI_VERSION 4
 
 #ifdef __cplusplus
 }

@@ -49,9 +49,19 @@ def default_scale(head_dim: int) -> float:
     return head_dim ** -0.5
 
 
-def causal_mask(nq: int, nk: int) -> np.ndarray:
-    """Top-left causal mask, True where the score is kept (``_pallas_gpu_kernel.py:37-41``)."""
-    return np.arange(nq)[:, None] >= np.arange(nk)[None, :]
+def causal_mask(nq: int, nk: int, causal=1, window: int = 0) -> np.ndarray:
+    """Causal band mask, True where the score is kept: query i sees key j iff
+    j <= i + diag and (window == 0 or i + diag - j < window), with diag = 0 for
+    ``causal`` 1 / True (top-left, ``_pallas_gpu_kernel.py:37-41``) and nk - nq for
+    ``causal`` 2 (bottom-right: ``get_mask_bottom_right``'s ``qi = qi + ks - qs``,
+    ``(qi >= kj) & (qi - kj < sliding_window_length)``,
+    ``flash_hog/_jax_refs/jax_impl.py:104-109``)."""
+    qi = np.arange(nq)[:, None] + (nk - nq if int(causal) == 2 else 0)
+    kj = np.arange(nk)[None, :]
+    keep = qi >= kj
+    if window:
+        keep &= (qi - kj) < window
+    return keep
 
 
 def _heads(x: np.ndarray) -> np.ndarray:
@@ -84,39 +94,51 @@ def _group(q, k) -> int:
     return q.shape[2] // k.shape[2]
 
 
-def _scores(q, k, scale, causal):
+def _scores(q, k, scale, causal, window=0):
     s = np.einsum("bhqd,bhkd->bhqk", q, k) * scale
     if causal:
-        s = np.where(causal_mask(q.shape[2], k.shape[2]), s, -np.inf)
+        s = np.where(causal_mask(q.shape[2], k.shape[2], causal, window), s, -np.inf)
     return s
+
+
+def _probs(s, lse):
+    """P = exp(S - L); a query that sees no key (L = -inf) has P = 0."""
+    lse = np.asarray(lse, np.float64)[..., None]
+    p = np.exp(s - np.where(np.isfinite(lse), lse, 0.0))
+    return np.where(np.isfinite(s), p, 0.0)
 
 
 # --------------------------------------------------------------------------------------
 # forward and first-order backward
 # --------------------------------------------------------------------------------------
 
-def attention_fwd(q, k, v, scale=None, causal=False):
+def attention_fwd(q, k, v, scale=None, causal=False, window=0):
     """O = softmax(scale*Q K^T + mask) V and L = logsumexp(scale*Q K^T + mask).
 
     Restates the forward the reference delegates to cuDNN
     (``flash_hog/jax/_attention_impl.py:224-239``; semantics of
     ``jax.nn.dot_product_attention``, ``tests/test_jax_fhog.py:14-15``).
-    Returns (O BTNH, L (B,N,T)).
+    Returns (O BTNH, L (B,N,T)). ``causal`` 1 (or True) masks top-left, 2 bottom-right;
+    ``window`` > 0 is a sliding window (``causal_mask``). A query that sees no key
+    gets O = 0 and L = -inf (the kernels' convention; softmax over an empty set is
+    undefined, and the reference's XLA statement gives NaN there).
     """
     scale = default_scale(q.shape[-1]) if scale is None else scale
     g = _group(q, k)
     qh, kh, vh = _heads(q), _expand(_heads(k), g), _expand(_heads(v), g)
-    s = _scores(qh, kh, scale, causal)
+    s = _scores(qh, kh, scale, causal, window)
     m = s.max(axis=-1, keepdims=True)
+    m = np.where(np.isfinite(m), m, 0.0)
     e = np.exp(s - m)
     den = e.sum(axis=-1, keepdims=True)
-    p = e / den
+    p = e / np.where(den > 0, den, 1.0)
     o = np.einsum("bhqk,bhkd->bhqd", p, vh)
-    lse = (m + np.log(den))[..., 0]
+    with np.errstate(divide="ignore"):
+        lse = np.where(den > 0, m + np.log(den), -np.inf)[..., 0]
     return _btnh(o), lse
 
 
-def attention_bwd(q, k, v, o, lse, do, scale=None, causal=False):
+def attention_bwd(q, k, v, o, lse, do, scale=None, causal=False, window=0):
     """First-order backward (dQ, dK, dV) from the saved (O, L).
 
     Restates ``flash_hog/_jax_refs/jax_impl.py:142-191`` (``attn_bwd``) with
@@ -127,8 +149,8 @@ def attention_bwd(q, k, v, o, lse, do, scale=None, causal=False):
     g = _group(q, k)
     qh, oh, doh = map(_heads, (q, o, do))
     kh, vh = (_expand(_heads(x), g) for x in (k, v))
-    s = _scores(qh, kh, scale, causal)
-    p = np.exp(s - np.asarray(lse, np.float64)[..., None])
+    s = _scores(qh, kh, scale, causal, window)
+    p = _probs(s, lse)
     dp = np.einsum("bhqd,bhkd->bhqk", doh, vh)
     d = np.einsum("bhqd,bhqd->bhq", doh, oh)[..., None]
     ds = scale * p * (dp - d)
@@ -188,7 +210,7 @@ def bwdbwd_stats_jax_dtype_flow(q, k, v, o, lse, do, ddq, ddk, ddv, scale):
 # double backward: explicit formulas
 # --------------------------------------------------------------------------------------
 
-def bwdbwd_stats(q, k, v, o, lse, do, ddq, ddk, ddv, scale=None, causal=False, return_stats=False):
+def bwdbwd_stats(q, k, v, o, lse, do, ddq, ddk, ddv, scale=None, causal=False, return_stats=False, window=0):
     """Double backward (dQ', dK', dV', ddO) from the saved (O, L).
 
     Restates ``flash_hog/_jax_refs/jax_impl.py:273-336`` (``attn_bwd_bwd_stats``),
@@ -212,8 +234,8 @@ def bwdbwd_stats(q, k, v, o, lse, do, ddq, ddk, ddv, scale=None, causal=False, r
     g = _group(q, k)
     qh, oh, doh, ddqh = map(_heads, (q, o, do, ddq))
     kh, vh, ddkh, ddvh = (_expand(_heads(x), g) for x in (k, v, ddk, ddv))
-    s = _scores(qh, kh, scale, causal)
-    p = np.exp(s - np.asarray(lse, np.float64)[..., None])
+    s = _scores(qh, kh, scale, causal, window)
+    p = _probs(s, lse)
     dp = np.einsum("bhqd,bhkd->bhqk", doh, vh)
     dds = scale * (np.einsum("bhqd,bhkd->bhqk", ddqh, kh) + np.einsum("bhqd,bhkd->bhqk", qh, ddkh))
     d = np.einsum("bhqd,bhqd->bhq", oh, doh)[..., None]
@@ -322,19 +344,20 @@ def bwdbwd_4pass(q, k, v, o, lse, do, ddq, ddk, ddv, scale=None, causal=False,
 # double backward: autodiff of naive attention (the "XLA reference" analogue)
 # --------------------------------------------------------------------------------------
 
-def _torch_attention(q, k, v, scale, causal):
+def _torch_attention(q, k, v, scale, causal, window=0):
+    """Naive attention in torch ops (every query must see at least one key)."""
     group = q.shape[2] // k.shape[2]
     if group > 1:  # query head n uses key head n // group; autograd sums the group
         k, v = k.repeat_interleave(group, dim=2), v.repeat_interleave(group, dim=2)
     s = torch.einsum("bqhd,bkhd->bhqk", q, k) * scale
     if causal:
-        keep = torch.ones(q.shape[1], k.shape[1], dtype=torch.bool).tril()
+        keep = torch.from_numpy(causal_mask(q.shape[1], k.shape[1], causal, window)).to(s.device)
         s = s.masked_fill(~keep, float("-inf"))
     p = torch.softmax(s, dim=-1)
     return torch.einsum("bhqk,bkhd->bqhd", p, v)
 
 
-def autograd_all(q, k, v, do, ddq, ddk, ddv, scale=None, causal=False):
+def autograd_all(q, k, v, do, ddq, ddk, ddv, scale=None, causal=False, window=0):
     """vjp-of-vjp of naive softmax attention, by torch autograd on the CPU.
 
     The analogue of the reference test oracle ``make_reference_dpa_bwd_bwd``
@@ -348,7 +371,7 @@ def autograd_all(q, k, v, do, ddq, ddk, ddv, scale=None, causal=False):
     scale = default_scale(q.shape[-1]) if scale is None else scale
     q, k, v, do = (t.detach().clone().requires_grad_(True) for t in (q, k, v, do))
     with torch.enable_grad():
-        o = _torch_attention(q, k, v, scale, causal)
+        o = _torch_attention(q, k, v, scale, causal, window)
         dq, dk, dv = torch.autograd.grad(o, (q, k, v), do, create_graph=True)
         dq2, dk2, dv2, ddo = torch.autograd.grad((dq, dk, dv), (q, k, v, do), (ddq, ddk, ddv))
     return dict(o=o.detach(), dq=dq.detach(), dk=dk.detach(), dv=dv.detach(),
@@ -359,7 +382,7 @@ def autograd_all(q, k, v, do, ddq, ddk, ddv, scale=None, causal=False):
 # forward mode: jvp of the forward and of the first-order backward
 # --------------------------------------------------------------------------------------
 
-def jvp_fwd(q, k, v, o, lse, tq, tk, tv, scale=None, causal=False):
+def jvp_fwd(q, k, v, o, lse, tq, tk, tv, scale=None, causal=False, window=0):
     """Forward tangents (tO, tL) of (O, L) along (tQ, tK, tV), in float64.
 
     No counterpart in the reference (reverse-mode rules only,
@@ -370,11 +393,11 @@ def jvp_fwd(q, k, v, o, lse, tq, tk, tv, scale=None, causal=False):
     """
     zero = np.zeros_like(np.asarray(q, np.float64))
     (_, _, _, to), (_, tl, _) = bwdbwd_stats(q, k, v, o, lse, zero, tq, tk, tv, scale=scale, causal=causal,
-                                              return_stats=True)
+                                              return_stats=True, window=window)
     return to, tl
 
 
-def jvp_bwd(q, k, v, o, lse, do, tq, tk, tv, tdo=None, scale=None, causal=False):
+def jvp_bwd(q, k, v, o, lse, do, tq, tk, tv, tdo=None, scale=None, causal=False, window=0):
     """Forward-mode derivative (tdQ, tdK, tdV) of the first-order backward, float64.
 
     The backward is grad_{Q,K,V} phi with phi = <O(Q, K, V), dO>, so
@@ -383,14 +406,14 @@ def jvp_bwd(q, k, v, o, lse, do, tq, tk, tv, tdo=None, scale=None, causal=False)
     backward (``bwdbwd_stats``) with (ddQ, ddK, ddV) = (tQ, tK, tV); J_O^T tdO
     is the first-order backward (``attention_bwd``) of tdO.
     """
-    dq2, dk2, dv2, _ = bwdbwd_stats(q, k, v, o, lse, do, tq, tk, tv, scale=scale, causal=causal)
+    dq2, dk2, dv2, _ = bwdbwd_stats(q, k, v, o, lse, do, tq, tk, tv, scale=scale, causal=causal, window=window)
     if tdo is None:
         return dq2, dk2, dv2
-    dq, dk, dv = attention_bwd(q, k, v, o, lse, tdo, scale=scale, causal=causal)
+    dq, dk, dv = attention_bwd(q, k, v, o, lse, tdo, scale=scale, causal=causal, window=window)
     return dq2 + dq, dk2 + dk, dv2 + dv
 
 
-def autograd_jvp(q, k, v, do, tq, tk, tv, tdo, scale=None, causal=False):
+def autograd_jvp(q, k, v, do, tq, tk, tv, tdo, scale=None, causal=False, window=0):
     """Forward-over-reverse derivatives of naive softmax attention by ``torch.func``
     (an independent statement of ``jvp_fwd`` / ``jvp_bwd``): returns
     ``dict(o, to, tlse, dq, dk, dv, tdq, tdk, tdv)`` for torch inputs (BTNH)."""
@@ -399,14 +422,14 @@ def autograd_jvp(q, k, v, do, tq, tk, tv, tdo, scale=None, causal=False):
     scale = default_scale(q.shape[-1]) if scale is None else scale
 
     def attn(q_, k_, v_):
-        return _torch_attention(q_, k_, v_, scale, causal)
+        return _torch_attention(q_, k_, v_, scale, causal, window)
 
     def lse_fn(q_, k_):
         group = q_.shape[2] // k_.shape[2]
         kk = k_.repeat_interleave(group, dim=2) if group > 1 else k_
         s = torch.einsum("bqhd,bkhd->bhqk", q_, kk) * scale
         if causal:
-            keep = torch.ones(q_.shape[1], kk.shape[1], dtype=torch.bool).tril()
+            keep = torch.from_numpy(causal_mask(q_.shape[1], kk.shape[1], causal, window))
             s = s.masked_fill(~keep, float("-inf"))
         return torch.logsumexp(s, dim=-1)
 

@@ -63,18 +63,21 @@ def _dims(**kw):
     d = dict(batch=1, heads=2, seq_q=128, seq_k=128, head_dim=64)
     d.update(kw)
     st = FhStrides(128 * 2 * 64, 2 * 64, 64)
-    return FhAttnDims(d["batch"], d["heads"], d["seq_q"], d["seq_k"], d["head_dim"], st, st)
+    return FhAttnDims(d["batch"], d["heads"], d["seq_q"], d["seq_k"], d["head_dim"], st, st, 0, d.get("window", 0))
 
 
-def _fwd(dims, ptr=64):
+def _fwd(dims, ptr=64, causal=1):
     from flash_hog_b200._capi import lib
 
     p = ctypes.c_void_p(ptr)
-    return lib().fh_attn_fwd(None, ctypes.byref(dims) if dims is not None else None, p, p, p, p, p, 0.125, 1)
+    return lib().fh_attn_fwd(None, ctypes.byref(dims) if dims is not None else None, p, p, p, p, p, 0.125, causal)
 
 
 def test_argument_validation_codes():
     assert _fwd(None) == 1                      # null dims
+    assert _fwd(_dims(), causal=3) == 1         # causal code outside 0..2
+    assert _fwd(_dims(window=-1)) == 1          # negative window
+    assert _fwd(_dims(window=8), causal=0) == 1  # a window needs a causal mask
     assert _fwd(_dims(head_dim=32)) == 2        # unsupported head_dim
     assert _fwd(_dims(seq_q=0)) == 1            # empty sequence
     assert _fwd(_dims(batch=0)) == 1
