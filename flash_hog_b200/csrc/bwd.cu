@@ -57,14 +57,27 @@ struct DqPass {
   static constexpr int STR_PANEL = BN * 128;
   static constexpr int SLOT = 2 * STR;                     // K, V
   static constexpr int SMEM = 1024 + 2 * RES + ST * SLOT;  // Q, dO, ring (O borrows the last slot)
-  // TMEM: one score buffer [S | dP] and one bf16 dS operand (BN/2 packed
-  // columns) per elementwise warpgroup, the dQ accumulator, then Q -- and dO at
-  // head_dim 64, where it fits -- as packed bf16 A operands of the score MMAs.
-  static constexpr bool DO_TMEM = HD == 64;
+  // Two layouts, both latency-bound loops made to overlap:
+  //  * head_dim 64 -- two CTAs per SM: one score buffer [S | dP] and one bf16 dS
+  //    operand shared by both elementwise warpgroups (each takes half the
+  //    columns of every tile), score MMAs from shared memory; 224 TMEM columns
+  //    and at most 93 registers a thread, so the two CTAs' tile loops (and one's
+  //    prologue and the other's tiles) hide each other's waits;
+  //  * head_dim 128 -- one CTA per SM: each warpgroup takes alternate key tiles
+  //    with its own score buffer and dS operand ("ping-pong"), so one computes
+  //    while the other waits; Q in TMEM as the A operand of S = Q K^T.
+  // TMEM: score buffers, the dQ accumulator, the dS operands (BN/2 packed
+  // columns each), then (ping-pong) Q as packed bf16.
+  static constexpr bool PP = HD == 128;
+  static constexpr int CTAS = PP ? 1 : 2;  // resident CTAs per SM
+  static constexpr int NBUF = PP ? 2 : 1;  // score buffers and dS operands
+  static constexpr int CW = PP ? BN : BN / 2;  // columns of a tile per elementwise thread
+  static constexpr int ARRIVALS = PP ? kBBEwWarps / 2 : kBBEwWarps;  // warps consuming one buffer
   static constexpr int C_S = 0, C_DP = BN, SCORE_COLS = 2 * BN, OPS_COLS = BN / 2;
-  static constexpr int C_DQ = 2 * SCORE_COLS, C_OPS = C_DQ + HD, C_QT = C_OPS + 2 * OPS_COLS, C_DOT = C_QT + HD / 2;
-  static constexpr int TMEM_COLS = 512;
-  static_assert(C_DOT + (DO_TMEM ? HD / 2 : 0) <= TMEM_COLS, "TMEM budget");
+  static constexpr int C_DQ = NBUF * SCORE_COLS, C_OPS = C_DQ + HD, C_QT = C_OPS + NBUF * OPS_COLS;
+  static constexpr int TMEM_COLS = PP ? 512 : 256;
+  static_assert(C_QT + (PP ? HD / 2 : 0) <= TMEM_COLS, "TMEM budget");
+  static_assert(CTAS * SMEM <= 228 * 1024 - CTAS * 2048, "shared memory of the resident CTAs");
   static_assert(RES <= SLOT, "O fits in one ring slot");
   static_assert(SMEM <= 232448, "shared memory budget");
   static_assert(HD % 64 == 0 && RES_PANEL == kBM * 128, "tile shapes");
@@ -89,7 +102,7 @@ __device__ __forceinline__ void dq_ops(const uint32_t (&vs)[CW], const uint32_t 
 }
 
 template <int HD>
-__global__ void __launch_bounds__(kBBThreads, 1)
+__global__ void __launch_bounds__(kBBThreads, DqPass<HD>::CTAS)
     bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
                   const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                   const __grid_constant__ CUtensorMap tm_o, const BwdArgs a) {
@@ -104,9 +117,8 @@ __global__ void __launch_bounds__(kBBThreads, 1)
   // use; the producer refills it only once every elementwise warp has read O.
   uint8_t* s_o = s_ring + (ST - 1) * G::SLOT;
   __shared__ uint64_t bar_res, bar_tres, bar_ofree, bar_dred, bar_full[ST], bar_empty[ST];
-  // Score buffer and dS operand w belong to elementwise warpgroup w, which
-  // takes key tiles w, w + 2, ...: the two warpgroups work on consecutive tiles
-  // independently, so one computes while the other waits for its scores.
+  // Ping-pong: score buffer and dS operand w belong to elementwise warpgroup w,
+  // which takes key tiles w, w + 2, ... Otherwise only index 0 is used.
   __shared__ uint64_t bar_sc_full[2], bar_sc_empty[2], bar_ops_full[2], bar_ops_empty[2], bar_acc;
   __shared__ float dred[2][kBM];  // partial rowsum(dO o O): warpgroup, row
   __shared__ uint32_t tmem_base;
@@ -132,8 +144,8 @@ __global__ void __launch_bounds__(kBBThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bar_sc_full[i], 1);
-      mbar_init(&bar_sc_empty[i], kBBEwWarps / 2);
-      mbar_init(&bar_ops_full[i], kBBEwWarps / 2);
+      mbar_init(&bar_sc_empty[i], G::ARRIVALS);
+      mbar_init(&bar_ops_full[i], G::ARRIVALS);
       mbar_init(&bar_ops_empty[i], 1);
     }
     mbar_init(&bar_acc, 1);
@@ -178,16 +190,16 @@ __global__ void __launch_bounds__(kBBThreads, 1)
     }
   } else if (warp == kBBWarpMma) {
     // ------------------------------ score MMA issuer ------------------------------
-    //   S = Q K^T,  dP = dO V^T   (Q, dO in TMEM; K, V K-major in the ring)
+    //   S = Q K^T,  dP = dO V^T   (K, V K-major in the ring; Q from TMEM when ping-ponging)
     constexpr int KS = HD / 16;
     const uint32_t id_s = idesc_bf16_f32(kBM, BN, false, false);
     const uint64_t b_ring = kdesc(s_ring);  // K of slot 0
-    const uint64_t a_do = kdesc(s_do);
+    const uint64_t a_q = kdesc(s_q), a_do = kdesc(s_do);
     constexpr uint64_t kSlot = G::SLOT >> 4, kStr = G::STR >> 4;
     bool ok = mbar_wait_warp(&bar_res, 0, &abort_flag) && mbar_wait_warp(&bar_tres, 0, &abort_flag);
     if (!ok && lane == 0) raise_error(a.status, &abort_flag, kDevTimeoutTmaFull);
     for (int it = 0; ok && it < n; ++it) {
-      const int s = it % ST, sb = it & 1, u = it >> 1;
+      const int s = it % ST, sb = G::PP ? (it & 1) : 0, u = G::PP ? (it >> 1) : it;
       if (!mbar_wait_warp(&bar_full[s], (it / ST) & 1, &abort_flag)) {
         if (lane == 0) raise_error(a.status, &abort_flag, kDevTimeoutTmaFull);
         break;
@@ -199,11 +211,11 @@ __global__ void __launch_bounds__(kBBThreads, 1)
       tc_fence_after();
       const uint64_t bk = b_ring + s * kSlot;
       const uint32_t tb = tmem + sb * G::SCORE_COLS;
-      umma_chain_tsk_w<KS, G::STR_PANEL>(tb + G::C_S, tmem + G::C_QT, bk, id_s, false);
-      if constexpr (G::DO_TMEM)
-        umma_chain_tsk_w<KS, G::STR_PANEL>(tb + G::C_DP, tmem + G::C_DOT, bk + kStr, id_s, false);
+      if constexpr (G::PP)
+        umma_chain_tsk_w<KS, G::STR_PANEL>(tb + G::C_S, tmem + G::C_QT, bk, id_s, false);
       else
-        umma_chain_w<KS, G::RES_PANEL, G::STR_PANEL, false>(tb + G::C_DP, a_do, bk + kStr, id_s, false);
+        umma_chain_w<KS, G::RES_PANEL, G::STR_PANEL, false>(tb + G::C_S, a_q, bk, id_s, false);
+      umma_chain_w<KS, G::RES_PANEL, G::STR_PANEL, false>(tb + G::C_DP, a_do, bk + kStr, id_s, false);
       umma_commit_w(&bar_sc_full[sb]);
     }
   } else if (warp == kBBWarpMmaOut) {
@@ -214,8 +226,8 @@ __global__ void __launch_bounds__(kBBThreads, 1)
     constexpr uint64_t kSlot = G::SLOT >> 4;
     bool ok = true;
     for (int j = 0; j < n; ++j) {
-      const int w = j & 1;
-      if (!mbar_wait_warp(&bar_ops_full[w], (j >> 1) & 1, &abort_flag)) {
+      const int w = G::PP ? (j & 1) : 0;
+      if (!mbar_wait_warp(&bar_ops_full[w], (G::PP ? (j >> 1) : j) & 1, &abort_flag)) {
         if (lane == 0) raise_error(a.status, &abort_flag, kDevTimeoutEpilogue);
         ok = false;
         break;
@@ -242,10 +254,10 @@ __global__ void __launch_bounds__(kBBThreads, 1)
     bool ok = mbar_wait_warp(&bar_res, 0, &abort_flag);
     float dv = 0.f;
     if (ok) {
-      // This warpgroup's half of the head_dim columns of Q (and dO) into TMEM.
-      row_to_tmem<HD / 2>(s_q, r, wg * (HD / 2), lane_t + G::C_QT);
-      if constexpr (G::DO_TMEM) row_to_tmem<HD / 2>(s_do, r, wg * (HD / 2), lane_t + G::C_DOT);
-      tmem_wait_st();
+      if constexpr (G::PP) {  // this warpgroup's half of the head_dim columns of Q into TMEM
+        row_to_tmem<HD / 2>(s_q, r, wg * (HD / 2), lane_t + G::C_QT);
+        tmem_wait_st();
+      }
       warp_arrive(&bar_tres);
       // D = rowsum(dO o O) of this row: each warpgroup sums half the columns.
       dred[wg][r] = rowdot_share<HD>(s_o, s_do, r, wg);
@@ -255,34 +267,65 @@ __global__ void __launch_bounds__(kBBThreads, 1)
       dv = dred[0][r] + dred[1][r];
       if (ok && wg == 0 && row_ok) a.delta[vi] = dv;
     }
-    const uint32_t tb = tmem + wg * G::SCORE_COLS;
-    const uint32_t to = lane_t + G::C_OPS + wg * G::OPS_COLS;
-    for (int j = wg; ok && j < n; j += 2) {
-      const int u = j >> 1;  // earlier tiles of this warpgroup
-      ok = mbar_wait_warp(&bar_sc_full[wg], u & 1, &abort_flag);
-      if (!ok) break;
-      tc_fence_after();
-      uint32_t vs[BN], vdp[BN];
-      tmem_share<BN>(tb, warp, G::C_S, vs);
-      tmem_share<BN>(tb, warp, G::C_DP, vdp);
-      tmem_wait_ld();
-      reg_fence(vs);
-      reg_fence(vdp);
-      warp_arrive(&bar_sc_empty[wg]);  // the tensor core may reuse this score buffer now
-      const int kc = (j0 + j) * BN;
-      const bool need_mask = kc + BN - 1 > khi || kc < klo;
-      uint32_t o_ds[BN / 2];
-      if (need_mask)
-        dq_ops<BN, true>(vs, vdp, kc, klo, khi, sc2, lg, dv, o_ds);
-      else
-        dq_ops<BN, false>(vs, vdp, kc, klo, khi, sc2, lg, dv, o_ds);
-      if (u > 0) ok = mbar_wait_warp(&bar_ops_empty[wg], (u - 1) & 1, &abort_flag);
-      if (!ok) break;
-      tc_fence_after();
-      tmem_st16(to, *reinterpret_cast<const uint32_t(*)[16]>(&o_ds[0]));
-      tmem_st16(to + 16, *reinterpret_cast<const uint32_t(*)[16]>(&o_ds[16]));
-      tmem_wait_st();
-      warp_arrive(&bar_ops_full[wg]);
+    if constexpr (G::PP) {
+      const uint32_t tb = tmem + wg * G::SCORE_COLS;
+      const uint32_t to = lane_t + G::C_OPS + wg * G::OPS_COLS;
+      for (int j = wg; ok && j < n; j += 2) {
+        const int u = j >> 1;  // earlier tiles of this warpgroup
+        ok = mbar_wait_warp(&bar_sc_full[wg], u & 1, &abort_flag);
+        if (!ok) break;
+        tc_fence_after();
+        uint32_t vs[BN], vdp[BN];
+        tmem_share<BN>(tb, warp, G::C_S, vs);
+        tmem_share<BN>(tb, warp, G::C_DP, vdp);
+        tmem_wait_ld();
+        reg_fence(vs);
+        reg_fence(vdp);
+        warp_arrive(&bar_sc_empty[wg]);  // the tensor core may reuse this score buffer now
+        const int kc = (j0 + j) * BN;
+        const bool need_mask = kc + BN - 1 > khi || kc < klo;
+        uint32_t o_ds[BN / 2];
+        if (need_mask)
+          dq_ops<BN, true>(vs, vdp, kc, klo, khi, sc2, lg, dv, o_ds);
+        else
+          dq_ops<BN, false>(vs, vdp, kc, klo, khi, sc2, lg, dv, o_ds);
+        if (u > 0) ok = mbar_wait_warp(&bar_ops_empty[wg], (u - 1) & 1, &abort_flag);
+        if (!ok) break;
+        tc_fence_after();
+        tmem_st16(to, *reinterpret_cast<const uint32_t(*)[16]>(&o_ds[0]));
+        tmem_st16(to + 16, *reinterpret_cast<const uint32_t(*)[16]>(&o_ds[16]));
+        tmem_wait_st();
+        warp_arrive(&bar_ops_full[wg]);
+      }
+    } else {
+      // Shared tiles: warpgroup wg takes columns [CW wg, CW wg + CW) of every tile.
+      constexpr int CW = G::CW;
+      const int cb = wg * CW;
+      for (int j = 0; ok && j < n; ++j) {
+        ok = mbar_wait_warp(&bar_sc_full[0], j & 1, &abort_flag);
+        if (!ok) break;
+        tc_fence_after();
+        uint32_t vs[CW], vdp[CW];
+        tmem_share<CW>(tmem, warp, G::C_S + cb, vs);
+        tmem_share<CW>(tmem, warp, G::C_DP + cb, vdp);
+        tmem_wait_ld();
+        reg_fence(vs);
+        reg_fence(vdp);
+        warp_arrive(&bar_sc_empty[0]);
+        const int kc = (j0 + j) * BN + cb;  // first key of this thread's columns
+        const bool need_mask = kc + CW - 1 > khi || kc < klo;
+        uint32_t o_ds[CW / 2];
+        if (need_mask)
+          dq_ops<CW, true>(vs, vdp, kc, klo, khi, sc2, lg, dv, o_ds);
+        else
+          dq_ops<CW, false>(vs, vdp, kc, klo, khi, sc2, lg, dv, o_ds);
+        if (j > 0) ok = mbar_wait_warp(&bar_ops_empty[0], (j - 1) & 1, &abort_flag);
+        if (!ok) break;
+        tc_fence_after();
+        tmem_st_ops(lane_t + G::C_OPS + (CW / 2) * wg, o_ds);
+        tmem_wait_st();
+        warp_arrive(&bar_ops_full[0]);
+      }
     }
     if (ok && n == 0) {
       // No key tile: dQ = 0 (plus the addend).
