@@ -342,7 +342,7 @@ __global__ void __launch_bounds__(kBBThreads, DqPass<HD>::CTAS)
       const size_t off = row_offset(sh.sq, b, srow, h) + wg * (HD / 2);
       tmem_row_to_global<HD / 2>(tmem, warp, G::C_DQ + wg * (HD / 2), a.dq + off, row_ok, sh.scale,
                                  a.dq_acc ? a.dq_acc + off : nullptr);
-    } else if (threadIdx.x == kBBFirstEwWarp * 32) {
+    } else if (!ok && threadIdx.x == kBBFirstEwWarp * 32) {
       raise_error(a.status, &abort_flag, kDevTimeoutMma);
     }
   }
@@ -358,8 +358,19 @@ __global__ void __launch_bounds__(kBBThreads, DqPass<HD>::CTAS)
 
 template <int HD>
 struct DkvPass {
+  // Two layouts:
+  //  * head_dim 64 -- two CTAs per SM: one score buffer [S^T | dP^T] into which
+  //    the elementwise warps write the bf16 operands P^T and dS^T back once both
+  //    warpgroups have read their scores; K and V stay in shared memory; 256 TMEM
+  //    columns. One warp issues every MMA, so each tile's operand products are
+  //    ordered before the next tile's bias MMA overwrites the buffer. The two
+  //    CTAs hide each other's waits;
+  //  * head_dim 128 -- one CTA per SM: separate operand columns, K in TMEM as the
+  //    A operand of S^T = K Q^T.
+  static constexpr bool TWO = HD == 64;
+  static constexpr int CTAS = TWO ? 2 : 1;
   static constexpr int BN = 64;  // queries per streamed tile
-  static constexpr int ST = 4;
+  static constexpr int ST = TWO ? 3 : 4;
   static constexpr int CW = BN / 2;
   static constexpr int RES = kBM * HD * 2;
   static constexpr int RES_PANEL = kBM * 128;
@@ -373,16 +384,16 @@ struct DkvPass {
   static constexpr int ONES = kBM * BIAS_ROW;  // resident A operand: (1, 1, 0, ...) per key row
   static constexpr int SLOT = 2 * STR + BIAS;  // Q, dO, biases
   static constexpr int SMEM = 1024 + 2 * RES + ONES + ST * SLOT;
-  // TMEM: score buffers [S^T | dP^T] (two at head_dim 64, one at 128), the dK
-  // and dV accumulators, the bf16 operands P^T and dS^T, then K -- and V at
-  // head_dim 64 -- as packed bf16 A operands of the score MMAs.
-  static constexpr bool V_TMEM = HD == 64;
-  static constexpr int NB = HD == 64 ? 2 : 1;
-  static constexpr int C_S = 0, C_DP = BN, SCORE_COLS = 2 * BN;
-  static constexpr int C_DK = NB * SCORE_COLS, C_DV = C_DK + HD, C_OPS = C_DV + HD, OPS_COLS = BN / 2;
-  static constexpr int C_KT = C_OPS + 2 * OPS_COLS, C_VT = C_KT + HD / 2;
-  static constexpr int TMEM_COLS = 512;
-  static_assert(C_VT + (V_TMEM ? HD / 2 : 0) <= TMEM_COLS, "TMEM budget");
+  // TMEM: the score buffer [S^T | dP^T], the dK and dV accumulators, the bf16
+  // operands P^T and dS^T (over the scores, or after the accumulators), then
+  // (one CTA per SM) K as packed bf16.
+  static constexpr int C_S = 0, C_DP = BN, SCORE_COLS = 2 * BN, OPS_COLS = BN / 2;
+  static constexpr int C_DK = SCORE_COLS, C_DV = C_DK + HD;
+  static constexpr int C_P = TWO ? C_S : C_DV + HD, C_DS = TWO ? C_DP : C_P + OPS_COLS;
+  static constexpr int C_KT = C_DV + HD + 2 * OPS_COLS;
+  static constexpr int TMEM_COLS = TWO ? 256 : 512;
+  static_assert(TWO ? C_DV + HD <= TMEM_COLS : C_KT + HD / 2 <= TMEM_COLS, "TMEM budget");
+  static_assert(CTAS * SMEM <= 228 * 1024 - CTAS * 2048, "shared memory of the resident CTAs");
   static_assert(C_DP == C_S + BN, "one bias MMA covers both products");
   static_assert(SLOT % 1024 == 0 && (2 * RES + ONES) % 1024 == 0, "slots must keep panels 1024-byte aligned");
   static_assert(SMEM <= 232448, "shared memory budget");
@@ -412,12 +423,12 @@ __device__ __forceinline__ void dkv_ops(const uint32_t (&vs)[CW], const uint32_t
 }
 
 template <int HD>
-__global__ void __launch_bounds__(kBBThreads, 1)
+__global__ void __launch_bounds__(kBBThreads, DkvPass<HD>::CTAS)
     bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                     const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
                     const BwdArgs a) {
   using G = DkvPass<HD>;
-  constexpr int BN = G::BN, ST = G::ST, CW = G::CW, NB = G::NB;
+  constexpr int BN = G::BN, ST = G::ST, CW = G::CW;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = align1024(smem_raw);
   uint8_t* s_k = sm;
@@ -425,7 +436,7 @@ __global__ void __launch_bounds__(kBBThreads, 1)
   uint8_t* s_ones = s_v + G::RES;
   uint8_t* s_ring = s_ones + G::ONES;
   __shared__ uint64_t bar_res, bar_tres, bar_full[ST], bar_empty[ST];
-  __shared__ uint64_t bar_sc_full[NB], bar_sc_empty[NB], bar_ops_full, bar_ops_empty, bar_acc;
+  __shared__ uint64_t bar_sc_full, bar_sc_empty, bar_ops_full, bar_ops_empty, bar_acc;
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
 
@@ -445,10 +456,8 @@ __global__ void __launch_bounds__(kBBThreads, 1)
       mbar_init(&bar_full[s], 1);
       mbar_init(&bar_empty[s], 1);
     }
-    for (int i = 0; i < NB; ++i) {
-      mbar_init(&bar_sc_full[i], 1);
-      mbar_init(&bar_sc_empty[i], kBBEwWarps);
-    }
+    mbar_init(&bar_sc_full, 1);
+    mbar_init(&bar_sc_empty, kBBEwWarps);  // both layouts: every score share has been read
     mbar_init(&bar_ops_full, kBBEwWarps);
     mbar_init(&bar_ops_empty, 1);
     mbar_init(&bar_acc, 1);
@@ -563,43 +572,61 @@ __global__ void __launch_bounds__(kBBThreads, 1)
     const uint32_t id_s = idesc_bf16_f32(kBM, BN, false, false);
     const uint32_t id_bias = idesc_bf16_f32(kBM, 2 * BN, false, false);
     const uint64_t b_q = kdesc(s_ring);  // Q of slot 0; dO follows at +STR
-    const uint64_t a_v = kdesc(s_v);
+    const uint64_t a_k = kdesc(s_k), a_v = kdesc(s_v);
+    constexpr int KO = BN / 16;
+    const uint32_t id_o = idesc_bf16_f32(kBM, HD, false, true);
+    const uint64_t mn_q = mndesc(s_ring, G::STR_PANEL);
+    const uint64_t mn_do = mndesc(s_ring + G::STR, G::STR_PANEL);
     const uint64_t a_ones = smem_desc(smem_u32(s_ones), 16, 8 * G::BIAS_ROW, kSwizzle32B);
     const uint64_t b_bias = smem_desc(smem_u32(s_ring + 2 * G::STR), 16, 8 * G::BIAS_ROW, kSwizzle32B);
     constexpr uint64_t kSlot = G::SLOT >> 4, kStr = G::STR >> 4;
     bool ok = mbar_wait_warp(&bar_res, 0, &abort_flag) && mbar_wait_warp(&bar_tres, 0, &abort_flag);
     if (!ok && lane == 0) raise_error(a.status, &abort_flag, kDevTimeoutTmaFull);
     for (int it = 0; ok && it < total; ++it) {
-      const int s = it % ST, sb = it % NB, u = it / NB;
+      const int s = it % ST;
       if (!mbar_wait_warp(&bar_full[s], (it / ST) & 1, &abort_flag)) {
         if (lane == 0) raise_error(a.status, &abort_flag, kDevTimeoutTmaFull);
         break;
       }
-      if (u > 0 && !mbar_wait_warp(&bar_sc_empty[sb], (u - 1) & 1, &abort_flag)) {
+      // One CTA per SM: the score buffer is free once its scores were read.
+      if (!G::TWO && it > 0 && !mbar_wait_warp(&bar_sc_empty, (it - 1) & 1, &abort_flag)) {
         if (lane == 0) raise_error(a.status, &abort_flag, kDevTimeoutEpilogue);
         break;
       }
       tc_fence_after();
       const uint64_t bq = b_q + s * kSlot;
-      const uint32_t tb = tmem + sb * G::SCORE_COLS;
-      umma_bf16_w(tb + G::C_S, a_ones, b_bias + s * kSlot, id_bias, 0u);
-      umma_chain_tsk_w<KS, G::STR_PANEL>(tb + G::C_S, tmem + G::C_KT, bq, id_s, true);
-      if constexpr (G::V_TMEM)
-        umma_chain_tsk_w<KS, G::STR_PANEL>(tb + G::C_DP, tmem + G::C_VT, bq + kStr, id_s, true);
+      umma_bf16_w(tmem + G::C_S, a_ones, b_bias + s * kSlot, id_bias, 0u);
+      if constexpr (G::TWO)
+        umma_chain_w<KS, G::RES_PANEL, G::STR_PANEL, false>(tmem + G::C_S, a_k, bq, id_s, true);
       else
-        umma_chain_w<KS, G::RES_PANEL, G::STR_PANEL, false>(tb + G::C_DP, a_v, bq + kStr, id_s, true);
-      umma_commit_w(&bar_sc_full[sb]);
+        umma_chain_tsk_w<KS, G::STR_PANEL>(tmem + G::C_S, tmem + G::C_KT, bq, id_s, true);
+      umma_chain_w<KS, G::RES_PANEL, G::STR_PANEL, false>(tmem + G::C_DP, a_v, bq + kStr, id_s, true);
+      umma_commit_w(&bar_sc_full);
+      if constexpr (G::TWO) {
+        // The operand products of this tile, issued before the next tile's bias
+        // MMA overwrites the operands (the tensor core runs in issue order).
+        if (!mbar_wait_warp(&bar_ops_full, it & 1, &abort_flag)) {
+          if (lane == 0) raise_error(a.status, &abort_flag, kDevTimeoutEpilogue);
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        umma_chain_ts_w<KO>(tmem + G::C_DV, tmem + G::C_P, mn_do + s * kSlot, id_o, it > 0);
+        umma_chain_ts_w<KO>(tmem + G::C_DK, tmem + G::C_DS, mn_q + s * kSlot, id_o, it > 0);
+        umma_commit_w(&bar_empty[s]);
+      }
     }
+    if (G::TWO && ok) umma_commit_w(&bar_acc);
   } else if (warp == kBBWarpMmaOut) {
-    // ----------------------------- operand MMA issuer -----------------------------
+    // ----------------------- operand MMA issuer (one CTA per SM) -----------------------
     //   dV += P^T dO,  dK/scale += dS^T Q   (A in TMEM, B MN-major in the ring)
-    constexpr int KO = BN / 16, OC = G::OPS_COLS;
+    constexpr int KO = BN / 16;
     const uint32_t id_o = idesc_bf16_f32(kBM, HD, false, true);
     const uint64_t mn_q = mndesc(s_ring, G::STR_PANEL);
     const uint64_t mn_do = mndesc(s_ring + G::STR, G::STR_PANEL);
     constexpr uint64_t kSlot = G::SLOT >> 4;
     bool ok = true;
-    for (int it = 0; it < total; ++it) {
+    for (int it = 0; !G::TWO && it < total; ++it) {
       if (!mbar_wait_warp(&bar_ops_full, it & 1, &abort_flag)) {
         if (lane == 0) raise_error(a.status, &abort_flag, kDevTimeoutEpilogue);
         ok = false;
@@ -607,12 +634,12 @@ __global__ void __launch_bounds__(kBBThreads, 1)
       }
       tc_fence_after();
       const int s = it % ST;
-      umma_chain_ts_w<KO>(tmem + G::C_DV, tmem + G::C_OPS, mn_do + s * kSlot, id_o, it > 0);
-      umma_chain_ts_w<KO>(tmem + G::C_DK, tmem + G::C_OPS + OC, mn_q + s * kSlot, id_o, it > 0);
+      umma_chain_ts_w<KO>(tmem + G::C_DV, tmem + G::C_P, mn_do + s * kSlot, id_o, it > 0);
+      umma_chain_ts_w<KO>(tmem + G::C_DK, tmem + G::C_DS, mn_q + s * kSlot, id_o, it > 0);
       umma_commit_w(&bar_ops_empty);
       umma_commit_w(&bar_empty[s]);
     }
-    if (ok) umma_commit_w(&bar_acc);
+    if (!G::TWO && ok) umma_commit_w(&bar_acc);
   } else {
     // --------------------------- elementwise warps ----------------------------
     const int wg = (warp - kBBFirstEwWarp) >> 2;
@@ -625,25 +652,23 @@ __global__ void __launch_bounds__(kBBThreads, 1)
     const float sc2 = sh.scale * kLog2e;
     bool ok = mbar_wait_warp(&bar_res, 0, &abort_flag);
     if (ok) {
-      // This warpgroup's half of the head_dim columns of K (and V) into TMEM.
-      row_to_tmem<HD / 2>(s_k, r, wg * (HD / 2), lane_t + G::C_KT);
-      if constexpr (G::V_TMEM) row_to_tmem<HD / 2>(s_v, r, wg * (HD / 2), lane_t + G::C_VT);
-      tmem_wait_st();
+      if constexpr (!G::TWO) {  // this warpgroup's half of the head_dim columns of K into TMEM
+        row_to_tmem<HD / 2>(s_k, r, wg * (HD / 2), lane_t + G::C_KT);
+        tmem_wait_st();
+      }
       warp_arrive(&bar_tres);
     }
     for (int it = 0; ok && it < total; ++it) {
-      const int sb = it % NB;
-      ok = mbar_wait_warp(&bar_sc_full[sb], (it / NB) & 1, &abort_flag);
+      ok = mbar_wait_warp(&bar_sc_full, it & 1, &abort_flag);
       if (!ok) break;
       tc_fence_after();
-      const uint32_t tb = tmem + sb * G::SCORE_COLS;
       uint32_t vs[CW], vdp[CW];
-      tmem_share<CW>(tb, warp, G::C_S + cb, vs);
-      tmem_share<CW>(tb, warp, G::C_DP + cb, vdp);
+      tmem_share<CW>(tmem, warp, G::C_S + cb, vs);
+      tmem_share<CW>(tmem, warp, G::C_DP + cb, vdp);
       tmem_wait_ld();
       reg_fence(vs);
       reg_fence(vdp);
-      warp_arrive(&bar_sc_empty[sb]);
+      warp_arrive(&bar_sc_empty);
       const int qc = (qt_begin + it % n) * BN + cb;  // first query of this thread's columns
       const bool need_mask = qc + CW - 1 > qhi || qc < qlo;
       uint32_t o_p[CW / 2], o_ds[CW / 2];
@@ -651,12 +676,17 @@ __global__ void __launch_bounds__(kBBThreads, 1)
         dkv_ops<CW, true>(vs, vdp, qc, qlo, qhi, sc2, o_p, o_ds);
       else
         dkv_ops<CW, false>(vs, vdp, qc, qlo, qhi, sc2, o_p, o_ds);
-      if (it > 0) ok = mbar_wait_warp(&bar_ops_empty, (it - 1) & 1, &abort_flag);
+      // Two CTAs per SM: the operands overwrite score columns that the other
+      // warpgroup reads, so wait until both have read theirs. One CTA per SM:
+      // wait until the previous operands have been consumed.
+      if constexpr (G::TWO)
+        ok = mbar_wait_warp(&bar_sc_empty, it & 1, &abort_flag);
+      else if (it > 0)
+        ok = mbar_wait_warp(&bar_ops_empty, (it - 1) & 1, &abort_flag);
       if (!ok) break;
       tc_fence_after();
-      const uint32_t to = lane_t + G::C_OPS + (CW / 2) * wg;
-      tmem_st_ops(to, o_p);
-      tmem_st_ops(to + G::OPS_COLS, o_ds);
+      tmem_st_ops(lane_t + G::C_P + (CW / 2) * wg, o_p);
+      tmem_st_ops(lane_t + G::C_DS + (CW / 2) * wg, o_ds);
       tmem_wait_st();
       warp_arrive(&bar_ops_full);
     }

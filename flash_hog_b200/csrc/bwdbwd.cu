@@ -407,7 +407,7 @@ __global__ void __launch_bounds__(kBBThreads, 1)
       } else {
         tmem_row_to_global<HD>(tmem, warp, G::C_DDO, a.ddo + row_offset(sh.sq, b, srow, h), row_ok);
       }
-    } else if (threadIdx.x == kBBFirstEwWarp * 32) {
+    } else if (!ok && threadIdx.x == kBBFirstEwWarp * 32) {
       raise_error(a.status, &abort_flag, kDevTimeoutMma);
     }
   }

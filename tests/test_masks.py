@@ -119,6 +119,9 @@ def test_band_masks_match_oracle(b, h, hk, tq, tk, causal, window, d):
     ref = ora.jvp_bwd(a["q"], a["k"], a["v"], a["o"], a["lse"], a["do"], a["ddq"], a["ddk"], a["ddv"], a["tdo"], **kw)
     for name, got, want in zip(("tdQ", "tdK", "tdV"), (tdq, tdk, tdv), ref):
         assert_close(name, np64(got), want)
+    from flash_hog_b200 import _capi
+
+    assert _capi.device_status() == 0  # no bounded wait expired, no spurious error code
 
 
 @pytest.mark.gpu
