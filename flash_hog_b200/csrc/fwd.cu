@@ -2,11 +2,12 @@
 // natural-log log-sum-exp L, the residuals the reference's forward rule saves
 // (flash_hog/jax/_attention_impl.py:224-239 -- there produced by cuDNN).
 //
-// One CTA per 256 query rows of one (batch, head), as two 128-row tiles A and B
-// that share every streamed 128-row K|V tile of a TMA ring. Warp 0 allocates
-// TMEM and issues every MMA (warp-convergent, one elected lane), warp 1 is the
-// TMA producer, warps 2-5 and 6-9 are the softmax warpgroups of tiles A and B:
-// thread (warp, lane) owns TMEM lane 32*(warp%4)+lane, one query row.
+// A CTA owns T 128-row query tiles of one (batch, head) -- T = 1 at head_dim
+// 64 (two CTAs per SM), T = 2 at 128 -- that share every streamed 128-row K|V
+// tile of a TMA ring. Warp 0 allocates TMEM and issues every MMA
+// (warp-convergent, one elected lane), warp 1 is the TMA producer, and each
+// query tile has a softmax warpgroup (warps 2-5, then 6-9): thread (warp, lane)
+// owns TMEM lane 32*(warp%4)+lane, one query row.
 //
 // TMEM per tile: a score buffer S (128 columns) and the output accumulator O,
 // and at head_dim 64 a separate bf16 buffer for P (64 columns). The softmax
@@ -14,15 +15,15 @@
 // from shared memory.
 //  * head_dim 64: the softmax warps release S as soon as they have loaded it, so
 //    S(j+1) is computed while they exponentiate tile j; P(j) goes to its own
-//    buffer once the previous product has read it.
+//    buffer once the previous product has read it. S, P and O take 256 TMEM
+//    columns, so two CTAs share an SM and hide each other's waits.
 //  * head_dim 128 (TMEM holds no extra P buffers): P(j) is written back over the
 //    first half of S(j), and S(j+1) is issued right behind O += P(j) V_j into the
-//    same buffer (the tensor core runs in issue order).
-// The two tiles share the exponential units; each warpgroup computes while the
-// other waits. Online softmax with lazy rescaling: P = exp2(s - m)
-// against a running maximum m that is only raised -- and O, l rescaled in TMEM --
-// when a row's maximum grows by more than 2^8, so P stays below 2^8 and most
-// tiles need no rescale at all.
+//    same buffer (the tensor core runs in issue order). The two tiles of a CTA
+//    share the exponential units; each warpgroup computes while the other waits.
+// Online softmax with lazy rescaling: P = exp2(s - m) against a running maximum
+// m that is only raised -- and O, l rescaled in TMEM -- when a row's maximum
+// grows by more than 2^8, so P stays below 2^8 and most tiles need no rescale.
 
 #include <cuda_runtime.h>
 
@@ -40,29 +41,35 @@ struct FwdArgs {
   int* status;
 };
 
-constexpr int kFwdThreads = 320;
+
 constexpr int kFwdWarpMma = 0;
 constexpr int kFwdWarpProducer = 1;
 constexpr int kFwdFirstEwWarp = 2;
 constexpr int kFwdEwWarps = 4;       // per query tile
-constexpr int kFwdRows = 2 * kBM;    // query rows per CTA
 constexpr float kRescaleLog2 = 8.f;  // P < 2^8 between rescales
 
 template <int HD>
 struct FPass {
+  // Query tiles per CTA: one at head_dim 64, where S, a separate P buffer and O
+  // take 256 TMEM columns and two CTAs share an SM; two at 128 (one CTA per SM).
+  static constexpr int T = HD == 64 ? 1 : 2;
+  static constexpr int CTAS = T == 1 ? 2 : 1;
+  static constexpr int THREADS = 64 + 128 * T;
+  static constexpr int ROWS = kBM * T;           // query rows per CTA
   static constexpr int BN = 128;                 // key rows per streamed tile
-  static constexpr int ST = HD == 128 ? 2 : 4;   // K|V slots: 32 KB at head_dim 64, 64 KB at 128
+  static constexpr int ST = 2;                   // K|V slots: 32 KB at head_dim 64, 64 KB at 128
   static constexpr int RES = kBM * HD * 2;       // one 128-row query tile
   static constexpr int STR = BN * HD * 2;
   static constexpr int SLOT = 2 * STR;  // K | V
-  static constexpr int SMEM = 1024 + 2 * RES + ST * SLOT;
+  static constexpr int SMEM = 1024 + T * RES + ST * SLOT;
   // TMEM: S of tile t at t*BN; with separate P buffers (head_dim 64), P of tile
   // t at 2*BN + t*BN/2; O of tile t at C_O + t*HD.
   static constexpr bool SEP_P = HD == 64;
-  static constexpr int C_P = 2 * BN;
-  static constexpr int C_O = SEP_P ? 3 * BN : 2 * BN;
-  static constexpr int TMEM_COLS = 512;
-  static_assert(C_O + 2 * HD <= TMEM_COLS, "TMEM budget");
+  static constexpr int C_P = T * BN;
+  static constexpr int C_O = SEP_P ? T * BN + T * BN / 2 : T * BN;
+  static constexpr int TMEM_COLS = CTAS == 2 ? 256 : 512;
+  static_assert(C_O + T * HD <= TMEM_COLS, "TMEM budget");
+  static_assert(CTAS * SMEM <= 228 * 1024 - CTAS * 2048, "shared memory of the resident CTAs");
   static_assert(SMEM <= 232448, "shared memory budget");
 };
 
@@ -74,16 +81,16 @@ __device__ __forceinline__ void fwd_warp_arrive(uint64_t* bar) {
 }
 
 template <int HD>
-__global__ void __launch_bounds__(kFwdThreads, 1)
+__global__ void __launch_bounds__(FPass<HD>::THREADS, FPass<HD>::CTAS)
     fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                const __grid_constant__ CUtensorMap tm_v, const FwdArgs a) {
   using G = FPass<HD>;
-  constexpr int BN = G::BN, ST = G::ST;
+  constexpr int BN = G::BN, ST = G::ST, T = G::T;
   constexpr bool SEP_P = G::SEP_P;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = align1024(smem_raw);
   uint8_t* s_q = sm;  // tile A, then tile B
-  uint8_t* s_ring = s_q + 2 * G::RES;
+  uint8_t* s_ring = s_q + T * G::RES;
   // Per query tile t: scores ready, scores loaded (separate P only), P written,
   // P read by its product (separate P only), last O update done.
   __shared__ uint64_t bar_q, bar_full[ST], bar_empty[ST], bar_s_full[2], bar_s_empty[2], bar_p_full[2],
@@ -95,17 +102,17 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int h = blockIdx.x, b = blockIdx.y;
   const int qt = gridDim.z - 1 - blockIdx.z;  // longest causal rows first
-  const int q0 = qt * kFwdRows;
+  const int q0 = qt * G::ROWS;
   // Key tiles of each query tile: nt[t] tiles from key tile jt[t] (0 when the
   // tile lies past the last query row or sees no key). The ring streams the
   // union [jlo, jlo + n); tile t joins at ring position at[t].
-  int nt[2], jt[2], at[2];
+  int nt[2] = {0, 0}, jt[2] = {0, 0}, at[2] = {0, 0};
 #pragma unroll
-  for (int t = 0; t < 2; ++t) nt[t] = key_tiles(sh, q0 + t * kBM, kBM, BN, &jt[t]);
+  for (int t = 0; t < T; ++t) nt[t] = key_tiles(sh, q0 + t * kBM, kBM, BN, &jt[t]);
   const int jlo = nt[0] > 0 ? (nt[1] > 0 ? min(jt[0], jt[1]) : jt[0]) : jt[1];
   int jhi = jlo;
 #pragma unroll
-  for (int t = 0; t < 2; ++t) {
+  for (int t = 0; t < T; ++t) {
     if (nt[t] > 0) jhi = max(jhi, jt[t] + nt[t]);
     at[t] = jt[t] - jlo;
   }
@@ -118,7 +125,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       mbar_init(&bar_full[s], 1);
       mbar_init(&bar_empty[s], 1);
     }
-    for (int t = 0; t < 2; ++t) {
+    for (int t = 0; t < T; ++t) {
       mbar_init(&bar_s_full[t], 1);
       mbar_init(&bar_s_empty[t], kFwdEwWarps);
       mbar_init(&bar_p_full[t], kFwdEwWarps);
@@ -138,9 +145,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
-      mbar_arrive_expect_tx(&bar_q, 2 * G::RES);
-      tma_rows<HD>(s_q, &tm_q, &bar_q, q0, kBM, h, b);
-      tma_rows<HD>(s_q + G::RES, &tm_q, &bar_q, q0 + kBM, kBM, h, b);
+      mbar_arrive_expect_tx(&bar_q, T * G::RES);
+      for (int t = 0; t < T; ++t) tma_rows<HD>(s_q + t * G::RES, &tm_q, &bar_q, q0 + t * kBM, kBM, h, b);
       int issued = 0;
       for (int j = 0; j < n; ++j) {
         const int s = j % ST;
@@ -182,19 +188,19 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     };
     // Ring position j holds key tile jlo + j; tile t's own step is u = j - at[t].
     bool ok = mbar_wait_warp(&bar_q, 0, &abort_flag);
-    for (int t = 0; ok && t < 2; ++t)
+    for (int t = 0; ok && t < T; ++t)
       if (nt[t] > 0 && at[t] == 0) ok = issue_s(t, 0);
     for (int j = 0; ok && SEP_P && j < n; ++j) {
       // Separate P: S(u+1) as soon as S(u) has been loaded, then the products.
 #pragma unroll
-      for (int t = 0; ok && t < 2; ++t) {
+      for (int t = 0; ok && t < T; ++t) {
         const int u = j - at[t];
         if (u + 1 < 0 || u + 1 >= nt[t]) continue;
         if (u >= 0) ok = mbar_wait_warp(&bar_s_empty[t], u & 1, &abort_flag);
         ok = ok && issue_s(t, j + 1);
       }
 #pragma unroll
-      for (int t = 0; ok && t < 2; ++t) {
+      for (int t = 0; ok && t < T; ++t) {
         const int u = j - at[t];
         if (u < 0 || u >= nt[t]) continue;
         if (!mbar_wait_warp(&bar_p_full[t], u & 1, &abort_flag)) {
@@ -211,7 +217,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     }
     for (int j = 0; ok && !SEP_P && j < n; ++j) {
 #pragma unroll
-      for (int t = 0; ok && t < 2; ++t) {
+      for (int t = 0; ok && t < T; ++t) {
         const int u = j - at[t];
         if (u == -1 && nt[t] > 0) {  // the tile's first key tile is the next one
           ok = issue_s(t, j + 1);
@@ -369,8 +375,8 @@ int launch_fwd_hd(const AttnShape& s, const FwdPtrs& p, int* status, cudaStream_
     return kInvalidArgument;
   if (ensure_smem_limit(reinterpret_cast<const void*>(&fwd_kernel<HD>), G::SMEM) != kOk) return kLaunchFailed;
   FwdArgs args{s, static_cast<__nv_bfloat16*>(p.o), p.lse, status};
-  const dim3 grid(s.H, s.B, (s.Tq + kFwdRows - 1) / kFwdRows);
-  fwd_kernel<HD><<<grid, kFwdThreads, G::SMEM, stream>>>(mq, mk, mv, args);
+  const dim3 grid(s.H, s.B, (s.Tq + G::ROWS - 1) / G::ROWS);
+  fwd_kernel<HD><<<grid, G::THREADS, G::SMEM, stream>>>(mq, mk, mv, args);
   return after_launch();
 }
 
