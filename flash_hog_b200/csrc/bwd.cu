@@ -662,20 +662,26 @@ __global__ void __launch_bounds__(kBBThreads, DkvPass<HD>::CTAS)
       ok = mbar_wait_warp(&bar_sc_full, it & 1, &abort_flag);
       if (!ok) break;
       tc_fence_after();
-      uint32_t vs[CW], vdp[CW];
-      tmem_share<CW>(tmem, warp, G::C_S + cb, vs);
-      tmem_share<CW>(tmem, warp, G::C_DP + cb, vdp);
-      tmem_wait_ld();
-      reg_fence(vs);
-      reg_fence(vdp);
-      warp_arrive(&bar_sc_empty);
       const int qc = (qt_begin + it % n) * BN + cb;  // first query of this thread's columns
-      const bool need_mask = qc + CW - 1 > qhi || qc < qlo;
-      uint32_t o_p[CW / 2], o_ds[CW / 2];
-      if (need_mask)
-        dkv_ops<CW, true>(vs, vdp, qc, qlo, qhi, sc2, o_p, o_ds);
-      else
-        dkv_ops<CW, false>(vs, vdp, qc, qlo, qhi, sc2, o_p, o_ds);
+      // Two CTAs per SM (80 registers a thread): the share in two halves of CW/2
+      // columns, so half the scores are live at a time.
+      constexpr int HW = G::TWO ? CW / 2 : CW, NH = CW / HW;
+      uint32_t o_p[NH][HW / 2], o_ds[NH][HW / 2];
+#pragma unroll
+      for (int hf = 0; hf < NH; ++hf) {
+        uint32_t vs[HW], vdp[HW];
+        tmem_share<HW>(tmem, warp, G::C_S + cb + hf * HW, vs);
+        tmem_share<HW>(tmem, warp, G::C_DP + cb + hf * HW, vdp);
+        tmem_wait_ld();
+        reg_fence(vs);
+        reg_fence(vdp);
+        if (hf == NH - 1) warp_arrive(&bar_sc_empty);  // this warp has read all its scores
+        const int qh = qc + hf * HW;
+        if (qh + HW - 1 > qhi || qh < qlo)
+          dkv_ops<HW, true>(vs, vdp, qh, qlo, qhi, sc2, o_p[hf], o_ds[hf]);
+        else
+          dkv_ops<HW, false>(vs, vdp, qh, qlo, qhi, sc2, o_p[hf], o_ds[hf]);
+      }
       // Two CTAs per SM: the operands overwrite score columns that the other
       // warpgroup reads, so wait until both have read theirs. One CTA per SM:
       // wait until the previous operands have been consumed.
@@ -685,8 +691,11 @@ __global__ void __launch_bounds__(kBBThreads, DkvPass<HD>::CTAS)
         ok = mbar_wait_warp(&bar_ops_empty, (it - 1) & 1, &abort_flag);
       if (!ok) break;
       tc_fence_after();
-      tmem_st_ops(lane_t + G::C_P + (CW / 2) * wg, o_p);
-      tmem_st_ops(lane_t + G::C_DS + (CW / 2) * wg, o_ds);
+#pragma unroll
+      for (int hf = 0; hf < NH; ++hf) {
+        tmem_st_ops(lane_t + G::C_P + (CW / 2) * wg + hf * (HW / 2), o_p[hf]);
+        tmem_st_ops(lane_t + G::C_DS + (CW / 2) * wg + hf * (HW / 2), o_ds[hf]);
+      }
       tmem_wait_st();
       warp_arrive(&bar_ops_full);
     }
