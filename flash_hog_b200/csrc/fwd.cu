@@ -71,6 +71,9 @@ struct FPass {
   static_assert(C_O + T * HD <= TMEM_COLS, "TMEM budget");
   static_assert(CTAS * SMEM <= 228 * 1024 - CTAS * 2048, "shared memory of the resident CTAs");
   static_assert(SMEM <= 232448, "shared memory budget");
+  // The issuer waits for key tile j+1 (S(j+1)) before it releases tile j's slot:
+  // with one slot that wait could never end.
+  static_assert(ST >= 2, "the ring must hold the next key tile while the current one is in use");
 };
 
 // All lanes of the warp have finished their TMEM accesses; one lane arrives.
