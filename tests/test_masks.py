@@ -193,9 +193,10 @@ def test_band_mask_edge_cases(b, h, hk, tq, tk, causal, window, d):
     for name, got, want in zip(("dQ", "dK", "dV", "dQ'", "dK'", "dV'", "ddO"), list(grads) + list(outs), refs):
         g = np64(got)
         assert np.isfinite(g).all(), name
-        if np.abs(want).max() == 0:
-            # Exact cancellation in float64 (one visible key: P = 1, O = V); the
-            # kernels round O to bf16 before D = rowsum(dO o O), so ~1e-6 remains.
+        if np.abs(want).max() < 1e-3:
+            # (Near-)exact cancellation (one visible key: P = 1, O = V): the kernels
+            # round O to bf16 before D = rowsum(dO o O), so ~1e-6 remains where the
+            # float64 oracle gives ~0; a relative bar is meaningless there.
             assert np.abs(g).max() < 1e-3, name
         else:
             assert_close(name, g, want)
