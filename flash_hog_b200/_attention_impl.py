@@ -59,13 +59,24 @@ def _is_causal(mask) -> bool:
     return _mask_args(mask)[0] != 0
 
 
-def _bf16(x: torch.Tensor) -> torch.Tensor:
-    """bf16 BTNH with a contiguous head_dim (the kernels' operand type).
+def _is_f32(x: torch.Tensor) -> bool:
+    """fp32 inputs run the fp32 kernels (fp32 products, ``fh_attn_*_f32``), as the
+    reference's Pallas rule keeps fp32 operands in fp32
+    (``flash_hog/jax/_pallas_gpu_kernel.py:251-256``); every other dtype runs the
+    bf16 tensor-core kernels."""
+    return x.dtype == torch.float32
 
-    fp32 inputs are cast like the reference's native plugin does
-    (``flash_hog/jax/_tk_gpu.py:90-92``)."""
-    x = x.to(torch.bfloat16)
+
+def _operand(x: torch.Tensor, f32: bool) -> torch.Tensor:
+    """BTNH with a contiguous layout in the kernels' operand type (fp32 or bf16)."""
+    x = x.to(torch.float32 if f32 else torch.bfloat16)
     return x if x.is_contiguous() else x.contiguous()
+
+
+def _bf16(x: torch.Tensor) -> torch.Tensor:
+    """bf16 BTNH with a contiguous layout (the tensor-core kernels' operand type);
+    a cast like the one of the reference's native plugin (``flash_hog/jax/_tk_gpu.py:90-92``)."""
+    return _operand(x, False)
 
 
 def _check_inputs(query, key, value):
@@ -82,11 +93,12 @@ def _check_inputs(query, key, value):
 def cuda_dot_product_attention(query, key, value, mask_type: MaskType, scale: float, return_residual=False):
     """Forward. Returns ``out`` or ``(out, activation)`` (activation = L, (B, N, T) fp32)."""
     _check_inputs(query, key, value)
-    q, k, v = _bf16(query), _bf16(key), _bf16(value)
+    f32 = _is_f32(query)
+    q, k, v = (_operand(x, f32) for x in (query, key, value))
     b, t, n, _ = q.shape
     out = torch.empty_like(q)
     lse = torch.empty((b, n, t), dtype=torch.float32, device=q.device)
-    _capi.attn_fwd(q, k, v, out, lse, scale, *_mask_args(mask_type))
+    (_capi.attn_fwd_f32 if f32 else _capi.attn_fwd)(q, k, v, out, lse, scale, *_mask_args(mask_type))
     out = out.to(query.dtype)
     return (out, lse) if return_residual else out
 
@@ -106,12 +118,13 @@ def dot_product_attention_fwd_rule(query, key, value, mask_type: MaskType, scale
 def dot_product_attention_bwd_rule(mask_type: MaskType, scale: float, res, g):
     """First-order backward: (dQ, dK, dV) (``_attention_impl.py:242-261``)."""
     query, key, value, activation, out = res
-    q, k, v, o, do = _bf16(query), _bf16(key), _bf16(value), _bf16(out), _bf16(g)
+    f32 = _is_f32(query)
+    q, k, v, o, do = (_operand(x, f32) for x in (query, key, value, out, g))
     b, t, n, _ = q.shape
     dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
     delta = torch.empty((b, n, t), dtype=torch.float32, device=q.device)
-    _capi.attn_bwd(q, k, v, o, do, activation.float().contiguous(), dq, dk, dv, delta, scale,
-                   *_mask_args(mask_type))
+    (_capi.attn_bwd_f32 if f32 else _capi.attn_bwd)(q, k, v, o, do, activation.float().contiguous(), dq, dk, dv,
+                                                    delta, scale, *_mask_args(mask_type))
     return dq.to(query.dtype), dk.to(key.dtype), dv.to(value.dtype)
 
 
@@ -150,15 +163,16 @@ def dot_product_attention_fwd_jvp(mask_type: MaskType, scale: float, res, tangen
     query, key, value, activation, out = res
     _require_plain(query, key, value, activation, out, *tangents)
     tq, tk, tv = _zeros_if_none(tangents, (query, key, value))
-    q, k, v, o = _bf16(query), _bf16(key), _bf16(value), _bf16(out)
-    tq, tk, tv = _bf16(tq), _bf16(tk), _bf16(tv)
+    f32 = _is_f32(query)
+    q, k, v, o, tq, tk, tv = (_operand(x, f32) for x in (query, key, value, out, tq, tk, tv))
     b, t, n, _ = q.shape
     stats = torch.empty((3, b, n, t), dtype=torch.float32, device=q.device)
     zero_do = torch.zeros_like(q)
     dq2, t_out = torch.empty_like(q), torch.empty_like(q)
-    _capi.attn_bwdbwd_o(q, k, v, o, zero_do, tq, tk, tv, activation.float().contiguous(), dq2, t_out, None, None,
-                        stats[0], stats[1], stats[2], scale, _mask_args(mask_type)[0], which=_capi.PASS_QUERY,
-                        window=_mask_args(mask_type)[1])
+    entry = _capi.attn_bwdbwd_f32 if f32 else _capi.attn_bwdbwd_o
+    entry(q, k, v, o, zero_do, tq, tk, tv, activation.float().contiguous(), dq2, t_out, None, None,
+          stats[0], stats[1], stats[2], scale, _mask_args(mask_type)[0], which=_capi.PASS_QUERY,
+          window=_mask_args(mask_type)[1])
     return t_out.to(out.dtype), stats[1].clone()
 
 
@@ -178,15 +192,16 @@ def dot_product_attention_bwd_jvp(mask_type: MaskType, scale: float, res, g, tan
     _require_plain(query, key, value, activation, out, g, *tangents)
     tq, tk, tv = _zeros_if_none(tangents[:3], (query, key, value))
     tdo = tangents[3]
-    q, k, v, o, do = _bf16(query), _bf16(key), _bf16(value), _bf16(out), _bf16(g)
-    tq, tk, tv = _bf16(tq), _bf16(tk), _bf16(tv)
-    tdo = None if tdo is None else _bf16(tdo)
+    f32 = _is_f32(query)
+    q, k, v, o, do, tq, tk, tv = (_operand(x, f32) for x in (query, key, value, out, g, tq, tk, tv))
+    tdo = None if tdo is None else _operand(tdo, f32)
     b, t, n, _ = q.shape
     stats = torch.empty((3, b, n, t), dtype=torch.float32, device=q.device)
     tdq, t_out = torch.empty_like(q), torch.empty_like(q)
     tdk, tdv = torch.empty_like(k), torch.empty_like(v)
-    _capi.attn_jvp_bwd(q, k, v, o, do, activation.float().contiguous(), tq, tk, tv, tdo, tdq, tdk, tdv, t_out,
-                       stats[0], stats[1], stats[2], scale, *_mask_args(mask_type))
+    (_capi.attn_jvp_bwd_f32 if f32 else _capi.attn_jvp_bwd)(
+        q, k, v, o, do, activation.float().contiguous(), tq, tk, tv, tdo, tdq, tdk, tdv, t_out,
+        stats[0], stats[1], stats[2], scale, *_mask_args(mask_type))
     return tdq.to(query.dtype), tdk.to(key.dtype), tdv.to(value.dtype)
 
 

@@ -40,13 +40,17 @@ EXPORTED_SYMBOLS = (
     "fh_attn_bwdbwd_o",
     "fh_attn_bwdbwd_noalloc",
     "fh_attn_jvp_bwd",
+    "fh_attn_fwd_f32",
+    "fh_attn_bwd_f32",
+    "fh_attn_bwdbwd_f32",
+    "fh_attn_jvp_bwd_f32",
     "fh_device_status",
     "fh_status_string",
     "fh_last_error",
     "fh_abi_version",
     "fh_launch_count",
 )
-ABI_VERSION = 4
+ABI_VERSION = 5
 
 
 class FlashHogError(RuntimeError):
@@ -97,6 +101,10 @@ def lib() -> ctypes.CDLL:
     h.fh_attn_bwdbwd_o.argtypes = [vp, dims] + [vp] * 16 + [f32, i32, i32]
     h.fh_attn_bwdbwd_noalloc.argtypes = [vp, dims] + [vp] * 13 + [f32, i32, vp]
     h.fh_attn_jvp_bwd.argtypes = [vp, dims] + [vp] * 17 + [f32, i32]
+    h.fh_attn_fwd_f32.argtypes = [vp, dims] + [vp] * 5 + [f32, i32]
+    h.fh_attn_bwd_f32.argtypes = [vp, dims] + [vp] * 10 + [f32, i32]
+    h.fh_attn_bwdbwd_f32.argtypes = [vp, dims] + [vp] * 16 + [f32, i32, i32]
+    h.fh_attn_jvp_bwd_f32.argtypes = [vp, dims] + [vp] * 17 + [f32, i32]
     h.fh_device_status.argtypes = [vp, ctypes.POINTER(ctypes.c_int)]
     h.fh_status_string.argtypes = [i32]
     h.fh_status_string.restype = ctypes.c_char_p
@@ -106,7 +114,8 @@ def lib() -> ctypes.CDLL:
     h.fh_last_error.argtypes = []
     h.fh_last_error.restype = ctypes.c_char_p
     for name in ("fh_attn_fwd", "fh_attn_rowdot", "fh_attn_bwd", "fh_attn_bwdbwd", "fh_attn_bwdbwd_pass",
-                 "fh_attn_bwdbwd_o", "fh_attn_bwdbwd_noalloc", "fh_attn_jvp_bwd", "fh_device_status",
+                 "fh_attn_bwdbwd_o", "fh_attn_bwdbwd_noalloc", "fh_attn_jvp_bwd", "fh_attn_fwd_f32",
+                 "fh_attn_bwd_f32", "fh_attn_bwdbwd_f32", "fh_attn_jvp_bwd_f32", "fh_device_status",
                  "fh_abi_version"):
         getattr(h, name).restype = i32
     if h.fh_abi_version() != ABI_VERSION:
@@ -151,16 +160,16 @@ def make_dims(q: torch.Tensor, k: torch.Tensor, window: int = 0) -> FhAttnDims:
     return FhAttnDims(b, h, tq, tk, d, _strides(q), _strides(k), hkv, int(window))
 
 
-def _same_layout(ref: torch.Tensor, *others: torch.Tensor) -> None:
+def _same_layout(ref: torch.Tensor, *others: torch.Tensor, dtype=torch.bfloat16) -> None:
     """Checks shape, strides, dtype and device against ``ref`` (None entries,
     unused outputs, are skipped)."""
-    for t in others:
+    for t in (ref,) + others:
         if t is None:
             continue
         if _layout_key(t) != _layout_key(ref):
             raise ValueError("tensors of one side must share shape and strides")
-        if t.dtype != torch.bfloat16 or t.device != ref.device:
-            raise ValueError("tensors must be bf16 on the same CUDA device")
+        if t.dtype != dtype or t.device != ref.device:
+            raise ValueError(f"tensors must be {dtype} on the same CUDA device")
 
 
 def attn_fwd(q, k, v, out, lse, scale: float, causal: int, window: int = 0) -> None:
@@ -232,6 +241,52 @@ def attn_jvp_bwd(q, k, v, o, dO, lse, tq, tk, tv, tdO, tdq, tdk, tdv, to, delta,
     _same_layout(k, v, tk, tv, tdk, tdv)
     dims = make_dims(q, k, window)
     _check("fh_attn_jvp_bwd", lib().fh_attn_jvp_bwd(
+        _stream(q.device), ctypes.byref(dims), _ptr(q), _ptr(k), _ptr(v), _ptr(o), _ptr(dO), _ptr(lse), _ptr(tq),
+        _ptr(tk), _ptr(tv), _ptr(tdO), _ptr(tdq), _ptr(tdk), _ptr(tdv), _ptr(to),
+        _ptr(delta), _ptr(dd), _ptr(bvec), float(scale), int(causal)))
+
+
+_F32 = torch.float32
+
+
+def attn_fwd_f32(q, k, v, out, lse, scale: float, causal: int, window: int = 0) -> None:
+    """``attn_fwd`` with fp32 tensors, fp32 products (``fh_attn_fwd_f32``)."""
+    _same_layout(q, out, dtype=_F32)
+    _same_layout(k, v, dtype=_F32)
+    dims = make_dims(q, k, window)
+    _check("fh_attn_fwd_f32", lib().fh_attn_fwd_f32(_stream(q.device), ctypes.byref(dims), _ptr(q), _ptr(k),
+                                                   _ptr(v), _ptr(out), _ptr(lse), float(scale), int(causal)))
+
+
+def attn_bwd_f32(q, k, v, o, dO, lse, dq, dk, dv, delta, scale: float, causal: int, window: int = 0) -> None:
+    """``attn_bwd`` with fp32 tensors (``fh_attn_bwd_f32``)."""
+    _same_layout(q, o, dO, dq, dtype=_F32)
+    _same_layout(k, v, dk, dv, dtype=_F32)
+    dims = make_dims(q, k, window)
+    _check("fh_attn_bwd_f32", lib().fh_attn_bwd_f32(_stream(q.device), ctypes.byref(dims), _ptr(q), _ptr(k),
+                                                   _ptr(v), _ptr(o), _ptr(dO), _ptr(lse), _ptr(dq), _ptr(dk),
+                                                   _ptr(dv), _ptr(delta), float(scale), int(causal)))
+
+
+def attn_bwdbwd_f32(q, k, v, o, dO, ddq, ddk, ddv, lse, dq2, ddo, dk2, dv2, delta, dd, bvec, scale: float,
+                    causal: int, which: int = PASS_QUERY | PASS_KEY, window: int = 0) -> None:
+    """``attn_bwdbwd_o`` with fp32 tensors (``fh_attn_bwdbwd_f32``)."""
+    _same_layout(q, o, dO, ddq, dq2, ddo, dtype=_F32)
+    _same_layout(k, v, ddk, ddv, dk2, dv2, dtype=_F32)
+    dims = make_dims(q, k, window)
+    _check("fh_attn_bwdbwd_f32", lib().fh_attn_bwdbwd_f32(
+        _stream(q.device), ctypes.byref(dims), _ptr(q), _ptr(k), _ptr(v), _ptr(o), _ptr(dO), _ptr(ddq),
+        _ptr(ddk), _ptr(ddv), _ptr(lse), _ptr(dq2), _ptr(ddo), _ptr(dk2), _ptr(dv2), _ptr(delta), _ptr(dd),
+        _ptr(bvec), float(scale), int(causal), int(which)))
+
+
+def attn_jvp_bwd_f32(q, k, v, o, dO, lse, tq, tk, tv, tdO, tdq, tdk, tdv, to, delta, dd, bvec, scale: float,
+                     causal: int, window: int = 0) -> None:
+    """``attn_jvp_bwd`` with fp32 tensors (``fh_attn_jvp_bwd_f32``)."""
+    _same_layout(q, o, dO, tq, tdq, to, tdO, dtype=_F32)
+    _same_layout(k, v, tk, tv, tdk, tdv, dtype=_F32)
+    dims = make_dims(q, k, window)
+    _check("fh_attn_jvp_bwd_f32", lib().fh_attn_jvp_bwd_f32(
         _stream(q.device), ctypes.byref(dims), _ptr(q), _ptr(k), _ptr(v), _ptr(o), _ptr(dO), _ptr(lse), _ptr(tq),
         _ptr(tk), _ptr(tv), _ptr(tdO), _ptr(tdq), _ptr(tdk), _ptr(tdv), _ptr(to),
         _ptr(delta), _ptr(dd), _ptr(bvec), float(scale), int(causal)))

@@ -18,7 +18,7 @@ import dataclasses
 import torch
 
 from flash_hog_b200 import _capi
-from flash_hog_b200._attention_impl import MaskType, _bf16, _mask_args
+from flash_hog_b200._attention_impl import MaskType, _is_f32, _mask_args, _operand
 
 
 @dataclasses.dataclass(frozen=True)
@@ -57,16 +57,17 @@ def flash_bwdbwd(Q, K, V, O, dO, ddQ, ddK, ddV, L, mask_type: MaskType = MaskTyp
     if Q.shape[2] % K.shape[2] != 0:
         raise ValueError(f"q_heads ({Q.shape[2]}) must be a multiple of kv_heads ({K.shape[2]})")
     causal, window = _mask_args(mask_type)
-    q, k, v, o, do, ddq, ddk, ddv = (_bf16(x) for x in (Q, K, V, O, dO, ddQ, ddK, ddV))
+    f32 = _is_f32(Q)
+    q, k, v, o, do, ddq, ddk, ddv = (_operand(x, f32) for x in (Q, K, V, O, dO, ddQ, ddK, ddV))
     b, t, n, _ = q.shape
     lse = L.reshape(b, n, t).float().contiguous()
     stats = torch.empty((3, b, n, t), dtype=torch.float32, device=q.device)
     delta, dd, bvec = stats[0], stats[1], stats[2]
     dq2, ddo = torch.empty_like(q), torch.empty_like(q)
     dk2, dv2 = torch.empty_like(k), torch.empty_like(k)
-    # D = rowsum(dO * O) is computed by the query-tiled pass itself.
-    _capi.attn_bwdbwd_o(q, k, v, o, do, ddq, ddk, ddv, lse, dq2, ddo, dk2, dv2, delta, dd, bvec, scale, causal,
-                        window=window)
+    # D = rowsum(dO * O) is computed on the device as part of the call.
+    entry = _capi.attn_bwdbwd_f32 if f32 else _capi.attn_bwdbwd_o
+    entry(q, k, v, o, do, ddq, ddk, ddv, lse, dq2, ddo, dk2, dv2, delta, dd, bvec, scale, causal, window=window)
     outs = (dq2.to(Q.dtype), dk2.to(K.dtype), dv2.to(V.dtype), ddo.to(dO.dtype))
     if return_stats:
         return outs, (delta, dd, bvec)

@@ -331,6 +331,77 @@ int fh_attn_jvp_bwd(void* stream, const fh_attn_dims* dims, const void* q, const
   return launch_bwd(s, dims->head_dim, p, status, st);
 }
 
+int fh_attn_fwd_f32(void* stream, const fh_attn_dims* dims, const float* q, const float* k, const float* v,
+                    float* o, float* lse, float scale, int causal) {
+  if (injected("fh_attn_fwd_f32")) return FH_ERR_INJECTED;
+  AttnShape s;
+  int rc = validate(dims, &s, scale, causal);
+  if (rc != kOk) return rc;
+  if (!all_aligned(q, k, v, o) || !lse) return fail(FH_ERR_INVALID_ARGUMENT, kAlignMsg);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if ((rc = select_stream_device(st)) != kOk) return rc;
+  return launch_fwd_f32(s, dims->head_dim, F32FwdPtrs{q, k, v, o, lse}, st);
+}
+
+int fh_attn_bwd_f32(void* stream, const fh_attn_dims* dims, const float* q, const float* k, const float* v,
+                    const float* o, const float* dO, const float* lse, float* dq, float* dk, float* dv, float* delta,
+                    float scale, int causal) {
+  if (injected("fh_attn_bwd_f32")) return FH_ERR_INJECTED;
+  AttnShape s;
+  int rc = validate(dims, &s, scale, causal);
+  if (rc != kOk) return rc;
+  if (!all_aligned(q, k, v, o, dO, dq, dk, dv) || !lse || !delta) return fail(FH_ERR_INVALID_ARGUMENT, kAlignMsg);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if ((rc = select_stream_device(st)) != kOk) return rc;
+  return launch_bwd_f32(s, dims->head_dim, F32BwdPtrs{q, k, v, o, dO, lse, dq, dk, dv, delta}, st);
+}
+
+int fh_attn_bwdbwd_f32(void* stream, const fh_attn_dims* dims, const float* q, const float* k, const float* v,
+                       const float* o, const float* dO, const float* ddq, const float* ddk, const float* ddv,
+                       const float* lse, float* dq2, float* ddo, float* dk2, float* dv2, float* delta, float* dd,
+                       float* bvec, float scale, int causal, int passes) {
+  if (injected("fh_attn_bwdbwd_f32")) return FH_ERR_INJECTED;
+  AttnShape s;
+  int rc = validate(dims, &s, scale, causal);
+  if (rc != kOk) return rc;
+  if (passes < 1 || passes > 3) return fail(FH_ERR_INVALID_ARGUMENT, "pass must be 1, 2 or 3");
+  if (!all_aligned(q, k, v, dO, ddq, ddk, ddv) || !lse || !delta || !dd || !bvec)
+    return fail(FH_ERR_INVALID_ARGUMENT, kAlignMsg);
+  if ((passes & kPassQuery) && (!all_aligned(o, ddo) || (dq2 && !aligned16(dq2))))
+    return fail(FH_ERR_INVALID_ARGUMENT, kAlignMsg);
+  if ((passes & kPassKey) && !all_aligned(dk2, dv2)) return fail(FH_ERR_INVALID_ARGUMENT, kAlignMsg);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if ((rc = select_stream_device(st)) != kOk) return rc;
+  return launch_bwdbwd_f32(s, dims->head_dim,
+                           F32BwdBwdPtrs{q, k, v, o, dO, ddq, ddk, ddv, lse, delta, dq2, ddo, dk2, dv2, dd, bvec},
+                           passes, st);
+}
+
+int fh_attn_jvp_bwd_f32(void* stream, const fh_attn_dims* dims, const float* q, const float* k, const float* v,
+                        const float* o, const float* dO, const float* lse, const float* tq, const float* tk,
+                        const float* tv, const float* tdO, float* tdq, float* tdk, float* tdv, float* to,
+                        float* delta, float* dd, float* bvec, float scale, int causal) {
+  if (injected("fh_attn_jvp_bwd_f32")) return FH_ERR_INJECTED;
+  AttnShape s;
+  int rc = validate(dims, &s, scale, causal);
+  if (rc != kOk) return rc;
+  if (!all_aligned(q, k, v, o, dO, tq, tk, tv, tdq, tdk, tdv, to) || !lse || !delta || !dd || !bvec)
+    return fail(FH_ERR_INVALID_ARGUMENT, kAlignMsg);
+  if (tdO && !all_aligned(tdO)) return fail(FH_ERR_INVALID_ARGUMENT, kAlignMsg);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if ((rc = select_stream_device(st)) != kOk) return rc;
+  rc = launch_bwdbwd_f32(s, dims->head_dim,
+                         F32BwdBwdPtrs{q, k, v, o, dO, tq, tk, tv, lse, delta, tdq, to, tdk, tdv, dd, bvec},
+                         kPassQuery | kPassKey, st);
+  if (rc != kOk || !tdO) return rc;
+  // The first-order backward of tdO reuses `delta` for rowsum(tdO * o).
+  F32BwdPtrs p{q, k, v, o, tdO, lse, tdq, tdk, tdv, delta};
+  p.dq_acc = tdq;
+  p.dk_acc = tdk;
+  p.dv_acc = tdv;
+  return launch_bwd_f32(s, dims->head_dim, p, st);
+}
+
 int fh_device_status(void* stream, int* code) {
   if (!code) return FH_ERR_INVALID_ARGUMENT;
   *code = 0;

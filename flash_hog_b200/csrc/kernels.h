@@ -56,6 +56,33 @@ int launch_bwd(const AttnShape& s, int hd, const BwdPtrs& p, int* status, cudaSt
 enum BwdBwdPass : int { kPassQuery = 1, kPassKey = 2 };
 int launch_bwdbwd(const AttnShape& s, int hd, const BwdBwdPtrs& p, int passes, int* status, cudaStream_t stream);
 
+// fp32 operands on the CUDA cores (f32.cu): same passes, masks, GQA mapping and
+// layouts as the bf16 kernels; `delta` is written by a rowdot kernel (forward
+// output `o` and `dO`) whenever a pass needs D. No device waits, so no status word.
+struct F32FwdPtrs {
+  const float *q, *k, *v;
+  float *o, *lse;
+};
+
+struct F32BwdPtrs {
+  const float *q, *k, *v, *o, *dO, *lse;
+  float *dq, *dk, *dv, *delta;
+  const float* dq_acc = nullptr;  // optional addends, as in BwdPtrs
+  const float* dk_acc = nullptr;
+  const float* dv_acc = nullptr;
+};
+
+struct F32BwdBwdPtrs {
+  const float *q, *k, *v, *o, *dO, *ddq, *ddk, *ddv, *lse;
+  float *delta;               // written by the query pass, read by the key pass
+  float *dq2, *ddo, *dk2, *dv2;  // dq2 may be null (query pass: ddO only)
+  float *dd, *bv;
+};
+
+int launch_fwd_f32(const AttnShape& s, int hd, const F32FwdPtrs& p, cudaStream_t stream);
+int launch_bwd_f32(const AttnShape& s, int hd, const F32BwdPtrs& p, cudaStream_t stream);
+int launch_bwdbwd_f32(const AttnShape& s, int hd, const F32BwdBwdPtrs& p, int passes, cudaStream_t stream);
+
 // Checks the kernel launch just made (cudaGetLastError) and, if it was queued,
 // counts it for fh_launch_count(). Returns kOk or kLaunchFailed.
 int after_launch();

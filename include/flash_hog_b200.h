@@ -202,6 +202,36 @@ int fh_attn_bwdbwd_noalloc(void* stream, const fh_attn_dims* dims, const void* q
                            const float* lse, void* dq2, void* ddo, void* dk2, void* dv2, float scale, int causal,
                            int* device_status);
 
+/* fp32 operands. The entry points above take bf16 tensors and compute their
+ * products on the tensor cores with bf16 operands. The reference also accepts
+ * fp32 inputs and then keeps them in fp32: its Pallas double backward casts
+ * each score-like operand to the dtype of the tensor it multiplies
+ * (flash_hog/jax/_pallas_gpu_kernel.py:251-256), and its XLA reference
+ * differentiates fp32 attention twice (flash_hog/_jax_refs/jax_impl.py:194-247).
+ * These four entry points do the same with fp32 products and fp32 accumulation
+ * on the CUDA cores, for results within 1e-3 of an fp32/fp64 reference. Same
+ * dims, masks, GQA mapping, strides, scratch and outputs as their bf16
+ * counterparts; all tensors are fp32. There are no device-side waits, so
+ * fh_device_status() has nothing to report for them.
+ *  - fh_attn_fwd_f32: as fh_attn_fwd.
+ *  - fh_attn_bwd_f32: as fh_attn_bwd (delta receives rowsum(dO * o)).
+ *  - fh_attn_bwdbwd_f32: as fh_attn_bwdbwd_o, including `passes` and the
+ *    forward-tangent use; dq2 may be NULL for a query pass.
+ *  - fh_attn_jvp_bwd_f32: as fh_attn_jvp_bwd. */
+int fh_attn_fwd_f32(void* stream, const fh_attn_dims* dims, const float* q, const float* k, const float* v,
+                    float* o, float* lse, float scale, int causal);
+int fh_attn_bwd_f32(void* stream, const fh_attn_dims* dims, const float* q, const float* k, const float* v,
+                    const float* o, const float* dO, const float* lse, float* dq, float* dk, float* dv, float* delta,
+                    float scale, int causal);
+int fh_attn_bwdbwd_f32(void* stream, const fh_attn_dims* dims, const float* q, const float* k, const float* v,
+                       const float* o, const float* dO, const float* ddq, const float* ddk, const float* ddv,
+                       const float* lse, float* dq2, float* ddo, float* dk2, float* dv2, float* delta, float* dd,
+                       float* bvec, float scale, int causal, int passes);
+int fh_attn_jvp_bwd_f32(void* stream, const fh_attn_dims* dims, const float* q, const float* k, const float* v,
+                        const float* o, const float* dO, const float* lse, const float* tq, const float* tk,
+                        const float* tv, const float* tdO, float* tdq, float* tdk, float* tdv, float* to,
+                        float* delta, float* dd, float* bvec, float scale, int causal);
+
 /* Synchronises `stream`, then reads and clears the status word the kernels of
  * the current device record device-side failures in. *code receives 0 or one
  * of the device error codes (1..5: which bounded wait expired). Returns FH_OK,
@@ -224,7 +254,7 @@ int fh_abi_version(void);
  * reads it before and after a timed region to report its kernel launches. */
 unsigned long long fh_launch_count(void);
 
-#define FH_ABI_VERSION 4
+#define FH_ABI_VERSION 5
 
 #ifdef __cplusplus
 }
