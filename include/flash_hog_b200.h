@@ -12,7 +12,8 @@
  * strides, a stream, an int status. No torch or XLA types cross this boundary.
  *
  * Conventions shared by all entry points
- *  - Every bf16 tensor is addressed as (batch, seq, head, head_dim) with the
+ *  - Every tensor operand (bf16; fp32 for the _f32 entry points) is addressed
+ *    as (batch, seq, head, head_dim) with the
  *    element strides given in fh_attn_dims (head_dim stride 1). BTNH, the layout
  *    of the reference API (flash_hog/jax/attention.py:19-49), and BHTD, the
  *    layout of the reference's native kernels (ffi.cu:7-10), are both strided
