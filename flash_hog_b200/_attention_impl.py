@@ -79,6 +79,19 @@ def _bf16(x: torch.Tensor) -> torch.Tensor:
     return _operand(x, False)
 
 
+def _fold(x: torch.Tensor, dim, size: int) -> torch.Tensor:
+    """For a batching (vmap) rule: moves the vmapped dimension ``dim`` (None: not
+    vmapped, broadcast) to the front and merges it with the batch dimension,
+    (size, B, ...) -> (size * B, ...), as ``flash_hog/jax/_pallas_gpu.py:92-93`` does."""
+    x = x.movedim(dim, 0) if dim is not None else x.unsqueeze(0).expand(size, *x.shape)
+    return x.reshape(size * x.shape[1], *x.shape[2:])
+
+
+def _unfold(x: torch.Tensor, size: int) -> torch.Tensor:
+    """Inverse of ``_fold`` on a result: (size * B, ...) -> (size, B, ...)."""
+    return x.reshape(size, x.shape[0] // size, *x.shape[1:])
+
+
 def _check_inputs(query, key, value):
     if query.ndim != 4 or key.ndim != 4 or value.ndim != 4:
         raise ValueError("expected BTNH tensors")

@@ -22,6 +22,11 @@ and the ``setup_context`` form, so ``torch.func`` transforms compose over them:
 Hessian-vector products -- runs fwd, bwd, the forward jvp (the double
 backward's query pass at dO = 0) and the backward's jvp (double backward plus
 first-order backward, ``fh_attn_jvp_bwd``) on the kernels.
+
+Both Functions, and ``flash_bwdbwd``, also have batching rules for
+``torch.func.vmap``: the vmapped axis is folded into the batch axis and the
+kernels run once, the rule the reference gives its double backward
+(``flash_hog/jax/_pallas_gpu.py:85-102``).
 """
 
 from __future__ import annotations
@@ -97,6 +102,14 @@ class _DotProductAttention(torch.autograd.Function):
         t_out, _ = attn_impl.dot_product_attention_fwd_jvp(ctx.mask_type, ctx.scale, res, (tq, tk, tv))
         return t_out, None
 
+    @staticmethod
+    def vmap(info, in_dims, query, key, value, mask_type, scale):
+        # Fold the vmapped axis into batch (the rule of flash_hog/jax/_pallas_gpu.py:85-102).
+        size = info.batch_size
+        q, k, v = (attn_impl._fold(x, d, size) for x, d in zip((query, key, value), in_dims[:3]))
+        out, activation = _DotProductAttention.apply(q, k, v, mask_type, scale)
+        return (attn_impl._unfold(out, size), attn_impl._unfold(activation, size)), (0, 0)
+
 
 class _DotProductAttentionBwd(torch.autograd.Function):
     """First-order backward (dQ, dK, dV); reverse mode gives the double backward,
@@ -129,3 +142,10 @@ class _DotProductAttentionBwd(torch.autograd.Function):
         query, key, value, activation, out, g = ctx.saved_tensors
         return attn_impl.dot_product_attention_bwd_jvp(ctx.mask_type, ctx.scale, (query, key, value, activation, out),
                                                       g, (tq, tk, tv, tg))
+
+    @staticmethod
+    def vmap(info, in_dims, query, key, value, activation, out, g, mask_type, scale):
+        size = info.batch_size
+        args = [attn_impl._fold(x, d, size) for x, d in zip((query, key, value, activation, out, g), in_dims[:6])]
+        dq, dk, dv = _DotProductAttentionBwd.apply(*args, mask_type, scale)
+        return tuple(attn_impl._unfold(x, size) for x in (dq, dk, dv)), (0, 0, 0)

@@ -7,6 +7,9 @@ arguments, same return order ``(dQ2, dK2, dV2, ddO)``, unbatched (T, N, H)
 inputs accepted by adding a batch dimension (``_pallas_gpu.py:65-68``), and
 D = rowsum(dO o O) computed on the device before the kernels (``_tk_gpu.py:93``).
 
+Under ``torch.func.vmap`` the vmapped axis is folded into the batch axis and
+the kernels run once, the reference's batching rule (``_pallas_gpu.py:85-102``).
+
 Unlike the reference's TK path there is no per-call fallback and no gate on
 GPU generation: every call runs the sm_100a kernels or raises.
 """
@@ -18,7 +21,7 @@ import dataclasses
 import torch
 
 from flash_hog_b200 import _capi
-from flash_hog_b200._attention_impl import MaskType, _is_f32, _mask_args, _operand
+from flash_hog_b200._attention_impl import MaskType, _fold, _is_f32, _mask_args, _operand, _unfold
 
 
 @dataclasses.dataclass(frozen=True)
@@ -57,6 +60,15 @@ def flash_bwdbwd(Q, K, V, O, dO, ddQ, ddK, ddV, L, mask_type: MaskType = MaskTyp
     if Q.shape[2] % K.shape[2] != 0:
         raise ValueError(f"q_heads ({Q.shape[2]}) must be a multiple of kv_heads ({K.shape[2]})")
     causal, window = _mask_args(mask_type)
+    dq2, dk2, dv2, ddo, stats = _FlashBwdBwd.apply(Q, K, V, O, dO, ddQ, ddK, ddV, L, causal, window, float(scale))
+    outs = (dq2, dk2, dv2, ddo)
+    if return_stats:
+        return outs, (stats[0], stats[1], stats[2])
+    return outs
+
+
+def _bwdbwd_device(Q, K, V, O, dO, ddQ, ddK, ddV, L, causal: int, window: int, scale: float):
+    """The kernels on 4-D BTNH tensors: ``(dQ2, dK2, dV2, ddO, stats)``, stats = (D, dD, B) stacked."""
     f32 = _is_f32(Q)
     q, k, v, o, do, ddq, ddk, ddv = (_operand(x, f32) for x in (Q, K, V, O, dO, ddQ, ddK, ddV))
     b, t, n, _ = q.shape
@@ -68,7 +80,37 @@ def flash_bwdbwd(Q, K, V, O, dO, ddQ, ddK, ddV, L, mask_type: MaskType = MaskTyp
     # D = rowsum(dO * O) is computed on the device as part of the call.
     entry = _capi.attn_bwdbwd_f32 if f32 else _capi.attn_bwdbwd_o
     entry(q, k, v, o, do, ddq, ddk, ddv, lse, dq2, ddo, dk2, dv2, delta, dd, bvec, scale, causal, window=window)
-    outs = (dq2.to(Q.dtype), dk2.to(K.dtype), dv2.to(V.dtype), ddo.to(dO.dtype))
-    if return_stats:
-        return outs, (delta, dd, bvec)
-    return outs
+    return dq2.to(Q.dtype), dk2.to(K.dtype), dv2.to(V.dtype), ddo.to(dO.dtype), stats
+
+
+class _FlashBwdBwd(torch.autograd.Function):
+    """The double backward as an autograd Function, so that ``torch.func`` transforms
+    reach its batching rule instead of handing batched wrappers to the C ABI.
+    Returns ``(dQ2, dK2, dV2, ddO, stats)``."""
+
+    @staticmethod
+    def forward(Q, K, V, O, dO, ddQ, ddK, ddV, L, causal, window, scale):
+        return _bwdbwd_device(Q, K, V, O, dO, ddQ, ddK, ddV, L, causal, window, scale)
+
+    @staticmethod
+    def setup_context(ctx, inputs, output):
+        ctx.mark_non_differentiable(output[4])
+
+    @staticmethod
+    def backward(ctx, *grads):
+        raise NotImplementedError(
+            "flash_bwdbwd has no derivative: third-order derivatives of attention are not supported (the "
+            "reference's double-backward rule is the last one it defines, flash_hog/jax/attention.py:100-130)")
+
+    @staticmethod
+    def vmap(info, in_dims, Q, K, V, O, dO, ddQ, ddK, ddV, L, causal, window, scale):
+        """Batching rule of ``flash_hog/jax/_pallas_gpu.py:85-102``: the vmapped axis is
+        folded into the batch axis, the kernels run once, and the results are unfolded.
+        The reference requires every input to be vmapped; here an input that is not is
+        broadcast along the vmapped axis first."""
+        size = info.batch_size
+        args = [_fold(x, d, size) for x, d in zip((Q, K, V, O, dO, ddQ, ddK, ddV, L), in_dims[:9])]
+        dq2, dk2, dv2, ddo, stats = _FlashBwdBwd.apply(*args, causal, window, scale)
+        stats = stats.reshape(3, size, stats.shape[1] // size, *stats.shape[2:])
+        return (_unfold(dq2, size), _unfold(dk2, size), _unfold(dv2, size), _unfold(ddo, size), stats), (0, 0, 0, 0, 1)
+
