@@ -7,15 +7,16 @@ query-tiled pass (D = rowsum(dO o O), dQ', ddO, dD, B) and the key-tiled pass
 ``dot_product_attention_bwd_rule_bwd_rule``. Credited FLOPs are
 22 GEMM-equivalents x 2 x D per kept (query, key) pair (378.1 GFLOP per step).
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload cfg2|cfg3|cfg4]
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload cfg2|cfg3|cfg4|...]
 
 ``--workload`` (default cfg2, the headline) also measures the other GPU
 configurations with the same kernels: cfg3 = causal B2 H32 S8192 D128 (plus peak
 device memory against the sequence length), cfg4 = non-causal B8 H16 Sq4096
 Sk2048 D128, gpt = the grad-norm-penalty training step of a 12-layer GPT (tokens/s,
 NCCL gradient all-reduce under torchrun), fwdbwd / fwdbwd128 = the first-order forward
-and backward on the cfg2 / cfg3 shapes beside torch SDPA (cuDNN). Those lines are
-reported measurements, not the headline.
+and backward on the cfg2 / cfg3 shapes beside torch SDPA (cuDNN), f32 = fp32 inputs on
+the cfg2 shape through the fp32-product kernels. Those lines are reported measurements,
+not the headline.
 
 Under torchrun every rank runs the workload on its own GPU (batch x heads of a
 global batch 4N; no collective on the data path) and rank 0 prints one JSON line
@@ -403,6 +404,89 @@ def run_fwdbwd(args):
     return 0
 
 
+FP32_FMA_TFLOPS_NOMINAL = 148 * 128 * 2 * 1.965e9 / 1e12  # SMs x fp32 lanes x 2 x max SM clock
+
+
+def run_f32(args):
+    """Diagnostic line, not the headline: fp32 inputs on the cfg2 shape (causal
+    B4 H16 S2048 D64) through the fp32-product kernels -- forward, backward and
+    double backward per step, each timed with CUDA events -- beside torch's SDPA
+    on the same fp32 inputs for the forward and backward. Roofline: the CUDA cores'
+    fp32 FMA rate (nominal; no measured figure exists for it). 1 GPU."""
+    import torch.nn.functional as F
+    from flash_hog_b200 import _capi
+    from oracle.attention_oracle import make_inputs
+
+    set_workload("cfg2")
+    dev = torch.device("cuda", 0)
+    sets = []
+    for i in range(N_SETS):
+        x = {k: v.to(dev) for k, v in make_inputs(B, H, SQ, SK, D, seed=i, dtype=torch.float32).items()}
+        x["o"], x["lse"] = torch.empty_like(x["q"]), torch.empty((B, H, SQ), dtype=torch.float32, device=dev)
+        x["out"] = [torch.empty_like(x[n]) for n in ("q", "k", "v", "q", "k", "v", "q")]
+        x["stats"] = torch.empty((3, B, H, SQ), dtype=torch.float32, device=dev)
+        sets.append(x)
+
+    def ours(i, ev):
+        x = sets[i % N_SETS]
+        dq, dk, dv, dq2, dk2, dv2, ddo = x["out"]
+        st = x["stats"]
+        ev[0].record()
+        _capi.attn_fwd_f32(x["q"], x["k"], x["v"], x["o"], x["lse"], SCALE, CAUSAL)
+        ev[1].record()
+        _capi.attn_bwd_f32(x["q"], x["k"], x["v"], x["o"], x["do"], x["lse"], dq, dk, dv, st[0], SCALE, CAUSAL)
+        ev[2].record()
+        _capi.attn_bwdbwd_f32(x["q"], x["k"], x["v"], x["o"], x["do"], x["ddq"], x["ddk"], x["ddv"], x["lse"], dq2,
+                              ddo, dk2, dv2, st[0], st[1], st[2], SCALE, CAUSAL)
+        ev[3].record()
+
+    bhtd = [{n: x[n].transpose(1, 2) for n in ("q", "k", "v", "do")} for x in sets]
+
+    def sdpa(i, ev):
+        x = bhtd[i % N_SETS]
+        q, k, v = (x[n].detach().requires_grad_(True) for n in ("q", "k", "v"))
+        ev[0].record()
+        out = F.scaled_dot_product_attention(q, k, v, is_causal=CAUSAL, scale=SCALE)
+        ev[1].record()
+        torch.autograd.grad(out, (q, k, v), x["do"])
+        ev[2].record()
+        ev[3].record()
+
+    def timed(fn, steps):
+        evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(steps)]
+        for i in range(args.warmup):
+            fn(i, evs[0])
+        torch.cuda.synchronize()
+        n0 = _capi.launch_count()
+        for i in range(steps):
+            fn(i, evs[i])
+        torch.cuda.synchronize()
+        return [statistics.median(e[j].elapsed_time(e[j + 1]) for e in evs) for j in range(3)], \
+            _capi.launch_count() - n0
+
+    with ClockSampler([0]) as clocks:
+        (f, b, bb), launches = timed(ours, args.steps)
+    (fs, bs, _), _ = timed(sdpa, args.steps)
+    p = pairs(B, H, SQ, SK, CAUSAL)
+    tf = lambda gemms, ms: gemms * 2 * D * p / (ms * 1e-3) / 1e12
+    print(json.dumps({
+        "metric": f"attention double backward TFLOP/s, fp32 inputs ({describe().replace('bf16', 'fp32')})",
+        "value": tf(22, bb), "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": f + b + bb, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": f"fwd + bwd + bwdbwd {describe().replace('bf16', 'fp32')}", "name": "f32",
+                   "l2": "3 rotating input sets of ~270 MB each", "credited_gemm_eq": {"fwd": 2, "bwd": 5, "bwdbwd": 22}},
+        "fwd": {"ms": f, "tflops": tf(2, f)}, "bwd": {"ms": b, "tflops": tf(5, b)},
+        "bwdbwd": {"ms": bb, "tflops": tf(22, bb)},
+        "torch_sdpa_fp32": {"fwd_ms": fs, "fwd_tflops": tf(2, fs), "bwd_ms": bs, "bwd_tflops": tf(5, bs)},
+        "roofline": {"bound": "fp32 FMA (CUDA cores)", "achieved": tf(22, bb), "peak": FP32_FMA_TFLOPS_NOMINAL,
+                     "unit": "TFLOP/s", "frac": tf(22, bb) / FP32_FMA_TFLOPS_NOMINAL,
+                     "peak_source": "nominal: 148 SMs x 128 lanes x 2 x 1.965 GHz", "traffic": None},
+        "cpu_baseline": None, "e2e": None, "clocks": clocks.summary(), "gpu_launches": launches,
+    }), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -411,11 +495,14 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--skip-e2e", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["gpt", "fwdbwd", "fwdbwd128"], default="cfg2")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["gpt", "fwdbwd", "fwdbwd128", "f32"], default="cfg2")
     args = ap.parse_args()
     if args.workload in ("fwdbwd", "fwdbwd128"):
         args.warmup = max(args.warmup, 3)
         return run_fwdbwd(args)
+    if args.workload == "f32":
+        args.warmup = max(args.warmup, 3)
+        return run_f32(args)
     if args.workload == "gpt":
         if args.warmup < 3:
             args.warmup = 3
