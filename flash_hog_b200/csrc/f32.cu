@@ -196,8 +196,16 @@ __device__ __forceinline__ long long stat_index(const AttnShape& s, int b, int h
 // Forward: O = softmax(scale Q K^T) V, L = log-sum-exp (natural log), online over key
 // tiles (flash_hog/jax/_attention_impl.py:224-239 computes these with cuDNN).
 // ------------------------------------------------------------------------------------
+// Two CTAs per SM where shared memory allows (forward and first-order backward; the
+// double-backward passes need 171-209 KB per CTA): twice the resident warps to hide
+// shared-memory and global-load latency, at <= 128 registers per thread.
 template <int HD>
-__global__ void __launch_bounds__(kThreads, 1)
+constexpr int kFwdCtas = 2;
+template <int HD>
+constexpr int kDkdvCtas = HD == 64 ? 2 : 1;
+
+template <int HD>
+__global__ void __launch_bounds__(kThreads, kFwdCtas<HD>)
     fwd_kernel(AttnShape s, const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v,
                float* __restrict__ o, float* __restrict__ lse) {
   using G = Geo<HD>;
@@ -287,7 +295,7 @@ __global__ void __launch_bounds__(kThreads)
 //   query side: dQ = dS K;   key side: dV = P^T dO, dK = dS^T Q.
 // ------------------------------------------------------------------------------------
 template <int HD>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, kFwdCtas<HD>)
     dq_kernel(AttnShape s, const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v,
               const float* __restrict__ dO, const float* __restrict__ lse, const float* __restrict__ delta,
               float* __restrict__ dq, const float* dq_acc) {
@@ -340,7 +348,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 template <int HD>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, kDkdvCtas<HD>)
     dkdv_kernel(AttnShape s, const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v,
                 const float* __restrict__ dO, const float* __restrict__ lse, const float* __restrict__ delta,
                 float* __restrict__ dk, float* __restrict__ dv, const float* dk_acc, const float* dv_acc) {
