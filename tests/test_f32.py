@@ -177,3 +177,22 @@ def test_f32_kernels_on_the_golden_inputs():
     for name, g, r in zip(("dq2", "dk2", "dv2", "ddo"), got, ref):
         assert_close(name, np64(g), r, F32_REL_TOL)
         assert ora.rel_err(np64(g)[0, :, 0], d[name].astype(np.float64)) <= 1e-2, name
+
+
+@pytest.mark.gpu
+def test_fp16_inputs_run_the_bf16_kernels():
+    """fp16 inputs are cast to bf16, as the reference's native plugin casts every dtype
+    (``flash_hog/jax/_tk_gpu.py:90-92``); results come back in fp16 within the bf16 bar."""
+    from flash_hog_b200.attention import dot_product_attention
+
+    x = ora.make_inputs(1, 2, 192, 192, 64, seed=8, dtype=torch.float16)
+    ref = ora.autograd_all(*(x[n].double() for n in ("q", "k", "v", "do", "ddq", "ddk", "ddv")), causal=True)
+    c = {n: t.cuda() for n, t in x.items()}
+    q, k, v, do = (c[n].clone().requires_grad_(True) for n in ("q", "k", "v", "do"))
+    o = dot_product_attention(q, k, v, is_causal=True)
+    dq, dk, dv = torch.autograd.grad(o, (q, k, v), do, create_graph=True)
+    dq2, dk2, dv2, ddo = torch.autograd.grad((dq, dk, dv), (q, k, v, do), (c["ddq"], c["ddk"], c["ddv"]))
+    for name, got in (("o", o), ("dq", dq), ("dk", dk), ("dv", dv), ("dq2", dq2), ("dk2", dk2), ("dv2", dv2),
+                      ("ddo", ddo)):
+        assert got.dtype == torch.float16, name
+        assert_close(name, np64(got), ref[name].numpy())
