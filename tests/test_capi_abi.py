@@ -87,6 +87,31 @@ def test_argument_validation_codes():
     assert _fwd(d) == 1
 
 
+def test_f32_entry_points_validate_like_the_bf16_ones():
+    """The fp32 entries share the dims/mask/alignment checks (all before any CUDA call)."""
+    from flash_hog_b200._capi import lib
+
+    h = lib()
+    p = ctypes.c_void_p(64)
+
+    def fwd(dims, ptr=64, causal=1):
+        q = ctypes.c_void_p(ptr)
+        return h.fh_attn_fwd_f32(None, ctypes.byref(dims), q, q, q, q, q, 0.125, causal)
+
+    assert fwd(_dims(), causal=3) == 1
+    assert fwd(_dims(head_dim=96)) == 2
+    assert fwd(_dims(window=8), causal=0) == 1
+    assert fwd(_dims(), ptr=8) == 1
+    assert h.fh_attn_bwd_f32(None, ctypes.byref(_dims()), p, p, p, p, p, None, p, p, p, p, 0.125, 1) == 1  # no lse
+    bb = lambda passes, dq2=p, o=p: h.fh_attn_bwdbwd_f32(None, ctypes.byref(_dims()), p, p, p, o, p, p, p, p, p,
+                                                        dq2, p, p, p, p, p, p, 0.125, 1, passes)
+    assert bb(0) == 1 and bb(4) == 1            # passes outside 1..3
+    assert bb(1, o=None) == 1                   # the query pass needs o (it computes D)
+    assert bb(1, dq2=ctypes.c_void_p(8)) == 1   # dq2 may be NULL, but not misaligned
+    assert h.fh_attn_jvp_bwd_f32(None, ctypes.byref(_dims()), *([p] * 9), ctypes.c_void_p(8), *([p] * 7), 0.125,
+                                 1) == 1        # misaligned tdO
+
+
 def test_error_injection_is_host_side():
     """FLASH_HOG_B200_INJECT_ERROR makes the named entry return FH_ERR_INJECTED
     before any validation or CUDA call (checked in a fresh process)."""
