@@ -273,8 +273,9 @@ def test_headline_config_full_size_sampled_heads():
 
 
 def test_device_status_clean_and_fp32_inputs():
-    """fp32 inputs are cast to bf16 (as the reference's native plugin does) and the
-    result returns in fp32; no device error is recorded."""
+    """fp32 inputs run the fp32-product kernels and the result returns in fp32 (held
+    here to the bf16 bar; ``tests/test_f32.py`` holds them to 1e-3); no device error
+    is recorded."""
     import flash_hog_b200 as fhb
     from flash_hog_b200._capi import device_status
 
