@@ -78,6 +78,31 @@ __device__ __forceinline__ void load_rows(float* dst, const float* __restrict__ 
   }
 }
 
+// load_rows with cp.async (16-byte copies, zero-filled past `len`): the copies
+// land in shared memory without passing through registers and complete at the
+// next cp_async_wait, so a tile can be fetched while the previous one is used.
+template <int HD, int ROWS>
+__device__ __forceinline__ void load_rows_async(float* dst, const float* __restrict__ src, const Strides3& st, int b,
+                                                int h, int row0, int len) {
+  constexpr int CH = HD / 4;
+  const float* base = src + static_cast<long long>(b) * st.b + static_cast<long long>(h) * st.h;
+  for (int idx = threadIdx.x; idx < ROWS * CH; idx += kThreads) {
+    const int r = idx / CH, c = idx - r * CH;
+    const int t = row0 + r;
+    const bool ok = t < len;
+    const float* g = ok ? base + static_cast<long long>(t) * st.t + 4 * c : base;  // no bytes read when !ok
+    const unsigned sa = static_cast<unsigned>(__cvta_generic_to_shared(dst + r * (HD + 4) + 4 * c));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(sa), "l"(g), "r"(ok ? 16 : 0) : "memory");
+  }
+  asm volatile("cp.async.commit_group;\n" ::: "memory");
+}
+
+// Waits until at most N of this thread's committed cp.async groups are pending.
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
 // Per-query statistics of a streamed query tile: dst[r] = src[(b H + h) Tq + q0 + r] (0 past Tq).
 __device__ __forceinline__ void load_stats(float* dst, const float* __restrict__ src, const AttnShape& s, int b, int h,
                                            int q0, int n) {
@@ -210,10 +235,11 @@ __global__ void __launch_bounds__(kThreads, kFwdCtas<HD>)
                float* __restrict__ o, float* __restrict__ lse) {
   using G = Geo<HD>;
   extern __shared__ float4 smem_f4[];
+  // K and V tiles are double-buffered: buffer it & 1 holds tile it, and tile it + 1
+  // is fetched (cp.async) while tile it is used.
   float* sQ = reinterpret_cast<float*>(smem_f4);
-  float* sK = sQ + G::RES;
-  float* sV = sK + G::STR;
-  float* sP = sV + G::STR;
+  float* sKV = sQ + G::RES;  // [2][K | V]
+  float* sP = sKV + 4 * G::STR;
   const int r0 = blockIdx.x * kRes, h = blockIdx.y, b = blockIdx.z, hk = h / s.G;
   const int rg = threadIdx.x >> 4, cg = threadIdx.x & 15;
   load_rows<HD, kRes>(sQ, q, s.sq, b, h, r0, s.Tq);
@@ -223,12 +249,24 @@ __global__ void __launch_bounds__(kThreads, kFwdCtas<HD>)
   zero(acc);
   int first;
   const int nt = key_tiles(s, r0, kRes, G::BN, &first);
+  auto fetch = [&](int t) {
+    float* buf = sKV + (t & 1) * 2 * G::STR;
+    load_rows_async<HD, G::BN>(buf, k, s.sk, b, hk, (first + t) * G::BN, s.Tk);
+    load_rows_async<HD, G::BN>(buf + G::STR, v, s.sk, b, hk, (first + t) * G::BN, s.Tk);
+  };
+  if (nt > 0) fetch(0);
   for (int it = 0; it < nt; ++it) {
     const int c0 = (first + it) * G::BN;
+    // Buffer (it + 1) & 1 was last read in iteration it - 1, which ended with a barrier.
+    if (it + 1 < nt) {
+      fetch(it + 1);
+      cp_async_wait<2>();  // tile it's two groups have landed; tile it + 1's may be pending
+    } else {
+      cp_async_wait<0>();
+    }
     __syncthreads();
-    load_rows<HD, G::BN>(sK, k, s.sk, b, hk, c0, s.Tk);
-    load_rows<HD, G::BN>(sV, v, s.sk, b, hk, c0, s.Tk);
-    __syncthreads();
+    const float* sK = sKV + (it & 1) * 2 * G::STR;
+    const float* sV = sK + G::STR;
     float sc[4][G::NC];
     zero(sc);
     score_acc<HD, kRes, G::NC>(sc, sQ, sK, rg, cg);
@@ -258,6 +296,7 @@ __global__ void __launch_bounds__(kThreads, kFwdCtas<HD>)
     }
     __syncthreads();
     out_acc<HD, G::BN>(acc, sP, sV, rg, cg);
+    __syncthreads();  // sP and this tile's buffer are free for the next iteration
   }
   float inv[4];
 #pragma unroll
@@ -637,8 +676,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 template <int HD>
 constexpr int smem_fwd() {
   using G = Geo<HD>;
-  return (G::RES + 2 * G::STR + G::SCORE) * 4;
+  return (G::RES + 4 * G::STR + G::SCORE) * 4;
 }
+static_assert(2 * (smem_fwd<64>() + 1024) <= 233472 && 2 * (smem_fwd<128>() + 1024) <= 233472,
+              "two forward CTAs per SM");
 template <int HD>
 constexpr int smem_dq() {
   using G = Geo<HD>;
