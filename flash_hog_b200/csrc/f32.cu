@@ -103,6 +103,28 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
 }
 
+// load_stats with 4-byte cp.async copies (zero past Tq); not committed here: the
+// caller's next load_rows_async commits them with its rows.
+__device__ __forceinline__ void stats_async(float* dst, const float* __restrict__ src, const AttnShape& s, int b,
+                                            int h, int q0, int n) {
+  for (int r = threadIdx.x; r < n; r += kThreads) {
+    const int t = q0 + r;
+    const bool ok = t < s.Tq;
+    const float* g = ok ? src + (static_cast<long long>(b) * s.H + h) * s.Tq + t : src;
+    const unsigned sa = static_cast<unsigned>(__cvta_generic_to_shared(dst + r));
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(sa), "l"(g), "r"(ok ? 4 : 0) : "memory");
+  }
+}
+
+// Streamed-tile buffers of the double backward's key pass: two where shared memory
+// allows (head_dim 64: 223 KB per CTA), else one.
+template <int HD>
+struct KeyPassBuffers {
+  using G = Geo<HD>;
+  static constexpr int bytes(int n) { return (4 * G::RES + n * (3 * G::STR + 4 * G::BN) + 3 * G::SCORE) * 4; }
+  static constexpr int N = bytes(2) <= 232448 ? 2 : 1;
+};
+
 // Per-query statistics of a streamed query tile: dst[r] = src[(b H + h) Tq + q0 + r] (0 past Tq).
 __device__ __forceinline__ void load_stats(float* dst, const float* __restrict__ src, const AttnShape& s, int b, int h,
                                            int q0, int n) {
@@ -594,20 +616,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                float* __restrict__ dv2) {
   using G = Geo<HD>;
   extern __shared__ float4 smem_f4[];
+  constexpr int NBUF = KeyPassBuffers<HD>::N;
+  constexpr int BUF = 3 * G::STR + 4 * G::BN;  // Q | dO | ddQ | L | D | dD | B of one query tile
   float* sK = reinterpret_cast<float*>(smem_f4);
   float* sV = sK + G::RES;
   float* sddK = sV + G::RES;
   float* sddV = sddK + G::RES;
-  float* sQ = sddV + G::RES;
-  float* sdO = sQ + G::STR;
-  float* sddQ = sdO + G::STR;
-  float* tDS = sddQ + G::STR;
+  float* sbuf = sddV + G::RES;  // [NBUF][BUF]
+  float* tDS = sbuf + NBUF * BUF;
   float* tDS2 = tDS + G::SCORE;
   float* tDDP = tDS2 + G::SCORE;
-  float* sL = tDDP + G::SCORE;
-  float* sD = sL + G::BN;
-  float* sdD = sD + G::BN;
-  float* sB = sdD + G::BN;
   const int k0 = blockIdx.x * kRes, hk = blockIdx.y, b = blockIdx.z;
   const int rg = threadIdx.x >> 4, cg = threadIdx.x & 15;
   load_rows<HD, kRes>(sK, k, s.sk, b, hk, k0, s.Tk);
@@ -619,19 +637,45 @@ __global__ void __launch_bounds__(kThreads, 1)
   zero(av);
   int first;
   const int nt = query_tiles(s, k0, kRes, G::BN, &first);
-  for (int g = 0; g < s.G; ++g) {
-    const int h = hk * s.G + g;
-    for (int it = 0; it < nt; ++it) {
-      const int q0 = (first + it) * G::BN;
-      __syncthreads();
-      load_rows<HD, G::BN>(sQ, q, s.sq, b, h, q0, s.Tq);
-      load_rows<HD, G::BN>(sdO, dO, s.sq, b, h, q0, s.Tq);
-      load_rows<HD, G::BN>(sddQ, ddq, s.sq, b, h, q0, s.Tq);
-      load_stats(sL, lse, s, b, h, q0, G::BN);
-      load_stats(sD, delta, s, b, h, q0, G::BN);
-      load_stats(sdD, dd, s, b, h, q0, G::BN);
-      load_stats(sB, bvec, s, b, h, q0, G::BN);
-      __syncthreads();
+  // Items u = (query head g of the group, query tile it) in order; with two buffers,
+  // item u + 1 is fetched (cp.async) while item u is used.
+  const int total = s.G * nt;
+  auto fetch = [&](int u) {
+    const int h = hk * s.G + u / nt, q0 = (first + u % nt) * G::BN;
+    float* buf = sbuf + (u % NBUF) * BUF;
+    float* st = buf + 3 * G::STR;
+    stats_async(st, lse, s, b, h, q0, G::BN);
+    stats_async(st + G::BN, delta, s, b, h, q0, G::BN);
+    stats_async(st + 2 * G::BN, dd, s, b, h, q0, G::BN);
+    stats_async(st + 3 * G::BN, bvec, s, b, h, q0, G::BN);
+    load_rows_async<HD, G::BN>(buf, q, s.sq, b, h, q0, s.Tq);  // commits the statistics too
+    load_rows_async<HD, G::BN>(buf + G::STR, dO, s.sq, b, h, q0, s.Tq);
+    load_rows_async<HD, G::BN>(buf + 2 * G::STR, ddq, s.sq, b, h, q0, s.Tq);
+  };
+  if (NBUF == 2 && total > 0) fetch(0);
+  for (int u = 0; u < total; ++u) {
+    const int q0 = (first + u % nt) * G::BN;
+    if (NBUF == 2) {
+      // Buffer (u + 1) % 2 was last read in item u - 1, which ended with a barrier.
+      if (u + 1 < total) {
+        fetch(u + 1);
+        cp_async_wait<3>();  // item u's three groups have landed
+      } else {
+        cp_async_wait<0>();
+      }
+    } else {
+      fetch(u);  // the previous item ended with a barrier
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    const float* sQ = sbuf + (u % NBUF) * BUF;
+    const float* sdO = sQ + G::STR;
+    const float* sddQ = sdO + G::STR;
+    const float* sL = sddQ + G::STR;
+    const float* sD = sL + G::BN;
+    const float* sdD = sD + G::BN;
+    const float* sB = sdD + G::BN;
+    {
       // Transposed products: rows are keys, columns queries.
       float st[4][G::NC], dpt[4][G::NC], ddst[4][G::NC], xt[4][G::NC];
       zero(st);
@@ -667,6 +711,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       out_acc<HD, G::BN>(ak, tDS2, sQ, rg, cg);
       out_acc<HD, G::BN>(av, tDDP, sdO, rg, cg);
     }
+    __syncthreads();  // this item's buffer and the score tiles are free
   }
   const float one[4] = {1.f, 1.f, 1.f, 1.f};
   store_rows<HD>(dk2, nullptr, s.sk, b, hk, k0, s.Tk, ak, one, rg, cg);
@@ -697,9 +742,9 @@ constexpr int smem_bbq() {
 }
 template <int HD>
 constexpr int smem_bbk() {
-  using G = Geo<HD>;
-  return (4 * G::RES + 3 * G::STR + 3 * G::SCORE + 4 * G::BN) * 4;
+  return KeyPassBuffers<HD>::bytes(KeyPassBuffers<HD>::N);
 }
+static_assert(KeyPassBuffers<64>::N == 2 && KeyPassBuffers<128>::N == 1, "key-pass buffering");
 static_assert(smem_bbq<64>() <= 232448 && smem_bbk<64>() <= 232448, "shared memory per CTA");
 static_assert(smem_bbq<128>() <= 232448 && smem_bbk<128>() <= 232448, "shared memory per CTA");
 
