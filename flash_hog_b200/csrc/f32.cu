@@ -116,6 +116,15 @@ __device__ __forceinline__ void stats_async(float* dst, const float* __restrict_
   }
 }
 
+// Key-tile buffers of the double backward's query pass: two where shared memory
+// allows (head_dim 64: 221 KB per CTA), else one.
+template <int HD>
+struct QueryPassBuffers {
+  using G = Geo<HD>;
+  static constexpr int bytes(int n) { return (3 * G::RES + n * 4 * G::STR + 2 * G::SCORE) * 4; }
+  static constexpr int N = bytes(2) <= 232448 ? 2 : 1;
+};
+
 // Streamed-tile buffers of the double backward's key pass: two where shared memory
 // allows (head_dim 64: 223 KB per CTA), else one.
 template <int HD>
@@ -486,18 +495,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                float* __restrict__ dq2, float* __restrict__ ddo, float* __restrict__ dd_out,
                float* __restrict__ b_out) {
   using G = Geo<HD>;
+  constexpr int NBUF = QueryPassBuffers<HD>::N;
+  constexpr int BUF = 4 * G::STR;  // K | V | ddK | ddV of one key tile
   extern __shared__ float4 smem_f4[];
   float* sQ = reinterpret_cast<float*>(smem_f4);
   float* sdO = sQ + G::RES;
   float* sddQ = sdO + G::RES;
-  float* sK = sddQ + G::RES;
-  float* sV = sK + G::STR;
-  float* sddK = sV + G::STR;
-  float* sddV = sddK + G::STR;
-  float* tDS = sddV + G::STR;
-  float* tDS2 = tDS + G::SCORE;
-  float* tDDP = tDS2 + G::SCORE;
-  float* tP = tDDP + G::SCORE;
+  float* kbuf = sddQ + G::RES;  // [NBUF][BUF]
+  float* tA = kbuf + NBUF * BUF;
+  float* tB = tA + G::SCORE;
   const int r0 = blockIdx.x * kRes, h = blockIdx.y, b = blockIdx.z, hk = h / s.G;
   const int rg = threadIdx.x >> 4, cg = threadIdx.x & 15;
   load_rows<HD, kRes>(sQ, q, s.sq, b, h, r0, s.Tq);
@@ -513,9 +519,60 @@ __global__ void __launch_bounds__(kThreads, 1)
   int first;
   const int nt = key_tiles(s, r0, kRes, G::BN, &first);
 
-  // One tile's four score-like products: S, dP, ddS (scaled) and X.
-  auto products = [&](float (&sc)[4][G::NC], float (&dp)[4][G::NC], float (&dds)[4][G::NC],
-                      float (&x)[4][G::NC]) {
+  // Items u = 0 .. 2 nt - 1: sweep 1 (row statistics) over the key tiles, then sweep 2
+  // (dQ', ddO) over the same tiles. With two buffers, item u + 1's tile is fetched
+  // (cp.async) while item u's is used, across the sweep boundary too.
+  const int total = 2 * nt;
+  auto fetch = [&](int u) {
+    const int c0 = (first + u % nt) * G::BN;
+    float* buf = kbuf + (u % NBUF) * BUF;
+    load_rows_async<HD, G::BN>(buf, k, s.sk, b, hk, c0, s.Tk);
+    load_rows_async<HD, G::BN>(buf + G::STR, v, s.sk, b, hk, c0, s.Tk);
+    load_rows_async<HD, G::BN>(buf + 2 * G::STR, ddk, s.sk, b, hk, c0, s.Tk);
+    load_rows_async<HD, G::BN>(buf + 3 * G::STR, ddv, s.sk, b, hk, c0, s.Tk);
+  };
+
+  float sdd[4] = {0.f, 0.f, 0.f, 0.f}, sy[4] = {0.f, 0.f, 0.f, 0.f}, sx[4] = {0.f, 0.f, 0.f, 0.f},
+        sz[4] = {0.f, 0.f, 0.f, 0.f};
+  float dD[4], Bv[4];
+  auto finish_stats = [&]() {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      dD[i] = sum16(sdd[i]);
+      Bv[i] = sum16(sx[i]) - dD[i] * sum16(sy[i]) - D[i] * dD[i] + sum16(sz[i]);
+      const int row = r0 + rg * 4 + i;
+      if (cg == 0 && row < s.Tq) {
+        dd_out[stat_index(s, b, h, row)] = dD[i];
+        b_out[stat_index(s, b, h, row)] = Bv[i];
+      }
+    }
+  };
+  float aq[4][G::NO], ao[4][G::NO];
+  zero(aq);
+  zero(ao);
+
+  if (NBUF == 2 && total > 0) fetch(0);
+  for (int u = 0; u < total; ++u) {
+    const int c0 = (first + u % nt) * G::BN;
+    if (NBUF == 2) {
+      // Buffer (u + 1) % 2 was last read in item u - 1, which ended with a barrier.
+      if (u + 1 < total) {
+        fetch(u + 1);
+        cp_async_wait<4>();  // item u's four groups have landed
+      } else {
+        cp_async_wait<0>();
+      }
+    } else {
+      fetch(u);  // the previous item ended with a barrier
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    const float* sK = kbuf + (u % NBUF) * BUF;
+    const float* sV = sK + G::STR;
+    const float* sddK = sV + G::STR;
+    const float* sddV = sddK + G::STR;
+    // The tile's four score-like products: S, dP, ddS (unscaled) and X.
+    float sc[4][G::NC], dp[4][G::NC], dds[4][G::NC], x[4][G::NC];
     zero(sc);
     zero(dp);
     zero(dds);
@@ -525,83 +582,60 @@ __global__ void __launch_bounds__(kThreads, 1)
     score_acc<HD, kRes, G::NC>(dds, sddQ, sK, rg, cg);
     score_acc<HD, kRes, G::NC>(dds, sQ, sddK, rg, cg);
     score_acc<HD, kRes, G::NC>(x, sdO, sddV, rg, cg);
-  };
-  auto load_tile = [&](int c0) {
-    __syncthreads();
-    load_rows<HD, G::BN>(sK, k, s.sk, b, hk, c0, s.Tk);
-    load_rows<HD, G::BN>(sV, v, s.sk, b, hk, c0, s.Tk);
-    load_rows<HD, G::BN>(sddK, ddk, s.sk, b, hk, c0, s.Tk);
-    load_rows<HD, G::BN>(sddV, ddv, s.sk, b, hk, c0, s.Tk);
-    __syncthreads();
-  };
-
-  // Sweep 1: row statistics.
-  float sdd[4] = {0.f, 0.f, 0.f, 0.f}, sy[4] = {0.f, 0.f, 0.f, 0.f}, sx[4] = {0.f, 0.f, 0.f, 0.f},
-        sz[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int it = 0; it < nt; ++it) {
-    const int c0 = (first + it) * G::BN;
-    load_tile(c0);
-    float sc[4][G::NC], dp[4][G::NC], dds[4][G::NC], x[4][G::NC];
-    products(sc, dp, dds, x);
+    if (u < nt) {  // sweep 1 (block-uniform branch)
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
+      for (int i = 0; i < 4; ++i)
 #pragma unroll
-      for (int j = 0; j < G::NC; ++j) {
-        if (!visible(s, r0 + rg * 4 + i, c0 + cg + 16 * j)) continue;
-        const float p = expf(sc[i][j] * s.scale - L[i]);
-        const float d2 = dds[i][j] * s.scale;
-        sdd[i] = fmaf(p, d2, sdd[i]);
-        sy[i] = fmaf(p, dp[i][j], sy[i]);
-        sx[i] = fmaf(p, x[i][j], sx[i]);
-        sz[i] = fmaf(p * dp[i][j], d2, sz[i]);
-      }
-  }
-  float dD[4], Bv[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    dD[i] = sum16(sdd[i]);
-    Bv[i] = sum16(sx[i]) - dD[i] * sum16(sy[i]) - D[i] * dD[i] + sum16(sz[i]);
-    const int row = r0 + rg * 4 + i;
-    if (cg == 0 && row < s.Tq) {
-      dd_out[stat_index(s, b, h, row)] = dD[i];
-      b_out[stat_index(s, b, h, row)] = Bv[i];
-    }
-  }
-
-  // Sweep 2: dQ' and ddO.
-  float aq[4][G::NO], ao[4][G::NO];
-  zero(aq);
-  zero(ao);
-  for (int it = 0; it < nt; ++it) {
-    const int c0 = (first + it) * G::BN;
-    load_tile(c0);
-    float sc[4][G::NC], dp[4][G::NC], dds[4][G::NC], x[4][G::NC];
-    products(sc, dp, dds, x);
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-#pragma unroll
-      for (int j = 0; j < G::NC; ++j) {
-        const int at = (rg * 4 + i) * G::SC + cg + 16 * j;
-        float p = 0.f, ds = 0.f, ds2 = 0.f, ddp = 0.f;
-        if (visible(s, r0 + rg * 4 + i, c0 + cg + 16 * j)) {
-          p = expf(sc[i][j] * s.scale - L[i]);
+        for (int j = 0; j < G::NC; ++j) {
+          if (!visible(s, r0 + rg * 4 + i, c0 + cg + 16 * j)) continue;
+          const float p = expf(sc[i][j] * s.scale - L[i]);
           const float d2 = dds[i][j] * s.scale;
-          const float dp2 = x[i][j] - dp[i][j] * dD[i] - d2 * D[i] + dp[i][j] * d2;
-          ds = s.scale * p * (dp[i][j] - D[i]);
-          ds2 = s.scale * p * (dp2 - Bv[i]);
-          ddp = p * (d2 - dD[i]);
+          sdd[i] = fmaf(p, d2, sdd[i]);
+          sy[i] = fmaf(p, dp[i][j], sy[i]);
+          sx[i] = fmaf(p, x[i][j], sx[i]);
+          sz[i] = fmaf(p * dp[i][j], d2, sz[i]);
         }
-        tP[at] = p;
-        tDS[at] = ds;
-        tDS2[at] = ds2;
-        tDDP[at] = ddp;
-      }
-    __syncthreads();
-    out_acc<HD, G::BN>(aq, tDS, sddK, rg, cg);
-    out_acc<HD, G::BN>(aq, tDS2, sK, rg, cg);
-    out_acc<HD, G::BN>(ao, tDDP, sV, rg, cg);
-    out_acc<HD, G::BN>(ao, tP, sddV, rg, cg);
+      if (u == nt - 1) finish_stats();
+    } else {  // sweep 2, in two halves over the two score tiles
+      float ds2[4][G::NC], pp[4][G::NC];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < G::NC; ++j) {
+          const int at = (rg * 4 + i) * G::SC + cg + 16 * j;
+          float p = 0.f, ds = 0.f, d2s = 0.f, ddp = 0.f;
+          if (visible(s, r0 + rg * 4 + i, c0 + cg + 16 * j)) {
+            p = expf(sc[i][j] * s.scale - L[i]);
+            const float d2 = dds[i][j] * s.scale;
+            const float dp2 = x[i][j] - dp[i][j] * dD[i] - d2 * D[i] + dp[i][j] * d2;
+            ds = s.scale * p * (dp[i][j] - D[i]);
+            d2s = s.scale * p * (dp2 - Bv[i]);
+            ddp = p * (d2 - dD[i]);
+          }
+          tA[at] = ds;
+          tB[at] = ddp;
+          ds2[i][j] = d2s;
+          pp[i][j] = p;
+        }
+      __syncthreads();
+      out_acc<HD, G::BN>(aq, tA, sddK, rg, cg);  // dQ' += dS ddK
+      out_acc<HD, G::BN>(ao, tB, sV, rg, cg);    // ddO += ddP V
+      __syncthreads();
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < G::NC; ++j) {
+          const int at = (rg * 4 + i) * G::SC + cg + 16 * j;
+          tA[at] = ds2[i][j];
+          tB[at] = pp[i][j];
+        }
+      __syncthreads();
+      out_acc<HD, G::BN>(aq, tA, sK, rg, cg);    // dQ' += dS2 K
+      out_acc<HD, G::BN>(ao, tB, sddV, rg, cg);  // ddO += P ddV
+    }
+    __syncthreads();  // this item's buffer and the score tiles are free
   }
+  if (nt == 0) finish_stats();  // rows that see no key: dD = B = 0
   const float one[4] = {1.f, 1.f, 1.f, 1.f};
   if (dq2) store_rows<HD>(dq2, nullptr, s.sq, b, h, r0, s.Tq, aq, one, rg, cg);
   store_rows<HD>(ddo, nullptr, s.sq, b, h, r0, s.Tq, ao, one, rg, cg);
@@ -737,9 +771,9 @@ constexpr int smem_dkdv() {
 }
 template <int HD>
 constexpr int smem_bbq() {
-  using G = Geo<HD>;
-  return (3 * G::RES + 4 * G::STR + 4 * G::SCORE) * 4;
+  return QueryPassBuffers<HD>::bytes(QueryPassBuffers<HD>::N);
 }
+static_assert(QueryPassBuffers<64>::N == 2 && QueryPassBuffers<128>::N == 1, "query-pass buffering");
 template <int HD>
 constexpr int smem_bbk() {
   return KeyPassBuffers<HD>::bytes(KeyPassBuffers<HD>::N);
