@@ -18,7 +18,10 @@
 // Thread (rg, cg) = (tid / 16, tid % 16) owns resident rows 4 rg .. 4 rg + 3;
 // of a score tile it owns columns cg + 16 j, of an output tile the 4-column
 // chunks cg + 16 m. A row's 16 owners are one half-warp, so row reductions are
-// 4 xor-shuffles. There are no waits other than __syncthreads.
+// 4 xor-shuffles. Where shared memory allows a second buffer (the forward; both
+// double-backward passes at head_dim 64) the next streamed tile is fetched with
+// cp.async while the current one is used. No kernel spins: the only waits are
+// __syncthreads and cp.async.wait_group on the CTA's own copies.
 
 #include <cuda_runtime.h>
 
