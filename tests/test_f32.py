@@ -196,3 +196,50 @@ def test_fp16_inputs_run_the_bf16_kernels():
                       ("ddo", ddo)):
         assert got.dtype == torch.float16, name
         assert_close(name, np64(got), ref[name].numpy())
+
+
+F32_EDGE_CASES = [  # b, h, hk, tq, tk, causal, window, d
+    (1, 2, 2, 64, 64, 1, 1, 64),       # window 1: each query sees only its diagonal key
+    (1, 2, 2, 1, 1, 1, 0, 64),         # one query, one key
+    (1, 2, 1, 1, 300, 2, 0, 64),       # one query sees every key (bottom-right), GQA
+    (1, 2, 2, 300, 1, 2, 0, 64),       # one key; only the last query sees it
+    (1, 2, 2, 333, 129, 2, 17, 128),   # bottom-right window, ragged, most rows keyless
+    (2, 4, 1, 130, 390, 2, 65, 64),    # GQA group of 4 with a window crossing tile edges
+]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("b,h,hk,tq,tk,causal,window,d", F32_EDGE_CASES)
+def test_f32_band_mask_edge_cases(b, h, hk, tq, tk, causal, window, d):
+    """The fp32 kernels (including their prefetching loops: one streamed tile, one item,
+    several query heads per key head) on the band's edge cases, at the 1e-3 bar."""
+    from flash_hog_b200 import _attention_impl as impl
+    from flash_hog_b200._attention_impl import MaskType, SlidingWindow
+    from flash_hog_b200.bwdbwd import flash_bwdbwd
+
+    x = _inputs(b, h, hk, tq, tk, d, seed=31)
+    c = {n: t.cuda() for n, t in x.items()}
+    mt = MaskType(causal)
+    mask = SlidingWindow(mt, window) if window else mt
+    sc = d ** -0.5
+    a = {n: np64(t) for n, t in x.items()}
+    kw = dict(scale=sc, causal=causal, window=window)
+    o, lse = impl.cuda_dot_product_attention(c["q"], c["k"], c["v"], mask, sc, return_residual=True)
+    o_r, lse_r = ora.attention_fwd(a["q"], a["k"], a["v"], **kw)
+    assert np.array_equal(np.isneginf(lse.cpu().numpy()), np.isneginf(lse_r))
+    a["o"], a["lse"] = np64(o), lse.double().cpu().numpy()
+    res = (c["q"], c["k"], c["v"], lse, o)
+    grads = impl.dot_product_attention_bwd_rule(mask, sc, res, c["do"])
+    outs = flash_bwdbwd(c["q"], c["k"], c["v"], o, c["do"], c["ddq"], c["ddk"], c["ddv"], lse, mask_type=mask, scale=sc)
+    refs = [o_r] + list(ora.attention_bwd(a["q"], a["k"], a["v"], a["o"], a["lse"], a["do"], **kw)) + list(
+        ora.bwdbwd_stats(a["q"], a["k"], a["v"], a["o"], a["lse"], a["do"], a["ddq"], a["ddk"], a["ddv"], **kw))
+    for name, got, want in zip(("O", "dQ", "dK", "dV", "dQ'", "dK'", "dV'", "ddO"), [o] + list(grads) + list(outs),
+                               refs):
+        g = np64(got)
+        assert np.isfinite(g).all(), name
+        if np.abs(want).max() < 1e-4:
+            # (Near-)exact cancellation (one visible key: P = 1, O = V) leaves fp32
+            # rounding where the float64 oracle gives ~0; a relative bar is meaningless.
+            assert np.abs(g).max() < 1e-4, name
+        else:
+            assert_close(name, g, want, F32_REL_TOL)
