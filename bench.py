@@ -642,12 +642,19 @@ def main():
         torch.cuda.synchronize()
         barrier()
         e2e_ms = e0.elapsed_time(e1) / n_e2e
+        # Diagnostics: whether every rank's host buffers are page-locked (staged copies
+        # of pageable memory are ~6x slower), and the fastest rank's step time.
+        pinned = all(t.is_pinned() for t in list(host.values()) + [x for r in res_host for x in r])
+        e2e_min_ms = e2e_ms
         if dist is not None:
-            t = torch.tensor([e2e_ms], device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            e2e_ms = float(t.item())
+            t = torch.tensor([e2e_ms, -e2e_ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)  # slowest and (negated) fastest rank
+            u = torch.tensor([1.0 if pinned else 0.0], device=dev)
+            dist.all_reduce(u, op=dist.ReduceOp.MIN)  # all pinned
+            e2e_ms, e2e_min_ms, pinned = float(t[0].item()), -float(t[1].item()), bool(u.item() > 0.5)
         e2e = {"value": world * credited_flops(B, H) / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
+               "ms_per_step_fastest_rank": e2e_min_ms, "host_buffers_pinned": pinned,
                "api": "flash_hog_b200.flash_bwdbwd",
                "pipeline": "copy-in, compute and copy-out streams; device inputs double-buffered"}
 
