@@ -16,6 +16,7 @@ from __future__ import annotations
 
 import dataclasses
 import enum
+import os
 
 import torch
 
@@ -59,12 +60,26 @@ def _is_causal(mask) -> bool:
     return _mask_args(mask)[0] != 0
 
 
+FP32_POLICY_ENV = "FLASH_HOG_B200_FP32"
+
+
+def fp32_policy() -> str:
+    """How fp32 inputs are computed: "fp32" (default) -- the fp32-product kernels, as
+    the reference's Pallas rule keeps fp32 operands in fp32
+    (``flash_hog/jax/_pallas_gpu_kernel.py:251-256``); or "bf16" -- cast to bf16 for the
+    tensor-core kernels, as the reference's native plugin does
+    (``flash_hog/jax/_tk_gpu.py:90-92``), with results returned in fp32. Set by the
+    ``FLASH_HOG_B200_FP32`` environment variable, read at each call."""
+    policy = os.environ.get(FP32_POLICY_ENV, "fp32").strip().lower() or "fp32"
+    if policy not in ("fp32", "bf16"):
+        raise ValueError(f"{FP32_POLICY_ENV} must be 'fp32' or 'bf16', got {policy!r}")
+    return policy
+
+
 def _is_f32(x: torch.Tensor) -> bool:
-    """fp32 inputs run the fp32 kernels (fp32 products, ``fh_attn_*_f32``), as the
-    reference's Pallas rule keeps fp32 operands in fp32
-    (``flash_hog/jax/_pallas_gpu_kernel.py:251-256``); every other dtype runs the
-    bf16 tensor-core kernels."""
-    return x.dtype == torch.float32
+    """Whether ``x``'s call runs the fp32 kernels (``fh_attn_*_f32``): fp32 inputs under
+    the default policy. Every other case runs the bf16 tensor-core kernels."""
+    return x.dtype == torch.float32 and fp32_policy() == "fp32"
 
 
 def _operand(x: torch.Tensor, f32: bool) -> torch.Tensor:

@@ -51,6 +51,21 @@ def test_f32_entry_points_are_bound():
     assert not impl._is_f32(torch.zeros(1, dtype=torch.float16))
 
 
+def test_fp32_policy_switch(monkeypatch):
+    """FLASH_HOG_B200_FP32=bf16 sends fp32 inputs to the bf16 kernels (the reference's
+    native-plugin behaviour); anything but fp32/bf16 is refused."""
+    from flash_hog_b200 import _attention_impl as impl
+
+    x = torch.zeros(1, dtype=torch.float32)
+    monkeypatch.setenv(impl.FP32_POLICY_ENV, "bf16")
+    assert impl.fp32_policy() == "bf16" and not impl._is_f32(x)
+    monkeypatch.setenv(impl.FP32_POLICY_ENV, "fp32")
+    assert impl._is_f32(x)
+    monkeypatch.setenv(impl.FP32_POLICY_ENV, "tf32")
+    with pytest.raises(ValueError):
+        impl.fp32_policy()
+
+
 @pytest.mark.gpu
 @pytest.mark.parametrize("b,h,hk,tq,tk,causal,window,d", F32_CASES)
 def test_f32_kernels_match_oracle(b, h, hk, tq, tk, causal, window, d):
@@ -243,3 +258,27 @@ def test_f32_band_mask_edge_cases(b, h, hk, tq, tk, causal, window, d):
             assert np.abs(g).max() < 1e-4, name
         else:
             assert_close(name, g, want, F32_REL_TOL)
+
+
+@pytest.mark.gpu
+def test_fp32_inputs_under_the_bf16_policy(monkeypatch):
+    """Under FLASH_HOG_B200_FP32=bf16 fp32 inputs run the bf16 kernels: fp32 outputs,
+    within the bf16 bar, and visibly less exact than the default fp32 policy."""
+    from flash_hog_b200 import _attention_impl as impl
+    from flash_hog_b200.attention import dot_product_attention
+
+    x = ora.make_inputs(1, 2, 256, 256, 64, seed=12, dtype=torch.float32)
+    ref = ora.autograd_all(*(x[n].double() for n in ("q", "k", "v", "do", "ddq", "ddk", "ddv")), causal=True)
+    c = {n: t.cuda() for n, t in x.items()}
+    errs = {}
+    for policy in ("bf16", "fp32"):
+        monkeypatch.setenv(impl.FP32_POLICY_ENV, policy)
+        q, k, v, do = (c[n].clone().requires_grad_(True) for n in ("q", "k", "v", "do"))
+        o = dot_product_attention(q, k, v, is_causal=True)
+        dq, dk, dv = torch.autograd.grad(o, (q, k, v), do, create_graph=True)
+        dq2, dk2, dv2, ddo = torch.autograd.grad((dq, dk, dv), (q, k, v, do), (c["ddq"], c["ddk"], c["ddv"]))
+        assert all(t.dtype == torch.float32 for t in (o, dq, dq2, ddo))
+        errs[policy] = max(assert_close(n, np64(t), ref[n].numpy()) for n, t in
+                           (("o", o), ("dq", dq), ("dk", dk), ("dv", dv), ("dq2", dq2), ("dk2", dk2), ("dv2", dv2),
+                            ("ddo", ddo)))
+    assert errs["fp32"] <= F32_REL_TOL < errs["bf16"]
