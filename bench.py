@@ -158,51 +158,94 @@ class ClockSampler:
 # reference arm and CPU baseline (the oracle port on host cores)
 # ----------------------------------------------------------------------------------
 
-def cpu_baseline_sample(steps=1, heads=1, threads=None):
-    """Times the oracle double backward on `heads` heads of the workload (fp32, CPU).
+CPU_CHUNK_HEADS = 4  # heads per oracle call on the host (B1 H4 S2048 D64: ~0.6 GB of autograd graph)
 
-    Each step: torch double autograd of naive attention (forward, backward and
-    backward-of-backward of B1 H`heads` S2048 D64 causal). Credited FLOPs are those
-    of the sampled heads' double backward only, so the rate is comparable with
-    the GPU's.
-    """
-    from oracle import attention_oracle as ora
 
-    threads = threads or os.cpu_count()
-    torch.set_num_threads(threads)
-    x = ora.make_inputs(1, heads, S, S, D, seed=0, dtype=torch.float32)
-    args = [x[n] for n in ("q", "k", "v", "do", "ddq", "ddk", "ddv")]
+class CpuWorkload:
+    """The headline workload on the host: the oracle port (torch double autograd of
+    naive attention, fp32, all host threads) over the whole B x H batch, a chunk of
+    ``CPU_CHUNK_HEADS`` heads per call. Both the reference arm and our arm's
+    ``cpu_baseline`` time this same procedure, so their rates agree."""
+
+    def __init__(self, threads=None):
+        from oracle import attention_oracle as ora
+
+        self.ora = ora
+        self.threads = threads or os.cpu_count()
+        torch.set_num_threads(self.threads)
+        x = ora.make_inputs(B, H, SQ, SK, D, seed=0, dtype=torch.float32)
+        names = ("q", "k", "v", "do", "ddq", "ddk", "ddv")
+        self.chunks = []
+        for b in range(B):
+            for h0 in range(0, H, CPU_CHUNK_HEADS):
+                self.chunks.append([x[n][b:b + 1, :, h0:h0 + CPU_CHUNK_HEADS].contiguous() for n in names])
+
+    def run_chunk(self, i):
+        self.ora.autograd_all(*self.chunks[i % len(self.chunks)], scale=SCALE, causal=CAUSAL)
+
+    def chunk_flops(self):
+        return credited_flops(1, CPU_CHUNK_HEADS)
+
+    def host(self):
+        try:
+            import cpuinfo
+
+            name = cpuinfo.get_cpu_info().get("brand_raw", "")
+        except Exception:  # noqa: BLE001 - the model name is informational
+            name = ""
+        return {"threads": self.threads, "logical_cpus": os.cpu_count(), "model": name}
+
+
+def cpu_baseline_sample(warmup=1, steps=5):
+    """Our arm's CPU baseline: ``steps`` chunks of the workload (after ``warmup``
+    chunks), median chunk time, as a rate over the chunk's credited FLOPs."""
+    w = CpuWorkload()
+    for i in range(warmup):
+        w.run_chunk(i)
     times = []
-    for _ in range(steps):
+    for i in range(steps):
         t0 = time.perf_counter()
-        ora.autograd_all(*args, scale=SCALE, causal=CAUSAL)
+        w.run_chunk(warmup + i)
         times.append(time.perf_counter() - t0)
     t = statistics.median(times)
-    value = credited_flops(1, heads) / t / 1e12
-    return {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "port",
-            "sample": f"{heads} of {B * H} heads of the workload per step (B1 H{heads} S{S} D{D} causal fp32, "
-                      f"torch double autograd of naive attention), median of {steps}"}, t
+    return {"value": w.chunk_flops() / t / 1e12, "unit": "TFLOP/s", "cores": w.threads, "kind": "port",
+            "host": w.host(),
+            "sample": f"{steps} chunks of {CPU_CHUNK_HEADS} heads (B1 H{CPU_CHUNK_HEADS} S{S} D{D} causal fp32, torch "
+                      f"double autograd of naive attention; {B * H // CPU_CHUNK_HEADS} chunks make the full "
+                      f"workload) after {warmup} warm-up chunk(s), median chunk time"}
 
 
 def run_reference(args):
+    """The reference algorithm's CPU path on the full workload: every step runs all
+    B x H heads (chunk by chunk); rank 0 only."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
-    for _ in range(args.warmup):
-        cpu_baseline_sample(steps=1)
-    t0 = time.perf_counter()
-    base, _ = cpu_baseline_sample(steps=args.steps)
-    wall = time.perf_counter() - t0
-    n = args.gpus
+    w = CpuWorkload()
+    n_chunks = len(w.chunks)
+    for i in range(args.warmup):
+        w.run_chunk(i)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        for c in range(n_chunks):
+            w.run_chunk(c)
+        times.append(time.perf_counter() - t0)
+    t = statistics.median(times)
+    value = credited_flops(B, H) / t / 1e12
     line = {
-        "impl": "reference", "metric": METRIC, "value": base["value"], "unit": "TFLOP/s", "n_gpus": n,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * wall / args.steps,
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * t,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"bwdbwd causal B{B} H{H} S{S} D{D} per GPU (sampled: 1 head per step)",
-                   "reference_path": "oracle port: torch CPU double autograd (reference XLA CPU path needs JAX, "
-                                     "absent)"},
-        "cpu_baseline": base,
-        "e2e": {"value": base["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "config": {"workload": f"bwdbwd {describe()} per GPU: the full B{B} H{H} batch every step, "
+                               f"{n_chunks} chunks of {CPU_CHUNK_HEADS} heads",
+                   "name": args.workload,
+                   "reference_path": "oracle port: torch CPU double autograd (the reference's XLA CPU path needs "
+                                     "JAX, absent)",
+                   "warmup_unit": "chunks", "step_time": "median over steps"},
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": w.threads, "kind": "port", "host": w.host(),
+                         "sample": f"the full workload per step ({n_chunks} chunks of {CPU_CHUNK_HEADS} heads)"},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
     return 0
@@ -515,11 +558,41 @@ def main():
     if args.impl == "reference":
         return run_reference(args)
 
+    return run_ours(args)
+
+
+def pin_host_cores(local, local_world):
+    """Restricts this rank's host threads to its share of its GPU's CPU affinity set
+    (NVML), so ranks do not contend for cores and pinned buffers are first touched on
+    the GPU's NUMA node. Returns the cores used (None if NVML is unavailable)."""
+    try:
+        import pynvml
+
+        pynvml.nvmlInit()
+        hdl = pynvml.nvmlDeviceGetHandleByIndex(torch.cuda.current_device())
+        words = pynvml.nvmlDeviceGetCpuAffinity(hdl, (os.cpu_count() + 63) // 64)
+        pynvml.nvmlShutdown()
+    except Exception:  # noqa: BLE001 - affinity is an optimisation, not a requirement
+        return None
+    cpus = [64 * w + b for w, word in enumerate(words) for b in range(64) if (word >> b) & 1]
+    cpus = [c for c in cpus if c in os.sched_getaffinity(0)]
+    if len(cpus) < local_world:
+        return None
+    share = len(cpus) // local_world
+    mine = cpus[local * share:(local + 1) * share]
+    os.sched_setaffinity(0, mine)
+    torch.set_num_threads(max(1, len(mine)))
+    return mine
+
+
+def run_ours(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    local_world = int(os.environ.get("LOCAL_WORLD_SIZE", str(world)))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    cores = pin_host_cores(local, local_world) if world > 1 else None
     dist = None
     if world > 1:
         import datetime
@@ -553,35 +626,78 @@ def main():
         if dist is not None:
             dist.barrier(device_ids=[local])
 
+    def gather(vals):
+        """Every rank's floats (rank order) on every rank."""
+        t = torch.tensor(vals, dtype=torch.float64, device=dev)
+        if dist is None:
+            return [t.tolist()]
+        out = [torch.empty_like(t) for _ in range(world)]
+        dist.all_gather(out, t)
+        return [o.tolist() for o in out]
+
     for i in range(args.warmup):
         launch(i % N_SETS)
     torch.cuda.synchronize()
     if _capi.device_status() != 0:
         raise RuntimeError("device-side error during warm-up")
 
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
-    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(list(range(world)) if rank == 0 else []) as clocks:
-        barrier()
-        torch.cuda.synchronize()
-        launches0 = _capi.launch_count()
-        start.record()
-        for i in range(args.steps):
-            launch(i % N_SETS, evs[i])
-        stop.record()
-        launches = _capi.launch_count() - launches0
-        torch.cuda.synchronize()
-        barrier()
-    if _capi.device_status() != 0:
-        raise RuntimeError("device-side error during the timed region")
-    peak_bytes = torch.cuda.max_memory_allocated(dev)
-    ms = start.elapsed_time(stop) / args.steps
+    # Per-pass times, eagerly launched with events between the passes (not the timed region).
+    n_eager = max(args.steps, 20)
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(n_eager)]
+    for i in range(n_eager):
+        launch(i % N_SETS, evs[i])
+    torch.cuda.synchronize()
     t_q = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
     t_k = statistics.mean(e[1].elapsed_time(e[2]) for e in evs)
-    if dist is not None:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    eager_ms = evs[0][0].elapsed_time(evs[-1][2]) / n_eager
+
+    # The timed region: the K steps captured once as a CUDA graph and replayed, so the
+    # host's launch timing (Python, ctypes, several ranks sharing host cores) cannot
+    # leave a GPU idle between steps. The graph holds exactly the 2K kernel launches.
+    graph, launches = None, 0
+    try:
+        cap = torch.cuda.Stream(dev)
+        cap.wait_stream(torch.cuda.current_stream(dev))
+        graph = torch.cuda.CUDAGraph()
+        n0 = _capi.launch_count()
+        with torch.cuda.graph(graph, stream=cap, capture_error_mode="relaxed"):
+            for i in range(args.steps):
+                launch(i % N_SETS)
+        launches = _capi.launch_count() - n0
+        graph.replay()  # one untimed replay: the graph's first launch uploads it
+        torch.cuda.synchronize()
+    except Exception as e:  # noqa: BLE001 - fall back to eager launches, recorded in the line
+        graph = None
+        print(f"bench: CUDA graph capture failed ({e}); timing eager launches", file=sys.stderr)
+
+    def timed_region():
+        nonlocal launches
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        torch.cuda.synchronize()
+        start.record()
+        if graph is not None:
+            graph.replay()
+        else:
+            n0 = _capi.launch_count()
+            for i in range(args.steps):
+                launch(i % N_SETS)
+            launches = _capi.launch_count() - n0
+        stop.record()
+        torch.cuda.synchronize()
+        barrier()
+        return start.elapsed_time(stop) / args.steps
+
+    with ClockSampler(list(range(world)) if rank == 0 else []) as clocks:
+        ms_rank = timed_region()
+    if _capi.device_status() != 0:
+        raise RuntimeError("device-side error during the timed region")
+    # Stability check outside the timed region: the same region again until >= 200 steps.
+    reps = max(1, -(-200 // args.steps))
+    long_ms = statistics.mean(timed_region() for _ in range(reps))
+    peak_bytes = torch.cuda.max_memory_allocated(dev)
+    per_rank = gather([ms_rank, long_ms, eager_ms, t_q, t_k])
+    ms = max(r[0] for r in per_rank)
 
     # end to end through the public API, host buffers, copies inside the timed region.
     # Steps are pipelined the way a serving loop would run them: step i's inputs go
@@ -642,23 +758,39 @@ def main():
         torch.cuda.synchronize()
         barrier()
         e2e_ms = e0.elapsed_time(e1) / n_e2e
-        # Diagnostics: whether every rank's host buffers are page-locked (staged copies
-        # of pageable memory are ~6x slower), and the fastest rank's step time.
+
+        # The host links alone, all ranks at once: one step's inputs up, then its results
+        # down (outside the timed region; attributes the e2e bound to a link).
+        def link_gbs(copy_fn, nbytes, reps=5):
+            a, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            barrier()
+            torch.cuda.synchronize()
+            a.record()
+            for _ in range(reps):
+                copy_fn()
+            b_.record()
+            torch.cuda.synchronize()
+            return reps * nbytes / (a.elapsed_time(b_) * 1e-3) / 1e9
+
+        h2d_gbs = link_gbs(lambda: [dev_in[0][n].copy_(host[n], non_blocking=True) for n in names], h2d)
+        d2h_gbs = link_gbs(lambda: [dst.copy_(src, non_blocking=True) for dst, src in zip(res_host[0], outs[0])],
+                           d2h)
         pinned = all(t.is_pinned() for t in list(host.values()) + [x for r in res_host for x in r])
-        e2e_min_ms = e2e_ms
-        if dist is not None:
-            t = torch.tensor([e2e_ms, -e2e_ms], device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)  # slowest and (negated) fastest rank
-            u = torch.tensor([1.0 if pinned else 0.0], device=dev)
-            dist.all_reduce(u, op=dist.ReduceOp.MIN)  # all pinned
-            e2e_ms, e2e_min_ms, pinned = float(t[0].item()), -float(t[1].item()), bool(u.item() > 0.5)
+        e2e_rank = gather([e2e_ms, h2d_gbs, d2h_gbs, 1.0 if pinned else 0.0])
+        e2e_ms = max(r[0] for r in e2e_rank)
         e2e = {"value": world * credited_flops(B, H) / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+               "value_per_gpu": credited_flops(B, H) / (e2e_ms * 1e-3) / 1e12,
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
-               "ms_per_step_fastest_rank": e2e_min_ms, "host_buffers_pinned": pinned,
+               "host_buffers_pinned": all(r[3] > 0.5 for r in e2e_rank),
+               "per_rank": [{"rank": i, "ms_per_step": r[0], "h2d_gbs_alone": r[1], "d2h_gbs_alone": r[2]}
+                            for i, r in enumerate(e2e_rank)],
+               "host_links_gbs_aggregate": {"h2d": sum(r[1] for r in e2e_rank),
+                                            "d2h": sum(r[2] for r in e2e_rank)},
                "api": "flash_hog_b200.flash_bwdbwd",
                "pipeline": "copy-in, compute and copy-out streams; device inputs double-buffered"}
 
     mem_rows = memory_vs_seq(dev) if args.workload == "cfg3" and rank == 0 else None
+    del graph
     if dist is not None:
         dist.destroy_process_group()
     if rank != 0:
@@ -675,25 +807,36 @@ def main():
                 "traffic": QPASS_DRAM_BYTES if args.workload == "cfg2" else None,
                 "traffic_unit": "bytes per launch (ncu)",
                 "per_launch_ms": {"query_pass": t_q, "key_pass": t_k},
-                "key_pass": {"achieved": credited_flops(B, H, gemms=8) / (t_k * 1e-3) / 1e12}}
+                "key_pass": {"achieved": credited_flops(B, H, gemms=8) / (t_k * 1e-3) / 1e12,
+                             "frac": credited_flops(B, H, gemms=8) / (t_k * 1e-3) / 1e12 / peaks["bf16_tflops"]},
+                "step": {"achieved": credited_flops(B, H) / (ms * 1e-3) / 1e12,
+                         "frac_of_sustained": credited_flops(B, H) / (ms * 1e-3) / 1e12
+                         / peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])}}
     cpu = None
     if not args.skip_cpu and world == 1:  # the CPU baseline is reported at N=1 only
-        cpu, _ = cpu_baseline_sample(steps=1, heads=4)
+        cpu = cpu_baseline_sample()
     value = world * credited_flops(B, H) / (ms * 1e-3) / 1e12
     line = {
         "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "value_per_gpu": value / world,
         "config": {"workload": f"bwdbwd {describe()} per GPU", "name": args.workload,
+                   "value": "aggregate over all n_gpus ranks (value_per_gpu = value / n_gpus)",
                    "global_batch": B * world, "heads": H, "seq_len": SQ, "seq_len_k": SK, "head_dim": D,
                    "causal": CAUSAL,
                    "parallelism": f"dp{world} (batch x heads sharded, no collective)",
                    "l2": f"{N_SETS} rotating input sets of ~136 MB each (> 126 MB L2)",
+                   "timed_region": ("the K steps as one CUDA graph (2K kernel launches), replayed once"
+                                    if graph is not None else "K steps launched eagerly"),
                    "credited_gflop_per_step_per_gpu": credited_flops(B, H) / 1e9,
                    "peak_device_bytes": peak_bytes},
+        "per_rank": [{"rank": i, "ms_per_step": r[0], "ms_per_step_200": r[1], "ms_per_step_eager": r[2],
+                      "query_pass_ms": r[3], "key_pass_ms": r[4]} for i, r in enumerate(per_rank)],
+        "host_cores_per_rank": len(cores) if cores else None,
         "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks.summary(),
         **({"memory_vs_seq": mem_rows} if mem_rows else {}),
-        "gpu_launches": launches,  # counted by the library (fh_launch_count) over the timed region
+        "gpu_launches": launches,  # counted by the library (fh_launch_count) for the timed region's launches
     }
     print(json.dumps(line), flush=True)
     return 0

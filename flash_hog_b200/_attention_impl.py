@@ -76,10 +76,13 @@ def fp32_policy() -> str:
     return policy
 
 
-def _is_f32(x: torch.Tensor) -> bool:
+def _is_f32(x: torch.Tensor, policy: str | None = None) -> bool:
     """Whether ``x``'s call runs the fp32 kernels (``fh_attn_*_f32``): fp32 inputs under
-    the default policy. Every other case runs the bf16 tensor-core kernels."""
-    return x.dtype == torch.float32 and fp32_policy() == "fp32"
+    the "fp32" policy. Every other case runs the bf16 tensor-core kernels. ``policy``
+    is the one the forward decided (kept with its residuals so that the backward,
+    the double backward and the forward-mode rules of one graph all follow it);
+    None reads ``fp32_policy()`` now."""
+    return x.dtype == torch.float32 and (fp32_policy() if policy is None else policy) == "fp32"
 
 
 def _operand(x: torch.Tensor, f32: bool) -> torch.Tensor:
@@ -118,10 +121,11 @@ def _check_inputs(query, key, value):
         raise ValueError(f"q_heads ({query.shape[2]}) must be a multiple of kv_heads ({key.shape[2]})")
 
 
-def cuda_dot_product_attention(query, key, value, mask_type: MaskType, scale: float, return_residual=False):
+def cuda_dot_product_attention(query, key, value, mask_type: MaskType, scale: float, return_residual=False,
+                               policy: str | None = None):
     """Forward. Returns ``out`` or ``(out, activation)`` (activation = L, (B, N, T) fp32)."""
     _check_inputs(query, key, value)
-    f32 = _is_f32(query)
+    f32 = _is_f32(query, policy)
     q, k, v = (_operand(x, f32) for x in (query, key, value))
     b, t, n, _ = q.shape
     out = torch.empty_like(q)
@@ -143,10 +147,10 @@ def dot_product_attention_fwd_rule(query, key, value, mask_type: MaskType, scale
     return out, (query, key, value, activation, out)
 
 
-def dot_product_attention_bwd_rule(mask_type: MaskType, scale: float, res, g):
+def dot_product_attention_bwd_rule(mask_type: MaskType, scale: float, res, g, policy: str | None = None):
     """First-order backward: (dQ, dK, dV) (``_attention_impl.py:242-261``)."""
     query, key, value, activation, out = res
-    f32 = _is_f32(query)
+    f32 = _is_f32(query, policy)
     q, k, v, o, do = (_operand(x, f32) for x in (query, key, value, out, g))
     b, t, n, _ = q.shape
     dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
@@ -156,10 +160,10 @@ def dot_product_attention_bwd_rule(mask_type: MaskType, scale: float, res, g):
     return dq.to(query.dtype), dk.to(key.dtype), dv.to(value.dtype)
 
 
-def dot_product_attention_bwd_rule_fwd_rule(mask_type: MaskType, scale: float, res, g):
+def dot_product_attention_bwd_rule_fwd_rule(mask_type: MaskType, scale: float, res, g, policy: str | None = None):
     """Backward saving ``(query, key, value, out, activation, dO)`` (``_attention_impl.py:264-275``)."""
     query, key, value, activation, out = res
-    grads = dot_product_attention_bwd_rule(mask_type=mask_type, scale=scale, res=res, g=g)
+    grads = dot_product_attention_bwd_rule(mask_type=mask_type, scale=scale, res=res, g=g, policy=policy)
     return grads, (query, key, value, out, activation, g)
 
 
@@ -178,7 +182,7 @@ def _require_plain(*ts) -> None:
             "the torch.func.jvp transform; torch.func.grad / vjp are supported")
 
 
-def dot_product_attention_fwd_jvp(mask_type: MaskType, scale: float, res, tangents):
+def dot_product_attention_fwd_jvp(mask_type: MaskType, scale: float, res, tangents, policy: str | None = None):
     """Forward-mode derivative of the forward: ``(t_out, t_activation)``.
 
     No counterpart in the reference, which has reverse-mode rules only
@@ -191,7 +195,7 @@ def dot_product_attention_fwd_jvp(mask_type: MaskType, scale: float, res, tangen
     query, key, value, activation, out = res
     _require_plain(query, key, value, activation, out, *tangents)
     tq, tk, tv = _zeros_if_none(tangents, (query, key, value))
-    f32 = _is_f32(query)
+    f32 = _is_f32(query, policy)
     q, k, v, o, tq, tk, tv = (_operand(x, f32) for x in (query, key, value, out, tq, tk, tv))
     b, t, n, _ = q.shape
     stats = torch.empty((3, b, n, t), dtype=torch.float32, device=q.device)
@@ -204,7 +208,7 @@ def dot_product_attention_fwd_jvp(mask_type: MaskType, scale: float, res, tangen
     return t_out.to(out.dtype), stats[1].clone()
 
 
-def dot_product_attention_bwd_jvp(mask_type: MaskType, scale: float, res, g, tangents):
+def dot_product_attention_bwd_jvp(mask_type: MaskType, scale: float, res, g, tangents, policy: str | None = None):
     """Forward-mode derivative of the first-order backward: ``(tdQ, tdK, tdV)``.
 
     ``res`` = (query, key, value, activation, out), ``g`` = dO, ``tangents`` =
@@ -220,7 +224,7 @@ def dot_product_attention_bwd_jvp(mask_type: MaskType, scale: float, res, g, tan
     _require_plain(query, key, value, activation, out, g, *tangents)
     tq, tk, tv = _zeros_if_none(tangents[:3], (query, key, value))
     tdo = tangents[3]
-    f32 = _is_f32(query)
+    f32 = _is_f32(query, policy)
     q, k, v, o, do, tq, tk, tv = (_operand(x, f32) for x in (query, key, value, out, g, tq, tk, tv))
     tdo = None if tdo is None else _operand(tdo, f32)
     b, t, n, _ = q.shape
@@ -233,7 +237,7 @@ def dot_product_attention_bwd_jvp(mask_type: MaskType, scale: float, res, g, tan
     return tdq.to(query.dtype), tdk.to(key.dtype), tdv.to(value.dtype)
 
 
-def dot_product_attention_bwd_rule_bwd_rule(mask_type: MaskType, scale: float, res, g):
+def dot_product_attention_bwd_rule_bwd_rule(mask_type: MaskType, scale: float, res, g, policy: str | None = None):
     """Backward through the backward (``_attention_impl.py:278-303``).
 
     Returns ``((dQ2, dK2, dV2, None, None), ddO)``: cotangents of the forward
@@ -246,5 +250,5 @@ def dot_product_attention_bwd_rule_bwd_rule(mask_type: MaskType, scale: float, r
     query, key, value, out, activation, dO = res
     ddQ, ddK, ddV = g
     dQ2, dK2, dV2, ddO = flash_bwdbwd(Q=query, K=key, V=value, O=out, dO=dO, ddQ=ddQ, ddK=ddK, ddV=ddV,
-                                      L=activation, mask_type=mask_type, scale=scale)
+                                      L=activation, mask_type=mask_type, scale=scale, _policy=policy)
     return (dQ2, dK2, dV2, None, None), ddO

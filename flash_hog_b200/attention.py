@@ -67,7 +67,9 @@ def dot_product_attention(query, key, value, is_causal: bool = False, scale: flo
     unbatched = query.ndim == 3
     if unbatched:
         query, key, value = query.unsqueeze(0), key.unsqueeze(0), value.unsqueeze(0)
-    result, _ = _DotProductAttention.apply(query, key, value, mask_type, float(scale))
+    # The fp32 policy is decided once here and kept with the residuals: the backward,
+    # double backward and forward-mode rules of this graph all follow it.
+    result, _ = _DotProductAttention.apply(query, key, value, mask_type, float(scale), attn_impl.fp32_policy())
     if unbatched:
         result = result.squeeze(0)
     return result
@@ -77,37 +79,39 @@ class _DotProductAttention(torch.autograd.Function):
     """Forward (outputs O and the log-sum-exp L, the latter non-differentiable)."""
 
     @staticmethod
-    def forward(query, key, value, mask_type, scale):
+    def forward(query, key, value, mask_type, scale, policy):
         return attn_impl.cuda_dot_product_attention(query, key, value, mask_type=mask_type, scale=scale,
-                                                    return_residual=True)
+                                                    return_residual=True, policy=policy)
 
     @staticmethod
     def setup_context(ctx, inputs, output):
-        query, key, value, mask_type, scale = inputs
+        query, key, value, mask_type, scale, policy = inputs
         out, activation = output
         ctx.mark_non_differentiable(activation)
         ctx.save_for_backward(query, key, value, activation, out)
         ctx.save_for_forward(query, key, value, activation, out)
-        ctx.mask_type, ctx.scale = mask_type, scale
+        ctx.mask_type, ctx.scale, ctx.policy = mask_type, scale, policy
 
     @staticmethod
     def backward(ctx, g, _g_activation):
         query, key, value, activation, out = ctx.saved_tensors
-        dq, dk, dv = _DotProductAttentionBwd.apply(query, key, value, activation, out, g, ctx.mask_type, ctx.scale)
-        return dq, dk, dv, None, None
+        dq, dk, dv = _DotProductAttentionBwd.apply(query, key, value, activation, out, g, ctx.mask_type, ctx.scale,
+                                                   ctx.policy)
+        return dq, dk, dv, None, None, None
 
     @staticmethod
-    def jvp(ctx, tq, tk, tv, _t_mask, _t_scale):
+    def jvp(ctx, tq, tk, tv, _t_mask, _t_scale, _t_policy):
         res = ctx.saved_tensors
-        t_out, _ = attn_impl.dot_product_attention_fwd_jvp(ctx.mask_type, ctx.scale, res, (tq, tk, tv))
+        t_out, _ = attn_impl.dot_product_attention_fwd_jvp(ctx.mask_type, ctx.scale, res, (tq, tk, tv),
+                                                           policy=ctx.policy)
         return t_out, None
 
     @staticmethod
-    def vmap(info, in_dims, query, key, value, mask_type, scale):
+    def vmap(info, in_dims, query, key, value, mask_type, scale, policy):
         # Fold the vmapped axis into batch (the rule of flash_hog/jax/_pallas_gpu.py:85-102).
         size = info.batch_size
         q, k, v = (attn_impl._fold(x, d, size) for x, d in zip((query, key, value), in_dims[:3]))
-        out, activation = _DotProductAttention.apply(q, k, v, mask_type, scale)
+        out, activation = _DotProductAttention.apply(q, k, v, mask_type, scale, policy)
         return (attn_impl._unfold(out, size), attn_impl._unfold(activation, size)), (0, 0)
 
 
@@ -116,36 +120,36 @@ class _DotProductAttentionBwd(torch.autograd.Function):
     forward mode its jvp."""
 
     @staticmethod
-    def forward(query, key, value, activation, out, g, mask_type, scale):
+    def forward(query, key, value, activation, out, g, mask_type, scale, policy):
         (dq, dk, dv), _ = attn_impl.dot_product_attention_bwd_rule_fwd_rule(
-            mask_type=mask_type, scale=scale, res=(query, key, value, activation, out), g=g)
+            mask_type=mask_type, scale=scale, res=(query, key, value, activation, out), g=g, policy=policy)
         return dq, dk, dv
 
     @staticmethod
     def setup_context(ctx, inputs, output):
-        query, key, value, activation, out, g, mask_type, scale = inputs
+        query, key, value, activation, out, g, mask_type, scale, policy = inputs
         # The residual order of the reference's bwd-of-bwd rule (_attention_impl.py:264-275).
         ctx.save_for_backward(query, key, value, out, activation, g)
         ctx.save_for_forward(query, key, value, activation, out, g)
-        ctx.mask_type, ctx.scale = mask_type, scale
+        ctx.mask_type, ctx.scale, ctx.policy = mask_type, scale, policy
 
     @staticmethod
     def backward(ctx, ddq, ddk, ddv):
         res = ctx.saved_tensors
         zeros = [torch.zeros_like(t) if c is None else c for c, t in zip((ddq, ddk, ddv), res[:3])]
         (dq2, dk2, dv2, _, _), ddo = attn_impl.dot_product_attention_bwd_rule_bwd_rule(
-            mask_type=ctx.mask_type, scale=ctx.scale, res=res, g=tuple(zeros))
-        return dq2, dk2, dv2, None, None, ddo, None, None
+            mask_type=ctx.mask_type, scale=ctx.scale, res=res, g=tuple(zeros), policy=ctx.policy)
+        return dq2, dk2, dv2, None, None, ddo, None, None, None
 
     @staticmethod
-    def jvp(ctx, tq, tk, tv, _t_activation, _t_out, tg, _t_mask, _t_scale):
+    def jvp(ctx, tq, tk, tv, _t_activation, _t_out, tg, _t_mask, _t_scale, _t_policy):
         query, key, value, activation, out, g = ctx.saved_tensors
         return attn_impl.dot_product_attention_bwd_jvp(ctx.mask_type, ctx.scale, (query, key, value, activation, out),
-                                                      g, (tq, tk, tv, tg))
+                                                      g, (tq, tk, tv, tg), policy=ctx.policy)
 
     @staticmethod
-    def vmap(info, in_dims, query, key, value, activation, out, g, mask_type, scale):
+    def vmap(info, in_dims, query, key, value, activation, out, g, mask_type, scale, policy):
         size = info.batch_size
         args = [attn_impl._fold(x, d, size) for x, d in zip((query, key, value, activation, out, g), in_dims[:6])]
-        dq, dk, dv = _DotProductAttentionBwd.apply(*args, mask_type, scale)
+        dq, dk, dv = _DotProductAttentionBwd.apply(*args, mask_type, scale, policy)
         return tuple(attn_impl._unfold(x, size) for x in (dq, dk, dv)), (0, 0, 0)

@@ -1,13 +1,9 @@
-"""Build the in-tree CUDA libraries for sm_100a with nvcc.
+"""Build the in-tree CUDA library for sm_100a with nvcc.
 
-* ``libflashhog_b200.so`` -- the attention kernels and the C ABI declared in
-  ``include/flash_hog_b200.h``;
-* ``libfh_selftest.so`` -- the tcgen05 building-block unit test used by
-  ``tests/test_gpu_primitives.py``.
-
-Both are written next to this file so they travel with the source tree. Object
-files are cached under ``_build/`` keyed by source and header modification
-times, so an unchanged tree rebuilds in well under a second.
+``libflashhog_b200.so`` -- the attention kernels and the C ABI declared in
+``include/flash_hog_b200.h`` -- is written next to this file so it travels with
+the source tree. Object files are cached under ``_build/`` keyed by source and
+header modification times, so an unchanged tree rebuilds in well under a second.
 """
 
 from __future__ import annotations
@@ -28,10 +24,8 @@ NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-O2", "--ex
               "-I" + os.path.join(ROOT, "include"), "-I" + CSRC]
 
 MAIN_SOURCES = ["capi.cu", "fwd.cu", "bwd.cu", "bwdbwd.cu", "rowdot.cu", "f32.cu"]
-SELFTEST_SOURCES = ["selftest.cu"]
 
 MAIN_LIB = os.path.join(PKG, "libflashhog_b200.so")
-SELFTEST_LIB = os.path.join(PKG, "libfh_selftest.so")
 
 
 def nvcc() -> str:
@@ -73,14 +67,13 @@ def _link(objs, out):
 
 
 def build(verbose: bool = False) -> None:
-    """Compile every CUDA source for sm_100a and link the two shared libraries."""
-    srcs = MAIN_SOURCES + SELFTEST_SOURCES
+    """Compile every CUDA source of the library for sm_100a and link it."""
+    srcs = MAIN_SOURCES
     with ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 1)) as ex:
         objs = dict(zip(srcs, ex.map(lambda s: _compile(s, verbose), srcs)))
     _link([objs[s] for s in MAIN_SOURCES], MAIN_LIB)
-    _link([objs[s] for s in SELFTEST_SOURCES], SELFTEST_LIB)
 
 
 if __name__ == "__main__":
     build(verbose="-v" in sys.argv)
-    print("built", MAIN_LIB, SELFTEST_LIB)
+    print("built", MAIN_LIB)

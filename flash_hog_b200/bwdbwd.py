@@ -21,7 +21,7 @@ import dataclasses
 import torch
 
 from flash_hog_b200 import _capi
-from flash_hog_b200._attention_impl import MaskType, _fold, _is_f32, _mask_args, _operand, _unfold
+from flash_hog_b200._attention_impl import MaskType, _fold, _is_f32, _mask_args, _operand, _unfold, fp32_policy
 
 
 @dataclasses.dataclass(frozen=True)
@@ -41,16 +41,18 @@ class TuningConfig:
 
 
 def flash_bwdbwd(Q, K, V, O, dO, ddQ, ddK, ddV, L, mask_type: MaskType = MaskType.NO_MASK, scale=None,
-                 config: TuningConfig | None = None, return_stats: bool = False):
+                 config: TuningConfig | None = None, return_stats: bool = False, _policy: str | None = None):
     """Double backward of attention; BTNH in, ``(dQ2, dK2, dV2, ddO)`` out.
 
     ``L`` is the forward log-sum-exp, (B, N, T) fp32 (natural log). Outputs
     have the input dtype. With ``return_stats`` also returns the fp32 row
-    statistics ``(D, dD, B)``, each (B, N, T).
+    statistics ``(D, dD, B)``, each (B, N, T). ``_policy`` (internal): the fp32
+    policy the forward of the same graph decided; None reads it now.
     """
     if Q.ndim == 3:
         batched = [x.unsqueeze(0) for x in (Q, K, V, O, dO, ddQ, ddK, ddV, L)]
-        res = flash_bwdbwd(*batched, mask_type=mask_type, scale=scale, config=config, return_stats=return_stats)
+        res = flash_bwdbwd(*batched, mask_type=mask_type, scale=scale, config=config, return_stats=return_stats,
+                           _policy=_policy)
         outs = tuple(x.squeeze(0) for x in res[0]) if return_stats else tuple(x.squeeze(0) for x in res)
         if return_stats:
             return outs, tuple(x.squeeze(0) for x in res[1])
@@ -60,16 +62,18 @@ def flash_bwdbwd(Q, K, V, O, dO, ddQ, ddK, ddV, L, mask_type: MaskType = MaskTyp
     if Q.shape[2] % K.shape[2] != 0:
         raise ValueError(f"q_heads ({Q.shape[2]}) must be a multiple of kv_heads ({K.shape[2]})")
     causal, window = _mask_args(mask_type)
-    dq2, dk2, dv2, ddo, stats = _FlashBwdBwd.apply(Q, K, V, O, dO, ddQ, ddK, ddV, L, causal, window, float(scale))
+    policy = fp32_policy() if _policy is None else _policy
+    dq2, dk2, dv2, ddo, stats = _FlashBwdBwd.apply(Q, K, V, O, dO, ddQ, ddK, ddV, L, causal, window, float(scale),
+                                                   policy)
     outs = (dq2, dk2, dv2, ddo)
     if return_stats:
         return outs, (stats[0], stats[1], stats[2])
     return outs
 
 
-def _bwdbwd_device(Q, K, V, O, dO, ddQ, ddK, ddV, L, causal: int, window: int, scale: float):
+def _bwdbwd_device(Q, K, V, O, dO, ddQ, ddK, ddV, L, causal: int, window: int, scale: float, policy: str):
     """The kernels on 4-D BTNH tensors: ``(dQ2, dK2, dV2, ddO, stats)``, stats = (D, dD, B) stacked."""
-    f32 = _is_f32(Q)
+    f32 = _is_f32(Q, policy)
     q, k, v, o, do, ddq, ddk, ddv = (_operand(x, f32) for x in (Q, K, V, O, dO, ddQ, ddK, ddV))
     b, t, n, _ = q.shape
     lse = L.reshape(b, n, t).float().contiguous()
@@ -89,8 +93,8 @@ class _FlashBwdBwd(torch.autograd.Function):
     Returns ``(dQ2, dK2, dV2, ddO, stats)``."""
 
     @staticmethod
-    def forward(Q, K, V, O, dO, ddQ, ddK, ddV, L, causal, window, scale):
-        return _bwdbwd_device(Q, K, V, O, dO, ddQ, ddK, ddV, L, causal, window, scale)
+    def forward(Q, K, V, O, dO, ddQ, ddK, ddV, L, causal, window, scale, policy):
+        return _bwdbwd_device(Q, K, V, O, dO, ddQ, ddK, ddV, L, causal, window, scale, policy)
 
     @staticmethod
     def setup_context(ctx, inputs, output):
@@ -103,14 +107,14 @@ class _FlashBwdBwd(torch.autograd.Function):
             "reference's double-backward rule is the last one it defines, flash_hog/jax/attention.py:100-130)")
 
     @staticmethod
-    def vmap(info, in_dims, Q, K, V, O, dO, ddQ, ddK, ddV, L, causal, window, scale):
+    def vmap(info, in_dims, Q, K, V, O, dO, ddQ, ddK, ddV, L, causal, window, scale, policy):
         """Batching rule of ``flash_hog/jax/_pallas_gpu.py:85-102``: the vmapped axis is
         folded into the batch axis, the kernels run once, and the results are unfolded.
         The reference requires every input to be vmapped; here an input that is not is
         broadcast along the vmapped axis first."""
         size = info.batch_size
         args = [_fold(x, d, size) for x, d in zip((Q, K, V, O, dO, ddQ, ddK, ddV, L), in_dims[:9])]
-        dq2, dk2, dv2, ddo, stats = _FlashBwdBwd.apply(*args, causal, window, scale)
+        dq2, dk2, dv2, ddo, stats = _FlashBwdBwd.apply(*args, causal, window, scale, policy)
         stats = stats.reshape(3, size, stats.shape[1] // size, *stats.shape[2:])
         return (_unfold(dq2, size), _unfold(dk2, size), _unfold(dv2, size), _unfold(ddo, size), stats), (0, 0, 0, 0, 1)
 

@@ -494,13 +494,15 @@ extern "C" int fh_attn_bwdbwd_noalloc(void* stream, const fh_attn_dims* dims, co
   if ((rc = select_stream_device(st)) != kOk) return rc;
   float* scratch = nullptr;
   if ((rc = noalloc_scratch(&scratch)) != kOk) return rc;
-  // Every element the kernels read is written earlier in the same call (D by
-  // rowdot, dD and B by the query-tiled pass), so nothing needs clearing.
+  // Two launches, as fh_attn_bwdbwd_o: the query-tiled pass computes D from o
+  // for its rows and writes D, dD and B; the key-tiled pass reads them. Every
+  // element the key pass reads is written earlier in the same call, so nothing
+  // needs clearing and a previous call's leftovers are never read.
   float* delta = scratch;
   float* dd = scratch + kNoAllocMaxRows;
   float* bv = scratch + 2 * kNoAllocMaxRows;
-  rc = launch_rowdot(s, dims->head_dim, o, dO, delta, st);
-  if (rc != kOk) return rc;
-  return launch_bwdbwd(s, dims->head_dim, BwdBwdPtrs{q, k, v, dO, ddq, ddk, ddv, lse, delta, dq2, ddo, dk2, dv2, dd, bv},
-                       kPassQuery | kPassKey, device_status, st);
+  return launch_bwdbwd(
+      s, dims->head_dim,
+      BwdBwdPtrs{q, k, v, dO, ddq, ddk, ddv, lse, nullptr, dq2, ddo, dk2, dv2, dd, bv, o, delta},
+      kPassQuery | kPassKey, device_status, st);
 }

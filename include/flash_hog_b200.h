@@ -182,17 +182,24 @@ int fh_attn_jvp_bwd(void* stream, const fh_attn_dims* dims, const void* q, const
  * the GPU for its own pool), and servers that reserve their whole memory budget
  * at start-up never allocate per request. Such a caller still passes the inputs
  * (q, k, v, o, dO, ddq, ddk, ddv, lse) and outputs (dq2, ddo, dk2, dv2) as for
- * fh_attn_bwdbwd, but no scratch: D = rowsum(dO * o), dD and B live in a 6 MiB
- * static device array inside the library (3 x 2^19 floats).
+ * fh_attn_bwdbwd_o, but no scratch: D = rowsum(dO * o), dD and B live in a
+ * 6 MiB static device array inside the library (3 x 2^19 floats). Two kernel
+ * launches, the same kernels as fh_attn_bwdbwd_o, and bit-identical results.
  *  - Limit: batch * heads * seq_q <= 524288 query rows; larger problems get
- *    FH_ERR_INVALID_ARGUMENT (see fh_last_error()) -- use fh_attn_bwdbwd.
+ *    FH_ERR_INVALID_ARGUMENT (see fh_last_error()) -- use fh_attn_bwdbwd_o.
  *  - It never calls cudaMalloc/cudaFree or any allocating routine. The first
  *    call on each device looks up the array's device address
  *    (cudaGetSymbolAddress, once per device); make that first call before any
  *    stream capture.
+ *  - Memory still appears once per device: with CUDA's lazy module loading (the
+ *    default), the first call on a device makes the driver load this library's
+ *    module there, which reserves the 6 MiB array and the kernel code at that
+ *    moment. A caller whose device memory is spoken for later (a JAX process
+ *    before it reserves its pool) should make one small call at start-up.
  *  - Every call shares the one array and leaves its contents behind. Nothing in
- *    it needs to start at zero (each call writes all it reads), but calls whose
- *    GPU work overlaps (different streams, no ordering between them) race on it.
+ *    it needs to start at zero (each call writes all it reads before reading
+ *    it), but calls whose GPU work overlaps (different streams, no ordering
+ *    between them) race on it.
  *  - The array is held by every GPU on which the library's module is loaded,
  *    until the process exits.
  *  - device_status: optional (may be NULL) caller-owned, zeroed device int in

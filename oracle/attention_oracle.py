@@ -255,6 +255,52 @@ def bwdbwd_stats(q, k, v, o, lse, do, ddq, ddk, ddv, scale=None, causal=False, r
     return out
 
 
+def bwdbwd_stats_rows(q, k, v, o, lse, do, ddq, ddk, ddv, scale=None, causal=False, window=0, chunk=1024):
+    """``bwdbwd_stats`` evaluated over chunks of ``chunk`` query rows, in float64 with
+    BLAS matmuls -- for the long sequences of the full-size checks (S = 8192), where
+    one (Nq, Nk) float64 array per product would take gigabytes per head.
+
+    Same formulas (``flash_hog/_jax_refs/jax_impl.py:273-336``). The split is exact:
+    a query row's statistics D, dD and B need only that row's scores over all keys,
+    so each chunk yields its dQ' and ddO rows and adds its share to dK' and dV'.
+    Returns (dq2, dk2, dv2, ddo), BTNH, plus (D, dD, B) each (B, N, Tq).
+    """
+    scale = default_scale(q.shape[-1]) if scale is None else scale
+    g = _group(q, k)
+    qh, oh, doh, ddqh = map(_heads, (q, o, do, ddq))
+    kh, vh, ddkh, ddvh = (_expand(_heads(x), g) for x in (k, v, ddk, ddv))
+    lse = np.asarray(lse, np.float64)
+    nq, nk = qh.shape[2], kh.shape[2]
+    dq2, ddo = np.zeros_like(qh), np.zeros_like(qh)
+    dk2, dv2 = np.zeros_like(kh), np.zeros_like(kh)
+    stats = np.zeros((3,) + qh.shape[:3])
+    kt, vt, ddkt, ddvt = (np.swapaxes(x, -1, -2) for x in (kh, vh, ddkh, ddvh))
+    keep_all = causal_mask(nq, nk, causal, window) if causal else None
+    for r0 in range(0, nq, chunk):
+        rs = slice(r0, min(r0 + chunk, nq))
+        qc, oc, doc, ddqc = qh[:, :, rs], oh[:, :, rs], doh[:, :, rs], ddqh[:, :, rs]
+        s = np.matmul(qc, kt) * scale
+        if causal:
+            s = np.where(keep_all[rs], s, -np.inf)
+        p = _probs(s, lse[:, :, rs])
+        dp = np.matmul(doc, vt)
+        dds = scale * (np.matmul(ddqc, kt) + np.matmul(qc, ddkt))
+        d = (oc * doc).sum(-1, keepdims=True)
+        dd = (dds * p).sum(-1, keepdims=True)
+        dp2 = np.matmul(doc, ddvt) - dp * dd - dds * d + dp * dds
+        bb = (dp2 * p).sum(-1, keepdims=True)
+        ddp = p * (dds - dd)
+        ds2 = scale * p * (dp2 - bb)
+        ds = scale * p * (dp - d)
+        dq2[:, :, rs] = np.matmul(ds, ddkh) + np.matmul(ds2, kh)
+        ddo[:, :, rs] = np.matmul(p, ddvh) + np.matmul(ddp, vh)
+        dk2 += np.matmul(np.swapaxes(ds, -1, -2), ddqc) + np.matmul(np.swapaxes(ds2, -1, -2), qc)
+        dv2 += np.matmul(np.swapaxes(ddp, -1, -2), doc)
+        stats[0][:, :, rs], stats[1][:, :, rs], stats[2][:, :, rs] = d[..., 0], dd[..., 0], bb[..., 0]
+    out = (_btnh(dq2), _btnh(_group_sum(dk2, g)), _btnh(_group_sum(dv2, g)), _btnh(ddo))
+    return out, (stats[0], stats[1], stats[2])
+
+
 def bwdbwd_4pass(q, k, v, o, lse, do, ddq, ddk, ddv, scale=None, causal=False,
                  tile_q=32, tile_k=32):
     """Tiled 4-pass schedule of the reference's Pallas kernels, in float64.

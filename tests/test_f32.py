@@ -282,3 +282,25 @@ def test_fp32_inputs_under_the_bf16_policy(monkeypatch):
                            (("o", o), ("dq", dq), ("dk", dk), ("dv", dv), ("dq2", dq2), ("dk2", dk2), ("dv2", dv2),
                             ("ddo", ddo)))
     assert errs["fp32"] <= F32_REL_TOL < errs["bf16"]
+
+
+@pytest.mark.gpu
+def test_fp32_policy_is_kept_from_the_forward(monkeypatch):
+    """The policy the forward decided holds for the whole graph: switching the variable
+    between the forward and the backward changes nothing (no mix of fp32-kernel and
+    bf16-kernel results in one graph)."""
+    from flash_hog_b200 import _attention_impl as impl
+    from flash_hog_b200.attention import dot_product_attention
+
+    x = ora.make_inputs(1, 2, 256, 256, 64, seed=13, dtype=torch.float32)
+    ref = ora.autograd_all(*(x[n].double() for n in ("q", "k", "v", "do", "ddq", "ddk", "ddv")), causal=True)
+    c = {n: t.cuda() for n, t in x.items()}
+    monkeypatch.setenv(impl.FP32_POLICY_ENV, "fp32")
+    q, k, v, do = (c[n].clone().requires_grad_(True) for n in ("q", "k", "v", "do"))
+    o = dot_product_attention(q, k, v, is_causal=True)
+    monkeypatch.setenv(impl.FP32_POLICY_ENV, "bf16")  # too late: the forward decided fp32
+    dq, dk, dv = torch.autograd.grad(o, (q, k, v), do, create_graph=True)
+    dq2, dk2, dv2, ddo = torch.autograd.grad((dq, dk, dv), (q, k, v, do), (c["ddq"], c["ddk"], c["ddv"]))
+    for n, t in (("o", o), ("dq", dq), ("dk", dk), ("dv", dv), ("dq2", dq2), ("dk2", dk2), ("dv2", dv2),
+                 ("ddo", ddo)):
+        assert_close(n, np64(t), ref[n].numpy(), tol=F32_REL_TOL)

@@ -11,7 +11,7 @@ import pytest
 import torch
 
 from oracle import attention_oracle as ora
-from parity_util import assert_close, case_inputs, np64, oracle_bwdbwd, select_heads
+from parity_util import assert_close, assert_elementwise, case_inputs, np64, oracle_bwdbwd, select_heads
 
 pytestmark = pytest.mark.gpu
 
@@ -137,6 +137,7 @@ HD128_CASES = [
     (1, 1, 200, 200, True),
     (1, 2, 72, 136, False),
     (2, 2, 512, 512, True),
+    (2, 2, 512, 256, False),   # non-causal cross attention with more queries than keys (configuration 4's form)
 ]
 
 
@@ -264,12 +265,50 @@ def test_headline_config_full_size_sampled_heads():
     torch.cuda.synchronize()
     for full, part in zip(out1, shard):
         assert torch.equal(full[1:3, :, 4:12], part)
-    heads = [(0, 0), (3, 15), (2, 7)]
-    xs = dict(x)
-    xs["o"], xs["lse"] = o.cpu(), lse.cpu()
-    (rq2, rk2, rv2, rdo), _ = oracle_bwdbwd(xs, True, heads=heads)
-    for name, got, ref in zip(("dQ2", "dK2", "dV2", "ddO"), out1, (rq2, rk2, rv2, rdo)):
+    heads = [(0, 0), (3, 15), (2, 7), (1, 3), (0, 11), (3, 0), (2, 14), (1, 8)]
+    arrs = {n: select_heads(x[n], heads) for n in ("q", "k", "v", "do", "ddq", "ddk", "ddv")}
+    want, _ = ora.bwdbwd_stats_rows(arrs["q"], arrs["k"], arrs["v"], select_heads(o, heads),
+                                    select_heads(lse, heads, stat=True), arrs["do"], arrs["ddq"], arrs["ddk"],
+                                    arrs["ddv"], causal=True)
+    for name, got, ref in zip(("dQ2", "dK2", "dV2", "ddO"), out1, want):
         assert_close(name, select_heads(got, heads), ref)
+        assert_elementwise(name, select_heads(got, heads), ref)
+
+
+def test_golden_inputs_through_the_bf16_kernels():
+    """The reference's own known-answer vectors (``test_data.zip``, written by
+    ``flash_hog/_jax_refs/jax_impl.py:404-477``: bf16 Q, K, V, dO, ddQ, ddK, ddV with
+    fp32 O and L, non-causal, Nq 128, Nk 256, scale 1/8) through the bf16 tensor-core
+    double backward: with D = rowsum(dO o O) from the stored fp32 O (the reference
+    computes D in fp32 too) via ``fh_attn_bwdbwd``, and with O rounded to bf16 via the
+    fused ``fh_attn_bwdbwd_o``. Both match the stored outputs to 1e-2 max-abs."""
+    import os
+
+    from flash_hog_b200 import _capi
+
+    d = np.load(os.path.join(os.path.dirname(__file__), "golden", "kat_bwdbwd.npz"))
+    bf = lambda n: torch.from_numpy(d[n + "_bf16"].view(np.int16)).view(torch.bfloat16)[None, :, None].cuda()
+    q, k, v, do, ddq, ddk, ddv = (bf(n) for n in ("q", "k", "v", "do", "ddq", "ddk", "ddv"))
+    o32 = torch.from_numpy(d["o"])[None, :, None].cuda()
+    lse = torch.from_numpy(d["L"])[None, None].cuda().contiguous()
+    scale = float(d["scale"])
+    assert not bool(d["causal"])
+    delta = (do.float() * o32).sum(-1).permute(0, 2, 1).contiguous()
+    outs = [torch.empty_like(q), torch.empty_like(q), torch.empty_like(k), torch.empty_like(k)]
+    dd, bv = torch.empty_like(delta), torch.empty_like(delta)
+    _capi.attn_bwdbwd(q, k, v, do, ddq, ddk, ddv, lse, delta, outs[0], outs[1], outs[2], outs[3], dd, bv, scale, 0)
+    fused = [torch.empty_like(t) for t in outs]
+    delta2, dd2, bv2 = (torch.empty_like(delta) for _ in range(3))
+    _capi.attn_bwdbwd_o(q, k, v, o32.to(torch.bfloat16), do, ddq, ddk, ddv, lse, fused[0], fused[1], fused[2],
+                        fused[3], delta2, dd2, bv2, scale, 0)
+    torch.cuda.synchronize()
+    assert _capi.device_status() == 0
+    for variant in (outs, fused):
+        for name, got in zip(("dq2", "ddo", "dk2", "dv2"), variant):
+            got = np64(got)[0, :, 0]
+            ref = d[name].astype(np.float64)
+            assert ora.max_abs(got, ref) <= 1e-2, f"{name}: max abs {ora.max_abs(got, ref):.3e}"
+            assert ora.rel_err(got, ref) <= 2e-2, f"{name}: rel err {ora.rel_err(got, ref):.3e}"
 
 
 def test_device_status_clean_and_fp32_inputs():

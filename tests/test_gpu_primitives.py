@@ -1,4 +1,5 @@
-"""GPU unit test of the tcgen05 / TMA / TMEM conventions (csrc/selftest.cu).
+"""GPU unit test of the tcgen05 / TMA / TMEM conventions (tests/csrc/selftest.cu,
+built by tests/csrc/build_selftest.py into tests/csrc/libfh_selftest.so).
 
 Every attention kernel builds its operands from the same panels and
 descriptors; this test isolates them on a single 128 x N x K GEMM against a
@@ -11,7 +12,7 @@ import os
 import pytest
 import torch
 
-LIB = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "flash_hog_b200", "libfh_selftest.so")
+LIB = os.path.join(os.path.dirname(os.path.abspath(__file__)), "csrc", "libfh_selftest.so")
 
 
 @pytest.mark.gpu

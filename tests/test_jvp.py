@@ -55,27 +55,27 @@ def _oracle_impl(monkeypatch):
     T = lambda a: torch.from_numpy(np.ascontiguousarray(a))
     causal = impl._is_causal
 
-    def fwd(query, key, value, mask_type, scale, return_residual=False):
+    def fwd(query, key, value, mask_type, scale, return_residual=False, policy=None):
         o, l = ora.attention_fwd(_np(query), _np(key), _np(value), scale=scale, causal=causal(mask_type))
         return (T(o), T(l)) if return_residual else T(o)
 
-    def bwd_fwd(mask_type, scale, res, g):
+    def bwd_fwd(mask_type, scale, res, g, policy=None):
         q, k, v, l, o = res
         d = ora.attention_bwd(*map(_np, (q, k, v, o, l, g)), scale=scale, causal=causal(mask_type))
         return tuple(map(T, d)), (q, k, v, o, l, g)
 
-    def bwd_bwd(mask_type, scale, res, g):
+    def bwd_bwd(mask_type, scale, res, g, policy=None):
         r = ora.bwdbwd_stats(*map(_np, res), *map(_np, g), scale=scale, causal=causal(mask_type))
         return (T(r[0]), T(r[1]), T(r[2]), None, None), T(r[3])
 
-    def fwd_jvp(mask_type, scale, res, tangents):
+    def fwd_jvp(mask_type, scale, res, tangents, policy=None):
         q, k, v, l, o = res
         impl._require_plain(*res, *tangents)
         t = impl._zeros_if_none(tangents, (q, k, v))
         to, tl = ora.jvp_fwd(*map(_np, (q, k, v, o, l)), *map(_np, t), scale=scale, causal=causal(mask_type))
         return T(to), T(tl)
 
-    def bwd_jvp(mask_type, scale, res, g, tangents):
+    def bwd_jvp(mask_type, scale, res, g, tangents, policy=None):
         q, k, v, l, o = res
         impl._require_plain(*res, g, *tangents)
         t = impl._zeros_if_none(tangents[:3], (q, k, v))

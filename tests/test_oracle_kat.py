@@ -102,3 +102,20 @@ def test_oracle_grouped_query_heads(causal):
                          ("dq2", "dk2", "dv2", "ddo")):
         assert got.shape == a[name].shape
         assert np.abs(got - a[name].numpy()).max() < 1e-12, name
+
+
+@pytest.mark.parametrize("causal,window,kv_heads,tq,tk", [(0, 0, None, 200, 136), (1, 0, 2, 160, 160),
+                                                          (2, 48, None, 96, 200), (1, 0, None, 300, 100)])
+def test_chunked_statement_matches_explicit_formulas(causal, window, kv_heads, tq, tk):
+    """The chunked matmul statement used by the full-size GPU checks equals the explicit
+    formulas, including masks that cut across chunk edges and grouped-query heads."""
+    x = ora.make_inputs(2, 4, tq, tk, 32, seed=tq * tk, dtype=torch.float64, kv_heads=kv_heads)
+    q, k, v, do, ddq, ddk, ddv = (x[n].numpy() for n in ("q", "k", "v", "do", "ddq", "ddk", "ddv"))
+    o, lse = ora.attention_fwd(q, k, v, causal=causal, window=window)
+    want, wstats = ora.bwdbwd_stats(q, k, v, o, lse, do, ddq, ddk, ddv, causal=causal, window=window,
+                                    return_stats=True)
+    got, gstats = ora.bwdbwd_stats_rows(q, k, v, o, lse, do, ddq, ddk, ddv, causal=causal, window=window, chunk=48)
+    for a, b_, n in zip(got, want, NAMES):
+        assert a.shape == b_.shape and ora.max_abs(a, b_) < 1e-11, n
+    for a, b_ in zip(gstats, wstats):
+        assert ora.max_abs(a, b_) < 1e-11

@@ -23,7 +23,7 @@ def _np(x):
     return x.detach().double().numpy()
 
 
-def _oracle_bwdbwd_device(Q, K, V, O, dO, ddQ, ddK, ddV, L, causal, window, scale):
+def _oracle_bwdbwd_device(Q, K, V, O, dO, ddQ, ddK, ddV, L, causal, window, scale, policy=None):
     b, t, n, _ = Q.shape
     outs, stats = ora.bwdbwd_stats(*(_np(x) for x in (Q, K, V, O)), L.reshape(b, n, t).double().numpy(),
                                    *(_np(x) for x in (dO, ddQ, ddK, ddV)), scale=scale, causal=causal, window=window,
@@ -31,7 +31,7 @@ def _oracle_bwdbwd_device(Q, K, V, O, dO, ddQ, ddK, ddV, L, causal, window, scal
     return tuple(torch.from_numpy(x).to(Q.dtype) for x in outs) + (torch.from_numpy(np.stack(stats)).float(),)
 
 
-def _oracle_fwd(query, key, value, mask_type, scale, return_residual=False):
+def _oracle_fwd(query, key, value, mask_type, scale, return_residual=False, policy=None):
     from flash_hog_b200._attention_impl import _mask_args
 
     causal, window = _mask_args(mask_type)
@@ -40,7 +40,7 @@ def _oracle_fwd(query, key, value, mask_type, scale, return_residual=False):
     return (out, torch.from_numpy(lse).float()) if return_residual else out
 
 
-def _oracle_bwd(mask_type, scale, res, g):
+def _oracle_bwd(mask_type, scale, res, g, policy=None):
     from flash_hog_b200._attention_impl import _mask_args
 
     query, key, value, activation, out = res
