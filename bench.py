@@ -255,12 +255,23 @@ def run_reference(args):
 # our arm
 # ----------------------------------------------------------------------------------
 
-def make_set(seed, device):
+# Workloads whose global batch is fixed and sharded over the ranks (strong scaling):
+# configuration 4 is "sharded over batch x heads across 1/2/4/8 GPUs".
+STRONG = {"cfg4"}
+
+
+def make_set(seed, device, shard=None, rank=0):
+    """One input set on the device. With ``shard`` (a BatchHeadsSharding) the set is
+    this rank's slice of the global batch drawn from ``seed``; otherwise the whole
+    B x H batch is this rank's own."""
     from flash_hog_b200 import MaskType
     from flash_hog_b200 import _attention_impl as impl
     from oracle.attention_oracle import make_inputs
 
     x = make_inputs(B, H, SQ, SK, D, seed=seed)
+    if shard is not None:
+        x = {k: (shard.shard(v, rank) if k in ("q", "do", "ddq") else shard.shard_kv(v, rank)).contiguous()
+             for k, v in x.items()}
     g = {k: v.to(device) for k, v in x.items()}
     mask = MaskType.CAUSAL if CAUSAL else MaskType.NO_MASK
     o, lse = impl.cuda_dot_product_attention(g["q"], g["k"], g["v"], mask, SCALE, return_residual=True)
@@ -585,6 +596,52 @@ def pin_host_cores(local, local_world):
     return mine
 
 
+def e2e_sharded(args, dev, rank, world, barrier, gather, sharded_flash_bwdbwd, MaskType):
+    """End to end through ``sharded_flash_bwdbwd`` for a strong-scaling workload: every
+    rank holds the same global batch in pinned host memory; each step, each rank copies
+    its slice to its GPU, runs the kernels and copies its results back to pinned host
+    buffers (one step after another on one stream)."""
+    from oracle.attention_oracle import make_inputs
+
+    from flash_hog_b200 import _attention_impl as impl
+
+    x = make_inputs(B, H, SQ, SK, D, seed=0)
+    mask = MaskType.CAUSAL if CAUSAL else MaskType.NO_MASK
+    o, lse = impl.cuda_dot_product_attention(x["q"].to(dev), x["k"].to(dev), x["v"].to(dev), mask, SCALE,
+                                             return_residual=True)  # the global forward, once
+    host = [t.cpu().pin_memory() for t in (x["q"], x["k"], x["v"], o, x["do"], x["ddq"], x["ddk"], x["ddv"], lse)]
+    del o, lse
+    local, sh = sharded_flash_bwdbwd(*host, mask_type=mask, scale=SCALE, rank=rank, world=world, device=dev)
+    res_host = [torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in local]
+    sb, hs = sh.slices(rank)
+    h2d = sum(t[sb].numel() * t.element_size() for t in host) // (1 if sh.head_parts == 1 else sh.head_parts)
+    d2h = sum(t.numel() * t.element_size() for t in res_host)
+
+    def step():
+        r, _ = sharded_flash_bwdbwd(*host, mask_type=mask, scale=SCALE, rank=rank, world=world, device=dev)
+        for dst, src in zip(res_host, r):
+            dst.copy_(src, non_blocking=True)
+
+    for _ in range(2):
+        step()
+    n = max(3, min(args.steps, 10))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(n):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    ms = max(r[0] for r in gather([e0.elapsed_time(e1) / n]))
+    flops = credited_flops(B, H)
+    return {"value": flops / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "value_per_gpu": flops / world / (ms * 1e-3) / 1e12,
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": ms,
+            "api": "flash_hog_b200.sharding.sharded_flash_bwdbwd (global batch in pinned host memory)",
+            "pipeline": "one stream: slice upload, kernels, result download per step"}
+
+
 def run_ours(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -602,10 +659,18 @@ def run_ours(args):
 
     from flash_hog_b200 import _capi
     from flash_hog_b200 import flash_bwdbwd, MaskType
+    from flash_hog_b200.sharding import BatchHeadsSharding, sharded_flash_bwdbwd
 
-    # Rank r holds batch rows [4r, 4r+4) of the global batch: distinct seeds.
-    sets = [make_set(1000 * rank + i, dev) for i in range(N_SETS)]
-    stats = torch.empty((N_SETS, 3, B, H, SQ), dtype=torch.float32, device=dev)
+    strong = args.workload in STRONG
+    shard = BatchHeadsSharding(B, H, world) if strong else None
+    # Weak scaling: rank r holds its own B x H batch (rows [B r, B r + B) of a global
+    # batch B N): distinct seeds. Strong scaling: every rank draws the same global batch
+    # and keeps its batch x heads slice.
+    sets = [make_set(i if strong else 1000 * rank + i, dev, shard, rank) for i in range(N_SETS)]
+    b_loc, h_loc = sets[0]["q"].shape[0], sets[0]["q"].shape[2]
+    flops_rank = credited_flops(b_loc, h_loc)  # this rank's credited FLOPs per step
+    flops_job = credited_flops(B, H) if strong else world * credited_flops(B, H)
+    stats = torch.empty((N_SETS, 3, b_loc, h_loc, SQ), dtype=torch.float32, device=dev)
     outs = [(torch.empty_like(s["q"]), torch.empty_like(s["q"]), torch.empty_like(s["k"]), torch.empty_like(s["k"]))
             for s in sets]
 
@@ -705,7 +770,9 @@ def run_ours(args):
     # on another (device inputs double-buffered); every step still copies all its
     # inputs host -> device and all its results device -> host inside the region.
     e2e = None
-    if not args.skip_e2e:
+    if not args.skip_e2e and strong:
+        e2e = e2e_sharded(args, dev, rank, world, barrier, gather, sharded_flash_bwdbwd, MaskType)
+    elif not args.skip_e2e:
         host = {k: v.cpu().pin_memory() for k, v in sets[0].items()}
         names = ("q", "k", "v", "o", "do", "ddq", "ddk", "ddv", "lse")
         h2d = sum(host[n].numel() * host[n].element_size() for n in names)
@@ -778,8 +845,8 @@ def run_ours(args):
         pinned = all(t.is_pinned() for t in list(host.values()) + [x for r in res_host for x in r])
         e2e_rank = gather([e2e_ms, h2d_gbs, d2h_gbs, 1.0 if pinned else 0.0])
         e2e_ms = max(r[0] for r in e2e_rank)
-        e2e = {"value": world * credited_flops(B, H) / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
-               "value_per_gpu": credited_flops(B, H) / (e2e_ms * 1e-3) / 1e12,
+        e2e = {"value": flops_job / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+               "value_per_gpu": flops_job / world / (e2e_ms * 1e-3) / 1e12,
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
                "host_buffers_pinned": all(r[3] > 0.5 for r in e2e_rank),
                "per_rank": [{"rank": i, "ms_per_step": r[0], "h2d_gbs_alone": r[1], "d2h_gbs_alone": r[2]}
@@ -797,7 +864,7 @@ def run_ours(args):
         return 0
 
     peaks, peak_kind = load_peaks()
-    flops_q = credited_flops(B, H, gemms=14)
+    flops_q = credited_flops(b_loc, h_loc, gemms=14)
     achieved = flops_q / (t_q * 1e-3) / 1e12
     roofline = {"bound": "tensor", "kernel": "bwdbwd_q_kernel (query-tiled pass, 14 of 22 GEMM-eq)",
                 "achieved": achieved, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
@@ -807,29 +874,32 @@ def run_ours(args):
                 "traffic": QPASS_DRAM_BYTES if args.workload == "cfg2" else None,
                 "traffic_unit": "bytes per launch (ncu)",
                 "per_launch_ms": {"query_pass": t_q, "key_pass": t_k},
-                "key_pass": {"achieved": credited_flops(B, H, gemms=8) / (t_k * 1e-3) / 1e12,
-                             "frac": credited_flops(B, H, gemms=8) / (t_k * 1e-3) / 1e12 / peaks["bf16_tflops"]},
-                "step": {"achieved": credited_flops(B, H) / (ms * 1e-3) / 1e12,
-                         "frac_of_sustained": credited_flops(B, H) / (ms * 1e-3) / 1e12
+                "key_pass": {"achieved": credited_flops(b_loc, h_loc, gemms=8) / (t_k * 1e-3) / 1e12,
+                             "frac": credited_flops(b_loc, h_loc, gemms=8) / (t_k * 1e-3) / 1e12
+                             / peaks["bf16_tflops"]},
+                "step": {"achieved": flops_rank / (ms * 1e-3) / 1e12,
+                         "frac_of_sustained": flops_rank / (ms * 1e-3) / 1e12
                          / peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])}}
     cpu = None
     if not args.skip_cpu and world == 1:  # the CPU baseline is reported at N=1 only
         cpu = cpu_baseline_sample()
-    value = world * credited_flops(B, H) / (ms * 1e-3) / 1e12
+    value = flops_job / (ms * 1e-3) / 1e12
     line = {
         "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "strong" if strong else "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "value_per_gpu": value / world,
-        "config": {"workload": f"bwdbwd {describe()} per GPU", "name": args.workload,
+        "config": {"workload": (f"bwdbwd {describe()} sharded over the ranks" if strong
+                                else f"bwdbwd {describe()} per GPU"), "name": args.workload,
                    "value": "aggregate over all n_gpus ranks (value_per_gpu = value / n_gpus)",
-                   "global_batch": B * world, "heads": H, "seq_len": SQ, "seq_len_k": SK, "head_dim": D,
-                   "causal": CAUSAL,
+                   "global_batch": B if strong else B * world, "heads": H, "seq_len": SQ, "seq_len_k": SK,
+                   "head_dim": D, "causal": CAUSAL, "per_rank_slice": {"batch": b_loc, "heads": h_loc},
                    "parallelism": f"dp{world} (batch x heads sharded, no collective)",
                    "l2": f"{N_SETS} rotating input sets of ~136 MB each (> 126 MB L2)",
                    "timed_region": ("the K steps as one CUDA graph (2K kernel launches), replayed once"
                                     if graph is not None else "K steps launched eagerly"),
-                   "credited_gflop_per_step_per_gpu": credited_flops(B, H) / 1e9,
+                   "credited_gflop_per_step_per_gpu": flops_rank / 1e9,
                    "peak_device_bytes": peak_bytes},
         "per_rank": [{"rank": i, "ms_per_step": r[0], "ms_per_step_200": r[1], "ms_per_step_eager": r[2],
                       "query_pass_ms": r[3], "key_pass_ms": r[4]} for i, r in enumerate(per_rank)],

@@ -74,6 +74,39 @@ def build(verbose: bool = False) -> None:
     _link([objs[s] for s in MAIN_SOURCES], MAIN_LIB)
 
 
+XLA_FFI_SOURCE = os.path.join(CSRC, "xla_ffi.cc")
+XLA_FFI_LIB = os.path.join(PKG, "libfh_xla_ffi.so")
+
+
+def xla_ffi_include_dir():
+    """jaxlib's FFI header directory, or None where JAX is not installed (this image)."""
+    try:
+        import jax.ffi
+
+        return jax.ffi.include_dir()
+    except Exception:  # noqa: BLE001 - any failure means the headers are not available
+        return None
+
+
+def build_xla_ffi():
+    """Compiles ``csrc/xla_ffi.cc`` (the XLA FFI handlers FhAttnFwd, FhAttnBwd, FhBwdBwd,
+    FhBwdBwdO) into ``libfh_xla_ffi.so``, linked against ``libflashhog_b200.so``.
+    Returns the library path, or None without building where jaxlib's FFI headers are
+    absent -- as on this image, where the handlers are therefore not built."""
+    inc = xla_ffi_include_dir()
+    if inc is None:
+        return None
+    build()
+    cmd = [nvcc(), *ARCH, *NVCC_FLAGS, "-x", "cu", "-shared", "-I" + inc, XLA_FFI_SOURCE, "-o", XLA_FFI_LIB,
+           "-L" + PKG, "-lflashhog_b200", "-Xlinker", "-rpath,$ORIGIN"]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"nvcc failed on xla_ffi.cc:\n{res.stdout}\n{res.stderr}")
+    return XLA_FFI_LIB
+
+
 if __name__ == "__main__":
     build(verbose="-v" in sys.argv)
     print("built", MAIN_LIB)
+    ffi_lib = build_xla_ffi()
+    print("built", ffi_lib) if ffi_lib else print("XLA FFI handlers not built: jaxlib's FFI headers are absent")

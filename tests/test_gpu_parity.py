@@ -325,3 +325,22 @@ def test_device_status_clean_and_fp32_inputs():
     ro, _ = ora.attention_fwd(np64(x["q"]), np64(x["k"]), np64(x["v"]), causal=True)
     assert_close("O fp32-in", np64(out), ro)
     assert device_status() == 0
+
+
+def test_sharded_entry_slices_equal_the_full_run():
+    """sharded_flash_bwdbwd for each rank of a 4-way split (emulated one rank after the
+    other on this GPU; grouped-query heads, so key heads split with their groups): every
+    rank's result is the matching slice of the unsharded call, bit for bit."""
+    from flash_hog_b200 import MaskType, flash_bwdbwd
+    from flash_hog_b200.sharding import sharded_flash_bwdbwd
+
+    x = _cuda(case_inputs(2, 8, 256, 384, d=128, seed=8, causal=False, kv_heads=4))
+    args = [x[n] for n in ("q", "k", "v", "o", "do", "ddq", "ddk", "ddv", "lse")]
+    full = flash_bwdbwd(*args, mask_type=MaskType.NO_MASK)
+    host = [a.cpu() for a in args]  # the global batch as a caller would hold it
+    for rank in range(4):
+        part, sh = sharded_flash_bwdbwd(*host, mask_type=MaskType.NO_MASK, rank=rank, world=4)
+        sb, hs = sh.slices(rank)
+        ks = sh.kv_slice(rank)
+        for i, (f, p) in enumerate(zip(full, part)):
+            assert torch.equal(f[sb, :, ks if i in (1, 2) else hs], p), (rank, i)

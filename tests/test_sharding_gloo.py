@@ -111,3 +111,59 @@ def test_sharding_rule():
     assert owned == {(b, h) for b in range(4) for h in range(16)}
     with pytest.raises(ValueError):
         BatchHeadsSharding(1, 3, 2)
+
+
+def _oracle_device(Q, K, V, O, dO, ddQ, ddK, ddV, L, causal, window, scale, policy=None):
+    """CPU stand-in for the kernels inside flash_bwdbwd (the oracle's explicit formulas)."""
+    from oracle import attention_oracle as ora
+
+    b, t, n, _ = Q.shape
+    np_ = lambda x: x.detach().double().numpy()
+    outs, stats = ora.bwdbwd_stats(*(np_(x) for x in (Q, K, V, O)), L.reshape(b, n, t).double().numpy(),
+                                   *(np_(x) for x in (dO, ddQ, ddK, ddV)), scale=scale, causal=causal, window=window,
+                                   return_stats=True)
+    return tuple(torch.from_numpy(x).to(Q.dtype) for x in outs) + (torch.from_numpy(np.stack(stats)).float(),)
+
+
+def _sharded_entry_worker(rank, world, port, outdir):
+    """sharded_flash_bwdbwd under a real process group (gloo, world 2), grouped-query
+    heads, gather=True: every rank ends with the global result of the unsharded call."""
+    _init(rank, world, port, 60)
+    from flash_hog_b200 import MaskType
+    from flash_hog_b200 import bwdbwd as bb
+    from flash_hog_b200.sharding import sharded_flash_bwdbwd
+    from oracle import attention_oracle as ora
+
+    bb._bwdbwd_device = _oracle_device  # the kernels need a GPU; the host logic is what is tested
+    x = ora.make_inputs(2, 4, 48, 64, 32, seed=5, dtype=torch.float64, kv_heads=2)
+    o, lse = ora.attention_fwd(x["q"].numpy(), x["k"].numpy(), x["v"].numpy(), causal=2)
+    args = [x["q"], x["k"], x["v"], torch.from_numpy(o), x["do"], x["ddq"], x["ddk"], x["ddv"],
+            torch.from_numpy(lse)]
+    got, sh = sharded_flash_bwdbwd(*args, mask_type=MaskType.CAUSAL_BOTTOM_RIGHT, device="cpu", gather=True)
+    want = ora.bwdbwd_stats(*(a.numpy() for a in args[:4]), lse, *(a.numpy() for a in args[4:8]), causal=2)
+    ok = sh.world == world and all(np.array_equal(g.numpy(), w_) for g, w_ in zip(got, (want[0], want[1], want[2],
+                                                                                       want[3])))
+    with open(os.path.join(outdir, f"result{rank}"), "w") as f:
+        f.write("ok" if ok else "mismatch")
+    dist.destroy_process_group()
+
+
+def test_sharded_entry_gathers_the_global_result(tmp_path):
+    ctx = mp.start_processes(_sharded_entry_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=False,
+                             start_method="spawn")
+    while not ctx.join(timeout=120):
+        pass
+    assert (tmp_path / "result0").read_text() == "ok"
+    assert (tmp_path / "result1").read_text() == "ok"
+
+
+def test_sharding_rule_keeps_query_groups_whole():
+    from flash_hog_b200.sharding import BatchHeadsSharding
+
+    s = BatchHeadsSharding(1, 8, 4, kv_heads=4)  # groups of 2 query heads
+    for r in range(4):
+        _, hs = s.slices(r)
+        ks = s.kv_slice(r)
+        assert {h // 2 for h in range(hs.start, hs.stop)} == set(range(ks.start, ks.stop))
+    with pytest.raises(ValueError):
+        BatchHeadsSharding(1, 8, 8, kv_heads=4)  # would split a group across ranks
