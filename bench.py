@@ -857,6 +857,7 @@ def run_ours(args):
                "pipeline": "copy-in, compute and copy-out streams; device inputs double-buffered"}
 
     mem_rows = memory_vs_seq(dev) if args.workload == "cfg3" and rank == 0 else None
+    graphed = graph is not None
     del graph
     if dist is not None:
         dist.destroy_process_group()
@@ -898,7 +899,7 @@ def run_ours(args):
                    "parallelism": f"dp{world} (batch x heads sharded, no collective)",
                    "l2": f"{N_SETS} rotating input sets of ~136 MB each (> 126 MB L2)",
                    "timed_region": ("the K steps as one CUDA graph (2K kernel launches), replayed once"
-                                    if graph is not None else "K steps launched eagerly"),
+                                    if graphed else "K steps launched eagerly"),
                    "credited_gflop_per_step_per_gpu": flops_rank / 1e9,
                    "peak_device_bytes": peak_bytes},
         "per_rank": [{"rank": i, "ms_per_step": r[0], "ms_per_step_200": r[1], "ms_per_step_eager": r[2],

@@ -45,8 +45,36 @@ class SlidingWindow:
     length: int
 
 
+@dataclasses.dataclass(frozen=True, eq=False)
+class PackedSequences:
+    """A packed variable-length batch: ``mask`` (a MaskType or SlidingWindow) applied
+    to each sequence on its own. Tensors are (1, total rows, heads, head_dim) (or
+    (total, heads, head_dim)); sequence b is query rows [cu_seqlens_q[b],
+    cu_seqlens_q[b+1]) and key rows [cu_seqlens_k[b], cu_seqlens_k[b+1]) (int32
+    device tensors); ``max_seqlen_q``/``max_seqlen_k`` bound the sequence lengths.
+    CAUSAL_BOTTOM_RIGHT aligns each sequence's own diagonal, as the reference's JAX
+    statements do for every (qs, ks) pair (``flash_hog/_jax_refs/jax_impl.py:104-130``).
+    Accepted wherever a MaskType is; packed batches run the bf16 kernels."""
+
+    mask: object
+    cu_seqlens_q: torch.Tensor
+    cu_seqlens_k: torch.Tensor
+    max_seqlen_q: int
+    max_seqlen_k: int
+
+    def capi(self) -> "_capi.Varlen":
+        return _capi.Varlen(self.cu_seqlens_q, self.cu_seqlens_k, self.max_seqlen_q, self.max_seqlen_k)
+
+
+def _varlen_kw(mask) -> dict:
+    """``{"varlen": ...}`` for the bf16 C ABI wrappers when ``mask`` packs sequences."""
+    return {"varlen": mask.capi()} if isinstance(mask, PackedSequences) else {}
+
+
 def _mask_args(mask) -> tuple[int, int]:
     """(causal code, window length) of a MaskType or SlidingWindow, for the C ABI."""
+    if isinstance(mask, PackedSequences):
+        return _mask_args(mask.mask)
     if isinstance(mask, SlidingWindow):
         if mask.mask_type not in (MaskType.CAUSAL, MaskType.CAUSAL_BOTTOM_RIGHT) or mask.length < 1:
             raise ValueError(f"a sliding window needs a causal mask type and a length >= 1, got {mask}")
@@ -76,12 +104,15 @@ def fp32_policy() -> str:
     return policy
 
 
-def _is_f32(x: torch.Tensor, policy: str | None = None) -> bool:
+def _is_f32(x: torch.Tensor, policy: str | None = None, mask=None) -> bool:
     """Whether ``x``'s call runs the fp32 kernels (``fh_attn_*_f32``): fp32 inputs under
     the "fp32" policy. Every other case runs the bf16 tensor-core kernels. ``policy``
     is the one the forward decided (kept with its residuals so that the backward,
     the double backward and the forward-mode rules of one graph all follow it);
-    None reads ``fp32_policy()`` now."""
+    None reads ``fp32_policy()`` now. Packed variable-length batches (``mask`` a
+    PackedSequences) always run the bf16 kernels."""
+    if isinstance(mask, PackedSequences):
+        return False
     return x.dtype == torch.float32 and (fp32_policy() if policy is None else policy) == "fp32"
 
 
@@ -125,12 +156,15 @@ def cuda_dot_product_attention(query, key, value, mask_type: MaskType, scale: fl
                                policy: str | None = None):
     """Forward. Returns ``out`` or ``(out, activation)`` (activation = L, (B, N, T) fp32)."""
     _check_inputs(query, key, value)
-    f32 = _is_f32(query, policy)
+    f32 = _is_f32(query, policy, mask_type)
     q, k, v = (_operand(x, f32) for x in (query, key, value))
     b, t, n, _ = q.shape
     out = torch.empty_like(q)
     lse = torch.empty((b, n, t), dtype=torch.float32, device=q.device)
-    (_capi.attn_fwd_f32 if f32 else _capi.attn_fwd)(q, k, v, out, lse, scale, *_mask_args(mask_type))
+    if f32:
+        _capi.attn_fwd_f32(q, k, v, out, lse, scale, *_mask_args(mask_type))
+    else:
+        _capi.attn_fwd(q, k, v, out, lse, scale, *_mask_args(mask_type), **_varlen_kw(mask_type))
     out = out.to(query.dtype)
     return (out, lse) if return_residual else out
 
@@ -150,13 +184,17 @@ def dot_product_attention_fwd_rule(query, key, value, mask_type: MaskType, scale
 def dot_product_attention_bwd_rule(mask_type: MaskType, scale: float, res, g, policy: str | None = None):
     """First-order backward: (dQ, dK, dV) (``_attention_impl.py:242-261``)."""
     query, key, value, activation, out = res
-    f32 = _is_f32(query, policy)
+    f32 = _is_f32(query, policy, mask_type)
     q, k, v, o, do = (_operand(x, f32) for x in (query, key, value, out, g))
     b, t, n, _ = q.shape
     dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
     delta = torch.empty((b, n, t), dtype=torch.float32, device=q.device)
-    (_capi.attn_bwd_f32 if f32 else _capi.attn_bwd)(q, k, v, o, do, activation.float().contiguous(), dq, dk, dv,
-                                                    delta, scale, *_mask_args(mask_type))
+    if f32:
+        _capi.attn_bwd_f32(q, k, v, o, do, activation.float().contiguous(), dq, dk, dv, delta, scale,
+                           *_mask_args(mask_type))
+    else:
+        _capi.attn_bwd(q, k, v, o, do, activation.float().contiguous(), dq, dk, dv, delta, scale,
+                       *_mask_args(mask_type), **_varlen_kw(mask_type))
     return dq.to(query.dtype), dk.to(key.dtype), dv.to(value.dtype)
 
 
@@ -195,7 +233,7 @@ def dot_product_attention_fwd_jvp(mask_type: MaskType, scale: float, res, tangen
     query, key, value, activation, out = res
     _require_plain(query, key, value, activation, out, *tangents)
     tq, tk, tv = _zeros_if_none(tangents, (query, key, value))
-    f32 = _is_f32(query, policy)
+    f32 = _is_f32(query, policy, mask_type)
     q, k, v, o, tq, tk, tv = (_operand(x, f32) for x in (query, key, value, out, tq, tk, tv))
     b, t, n, _ = q.shape
     stats = torch.empty((3, b, n, t), dtype=torch.float32, device=q.device)
@@ -204,7 +242,7 @@ def dot_product_attention_fwd_jvp(mask_type: MaskType, scale: float, res, tangen
     entry = _capi.attn_bwdbwd_f32 if f32 else _capi.attn_bwdbwd_o
     entry(q, k, v, o, zero_do, tq, tk, tv, activation.float().contiguous(), dq2, t_out, None, None,
           stats[0], stats[1], stats[2], scale, _mask_args(mask_type)[0], which=_capi.PASS_QUERY,
-          window=_mask_args(mask_type)[1])
+          window=_mask_args(mask_type)[1], **({} if f32 else _varlen_kw(mask_type)))
     return t_out.to(out.dtype), stats[1].clone()
 
 
@@ -224,7 +262,7 @@ def dot_product_attention_bwd_jvp(mask_type: MaskType, scale: float, res, g, tan
     _require_plain(query, key, value, activation, out, g, *tangents)
     tq, tk, tv = _zeros_if_none(tangents[:3], (query, key, value))
     tdo = tangents[3]
-    f32 = _is_f32(query, policy)
+    f32 = _is_f32(query, policy, mask_type)
     q, k, v, o, do, tq, tk, tv = (_operand(x, f32) for x in (query, key, value, out, g, tq, tk, tv))
     tdo = None if tdo is None else _operand(tdo, f32)
     b, t, n, _ = q.shape
@@ -233,7 +271,7 @@ def dot_product_attention_bwd_jvp(mask_type: MaskType, scale: float, res, g, tan
     tdk, tdv = torch.empty_like(k), torch.empty_like(v)
     (_capi.attn_jvp_bwd_f32 if f32 else _capi.attn_jvp_bwd)(
         q, k, v, o, do, activation.float().contiguous(), tq, tk, tv, tdo, tdq, tdk, tdv, t_out,
-        stats[0], stats[1], stats[2], scale, *_mask_args(mask_type))
+        stats[0], stats[1], stats[2], scale, *_mask_args(mask_type), **({} if f32 else _varlen_kw(mask_type)))
     return tdq.to(query.dtype), tdk.to(key.dtype), tdv.to(value.dtype)
 
 

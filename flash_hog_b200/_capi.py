@@ -50,7 +50,7 @@ EXPORTED_SYMBOLS = (
     "fh_abi_version",
     "fh_launch_count",
 )
-ABI_VERSION = 5
+ABI_VERSION = 6
 
 
 class FlashHogError(RuntimeError):
@@ -77,6 +77,10 @@ class FhAttnDims(ctypes.Structure):
         ("k", FhStrides),
         ("kv_heads", ctypes.c_int32),
         ("window", ctypes.c_int32),
+        ("cu_seqlens_q", ctypes.c_void_p),
+        ("cu_seqlens_k", ctypes.c_void_p),
+        ("max_seqlen_q", ctypes.c_int32),
+        ("max_seqlen_k", ctypes.c_int32),
     ]
 
 
@@ -152,12 +156,43 @@ def _layout_key(t: torch.Tensor):
     return tuple(t.shape), (s.batch, s.seq, s.head)
 
 
-def make_dims(q: torch.Tensor, k: torch.Tensor, window: int = 0) -> FhAttnDims:
+class Varlen:
+    """A packed variable-length batch for the C ABI: int32 device offsets
+    ``cu_seqlens_q``/``cu_seqlens_k`` (sequences + 1 entries) and the longest
+    sequence lengths. The tensors are then (1, total rows, heads, head_dim)."""
+
+    def __init__(self, cu_seqlens_q: torch.Tensor, cu_seqlens_k: torch.Tensor, max_seqlen_q: int,
+                 max_seqlen_k: int):
+        for name, c in (("cu_seqlens_q", cu_seqlens_q), ("cu_seqlens_k", cu_seqlens_k)):
+            if c.dtype != torch.int32 or c.ndim != 1 or not c.is_contiguous() or c.numel() < 2:
+                raise ValueError(f"{name} must be a contiguous 1-D int32 tensor of sequences + 1 offsets")
+        if cu_seqlens_q.numel() != cu_seqlens_k.numel():
+            raise ValueError("cu_seqlens_q and cu_seqlens_k must describe the same number of sequences")
+        self.cu_seqlens_q, self.cu_seqlens_k = cu_seqlens_q, cu_seqlens_k
+        self.max_seqlen_q, self.max_seqlen_k = int(max_seqlen_q), int(max_seqlen_k)
+
+    @property
+    def batch(self) -> int:
+        return self.cu_seqlens_q.numel() - 1
+
+
+def make_dims(q: torch.Tensor, k: torch.Tensor, window: int = 0, varlen: Varlen | None = None) -> FhAttnDims:
     """Dims for BTNH tensors: q (B, Tq, H, D), k (B, Tk, Hkv, D) with H a multiple of
-    Hkv; ``window`` is the sliding-window length of a causal mask (0 = unlimited)."""
+    Hkv; ``window`` is the sliding-window length of a causal mask (0 = unlimited).
+    With ``varlen`` the tensors are packed (1, total, H, D) sequences."""
     b, tq, h, d = q.shape
     tk, hkv = k.shape[1], k.shape[2]
-    return FhAttnDims(b, h, tq, tk, d, _strides(q), _strides(k), hkv, int(window))
+    dims = FhAttnDims(b, h, tq, tk, d, _strides(q), _strides(k), hkv, int(window))
+    if varlen is not None:
+        if b != 1:
+            raise ValueError("packed variable-length tensors have one batch entry: (1, total, heads, head_dim)")
+        if varlen.cu_seqlens_q.device != q.device or varlen.cu_seqlens_k.device != q.device:
+            raise ValueError("cu_seqlens must be on the tensors' device")
+        dims.batch = varlen.batch
+        dims.cu_seqlens_q = varlen.cu_seqlens_q.data_ptr()
+        dims.cu_seqlens_k = varlen.cu_seqlens_k.data_ptr()
+        dims.max_seqlen_q, dims.max_seqlen_k = varlen.max_seqlen_q, varlen.max_seqlen_k
+    return dims
 
 
 def _same_layout(ref: torch.Tensor, *others: torch.Tensor, dtype=torch.bfloat16) -> None:
@@ -172,35 +207,35 @@ def _same_layout(ref: torch.Tensor, *others: torch.Tensor, dtype=torch.bfloat16)
             raise ValueError(f"tensors must be {dtype} on the same CUDA device")
 
 
-def attn_fwd(q, k, v, out, lse, scale: float, causal: int, window: int = 0) -> None:
+def attn_fwd(q, k, v, out, lse, scale: float, causal: int, window: int = 0, varlen: Varlen | None = None) -> None:
     _same_layout(q, out)
     _same_layout(k, v)
-    dims = make_dims(q, k, window)
+    dims = make_dims(q, k, window, varlen)
     _check("fh_attn_fwd", lib().fh_attn_fwd(_stream(q.device), ctypes.byref(dims), _ptr(q), _ptr(k), _ptr(v),
                                            _ptr(out), _ptr(lse), float(scale), int(causal)))
 
 
-def attn_rowdot(o, dO, delta) -> None:
+def attn_rowdot(o, dO, delta, varlen: Varlen | None = None) -> None:
     _same_layout(o, dO)
-    dims = make_dims(o, o)
+    dims = make_dims(o, o, 0, varlen)
     _check("fh_attn_rowdot", lib().fh_attn_rowdot(_stream(o.device), ctypes.byref(dims), _ptr(o), _ptr(dO),
                                                  _ptr(delta)))
 
 
-def attn_bwd(q, k, v, o, dO, lse, dq, dk, dv, delta, scale: float, causal: int, window: int = 0) -> None:
+def attn_bwd(q, k, v, o, dO, lse, dq, dk, dv, delta, scale: float, causal: int, window: int = 0, varlen: Varlen | None = None) -> None:
     _same_layout(q, o, dO, dq)
     _same_layout(k, v, dk, dv)
-    dims = make_dims(q, k, window)
+    dims = make_dims(q, k, window, varlen)
     _check("fh_attn_bwd", lib().fh_attn_bwd(_stream(q.device), ctypes.byref(dims), _ptr(q), _ptr(k), _ptr(v),
                                            _ptr(o), _ptr(dO), _ptr(lse), _ptr(dq), _ptr(dk), _ptr(dv),
                                            _ptr(delta), float(scale), int(causal)))
 
 
 def attn_bwdbwd(q, k, v, dO, ddq, ddk, ddv, lse, delta, dq2, ddo, dk2, dv2, dd, bvec, scale: float,
-                causal: int, window: int = 0) -> None:
+                causal: int, window: int = 0, varlen: Varlen | None = None) -> None:
     _same_layout(q, dO, ddq, dq2, ddo)
     _same_layout(k, v, ddk, ddv, dk2, dv2)
-    dims = make_dims(q, k, window)
+    dims = make_dims(q, k, window, varlen)
     _check("fh_attn_bwdbwd", lib().fh_attn_bwdbwd(
         _stream(q.device), ctypes.byref(dims), _ptr(q), _ptr(k), _ptr(v), _ptr(dO), _ptr(ddq), _ptr(ddk),
         _ptr(ddv), _ptr(lse), _ptr(delta), _ptr(dq2), _ptr(ddo), _ptr(dk2), _ptr(dv2), _ptr(dd), _ptr(bvec),
@@ -211,11 +246,11 @@ PASS_QUERY, PASS_KEY = 1, 2
 
 
 def attn_bwdbwd_pass(q, k, v, dO, ddq, ddk, ddv, lse, delta, dq2, ddo, dk2, dv2, dd, bvec, scale: float,
-                     causal: int, which: int, window: int = 0) -> None:
+                     causal: int, which: int, window: int = 0, varlen: Varlen | None = None) -> None:
     """One pass of the double backward (PASS_QUERY, PASS_KEY or both)."""
     _same_layout(q, dO, ddq, dq2, ddo)
     _same_layout(k, v, ddk, ddv, dk2, dv2)
-    dims = make_dims(q, k, window)
+    dims = make_dims(q, k, window, varlen)
     _check("fh_attn_bwdbwd_pass", lib().fh_attn_bwdbwd_pass(
         _stream(q.device), ctypes.byref(dims), _ptr(q), _ptr(k), _ptr(v), _ptr(dO), _ptr(ddq), _ptr(ddk),
         _ptr(ddv), _ptr(lse), _ptr(delta), _ptr(dq2), _ptr(ddo), _ptr(dk2), _ptr(dv2), _ptr(dd), _ptr(bvec),
@@ -223,11 +258,11 @@ def attn_bwdbwd_pass(q, k, v, dO, ddq, ddk, ddv, lse, delta, dq2, ddo, dk2, dv2,
 
 
 def attn_bwdbwd_o(q, k, v, o, dO, ddq, ddk, ddv, lse, dq2, ddo, dk2, dv2, delta, dd, bvec, scale: float,
-                  causal: int, which: int = PASS_QUERY | PASS_KEY, window: int = 0) -> None:
+                  causal: int, which: int = PASS_QUERY | PASS_KEY, window: int = 0, varlen: Varlen | None = None) -> None:
     """Double backward from the forward output: the query pass computes delta itself."""
     _same_layout(q, o, dO, ddq, dq2, ddo)
     _same_layout(k, v, ddk, ddv, dk2, dv2)
-    dims = make_dims(q, k, window)
+    dims = make_dims(q, k, window, varlen)
     _check("fh_attn_bwdbwd_o", lib().fh_attn_bwdbwd_o(
         _stream(q.device), ctypes.byref(dims), _ptr(q), _ptr(k), _ptr(v), _ptr(o), _ptr(dO), _ptr(ddq),
         _ptr(ddk), _ptr(ddv), _ptr(lse), _ptr(dq2), _ptr(ddo), _ptr(dk2), _ptr(dv2), _ptr(delta), _ptr(dd),
@@ -235,11 +270,11 @@ def attn_bwdbwd_o(q, k, v, o, dO, ddq, ddk, ddv, lse, dq2, ddo, dk2, dv2, delta,
 
 
 def attn_jvp_bwd(q, k, v, o, dO, lse, tq, tk, tv, tdO, tdq, tdk, tdv, to, delta, dd, bvec, scale: float,
-                 causal: int, window: int = 0) -> None:
+                 causal: int, window: int = 0, varlen: Varlen | None = None) -> None:
     """Forward-mode derivative of the first-order backward (``tdO`` may be None)."""
     _same_layout(q, o, dO, tq, tdq, to, tdO)
     _same_layout(k, v, tk, tv, tdk, tdv)
-    dims = make_dims(q, k, window)
+    dims = make_dims(q, k, window, varlen)
     _check("fh_attn_jvp_bwd", lib().fh_attn_jvp_bwd(
         _stream(q.device), ctypes.byref(dims), _ptr(q), _ptr(k), _ptr(v), _ptr(o), _ptr(dO), _ptr(lse), _ptr(tq),
         _ptr(tk), _ptr(tv), _ptr(tdO), _ptr(tdq), _ptr(tdk), _ptr(tdv), _ptr(to),

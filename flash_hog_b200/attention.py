@@ -34,7 +34,7 @@ from __future__ import annotations
 import torch
 
 from flash_hog_b200 import _attention_impl as attn_impl
-from flash_hog_b200._attention_impl import MaskType, SlidingWindow
+from flash_hog_b200._attention_impl import MaskType, PackedSequences, SlidingWindow
 
 
 def dot_product_attention(query, key, value, is_causal: bool = False, scale: float | None = None, *,
@@ -75,6 +75,46 @@ def dot_product_attention(query, key, value, is_causal: bool = False, scale: flo
     return result
 
 
+def dot_product_attention_varlen(query, key, value, cu_seqlens_q, cu_seqlens_k, max_seqlen_q: int,
+                                 max_seqlen_k: int, is_causal: bool = False, scale: float | None = None, *,
+                                 causal_alignment: str = "top_left", sliding_window_length: int | None = None):
+    """``dot_product_attention`` over a packed batch of variable-length sequences,
+    differentiable twice like it (fwd -> bwd -> bwdbwd on the kernels).
+
+    query (total_q, N, H); key, value (total_k, Nkv, H); sequence b is query rows
+    [cu_seqlens_q[b], cu_seqlens_q[b+1]) against key rows [cu_seqlens_k[b],
+    cu_seqlens_k[b+1]) (int32 tensors on the tensors' device, sequences + 1 entries,
+    non-decreasing from 0); ``max_seqlen_q``/``max_seqlen_k`` bound the lengths. Masks
+    apply per sequence: "bottom_right" aligns each sequence's own diagonal, the mask of
+    the reference's JAX statements for a (qs, ks) pair
+    (``flash_hog/_jax_refs/jax_impl.py:104-130``). Each sequence's result equals the
+    dense call on that sequence alone. Computes with bf16 operands (any input dtype;
+    results in the input dtype).
+    """
+    if query.ndim != 3 or key.ndim != 3 or value.ndim != 3:
+        raise ValueError("packed tensors are (total, heads, head_dim)")
+    if scale is None:
+        scale = query.shape[-1] ** -0.5
+    if causal_alignment not in ("top_left", "bottom_right"):
+        raise ValueError(f"causal_alignment must be 'top_left' or 'bottom_right', got {causal_alignment!r}")
+    if not is_causal and (sliding_window_length is not None or causal_alignment != "top_left"):
+        raise ValueError("causal_alignment and sliding_window_length apply to causal attention only")
+    mask = MaskType.NO_MASK
+    if is_causal:
+        mask = MaskType.CAUSAL if causal_alignment == "top_left" else MaskType.CAUSAL_BOTTOM_RIGHT
+        if sliding_window_length is not None:
+            mask = SlidingWindow(mask, int(sliding_window_length))
+    packed = PackedSequences(mask, cu_seqlens_q, cu_seqlens_k, int(max_seqlen_q), int(max_seqlen_k))
+    result, _ = _DotProductAttention.apply(query.unsqueeze(0), key.unsqueeze(0), value.unsqueeze(0), packed,
+                                           float(scale), "bf16")
+    return result.squeeze(0)
+
+
+def _no_packed_vmap(mask_type):
+    if isinstance(mask_type, PackedSequences):
+        raise NotImplementedError("packed variable-length batches are not vmapped: pack the sequences instead")
+
+
 class _DotProductAttention(torch.autograd.Function):
     """Forward (outputs O and the log-sum-exp L, the latter non-differentiable)."""
 
@@ -109,6 +149,7 @@ class _DotProductAttention(torch.autograd.Function):
     @staticmethod
     def vmap(info, in_dims, query, key, value, mask_type, scale, policy):
         # Fold the vmapped axis into batch (the rule of flash_hog/jax/_pallas_gpu.py:85-102).
+        _no_packed_vmap(mask_type)
         size = info.batch_size
         q, k, v = (attn_impl._fold(x, d, size) for x, d in zip((query, key, value), in_dims[:3]))
         out, activation = _DotProductAttention.apply(q, k, v, mask_type, scale, policy)
@@ -149,6 +190,7 @@ class _DotProductAttentionBwd(torch.autograd.Function):
 
     @staticmethod
     def vmap(info, in_dims, query, key, value, activation, out, g, mask_type, scale, policy):
+        _no_packed_vmap(mask_type)
         size = info.batch_size
         args = [attn_impl._fold(x, d, size) for x, d in zip((query, key, value, activation, out, g), in_dims[:6])]
         dq, dk, dv = _DotProductAttentionBwd.apply(*args, mask_type, scale, policy)

@@ -21,7 +21,8 @@ import dataclasses
 import torch
 
 from flash_hog_b200 import _capi
-from flash_hog_b200._attention_impl import MaskType, _fold, _is_f32, _mask_args, _operand, _unfold, fp32_policy
+from flash_hog_b200._attention_impl import (MaskType, PackedSequences, _fold, _is_f32, _mask_args, _operand, _unfold,
+                                            _varlen_kw, fp32_policy)
 
 
 @dataclasses.dataclass(frozen=True)
@@ -63,17 +64,20 @@ def flash_bwdbwd(Q, K, V, O, dO, ddQ, ddK, ddV, L, mask_type: MaskType = MaskTyp
         raise ValueError(f"q_heads ({Q.shape[2]}) must be a multiple of kv_heads ({K.shape[2]})")
     causal, window = _mask_args(mask_type)
     policy = fp32_policy() if _policy is None else _policy
+    packed = mask_type if isinstance(mask_type, PackedSequences) else None
     dq2, dk2, dv2, ddo, stats = _FlashBwdBwd.apply(Q, K, V, O, dO, ddQ, ddK, ddV, L, causal, window, float(scale),
-                                                   policy)
+                                                   policy, packed)
     outs = (dq2, dk2, dv2, ddo)
     if return_stats:
         return outs, (stats[0], stats[1], stats[2])
     return outs
 
 
-def _bwdbwd_device(Q, K, V, O, dO, ddQ, ddK, ddV, L, causal: int, window: int, scale: float, policy: str):
-    """The kernels on 4-D BTNH tensors: ``(dQ2, dK2, dV2, ddO, stats)``, stats = (D, dD, B) stacked."""
-    f32 = _is_f32(Q, policy)
+def _bwdbwd_device(Q, K, V, O, dO, ddQ, ddK, ddV, L, causal: int, window: int, scale: float, policy: str,
+                   packed: PackedSequences | None = None):
+    """The kernels on 4-D BTNH tensors: ``(dQ2, dK2, dV2, ddO, stats)``, stats = (D, dD, B) stacked.
+    ``packed``: the tensors are (1, total, heads, head_dim) packed sequences."""
+    f32 = _is_f32(Q, policy, packed)
     q, k, v, o, do, ddq, ddk, ddv = (_operand(x, f32) for x in (Q, K, V, O, dO, ddQ, ddK, ddV))
     b, t, n, _ = q.shape
     lse = L.reshape(b, n, t).float().contiguous()
@@ -83,7 +87,8 @@ def _bwdbwd_device(Q, K, V, O, dO, ddQ, ddK, ddV, L, causal: int, window: int, s
     dk2, dv2 = torch.empty_like(k), torch.empty_like(k)
     # D = rowsum(dO * O) is computed on the device as part of the call.
     entry = _capi.attn_bwdbwd_f32 if f32 else _capi.attn_bwdbwd_o
-    entry(q, k, v, o, do, ddq, ddk, ddv, lse, dq2, ddo, dk2, dv2, delta, dd, bvec, scale, causal, window=window)
+    entry(q, k, v, o, do, ddq, ddk, ddv, lse, dq2, ddo, dk2, dv2, delta, dd, bvec, scale, causal, window=window,
+          **({} if f32 else _varlen_kw(packed)))
     return dq2.to(Q.dtype), dk2.to(K.dtype), dv2.to(V.dtype), ddo.to(dO.dtype), stats
 
 
@@ -93,8 +98,8 @@ class _FlashBwdBwd(torch.autograd.Function):
     Returns ``(dQ2, dK2, dV2, ddO, stats)``."""
 
     @staticmethod
-    def forward(Q, K, V, O, dO, ddQ, ddK, ddV, L, causal, window, scale, policy):
-        return _bwdbwd_device(Q, K, V, O, dO, ddQ, ddK, ddV, L, causal, window, scale, policy)
+    def forward(Q, K, V, O, dO, ddQ, ddK, ddV, L, causal, window, scale, policy, packed):
+        return _bwdbwd_device(Q, K, V, O, dO, ddQ, ddK, ddV, L, causal, window, scale, policy, packed)
 
     @staticmethod
     def setup_context(ctx, inputs, output):
@@ -107,14 +112,16 @@ class _FlashBwdBwd(torch.autograd.Function):
             "reference's double-backward rule is the last one it defines, flash_hog/jax/attention.py:100-130)")
 
     @staticmethod
-    def vmap(info, in_dims, Q, K, V, O, dO, ddQ, ddK, ddV, L, causal, window, scale, policy):
+    def vmap(info, in_dims, Q, K, V, O, dO, ddQ, ddK, ddV, L, causal, window, scale, policy, packed):
         """Batching rule of ``flash_hog/jax/_pallas_gpu.py:85-102``: the vmapped axis is
         folded into the batch axis, the kernels run once, and the results are unfolded.
         The reference requires every input to be vmapped; here an input that is not is
         broadcast along the vmapped axis first."""
+        if packed is not None:
+            raise NotImplementedError("packed variable-length batches are not vmapped: pack the sequences instead")
         size = info.batch_size
         args = [_fold(x, d, size) for x, d in zip((Q, K, V, O, dO, ddQ, ddK, ddV, L), in_dims[:9])]
-        dq2, dk2, dv2, ddo, stats = _FlashBwdBwd.apply(*args, causal, window, scale, policy)
+        dq2, dk2, dv2, ddo, stats = _FlashBwdBwd.apply(*args, causal, window, scale, policy, None)
         stats = stats.reshape(3, size, stats.shape[1] // size, *stats.shape[2:])
         return (_unfold(dq2, size), _unfold(dk2, size), _unfold(dv2, size), _unfold(ddo, size), stats), (0, 0, 0, 0, 1)
 

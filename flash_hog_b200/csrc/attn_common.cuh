@@ -41,8 +41,15 @@ struct Strides3 {
 // when window > 0, j > i + diag - window (diag = 0: top-left causal; diag =
 // Tk - Tq: bottom-right; window: sliding-window length). Without `causal` every
 // key is visible.
+//
+// Packed variable-length batches: with cu_q/cu_k set, sequence b is rows
+// [cu_q[b], cu_q[b+1]) of the packed query-side tensors (batch 1, total_q rows)
+// and rows [cu_k[b], cu_k[b+1]) of the key-side ones; Tq/Tk are then the longest
+// sequence lengths (grid sizes) and each sequence is masked on its own (its own
+// lengths and, with `br`, its own bottom-right diagonal). seq_shape() gives a
+// kernel the shape of one sequence and where its rows start.
 struct AttnShape {
-  int B, H, Tq, Tk;  // H: query heads
+  int B, H, Tq, Tk;  // H: query heads; B: sequences
   int Hk, G;         // key/value heads and the group size H / Hk (query head h uses key head h / G)
   Strides3 sq;   // query-side tensors
   Strides3 sk;   // key-side tensors
@@ -50,7 +57,38 @@ struct AttnShape {
   int causal;
   int diag;
   int window;
+  int br;                     // bottom-right alignment: diag = Tk - Tq of each sequence
+  const int* cu_q;            // varlen sequence starts (B + 1 entries), or null (dense)
+  const int* cu_k;
+  int total_q, total_k;       // rows of the packed tensors (varlen); Tq, Tk (dense)
 };
+
+// Where sequence b's rows start: the batch coordinate of its tensors' views and
+// its first query and key row (0, 0 for a dense batch).
+struct SeqRange {
+  int bc, q0, k0;
+};
+
+// The shape of sequence b alone and, in *r, where its rows start. Dense batches
+// return `s` itself. Varlen offsets are clamped to the packed tensors, so even
+// inconsistent cu_seqlens never address a row outside them.
+// Kernels are instantiated for dense (VL = false: `s` itself, no varlen arithmetic)
+// and packed (VL = true) batches.
+template <bool VL>
+__device__ __forceinline__ AttnShape seq_shape(const AttnShape& s, int b, SeqRange* r) {
+  if constexpr (!VL) {
+    *r = SeqRange{b, 0, 0};
+    return s;
+  }
+  AttnShape l = s;
+  const int q0 = max(0, min(s.cu_q[b], s.total_q)), q1 = max(q0, min(s.cu_q[b + 1], s.total_q));
+  const int k0 = max(0, min(s.cu_k[b], s.total_k)), k1 = max(k0, min(s.cu_k[b + 1], s.total_k));
+  l.Tq = min(q1 - q0, s.Tq);
+  l.Tk = min(k1 - k0, s.Tk);
+  l.diag = s.br ? l.Tk - l.Tq : 0;
+  *r = SeqRange{0, q0, k0};
+  return l;
+}
 
 // Visible keys [key_lo, key_hi] of query row i (empty when key_hi < key_lo).
 __host__ __device__ __forceinline__ int key_hi(const AttnShape& s, int i) {
@@ -96,6 +134,17 @@ __device__ __forceinline__ size_t row_offset(const Strides3& s, int b, int t, in
 // Index into a (B, H, T) fp32 statistics vector.
 __device__ __forceinline__ size_t stat_index(int b, int h, int t, int H, int T) {
   return (static_cast<size_t>(b) * H + h) * T + t;
+}
+
+// Offset of query row t (of its sequence) of head h: query-side tensors and statistics.
+__device__ __forceinline__ size_t q_row(const AttnShape& s, const SeqRange& r, int t, int h) {
+  return row_offset(s.sq, r.bc, r.q0 + t, h);
+}
+__device__ __forceinline__ size_t k_row(const AttnShape& s, const SeqRange& r, int t, int h) {
+  return row_offset(s.sk, r.bc, r.k0 + t, h);
+}
+__device__ __forceinline__ size_t q_stat(const AttnShape& s, const SeqRange& r, int t, int h) {
+  return stat_index(r.bc, h, r.q0 + t, s.H, s.total_q);
 }
 
 __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {

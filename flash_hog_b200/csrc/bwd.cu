@@ -101,7 +101,7 @@ __device__ __forceinline__ void dq_ops(const uint32_t (&vs)[CW], const uint32_t 
   }
 }
 
-template <int HD>
+template <int HD, bool VL>
 __global__ void __launch_bounds__(kBBThreads, DqPass<HD>::CTAS)
     bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
                   const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
@@ -124,9 +124,10 @@ __global__ void __launch_bounds__(kBBThreads, DqPass<HD>::CTAS)
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
 
-  const AttnShape& sh = a.sh;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int h = blockIdx.x, b = blockIdx.y;
+  SeqRange sr;
+  const AttnShape sh = seq_shape<VL>(a.sh, b, &sr);  // this sequence's lengths and mask; sr: where its rows start
   const int qt = gridDim.z - 1 - blockIdx.z;  // longest causal rows first
   const int q0 = qt * kBM;
   int j0;
@@ -162,9 +163,9 @@ __global__ void __launch_bounds__(kBBThreads, DqPass<HD>::CTAS)
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
       mbar_arrive_expect_tx(&bar_res, 3 * G::RES);
-      tma_rows<HD>(s_q, &tm_q, &bar_res, q0, kBM, h, b);
-      tma_rows<HD>(s_do, &tm_do, &bar_res, q0, kBM, h, b);
-      tma_rows<HD>(s_o, &tm_o, &bar_res, q0, kBM, h, b);
+      tma_rows<HD>(s_q, &tm_q, &bar_res, sr.q0 + q0, kBM, h, sr.bc);
+      tma_rows<HD>(s_do, &tm_do, &bar_res, sr.q0 + q0, kBM, h, sr.bc);
+      tma_rows<HD>(s_o, &tm_o, &bar_res, sr.q0 + q0, kBM, h, sr.bc);
       int issued = 0;
       for (int it = 0; it < n; ++it) {
         const int s = it % ST;
@@ -178,8 +179,8 @@ __global__ void __launch_bounds__(kBBThreads, DqPass<HD>::CTAS)
         }
         uint8_t* slot = s_ring + s * G::SLOT;
         mbar_arrive_expect_tx(&bar_full[s], G::SLOT);
-        tma_rows<HD>(slot, &tm_k, &bar_full[s], (j0 + it) * BN, BN, h / sh.G, b);
-        tma_rows<HD>(slot + G::STR, &tm_v, &bar_full[s], (j0 + it) * BN, BN, h / sh.G, b);
+        tma_rows<HD>(slot, &tm_k, &bar_full[s], sr.k0 + (j0 + it) * BN, BN, h / sh.G, sr.bc);
+        tma_rows<HD>(slot + G::STR, &tm_v, &bar_full[s], sr.k0 + (j0 + it) * BN, BN, h / sh.G, sr.bc);
         issued = it + 1;
       }
       // Every issued copy must land before this CTA's shared memory is released.
@@ -246,7 +247,7 @@ __global__ void __launch_bounds__(kBBThreads, DqPass<HD>::CTAS)
     const uint32_t lane_t = tmem + tmem_lane_base(warp & 3);
     const int row = q0 + r;
     const bool row_ok = row < sh.Tq;
-    const size_t vi = stat_index(b, h, row_ok ? row : 0, sh.H, sh.Tq);
+    const size_t vi = q_stat(sh, sr, row_ok ? row : 0, h);
     const float lse = row_ok ? a.lse[vi] : 0.f;
     const float lg = lse > -INFINITY ? lse * kLog2e : 0.f;  // -inf: the row sees no key (all masked)
     const int khi = key_hi(sh, row), klo = key_lo(sh, row);
@@ -329,7 +330,7 @@ __global__ void __launch_bounds__(kBBThreads, DqPass<HD>::CTAS)
     }
     if (ok && n == 0) {
       // No key tile: dQ = 0 (plus the addend).
-      const size_t off = row_offset(sh.sq, b, row_ok ? row : 0, h) + wg * (HD / 2);
+      const size_t off = q_row(sh, sr, row_ok ? row : 0, h) + wg * (HD / 2);
       for (int c = 0; row_ok && c < HD / 2; c += 8)
         reinterpret_cast<uint4*>(a.dq + off + c)[0] =
             a.dq_acc ? reinterpret_cast<const uint4*>(a.dq_acc + off + c)[0] : make_uint4(0, 0, 0, 0);
@@ -339,7 +340,7 @@ __global__ void __launch_bounds__(kBBThreads, DqPass<HD>::CTAS)
     if (ok && n > 0) {
       tc_fence_after();
       const int srow = row_ok ? row : 0;
-      const size_t off = row_offset(sh.sq, b, srow, h) + wg * (HD / 2);
+      const size_t off = q_row(sh, sr, srow, h) + wg * (HD / 2);
       tmem_row_to_global<HD / 2>(tmem, warp, G::C_DQ + wg * (HD / 2), a.dq + off, row_ok, sh.scale,
                                  a.dq_acc ? a.dq_acc + off : nullptr);
     } else if (!ok && threadIdx.x == kBBFirstEwWarp * 32) {
@@ -422,7 +423,7 @@ __device__ __forceinline__ void dkv_ops(const uint32_t (&vs)[CW], const uint32_t
   }
 }
 
-template <int HD>
+template <int HD, bool VL>
 __global__ void __launch_bounds__(kBBThreads, DkvPass<HD>::CTAS)
     bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                     const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
@@ -440,9 +441,10 @@ __global__ void __launch_bounds__(kBBThreads, DkvPass<HD>::CTAS)
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
 
-  const AttnShape& sh = a.sh;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int hk = blockIdx.x, b = blockIdx.y;
+  SeqRange sr;
+  const AttnShape sh = seq_shape<VL>(a.sh, b, &sr);
   const int k0 = blockIdx.z * kBM;  // key tile 0 first: the most causal query tiles
   int qt_begin;
   const int n = query_tiles(sh, k0, kBM, BN, &qt_begin);  // query tiles that see any of these keys
@@ -481,7 +483,7 @@ __global__ void __launch_bounds__(kBBThreads, DkvPass<HD>::CTAS)
     if (warp >= kBBFirstEwWarp) {
       const int wg = (warp - kBBFirstEwWarp) >> 2;
       const int key = k0 + (warp & 3) * 32 + lane;
-      const size_t off = row_offset(sh.sk, b, key < sh.Tk ? key : 0, hk);
+      const size_t off = k_row(sh, sr, key < sh.Tk ? key : 0, hk);
       const __nv_bfloat16* add = wg == 0 ? a.dk_acc : a.dv_acc;
       __nv_bfloat16* dst = (wg == 0 ? a.dk : a.dv) + off;
       if (key < sh.Tk) {
@@ -499,8 +501,8 @@ __global__ void __launch_bounds__(kBBThreads, DkvPass<HD>::CTAS)
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_q);
       mbar_arrive_expect_tx(&bar_res, 2 * G::RES);
-      tma_rows<HD>(s_k, &tm_k, &bar_res, k0, kBM, hk, b);
-      tma_rows<HD>(s_v, &tm_v, &bar_res, k0, kBM, hk, b);
+      tma_rows<HD>(s_k, &tm_k, &bar_res, sr.k0 + k0, kBM, hk, sr.bc);
+      tma_rows<HD>(s_v, &tm_v, &bar_res, sr.k0 + k0, kBM, hk, sr.bc);
     }
     const float inv_scale = 1.f / sh.scale;
     constexpr int RPL = BN / 32;
@@ -511,7 +513,7 @@ __global__ void __launch_bounds__(kBBThreads, DkvPass<HD>::CTAS)
 #pragma unroll
       for (int k = 0; k < RPL; ++k) {
         const int q = q0 + lane + 32 * k;
-        const size_t idx = stat_index(b, h, q < sh.Tq ? q : 0, sh.H, sh.Tq);
+        const size_t idx = q_stat(sh, sr, q < sh.Tq ? q : 0, h);
         raw[k][0] = a.lse[idx];
         raw[k][1] = a.delta[idx];
       }
@@ -533,8 +535,8 @@ __global__ void __launch_bounds__(kBBThreads, DkvPass<HD>::CTAS)
       // together with the copies.
       if (lane == 0) {
         mbar_expect_tx(&bar_full[s], 2 * G::STR);
-        tma_rows<HD>(slot, &tm_q, &bar_full[s], q0, BN, h, b);
-        tma_rows<HD>(slot + G::STR, &tm_do, &bar_full[s], q0, BN, h, b);
+        tma_rows<HD>(slot, &tm_q, &bar_full[s], sr.q0 + q0, BN, h, sr.bc);
+        tma_rows<HD>(slot + G::STR, &tm_do, &bar_full[s], sr.q0 + q0, BN, h, sr.bc);
       }
       float raw[RPL][2];
 #pragma unroll
@@ -702,7 +704,7 @@ __global__ void __launch_bounds__(kBBThreads, DkvPass<HD>::CTAS)
     if (ok) ok = mbar_wait_warp(&bar_acc, 0, &abort_flag);
     if (ok) {
       tc_fence_after();
-      const size_t off = row_offset(sh.sk, b, key_ok ? key : 0, hk);
+      const size_t off = k_row(sh, sr, key_ok ? key : 0, hk);
       const __nv_bfloat16* add = wg == 0 ? a.dk_acc : a.dv_acc;
       tmem_row_to_global<HD>(tmem, warp, wg == 0 ? G::C_DK : G::C_DV, (wg == 0 ? a.dk : a.dv) + off, key_ok,
                              wg == 0 ? sh.scale : 1.f, add ? add + off : nullptr);
@@ -716,23 +718,23 @@ __global__ void __launch_bounds__(kBBThreads, DkvPass<HD>::CTAS)
   if (warp == kBBWarpMma) tmem_dealloc(tmem, G::TMEM_COLS);
 }
 
-template <int HD>
+template <int HD, bool VL>
 int launch_bwd_hd(const AttnShape& s, const BwdPtrs& p, int* status, cudaStream_t stream) {
   using GQ = DqPass<HD>;
   using GK = DkvPass<HD>;
   CUtensorMap mq[5], mk[4];
-  bool ok = make_seq_map(&mq[0], p.q, HD, s.Tq, s.H, s.B, s.sq, kBM) &&
-            make_seq_map(&mq[1], p.dO, HD, s.Tq, s.H, s.B, s.sq, kBM) &&
-            make_seq_map(&mq[2], p.k, HD, s.Tk, s.Hk, s.B, s.sk, GQ::BN) &&
-            make_seq_map(&mq[3], p.v, HD, s.Tk, s.Hk, s.B, s.sk, GQ::BN) &&
-            make_seq_map(&mq[4], p.o, HD, s.Tq, s.H, s.B, s.sq, kBM) &&
-            make_seq_map(&mk[0], p.k, HD, s.Tk, s.Hk, s.B, s.sk, kBM) &&
-            make_seq_map(&mk[1], p.v, HD, s.Tk, s.Hk, s.B, s.sk, kBM) &&
-            make_seq_map(&mk[2], p.q, HD, s.Tq, s.H, s.B, s.sq, GK::BN) &&
-            make_seq_map(&mk[3], p.dO, HD, s.Tq, s.H, s.B, s.sq, GK::BN);
+  bool ok = make_seq_map(&mq[0], p.q, HD, s.total_q, s.H, map_batch(s), s.sq, kBM) &&
+            make_seq_map(&mq[1], p.dO, HD, s.total_q, s.H, map_batch(s), s.sq, kBM) &&
+            make_seq_map(&mq[2], p.k, HD, s.total_k, s.Hk, map_batch(s), s.sk, GQ::BN) &&
+            make_seq_map(&mq[3], p.v, HD, s.total_k, s.Hk, map_batch(s), s.sk, GQ::BN) &&
+            make_seq_map(&mq[4], p.o, HD, s.total_q, s.H, map_batch(s), s.sq, kBM) &&
+            make_seq_map(&mk[0], p.k, HD, s.total_k, s.Hk, map_batch(s), s.sk, kBM) &&
+            make_seq_map(&mk[1], p.v, HD, s.total_k, s.Hk, map_batch(s), s.sk, kBM) &&
+            make_seq_map(&mk[2], p.q, HD, s.total_q, s.H, map_batch(s), s.sq, GK::BN) &&
+            make_seq_map(&mk[3], p.dO, HD, s.total_q, s.H, map_batch(s), s.sq, GK::BN);
   if (!ok) return kInvalidArgument;
-  if (ensure_smem_limit(reinterpret_cast<const void*>(&bwd_dq_kernel<HD>), GQ::SMEM) != kOk ||
-      ensure_smem_limit(reinterpret_cast<const void*>(&bwd_dkdv_kernel<HD>), GK::SMEM) != kOk)
+  if (ensure_smem_limit(reinterpret_cast<const void*>(&bwd_dq_kernel<HD, VL>), GQ::SMEM) != kOk ||
+      ensure_smem_limit(reinterpret_cast<const void*>(&bwd_dkdv_kernel<HD, VL>), GK::SMEM) != kOk)
     return kLaunchFailed;
   BwdArgs args{s,
                p.lse,
@@ -744,10 +746,10 @@ int launch_bwd_hd(const AttnShape& s, const BwdPtrs& p, int* status, cudaStream_
                static_cast<const __nv_bfloat16*>(p.dk_acc),
                static_cast<const __nv_bfloat16*>(p.dv_acc),
                status};
-  bwd_dq_kernel<HD><<<dim3(s.H, s.B, (s.Tq + kBM - 1) / kBM), kBBThreads, GQ::SMEM, stream>>>(mq[0], mq[1], mq[2],
+  bwd_dq_kernel<HD, VL><<<dim3(s.H, s.B, (s.Tq + kBM - 1) / kBM), kBBThreads, GQ::SMEM, stream>>>(mq[0], mq[1], mq[2],
                                                                                              mq[3], mq[4], args);
   if (after_launch() != kOk) return kLaunchFailed;
-  bwd_dkdv_kernel<HD><<<dim3(s.Hk, s.B, (s.Tk + kBM - 1) / kBM), kBBThreads, GK::SMEM, stream>>>(mk[0], mk[1], mk[2],
+  bwd_dkdv_kernel<HD, VL><<<dim3(s.Hk, s.B, (s.Tk + kBM - 1) / kBM), kBBThreads, GK::SMEM, stream>>>(mk[0], mk[1], mk[2],
                                                                                                mk[3], args);
   return after_launch();
 }
@@ -755,8 +757,8 @@ int launch_bwd_hd(const AttnShape& s, const BwdPtrs& p, int* status, cudaStream_
 }  // namespace
 
 int launch_bwd(const AttnShape& s, int hd, const BwdPtrs& p, int* status, cudaStream_t stream) {
-  if (hd == 64) return launch_bwd_hd<64>(s, p, status, stream);
-  if (hd == 128) return launch_bwd_hd<128>(s, p, status, stream);
+  if (hd == 64) return s.cu_q ? launch_bwd_hd<64, true>(s, p, status, stream) : launch_bwd_hd<64, false>(s, p, status, stream);
+  if (hd == 128) return s.cu_q ? launch_bwd_hd<128, true>(s, p, status, stream) : launch_bwd_hd<128, false>(s, p, status, stream);
   return kUnsupported;
 }
 

@@ -80,22 +80,29 @@ struct QPass {
 // Stats sweep: row partial sums over this thread's CW columns. dD and r3 are
 // accumulated without the softmax scale of ddS (applied once per row after the
 // sweep): dD/scale += P ddS', r1 += P dPa, r2 += P dP, r3/scale += P ddS' dP.
+// The arithmetic runs on column pairs with the packed fp32x2 instructions
+// (fma/mul/add.rn.f32x2: per lane the same IEEE results as the scalar forms, one
+// issue slot for two), so the sums are kept as (even, odd) column pairs.
 template <int CW, bool MASK>
 __device__ __forceinline__ void q_stats(const uint32_t (&vs)[CW], const uint32_t (&vdds)[CW],
                                         const uint32_t (&vdp)[CW], const uint32_t (&vdpa)[CW], int kc, int klo,
-                                        int khi, float sc, float sc2, float lg, float& dD, float& r1, float& r2,
-                                        float& r3) {
+                                        int khi, float sc2, float lg, float2& dD, float2& r1, float2& r2,
+                                        float2& r3) {
+  const float2 m = make_float2(sc2, sc2), nl = make_float2(-lg, -lg);
 #pragma unroll
-  for (int i = 0; i < CW; ++i) {
-    float s = fmaf(__uint_as_float(vs[i]), sc2, -lg);
-    if (MASK && (kc + i > khi || kc + i < klo)) s = -INFINITY;
-    const float p = ex2(s);
-    const float t = __uint_as_float(vdds[i]) * p;
-    const float dp = __uint_as_float(vdp[i]);
-    dD += t;
-    r3 = fmaf(t, dp, r3);
-    r1 = fmaf(__uint_as_float(vdpa[i]), p, r1);
-    r2 = fmaf(dp, p, r2);
+  for (int i = 0; i < CW; i += 2) {
+    float2 s = __ffma2_rn(f2(vs[i], vs[i + 1]), m, nl);
+    if (MASK) {
+      if (kc + i > khi || kc + i < klo) s.x = -INFINITY;
+      if (kc + i + 1 > khi || kc + i + 1 < klo) s.y = -INFINITY;
+    }
+    const float2 p = make_float2(ex2(s.x), ex2(s.y));
+    const float2 dp = f2(vdp[i], vdp[i + 1]);
+    const float2 t = __fmul2_rn(f2(vdds[i], vdds[i + 1]), p);
+    dD = __fadd2_rn(dD, t);
+    r3 = __ffma2_rn(t, dp, r3);
+    r1 = __ffma2_rn(f2(vdpa[i], vdpa[i + 1]), p, r1);
+    r2 = __ffma2_rn(dp, p, r2);
   }
 }
 
@@ -104,36 +111,36 @@ __device__ __forceinline__ void q_stats(const uint32_t (&vs)[CW], const uint32_t
 // the epilogue instead of per element). With u = ddS - dD and c = dD D + B,
 //   ddP = P u,  dS/scale = P (dP - D),
 //   dS2/scale = P (dPa + dP u - ddS D - B) = P (dPa - c) + ddP (dP - D).
+// Column pairs go through the packed fp32x2 instructions, as in q_stats.
 template <int CW, bool MASK>
 __device__ __forceinline__ void q_ops(const uint32_t (&vs)[CW], const uint32_t (&vdds)[CW],
                                       const uint32_t (&vdp)[CW], const uint32_t (&vdpa)[CW], int kc, int klo, int khi,
                                       float sc, float sc2, float lg, float dv, float dD, float cq,
                                       uint32_t (&o_ds)[CW / 2], uint32_t (&o_ds2)[CW / 2], uint32_t (&o_ddp)[CW / 2],
                                       uint32_t (&o_p)[CW / 2]) {
+  const float2 m = make_float2(sc2, sc2), nl = make_float2(-lg, -lg), msc = make_float2(sc, sc);
+  const float2 ndd = make_float2(-dD, -dD), ndv = make_float2(-dv, -dv), ncq = make_float2(-cq, -cq);
 #pragma unroll
   for (int i = 0; i < CW; i += 2) {
-    float pp[2], ddp[2], ds[2], ds2[2];
-#pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      const int c = i + e;
-      float s = fmaf(__uint_as_float(vs[c]), sc2, -lg);
-      if (MASK && (kc + c > khi || kc + c < klo)) s = -INFINITY;
-      const float p = ex2(s);
-      const float u = fmaf(__uint_as_float(vdds[c]), sc, -dD);  // ddS - dD
-      const float dpd = __uint_as_float(vdp[c]) - dv;            // dP - D
-      pp[e] = p;
-      ddp[e] = p * u;
-      ds[e] = p * dpd;
-      ds2[e] = fmaf(ddp[e], dpd, p * (__uint_as_float(vdpa[c]) - cq));
+    float2 s = __ffma2_rn(f2(vs[i], vs[i + 1]), m, nl);
+    if (MASK) {
+      if (kc + i > khi || kc + i < klo) s.x = -INFINITY;
+      if (kc + i + 1 > khi || kc + i + 1 < klo) s.y = -INFINITY;
     }
-    o_p[i / 2] = pack_bf16(pp[0], pp[1]);
-    o_ddp[i / 2] = pack_bf16(ddp[0], ddp[1]);
-    o_ds[i / 2] = pack_bf16(ds[0], ds[1]);
-    o_ds2[i / 2] = pack_bf16(ds2[0], ds2[1]);
+    const float2 p = make_float2(ex2(s.x), ex2(s.y));
+    const float2 u = __ffma2_rn(f2(vdds[i], vdds[i + 1]), msc, ndd);  // ddS - dD
+    const float2 dpd = __fadd2_rn(f2(vdp[i], vdp[i + 1]), ndv);       // dP - D
+    const float2 ddp = __fmul2_rn(p, u);
+    const float2 ds = __fmul2_rn(p, dpd);
+    const float2 ds2 = __ffma2_rn(ddp, dpd, __fmul2_rn(p, __fadd2_rn(f2(vdpa[i], vdpa[i + 1]), ncq)));
+    o_p[i / 2] = pack_bf16(p.x, p.y);
+    o_ddp[i / 2] = pack_bf16(ddp.x, ddp.y);
+    o_ds[i / 2] = pack_bf16(ds.x, ds.y);
+    o_ds2[i / 2] = pack_bf16(ds2.x, ds2.y);
   }
 }
 
-template <int HD>
+template <int HD, bool VL>
 __global__ void __launch_bounds__(kBBThreads, 1)
     bwdbwd_q_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
                     const __grid_constant__ CUtensorMap tm_ddq, const __grid_constant__ CUtensorMap tm_k,
@@ -160,9 +167,10 @@ __global__ void __launch_bounds__(kBBThreads, 1)
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
 
-  const AttnShape& sh = a.sh;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int h = blockIdx.x, b = blockIdx.y;
+  SeqRange sr;
+  const AttnShape sh = seq_shape<VL>(a.sh, b, &sr);  // this sequence's lengths and mask; sr: where its rows start
   const int qt = gridDim.z - 1 - blockIdx.z;  // longest causal rows first
   const int q0 = qt * kBM;
   int j0;
@@ -203,10 +211,10 @@ __global__ void __launch_bounds__(kBBThreads, 1)
       tma_prefetch_desc(&tm_k);
       const bool fuse_d = a.delta_out != nullptr;
       mbar_arrive_expect_tx(&bar_res, (fuse_d ? 4 : 3) * G::RES);
-      tma_rows<HD>(s_q, &tm_q, &bar_res, q0, kBM, h, b);
-      tma_rows<HD>(s_do, &tm_do, &bar_res, q0, kBM, h, b);
-      tma_rows<HD>(s_ddq, &tm_ddq, &bar_res, q0, kBM, h, b);
-      if (fuse_d) tma_rows<HD>(s_o, &tm_o, &bar_res, q0, kBM, h, b);
+      tma_rows<HD>(s_q, &tm_q, &bar_res, sr.q0 + q0, kBM, h, sr.bc);
+      tma_rows<HD>(s_do, &tm_do, &bar_res, sr.q0 + q0, kBM, h, sr.bc);
+      tma_rows<HD>(s_ddq, &tm_ddq, &bar_res, sr.q0 + q0, kBM, h, sr.bc);
+      if (fuse_d) tma_rows<HD>(s_o, &tm_o, &bar_res, sr.q0 + q0, kBM, h, sr.bc);
       int issued = 0;
       for (int it = 0; it < total; ++it) {
         const int s = it % ST;
@@ -221,8 +229,8 @@ __global__ void __launch_bounds__(kBBThreads, 1)
         const int k0 = (j0 + it % n) * BN;
         uint8_t* slot = s_ring + s * G::SLOT;
         mbar_arrive_expect_tx(&bar_full[s], G::SLOT);
-        tma_pair<HD>(slot, &tm_k, &tm_ddk, &bar_full[s], k0, BN, h / sh.G, b);
-        tma_pair<HD>(slot + G::PAIR, &tm_v, &tm_ddv, &bar_full[s], k0, BN, h / sh.G, b);
+        tma_pair<HD>(slot, &tm_k, &tm_ddk, &bar_full[s], sr.k0 + k0, BN, h / sh.G, sr.bc);
+        tma_pair<HD>(slot + G::PAIR, &tm_v, &tm_ddv, &bar_full[s], sr.k0 + k0, BN, h / sh.G, sr.bc);
         issued = it + 1;
       }
       // Every issued copy must land before this CTA's shared memory is released.
@@ -301,12 +309,12 @@ __global__ void __launch_bounds__(kBBThreads, 1)
     const int cb = wg * CW;
     const int row = q0 + r;
     const bool row_ok = row < sh.Tq;
-    const size_t vi = stat_index(b, h, row_ok ? row : 0, sh.H, sh.Tq);
+    const size_t vi = q_stat(sh, sr, row_ok ? row : 0, h);
     const float lse = row_ok ? a.lse[vi] : 0.f;
     const float lg = lse > -INFINITY ? lse * kLog2e : 0.f;  // -inf: the row sees no key (all masked)
     const int khi = key_hi(sh, row), klo = key_lo(sh, row);
     const float sc = sh.scale, sc2 = sh.scale * kLog2e;
-    float dD = 0.f, r1 = 0.f, r2 = 0.f, r3 = 0.f, Bv = 0.f, cq = 0.f;
+    float dD = 0.f, Bv = 0.f, cq = 0.f;
     bool ok = true;
     float dv = 0.f;
     if (a.delta_out == nullptr) {
@@ -322,16 +330,14 @@ __global__ void __launch_bounds__(kBBThreads, 1)
       dv = dred[0][r] + dred[1][r];
       if (wg == 0 && row_ok) a.delta_out[vi] = dv;
     }
-    for (int it = 0; ok && it < total; ++it) {
-      const int j = it % n;
-      const bool sweep2 = it >= n;
-      const int kc = (j0 + j) * BN + cb;  // first key of this thread's columns
+    // Waits for streamed tile `it`'s scores and loads this thread's share of them into
+    // registers, then releases the score buffer to the tensor core.
+    auto load_scores = [&](int it, uint32_t (&vs)[CW], uint32_t (&vdds)[CW], uint32_t (&vdp)[CW],
+                           uint32_t (&vdpa)[CW]) {
       const int sb = buf_of(it);
-      ok = mbar_wait_warp(&bar_sc_full[sb], use_of(it) & 1, &abort_flag);
-      if (!ok) break;
+      if (!mbar_wait_warp(&bar_sc_full[sb], use_of(it) & 1, &abort_flag)) return false;
       tc_fence_after();
       const uint32_t tb = tmem + sb * G::SCORE_COLS;
-      uint32_t vs[CW], vdds[CW], vdp[CW], vdpa[CW];
       tmem_share<CW>(tb, warp, G::C_S + cb, vs);
       tmem_share<CW>(tb, warp, G::C_DDS + cb, vdds);
       tmem_share<CW>(tb, warp, G::C_DP + cb, vdp);
@@ -342,51 +348,67 @@ __global__ void __launch_bounds__(kBBThreads, 1)
       reg_fence(vdp);
       reg_fence(vdpa);
       warp_arrive(&bar_sc_empty[sb]);  // the tensor core may reuse this score buffer now
-      const bool need_mask = kc + CW - 1 > khi || kc < klo;
-      if (!sweep2) {
-        if (need_mask)
-          q_stats<CW, true>(vs, vdds, vdp, vdpa, kc, klo, khi, sc, sc2, lg, dD, r1, r2, r3);
-        else
-          q_stats<CW, false>(vs, vdds, vdp, vdpa, kc, klo, khi, sc, sc2, lg, dD, r1, r2, r3);
-        if (it == n - 1) {
-          // Combine the two warpgroups' column halves (same order on both sides).
-          red[0][wg][r] = dD;
-          red[1][wg][r] = r1;
-          red[2][wg][r] = r2;
-          red[3][wg][r] = r3;
-          warp_arrive(&bar_red);
-          ok = mbar_wait_warp(&bar_red, 0, &abort_flag);
-          if (!ok) break;
-          dD = (red[0][0][r] + red[0][1][r]) * sc;
-          r1 = red[1][0][r] + red[1][1][r];
-          r2 = red[2][0][r] + red[2][1][r];
-          r3 = (red[3][0][r] + red[3][1][r]) * sc;
-          Bv = r1 - dD * r2 - dv * dD + r3;
-          cq = r1 - dD * r2 + r3;  // dD D + B
-        }
-      } else {
-        uint32_t o_ds[CW / 2], o_ds2[CW / 2], o_ddp[CW / 2], o_p[CW / 2];
-        if (need_mask)
-          q_ops<CW, true>(vs, vdds, vdp, vdpa, kc, klo, khi, sc, sc2, lg, dv, dD, cq, o_ds, o_ds2, o_ddp, o_p);
-        else
-          q_ops<CW, false>(vs, vdds, vdp, vdpa, kc, klo, khi, sc, sc2, lg, dv, dD, cq, o_ds, o_ds2, o_ddp, o_p);
-        if (j > 0) ok = mbar_wait_warp(&bar_ops_empty, (j - 1) & 1, &abort_flag);
+      return true;
+    };
+    // Sweep 1: the row statistics. Its partial sums live only in this loop.
+    if (ok && n > 0) {
+      float2 pdD = make_float2(0.f, 0.f), pr1 = pdD, pr2 = pdD, pr3 = pdD;  // (even, odd) column partial sums
+      for (int j = 0; ok && j < n; ++j) {
+        const int kc = (j0 + j) * BN + cb;  // first key of this thread's columns
+        uint32_t vs[CW], vdds[CW], vdp[CW], vdpa[CW];
+        ok = load_scores(j, vs, vdds, vdp, vdpa);
         if (!ok) break;
-        tc_fence_after();
-        // This warpgroup's CW keys are packed columns [CW/2 wg, CW/2 wg + CW/2) of each operand.
-        const uint32_t to = tmem + tmem_lane_base(warp & 3) + G::C_OPS + (CW / 2) * wg;
-        tmem_st_ops(to, o_ds);
-        tmem_st_ops(to + G::OPS_COLS, o_ds2);
-        tmem_st_ops(to + 2 * G::OPS_COLS, o_ddp);
-        tmem_st_ops(to + 3 * G::OPS_COLS, o_p);
-        tmem_wait_st();
-        warp_arrive(&bar_ops_full);
+        if (kc + CW - 1 > khi || kc < klo)
+          q_stats<CW, true>(vs, vdds, vdp, vdpa, kc, klo, khi, sc2, lg, pdD, pr1, pr2, pr3);
+        else
+          q_stats<CW, false>(vs, vdds, vdp, vdpa, kc, klo, khi, sc2, lg, pdD, pr1, pr2, pr3);
       }
+      if (ok) {
+        // Combine the column pairs, then the two warpgroups' column halves (same
+        // order on both sides).
+        red[0][wg][r] = pdD.x + pdD.y;
+        red[1][wg][r] = pr1.x + pr1.y;
+        red[2][wg][r] = pr2.x + pr2.y;
+        red[3][wg][r] = pr3.x + pr3.y;
+        warp_arrive(&bar_red);
+        ok = mbar_wait_warp(&bar_red, 0, &abort_flag);
+      }
+      if (ok) {
+        dD = (red[0][0][r] + red[0][1][r]) * sc;
+        const float r1 = red[1][0][r] + red[1][1][r];
+        const float r2 = red[2][0][r] + red[2][1][r];
+        const float r3 = (red[3][0][r] + red[3][1][r]) * sc;
+        Bv = r1 - dD * r2 - dv * dD + r3;
+        cq = r1 - dD * r2 + r3;  // dD D + B
+      }
+    }
+    // Sweep 2: the bf16 operands of the accumulating MMAs.
+    for (int j = 0; ok && j < n; ++j) {
+      const int kc = (j0 + j) * BN + cb;
+      uint32_t vs[CW], vdds[CW], vdp[CW], vdpa[CW];
+      ok = load_scores(n + j, vs, vdds, vdp, vdpa);
+      if (!ok) break;
+      uint32_t o_ds[CW / 2], o_ds2[CW / 2], o_ddp[CW / 2], o_p[CW / 2];
+      if (kc + CW - 1 > khi || kc < klo)
+        q_ops<CW, true>(vs, vdds, vdp, vdpa, kc, klo, khi, sc, sc2, lg, dv, dD, cq, o_ds, o_ds2, o_ddp, o_p);
+      else
+        q_ops<CW, false>(vs, vdds, vdp, vdpa, kc, klo, khi, sc, sc2, lg, dv, dD, cq, o_ds, o_ds2, o_ddp, o_p);
+      if (j > 0) ok = mbar_wait_warp(&bar_ops_empty, (j - 1) & 1, &abort_flag);
+      if (!ok) break;
+      tc_fence_after();
+      // This warpgroup's CW keys are packed columns [CW/2 wg, CW/2 wg + CW/2) of each operand.
+      const uint32_t to = tmem + tmem_lane_base(warp & 3) + G::C_OPS + (CW / 2) * wg;
+      tmem_st_ops(to, o_ds);
+      tmem_st_ops(to + G::OPS_COLS, o_ds2);
+      tmem_st_ops(to + 2 * G::OPS_COLS, o_ddp);
+      tmem_st_ops(to + 3 * G::OPS_COLS, o_p);
+      tmem_wait_st();
+      warp_arrive(&bar_ops_full);
     }
     if (ok && n == 0) {
       // No key tile: every output of these rows is zero.
       if (row_ok) {
-        zero_row_global<HD>((wg == 0 ? a.dq2 : a.ddo) + row_offset(sh.sq, b, row, h));
+        zero_row_global<HD>((wg == 0 ? a.dq2 : a.ddo) + q_row(sh, sr, row, h));
         if (wg == 0) {
           a.dd[vi] = 0.f;
           a.bv[vi] = 0.f;
@@ -399,13 +421,13 @@ __global__ void __launch_bounds__(kBBThreads, 1)
       tc_fence_after();
       const int srow = row_ok ? row : 0;
       if (wg == 0) {
-        tmem_row_to_global<HD>(tmem, warp, G::C_DQ, a.dq2 + row_offset(sh.sq, b, srow, h), row_ok, sc);
+        tmem_row_to_global<HD>(tmem, warp, G::C_DQ, a.dq2 + q_row(sh, sr, srow, h), row_ok, sc);
         if (row_ok) {
           a.dd[vi] = dD;
           a.bv[vi] = Bv;
         }
       } else {
-        tmem_row_to_global<HD>(tmem, warp, G::C_DDO, a.ddo + row_offset(sh.sq, b, srow, h), row_ok);
+        tmem_row_to_global<HD>(tmem, warp, G::C_DDO, a.ddo + q_row(sh, sr, srow, h), row_ok);
       }
     } else if (!ok && threadIdx.x == kBBFirstEwWarp * 32) {
       raise_error(a.status, &abort_flag, kDevTimeoutMma);
@@ -458,40 +480,44 @@ struct KPass {
 // the same identities as the query pass. The per-query statistics arrive
 // already folded into the score products by the bias MMA:
 //   vs = S - L/scale,  vdds = ddS/scale - dD/scale,  vdp = dP - D,  vdpa = dPa - c.
+// Column pairs go through the packed fp32x2 instructions.
 template <int CW, bool MASK>
 __device__ __forceinline__ void k_ops(const uint32_t (&vs)[CW], const uint32_t (&vdds)[CW],
                                       const uint32_t (&vdp)[CW], const uint32_t (&vdpa)[CW], int qc, int qlo, int qhi,
                                       float sc, float sc2, uint32_t (&o_ds)[CW / 2],
                                       uint32_t (&o_ds2)[CW / 2], uint32_t (&o_ddp)[CW / 2]) {
+  const float2 m = make_float2(sc2, sc2), msc = make_float2(sc, sc);
 #pragma unroll
   for (int i = 0; i < CW; i += 2) {
-    float ddp[2], ds[2], ds2[2];
-#pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      const int c = i + e;
-      float s = __uint_as_float(vs[c]) * sc2;
-      if (MASK && (qc + c > qhi || qc + c < qlo)) s = -INFINITY;
-      const float p = ex2(s);
-      const float u = __uint_as_float(vdds[c]) * sc;  // ddS - dD
-      const float dpd = __uint_as_float(vdp[c]);      // dP - D
-      ddp[e] = p * u;
-      ds[e] = p * dpd;
-      ds2[e] = fmaf(ddp[e], dpd, p * __uint_as_float(vdpa[c]));
+    float2 s = __fmul2_rn(f2(vs[i], vs[i + 1]), m);
+    if (MASK) {
+      if (qc + i > qhi || qc + i < qlo) s.x = -INFINITY;
+      if (qc + i + 1 > qhi || qc + i + 1 < qlo) s.y = -INFINITY;
     }
-    o_ddp[i / 2] = pack_bf16(ddp[0], ddp[1]);
-    o_ds[i / 2] = pack_bf16(ds[0], ds[1]);
-    o_ds2[i / 2] = pack_bf16(ds2[0], ds2[1]);
+    const float2 p = make_float2(ex2(s.x), ex2(s.y));
+    const float2 u = __fmul2_rn(f2(vdds[i], vdds[i + 1]), msc);  // ddS - dD
+    const float2 dpd = f2(vdp[i], vdp[i + 1]);                     // dP - D
+    const float2 ddp = __fmul2_rn(p, u);
+    const float2 ds = __fmul2_rn(p, dpd);
+    const float2 ds2 = __ffma2_rn(ddp, dpd, __fmul2_rn(p, f2(vdpa[i], vdpa[i + 1])));
+    o_ddp[i / 2] = pack_bf16(ddp.x, ddp.y);
+    o_ds[i / 2] = pack_bf16(ds.x, ds.y);
+    o_ds2[i / 2] = pack_bf16(ds2.x, ds2.y);
   }
 }
 
 
 // A unit of key-pass work: one 128-row key tile of one (key head, batch).
+// `l` is the item's sequence (its lengths and mask), `r` where that sequence's rows start.
 struct KItem {
   int hk, b, k0, qt_begin, n, total;  // n query tiles per query head; total = n * G streamed tiles
+  AttnShape l;
+  SeqRange r;
 };
 
 // Work item w in heaviest-first order (key tile 0 first: the most causal query
 // tiles), key heads fastest.
+template <bool VL>
 __device__ __forceinline__ KItem k_item(const AttnShape& sh, int w, int bn) {
   const int per_kt = sh.Hk * sh.B;
   const int kt = w / per_kt, rem = w - kt * per_kt;
@@ -499,7 +525,8 @@ __device__ __forceinline__ KItem k_item(const AttnShape& sh, int w, int bn) {
   it.hk = rem % sh.Hk;
   it.b = rem / sh.Hk;
   it.k0 = kt * kBM;
-  it.n = query_tiles(sh, it.k0, kBM, bn, &it.qt_begin);  // query tiles that see any of these keys
+  it.l = seq_shape<VL>(sh, it.b, &it.r);
+  it.n = query_tiles(it.l, it.k0, kBM, bn, &it.qt_begin);  // query tiles that see any of these keys
   it.total = it.n * sh.G;
   return it;
 }
@@ -511,7 +538,7 @@ __device__ __forceinline__ KItem k_item(const AttnShape& sh, int w, int bn) {
 // MMAs of the previous item are done (bar_res_empty), so the reload overlaps the
 // previous item's last tile and epilogue, and the operand MMAs of an item start
 // only once the previous item's accumulators were read out (bar_acc_empty).
-template <int HD>
+template <int HD, bool VL>
 __global__ void __launch_bounds__(kBBThreads, 1)
     bwdbwd_k_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                     const __grid_constant__ CUtensorMap tm_ddk, const __grid_constant__ CUtensorMap tm_ddv,
@@ -581,7 +608,7 @@ __global__ void __launch_bounds__(kBBThreads, 1)
 #pragma unroll
       for (int k = 0; k < RPL; ++k) {
         const int q = q0 + lane + 32 * k;
-        const size_t idx = stat_index(w.b, h, q < sh.Tq ? q : 0, sh.H, sh.Tq);
+        const size_t idx = q_stat(w.l, w.r, q < w.l.Tq ? q : 0, h);
         raw[k][0] = a.lse[idx];
         raw[k][1] = a.delta[idx];
         raw[k][2] = a.dd[idx];
@@ -593,7 +620,7 @@ __global__ void __launch_bounds__(kBBThreads, 1)
     for (int j = 0; ok; ++j) {
       const int wi = snake_item(j, c, P);
       if (wi >= n_items) break;
-      const KItem w = k_item(sh, wi, BN);
+      const KItem w = k_item<VL>(sh, wi, BN);
       if (w.total == 0) continue;
       // The previous item's score MMAs no longer read the resident tiles.
       if (ai > 0 && !mbar_wait_warp(&bar_res_empty, (ai - 1) & 1, &abort_flag)) {
@@ -602,10 +629,10 @@ __global__ void __launch_bounds__(kBBThreads, 1)
       }
       if (lane == 0) {
         mbar_arrive_expect_tx(&bar_res, 4 * G::RES);
-        tma_rows<HD>(s_k, &tm_k, &bar_res, w.k0, kBM, w.hk, w.b);
-        tma_rows<HD>(s_v, &tm_v, &bar_res, w.k0, kBM, w.hk, w.b);
-        tma_rows<HD>(s_ddk, &tm_ddk, &bar_res, w.k0, kBM, w.hk, w.b);
-        tma_rows<HD>(s_ddv, &tm_ddv, &bar_res, w.k0, kBM, w.hk, w.b);
+        tma_rows<HD>(s_k, &tm_k, &bar_res, w.r.k0 + w.k0, kBM, w.hk, w.r.bc);
+        tma_rows<HD>(s_v, &tm_v, &bar_res, w.r.k0 + w.k0, kBM, w.hk, w.r.bc);
+        tma_rows<HD>(s_ddk, &tm_ddk, &bar_res, w.r.k0 + w.k0, kBM, w.hk, w.r.bc);
+        tma_rows<HD>(s_ddv, &tm_ddv, &bar_res, w.r.k0 + w.k0, kBM, w.hk, w.r.bc);
       }
       ++ai;
       float raw_next[RPL][4];
@@ -625,8 +652,8 @@ __global__ void __launch_bounds__(kBBThreads, 1)
         // together with the copies.
         if (lane == 0) {
           mbar_expect_tx(&bar_full[s], G::PAIR + G::STR);
-          tma_pair<HD>(slot, &tm_q, &tm_ddq, &bar_full[s], q0, BN, h, w.b);
-          tma_rows<HD>(slot + G::PAIR, &tm_do, &bar_full[s], q0, BN, h, w.b);
+          tma_pair<HD>(slot, &tm_q, &tm_ddq, &bar_full[s], w.r.q0 + q0, BN, h, w.r.bc);
+          tma_rows<HD>(slot + G::PAIR, &tm_do, &bar_full[s], w.r.q0 + q0, BN, h, w.r.bc);
         }
         float raw[RPL][4];  // first use of this tile's statistics: after its copies are issued
 #pragma unroll
@@ -636,7 +663,7 @@ __global__ void __launch_bounds__(kBBThreads, 1)
         const uint32_t bias = smem_u32(slot + G::PAIR + G::STR);
 #pragma unroll
         for (int k = 0; k < RPL; ++k) {
-          const bool v = q0 + lane + 32 * k < sh.Tq;
+          const bool v = q0 + lane + 32 * k < w.l.Tq;
           const float lse = raw[k][0], dl = raw[k][1], ddl = raw[k][2];
           const int r = lane + 32 * k;
           // L = -inf: the query sees no key and all its elements are masked.
@@ -677,7 +704,7 @@ __global__ void __launch_bounds__(kBBThreads, 1)
     for (int j = 0; ok; ++j) {
       const int wi = snake_item(j, c, P);
       if (wi >= n_items) break;
-      const KItem w = k_item(sh, wi, BN);
+      const KItem w = k_item<VL>(sh, wi, BN);
       if (w.total == 0) continue;
       if (!mbar_wait_warp(&bar_res, ai & 1, &abort_flag)) {
         if (lane == 0) raise_error(a.status, &abort_flag, kDevTimeoutTmaFull);
@@ -723,7 +750,7 @@ __global__ void __launch_bounds__(kBBThreads, 1)
     for (int j = 0; ok; ++j) {
       const int wi = snake_item(j, c, P);
       if (wi >= n_items) break;
-      const KItem w = k_item(sh, wi, BN);
+      const KItem w = k_item<VL>(sh, wi, BN);
       if (w.total == 0) continue;
       for (int it = 0; it < w.total; ++it, ++gt) {
         if (!mbar_wait_warp(&bar_ops_full, gt & 1, &abort_flag)) {
@@ -764,12 +791,12 @@ __global__ void __launch_bounds__(kBBThreads, 1)
     for (int j = 0; ok; ++j) {
       const int wi = snake_item(j, c, P);
       if (wi >= n_items) break;
-      const KItem w = k_item(sh, wi, BN);
+      const KItem w = k_item<VL>(sh, wi, BN);
       const int key = w.k0 + r;
-      const bool key_ok = key < sh.Tk;
-      const int qhi = query_hi(sh, key), qlo = query_lo(sh, key);  // queries that see this key
+      const bool key_ok = key < w.l.Tk;
+      const int qhi = query_hi(w.l, key), qlo = query_lo(w.l, key);  // queries that see this key
       const int skey = key_ok ? key : 0;
-      __nv_bfloat16* dst = (wg == 0 ? a.dk2 : a.dv2) + row_offset(sh.sk, w.b, skey, w.hk);
+      __nv_bfloat16* dst = (wg == 0 ? a.dk2 : a.dv2) + k_row(w.l, w.r, skey, w.hk);
       if (w.total == 0) {
         // No query sees these keys (causal with Tk > Tq): the gradients are zero.
         if (key_ok) zero_row_global<HD>(dst);
@@ -824,31 +851,31 @@ __global__ void __launch_bounds__(kBBThreads, 1)
   if (warp == kBBWarpMma) tmem_dealloc(tmem, G::TMEM_COLS);
 }
 
-template <int HD>
+template <int HD, bool VL>
 int launch_bwdbwd_hd(const AttnShape& s, const BwdBwdPtrs& p, int passes, int* status, cudaStream_t stream) {
   using GQ = QPass<HD>;
   using GK = KPass<HD>;
   CUtensorMap mq[8], mk[7];
   // Query-tiled pass: 128-row query tiles, 64-row key tiles.
-  bool ok = make_seq_map(&mq[0], p.q, HD, s.Tq, s.H, s.B, s.sq, kBM) &&
-            make_seq_map(&mq[1], p.dO, HD, s.Tq, s.H, s.B, s.sq, kBM) &&
-            make_seq_map(&mq[2], p.ddq, HD, s.Tq, s.H, s.B, s.sq, kBM) &&
-            make_seq_map(&mq[3], p.k, HD, s.Tk, s.Hk, s.B, s.sk, GQ::BN) &&
-            make_seq_map(&mq[4], p.v, HD, s.Tk, s.Hk, s.B, s.sk, GQ::BN) &&
-            make_seq_map(&mq[5], p.ddk, HD, s.Tk, s.Hk, s.B, s.sk, GQ::BN) &&
-            make_seq_map(&mq[6], p.ddv, HD, s.Tk, s.Hk, s.B, s.sk, GQ::BN) &&
-            make_seq_map(&mq[7], p.o ? p.o : p.q, HD, s.Tq, s.H, s.B, s.sq, kBM);  // O: only read when D is fused
+  bool ok = make_seq_map(&mq[0], p.q, HD, s.total_q, s.H, map_batch(s), s.sq, kBM) &&
+            make_seq_map(&mq[1], p.dO, HD, s.total_q, s.H, map_batch(s), s.sq, kBM) &&
+            make_seq_map(&mq[2], p.ddq, HD, s.total_q, s.H, map_batch(s), s.sq, kBM) &&
+            make_seq_map(&mq[3], p.k, HD, s.total_k, s.Hk, map_batch(s), s.sk, GQ::BN) &&
+            make_seq_map(&mq[4], p.v, HD, s.total_k, s.Hk, map_batch(s), s.sk, GQ::BN) &&
+            make_seq_map(&mq[5], p.ddk, HD, s.total_k, s.Hk, map_batch(s), s.sk, GQ::BN) &&
+            make_seq_map(&mq[6], p.ddv, HD, s.total_k, s.Hk, map_batch(s), s.sk, GQ::BN) &&
+            make_seq_map(&mq[7], p.o ? p.o : p.q, HD, s.total_q, s.H, map_batch(s), s.sq, kBM);  // O: only read when D is fused
   // Key-tiled pass: 128-row key tiles, 64-row query tiles.
-  ok = ok && make_seq_map(&mk[0], p.k, HD, s.Tk, s.Hk, s.B, s.sk, kBM) &&
-       make_seq_map(&mk[1], p.v, HD, s.Tk, s.Hk, s.B, s.sk, kBM) &&
-       make_seq_map(&mk[2], p.ddk, HD, s.Tk, s.Hk, s.B, s.sk, kBM) &&
-       make_seq_map(&mk[3], p.ddv, HD, s.Tk, s.Hk, s.B, s.sk, kBM) &&
-       make_seq_map(&mk[4], p.q, HD, s.Tq, s.H, s.B, s.sq, GK::BN) &&
-       make_seq_map(&mk[5], p.dO, HD, s.Tq, s.H, s.B, s.sq, GK::BN) &&
-       make_seq_map(&mk[6], p.ddq, HD, s.Tq, s.H, s.B, s.sq, GK::BN);
+  ok = ok && make_seq_map(&mk[0], p.k, HD, s.total_k, s.Hk, map_batch(s), s.sk, kBM) &&
+       make_seq_map(&mk[1], p.v, HD, s.total_k, s.Hk, map_batch(s), s.sk, kBM) &&
+       make_seq_map(&mk[2], p.ddk, HD, s.total_k, s.Hk, map_batch(s), s.sk, kBM) &&
+       make_seq_map(&mk[3], p.ddv, HD, s.total_k, s.Hk, map_batch(s), s.sk, kBM) &&
+       make_seq_map(&mk[4], p.q, HD, s.total_q, s.H, map_batch(s), s.sq, GK::BN) &&
+       make_seq_map(&mk[5], p.dO, HD, s.total_q, s.H, map_batch(s), s.sq, GK::BN) &&
+       make_seq_map(&mk[6], p.ddq, HD, s.total_q, s.H, map_batch(s), s.sq, GK::BN);
   if (!ok) return kInvalidArgument;
-  if (ensure_smem_limit(reinterpret_cast<const void*>(&bwdbwd_q_kernel<HD>), GQ::SMEM) != kOk ||
-      ensure_smem_limit(reinterpret_cast<const void*>(&bwdbwd_k_kernel<HD>), GK::SMEM) != kOk)
+  if (ensure_smem_limit(reinterpret_cast<const void*>(&bwdbwd_q_kernel<HD, VL>), GQ::SMEM) != kOk ||
+      ensure_smem_limit(reinterpret_cast<const void*>(&bwdbwd_k_kernel<HD, VL>), GK::SMEM) != kOk)
     return kLaunchFailed;
   // With `o`, the query pass computes D into delta_out and the key pass reads it there.
   BBArgs args{s,
@@ -864,7 +891,7 @@ int launch_bwdbwd_hd(const AttnShape& s, const BwdBwdPtrs& p, int passes, int* s
               status};
   if (passes & kPassQuery) {
     const dim3 gq(s.H, s.B, (s.Tq + kBM - 1) / kBM);
-    bwdbwd_q_kernel<HD><<<gq, kBBThreads, GQ::SMEM, stream>>>(mq[0], mq[1], mq[2], mq[3], mq[4], mq[5], mq[6],
+    bwdbwd_q_kernel<HD, VL><<<gq, kBBThreads, GQ::SMEM, stream>>>(mq[0], mq[1], mq[2], mq[3], mq[4], mq[5], mq[6],
                                                               mq[7], args);
     if (after_launch() != kOk) return kLaunchFailed;
   }
@@ -872,7 +899,7 @@ int launch_bwdbwd_hd(const AttnShape& s, const BwdBwdPtrs& p, int passes, int* s
     // Persistent: one CTA per SM (at most one per work item).
     const int items = s.Hk * s.B * ((s.Tk + kBM - 1) / kBM);
     const dim3 gk(static_cast<unsigned>(items < sm_count() ? items : sm_count()));
-    bwdbwd_k_kernel<HD><<<gk, kBBThreads, GK::SMEM, stream>>>(mk[0], mk[1], mk[2], mk[3], mk[4], mk[5], mk[6], args);
+    bwdbwd_k_kernel<HD, VL><<<gk, kBBThreads, GK::SMEM, stream>>>(mk[0], mk[1], mk[2], mk[3], mk[4], mk[5], mk[6], args);
     if (after_launch() != kOk) return kLaunchFailed;
   }
   return kOk;
@@ -881,8 +908,8 @@ int launch_bwdbwd_hd(const AttnShape& s, const BwdBwdPtrs& p, int passes, int* s
 }  // namespace
 
 int launch_bwdbwd(const AttnShape& s, int hd, const BwdBwdPtrs& p, int passes, int* status, cudaStream_t stream) {
-  if (hd == 64) return launch_bwdbwd_hd<64>(s, p, passes, status, stream);
-  if (hd == 128) return launch_bwdbwd_hd<128>(s, p, passes, status, stream);
+  if (hd == 64) return s.cu_q ? launch_bwdbwd_hd<64, true>(s, p, passes, status, stream) : launch_bwdbwd_hd<64, false>(s, p, passes, status, stream);
+  if (hd == 128) return s.cu_q ? launch_bwdbwd_hd<128, true>(s, p, passes, status, stream) : launch_bwdbwd_hd<128, false>(s, p, passes, status, stream);
   return kUnsupported;
 }
 

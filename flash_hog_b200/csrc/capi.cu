@@ -43,9 +43,14 @@ int current_device() {
 // calling thread. Callers such as autograd worker threads may have a current
 // device in their own CUDA runtime without a driver context bound to the
 // thread; TMA descriptor encoding needs one (else CUDA_ERROR_INVALID_CONTEXT).
+// A stream that is being captured into a CUDA graph is not queried (a query can
+// invalidate the capture); it belongs to the current device, as during capture
+// the capturing thread has that device current.
 int select_stream_device(cudaStream_t stream) {
   int dev = current_device();
-  if (stream != nullptr) {
+  cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
+  if (stream != nullptr && cudaStreamIsCapturing(stream, &capture) == cudaSuccess &&
+      capture == cudaStreamCaptureStatusNone) {
     int sdev = -1;
     if (cudaStreamGetDevice(stream, &sdev) == cudaSuccess) {
       dev = sdev;
@@ -97,9 +102,18 @@ bool strides_ok(const fh_strides& s) {
   return s.batch >= 0 && s.seq > 0 && s.head >= 0 && s.batch % 8 == 0 && s.seq % 8 == 0 && s.head % 8 == 0;
 }
 
-int validate(const fh_attn_dims* d, AttnShape* out, float scale, int causal) {
+int validate(const fh_attn_dims* d, AttnShape* out, float scale, int causal, bool allow_varlen = true) {
   g_last_error[0] = 0;
   if (!d) return fail(kInvalidArgument, "dims is NULL");
+  const bool varlen = d->cu_seqlens_q != nullptr || d->cu_seqlens_k != nullptr;
+  if (varlen && !allow_varlen) return fail(kUnsupported, "packed variable-length batches need the bf16 entry points");
+  if (varlen && (!d->cu_seqlens_q || !d->cu_seqlens_k))
+    return fail(kInvalidArgument, "a packed batch needs both cu_seqlens_q and cu_seqlens_k");
+  if (varlen && ((reinterpret_cast<uintptr_t>(d->cu_seqlens_q) | reinterpret_cast<uintptr_t>(d->cu_seqlens_k)) & 3u))
+    return fail(kInvalidArgument, "cu_seqlens arrays must be 4-byte aligned");
+  if (varlen && (d->max_seqlen_q < 1 || d->max_seqlen_k < 1 || d->max_seqlen_q > d->seq_q ||
+                 d->max_seqlen_k > d->seq_k))
+    return fail(kInvalidArgument, "max_seqlen_q/k must be in [1, seq_q/k] (seq_q/k: packed rows)");
   if (d->batch < 1 || d->heads < 1 || d->seq_q < 1 || d->seq_k < 1)
     return fail(kInvalidArgument, "batch, heads, seq_q and seq_k must be >= 1");
   if (d->head_dim != 64 && d->head_dim != 128) return fail(kUnsupported, "head_dim must be 64 or 128");
@@ -114,16 +128,30 @@ int validate(const fh_attn_dims* d, AttnShape* out, float scale, int causal) {
   out->G = d->heads / kv;
   out->Tq = d->seq_q;
   out->Tk = d->seq_k;
-  out->sq = Strides3{d->q.batch, d->q.seq, d->q.head};
-  out->sk = Strides3{d->k.batch, d->k.seq, d->k.head};
+  out->sq = Strides3{varlen ? 0 : d->q.batch, d->q.seq, d->q.head};
+  out->sk = Strides3{varlen ? 0 : d->k.batch, d->k.seq, d->k.head};
   if (causal < 0 || causal > 2)
     return fail(kInvalidArgument, "causal must be 0 (no mask), 1 (top-left) or 2 (bottom-right)");
   if (d->window < 0) return fail(kInvalidArgument, "window must be >= 0");
   if (d->window > 0 && !causal) return fail(kInvalidArgument, "a sliding window needs a causal mask");
   out->scale = scale;
   out->causal = causal ? 1 : 0;
-  out->diag = causal == 2 ? d->seq_k - d->seq_q : 0;
+  out->br = causal == 2 ? 1 : 0;
   out->window = d->window;
+  out->total_q = d->seq_q;
+  out->total_k = d->seq_k;
+  if (varlen) {
+    // Sequences are row ranges of one batch entry; each kernel derives its
+    // sequence's lengths and diagonal (seq_shape). Tq/Tk size the grids.
+    out->cu_q = d->cu_seqlens_q;
+    out->cu_k = d->cu_seqlens_k;
+    out->Tq = d->max_seqlen_q;
+    out->Tk = d->max_seqlen_k;
+    out->diag = 0;
+  } else {
+    out->cu_q = out->cu_k = nullptr;
+    out->diag = causal == 2 ? d->seq_k - d->seq_q : 0;
+  }
   return kOk;
 }
 
@@ -335,7 +363,7 @@ int fh_attn_fwd_f32(void* stream, const fh_attn_dims* dims, const float* q, cons
                     float* o, float* lse, float scale, int causal) {
   if (injected("fh_attn_fwd_f32")) return FH_ERR_INJECTED;
   AttnShape s;
-  int rc = validate(dims, &s, scale, causal);
+  int rc = validate(dims, &s, scale, causal, false);
   if (rc != kOk) return rc;
   if (!all_aligned(q, k, v, o) || !lse) return fail(FH_ERR_INVALID_ARGUMENT, kAlignMsg);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -348,7 +376,7 @@ int fh_attn_bwd_f32(void* stream, const fh_attn_dims* dims, const float* q, cons
                     float scale, int causal) {
   if (injected("fh_attn_bwd_f32")) return FH_ERR_INJECTED;
   AttnShape s;
-  int rc = validate(dims, &s, scale, causal);
+  int rc = validate(dims, &s, scale, causal, false);
   if (rc != kOk) return rc;
   if (!all_aligned(q, k, v, o, dO, dq, dk, dv) || !lse || !delta) return fail(FH_ERR_INVALID_ARGUMENT, kAlignMsg);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -362,7 +390,7 @@ int fh_attn_bwdbwd_f32(void* stream, const fh_attn_dims* dims, const float* q, c
                        float* bvec, float scale, int causal, int passes) {
   if (injected("fh_attn_bwdbwd_f32")) return FH_ERR_INJECTED;
   AttnShape s;
-  int rc = validate(dims, &s, scale, causal);
+  int rc = validate(dims, &s, scale, causal, false);
   if (rc != kOk) return rc;
   if (passes < 1 || passes > 3) return fail(FH_ERR_INVALID_ARGUMENT, "pass must be 1, 2 or 3");
   if (!all_aligned(q, k, v, dO, ddq, ddk, ddv) || !lse || !delta || !dd || !bvec)
@@ -383,7 +411,7 @@ int fh_attn_jvp_bwd_f32(void* stream, const fh_attn_dims* dims, const float* q, 
                         float* delta, float* dd, float* bvec, float scale, int causal) {
   if (injected("fh_attn_jvp_bwd_f32")) return FH_ERR_INJECTED;
   AttnShape s;
-  int rc = validate(dims, &s, scale, causal);
+  int rc = validate(dims, &s, scale, causal, false);
   if (rc != kOk) return rc;
   if (!all_aligned(q, k, v, o, dO, tq, tk, tv, tdq, tdk, tdv, to) || !lse || !delta || !dd || !bvec)
     return fail(FH_ERR_INVALID_ARGUMENT, kAlignMsg);
@@ -479,7 +507,7 @@ extern "C" int fh_attn_bwdbwd_noalloc(void* stream, const fh_attn_dims* dims, co
   AttnShape s;
   int rc = validate(dims, &s, scale, causal);
   if (rc != kOk) return rc;
-  const long long rows = static_cast<long long>(s.B) * s.H * s.Tq;
+  const long long rows = static_cast<long long>(s.cu_q ? 1 : s.B) * s.H * s.total_q;
   if (rows > kNoAllocMaxRows) {
     char msg[240];
     std::snprintf(msg, sizeof(msg),

@@ -83,7 +83,7 @@ __device__ __forceinline__ void fwd_warp_arrive(uint64_t* bar) {
   if ((threadIdx.x & 31) == 0) mbar_arrive(bar);
 }
 
-template <int HD>
+template <int HD, bool VL>
 __global__ void __launch_bounds__(FPass<HD>::THREADS, FPass<HD>::CTAS)
     fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                const __grid_constant__ CUtensorMap tm_v, const FwdArgs a) {
@@ -101,9 +101,10 @@ __global__ void __launch_bounds__(FPass<HD>::THREADS, FPass<HD>::CTAS)
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
 
-  const AttnShape& sh = a.sh;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int h = blockIdx.x, b = blockIdx.y;
+  SeqRange sr;
+  const AttnShape sh = seq_shape<VL>(a.sh, b, &sr);  // this sequence's lengths and mask; sr: where its rows start
   const int qt = gridDim.z - 1 - blockIdx.z;  // longest causal rows first
   const int q0 = qt * G::ROWS;
   // Key tiles of each query tile: nt[t] tiles from key tile jt[t] (0 when the
@@ -149,7 +150,7 @@ __global__ void __launch_bounds__(FPass<HD>::THREADS, FPass<HD>::CTAS)
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
       mbar_arrive_expect_tx(&bar_q, T * G::RES);
-      for (int t = 0; t < T; ++t) tma_rows<HD>(s_q + t * G::RES, &tm_q, &bar_q, q0 + t * kBM, kBM, h, b);
+      for (int t = 0; t < T; ++t) tma_rows<HD>(s_q + t * G::RES, &tm_q, &bar_q, sr.q0 + q0 + t * kBM, kBM, h, sr.bc);
       int issued = 0;
       for (int j = 0; j < n; ++j) {
         const int s = j % ST;
@@ -159,8 +160,8 @@ __global__ void __launch_bounds__(FPass<HD>::THREADS, FPass<HD>::CTAS)
         }
         uint8_t* slot = s_ring + s * G::SLOT;
         mbar_arrive_expect_tx(&bar_full[s], G::SLOT);
-        tma_rows<HD>(slot, &tm_k, &bar_full[s], (jlo + j) * BN, BN, h / sh.G, b);
-        tma_rows<HD>(slot + G::STR, &tm_v, &bar_full[s], (jlo + j) * BN, BN, h / sh.G, b);
+        tma_rows<HD>(slot, &tm_k, &bar_full[s], sr.k0 + (jlo + j) * BN, BN, h / sh.G, sr.bc);
+        tma_rows<HD>(slot + G::STR, &tm_v, &bar_full[s], sr.k0 + (jlo + j) * BN, BN, h / sh.G, sr.bc);
         issued = j + 1;
       }
       // Every issued copy must land before this CTA's shared memory is released.
@@ -342,7 +343,7 @@ __global__ void __launch_bounds__(FPass<HD>::THREADS, FPass<HD>::CTAS)
     if (ok && nj > 0) {
       tc_fence_after();
       const float inv = (l > 0.f) ? 1.f / l : 0.f;
-      __nv_bfloat16* dst = a.o + row_offset(sh.sq, b, row_ok ? row : 0, h);
+      __nv_bfloat16* dst = a.o + q_row(sh, sr, row_ok ? row : 0, h);
 #pragma unroll
       for (int c = 0; c < HD; c += 16) {
         uint32_t o[16];
@@ -353,11 +354,11 @@ __global__ void __launch_bounds__(FPass<HD>::THREADS, FPass<HD>::CTAS)
         for (int i = 0; i < 16; ++i) x[i] = __uint_as_float(o[i]) * inv;
         if (row_ok) store_bf16x16(dst + c, x);
       }
-      if (row_ok) a.lse[stat_index(b, h, row, sh.H, sh.Tq)] = (m_used + log2f(l)) * kLn2;
+      if (row_ok) a.lse[q_stat(sh, sr, row, h)] = (m_used + log2f(l)) * kLn2;
     } else if (ok && row_ok) {
       // No key tile for these rows: O = 0 and L = -inf (no visible key).
-      zero_row_global<HD>(a.o + row_offset(sh.sq, b, row, h));
-      a.lse[stat_index(b, h, row, sh.H, sh.Tq)] = -INFINITY;
+      zero_row_global<HD>(a.o + q_row(sh, sr, row, h));
+      a.lse[q_stat(sh, sr, row, h)] = -INFINITY;
     } else if (!ok && (threadIdx.x & 127) == 0) {
       raise_error(a.status, &abort_flag, kDevTimeoutMma);
     }
@@ -368,26 +369,26 @@ __global__ void __launch_bounds__(FPass<HD>::THREADS, FPass<HD>::CTAS)
   if (warp == kFwdWarpMma) tmem_dealloc(tmem, G::TMEM_COLS);
 }
 
-template <int HD>
+template <int HD, bool VL>
 int launch_fwd_hd(const AttnShape& s, const FwdPtrs& p, int* status, cudaStream_t stream) {
   using G = FPass<HD>;
   CUtensorMap mq, mk, mv;
-  if (!make_seq_map(&mq, p.q, HD, s.Tq, s.H, s.B, s.sq, kBM) ||
-      !make_seq_map(&mk, p.k, HD, s.Tk, s.Hk, s.B, s.sk, G::BN) ||
-      !make_seq_map(&mv, p.v, HD, s.Tk, s.Hk, s.B, s.sk, G::BN))
+  if (!make_seq_map(&mq, p.q, HD, s.total_q, s.H, map_batch(s), s.sq, kBM) ||
+      !make_seq_map(&mk, p.k, HD, s.total_k, s.Hk, map_batch(s), s.sk, G::BN) ||
+      !make_seq_map(&mv, p.v, HD, s.total_k, s.Hk, map_batch(s), s.sk, G::BN))
     return kInvalidArgument;
-  if (ensure_smem_limit(reinterpret_cast<const void*>(&fwd_kernel<HD>), G::SMEM) != kOk) return kLaunchFailed;
+  if (ensure_smem_limit(reinterpret_cast<const void*>(&fwd_kernel<HD, VL>), G::SMEM) != kOk) return kLaunchFailed;
   FwdArgs args{s, static_cast<__nv_bfloat16*>(p.o), p.lse, status};
   const dim3 grid(s.H, s.B, (s.Tq + G::ROWS - 1) / G::ROWS);
-  fwd_kernel<HD><<<grid, G::THREADS, G::SMEM, stream>>>(mq, mk, mv, args);
+  fwd_kernel<HD, VL><<<grid, G::THREADS, G::SMEM, stream>>>(mq, mk, mv, args);
   return after_launch();
 }
 
 }  // namespace
 
 int launch_fwd(const AttnShape& s, int hd, const FwdPtrs& p, int* status, cudaStream_t stream) {
-  if (hd == 64) return launch_fwd_hd<64>(s, p, status, stream);
-  if (hd == 128) return launch_fwd_hd<128>(s, p, status, stream);
+  if (hd == 64) return s.cu_q ? launch_fwd_hd<64, true>(s, p, status, stream) : launch_fwd_hd<64, false>(s, p, status, stream);
+  if (hd == 128) return s.cu_q ? launch_fwd_hd<128, true>(s, p, status, stream) : launch_fwd_hd<128, false>(s, p, status, stream);
   return kUnsupported;
 }
 

@@ -94,6 +94,10 @@ int sm_count();
 // Sets the dynamic shared memory limit of `func` on the current device once.
 int ensure_smem_limit(const void* func, int bytes);
 
+// Batch extent of the tensors' TMA maps: the batch for dense inputs, 1 for packed
+// variable-length ones (whose sequences are row ranges of one batch entry).
+inline int map_batch(const AttnShape& s) { return s.cu_q ? 1 : s.B; }
+
 // 4-D (head_dim, seq, head, batch) bf16 map with a {64, rows, 1, 1} box.
 bool make_seq_map(CUtensorMap* map, const void* base, int hd, int seq, int heads, int batch, const Strides3& st,
                   int rows);

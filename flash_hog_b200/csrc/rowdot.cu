@@ -57,7 +57,13 @@ int launch_rowdot_hd(const AttnShape& s, const void* o, const void* dO, float* d
 
 }  // namespace
 
-int launch_rowdot(const AttnShape& s, int hd, const void* o, const void* dO, float* delta, cudaStream_t stream) {
+int launch_rowdot(const AttnShape& shape, int hd, const void* o, const void* dO, float* delta, cudaStream_t stream) {
+  // D is per query row: a packed variable-length batch is one batch entry of total_q rows.
+  AttnShape s = shape;
+  if (s.cu_q) {
+    s.B = 1;
+    s.Tq = s.total_q;
+  }
   if (hd == 64) return launch_rowdot_hd<64>(s, o, dO, delta, stream);
   if (hd == 128) return launch_rowdot_hd<128>(s, o, dO, delta, stream);
   return kUnsupported;

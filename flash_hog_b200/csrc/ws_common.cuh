@@ -48,6 +48,9 @@ __device__ __forceinline__ void tmem_share(uint32_t tmem, int warp, int col, uin
     tmem_ld16(tmem + tmem_lane_base(warp & 3) + col + c, *reinterpret_cast<uint32_t(*)[16]>(&r[c]));
 }
 
+// Two raw fp32 register values as an fp32x2 operand of the packed instructions.
+__device__ __forceinline__ float2 f2(uint32_t a, uint32_t b) { return make_float2(__uint_as_float(a), __uint_as_float(b)); }
+
 template <int N>
 __device__ __forceinline__ void reg_fence(uint32_t (&r)[N]) {
 #pragma unroll

@@ -47,6 +47,7 @@ namespace {
 // fh_attn_dims of a query-side and a key-side buffer (rank 4, contiguous).
 bool make_dims(const ffi::AnyBuffer& q, const ffi::AnyBuffer& k, bool bhtd, int32_t window, fh_attn_dims* d,
                std::string* why) {
+  *d = fh_attn_dims{};  // dense batch: no cu_seqlens
   auto qd = q.dimensions();
   auto kd = k.dimensions();
   if (qd.size() != 4 || kd.size() != 4) {

@@ -88,6 +88,28 @@ typedef struct fh_attn_dims {
    * i + seq_k - seq_q (causal = 2) -- get_mask_bottom_right's
    * (qi >= kj) & (qi - kj < sliding_window_length), flash_hog/_jax_refs/jax_impl.py:104-109. */
   int32_t window;
+  /* Packed variable-length batches (bf16 entry points; NULL = a dense batch).
+   * With cu_seqlens_q and cu_seqlens_k set (device arrays of batch + 1
+   * non-decreasing int32 offsets, first 0), sequence b is query rows
+   * [cu_seqlens_q[b], cu_seqlens_q[b+1]) and key rows [cu_seqlens_k[b],
+   * cu_seqlens_k[b+1]) of packed tensors with one batch entry:
+   *  - seq_q / seq_k are the packed row counts (total tokens) and the strides'
+   *    batch members are ignored;
+   *  - max_seqlen_q / max_seqlen_k bound every sequence's lengths (they size
+   *    the grids; rows of a longer sequence past them are not written);
+   *  - per-query vectors (lse, delta, dd, bvec) are (heads, seq_q), i.e. (1,
+   *    heads, total rows);
+   *  - each sequence is masked on its own: causal = 2 aligns each sequence's
+   *    diagonal bottom-right (query i sees keys j <= i + Tk_b - Tq_b), the
+   *    window applies per sequence, and a sequence with no keys gets o = 0,
+   *    lse = -inf and zero gradients.
+   * The reference's JAX statements give each (qs, ks) pair its own bottom-right
+   * mask (flash_hog/_jax_refs/jax_impl.py:104-130); this packs such pairs into
+   * one call. The fp32 entry points reject packed batches. */
+  const int32_t* cu_seqlens_q;
+  const int32_t* cu_seqlens_k;
+  int32_t max_seqlen_q;
+  int32_t max_seqlen_k;
 } fh_attn_dims;
 
 /* Forward: o = softmax(scale * q k^T + mask) v, lse = logsumexp(scale * q k^T + mask).
@@ -262,7 +284,7 @@ int fh_abi_version(void);
  * reads it before and after a timed region to report its kernel launches. */
 unsigned long long fh_launch_count(void);
 
-#define FH_ABI_VERSION 5
+#define FH_ABI_VERSION 6
 
 #ifdef __cplusplus
 }

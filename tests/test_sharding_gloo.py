@@ -113,7 +113,7 @@ def test_sharding_rule():
         BatchHeadsSharding(1, 3, 2)
 
 
-def _oracle_device(Q, K, V, O, dO, ddQ, ddK, ddV, L, causal, window, scale, policy=None):
+def _oracle_device(Q, K, V, O, dO, ddQ, ddK, ddV, L, causal, window, scale, policy=None, packed=None):
     """CPU stand-in for the kernels inside flash_bwdbwd (the oracle's explicit formulas)."""
     from oracle import attention_oracle as ora
 

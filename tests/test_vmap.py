@@ -23,7 +23,7 @@ def _np(x):
     return x.detach().double().numpy()
 
 
-def _oracle_bwdbwd_device(Q, K, V, O, dO, ddQ, ddK, ddV, L, causal, window, scale, policy=None):
+def _oracle_bwdbwd_device(Q, K, V, O, dO, ddQ, ddK, ddV, L, causal, window, scale, policy=None, packed=None):
     b, t, n, _ = Q.shape
     outs, stats = ora.bwdbwd_stats(*(_np(x) for x in (Q, K, V, O)), L.reshape(b, n, t).double().numpy(),
                                    *(_np(x) for x in (dO, ddQ, ddK, ddV)), scale=scale, causal=causal, window=window,
