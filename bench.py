@@ -307,27 +307,39 @@ def run_gpt(args):
     """The grad-norm-penalty GPT training step (12 layers, d768, 12 heads of 64, MLP
     3072, vocab 32000, sequence 1024, 4 sequences per GPU; tokens uniform in
     [0, 32000)), data-parallel over the ranks with an NCCL gradient all-reduce.
-    Metric: tokens per second of the whole job."""
+    Metric: tokens per second of the whole job.
+
+    ``value``: attention, LayerNorm and GELU on this package's kernels (first- and
+    second-order), the step's compute replayed as one CUDA graph (PenaltyStepGraph),
+    then the NCCL all-reduce and the SGD update. ``baseline_torch_autograd``: the same
+    model with torch's LayerNorm and GELU and eager launches (attention still on the
+    kernels), timed the same way on the same GPUs."""
     import datetime
     from flash_hog_b200 import _capi
-    from flash_hog_b200.gpt import GPT, GPTConfig, train_step
+    from flash_hog_b200.gpt import GPT, GPTConfig, PenaltyStepGraph, train_step
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    local_world = int(os.environ.get("LOCAL_WORLD_SIZE", str(world)))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    if world > 1:
+        pin_host_cores(local, local_world)
     dist = None
     if world > 1:
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    distributed = dist is not None
     cfg, batch, lam = GPTConfig(), 4, 1e-2
-    torch.manual_seed(0)  # the same initial weights on every rank
-    model = GPT(cfg).to(dev)
-    opt = torch.optim.SGD(model.parameters(), lr=1e-4)
     g = torch.Generator().manual_seed(1000 + rank)
     host = [torch.randint(0, cfg.vocab, (batch, cfg.seq_len + 1), generator=g).pin_memory() for _ in range(2)]
     resident = [t.to(dev) for t in host]
+
+    def make(fused):
+        torch.manual_seed(0)  # the same initial weights on every rank
+        model = GPT(cfg, fused=fused).to(dev)
+        return model, torch.optim.SGD(model.parameters(), lr=1e-4)
 
     def barrier():
         if dist is not None:
@@ -351,23 +363,34 @@ def run_gpt(args):
             ms = float(t.item())
         return ms, _capi.launch_count() - n0
 
-    def device_step(i):
-        train_step(model, resident[i % 2], lam, optimizer=opt, distributed=dist is not None)
+    # Baseline: torch LayerNorm/GELU, eager launches.
+    base_model, base_opt = make(False)
+    base_step = lambda i: train_step(base_model, resident[i % 2], lam, optimizer=base_opt, distributed=distributed)
+    for i in range(args.warmup):
+        base_step(i)
+    base_ms, _ = timed(base_step, max(3, min(args.steps, 10)))
+    del base_model, base_opt
+    torch.cuda.empty_cache()
 
+    # Ours: fused kernels, the step's compute replayed as a CUDA graph.
+    model, opt = make(True)
+    graph = PenaltyStepGraph(model, batch, lam, warmup=args.warmup)
+    device_step = lambda i: graph.step(resident[i % 2], optimizer=opt, distributed=distributed)
+    with ClockSampler(list(range(world)) if rank == 0 else []) as clocks:
+        ms, _ = timed(device_step, args.steps)
+    launches = graph.kernels_per_step * args.steps  # replays do not pass through the C ABI's counter
     loss_host = torch.empty((), dtype=torch.float32).pin_memory()
 
     def e2e_step(i):
         tokens = host[i % 2].to(dev, non_blocking=True)
-        loss, _ = train_step(model, tokens, lam, optimizer=opt, distributed=dist is not None)
+        loss, _ = graph.step(tokens, optimizer=opt, distributed=distributed)
         loss_host.copy_(loss, non_blocking=True)
 
-    for i in range(args.warmup):
-        device_step(i)
-    with ClockSampler(list(range(world)) if rank == 0 else []) as clocks:
-        ms, launches = timed(device_step, args.steps)
     e2e_ms, _ = timed(e2e_step, max(3, min(args.steps, 10)))
     if _capi.device_status() != 0:
         raise RuntimeError("device-side error in the GPT step")
+    peak = torch.cuda.max_memory_allocated(dev)
+    del graph
     if dist is not None:
         dist.destroy_process_group()
     if rank != 0:
@@ -378,10 +401,15 @@ def run_gpt(args):
         "value": tokens_step / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (tokens uniform in [0, 32000), random init)",
+        "value_per_gpu": tokens_step / world / (ms * 1e-3),
         "config": {"workload": "gpt grad-norm penalty L + 0.01 ||dL/dtheta||^2, SGD update", "name": "gpt",
                    "layers": cfg.n_layer, "d_model": cfg.d_model, "heads": cfg.n_head, "seq_len": cfg.seq_len,
                    "global_batch": world * batch, "parallelism": f"dp{world} (NCCL all-reduce of gradients)",
-                   "peak_device_bytes": torch.cuda.max_memory_allocated(dev)},
+                   "step": "fused LayerNorm/GELU kernels, compute replayed as one CUDA graph, then all-reduce + SGD",
+                   "peak_device_bytes": peak},
+        "baseline_torch_autograd": {"tokens_per_s": tokens_step / (base_ms * 1e-3), "ms_per_step": base_ms,
+                                    "step": "torch LayerNorm/GELU autograd, eager launches (attention on the "
+                                            "kernels)"},
         "roofline": None, "cpu_baseline": None,
         "e2e": {"value": tokens_step / (e2e_ms * 1e-3), "unit": "tokens/s",
                 "h2d_bytes_per_step": host[0].numel() * host[0].element_size(), "d2h_bytes_per_step": 4},

@@ -44,13 +44,18 @@ EXPORTED_SYMBOLS = (
     "fh_attn_bwd_f32",
     "fh_attn_bwdbwd_f32",
     "fh_attn_jvp_bwd_f32",
+    "fh_layernorm_scratch_floats",
+    "fh_layernorm_fwd",
+    "fh_layernorm_bwd",
+    "fh_layernorm_bwd_bwd",
+    "fh_gelu",
     "fh_device_status",
     "fh_status_string",
     "fh_last_error",
     "fh_abi_version",
     "fh_launch_count",
 )
-ABI_VERSION = 6
+ABI_VERSION = 7
 
 
 class FlashHogError(RuntimeError):
@@ -109,6 +114,12 @@ def lib() -> ctypes.CDLL:
     h.fh_attn_bwd_f32.argtypes = [vp, dims] + [vp] * 10 + [f32, i32]
     h.fh_attn_bwdbwd_f32.argtypes = [vp, dims] + [vp] * 16 + [f32, i32, i32]
     h.fh_attn_jvp_bwd_f32.argtypes = [vp, dims] + [vp] * 17 + [f32, i32]
+    h.fh_layernorm_scratch_floats.argtypes = [i32, i32]
+    h.fh_layernorm_scratch_floats.restype = ctypes.c_longlong
+    h.fh_layernorm_fwd.argtypes = [vp, i32, i32, vp, vp, vp, f32, vp, vp, vp]
+    h.fh_layernorm_bwd.argtypes = [vp, i32, i32] + [vp] * 9
+    h.fh_layernorm_bwd_bwd.argtypes = [vp, i32, i32] + [vp] * 12
+    h.fh_gelu.argtypes = [vp, i32, i32, ctypes.c_longlong, vp, vp, vp, vp, vp]
     h.fh_device_status.argtypes = [vp, ctypes.POINTER(ctypes.c_int)]
     h.fh_status_string.argtypes = [i32]
     h.fh_status_string.restype = ctypes.c_char_p
@@ -120,7 +131,7 @@ def lib() -> ctypes.CDLL:
     for name in ("fh_attn_fwd", "fh_attn_rowdot", "fh_attn_bwd", "fh_attn_bwdbwd", "fh_attn_bwdbwd_pass",
                  "fh_attn_bwdbwd_o", "fh_attn_bwdbwd_noalloc", "fh_attn_jvp_bwd", "fh_attn_fwd_f32",
                  "fh_attn_bwd_f32", "fh_attn_bwdbwd_f32", "fh_attn_jvp_bwd_f32", "fh_device_status",
-                 "fh_abi_version"):
+                 "fh_abi_version", "fh_layernorm_fwd", "fh_layernorm_bwd", "fh_layernorm_bwd_bwd", "fh_gelu"):
         getattr(h, name).restype = i32
     if h.fh_abi_version() != ABI_VERSION:
         raise RuntimeError(f"flash_hog_b200 ABI mismatch: library {h.fh_abi_version()}, binding {ABI_VERSION}")
@@ -325,6 +336,60 @@ def attn_jvp_bwd_f32(q, k, v, o, dO, lse, tq, tk, tv, tdO, tdq, tdk, tdv, to, de
         _stream(q.device), ctypes.byref(dims), _ptr(q), _ptr(k), _ptr(v), _ptr(o), _ptr(dO), _ptr(lse), _ptr(tq),
         _ptr(tk), _ptr(tv), _ptr(tdO), _ptr(tdq), _ptr(tdk), _ptr(tdv), _ptr(to),
         _ptr(delta), _ptr(dd), _ptr(bvec), float(scale), int(causal)))
+
+
+def _ln_rows(x: torch.Tensor, cols: int) -> int:
+    if x.dtype != torch.float32 or not x.is_contiguous() or x.shape[-1] != cols:
+        raise ValueError("layernorm tensors are contiguous fp32 (..., cols)")
+    return x.numel() // cols
+
+
+def layernorm_scratch(rows: int, cols: int, device) -> torch.Tensor:
+    with torch.cuda.device(device):
+        n = int(lib().fh_layernorm_scratch_floats(int(rows), int(cols)))
+    if n < 0:
+        _check("fh_layernorm_scratch_floats", 2)
+    return torch.empty(n, dtype=torch.float32, device=device)
+
+
+def layernorm_fwd(x, w, b, eps: float, y, mean, rstd) -> None:
+    cols = w.numel()
+    rows = _ln_rows(x, cols)
+    _check("fh_layernorm_fwd", lib().fh_layernorm_fwd(_stream(x.device), rows, cols, _ptr(x), _ptr(w), _ptr(b),
+                                                     float(eps), _ptr(y), _ptr(mean), _ptr(rstd)))
+
+
+def layernorm_bwd(x, w, mean, rstd, dy, dx, dw, db) -> None:
+    cols = w.numel()
+    rows = _ln_rows(x, cols)
+    scratch = layernorm_scratch(rows, cols, x.device)
+    _check("fh_layernorm_bwd", lib().fh_layernorm_bwd(_stream(x.device), rows, cols, _ptr(x), _ptr(w), _ptr(mean),
+                                                     _ptr(rstd), _ptr(dy), _ptr(dx), _ptr(dw), _ptr(db),
+                                                     _ptr(scratch)))
+
+
+def layernorm_bwd_bwd(x, w, mean, rstd, dy, ddx, ddw, ddb, gx, gw, gdy) -> None:
+    """Cotangents ddx, ddw, ddb may be None (zero)."""
+    cols = w.numel()
+    rows = _ln_rows(x, cols)
+    scratch = layernorm_scratch(rows, cols, x.device)
+    _check("fh_layernorm_bwd_bwd", lib().fh_layernorm_bwd_bwd(
+        _stream(x.device), rows, cols, _ptr(x), _ptr(w), _ptr(mean), _ptr(rstd), _ptr(dy), _ptr(ddx), _ptr(ddw),
+        _ptr(ddb), _ptr(gx), _ptr(gw), _ptr(gdy), _ptr(scratch)))
+
+
+_GELU_DTYPES = {torch.float32: 0, torch.bfloat16: 1}
+
+
+def gelu(mode: int, a, dh, c, out0, out1) -> None:
+    """Exact GELU (mode 0), its backward (1) or its backward's backward (2); see fh_gelu."""
+    if a.dtype not in _GELU_DTYPES or not a.is_contiguous():
+        raise ValueError("gelu tensors are contiguous fp32 or bf16")
+    for t in (dh, c, out0, out1):
+        if t is not None and (t.dtype != a.dtype or not t.is_contiguous() or t.numel() != a.numel()):
+            raise ValueError("gelu tensors must share dtype, size and contiguity")
+    _check("fh_gelu", lib().fh_gelu(_stream(a.device), int(mode), _GELU_DTYPES[a.dtype], a.numel(), _ptr(a), _ptr(dh),
+                                   _ptr(c), _ptr(out0), _ptr(out1)))
 
 
 def launch_count() -> int:

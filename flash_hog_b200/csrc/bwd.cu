@@ -83,21 +83,21 @@ struct DqPass {
   static_assert(HD % 64 == 0 && RES_PANEL == kBM * 128, "tile shapes");
 };
 
-// Packed bf16 pairs of dS/scale = P (dP - D) for this thread's CW key columns.
+// Packed bf16 pairs of dS/scale = P (dP - D) for this thread's CW key columns
+// (column pairs through the packed fp32x2 instructions).
 template <int CW, bool MASK>
 __device__ __forceinline__ void dq_ops(const uint32_t (&vs)[CW], const uint32_t (&vdp)[CW], int kc, int klo, int khi,
                                        float sc2, float lg, float dv, uint32_t (&o_ds)[CW / 2]) {
+  const float2 m = make_float2(sc2, sc2), nl = make_float2(-lg, -lg), ndv = make_float2(-dv, -dv);
 #pragma unroll
   for (int i = 0; i < CW; i += 2) {
-    float ds[2];
-#pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      const int c = i + e;
-      float s = fmaf(__uint_as_float(vs[c]), sc2, -lg);
-      if (MASK && (kc + c > khi || kc + c < klo)) s = -INFINITY;
-      ds[e] = ex2(s) * (__uint_as_float(vdp[c]) - dv);
+    float2 s = __ffma2_rn(f2(vs[i], vs[i + 1]), m, nl);
+    if (MASK) {
+      if (kc + i > khi || kc + i < klo) s.x = -INFINITY;
+      if (kc + i + 1 > khi || kc + i + 1 < klo) s.y = -INFINITY;
     }
-    o_ds[i / 2] = pack_bf16(ds[0], ds[1]);
+    const float2 ds = __fmul2_rn(make_float2(ex2(s.x), ex2(s.y)), __fadd2_rn(f2(vdp[i], vdp[i + 1]), ndv));
+    o_ds[i / 2] = pack_bf16(ds.x, ds.y);
   }
 }
 
@@ -407,19 +407,18 @@ struct DkvPass {
 template <int CW, bool MASK>
 __device__ __forceinline__ void dkv_ops(const uint32_t (&vs)[CW], const uint32_t (&vdp)[CW], int qc, int qlo, int qhi,
                                         float sc2, uint32_t (&o_p)[CW / 2], uint32_t (&o_ds)[CW / 2]) {
+  const float2 m = make_float2(sc2, sc2);
 #pragma unroll
   for (int i = 0; i < CW; i += 2) {
-    float pp[2], ds[2];
-#pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      const int c = i + e;
-      float s = __uint_as_float(vs[c]) * sc2;
-      if (MASK && (qc + c > qhi || qc + c < qlo)) s = -INFINITY;
-      pp[e] = ex2(s);
-      ds[e] = pp[e] * __uint_as_float(vdp[c]);
+    float2 s = __fmul2_rn(f2(vs[i], vs[i + 1]), m);
+    if (MASK) {
+      if (qc + i > qhi || qc + i < qlo) s.x = -INFINITY;
+      if (qc + i + 1 > qhi || qc + i + 1 < qlo) s.y = -INFINITY;
     }
-    o_p[i / 2] = pack_bf16(pp[0], pp[1]);
-    o_ds[i / 2] = pack_bf16(ds[0], ds[1]);
+    const float2 p = make_float2(ex2(s.x), ex2(s.y));
+    const float2 ds = __fmul2_rn(p, f2(vdp[i], vdp[i + 1]));
+    o_p[i / 2] = pack_bf16(p.x, p.y);
+    o_ds[i / 2] = pack_bf16(ds.x, ds.y);
   }
 }
 

@@ -430,6 +430,74 @@ int fh_attn_jvp_bwd_f32(void* stream, const fh_attn_dims* dims, const float* q, 
   return launch_bwd_f32(s, dims->head_dim, p, st);
 }
 
+// ------------------------------------------------------------------------------------
+// LayerNorm and GELU of the grad-norm-penalty model step
+// ------------------------------------------------------------------------------------
+
+static int ln_check(int rows, int cols) {
+  g_last_error[0] = 0;
+  if (rows < 1 || cols < 4 || cols % 4 != 0 || cols > 1024)
+    return fail(FH_ERR_UNSUPPORTED, "layernorm needs rows >= 1 and cols a multiple of 4 in [4, 1024]");
+  return kOk;
+}
+
+long long fh_layernorm_scratch_floats(int rows, int cols) {
+  if (ln_check(rows, cols) != kOk) return -1;
+  return static_cast<long long>(ln_partials_rows(rows)) * 2 * cols;
+}
+
+int fh_layernorm_fwd(void* stream, int rows, int cols, const float* x, const float* w, const float* b, float eps,
+                     float* y, float* mean, float* rstd) {
+  if (injected("fh_layernorm_fwd")) return FH_ERR_INJECTED;
+  int rc = ln_check(rows, cols);
+  if (rc != kOk) return rc;
+  if (!all_aligned(x, w, b, y) || !mean || !rstd) return fail(FH_ERR_INVALID_ARGUMENT, kAlignMsg);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if ((rc = select_stream_device(st)) != kOk) return rc;
+  return launch_layernorm(0, rows, cols, x, w, b, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, eps, y, mean,
+                          rstd, nullptr, st);
+}
+
+int fh_layernorm_bwd(void* stream, int rows, int cols, const float* x, const float* w, const float* mean,
+                     const float* rstd, const float* dy, float* dx, float* dw, float* db, float* scratch) {
+  if (injected("fh_layernorm_bwd")) return FH_ERR_INJECTED;
+  int rc = ln_check(rows, cols);
+  if (rc != kOk) return rc;
+  if (!all_aligned(x, w, dy, dx, dw, db, scratch) || !mean || !rstd) return fail(FH_ERR_INVALID_ARGUMENT, kAlignMsg);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if ((rc = select_stream_device(st)) != kOk) return rc;
+  return launch_layernorm(1, rows, cols, x, w, nullptr, mean, rstd, dy, nullptr, nullptr, nullptr, 0.f, dx, dw, db,
+                          scratch, st);
+}
+
+int fh_layernorm_bwd_bwd(void* stream, int rows, int cols, const float* x, const float* w, const float* mean,
+                         const float* rstd, const float* dy, const float* ddx, const float* ddw, const float* ddb,
+                         float* gx, float* gw, float* gdy, float* scratch) {
+  if (injected("fh_layernorm_bwd_bwd")) return FH_ERR_INJECTED;
+  int rc = ln_check(rows, cols);
+  if (rc != kOk) return rc;
+  if (!all_aligned(x, w, dy, gx, gw, gdy, scratch) || !mean || !rstd) return fail(FH_ERR_INVALID_ARGUMENT, kAlignMsg);
+  if ((ddx && !aligned16(ddx)) || (ddw && !aligned16(ddw)) || (ddb && !aligned16(ddb)))
+    return fail(FH_ERR_INVALID_ARGUMENT, kAlignMsg);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if ((rc = select_stream_device(st)) != kOk) return rc;
+  return launch_layernorm(2, rows, cols, x, w, nullptr, mean, rstd, dy, ddx, ddw, ddb, 0.f, gx, gdy, gw, scratch, st);
+}
+
+int fh_gelu(void* stream, int mode, int dtype, long long n, const void* a, const void* dh, const void* c, void* out0,
+            void* out1) {
+  if (injected("fh_gelu")) return FH_ERR_INJECTED;
+  g_last_error[0] = 0;
+  if (mode < 0 || mode > 2 || (dtype != 0 && dtype != 1) || n < 0)
+    return fail(FH_ERR_INVALID_ARGUMENT, "gelu: mode 0..2, dtype 0 (fp32) or 1 (bf16), n >= 0");
+  if (!a || !out0 || (mode == 1 && !dh) || (mode == 2 && !c)) return fail(FH_ERR_INVALID_ARGUMENT, kAlignMsg);
+  if (n == 0) return FH_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int rc = select_stream_device(st);
+  if (rc != kOk) return rc;
+  return launch_gelu(mode, dtype == 1, n, a, dh, c, out0, out1, st);
+}
+
 int fh_device_status(void* stream, int* code) {
   if (!code) return FH_ERR_INVALID_ARGUMENT;
   *code = 0;

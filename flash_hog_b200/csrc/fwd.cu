@@ -314,14 +314,18 @@ __global__ void __launch_bounds__(FPass<HD>::THREADS, FPass<HD>::CTAS)
       if (!G::SEP_P && warp_rescale) rescale_o();
       const float base = (m_used == -INFINITY) ? 0.f : m_used;
       uint32_t pk[BN / 2];
-      float ps[4] = {0.f, 0.f, 0.f, 0.f};
+      // Column pairs through the packed fp32x2 instructions; the row sum in two
+      // (even, odd) pair accumulators.
+      float2 ps2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+      const float2 m2 = make_float2(sc2, sc2), nb2 = make_float2(-base, -base);
 #pragma unroll
       for (int i = 0; i < BN; i += 2) {
-        const float p0 = ex2(fmaf(__uint_as_float(v[i]), sc2, -base));
-        const float p1 = ex2(fmaf(__uint_as_float(v[i + 1]), sc2, -base));
-        ps[(i >> 1) & 3] += p0 + p1;
-        pk[i / 2] = pack_bf16(p0, p1);
+        const float2 s = __ffma2_rn(make_float2(__uint_as_float(v[i]), __uint_as_float(v[i + 1])), m2, nb2);
+        const float2 p = make_float2(ex2(s.x), ex2(s.y));
+        ps2[(i >> 1) & 1] = __fadd2_rn(ps2[(i >> 1) & 1], p);
+        pk[i / 2] = pack_bf16(p.x, p.y);
       }
+      const float ps[4] = {ps2[0].x, ps2[0].y, ps2[1].x, ps2[1].y};
       uint32_t pcol = tcol;
       if constexpr (G::SEP_P) {
         // The P buffer and O are free once the previous product is done.

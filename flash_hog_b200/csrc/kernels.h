@@ -83,6 +83,21 @@ int launch_fwd_f32(const AttnShape& s, int hd, const F32FwdPtrs& p, cudaStream_t
 int launch_bwd_f32(const AttnShape& s, int hd, const F32BwdPtrs& p, cudaStream_t stream);
 int launch_bwdbwd_f32(const AttnShape& s, int hd, const F32BwdBwdPtrs& p, int passes, cudaStream_t stream);
 
+// LayerNorm over rows of `cols` fp32 values and its backward / double backward
+// (ln_gelu.cu). op 0: forward (out0 = y, out1 = mean, out2 = rstd); op 1: backward
+// (out0 = dx, out1 = dw, out2 = db); op 2: double backward with cotangents u, vb, cb
+// of (dx, dw, db), any of them null = zero (out0 = grad x, out1 = grad dy,
+// out2 = grad w). `part` is scratch of ln_partials_rows(rows) * 2 * cols floats
+// (ops 1 and 2).
+int launch_layernorm(int op, int rows, int cols, const float* x, const float* w, const float* b, const float* mean,
+                     const float* rstd, const float* dy, const float* u, const float* vb, const float* cb, float eps,
+                     float* out0, float* out1, float* out2, float* part, cudaStream_t stream);
+int ln_partials_rows(int rows);
+// Exact GELU over n elements (fp32 or bf16): mode 0 out0 = gelu(a); mode 1 out0 =
+// dh gelu'(a); mode 2 out0 = c gelu'(a), out1 = c dh gelu''(a) (dh null = zero).
+int launch_gelu(int mode, bool bf16, long long n, const void* a, const void* dh, const void* c, void* out0, void* out1,
+                cudaStream_t stream);
+
 // Checks the kernel launch just made (cudaGetLastError) and, if it was queued,
 // counts it for fh_launch_count(). Returns kOk or kLaunchFailed.
 int after_launch();

@@ -8,8 +8,11 @@ the objective
 
 whose gradient needs the double backward of every layer. Attention's double
 backward runs on this package's kernels through ``dot_product_attention`` (two
-nested autograd Functions, the analogue of the reference's nested custom_vjp);
-LayerNorm, the MLP, the embeddings and the loss stay in torch autograd. Data
+nested autograd Functions, the analogue of the reference's nested custom_vjp).
+With ``fused=True`` (the default for the "flash" model) LayerNorm and the MLP's
+GELU run on the fused kernels of ``flash_hog_b200.fused`` -- forward, backward and
+double backward one kernel each -- and the MLP's contractions on cuBLAS (plain
+GEMMs); the embeddings and the loss stay in torch autograd. Data
 parallelism: each rank computes the full step on its own token batch and the
 parameter gradients (penalty terms included) are averaged with one NCCL
 all-reduce over a flat buffer.
@@ -28,6 +31,8 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
+from flash_hog_b200 import _capi
+from flash_hog_b200 import fused as fused_ops
 from flash_hog_b200.attention import dot_product_attention
 
 
@@ -53,13 +58,15 @@ def naive_attention(q, k, v, is_causal=True):
 
 
 class Block(nn.Module):
-    def __init__(self, cfg: GPTConfig, attention):
+    def __init__(self, cfg: GPTConfig, attention, fused: bool):
         super().__init__()
+        ln = fused_ops.LayerNorm if fused else nn.LayerNorm
         self.cfg, self.attention = cfg, attention
-        self.ln1 = nn.LayerNorm(cfg.d_model)
+        self.act = fused_ops.gelu if fused else F.gelu
+        self.ln1 = ln(cfg.d_model)
         self.qkv = nn.Linear(cfg.d_model, 3 * cfg.d_model)
         self.proj = nn.Linear(cfg.d_model, cfg.d_model)
-        self.ln2 = nn.LayerNorm(cfg.d_model)
+        self.ln2 = ln(cfg.d_model)
         self.fc1 = nn.Linear(cfg.d_model, cfg.d_mlp)
         self.fc2 = nn.Linear(cfg.d_mlp, cfg.d_model)
 
@@ -68,20 +75,22 @@ class Block(nn.Module):
         h = self.cfg.n_head
         q, k, v = self.qkv(self.ln1(x)).view(b, t, 3, h, d // h).unbind(2)
         x = x + self.proj(self.attention(q, k, v, is_causal=True).reshape(b, t, d))
-        return x + self.fc2(F.gelu(self.fc1(self.ln2(x))))
+        return x + self.fc2(self.act(self.fc1(self.ln2(x))))
 
 
 class GPT(nn.Module):
-    """Pre-LN GPT; ``attention`` is "flash" (the sm_100a op) or "naive" (torch math)."""
+    """Pre-LN GPT; ``attention`` is "flash" (the sm_100a op) or "naive" (torch math);
+    ``fused`` (default: with "flash") puts LayerNorm and GELU on the fused kernels."""
 
-    def __init__(self, cfg: GPTConfig, attention: str = "flash"):
+    def __init__(self, cfg: GPTConfig, attention: str = "flash", fused: bool | None = None):
         super().__init__()
         fn = {"flash": dot_product_attention, "naive": naive_attention}[attention]
+        fused = attention == "flash" if fused is None else fused
         self.cfg = cfg
         self.wte = nn.Embedding(cfg.vocab, cfg.d_model)
         self.wpe = nn.Embedding(cfg.seq_len, cfg.d_model)
-        self.blocks = nn.ModuleList(Block(cfg, fn) for _ in range(cfg.n_layer))
-        self.ln_f = nn.LayerNorm(cfg.d_model)
+        self.blocks = nn.ModuleList(Block(cfg, fn, fused) for _ in range(cfg.n_layer))
+        self.ln_f = (fused_ops.LayerNorm if fused else nn.LayerNorm)(cfg.d_model)
         self.apply(self._init)
         for blk in self.blocks:  # GPT-2 style scaled init of the residual projections
             for lin in (blk.proj, blk.fc2):
@@ -129,6 +138,56 @@ def allreduce_grads(model: nn.Module, group=None) -> None:
         n = p.grad.numel()
         p.grad.copy_(flat[off:off + n].view_as(p.grad))
         off += n
+
+
+class PenaltyStepGraph:
+    """The compute of one grad-norm-penalty step -- forward, ``autograd.grad`` with
+    ``create_graph``, the penalty and ``backward()`` into the parameters' ``.grad`` --
+    captured once as a CUDA graph and replayed for each new token batch.
+
+    The step launches thousands of small kernels (every layer differentiated twice),
+    so launched one by one from Python it is bound by host launch latency; replayed
+    as one graph it runs at the GPU's pace. Shapes, parameters and ``.grad`` tensors
+    stay fixed (the graph writes the gradients in place); the data-parallel gradient
+    all-reduce and the optimizer update run after the replay, outside the graph.
+    Autocast runs with its cast cache off, as graph capture requires.
+    """
+
+    def __init__(self, model: GPT, batch: int, lam: float, autocast: bool = True, warmup: int = 3):
+        dev = next(model.parameters()).device
+        self.model, self.lam, self.autocast = model, lam, autocast
+        self.tokens = torch.zeros((batch, model.cfg.seq_len + 1), dtype=torch.long, device=dev)
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):  # warm-up off the capture stream (allocator and library set-up)
+            for _ in range(warmup):
+                model.zero_grad(set_to_none=True)
+                self._compute()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        model.zero_grad(set_to_none=True)
+        self.graph = torch.cuda.CUDAGraph()
+        n0 = _capi.launch_count()
+        with torch.cuda.graph(self.graph):
+            self.loss, self.penalty = self._compute()
+        self.kernels_per_step = _capi.launch_count() - n0  # this library's kernels in one replay
+
+    def _compute(self):
+        with torch.autocast(device_type="cuda", dtype=torch.bfloat16, enabled=self.autocast, cache_enabled=False):
+            total, loss, penalty = penalty_objective(self.model, self.tokens, self.lam)
+        total.backward()
+        return loss, penalty
+
+    def step(self, tokens: torch.Tensor, optimizer=None, distributed: bool = False):
+        """Copies ``tokens`` into the graph's input, replays the step, then averages the
+        gradients over the ranks (``distributed``) and applies ``optimizer``. Returns the
+        (loss, penalty) device scalars, overwritten by the next replay."""
+        self.tokens.copy_(tokens, non_blocking=True)
+        self.graph.replay()
+        if distributed:
+            allreduce_grads(self.model)
+        if optimizer is not None:
+            optimizer.step()
+        return self.loss, self.penalty
 
 
 def train_step(model: GPT, tokens: torch.Tensor, lam: float, optimizer=None, distributed: bool = False,

@@ -262,6 +262,37 @@ int fh_attn_jvp_bwd_f32(void* stream, const fh_attn_dims* dims, const float* q, 
                         const float* tv, const float* tdO, float* tdq, float* tdk, float* tdv, float* to,
                         float* delta, float* dd, float* bvec, float scale, int causal);
 
+/* LayerNorm and GELU of the grad-norm-penalty training step (the model step of
+ * configuration 5: L + lam ||dL/dtheta||^2 differentiates every layer's backward).
+ * No counterpart in the reference, which has no model code (its hot path is the
+ * attention op alone). Each pass is one kernel over the rows (LayerNorm weight
+ * gradients add one deterministic column reduction), so a second-order step does
+ * not run the dozens of elementwise kernels a framework composes these gradients
+ * from.
+ *  - LayerNorm over the last dimension of a (rows, cols) fp32 row-major tensor,
+ *    cols a multiple of 4 in [4, 1024]; eps inside the square root.
+ *    fh_layernorm_fwd: y = (x - mean) rstd w + b; mean, rstd per row (rows floats).
+ *    fh_layernorm_bwd: dx, dw = sum_rows dy xhat, db = sum_rows dy.
+ *    fh_layernorm_bwd_bwd: the gradient of <ddx, dx> + <ddw, dw> + <ddb, db>
+ *      w.r.t. x (gx), w (gw) and dy (gdy); ddx, ddw, ddb may be NULL (zero).
+ *    `scratch`: fh_layernorm_scratch_floats(rows, cols) floats (per-block column
+ *    partials of the weight gradients), on the current device.
+ *  - fh_gelu: exact GELU x Phi(x) over n elements, dtype 0 = fp32, 1 = bf16
+ *    (fp32 arithmetic either way). mode 0: out0 = gelu(a); mode 1: out0 =
+ *    dh gelu'(a); mode 2 (the backward's backward, given the cotangent c of its
+ *    output): out0 = c gelu'(a) (w.r.t. dh), out1 = c dh gelu''(a) (w.r.t. a;
+ *    dh NULL = zero, out1 NULL = not computed). */
+long long fh_layernorm_scratch_floats(int rows, int cols);
+int fh_layernorm_fwd(void* stream, int rows, int cols, const float* x, const float* w, const float* b, float eps,
+                     float* y, float* mean, float* rstd);
+int fh_layernorm_bwd(void* stream, int rows, int cols, const float* x, const float* w, const float* mean,
+                     const float* rstd, const float* dy, float* dx, float* dw, float* db, float* scratch);
+int fh_layernorm_bwd_bwd(void* stream, int rows, int cols, const float* x, const float* w, const float* mean,
+                         const float* rstd, const float* dy, const float* ddx, const float* ddw, const float* ddb,
+                         float* gx, float* gw, float* gdy, float* scratch);
+int fh_gelu(void* stream, int mode, int dtype, long long n, const void* a, const void* dh, const void* c, void* out0,
+            void* out1);
+
 /* Synchronises `stream`, then reads and clears the status word the kernels of
  * the current device record device-side failures in. *code receives 0 or one
  * of the device error codes (1..5: which bounded wait expired). Returns FH_OK,
@@ -284,7 +315,7 @@ int fh_abi_version(void);
  * reads it before and after a timed region to report its kernel launches. */
 unsigned long long fh_launch_count(void);
 
-#define FH_ABI_VERSION 6
+#define FH_ABI_VERSION 7
 
 #ifdef __cplusplus
 }

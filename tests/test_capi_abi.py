@@ -16,7 +16,8 @@ HEADER = os.path.join(ROOT, "include", "flash_hog_b200.h")
 
 def _declared():
     text = open(HEADER).read()
-    return sorted(set(re.findall(r"^\s*(?:int|const char\*|unsigned long long)\s+(fh_\w+)\s*\(", text, re.M)))
+    return sorted(set(re.findall(r"^\s*(?:int|const char\*|unsigned long long|long long)\s+(fh_\w+)\s*\(", text,
+                                 re.M)))
 
 
 def test_header_declares_the_binding_symbols():

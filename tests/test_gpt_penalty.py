@@ -57,6 +57,50 @@ def test_penalty_step_bf16_autocast_runs():
     assert all(torch.isfinite(p).all() for p in model.parameters())
 
 
+@pytest.mark.gpu
+def test_fused_layernorm_gelu_match_torch_modules_in_the_step():
+    """fp32 model: LayerNorm and GELU on the fused kernels (forward, backward, double
+    backward) against torch's modules, same weights, attention on the kernels in both."""
+    from flash_hog_b200.gpt import GPT
+
+    torch.manual_seed(0)
+    ref = GPT(SMALL, attention="flash", fused=False).cuda()
+    ours = GPT(SMALL, attention="flash", fused=True).cuda()
+    ours.load_state_dict(ref.state_dict())
+    tokens = _tokens(SMALL, 2, seed=4, device="cuda")
+    out = []
+    for model in (ref, ours):
+        loss, pen = train_step(model, tokens, 0.5, autocast=False)
+        out.append((loss.item(), pen.item(), [p.grad.detach().clone() for p in model.parameters()]))
+    (l0, p0, g0), (l1, p1, g1) = out
+    assert abs(l1 - l0) <= 1e-5 * abs(l0) and abs(p1 - p0) <= 1e-4 * abs(p0)
+    for a, b in zip(g1, g0):
+        assert ((a - b).norm() / b.norm().clamp_min(1e-12)).item() <= 1e-4
+
+
+@pytest.mark.gpu
+def test_graphed_step_equals_eager_step():
+    """The step captured as a CUDA graph and replayed on new tokens gives the eager
+    step's loss, penalty and gradients (bf16 autocast, the benchmark's policy)."""
+    from flash_hog_b200.gpt import GPT, PenaltyStepGraph
+
+    torch.manual_seed(0)
+    eager = GPT(SMALL, attention="flash").cuda()
+    graphed = GPT(SMALL, attention="flash").cuda()
+    graphed.load_state_dict(eager.state_dict())
+    step = PenaltyStepGraph(graphed, batch=2, lam=0.1)
+    for seed in (21, 22):
+        tokens = _tokens(SMALL, 2, seed=seed, device="cuda")
+        eager.zero_grad(set_to_none=True)
+        l0, p0 = train_step(eager, tokens, 0.1)
+        l1, p1 = step.step(tokens)
+        torch.cuda.synchronize()
+        assert abs(l1.item() - l0.item()) <= 1e-6 * abs(l0.item())
+        assert abs(p1.item() - p0.item()) <= 1e-4 * abs(p0.item())
+        for a, b in zip(graphed.parameters(), eager.parameters()):
+            assert ((a.grad - b.grad).norm() / b.grad.norm().clamp_min(1e-12)).item() <= 1e-3
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
