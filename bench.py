@@ -237,9 +237,9 @@ def run_reference(args):
         "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * t,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"bwdbwd {describe()} per GPU: the full B{B} H{H} batch every step, "
-                               f"{n_chunks} chunks of {CPU_CHUNK_HEADS} heads",
-                   "name": args.workload,
+        "config": {"workload": f"bwdbwd {describe()} per GPU", "name": args.workload,
+                   "reference_sample": f"the full B{B} H{H} batch every step, {n_chunks} chunks of "
+                                       f"{CPU_CHUNK_HEADS} heads",
                    "reference_path": "oracle port: torch CPU double autograd (the reference's XLA CPU path needs "
                                      "JAX, absent)",
                    "warmup_unit": "chunks", "step_time": "median over steps"},
