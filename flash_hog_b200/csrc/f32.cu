@@ -147,11 +147,18 @@ __device__ __forceinline__ void load_stats(float* dst, const float* __restrict__
 }
 
 // acc[i][j] += sum_d A[4 rg + i][d] * B[cg + 16 j][d]  (A: resident tile, B: streamed tile)
+// The products run on the packed fp32x2 FMA (one issue slot for two IEEE fmas):
+// each dot product keeps (even, odd) head_dim partial sums, added at the end.
 template <int HD, int NR, int NC>
 __device__ __forceinline__ void score_acc(float (&acc)[4][NC], const float* A, const float* B, int rg, int cg) {
   constexpr int SP = HD + 4;
   const float* a0 = A + rg * 4 * SP;
   const float* b0 = B + cg * SP;
+  float2 acc2[4][NC];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < NC; ++j) acc2[i][j] = make_float2(acc[i][j], 0.f);
 #pragma unroll 4
   for (int d = 0; d < HD; d += 4) {
     float4 a[4], bb[NC];
@@ -163,14 +170,14 @@ __device__ __forceinline__ void score_acc(float (&acc)[4][NC], const float* A, c
     for (int i = 0; i < 4; ++i)
 #pragma unroll
       for (int j = 0; j < NC; ++j) {
-        float x = acc[i][j];
-        x = fmaf(a[i].x, bb[j].x, x);
-        x = fmaf(a[i].y, bb[j].y, x);
-        x = fmaf(a[i].z, bb[j].z, x);
-        x = fmaf(a[i].w, bb[j].w, x);
-        acc[i][j] = x;
+        acc2[i][j] = __ffma2_rn(make_float2(a[i].x, a[i].y), make_float2(bb[j].x, bb[j].y), acc2[i][j]);
+        acc2[i][j] = __ffma2_rn(make_float2(a[i].z, a[i].w), make_float2(bb[j].z, bb[j].w), acc2[i][j]);
       }
   }
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < NC; ++j) acc[i][j] = acc2[i][j].x + acc2[i][j].y;
 }
 
 template <int C>
@@ -178,18 +185,17 @@ __device__ __forceinline__ float lane4(const float4& v) {
   return C == 0 ? v.x : C == 1 ? v.y : C == 2 ? v.z : v.w;
 }
 
+// acc columns (4 m, 4 m + 1) and (4 m + 2, 4 m + 3) as fp32x2 pairs: two packed fmas per 4 columns.
 template <int C, int M>
-__device__ __forceinline__ void out_step(float (&acc)[4][4 * M], const float4 (&p)[4], const float* brow, int cg) {
+__device__ __forceinline__ void out_step(float2 (&acc)[4][2 * M], const float4 (&p)[4], const float* brow, int cg) {
 #pragma unroll
   for (int m = 0; m < M; ++m) {
     const float4 b = *reinterpret_cast<const float4*>(brow + (cg + 16 * m) * 4);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const float pv = lane4<C>(p[i]);
-      acc[i][4 * m + 0] = fmaf(pv, b.x, acc[i][4 * m + 0]);
-      acc[i][4 * m + 1] = fmaf(pv, b.y, acc[i][4 * m + 1]);
-      acc[i][4 * m + 2] = fmaf(pv, b.z, acc[i][4 * m + 2]);
-      acc[i][4 * m + 3] = fmaf(pv, b.w, acc[i][4 * m + 3]);
+      acc[i][2 * m] = __ffma2_rn(make_float2(pv, pv), make_float2(b.x, b.y), acc[i][2 * m]);
+      acc[i][2 * m + 1] = __ffma2_rn(make_float2(pv, pv), make_float2(b.z, b.w), acc[i][2 * m + 1]);
     }
   }
 }
@@ -199,16 +205,28 @@ template <int HD, int BN>
 __device__ __forceinline__ void out_acc(float (&acc)[4][HD / 16], const float* P, const float* B, int rg, int cg) {
   constexpr int SP = HD + 4, SC = BN + 4, M = HD / 64;
   const float* p0 = P + rg * 4 * SC;
+  float2 acc2[4][2 * M];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 2 * M; ++j) acc2[i][j] = make_float2(acc[i][2 * j], acc[i][2 * j + 1]);
 #pragma unroll 2
   for (int n = 0; n < BN; n += 4) {
     float4 p[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) p[i] = *reinterpret_cast<const float4*>(p0 + i * SC + n);
-    out_step<0, M>(acc, p, B + (n + 0) * SP, cg);
-    out_step<1, M>(acc, p, B + (n + 1) * SP, cg);
-    out_step<2, M>(acc, p, B + (n + 2) * SP, cg);
-    out_step<3, M>(acc, p, B + (n + 3) * SP, cg);
+    out_step<0, M>(acc2, p, B + (n + 0) * SP, cg);
+    out_step<1, M>(acc2, p, B + (n + 1) * SP, cg);
+    out_step<2, M>(acc2, p, B + (n + 2) * SP, cg);
+    out_step<3, M>(acc2, p, B + (n + 3) * SP, cg);
   }
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 2 * M; ++j) {
+      acc[i][2 * j] = acc2[i][j].x;
+      acc[i][2 * j + 1] = acc2[i][j].y;
+    }
 }
 
 // out rows (4 rg + i) of the resident tile = mult * acc (+ add, same layout as out).

@@ -167,7 +167,9 @@ class PenaltyStepGraph:
         model.zero_grad(set_to_none=True)
         self.graph = torch.cuda.CUDAGraph()
         n0 = _capi.launch_count()
-        with torch.cuda.graph(self.graph):
+        # thread_local: calls from other threads (NCCL's watchdog under torchrun) cannot
+        # invalidate the capture.
+        with torch.cuda.graph(self.graph, capture_error_mode="thread_local"):
             self.loss, self.penalty = self._compute()
         self.kernels_per_step = _capi.launch_count() - n0  # this library's kernels in one replay
 

@@ -85,9 +85,8 @@ def test_layernorm_kernels(rows, cols):
     for name, got, want in zip(("gx", "gw", "gdy"), (gx, gw, gdy), second64):
         assert _rel(got.cpu(), want) < 1e-4, name
     # Only dx receives a cotangent (dw, db unused): the closed form with vb = cb = 0.
-    x2, w2, dy2 = (g[n].clone().requires_grad_(True) for n in ("x", "w", "dy"))
-    dx2, _, _ = torch.autograd.grad(fused.layer_norm(x2, w2, g["b"]), (x2, w2, g["b"].requires_grad_(True)), dy2,
-                                    create_graph=True)
+    x2, w2, b2, dy2 = (g[n].clone().requires_grad_(True) for n in ("x", "w", "b", "dy"))
+    dx2, _, _ = torch.autograd.grad(fused.layer_norm(x2, w2, b2), (x2, w2, b2), dy2, create_graph=True)
     gx2, gw2, gdy2 = torch.autograd.grad(dx2, (x2, w2, dy2), g["u"])
     n = {k: v.numpy() for k, v in c.items()}
     want = lno.layernorm_bwd_bwd(n["x"], n["w"], n["dy"], n["u"])
