@@ -69,7 +69,7 @@ def describe():
     return f"{'causal' if CAUSAL else 'non-causal'} bf16 B{B} H{H} {seq} D{D}"
 N_SETS = 3  # rotating input sets, each larger than the 126 MB L2
 PEAKS_FILE = os.path.join(ROOT, "MEASURED_PEAKS.json")
-QPASS_DRAM_BYTES = 214.9e6  # ncu dram read + write of one query-pass launch (profiles/)
+QPASS_DRAM_BYTES = 212.4e6  # ncu dram read + write of one query-pass launch (profiles/)
 FALLBACK_PEAKS = {"bf16_tflops": 1590.0, "hbm_gbs": 6650.0}
 
 
