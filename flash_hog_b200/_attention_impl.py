@@ -236,14 +236,19 @@ def dot_product_attention_fwd_jvp(mask_type: MaskType, scale: float, res, tangen
     f32 = _is_f32(query, policy, mask_type)
     q, k, v, o, tq, tk, tv = (_operand(x, f32) for x in (query, key, value, out, tq, tk, tv))
     b, t, n, _ = q.shape
-    stats = torch.empty((3, b, n, t), dtype=torch.float32, device=q.device)
-    zero_do = torch.zeros_like(q)
-    dq2, t_out = torch.empty_like(q), torch.empty_like(q)
-    entry = _capi.attn_bwdbwd_f32 if f32 else _capi.attn_bwdbwd_o
-    entry(q, k, v, o, zero_do, tq, tk, tv, activation.float().contiguous(), dq2, t_out, None, None,
-          stats[0], stats[1], stats[2], scale, _mask_args(mask_type)[0], which=_capi.PASS_QUERY,
-          window=_mask_args(mask_type)[1], **({} if f32 else _varlen_kw(mask_type)))
-    return t_out.to(out.dtype), stats[1].clone()
+    t_lse = torch.empty((b, n, t), dtype=torch.float32, device=q.device)
+    t_out = torch.empty_like(q)
+    causal, window = _mask_args(mask_type)
+    lse = activation.float().contiguous()
+    if f32:
+        stats = torch.empty((2, b, n, t), dtype=torch.float32, device=q.device)
+        _capi.attn_bwdbwd_f32(q, k, v, o, torch.zeros_like(q), tq, tk, tv, lse, None, t_out, None, None, stats[0],
+                              t_lse, stats[1], scale, causal, which=_capi.PASS_QUERY, window=window)
+    else:
+        # The forward-tangent pass: the query pass at dO = 0, without the products that vanish there.
+        _capi.attn_bwdbwd_o(q, k, v, None, None, tq, tk, tv, lse, None, t_out, None, None, None, t_lse, None, scale,
+                            causal, which=_capi.PASS_FWD_TANGENT, window=window, **_varlen_kw(mask_type))
+    return t_out.to(out.dtype), t_lse
 
 
 def dot_product_attention_bwd_jvp(mask_type: MaskType, scale: float, res, g, tangents, policy: str | None = None):

@@ -253,7 +253,7 @@ def attn_bwdbwd(q, k, v, dO, ddq, ddk, ddv, lse, delta, dq2, ddo, dk2, dv2, dd, 
         float(scale), int(causal)))
 
 
-PASS_QUERY, PASS_KEY = 1, 2
+PASS_QUERY, PASS_KEY, PASS_FWD_TANGENT = 1, 2, 4
 
 
 def attn_bwdbwd_pass(q, k, v, dO, ddq, ddk, ddv, lse, delta, dq2, ddo, dk2, dv2, dd, bvec, scale: float,

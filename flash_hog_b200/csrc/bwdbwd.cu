@@ -140,7 +140,48 @@ __device__ __forceinline__ void q_ops(const uint32_t (&vs)[CW], const uint32_t (
   }
 }
 
-template <int HD, bool VL>
+// Forward-tangent forms (dO = 0): the stats sweep needs only dD/scale += P ddS', and
+// the second sweep only P and ddP = P (ddS - dD).
+template <int CW, bool MASK>
+__device__ __forceinline__ void q_stats_tj(const uint32_t (&vs)[CW], const uint32_t (&vdds)[CW], int kc, int klo,
+                                           int khi, float sc2, float lg, float2& dD) {
+  const float2 m = make_float2(sc2, sc2), nl = make_float2(-lg, -lg);
+#pragma unroll
+  for (int i = 0; i < CW; i += 2) {
+    float2 s = __ffma2_rn(f2(vs[i], vs[i + 1]), m, nl);
+    if (MASK) {
+      if (kc + i > khi || kc + i < klo) s.x = -INFINITY;
+      if (kc + i + 1 > khi || kc + i + 1 < klo) s.y = -INFINITY;
+    }
+    dD = __fadd2_rn(dD, __fmul2_rn(f2(vdds[i], vdds[i + 1]), make_float2(ex2(s.x), ex2(s.y))));
+  }
+}
+
+template <int CW, bool MASK>
+__device__ __forceinline__ void q_ops_tj(const uint32_t (&vs)[CW], const uint32_t (&vdds)[CW], int kc, int klo,
+                                         int khi, float sc, float sc2, float lg, float dD,
+                                         uint32_t (&o_ddp)[CW / 2], uint32_t (&o_p)[CW / 2]) {
+  const float2 m = make_float2(sc2, sc2), nl = make_float2(-lg, -lg), msc = make_float2(sc, sc);
+  const float2 ndd = make_float2(-dD, -dD);
+#pragma unroll
+  for (int i = 0; i < CW; i += 2) {
+    float2 s = __ffma2_rn(f2(vs[i], vs[i + 1]), m, nl);
+    if (MASK) {
+      if (kc + i > khi || kc + i < klo) s.x = -INFINITY;
+      if (kc + i + 1 > khi || kc + i + 1 < klo) s.y = -INFINITY;
+    }
+    const float2 p = make_float2(ex2(s.x), ex2(s.y));
+    const float2 ddp = __fmul2_rn(p, __ffma2_rn(f2(vdds[i], vdds[i + 1]), msc, ndd));
+    o_p[i / 2] = pack_bf16(p.x, p.y);
+    o_ddp[i / 2] = pack_bf16(ddp.x, ddp.y);
+  }
+}
+
+// TJ (forward tangent): dO = 0 and (ddQ, ddK, ddV) = (tQ, tK, tV). Then dP = dPa = 0,
+// D = B = 0, dS = dS2 = 0 and dQ' = 0, and the pass reduces to the jvp of the forward:
+// ddO = ddP V + P ddV = tO and dD = rowsum(P ddS) = tL. It skips the dO products, the
+// dQ' products and dO's tile: 8 of the 14 GEMM-equivalents per pair remain.
+template <int HD, bool VL, bool TJ>
 __global__ void __launch_bounds__(kBBThreads, 1)
     bwdbwd_q_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
                     const __grid_constant__ CUtensorMap tm_ddq, const __grid_constant__ CUtensorMap tm_k,
@@ -209,10 +250,10 @@ __global__ void __launch_bounds__(kBBThreads, 1)
     if (lane == 0) {
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
-      const bool fuse_d = a.delta_out != nullptr;
-      mbar_arrive_expect_tx(&bar_res, (fuse_d ? 4 : 3) * G::RES);
+      const bool fuse_d = !TJ && a.delta_out != nullptr;
+      mbar_arrive_expect_tx(&bar_res, (fuse_d ? 4 : TJ ? 2 : 3) * G::RES);
       tma_rows<HD>(s_q, &tm_q, &bar_res, sr.q0 + q0, kBM, h, sr.bc);
-      tma_rows<HD>(s_do, &tm_do, &bar_res, sr.q0 + q0, kBM, h, sr.bc);
+      if (!TJ) tma_rows<HD>(s_do, &tm_do, &bar_res, sr.q0 + q0, kBM, h, sr.bc);
       tma_rows<HD>(s_ddq, &tm_ddq, &bar_res, sr.q0 + q0, kBM, h, sr.bc);
       if (fuse_d) tma_rows<HD>(s_o, &tm_o, &bar_res, sr.q0 + q0, kBM, h, sr.bc);
       int issued = 0;
@@ -267,7 +308,8 @@ __global__ void __launch_bounds__(kBBThreads, 1)
         const uint32_t tb = tmem + sb * G::SCORE_COLS;
         umma_chain_w<KS, G::RES_PANEL, G::PAIR_PANEL, false>(tb + G::C_S, a_q, bk, id128, false);
         umma_chain_w<KS, G::RES_PANEL, G::PAIR_PANEL, false>(tb + G::C_DDS, a_ddq, bk, id64, true);
-        umma_chain_w<KS, G::RES_PANEL, G::PAIR_PANEL, false>(tb + G::C_DP, a_do, bk + kPair, id128, false);
+        if constexpr (!TJ)
+          umma_chain_w<KS, G::RES_PANEL, G::PAIR_PANEL, false>(tb + G::C_DP, a_do, bk + kPair, id128, false);
         umma_commit_w(&bar_sc_full[sb]);
         if (it < n) umma_commit_w(&bar_empty[s]);  // stats sweep: slot free once scored
       }
@@ -292,8 +334,10 @@ __global__ void __launch_bounds__(kBBThreads, 1)
         const int sp = (n + j) % ST;
         const uint64_t mk = mn_ring + sp * kSlot;  // K; ddK = +kHalf; V = +kPair; ddV = +kPair+kHalf
         const bool acc = j > 0;
-        umma_chain_ts_w<KO>(tmem + G::C_DQ, t_ops, mk + kHalf, id_out, acc);
-        umma_chain_ts_w<KO>(tmem + G::C_DQ, t_ops + OC, mk, id_out, true);
+        if constexpr (!TJ) {
+          umma_chain_ts_w<KO>(tmem + G::C_DQ, t_ops, mk + kHalf, id_out, acc);
+          umma_chain_ts_w<KO>(tmem + G::C_DQ, t_ops + OC, mk, id_out, true);
+        }
         umma_chain_ts_w<KO>(tmem + G::C_DDO, t_ops + 2 * OC, mk + kPair, id_out, acc);
         umma_chain_ts_w<KO>(tmem + G::C_DDO, t_ops + 3 * OC, mk + kPair + kHalf, id_out, true);
         umma_commit_w(&bar_ops_empty);
@@ -317,7 +361,9 @@ __global__ void __launch_bounds__(kBBThreads, 1)
     float dD = 0.f, Bv = 0.f, cq = 0.f;
     bool ok = true;
     float dv = 0.f;
-    if (a.delta_out == nullptr) {
+    if constexpr (TJ) {
+      dv = 0.f;  // dO = 0
+    } else if (a.delta_out == nullptr) {
       dv = row_ok ? a.delta[vi] : 0.f;
     } else {
       // D = rowsum(dO o) of this row from the resident tiles, while the first
@@ -340,13 +386,17 @@ __global__ void __launch_bounds__(kBBThreads, 1)
       const uint32_t tb = tmem + sb * G::SCORE_COLS;
       tmem_share<CW>(tb, warp, G::C_S + cb, vs);
       tmem_share<CW>(tb, warp, G::C_DDS + cb, vdds);
-      tmem_share<CW>(tb, warp, G::C_DP + cb, vdp);
-      tmem_share<CW>(tb, warp, G::C_DPA + cb, vdpa);
+      if constexpr (!TJ) {
+        tmem_share<CW>(tb, warp, G::C_DP + cb, vdp);
+        tmem_share<CW>(tb, warp, G::C_DPA + cb, vdpa);
+      }
       tmem_wait_ld();
       reg_fence(vs);
       reg_fence(vdds);
-      reg_fence(vdp);
-      reg_fence(vdpa);
+      if constexpr (!TJ) {
+        reg_fence(vdp);
+        reg_fence(vdpa);
+      }
       warp_arrive(&bar_sc_empty[sb]);  // the tensor core may reuse this score buffer now
       return true;
     };
@@ -358,10 +408,17 @@ __global__ void __launch_bounds__(kBBThreads, 1)
         uint32_t vs[CW], vdds[CW], vdp[CW], vdpa[CW];
         ok = load_scores(j, vs, vdds, vdp, vdpa);
         if (!ok) break;
-        if (kc + CW - 1 > khi || kc < klo)
-          q_stats<CW, true>(vs, vdds, vdp, vdpa, kc, klo, khi, sc2, lg, pdD, pr1, pr2, pr3);
-        else
-          q_stats<CW, false>(vs, vdds, vdp, vdpa, kc, klo, khi, sc2, lg, pdD, pr1, pr2, pr3);
+        if constexpr (TJ) {
+          if (kc + CW - 1 > khi || kc < klo)
+            q_stats_tj<CW, true>(vs, vdds, kc, klo, khi, sc2, lg, pdD);
+          else
+            q_stats_tj<CW, false>(vs, vdds, kc, klo, khi, sc2, lg, pdD);
+        } else {
+          if (kc + CW - 1 > khi || kc < klo)
+            q_stats<CW, true>(vs, vdds, vdp, vdpa, kc, klo, khi, sc2, lg, pdD, pr1, pr2, pr3);
+          else
+            q_stats<CW, false>(vs, vdds, vdp, vdpa, kc, klo, khi, sc2, lg, pdD, pr1, pr2, pr3);
+        }
       }
       if (ok) {
         // Combine the column pairs, then the two warpgroups' column halves (same
@@ -389,17 +446,26 @@ __global__ void __launch_bounds__(kBBThreads, 1)
       ok = load_scores(n + j, vs, vdds, vdp, vdpa);
       if (!ok) break;
       uint32_t o_ds[CW / 2], o_ds2[CW / 2], o_ddp[CW / 2], o_p[CW / 2];
-      if (kc + CW - 1 > khi || kc < klo)
-        q_ops<CW, true>(vs, vdds, vdp, vdpa, kc, klo, khi, sc, sc2, lg, dv, dD, cq, o_ds, o_ds2, o_ddp, o_p);
-      else
-        q_ops<CW, false>(vs, vdds, vdp, vdpa, kc, klo, khi, sc, sc2, lg, dv, dD, cq, o_ds, o_ds2, o_ddp, o_p);
+      if constexpr (TJ) {
+        if (kc + CW - 1 > khi || kc < klo)
+          q_ops_tj<CW, true>(vs, vdds, kc, klo, khi, sc, sc2, lg, dD, o_ddp, o_p);
+        else
+          q_ops_tj<CW, false>(vs, vdds, kc, klo, khi, sc, sc2, lg, dD, o_ddp, o_p);
+      } else {
+        if (kc + CW - 1 > khi || kc < klo)
+          q_ops<CW, true>(vs, vdds, vdp, vdpa, kc, klo, khi, sc, sc2, lg, dv, dD, cq, o_ds, o_ds2, o_ddp, o_p);
+        else
+          q_ops<CW, false>(vs, vdds, vdp, vdpa, kc, klo, khi, sc, sc2, lg, dv, dD, cq, o_ds, o_ds2, o_ddp, o_p);
+      }
       if (j > 0) ok = mbar_wait_warp(&bar_ops_empty, (j - 1) & 1, &abort_flag);
       if (!ok) break;
       tc_fence_after();
       // This warpgroup's CW keys are packed columns [CW/2 wg, CW/2 wg + CW/2) of each operand.
       const uint32_t to = tmem + tmem_lane_base(warp & 3) + G::C_OPS + (CW / 2) * wg;
-      tmem_st_ops(to, o_ds);
-      tmem_st_ops(to + G::OPS_COLS, o_ds2);
+      if constexpr (!TJ) {
+        tmem_st_ops(to, o_ds);
+        tmem_st_ops(to + G::OPS_COLS, o_ds2);
+      }
       tmem_st_ops(to + 2 * G::OPS_COLS, o_ddp);
       tmem_st_ops(to + 3 * G::OPS_COLS, o_p);
       tmem_wait_st();
@@ -408,10 +474,10 @@ __global__ void __launch_bounds__(kBBThreads, 1)
     if (ok && n == 0) {
       // No key tile: every output of these rows is zero.
       if (row_ok) {
-        zero_row_global<HD>((wg == 0 ? a.dq2 : a.ddo) + q_row(sh, sr, row, h));
+        if (!TJ || wg == 1) zero_row_global<HD>((wg == 0 ? a.dq2 : a.ddo) + q_row(sh, sr, row, h));
         if (wg == 0) {
           a.dd[vi] = 0.f;
-          a.bv[vi] = 0.f;
+          if (!TJ) a.bv[vi] = 0.f;
         }
       }
     } else if (ok) {
@@ -421,10 +487,10 @@ __global__ void __launch_bounds__(kBBThreads, 1)
       tc_fence_after();
       const int srow = row_ok ? row : 0;
       if (wg == 0) {
-        tmem_row_to_global<HD>(tmem, warp, G::C_DQ, a.dq2 + q_row(sh, sr, srow, h), row_ok, sc);
+        if constexpr (!TJ) tmem_row_to_global<HD>(tmem, warp, G::C_DQ, a.dq2 + q_row(sh, sr, srow, h), row_ok, sc);
         if (row_ok) {
           a.dd[vi] = dD;
-          a.bv[vi] = Bv;
+          if (!TJ) a.bv[vi] = Bv;
         }
       } else {
         tmem_row_to_global<HD>(tmem, warp, G::C_DDO, a.ddo + q_row(sh, sr, srow, h), row_ok);
@@ -857,8 +923,10 @@ int launch_bwdbwd_hd(const AttnShape& s, const BwdBwdPtrs& p, int passes, int* s
   using GK = KPass<HD>;
   CUtensorMap mq[8], mk[7];
   // Query-tiled pass: 128-row query tiles, 64-row key tiles.
+  // dO and O are only read by the passes that need them (the forward-tangent pass reads
+  // neither); a stand-in base keeps their maps valid when they are absent.
   bool ok = make_seq_map(&mq[0], p.q, HD, s.total_q, s.H, map_batch(s), s.sq, kBM) &&
-            make_seq_map(&mq[1], p.dO, HD, s.total_q, s.H, map_batch(s), s.sq, kBM) &&
+            make_seq_map(&mq[1], p.dO ? p.dO : p.q, HD, s.total_q, s.H, map_batch(s), s.sq, kBM) &&
             make_seq_map(&mq[2], p.ddq, HD, s.total_q, s.H, map_batch(s), s.sq, kBM) &&
             make_seq_map(&mq[3], p.k, HD, s.total_k, s.Hk, map_batch(s), s.sk, GQ::BN) &&
             make_seq_map(&mq[4], p.v, HD, s.total_k, s.Hk, map_batch(s), s.sk, GQ::BN) &&
@@ -871,10 +939,11 @@ int launch_bwdbwd_hd(const AttnShape& s, const BwdBwdPtrs& p, int passes, int* s
        make_seq_map(&mk[2], p.ddk, HD, s.total_k, s.Hk, map_batch(s), s.sk, kBM) &&
        make_seq_map(&mk[3], p.ddv, HD, s.total_k, s.Hk, map_batch(s), s.sk, kBM) &&
        make_seq_map(&mk[4], p.q, HD, s.total_q, s.H, map_batch(s), s.sq, GK::BN) &&
-       make_seq_map(&mk[5], p.dO, HD, s.total_q, s.H, map_batch(s), s.sq, GK::BN) &&
+       make_seq_map(&mk[5], p.dO ? p.dO : p.q, HD, s.total_q, s.H, map_batch(s), s.sq, GK::BN) &&
        make_seq_map(&mk[6], p.ddq, HD, s.total_q, s.H, map_batch(s), s.sq, GK::BN);
   if (!ok) return kInvalidArgument;
-  if (ensure_smem_limit(reinterpret_cast<const void*>(&bwdbwd_q_kernel<HD, VL>), GQ::SMEM) != kOk ||
+  if (ensure_smem_limit(reinterpret_cast<const void*>(&bwdbwd_q_kernel<HD, VL, false>), GQ::SMEM) != kOk ||
+      ensure_smem_limit(reinterpret_cast<const void*>(&bwdbwd_q_kernel<HD, VL, true>), GQ::SMEM) != kOk ||
       ensure_smem_limit(reinterpret_cast<const void*>(&bwdbwd_k_kernel<HD, VL>), GK::SMEM) != kOk)
     return kLaunchFailed;
   // With `o`, the query pass computes D into delta_out and the key pass reads it there.
@@ -889,10 +958,14 @@ int launch_bwdbwd_hd(const AttnShape& s, const BwdBwdPtrs& p, int passes, int* s
               static_cast<__nv_bfloat16*>(p.dk2),
               static_cast<__nv_bfloat16*>(p.dv2),
               status};
-  if (passes & kPassQuery) {
-    const dim3 gq(s.H, s.B, (s.Tq + kBM - 1) / kBM);
-    bwdbwd_q_kernel<HD, VL><<<gq, kBBThreads, GQ::SMEM, stream>>>(mq[0], mq[1], mq[2], mq[3], mq[4], mq[5], mq[6],
-                                                              mq[7], args);
+  const dim3 gq(s.H, s.B, (s.Tq + kBM - 1) / kBM);
+  if (passes & kPassFwdTangent) {
+    bwdbwd_q_kernel<HD, VL, true><<<gq, kBBThreads, GQ::SMEM, stream>>>(mq[0], mq[1], mq[2], mq[3], mq[4], mq[5],
+                                                                       mq[6], mq[7], args);
+    if (after_launch() != kOk) return kLaunchFailed;
+  } else if (passes & kPassQuery) {
+    bwdbwd_q_kernel<HD, VL, false><<<gq, kBBThreads, GQ::SMEM, stream>>>(mq[0], mq[1], mq[2], mq[3], mq[4], mq[5],
+                                                                        mq[6], mq[7], args);
     if (after_launch() != kOk) return kLaunchFailed;
   }
   if (passes & kPassKey) {

@@ -291,7 +291,19 @@ static int bwdbwd_entry(const char* entry, void* stream, const fh_attn_dims* dim
   AttnShape s;
   int rc = validate(dims, &s, scale, causal);
   if (rc != kOk) return rc;
-  if (passes < 1 || passes > 3) return fail(FH_ERR_INVALID_ARGUMENT, "pass must be 1, 2 or 3");
+  if (passes == kPassFwdTangent) {
+    // dO = 0: only q, k, v, the tangents (ddq, ddk, ddv), lse and the outputs ddo, dd are used.
+    if (!all_aligned(q, k, v, ddq, ddk, ddv, ddo) || !lse || !dd) return fail(FH_ERR_INVALID_ARGUMENT, kAlignMsg);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if ((rc = select_stream_device(st)) != kOk) return rc;
+    int* status = status_word();
+    if (!status) return FH_ERR_NO_DEVICE;
+    return launch_bwdbwd(
+        s, dims->head_dim,
+        BwdBwdPtrs{q, k, v, nullptr, ddq, ddk, ddv, lse, nullptr, nullptr, ddo, nullptr, nullptr, dd, nullptr},
+        kPassFwdTangent, status, st);
+  }
+  if (passes < 1 || passes > 3) return fail(FH_ERR_INVALID_ARGUMENT, "pass must be 1, 2, 3 or 4 (forward tangent)");
   if (!all_aligned(q, k, v, dO, ddq, ddk, ddv) || !lse || !dd || !bvec)
     return fail(FH_ERR_INVALID_ARGUMENT, kAlignMsg);
   if (o ? (!all_aligned(o) || !delta_out) : !delta) return fail(FH_ERR_INVALID_ARGUMENT, kAlignMsg);

@@ -52,8 +52,10 @@ struct BwdBwdPtrs {
 int launch_fwd(const AttnShape& s, int hd, const FwdPtrs& p, int* status, cudaStream_t stream);
 int launch_rowdot(const AttnShape& s, int hd, const void* o, const void* dO, float* delta, cudaStream_t stream);
 int launch_bwd(const AttnShape& s, int hd, const BwdPtrs& p, int* status, cudaStream_t stream);
-// passes: bitmask of kPassQuery (query-tiled: dQ', ddO, dD, B) and kPassKey (key-tiled: dK', dV').
-enum BwdBwdPass : int { kPassQuery = 1, kPassKey = 2 };
+// passes: bitmask of kPassQuery (query-tiled: dQ', ddO, dD, B) and kPassKey (key-tiled: dK', dV'),
+// or kPassFwdTangent alone: the query-tiled pass for dO = 0 (ddO = the forward's tangent,
+// dD = the log-sum-exp's tangent; dO, O, delta, dq2 and bv are neither read nor written).
+enum BwdBwdPass : int { kPassQuery = 1, kPassKey = 2, kPassFwdTangent = 4 };
 int launch_bwdbwd(const AttnShape& s, int hd, const BwdBwdPtrs& p, int passes, int* status, cudaStream_t stream);
 
 // fp32 operands on the CUDA cores (f32.cu): same passes, masks, GQA mapping and

@@ -154,7 +154,7 @@ int fh_attn_bwdbwd(void* stream, const fh_attn_dims* dims, const void* q, const 
  * The reference runs the same two stages as separate kernels and times them
  * separately (flash_hog/csrc/tk_bwdbwd/ffi.cu:71-73, BENCHMARKS.md:45-46); this
  * entry lets a caller schedule or time them one at a time. */
-enum fh_bwdbwd_pass { FH_PASS_QUERY = 1, FH_PASS_KEY = 2 };
+enum fh_bwdbwd_pass { FH_PASS_QUERY = 1, FH_PASS_KEY = 2, FH_PASS_FWD_TANGENT = 4 };
 int fh_attn_bwdbwd_pass(void* stream, const fh_attn_dims* dims, const void* q, const void* k, const void* v,
                         const void* dO, const void* ddq, const void* ddk, const void* ddv, const float* lse,
                         const float* delta, void* dq2, void* ddo, void* dk2, void* dv2, float* dd, float* bvec,
@@ -170,9 +170,12 @@ int fh_attn_bwdbwd_pass(void* stream, const fh_attn_dims* dims, const void* q, c
  * the Pallas rule does the same at _pallas_gpu_kernel.py:110).
  * `passes`: FH_PASS_QUERY, FH_PASS_KEY (after a query pass on the same
  * buffers) or both (3).
- * Forward tangent: with dO = 0 (a zero-filled buffer) and (ddq, ddk, ddv) =
- * (tq, tk, tv), the query pass alone writes the jvp of the forward, to = d O
- * into `ddo` and tlse = d lse into `dd` (dq2 is then zero). */
+ * Forward tangent: `passes` = FH_PASS_FWD_TANGENT with (ddq, ddk, ddv) =
+ * (tq, tk, tv) runs the query pass for dO = 0 and writes the jvp of the forward,
+ * to = d O into `ddo` and tlse = d lse into `dd`. It skips the products that vanish
+ * at dO = 0 (8 of the pass's 14 GEMM-equivalents per pair remain); o, dO, dq2,
+ * delta and bvec are neither read nor written (may be NULL). The same result
+ * (bit for bit) comes from FH_PASS_QUERY with a zero-filled dO. */
 int fh_attn_bwdbwd_o(void* stream, const fh_attn_dims* dims, const void* q, const void* k, const void* v,
                      const void* o, const void* dO, const void* ddq, const void* ddk, const void* ddv,
                      const float* lse, void* dq2, void* ddo, void* dk2, void* dv2, float* delta, float* dd,

@@ -209,3 +209,33 @@ def test_forward_over_reverse_hvp_on_gpu(causal):
                       (x64["q"], x64["k"], x64["v"]), (x64["ddq"], x64["ddk"], x64["ddv"]))
     for name, got, want in zip(("q", "k", "v"), hv, h_ref):
         assert_close(f"hvp_{name}", np64(got), _np(want), tol=3e-2)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("b,h,hk,tq,tk,causal,d,window", [(1, 4, 2, 256, 384, 0, 64, 0), (2, 2, 2, 200, 200, 1, 128, 0),
+                                                          (1, 2, 1, 320, 256, 2, 64, 96)])
+def test_forward_tangent_pass_equals_the_query_pass_at_zero_do(b, h, hk, tq, tk, causal, d, window):
+    """FH_PASS_FWD_TANGENT (the query pass without the products that vanish at dO = 0)
+    writes the same tO and tL, bit for bit, as FH_PASS_QUERY with a zero-filled dO; and
+    both match the oracle's jvp of the forward."""
+    from flash_hog_b200 import _capi
+
+    x = {n: t.cuda() for n, t in ora.make_inputs(b, h, tq, tk, d, seed=tq + d, kv_heads=hk).items()}
+    o, lse = torch.empty_like(x["q"]), torch.empty((b, h, tq), dtype=torch.float32, device="cuda")
+    _capi.attn_fwd(x["q"], x["k"], x["v"], o, lse, d ** -0.5, causal, window)
+    st = torch.empty((3, b, h, tq), dtype=torch.float32, device="cuda")
+    to_ref, dq2 = torch.empty_like(o), torch.empty_like(o)
+    _capi.attn_bwdbwd_o(x["q"], x["k"], x["v"], o, torch.zeros_like(o), x["ddq"], x["ddk"], x["ddv"], lse, dq2, to_ref,
+                        None, None, st[0], st[1], st[2], d ** -0.5, causal, which=_capi.PASS_QUERY, window=window)
+    to, tl = torch.empty_like(o), torch.empty((b, h, tq), dtype=torch.float32, device="cuda")
+    _capi.attn_bwdbwd_o(x["q"], x["k"], x["v"], None, None, x["ddq"], x["ddk"], x["ddv"], lse, None, to, None, None,
+                        None, tl, None, d ** -0.5, causal, which=_capi.PASS_FWD_TANGENT, window=window)
+    torch.cuda.synchronize()
+    assert _capi.device_status() == 0
+    assert torch.equal(to, to_ref) and torch.equal(tl, st[1])
+    n = lambda t: t.detach().double().cpu().numpy()
+    want_o, want_l = ora.jvp_fwd(n(x["q"]), n(x["k"]), n(x["v"]), n(o), n(lse), n(x["ddq"]), n(x["ddk"]), n(x["ddv"]),
+                                 causal=causal, window=window)
+    assert ora.rel_err(n(to), want_o) <= 2e-2
+    finite = np.isfinite(want_l)
+    assert ora.rel_err(n(tl)[finite], want_l[finite]) <= 2e-2
