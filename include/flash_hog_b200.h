@@ -174,8 +174,8 @@ int fh_attn_bwdbwd_pass(void* stream, const fh_attn_dims* dims, const void* q, c
  * (tq, tk, tv) runs the query pass for dO = 0 and writes the jvp of the forward,
  * to = d O into `ddo` and tlse = d lse into `dd`. It skips the products that vanish
  * at dO = 0 (8 of the pass's 14 GEMM-equivalents per pair remain); o, dO, dq2,
- * delta and bvec are neither read nor written (may be NULL). The same result
- * (bit for bit) comes from FH_PASS_QUERY with a zero-filled dO. */
+ * delta and bvec are neither read nor written (may be NULL). FH_PASS_QUERY with a
+ * zero-filled dO gives the same result to within rounding. */
 int fh_attn_bwdbwd_o(void* stream, const fh_attn_dims* dims, const void* q, const void* k, const void* v,
                      const void* o, const void* dO, const void* ddq, const void* ddk, const void* ddv,
                      const float* lse, void* dq2, void* ddo, void* dk2, void* dv2, float* delta, float* dd,
