@@ -49,8 +49,12 @@ int current_device() {
 int select_stream_device(cudaStream_t stream) {
   int dev = current_device();
   cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
-  if (stream != nullptr && cudaStreamIsCapturing(stream, &capture) == cudaSuccess &&
-      capture == cudaStreamCaptureStatusNone) {
+  bool query = stream != nullptr;
+  if (query && cudaStreamIsCapturing(stream, &capture) != cudaSuccess) {
+    cudaGetLastError();  // not a launch failure: leave no error for after_launch() to find
+    query = false;
+  }
+  if (query && capture == cudaStreamCaptureStatusNone) {
     int sdev = -1;
     if (cudaStreamGetDevice(stream, &sdev) == cudaSuccess) {
       dev = sdev;
