@@ -21,6 +21,11 @@
 //    first half of S(j), and S(j+1) is issued right behind O += P(j) V_j into the
 //    same buffer (the tensor core runs in issue order). The two tiles of a CTA
 //    share the exponential units; each warpgroup computes while the other waits.
+//    A quarter of the exponentials go to a polynomial on the FMA pipe, which
+//    shortens the softmax step that lies on each tile's critical path.
+// K and V of a ring slot land and are released on their own barriers: a slot's K is
+// free once the score products of its key tile are done, so the next K load starts
+// about one key tile earlier than it could if K and V were released together.
 // Online softmax with lazy rescaling: P = exp2(s - m) against a running maximum
 // m that is only raised -- and O, l rescaled in TMEM -- when a row's maximum
 // grows by more than 2^8, so P stays below 2^8 and most tiles need no rescale.
@@ -71,10 +76,33 @@ struct FPass {
   static_assert(C_O + T * HD <= TMEM_COLS, "TMEM budget");
   static_assert(CTAS * SMEM <= 228 * 1024 - CTAS * 2048, "shared memory of the resident CTAs");
   static_assert(SMEM <= 232448, "shared memory budget");
-  // The issuer waits for key tile j+1 (S(j+1)) before it releases tile j's slot:
+  // The issuer waits for K of key tile j+1 (S(j+1)) before it releases tile j's V:
   // with one slot that wait could never end.
   static_assert(ST >= 2, "the ring must hold the next key tile while the current one is in use");
 };
+
+// 2^x for a pair of floats on the FMA and integer pipes instead of the MUFU unit:
+// x = j + f with j = round(x) (adding 1.5 * 2^23 rounds to an integer) and f in
+// [-0.5, 0.5]; 2^f by a degree-3 polynomial whose coefficients were fitted for this
+// library by a Lawson (iteratively reweighted least-squares) minimax iteration on the
+// relative error over [-0.5, 0.5] (max 7.5e-5, far below the bf16 rounding of P); j
+// is added to the result's exponent field. x < -126, including a masked -inf, gives 0.
+__device__ __forceinline__ float2 exp2_fma2(float2 x) {
+  const float2 big = make_float2(12582912.f, 12582912.f);
+  const float2 t = __fadd2_rn(x, big);
+  const float2 j = __fadd2_rn(t, make_float2(-12582912.f, -12582912.f));
+  const float2 f = __ffma2_rn(j, make_float2(-1.f, -1.f), x);
+  float2 p = __ffma2_rn(f, make_float2(0.055171342699099686f, 0.055171342699099686f),
+                        make_float2(0.24261034141576007f, 0.24261034141576007f));
+  p = __ffma2_rn(p, f, make_float2(0.6932609672206897f, 0.6932609672206897f));
+  p = __ffma2_rn(p, f, make_float2(0.9999281213111199f, 0.9999281213111199f));
+  float2 r;
+  r.x = __int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23));
+  r.y = __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23));
+  r.x = x.x < -126.f ? 0.f : r.x;
+  r.y = x.y < -126.f ? 0.f : r.y;
+  return r;
+}
 
 // All lanes of the warp have finished their TMEM accesses; one lane arrives.
 __device__ __forceinline__ void fwd_warp_arrive(uint64_t* bar) {
@@ -96,8 +124,10 @@ __global__ void __launch_bounds__(FPass<HD>::THREADS, FPass<HD>::CTAS)
   uint8_t* s_ring = s_q + T * G::RES;
   // Per query tile t: scores ready, scores loaded (separate P only), P written,
   // P read by its product (separate P only), last O update done.
-  __shared__ uint64_t bar_q, bar_full[ST], bar_empty[ST], bar_s_full[2], bar_s_empty[2], bar_p_full[2],
-      bar_p_free[2], bar_o_done[2];
+  // K and V of a ring slot land and are released separately: a slot's K is free once
+  // the score products of its key tile are done, long before its V has been used.
+  __shared__ uint64_t bar_q, bar_kfull[ST], bar_vfull[ST], bar_kempty[ST], bar_vempty[ST], bar_s_full[2],
+      bar_s_empty[2], bar_p_full[2], bar_p_free[2], bar_o_done[2];
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
 
@@ -126,8 +156,10 @@ __global__ void __launch_bounds__(FPass<HD>::THREADS, FPass<HD>::CTAS)
     abort_flag = 0;
     mbar_init(&bar_q, 1);
     for (int s = 0; s < ST; ++s) {
-      mbar_init(&bar_full[s], 1);
-      mbar_init(&bar_empty[s], 1);
+      mbar_init(&bar_kfull[s], 1);
+      mbar_init(&bar_vfull[s], 1);
+      mbar_init(&bar_kempty[s], 1);
+      mbar_init(&bar_vempty[s], 1);
     }
     for (int t = 0; t < T; ++t) {
       mbar_init(&bar_s_full[t], 1);
@@ -151,23 +183,32 @@ __global__ void __launch_bounds__(FPass<HD>::THREADS, FPass<HD>::CTAS)
       tma_prefetch_desc(&tm_v);
       mbar_arrive_expect_tx(&bar_q, T * G::RES);
       for (int t = 0; t < T; ++t) tma_rows<HD>(s_q + t * G::RES, &tm_q, &bar_q, sr.q0 + q0 + t * kBM, kBM, h, sr.bc);
-      int issued = 0;
+      int k_issued = 0, v_issued = 0;
       for (int j = 0; j < n; ++j) {
         const int s = j % ST;
-        if (j >= ST && !mbar_wait(&bar_empty[s], ((j / ST) - 1) & 1, &abort_flag)) {
+        const uint32_t ph = ((j / ST) - 1) & 1;
+        uint8_t* slot = s_ring + s * G::SLOT;
+        if (j >= ST && !mbar_wait(&bar_kempty[s], ph, &abort_flag)) {
           raise_error(a.status, &abort_flag, kDevTimeoutSlotEmpty);
           break;
         }
-        uint8_t* slot = s_ring + s * G::SLOT;
-        mbar_arrive_expect_tx(&bar_full[s], G::SLOT);
-        tma_rows<HD>(slot, &tm_k, &bar_full[s], sr.k0 + (jlo + j) * BN, BN, h / sh.G, sr.bc);
-        tma_rows<HD>(slot + G::STR, &tm_v, &bar_full[s], sr.k0 + (jlo + j) * BN, BN, h / sh.G, sr.bc);
-        issued = j + 1;
+        mbar_arrive_expect_tx(&bar_kfull[s], G::STR);
+        tma_rows<HD>(slot, &tm_k, &bar_kfull[s], sr.k0 + (jlo + j) * BN, BN, h / sh.G, sr.bc);
+        k_issued = j + 1;
+        if (j >= ST && !mbar_wait(&bar_vempty[s], ph, &abort_flag)) {
+          raise_error(a.status, &abort_flag, kDevTimeoutSlotEmpty);
+          break;
+        }
+        mbar_arrive_expect_tx(&bar_vfull[s], G::STR);
+        tma_rows<HD>(slot + G::STR, &tm_v, &bar_vfull[s], sr.k0 + (jlo + j) * BN, BN, h / sh.G, sr.bc);
+        v_issued = j + 1;
       }
       // Every issued copy must land before this CTA's shared memory is released.
       bool drained = mbar_wait(&bar_q, 0, nullptr);
-      for (int j = issued > ST ? issued - ST : 0; j < issued; ++j)
-        drained &= mbar_wait(&bar_full[j % ST], (j / ST) & 1, nullptr);
+      for (int j = k_issued > ST ? k_issued - ST : 0; j < k_issued; ++j)
+        drained &= mbar_wait(&bar_kfull[j % ST], (j / ST) & 1, nullptr);
+      for (int j = v_issued > ST ? v_issued - ST : 0; j < v_issued; ++j)
+        drained &= mbar_wait(&bar_vfull[j % ST], (j / ST) & 1, nullptr);
       if (!drained) raise_error(a.status, &abort_flag, kDevTimeoutDrain);
     }
   } else if (warp == kFwdWarpMma) {
@@ -184,16 +225,25 @@ __global__ void __launch_bounds__(FPass<HD>::THREADS, FPass<HD>::CTAS)
     constexpr uint64_t kSlot = G::SLOT >> 4;
     auto issue_s = [&](int t, int j) -> bool {
       const int s = j % ST;
-      if (!mbar_wait_warp(&bar_full[s], (j / ST) & 1, &abort_flag)) return false;
+      if (!mbar_wait_warp(&bar_kfull[s], (j / ST) & 1, &abort_flag)) return false;
       tc_fence_after();
       umma_chain_w<KS, kBM * 128, BN * 128, false>(tmem + t * BN, a_q + t * kRes, b_k + s * kSlot, id_s, false);
       umma_commit_w(&bar_s_full[t]);
       return true;
     };
     // Ring position j holds key tile jlo + j; tile t's own step is u = j - at[t].
+    // Every score product of ring position j is issued before iteration j (position 0
+    // before the loop), so K of position j + 1 is released at the end of iteration j;
+    // V of position j once iteration j's products are done.
+    auto wait_v = [&](int j) -> bool {
+      if (!mbar_wait_warp(&bar_vfull[j % ST], (j / ST) & 1, &abort_flag)) return false;
+      tc_fence_after();
+      return true;
+    };
     bool ok = mbar_wait_warp(&bar_q, 0, &abort_flag);
     for (int t = 0; ok && t < T; ++t)
       if (nt[t] > 0 && at[t] == 0) ok = issue_s(t, 0);
+    if (ok && n > 0) umma_commit_w(&bar_kempty[0]);
     for (int j = 0; ok && SEP_P && j < n; ++j) {
       // Separate P: S(u+1) as soon as S(u) has been loaded, then the products.
 #pragma unroll
@@ -203,6 +253,8 @@ __global__ void __launch_bounds__(FPass<HD>::THREADS, FPass<HD>::CTAS)
         if (u >= 0) ok = mbar_wait_warp(&bar_s_empty[t], u & 1, &abort_flag);
         ok = ok && issue_s(t, j + 1);
       }
+      if (ok && j + 1 < n) umma_commit_w(&bar_kempty[(j + 1) % ST]);
+      ok = ok && wait_v(j);
 #pragma unroll
       for (int t = 0; ok && t < T; ++t) {
         const int u = j - at[t];
@@ -217,9 +269,10 @@ __global__ void __launch_bounds__(FPass<HD>::THREADS, FPass<HD>::CTAS)
         umma_commit_w(&bar_p_free[t]);
         if (u + 1 == nt[t]) umma_commit_w(&bar_o_done[t]);
       }
-      if (ok) umma_commit_w(&bar_empty[j % ST]);
+      if (ok) umma_commit_w(&bar_vempty[j % ST]);
     }
     for (int j = 0; ok && !SEP_P && j < n; ++j) {
+      ok = wait_v(j);
 #pragma unroll
       for (int t = 0; ok && t < T; ++t) {
         const int u = j - at[t];
@@ -240,7 +293,8 @@ __global__ void __launch_bounds__(FPass<HD>::THREADS, FPass<HD>::CTAS)
           umma_commit_w(&bar_o_done[t]);
         }
       }
-      if (ok) umma_commit_w(&bar_empty[j % ST]);
+      if (ok && j + 1 < n) umma_commit_w(&bar_kempty[(j + 1) % ST]);
+      if (ok) umma_commit_w(&bar_vempty[j % ST]);
     }
     if (!ok && lane == 0) raise_error(a.status, &abort_flag, kDevTimeoutTmaFull);
   } else {
@@ -321,7 +375,7 @@ __global__ void __launch_bounds__(FPass<HD>::THREADS, FPass<HD>::CTAS)
 #pragma unroll
       for (int i = 0; i < BN; i += 2) {
         const float2 s = __ffma2_rn(make_float2(__uint_as_float(v[i]), __uint_as_float(v[i + 1])), m2, nb2);
-        const float2 p = make_float2(ex2(s.x), ex2(s.y));
+        const float2 p = (HD == 128 && ((i >> 1) & 7) < 2) ? exp2_fma2(s) : make_float2(ex2(s.x), ex2(s.y));
         ps2[(i >> 1) & 1] = __fadd2_rn(ps2[(i >> 1) & 1], p);
         pk[i / 2] = pack_bf16(p.x, p.y);
       }
