@@ -21,8 +21,8 @@
 //    first half of S(j), and S(j+1) is issued right behind O += P(j) V_j into the
 //    same buffer (the tensor core runs in issue order). The two tiles of a CTA
 //    share the exponential units; each warpgroup computes while the other waits.
-//    A quarter of the exponentials go to a polynomial on the FMA pipe, which
-//    shortens the softmax step that lies on each tile's critical path.
+// At both head dims a quarter of the exponentials go to a polynomial on the FMA
+// pipe, which shortens the softmax step that lies on each tile's critical path.
 // K and V of a ring slot land and are released on their own barriers: a slot's K is
 // free once the score products of its key tile are done, so the next K load starts
 // about one key tile earlier than it could if K and V were released together.
@@ -375,7 +375,8 @@ __global__ void __launch_bounds__(FPass<HD>::THREADS, FPass<HD>::CTAS)
 #pragma unroll
       for (int i = 0; i < BN; i += 2) {
         const float2 s = __ffma2_rn(make_float2(__uint_as_float(v[i]), __uint_as_float(v[i + 1])), m2, nb2);
-        const float2 p = (HD == 128 && ((i >> 1) & 7) < 2) ? exp2_fma2(s) : make_float2(ex2(s.x), ex2(s.y));
+        // A quarter of the column pairs take 2^x on the FMA pipe (exp2_fma2).
+        const float2 p = ((i >> 1) & 7) < 2 ? exp2_fma2(s) : make_float2(ex2(s.x), ex2(s.y));
         ps2[(i >> 1) & 1] = __fadd2_rn(ps2[(i >> 1) & 1], p);
         pk[i / 2] = pack_bf16(p.x, p.y);
       }
