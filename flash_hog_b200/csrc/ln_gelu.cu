@@ -258,17 +258,35 @@ __global__ void __launch_bounds__(32 * kLnWarps) ln_bwd_bwd_kernel(
   block_column_partials<C>(agw, unused, nch, cols, part, smem);
 }
 
-// out0[col] = sum_p part[p][0][col], out1 likewise (nparts in order).
-__global__ void column_sum_kernel(int nparts, int cols, const float* __restrict__ part, float* __restrict__ out0,
-                                  float* __restrict__ out1) {
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= 2 * cols) return;
-  const int k = i / cols, col = i - k * cols;
-  float* out = k == 0 ? out0 : out1;
-  if (!out) return;
+// out0[col] = sum_p part[p][0][col], out1 likewise, in a fixed order: the parts are
+// split into kSumGroups runs of consecutive parts, each run summed in order by one
+// warp of the block (32 columns per block), then the run sums added in run order.
+constexpr int kSumGroups = 16;
+__global__ void __launch_bounds__(32 * kSumGroups) column_sum_kernel(int nparts, int cols,
+                                                                     const float* __restrict__ part,
+                                                                     float* __restrict__ out0,
+                                                                     float* __restrict__ out1) {
+  __shared__ float runs[kSumGroups][32];
+  const int cx = threadIdx.x & 31, g = threadIdx.x >> 5;
+  const int i = blockIdx.x * 32 + cx;  // (k, col) flattened over 2 * cols
+  const bool valid = i < 2 * cols;
+  const int k = valid ? i / cols : 0, col = valid ? i - k * cols : 0;
+  const int per = (nparts + kSumGroups - 1) / kSumGroups;
+  const int p0 = g * per, p1 = min(nparts, p0 + per);
   float s = 0.f;
-  for (int p = 0; p < nparts; ++p) s += part[(static_cast<size_t>(p) * 2 + k) * cols + col];
-  out[col] = s;
+  if (valid) {
+#pragma unroll 8
+    for (int p = p0; p < p1; ++p) s += part[(static_cast<size_t>(p) * 2 + k) * cols + col];
+  }
+  runs[g][cx] = s;
+  __syncthreads();
+  if (g == 0 && valid) {
+    float t = 0.f;
+#pragma unroll
+    for (int q = 0; q < kSumGroups; ++q) t += runs[q][cx];
+    float* out = k == 0 ? out0 : out1;
+    if (out) out[col] = t;
+  }
 }
 
 // ---------------------------------------------------------------------------------
@@ -290,26 +308,73 @@ __device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float v) { return
 // mode 0: out0 = gelu(a)
 // mode 1: out0 = dh gelu'(a)
 // mode 2: out0 = c gelu'(a) (cotangent of dh), out1 = c dh gelu''(a) (cotangent of a); dh may be null (zero)
+// One element: the outputs of `mode` from a (and dh, c where the mode reads them).
+template <int MODE>
+__device__ __forceinline__ void gelu_elem(float x, float dhv, float cv, bool has_dh, float& o0, float& o1) {
+  const float cdf = 0.5f * (1.f + erff(x * kInvSqrt2));
+  if constexpr (MODE == 0) {
+    o0 = x * cdf;
+  } else {
+    const float pdf = kInvSqrt2Pi * expf(-0.5f * x * x);
+    const float d1 = fmaf(x, pdf, cdf);
+    if constexpr (MODE == 1) {
+      o0 = dhv * d1;
+    } else {
+      o0 = cv * d1;
+      o1 = has_dh ? cv * dhv * pdf * (2.f - x * x) : 0.f;
+    }
+  }
+}
+
 template <typename T, int MODE>
 __global__ void gelu_kernel(long long n, const T* __restrict__ a, const T* __restrict__ dh, const T* __restrict__ c,
                             T* __restrict__ out0, T* __restrict__ out1) {
   for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const float x = to_f(a[i]);
-    const float cdf = 0.5f * (1.f + erff(x * kInvSqrt2));
-    if constexpr (MODE == 0) {
-      out0[i] = from_f<T>(x * cdf);
-    } else {
-      const float pdf = kInvSqrt2Pi * expf(-0.5f * x * x);
-      const float d1 = fmaf(x, pdf, cdf);
-      if constexpr (MODE == 1) {
-        out0[i] = from_f<T>(to_f(dh[i]) * d1);
-      } else {
-        const float cv = to_f(c[i]);
-        out0[i] = from_f<T>(cv * d1);
-        if (out1) out1[i] = from_f<T>(dh ? cv * to_f(dh[i]) * pdf * (2.f - x * x) : 0.f);
-      }
+    float o0 = 0.f, o1 = 0.f;
+    gelu_elem<MODE>(to_f(a[i]), MODE == 1 || (MODE == 2 && dh) ? to_f(dh[i]) : 0.f, MODE == 2 ? to_f(c[i]) : 0.f,
+                    dh != nullptr, o0, o1);
+    out0[i] = from_f<T>(o0);
+    if (MODE == 2 && out1) out1[i] = from_f<T>(o1);
+  }
+}
+
+// 16-byte vectors of E = 16 / sizeof(T) elements (all pointers 16-byte aligned); the
+// last n % E elements by the first threads of block 0. Same per-element math.
+template <typename T, int MODE>
+__global__ void gelu_vec_kernel(long long n, const T* __restrict__ a, const T* __restrict__ dh,
+                                const T* __restrict__ c, T* __restrict__ out0, T* __restrict__ out1) {
+  constexpr int E = 16 / sizeof(T);
+  const long long nvec = n / E;
+  const bool has_dh = dh != nullptr;
+  for (long long v = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; v < nvec;
+       v += static_cast<long long>(gridDim.x) * blockDim.x) {
+    uint4 av = reinterpret_cast<const uint4*>(a)[v], dv = make_uint4(0u, 0u, 0u, 0u), cvv = dv;
+    if (MODE == 1 || (MODE == 2 && has_dh)) dv = reinterpret_cast<const uint4*>(dh)[v];
+    if (MODE == 2) cvv = reinterpret_cast<const uint4*>(c)[v];
+    const T* ae = reinterpret_cast<const T*>(&av);
+    const T* de = reinterpret_cast<const T*>(&dv);
+    const T* ce = reinterpret_cast<const T*>(&cvv);
+    uint4 r0, r1;
+    T* e0 = reinterpret_cast<T*>(&r0);
+    T* e1 = reinterpret_cast<T*>(&r1);
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      float o0 = 0.f, o1 = 0.f;
+      gelu_elem<MODE>(to_f(ae[e]), to_f(de[e]), to_f(ce[e]), has_dh, o0, o1);
+      e0[e] = from_f<T>(o0);
+      e1[e] = from_f<T>(o1);
     }
+    reinterpret_cast<uint4*>(out0)[v] = r0;
+    if (MODE == 2 && out1) reinterpret_cast<uint4*>(out1)[v] = r1;
+  }
+  if (blockIdx.x == 0 && threadIdx.x < n - nvec * E) {
+    const long long i = nvec * E + threadIdx.x;
+    float o0 = 0.f, o1 = 0.f;
+    gelu_elem<MODE>(to_f(a[i]), MODE == 1 || (MODE == 2 && has_dh) ? to_f(dh[i]) : 0.f,
+                    MODE == 2 ? to_f(c[i]) : 0.f, has_dh, o0, o1);
+    out0[i] = from_f<T>(o0);
+    if (MODE == 2 && out1) out1[i] = from_f<T>(o1);
   }
 }
 
@@ -345,7 +410,7 @@ int ln_launch(int op, int rows, int cols, const float* x, const float* w, const 
   if (after_launch() != kOk) return kLaunchFailed;
   float* c0 = op == 1 ? out1 : out2;
   float* c1 = op == 1 ? out2 : nullptr;
-  column_sum_kernel<<<(2 * cols + 255) / 256, 256, 0, stream>>>(grid, cols, part, c0, c1);
+  column_sum_kernel<<<(2 * cols + 31) / 32, 32 * kSumGroups, 0, stream>>>(grid, cols, part, c0, c1);
   return after_launch();
 }
 
@@ -369,21 +434,27 @@ int launch_layernorm(int op, int rows, int cols, const float* x, const float* w,
 int launch_gelu(int mode, bool bf16, long long n, const void* a, const void* dh, const void* c, void* out0, void* out1,
                 cudaStream_t stream) {
   const int block = 256;
-  long long blocks = (n + block - 1) / block;
+  // 16-byte vectors when every pointer allows them (torch allocations do).
+  auto aligned = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  const bool vec = aligned(a) && aligned(dh) && aligned(c) && aligned(out0) && aligned(out1);
+  const long long per_thread = vec ? (bf16 ? 8 : 4) : 1;
+  long long blocks = (n / per_thread + block - 1) / block;
   const long long cap = 8LL * sm_count();
   if (blocks > cap) blocks = cap;
   if (blocks < 1) blocks = 1;
   const unsigned g = static_cast<unsigned>(blocks);
-#define FH_GELU(T)                                                                                                   \
+#define FH_GELU(T, K)                                                                                                \
   do {                                                                                                               \
     const T *pa = static_cast<const T*>(a), *pdh = static_cast<const T*>(dh), *pc = static_cast<const T*>(c);       \
     T *p0 = static_cast<T*>(out0), *p1 = static_cast<T*>(out1);                                                      \
-    if (mode == 0) gelu_kernel<T, 0><<<g, block, 0, stream>>>(n, pa, pdh, pc, p0, p1);                              \
-    else if (mode == 1) gelu_kernel<T, 1><<<g, block, 0, stream>>>(n, pa, pdh, pc, p0, p1);                         \
-    else gelu_kernel<T, 2><<<g, block, 0, stream>>>(n, pa, pdh, pc, p0, p1);                                        \
+    if (mode == 0) K<T, 0><<<g, block, 0, stream>>>(n, pa, pdh, pc, p0, p1);                                         \
+    else if (mode == 1) K<T, 1><<<g, block, 0, stream>>>(n, pa, pdh, pc, p0, p1);                                    \
+    else K<T, 2><<<g, block, 0, stream>>>(n, pa, pdh, pc, p0, p1);                                                   \
   } while (0)
-  if (bf16) FH_GELU(__nv_bfloat16);
-  else FH_GELU(float);
+  if (bf16 && vec) FH_GELU(__nv_bfloat16, gelu_vec_kernel);
+  else if (bf16) FH_GELU(__nv_bfloat16, gelu_kernel);
+  else if (vec) FH_GELU(float, gelu_vec_kernel);
+  else FH_GELU(float, gelu_kernel);
 #undef FH_GELU
   return after_launch();
 }
