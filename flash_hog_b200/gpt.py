@@ -73,7 +73,10 @@ class Block(nn.Module):
     def forward(self, x):
         b, t, d = x.shape
         h = self.cfg.n_head
-        q, k, v = self.qkv(self.ln1(x)).view(b, t, 3, h, d // h).unbind(2)
+        # One projection, then one copy to (3, b, t, h, dh): q, k and v come out contiguous,
+        # so the attention op (and its backward and double backward) copies none of them.
+        qkv = self.qkv(self.ln1(x)).view(b, t, 3, h, d // h).permute(2, 0, 1, 3, 4).contiguous()
+        q, k, v = qkv.unbind(0)
         x = x + self.proj(self.attention(q, k, v, is_causal=True).reshape(b, t, d))
         return x + self.fc2(self.act(self.fc1(self.ln2(x))))
 
