@@ -49,13 +49,16 @@ EXPORTED_SYMBOLS = (
     "fh_layernorm_bwd",
     "fh_layernorm_bwd_bwd",
     "fh_gelu",
+    "fh_xent_fwd",
+    "fh_xent_bwd",
+    "fh_xent_bwd_bwd",
     "fh_device_status",
     "fh_status_string",
     "fh_last_error",
     "fh_abi_version",
     "fh_launch_count",
 )
-ABI_VERSION = 7
+ABI_VERSION = 8
 
 
 class FlashHogError(RuntimeError):
@@ -120,6 +123,10 @@ def lib() -> ctypes.CDLL:
     h.fh_layernorm_bwd.argtypes = [vp, i32, i32] + [vp] * 9
     h.fh_layernorm_bwd_bwd.argtypes = [vp, i32, i32] + [vp] * 12
     h.fh_gelu.argtypes = [vp, i32, i32, ctypes.c_longlong, vp, vp, vp, vp, vp]
+    ll = ctypes.c_longlong
+    h.fh_xent_fwd.argtypes = [vp, i32, i32, i32, ll, vp, vp, vp, vp]
+    h.fh_xent_bwd.argtypes = [vp, i32, i32, i32, ll, vp, vp, vp, vp, f32, vp]
+    h.fh_xent_bwd_bwd.argtypes = [vp, i32, i32, i32, ll, vp, vp, vp, vp, f32, vp, vp, vp]
     h.fh_device_status.argtypes = [vp, ctypes.POINTER(ctypes.c_int)]
     h.fh_status_string.argtypes = [i32]
     h.fh_status_string.restype = ctypes.c_char_p
@@ -131,7 +138,8 @@ def lib() -> ctypes.CDLL:
     for name in ("fh_attn_fwd", "fh_attn_rowdot", "fh_attn_bwd", "fh_attn_bwdbwd", "fh_attn_bwdbwd_pass",
                  "fh_attn_bwdbwd_o", "fh_attn_bwdbwd_noalloc", "fh_attn_jvp_bwd", "fh_attn_fwd_f32",
                  "fh_attn_bwd_f32", "fh_attn_bwdbwd_f32", "fh_attn_jvp_bwd_f32", "fh_device_status",
-                 "fh_abi_version", "fh_layernorm_fwd", "fh_layernorm_bwd", "fh_layernorm_bwd_bwd", "fh_gelu"):
+                 "fh_abi_version", "fh_layernorm_fwd", "fh_layernorm_bwd", "fh_layernorm_bwd_bwd", "fh_gelu",
+                 "fh_xent_fwd", "fh_xent_bwd", "fh_xent_bwd_bwd"):
         getattr(h, name).restype = i32
     if h.fh_abi_version() != ABI_VERSION:
         raise RuntimeError(f"flash_hog_b200 ABI mismatch: library {h.fh_abi_version()}, binding {ABI_VERSION}")
@@ -390,6 +398,40 @@ def gelu(mode: int, a, dh, c, out0, out1) -> None:
             raise ValueError("gelu tensors must share dtype, size and contiguity")
     _check("fh_gelu", lib().fh_gelu(_stream(a.device), int(mode), _GELU_DTYPES[a.dtype], a.numel(), _ptr(a), _ptr(dh),
                                    _ptr(c), _ptr(out0), _ptr(out1)))
+
+
+def _xent_args(z, t):
+    if z.dim() != 2 or z.dtype not in _GELU_DTYPES or z.stride(1) != 1:
+        raise ValueError("xent logits are a (rows, vocab) fp32 or bf16 tensor with unit column stride")
+    if t.dtype != torch.int64 or not t.is_contiguous() or t.numel() != z.shape[0]:
+        raise ValueError("xent targets are a contiguous int64 vector of one entry per row")
+    return _GELU_DTYPES[z.dtype], z.shape[0], z.shape[1], z.stride(0)
+
+
+def xent_fwd(z, t, lse, loss) -> None:
+    """Per-row log-sum-exp and loss of (rows, vocab) logits; see fh_xent_fwd."""
+    dt, rows, vocab, ld = _xent_args(z, t)
+    _check("fh_xent_fwd", lib().fh_xent_fwd(_stream(z.device), dt, rows, vocab, ld, _ptr(z), _ptr(t), _ptr(lse),
+                                             _ptr(loss)))
+
+
+def xent_bwd(z, t, lse, g, s: float, dz) -> None:
+    """dz = g s (softmax(z) - onehot(t)); g a one-element fp32 device tensor."""
+    dt, rows, vocab, ld = _xent_args(z, t)
+    if dz.dtype != z.dtype or not dz.is_contiguous() or dz.shape != z.shape:
+        raise ValueError("dz is a contiguous tensor of the logits' shape and dtype")
+    _check("fh_xent_bwd", lib().fh_xent_bwd(_stream(z.device), dt, rows, vocab, ld, _ptr(z), _ptr(t), _ptr(lse),
+                                             _ptr(g), float(s), _ptr(dz)))
+
+
+def xent_bwd_bwd(z, t, lse, g, s: float, u, gz, gg) -> None:
+    """Backward's backward given the cotangent u of dz; see fh_xent_bwd_bwd."""
+    dt, rows, vocab, ld = _xent_args(z, t)
+    for x in (u, gz):
+        if x.dtype != z.dtype or not x.is_contiguous() or x.shape != z.shape:
+            raise ValueError("u and gz are contiguous tensors of the logits' shape and dtype")
+    _check("fh_xent_bwd_bwd", lib().fh_xent_bwd_bwd(_stream(z.device), dt, rows, vocab, ld, _ptr(z), _ptr(t),
+                                                     _ptr(lse), _ptr(g), float(s), _ptr(u), _ptr(gz), _ptr(gg)))
 
 
 def launch_count() -> int:

@@ -23,7 +23,7 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-O2", "--expt-relaxed-constexpr",
               "-I" + os.path.join(ROOT, "include"), "-I" + CSRC]
 
-MAIN_SOURCES = ["capi.cu", "fwd.cu", "bwd.cu", "bwdbwd.cu", "rowdot.cu", "f32.cu", "ln_gelu.cu"]
+MAIN_SOURCES = ["capi.cu", "fwd.cu", "bwd.cu", "bwdbwd.cu", "rowdot.cu", "f32.cu", "ln_gelu.cu", "xent.cu"]
 
 MAIN_LIB = os.path.join(PKG, "libflashhog_b200.so")
 

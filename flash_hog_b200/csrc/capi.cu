@@ -514,6 +514,47 @@ int fh_gelu(void* stream, int mode, int dtype, long long n, const void* a, const
   return launch_gelu(mode, dtype == 1, n, a, dh, c, out0, out1, st);
 }
 
+static int xent_check(int rows, int vocab, long long ld, int dtype, const void* z, const long long* t) {
+  g_last_error[0] = 0;
+  if (rows < 1 || vocab < 1 || ld < vocab || (dtype != 0 && dtype != 1) || !z || !t)
+    return fail(FH_ERR_INVALID_ARGUMENT, "xent: rows >= 1, vocab >= 1, ld >= vocab, dtype 0 (fp32) or 1 (bf16)");
+  return kOk;
+}
+
+int fh_xent_fwd(void* stream, int dtype, int rows, int vocab, long long ld, const void* z, const long long* t,
+                float* lse, float* loss) {
+  if (injected("fh_xent_fwd")) return FH_ERR_INJECTED;
+  int rc = xent_check(rows, vocab, ld, dtype, z, t);
+  if (rc != kOk) return rc;
+  if (!lse || !loss) return fail(FH_ERR_INVALID_ARGUMENT, "xent: lse and loss are required");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if ((rc = select_stream_device(st)) != kOk) return rc;
+  return launch_xent(0, dtype == 1, rows, vocab, ld, z, t, lse, loss, nullptr, 0.f, nullptr, nullptr, nullptr, st);
+}
+
+int fh_xent_bwd(void* stream, int dtype, int rows, int vocab, long long ld, const void* z, const long long* t,
+                const float* lse, const float* g, float s, void* dz) {
+  if (injected("fh_xent_bwd")) return FH_ERR_INJECTED;
+  int rc = xent_check(rows, vocab, ld, dtype, z, t);
+  if (rc != kOk) return rc;
+  if (!lse || !g || !dz) return fail(FH_ERR_INVALID_ARGUMENT, "xent: lse, g and dz are required");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if ((rc = select_stream_device(st)) != kOk) return rc;
+  return launch_xent(1, dtype == 1, rows, vocab, ld, z, t, const_cast<float*>(lse), nullptr, g, s, nullptr, dz,
+                     nullptr, st);
+}
+
+int fh_xent_bwd_bwd(void* stream, int dtype, int rows, int vocab, long long ld, const void* z, const long long* t,
+                    const float* lse, const float* g, float s, const void* u, void* gz, float* gg) {
+  if (injected("fh_xent_bwd_bwd")) return FH_ERR_INJECTED;
+  int rc = xent_check(rows, vocab, ld, dtype, z, t);
+  if (rc != kOk) return rc;
+  if (!lse || !g || !u || !gz || !gg) return fail(FH_ERR_INVALID_ARGUMENT, "xent: lse, g, u, gz and gg are required");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if ((rc = select_stream_device(st)) != kOk) return rc;
+  return launch_xent(2, dtype == 1, rows, vocab, ld, z, t, const_cast<float*>(lse), nullptr, g, s, u, gz, gg, st);
+}
+
 int fh_device_status(void* stream, int* code) {
   if (!code) return FH_ERR_INVALID_ARGUMENT;
   *code = 0;

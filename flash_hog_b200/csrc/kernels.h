@@ -99,6 +99,11 @@ int ln_partials_rows(int rows);
 // dh gelu'(a); mode 2 out0 = c gelu'(a), out1 = c dh gelu''(a) (dh null = zero).
 int launch_gelu(int mode, bool bf16, long long n, const void* a, const void* dh, const void* c, void* out0, void* out1,
                 cudaStream_t stream);
+// Cross entropy over (rows, vocab) logits: op 0 forward (lse, loss), 1 backward
+// (out = dz), 2 backward's backward (u = cotangent of dz; out = gz, gg per row).
+// `lse` is written by op 0 and read by ops 1 and 2.
+int launch_xent(int op, bool bf16, int rows, int vocab, long long ld, const void* z, const long long* t, float* lse,
+                float* loss, const float* g, float s, const void* u, void* out, float* gg, cudaStream_t stream);
 
 // Checks the kernel launch just made (cudaGetLastError) and, if it was queued,
 // counts it for fh_launch_count(). Returns kOk or kLaunchFailed.

@@ -13,6 +13,10 @@ double backward. Third-order derivatives raise.
   autocast the inputs are cast to fp32, as autocast does for torch's layer_norm.
 * ``gelu(x)``: exact GELU (x Phi(x)) in the input dtype (fp32 or bf16; fp32
   arithmetic), as ``torch.nn.functional.gelu`` under autocast.
+* ``cross_entropy(logits, targets)``: the mean cross entropy of (rows, vocab) logits
+  (fp32 or bf16, fp32 arithmetic) as ``torch.nn.functional.cross_entropy`` on the
+  logits cast to fp32; its gradient comes back in the logits' dtype, as autocast
+  would cast it for the head's matmul (``csrc/xent.cu``, ``fh_xent_*``).
 """
 
 from __future__ import annotations
@@ -119,3 +123,50 @@ class _Gelu(torch.autograd.Function):
 def gelu(x):
     """Exact GELU in the input dtype (fp32 or bf16), differentiable twice on the fused kernels."""
     return _Gelu.apply(_contig(x))
+
+
+class _CrossEntropyBwd(torch.autograd.Function):
+    """dz = g (softmax(z) - onehot(t)) / rows; its backward is the double backward."""
+
+    @staticmethod
+    def forward(ctx, z, t, lse, g):
+        g32 = _contig(g.detach().float().reshape(1))
+        dz = torch.empty(z.shape, dtype=z.dtype, device=z.device)
+        _capi.xent_bwd(z, t, lse, g32, 1.0 / z.shape[0], dz)
+        ctx.save_for_backward(z, t, lse, g32)
+        ctx.g_shape, ctx.g_dtype = g.shape, g.dtype
+        return dz
+
+    @staticmethod
+    def backward(ctx, u):
+        z, t, lse, g32 = ctx.saved_tensors
+        if any(ctx.needs_input_grad) and torch.is_grad_enabled():
+            raise NotImplementedError("third-order derivatives of the fused cross entropy are not supported")
+        u = _contig(u.to(z.dtype))
+        gz = torch.empty(z.shape, dtype=z.dtype, device=z.device)
+        gg = torch.empty(z.shape[0], dtype=torch.float32, device=z.device)
+        _capi.xent_bwd_bwd(z, t, lse, g32, 1.0 / z.shape[0], u, gz, gg)
+        return gz, None, None, gg.sum().to(ctx.g_dtype).reshape(ctx.g_shape)
+
+
+class _CrossEntropy(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, z, t):
+        lse = torch.empty(z.shape[0], dtype=torch.float32, device=z.device)
+        loss = torch.empty_like(lse)
+        _capi.xent_fwd(z, t, lse, loss)
+        ctx.save_for_backward(z, t, lse)
+        return loss.mean()
+
+    @staticmethod
+    def backward(ctx, g):
+        z, t, lse = ctx.saved_tensors
+        return _CrossEntropyBwd.apply(z, t, lse, g), None
+
+
+def cross_entropy(logits, targets):
+    """Mean cross entropy of (rows, vocab) logits against int64 targets, differentiable
+    twice on the fused kernels (fp32 result; the logits' gradient in their dtype)."""
+    if logits.stride(-1) != 1:
+        logits = logits.contiguous()
+    return _CrossEntropy.apply(logits, _contig(targets.long()))

@@ -9,10 +9,10 @@ the objective
 whose gradient needs the double backward of every layer. Attention's double
 backward runs on this package's kernels through ``dot_product_attention`` (two
 nested autograd Functions, the analogue of the reference's nested custom_vjp).
-With ``fused=True`` (the default for the "flash" model) LayerNorm and the MLP's
-GELU run on the fused kernels of ``flash_hog_b200.fused`` -- forward, backward and
-double backward one kernel each -- and the MLP's contractions on cuBLAS (plain
-GEMMs); the embeddings and the loss stay in torch autograd. Data
+With ``fused=True`` (the default for the "flash" model) LayerNorm, the MLP's GELU
+and the cross-entropy loss run on the fused kernels of ``flash_hog_b200.fused`` --
+forward, backward and double backward one kernel each -- and the MLP's contractions
+on cuBLAS (plain GEMMs); the embeddings stay in torch autograd. Data
 parallelism: each rank computes the full step on its own token batch and the
 parameter gradients (penalty terms included) are averaged with one NCCL
 all-reduce over a flat buffer.
@@ -89,7 +89,7 @@ class GPT(nn.Module):
         super().__init__()
         fn = {"flash": dot_product_attention, "naive": naive_attention}[attention]
         fused = attention == "flash" if fused is None else fused
-        self.cfg = cfg
+        self.cfg, self.fused = cfg, fused
         self.wte = nn.Embedding(cfg.vocab, cfg.d_model)
         self.wpe = nn.Embedding(cfg.seq_len, cfg.d_model)
         self.blocks = nn.ModuleList(Block(cfg, fn, fused) for _ in range(cfg.n_layer))
@@ -118,7 +118,10 @@ def penalty_objective(model: GPT, tokens: torch.Tensor, lam: float):
     """(L + lam ||dL/dtheta||^2, L, ||dL/dtheta||^2) for next-token cross-entropy L
     on ``tokens`` (B, T+1); the gradient is kept in the graph (create_graph)."""
     logits = model(tokens[:, :-1])
-    loss = F.cross_entropy(logits.float().flatten(0, 1), tokens[:, 1:].flatten())
+    if getattr(model, "fused", False):  # one kernel per pass, gradient in the logits' dtype
+        loss = fused_ops.cross_entropy(logits.flatten(0, 1), tokens[:, 1:].flatten())
+    else:
+        loss = F.cross_entropy(logits.float().flatten(0, 1), tokens[:, 1:].flatten())
     params = [p for p in model.parameters() if p.requires_grad]
     grads = torch.autograd.grad(loss, params, create_graph=True)
     penalty = sum((g.float() ** 2).sum() for g in grads)

@@ -296,6 +296,24 @@ int fh_layernorm_bwd_bwd(void* stream, int rows, int cols, const float* x, const
 int fh_gelu(void* stream, int mode, int dtype, long long n, const void* a, const void* dh, const void* c, void* out0,
             void* out1);
 
+/* Cross entropy of the same step's language-model head (no counterpart in the
+ * reference either). Logits z are `rows` rows of `vocab` elements, dtype 0 = fp32,
+ * 1 = bf16, row stride `ld` elements (>= vocab); targets t are int64 in [0, vocab)
+ * (one outside gives a NaN loss and no one-hot term). One kernel per pass, one CTA
+ * per row; all outputs are contiguous, fp32 vectors have `rows` entries.
+ *  - fh_xent_fwd: lse[r] = log sum_v exp(z[r,v]), loss[r] = lse[r] - z[r,t[r]].
+ *  - fh_xent_bwd: dz = g s (softmax(z) - onehot(t)), in z's dtype; g points to the
+ *    fp32 upstream scalar (device memory), s is a host scale (1/rows for a mean).
+ *  - fh_xent_bwd_bwd: given the cotangent u of dz (z's dtype, contiguous):
+ *    gz = g s p (u - <p, u>_row) with p = softmax(z) (z's dtype), and
+ *    gg[r] = s (<p_r, u_r> - u[r,t[r]]), whose sum is the cotangent of g. */
+int fh_xent_fwd(void* stream, int dtype, int rows, int vocab, long long ld, const void* z, const long long* t,
+                float* lse, float* loss);
+int fh_xent_bwd(void* stream, int dtype, int rows, int vocab, long long ld, const void* z, const long long* t,
+                const float* lse, const float* g, float s, void* dz);
+int fh_xent_bwd_bwd(void* stream, int dtype, int rows, int vocab, long long ld, const void* z, const long long* t,
+                    const float* lse, const float* g, float s, const void* u, void* gz, float* gg);
+
 /* Synchronises `stream`, then reads and clears the status word the kernels of
  * the current device record device-side failures in. *code receives 0 or one
  * of the device error codes (1..5: which bounded wait expired). Returns FH_OK,
@@ -318,7 +336,7 @@ int fh_abi_version(void);
  * reads it before and after a timed region to report its kernel launches. */
 unsigned long long fh_launch_count(void);
 
-#define FH_ABI_VERSION 7
+#define FH_ABI_VERSION 8
 
 #ifdef __cplusplus
 }

@@ -1,7 +1,7 @@
-"""CPU statements of the LayerNorm and GELU double backward -- TEST INFRASTRUCTURE ONLY.
+"""CPU statements of the LayerNorm, GELU and cross-entropy double backward -- TEST INFRASTRUCTURE ONLY.
 
 Nothing in the product package imports this module; ``tests/`` use it as the
-checker of ``flash_hog_b200/csrc/ln_gelu.cu``. The formulas are the closed forms
+checker of ``flash_hog_b200/csrc/ln_gelu.cu`` and ``csrc/xent.cu``. The formulas are the closed forms
 the kernels evaluate, restated in float64 numpy; ``tests/test_fused_ln_gelu.py``
 checks them against torch's double autograd of ``layer_norm`` and ``gelu`` on the
 CPU, and the kernels against torch on the GPU. (The reference has no model code:
@@ -67,3 +67,31 @@ def gelu_terms(a):
     cdf = 0.5 * (1.0 + _ERF(a / math.sqrt(2.0)))
     pdf = np.exp(-0.5 * a * a) / math.sqrt(2.0 * math.pi)
     return a * cdf, cdf + a * pdf, pdf * (2.0 - a * a)
+
+
+def xent_fwd(z, t):
+    """Per-row (lse, loss) of logits z (rows, vocab) against integer targets t."""
+    z = np.asarray(z, np.float64)
+    m = z.max(-1, keepdims=True)
+    lse = (m + np.log(np.exp(z - m).sum(-1, keepdims=True)))[:, 0]
+    return lse, lse - z[np.arange(z.shape[0]), t]
+
+
+def xent_bwd(z, t, g, s):
+    """dz = g s (softmax(z) - onehot(t))."""
+    z = np.asarray(z, np.float64)
+    lse, _ = xent_fwd(z, t)
+    p = np.exp(z - lse[:, None])
+    p[np.arange(z.shape[0]), t] -= 1.0
+    return g * s * p
+
+
+def xent_bwd_bwd(z, t, g, s, u):
+    """Cotangents of (z, g) for the cotangent u of dz: (g s p (u - <p, u>), sum_r s (<p_r, u_r> - u_r,t_r))."""
+    z, u = np.asarray(z, np.float64), np.asarray(u, np.float64)
+    lse, _ = xent_fwd(z, t)
+    p = np.exp(z - lse[:, None])
+    dot = (p * u).sum(-1, keepdims=True)
+    gz = g * s * p * (u - dot)
+    gg = (s * (dot[:, 0] - u[np.arange(z.shape[0]), t])).sum()
+    return gz, gg

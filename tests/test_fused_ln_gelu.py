@@ -116,3 +116,58 @@ def test_gelu_kernels(dtype, tol):
     assert _rel(da.detach().double().cpu(), dh_r * d1) < tol
     assert _rel(gdh.double().cpu(), c_r * d1) < tol
     assert _rel(ga.double().cpu(), c_r * dh_r * d2) < tol
+
+
+def _torch_xent_second_order(z, t, u):
+    """torch float64: loss, dz (= d loss / dz) and the cotangents of z and of the upstream
+    scalar g for the cotangent u of dz."""
+    z = z.clone().requires_grad_(True)
+    g = torch.ones((), dtype=z.dtype, requires_grad=True)
+    loss = F.cross_entropy(z, t)
+    (dz,) = torch.autograd.grad(loss, z, g, create_graph=True)
+    gz, gg = torch.autograd.grad(dz, (z, g), u)
+    return loss.detach(), dz.detach(), gz, gg
+
+
+@pytest.mark.parametrize("rows,vocab", [(5, 37), (16, 512)])
+def test_xent_closed_forms_match_torch_double_autograd(rows, vocab):
+    gen = torch.Generator().manual_seed(rows + vocab)
+    z = torch.randn(rows, vocab, generator=gen, dtype=torch.float64) * 3
+    t = torch.randint(0, vocab, (rows,), generator=gen)
+    u = torch.randn(rows, vocab, generator=gen, dtype=torch.float64)
+    loss, dz, gz, gg = _torch_xent_second_order(z, t, u)
+    lse, loss_r = lno.xent_fwd(z.numpy(), t.numpy())
+    assert abs(loss_r.mean() - float(loss)) < 1e-12
+    assert _rel(lno.xent_bwd(z.numpy(), t.numpy(), 1.0, 1.0 / rows), dz) < 1e-12
+    gz_o, gg_o = lno.xent_bwd_bwd(z.numpy(), t.numpy(), 1.0, 1.0 / rows, u.numpy())
+    assert _rel(gz_o, gz) < 1e-10
+    assert abs(gg_o - float(gg)) < 1e-10 * max(1.0, abs(float(gg)))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype,tol", [(torch.float32, 2e-5), (torch.bfloat16, 1e-2)])
+@pytest.mark.parametrize("rows,vocab,pad", [(64, 1000, 0), (33, 517, 0), (48, 768, 24)])
+def test_xent_kernels(dtype, tol, rows, vocab, pad):
+    """Forward, backward and backward's backward through the autograd Functions against
+    torch float64 on the values the kernels see; vocab not a multiple of 8 (scalar tail)
+    and a row stride above vocab (pad) included."""
+    from flash_hog_b200 import fused
+
+    gen = torch.Generator().manual_seed(rows * vocab + pad)
+    zfull = (torch.randn(rows, vocab + pad, generator=gen) * 3).to(dtype)
+    t = torch.randint(0, vocab, (rows,), generator=gen)
+    u = torch.randn(rows, vocab, generator=gen).to(dtype)
+    z64 = zfull[:, :vocab].double()
+    loss64, dz64, gz64, gg64 = _torch_xent_second_order(z64, t, u.double())
+    zg = zfull.cuda()[:, :vocab].requires_grad_(True)
+    assert zg.stride(0) == vocab + pad
+    g = torch.ones((), device="cuda", requires_grad=True)
+    loss = fused.cross_entropy(zg, t.cuda())
+    (dz,) = torch.autograd.grad(loss, zg, g, create_graph=True)
+    gz, gg = torch.autograd.grad(dz, (zg, g), u.cuda())
+    torch.cuda.synchronize()
+    assert dz.dtype == dtype and gz.dtype == dtype
+    assert abs(float(loss) - float(loss64)) < 1e-5 * max(1.0, abs(float(loss64)))
+    assert _rel(dz.detach().double().cpu(), dz64) < tol
+    assert _rel(gz.double().cpu(), gz64) < tol
+    assert abs(float(gg) - float(gg64)) < 1e-4 * max(1.0, abs(float(gg64)))
