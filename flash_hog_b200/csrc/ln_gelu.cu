@@ -133,7 +133,7 @@ __device__ __forceinline__ void block_column_partials(const float4 (&acc0)[C], c
 }
 
 template <int C>
-__global__ void __launch_bounds__(32 * kLnWarps) ln_bwd_kernel(int rows, int cols, const float* __restrict__ x,
+__global__ void __launch_bounds__(32 * kLnWarps, 2) ln_bwd_kernel(int rows, int cols, const float* __restrict__ x,
                                                                 const float* __restrict__ w,
                                                                 const float* __restrict__ mean,
                                                                 const float* __restrict__ rstd,
@@ -148,34 +148,35 @@ __global__ void __launch_bounds__(32 * kLnWarps) ln_bwd_kernel(int rows, int col
   for (int row = blockIdx.x * kLnWarps + (threadIdx.x >> 5); row < rows; row += gridDim.x * kLnWarps) {
     const size_t off = static_cast<size_t>(row) * cols;
     const float mu = mean[row], r = rstd[row];
-    float4 xh[C], g[C], dyv[C];
+    // Two passes over the row; the second re-reads x, w, dy (from L1) instead of
+    // keeping them in registers, which leaves room for two blocks per SM.
     float sg = 0.f, sgx = 0.f;
 #pragma unroll
     for (int c = 0; c < C; ++c) {
       const bool ok = c < nch;
       const int col = c * 128 + lane * 4;
-      const float4 xv = ld4_or0(x + off + col, ok), wv = ld4_or0(w + col, ok);
-      dyv[c] = ld4_or0(dy + off + col, ok);
+      const float4 xv = ld4_or0(x + off + col, ok), wv = ld4_or0(w + col, ok), dyv = ld4_or0(dy + off + col, ok);
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const float xhi = ok ? (at(xv, i) - mu) * r : 0.f;
-        const float gi = at(dyv[c], i) * at(wv, i);
-        set(xh[c], i, xhi);
-        set(g[c], i, gi);
+        const float gi = at(dyv, i) * at(wv, i);
         sg += gi;
         sgx = fmaf(gi, xhi, sgx);
-        set(adw[c], i, fmaf(at(dyv[c], i), xhi, at(adw[c], i)));
-        set(adb[c], i, at(adb[c], i) + at(dyv[c], i));
+        set(adw[c], i, fmaf(at(dyv, i), xhi, at(adw[c], i)));
+        set(adb[c], i, at(adb[c], i) + at(dyv, i));
       }
     }
     const float a = warp_sum(sg) * inv_n, be = warp_sum(sgx) * inv_n;
 #pragma unroll
     for (int c = 0; c < C; ++c) {
       if (c >= nch) continue;
+      const int col = c * 128 + lane * 4;
+      const float4 xv = ld4(x + off + col), wv = ld4(w + col), dyv = ld4(dy + off + col);
       float4 o;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) set(o, i, r * (at(g[c], i) - a - at(xh[c], i) * be));
-      st4(dx + off + c * 128 + lane * 4, o);
+      for (int i = 0; i < 4; ++i)
+        set(o, i, r * (at(dyv, i) * at(wv, i) - a - (at(xv, i) - mu) * r * be));
+      st4(dx + off + col, o);
     }
   }
   block_column_partials<C>(adw, adb, nch, cols, part, smem);
@@ -183,7 +184,7 @@ __global__ void __launch_bounds__(32 * kLnWarps) ln_bwd_kernel(int rows, int col
 
 // Second-order backward. u, vb, cb may be null (zero cotangents).
 template <int C>
-__global__ void __launch_bounds__(32 * kLnWarps) ln_bwd_bwd_kernel(
+__global__ void __launch_bounds__(32 * kLnWarps, 2) ln_bwd_bwd_kernel(
     int rows, int cols, const float* __restrict__ x, const float* __restrict__ w, const float* __restrict__ mean,
     const float* __restrict__ rstd, const float* __restrict__ dy, const float* __restrict__ u,
     const float* __restrict__ vb, const float* __restrict__ cb, float* __restrict__ gx, float* __restrict__ gdy,
@@ -197,7 +198,8 @@ __global__ void __launch_bounds__(32 * kLnWarps) ln_bwd_bwd_kernel(
   for (int row = blockIdx.x * kLnWarps + (threadIdx.x >> 5); row < rows; row += gridDim.x * kLnWarps) {
     const size_t off = static_cast<size_t>(row) * cols;
     const float mu = mean[row], r = rstd[row];
-    float4 xh[C], uv[C], dyv[C];
+    // Two passes over the row; the second re-reads x, dy, u (from L1) instead of
+    // keeping them in registers, which leaves room for two blocks per SM.
     float su = 0.f, sux = 0.f, sg = 0.f, sgx = 0.f, sug = 0.f, svd = 0.f, svdx = 0.f;
 #pragma unroll
     for (int c = 0; c < C; ++c) {
@@ -205,13 +207,11 @@ __global__ void __launch_bounds__(32 * kLnWarps) ln_bwd_bwd_kernel(
       const int col = c * 128 + lane * 4;
       const float4 xv = ld4_or0(x + off + col, ok), wv = ld4_or0(w + col, ok);
       const float4 vv = ld4_or0(vb + col, ok && vb);
-      dyv[c] = ld4_or0(dy + off + col, ok);
-      uv[c] = ld4_or0(u + off + col, ok && u);
+      const float4 dyv = ld4_or0(dy + off + col, ok), uv = ld4_or0(u + off + col, ok && u);
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const float xhi = ok ? (at(xv, i) - mu) * r : 0.f;
-        const float gi = at(dyv[c], i) * at(wv, i), ui = at(uv[c], i), vd = at(vv, i) * at(dyv[c], i);
-        set(xh[c], i, xhi);
+        const float gi = at(dyv, i) * at(wv, i), ui = at(uv, i), vd = at(vv, i) * at(dyv, i);
         su += ui;
         sux = fmaf(ui, xhi, sux);
         sg += gi;
@@ -240,10 +240,12 @@ __global__ void __launch_bounds__(32 * kLnWarps) ln_bwd_bwd_kernel(
       const float4 wv = ld4(w + col);
       const float4 vv = vb ? ld4(vb + col) : make_float4(0.f, 0.f, 0.f, 0.f);
       const float4 cv = cb ? ld4(cb + col) : make_float4(0.f, 0.f, 0.f, 0.f);
+      const float4 xv = ld4(x + off + col), dyv = ld4(dy + off + col);
+      const float4 uv = u ? ld4(u + off + col) : make_float4(0.f, 0.f, 0.f, 0.f);
       float4 ox, od;
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        const float xhi = at(xh[c], i), ui = at(uv[c], i), dyi = at(dyv[c], i);
+        const float xhi = (at(xv, i) - mu) * r, ui = at(uv, i), dyi = at(dyv, i);
         const float t = r * (ui - mu_u - xhi * mu_ux);
         set(od, i, fmaf(at(wv, i), t, fmaf(at(vv, i), xhi, at(cv, i))));
         set(agw[c], i, fmaf(dyi, t, at(agw[c], i)));
