@@ -170,3 +170,24 @@ def cross_entropy(logits, targets):
     if logits.stride(-1) != 1:
         logits = logits.contiguous()
     return _CrossEntropy.apply(logits, _contig(targets.long()))
+
+
+class _SumOfSquares(torch.autograd.Function):
+    """sum_i ||t_i||^2 over a list of tensors with multi-tensor kernels: one pass for the
+    norms forward, one scaled copy of every tensor backward (instead of a square, a
+    reduction and their gradients per tensor)."""
+
+    @staticmethod
+    def forward(ctx, *ts):
+        ctx.save_for_backward(*ts)
+        return torch.stack(torch._foreach_norm(list(ts), 2)).float().square().sum()
+
+    @staticmethod
+    def backward(ctx, g):
+        ts = ctx.saved_tensors
+        return tuple(torch._foreach_mul(list(ts), 2.0 * g))
+
+
+def sum_of_squares(tensors):
+    """sum_i ||t_i||^2 (fp32), differentiable once (the penalty term of the step)."""
+    return _SumOfSquares.apply(*tensors)

@@ -124,7 +124,10 @@ def penalty_objective(model: GPT, tokens: torch.Tensor, lam: float):
         loss = F.cross_entropy(logits.float().flatten(0, 1), tokens[:, 1:].flatten())
     params = [p for p in model.parameters() if p.requires_grad]
     grads = torch.autograd.grad(loss, params, create_graph=True)
-    penalty = sum((g.float() ** 2).sum() for g in grads)
+    if getattr(model, "fused", False):  # multi-tensor kernels instead of three per parameter
+        penalty = fused_ops.sum_of_squares(grads)
+    else:
+        penalty = sum((g.float() ** 2).sum() for g in grads)
     return loss + lam * penalty, loss.detach(), penalty.detach()
 
 
