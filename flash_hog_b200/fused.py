@@ -1,4 +1,4 @@
-"""LayerNorm and GELU with fused first- and second-order backward kernels.
+"""LayerNorm, GELU and cross entropy with fused first- and second-order backward kernels.
 
 The grad-norm-penalty step (L + lam ||dL/dtheta||^2, configuration 5) differentiates
 every layer's backward once more. In torch autograd the double backward of
@@ -17,6 +17,8 @@ double backward. Third-order derivatives raise.
   (fp32 or bf16, fp32 arithmetic) as ``torch.nn.functional.cross_entropy`` on the
   logits cast to fp32; its gradient comes back in the logits' dtype, as autocast
   would cast it for the head's matmul (``csrc/xent.cu``, ``fh_xent_*``).
+* ``sum_of_squares(tensors)``: the penalty sum_i ||t_i||^2 with torch's multi-tensor
+  kernels (one norm pass forward, one scaled copy backward), differentiable once.
 """
 
 from __future__ import annotations
