@@ -159,10 +159,16 @@ class PenaltyStepGraph:
     as one graph it runs at the GPU's pace. Shapes, parameters and ``.grad`` tensors
     stay fixed (the graph writes the gradients in place); the data-parallel gradient
     all-reduce and the optimizer update run after the replay, outside the graph.
-    Autocast runs with its cast cache off, as graph capture requires.
+    With ``flat_grads`` (default: when a multi-rank process group is initialised) every
+    ``.grad`` is a view of one flat fp32 buffer, which the graph zeroes first and the
+    backward accumulates into, so the all-reduce runs on it in place (no gather or
+    scatter copies); on one GPU the backward's own gradient tensors are kept instead
+    (no zeroing, no accumulation pass). Autocast runs with its cast cache off, as graph
+    capture requires.
     """
 
-    def __init__(self, model: GPT, batch: int, lam: float, autocast: bool = True, warmup: int = 3):
+    def __init__(self, model: GPT, batch: int, lam: float, autocast: bool = True, warmup: int = 3,
+                 flat_grads: bool | None = None):
         dev = next(model.parameters()).device
         self.model, self.lam, self.autocast = model, lam, autocast
         self.tokens = torch.zeros((batch, model.cfg.seq_len + 1), dtype=torch.long, device=dev)
@@ -173,7 +179,21 @@ class PenaltyStepGraph:
                 model.zero_grad(set_to_none=True)
                 self._compute()
         torch.cuda.current_stream(dev).wait_stream(side)
+        if flat_grads is None:
+            import torch.distributed as dist
+
+            flat_grads = dist.is_available() and dist.is_initialized() and dist.get_world_size() > 1
+        self.flat = None
         model.zero_grad(set_to_none=True)
+        if flat_grads:
+            params = [p for p in model.parameters() if p.requires_grad]
+            if any(p.dtype != torch.float32 for p in params):
+                raise ValueError("flat_grads keeps the gradients in one fp32 buffer: fp32 parameters only")
+            self.flat = torch.zeros(sum(p.numel() for p in params), dtype=torch.float32, device=dev)
+            off = 0
+            for p in params:
+                p.grad = self.flat[off:off + p.numel()].view_as(p)
+                off += p.numel()
         self.graph = torch.cuda.CUDAGraph()
         n0 = _capi.launch_count()
         # thread_local: calls from other threads (NCCL's watchdog under torchrun) cannot
@@ -183,6 +203,8 @@ class PenaltyStepGraph:
         self.kernels_per_step = _capi.launch_count() - n0  # this library's kernels in one replay
 
     def _compute(self):
+        if getattr(self, "flat", None) is not None:
+            self.flat.zero_()  # the backward accumulates into the flat gradient views
         with torch.autocast(device_type="cuda", dtype=torch.bfloat16, enabled=self.autocast, cache_enabled=False):
             total, loss, penalty = penalty_objective(self.model, self.tokens, self.lam)
         total.backward()
@@ -194,7 +216,12 @@ class PenaltyStepGraph:
         (loss, penalty) device scalars, overwritten by the next replay."""
         self.tokens.copy_(tokens, non_blocking=True)
         self.graph.replay()
-        if distributed:
+        if distributed and self.flat is not None:
+            import torch.distributed as dist
+
+            dist.all_reduce(self.flat)
+            self.flat /= dist.get_world_size()
+        elif distributed:
             allreduce_grads(self.model)
         if optimizer is not None:
             optimizer.step()

@@ -79,16 +79,20 @@ def test_fused_layernorm_gelu_match_torch_modules_in_the_step():
 
 
 @pytest.mark.gpu
-def test_graphed_step_equals_eager_step():
+@pytest.mark.parametrize("flat_grads", [False, True])
+def test_graphed_step_equals_eager_step(flat_grads):
     """The step captured as a CUDA graph and replayed on new tokens gives the eager
-    step's loss, penalty and gradients (bf16 autocast, the benchmark's policy)."""
+    step's loss, penalty and gradients (bf16 autocast, the benchmark's policy), with the
+    backward's own gradient tensors and with all gradients in one flat buffer (the
+    multi-rank layout, whose buffer the graph zeroes and accumulates into)."""
     from flash_hog_b200.gpt import GPT, PenaltyStepGraph
 
     torch.manual_seed(0)
     eager = GPT(SMALL, attention="flash").cuda()
     graphed = GPT(SMALL, attention="flash").cuda()
     graphed.load_state_dict(eager.state_dict())
-    step = PenaltyStepGraph(graphed, batch=2, lam=0.1)
+    step = PenaltyStepGraph(graphed, batch=2, lam=0.1, flat_grads=flat_grads)
+    assert (step.flat is not None) == flat_grads
     for seed in (21, 22):
         tokens = _tokens(SMALL, 2, seed=seed, device="cuda")
         eager.zero_grad(set_to_none=True)
