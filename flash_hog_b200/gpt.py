@@ -157,7 +157,8 @@ class PenaltyStepGraph:
     The step launches thousands of small kernels (every layer differentiated twice),
     so launched one by one from Python it is bound by host launch latency; replayed
     as one graph it runs at the GPU's pace. Shapes, parameters and ``.grad`` tensors
-    stay fixed (the graph writes the gradients in place); the data-parallel gradient
+    stay fixed (the graph writes the gradients in place: do not reset them with
+    ``zero_grad(set_to_none=True)`` between replays); the data-parallel gradient
     all-reduce and the optimizer update run after the replay, outside the graph.
     With ``flat_grads`` (default: when a multi-rank process group is initialised) every
     ``.grad`` is a view of one flat fp32 buffer, which the graph zeroes first and the
