@@ -171,3 +171,27 @@ def test_xent_kernels(dtype, tol, rows, vocab, pad):
     assert _rel(dz.detach().double().cpu(), dz64) < tol
     assert _rel(gz.double().cpu(), gz64) < tol
     assert abs(float(gg) - float(gg64)) < 1e-4 * max(1.0, abs(float(gg64)))
+
+
+@pytest.mark.gpu
+def test_xent_targets_outside_the_vocabulary():
+    """A target outside [0, vocab) is caught by the kernels' own bounds check: its row's
+    loss is NaN and its gradient has no one-hot term (softmax / rows); other rows are
+    unaffected."""
+    from flash_hog_b200 import _capi
+
+    rows, vocab = 4, 40
+    z = torch.randn(rows, vocab, generator=torch.Generator().manual_seed(3)).cuda()
+    t = torch.tensor([3, -1, vocab, 7], dtype=torch.int64, device="cuda")
+    lse = torch.empty(rows, device="cuda")
+    loss = torch.empty(rows, device="cuda")
+    _capi.xent_fwd(z, t, lse, loss)
+    g = torch.ones(1, device="cuda")
+    dz = torch.empty_like(z)
+    _capi.xent_bwd(z, t, lse, g, 1.0 / rows, dz)
+    torch.cuda.synchronize()
+    assert torch.isnan(loss[1]) and torch.isnan(loss[2])
+    ref = torch.nn.functional.cross_entropy(z[[0, 3]].double().cpu(), t[[0, 3]].cpu(), reduction="none")
+    assert torch.allclose(loss[[0, 3]].double().cpu(), ref, rtol=1e-5, atol=1e-5)
+    p = torch.softmax(z.double(), -1).cpu() / rows
+    assert torch.allclose(dz[1:3].double().cpu(), p[1:3], rtol=1e-4, atol=1e-7)
