@@ -70,9 +70,15 @@ struct QPass {
   static constexpr int C_S = 0, C_DDS = BN, C_DP = 2 * BN, C_DPA = 3 * BN, SCORE_COLS = 4 * BN;
   static constexpr int C_DQ = SCORE_COLS, C_DDO = SCORE_COLS + HD, C_OPS = SCORE_COLS + 2 * HD;
   static constexpr int OPS_COLS = BN / 2;
+  // head_dim 128: ddQ as packed bf16 in TMEM (HD/2 columns after the operands), the A
+  // operand of ddS += ddQ K^T as a TS product that reads only K from shared memory (the
+  // SS form with 32-key tiles is bound by shared-memory reads: 40 cycles a k-step
+  // against 16 of math).
+  static constexpr bool DDQ_T = HD == 128;
+  static constexpr int C_DDQ = C_OPS + 4 * OPS_COLS;
   static constexpr int TMEM_COLS = 512;
-  static_assert(C_OPS + 4 * OPS_COLS <= TMEM_COLS, "TMEM budget");
-  static_assert(2 * SCORE_COLS <= TMEM_COLS, "stats sweep double-buffers the scores");
+  static_assert(C_DDQ + (DDQ_T ? HD / 2 : 0) <= TMEM_COLS, "TMEM budget");
+  static_assert(2 * SCORE_COLS <= (DDQ_T ? C_DDQ : TMEM_COLS), "stats sweep double-buffers the scores");
   static_assert(SMEM <= 232448, "shared memory budget");
   static_assert(CW % 16 == 0 && HD % 64 == 0, "tile shapes");
 };
@@ -203,6 +209,7 @@ __global__ void __launch_bounds__(kBBThreads, 1)
   static_assert(G::RES <= G::SLOT, "O fits in one ring slot");
   __shared__ uint64_t bar_res, bar_full[ST], bar_empty[ST];
   __shared__ uint64_t bar_sc_full[2], bar_sc_empty[2], bar_ops_full, bar_ops_empty, bar_acc, bar_red, bar_ofree;
+  __shared__ uint64_t bar_tres;  // head_dim 128: ddQ copied into TMEM
   __shared__ float red[4][2][kBM];  // stats-sweep partial sums: statistic, warpgroup, row
   __shared__ float dred[2][kBM];    // partial rowsum(dO o): warpgroup, row
   __shared__ uint32_t tmem_base;
@@ -238,6 +245,7 @@ __global__ void __launch_bounds__(kBBThreads, 1)
     mbar_init(&bar_acc, 1);
     mbar_init(&bar_red, kBBEwWarps);
     mbar_init(&bar_ofree, kBBEwWarps);
+    mbar_init(&bar_tres, kBBEwWarps);
     mbar_fence_init();
   }
   if (warp == kBBWarpMma) tmem_alloc(&tmem_base, G::TMEM_COLS);
@@ -288,11 +296,16 @@ __global__ void __launch_bounds__(kBBThreads, 1)
       constexpr int KS = HD / 16;
       const uint32_t id128 = idesc_bf16_f32(kBM, 2 * BN, false, false);
       const uint32_t id64 = idesc_bf16_f32(kBM, BN, false, false);
-      const uint64_t a_q = kdesc(s_q), a_do = kdesc(s_do), a_ddq = kdesc(s_ddq);
+      const uint64_t a_q = kdesc(s_q), a_do = kdesc(s_do);
+      [[maybe_unused]] const uint64_t a_ddq = kdesc(s_ddq);  // head_dim 64 (SS form)
       const uint64_t b_ring = kdesc(s_ring);  // pair (K | ddK) of slot 0, K-major
       constexpr uint64_t kSlot = G::SLOT >> 4, kPair = G::PAIR >> 4;
       bool ok = mbar_wait_warp(&bar_res, 0, &abort_flag);
       if (!ok && lane == 0) raise_error(a.status, &abort_flag, kDevTimeoutTmaFull);
+      if (G::DDQ_T && ok) {  // ddQ in TMEM (copied by the elementwise warps)
+        ok = mbar_wait_warp(&bar_tres, 0, &abort_flag);
+        if (!ok && lane == 0) raise_error(a.status, &abort_flag, kDevTimeoutEpilogue);
+      }
       for (int it = 0; ok && it < total; ++it) {
         const int s = it % ST, sb = buf_of(it), u = use_of(it);
         if (!mbar_wait_warp(&bar_full[s], (it / ST) & 1, &abort_flag)) {
@@ -307,7 +320,11 @@ __global__ void __launch_bounds__(kBBThreads, 1)
         const uint64_t bk = b_ring + s * kSlot;
         const uint32_t tb = tmem + sb * G::SCORE_COLS;
         umma_chain_w<KS, G::RES_PANEL, G::PAIR_PANEL, false>(tb + G::C_S, a_q, bk, id128, false);
-        umma_chain_w<KS, G::RES_PANEL, G::PAIR_PANEL, false>(tb + G::C_DDS, a_ddq, bk, id64, true);
+        if constexpr (G::DDQ_T) {
+          umma_chain_tsk_w<KS, G::PAIR_PANEL>(tb + G::C_DDS, tmem + G::C_DDQ, bk, id64, true);
+        } else {
+          umma_chain_w<KS, G::RES_PANEL, G::PAIR_PANEL, false>(tb + G::C_DDS, a_ddq, bk, id64, true);
+        }
         if constexpr (!TJ)
           umma_chain_w<KS, G::RES_PANEL, G::PAIR_PANEL, false>(tb + G::C_DP, a_do, bk + kPair, id128, false);
         umma_commit_w(&bar_sc_full[sb]);
@@ -361,6 +378,17 @@ __global__ void __launch_bounds__(kBBThreads, 1)
     float dD = 0.f, Bv = 0.f, cq = 0.f;
     bool ok = true;
     float dv = 0.f;
+    if constexpr (G::DDQ_T) {
+      // head_dim 128: this CTA's ddQ rows into TMEM, each warpgroup half of the head_dim
+      // columns, for the TS form of ddS += ddQ K^T (the score issuer waits for it before
+      // the first ddS product).
+      ok = mbar_wait_warp(&bar_res, 0, &abort_flag);
+      if (ok) {
+        row_to_tmem<HD / 2>(s_ddq, r, wg * (HD / 2), tmem + tmem_lane_base(warp & 3) + G::C_DDQ);
+        tmem_wait_st();
+        warp_arrive(&bar_tres);
+      }
+    }
     if constexpr (TJ) {
       dv = 0.f;  // dO = 0
     } else if (a.delta_out == nullptr) {
@@ -368,7 +396,7 @@ __global__ void __launch_bounds__(kBBThreads, 1)
     } else {
       // D = rowsum(dO o) of this row from the resident tiles, while the first
       // scores are computed: each warpgroup sums half of the head_dim columns.
-      ok = mbar_wait_warp(&bar_res, 0, &abort_flag);
+      if (ok) ok = mbar_wait_warp(&bar_res, 0, &abort_flag);
       dv = ok ? rowdot_share<HD>(s_o, s_do, r, wg) : 0.f;
       dred[wg][r] = dv;
       warp_arrive(&bar_ofree);  // O has been read: its ring slot may be refilled
@@ -532,10 +560,16 @@ struct KPass {
   // TMEM: scores, accumulators dK', dV', bf16 operands dS^T, dS2^T, ddP^T (A of the MMAs).
   static constexpr int C_S = 0, C_DDS = BN, C_DP = 2 * BN, C_DPA = 3 * BN;
   static constexpr int C_DK = 4 * BN, C_DV = 4 * BN + HD, C_OPS = 4 * BN + 2 * HD;
+  // head_dim 128: ddV as packed bf16 in TMEM (HD/2 columns), the A operand of
+  // dPa^T = ddV dO^T as a TS product that reads only dO from shared memory (with 32-query
+  // tiles the SS form is shared-memory bound at 40 cycles per k-step against 16 of math).
+  // At head_dim 64 the per-item copy costs more than the 64-query chain saves.
+  static constexpr bool DDV_T = HD == 128;
+  static constexpr int C_DDV = C_OPS + 3 * (BN / 2);
   static constexpr int OPS_COLS = BN / 2;
   static constexpr int TMEM_COLS = 512;
   static_assert(SLOT % 1024 == 0 && (4 * RES + ONES) % 1024 == 0, "slots must keep panels 1024-byte aligned");
-  static_assert(C_OPS + 3 * OPS_COLS <= TMEM_COLS, "TMEM budget");
+  static_assert(C_DDV + (DDV_T ? HD / 2 : 0) <= TMEM_COLS, "TMEM budget");
   static_assert(C_DDS == C_S + BN && C_DP == C_S + 2 * BN && C_DPA == C_S + 3 * BN, "one bias MMA covers 4 products");
   static_assert(SMEM <= 232448, "shared memory budget");
   static_assert(CW % 16 == 0 && BN % 32 == 0, "tile shapes");
@@ -621,7 +655,7 @@ __global__ void __launch_bounds__(kBBThreads, 1)
   uint8_t* s_ones = s_ddv + G::RES;
   uint8_t* s_ring = s_ones + G::ONES;
   __shared__ uint64_t bar_res, bar_res_empty, bar_full[ST], bar_empty[ST];
-  __shared__ uint64_t bar_sc_full, bar_sc_empty, bar_ops_full, bar_ops_empty, bar_acc, bar_acc_empty;
+  __shared__ uint64_t bar_sc_full, bar_sc_empty, bar_ops_full, bar_ops_empty, bar_acc, bar_acc_empty, bar_tres;
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
 
@@ -644,6 +678,7 @@ __global__ void __launch_bounds__(kBBThreads, 1)
     mbar_init(&bar_ops_empty, 1);
     mbar_init(&bar_acc, 1);
     mbar_init(&bar_acc_empty, kBBEwWarps);
+    mbar_init(&bar_tres, kBBEwWarps);
     mbar_fence_init();
   }
   if (threadIdx.x < kBM) {
@@ -776,6 +811,11 @@ __global__ void __launch_bounds__(kBBThreads, 1)
         if (lane == 0) raise_error(a.status, &abort_flag, kDevTimeoutTmaFull);
         break;
       }
+      // This item's ddV in TMEM (copied by the elementwise warps once the residents landed).
+      if (G::DDV_T && !mbar_wait_warp(&bar_tres, ai & 1, &abort_flag)) {
+        if (lane == 0) raise_error(a.status, &abort_flag, kDevTimeoutEpilogue);
+        break;
+      }
       for (int it = 0; it < w.total; ++it, ++gt) {
         const int s = gt % ST;
         if (!mbar_wait_warp(&bar_full[s], (gt / ST) & 1, &abort_flag)) {
@@ -795,7 +835,10 @@ __global__ void __launch_bounds__(kBBThreads, 1)
         umma_chain_w<KS, G::RES_PANEL, G::PAIR_PANEL, false>(tmem + G::C_S, a_k, bq, id128, true);
         umma_chain_w<KS, G::RES_PANEL, G::PAIR_PANEL, false>(tmem + G::C_DDS, a_ddk, bq, id64, true);
         umma_chain_w<KS, G::RES_PANEL, BN * 128, false>(tmem + G::C_DP, a_v, bo, id64, true);
-        umma_chain_w<KS, G::RES_PANEL, BN * 128, false>(tmem + G::C_DPA, a_ddv, bo, id64, true);
+        if constexpr (G::DDV_T)
+          umma_chain_tsk_w<KS, BN * 128>(tmem + G::C_DPA, tmem + G::C_DDV, bo, id64, true);
+        else
+          umma_chain_w<KS, G::RES_PANEL, BN * 128, false>(tmem + G::C_DPA, a_ddv, bo, id64, true);
         umma_commit_w(&bar_sc_full);
       }
       if (!ok) break;
@@ -867,6 +910,16 @@ __global__ void __launch_bounds__(kBBThreads, 1)
         // No query sees these keys (causal with Tk > Tq): the gradients are zero.
         if (key_ok) zero_row_global<HD>(dst);
         continue;
+      }
+      // head_dim 128: this item's ddV rows into TMEM, each warpgroup half of the head_dim columns, once
+      // the residents landed (which also means the previous item's score MMAs, the last
+      // readers of the TMEM copy, are done).
+      if constexpr (G::DDV_T) {
+        ok = mbar_wait_warp(&bar_res, ai & 1, &abort_flag);
+        if (!ok) break;
+        row_to_tmem<HD / 2>(s_ddv, r, wg * (HD / 2), tmem + tmem_lane_base(warp & 3) + G::C_DDV);
+        tmem_wait_st();
+        warp_arrive(&bar_tres);
       }
       for (int it = 0; it < w.total; ++it, ++gt) {
         const int qc = (w.qt_begin + it % w.n) * BN + cb;  // first query of this thread's columns
