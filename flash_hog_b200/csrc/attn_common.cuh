@@ -127,6 +127,32 @@ __host__ __device__ __forceinline__ int query_tiles(const AttnShape& s, int k0, 
   return hi / bn + 1 - *first;
 }
 
+// Launch order with L2 locality. A grid of `pairs` (head, batch) pairs x `tiles` tiles
+// runs in groups of g pairs: each group's tiles heaviest first (ti = 0) with the group's
+// pairs fastest. The CTAs in flight at once then stream the per-head tiles they share
+// (K and V for query tiles, Q and dO for key tiles) of a few heads, which stay in L2,
+// instead of one or two tiles of every head. w in [0, pairs * tiles).
+__host__ __device__ __forceinline__ void grouped_order(int w, int tiles, int pairs, int g, int* ti, int* pair) {
+  const int span = g * tiles;
+  const int grp = w / span, rem = w - grp * span;
+  const int gs = min(g, pairs - grp * g);
+  *ti = rem / gs;
+  *pair = grp * g + rem % gs;
+}
+
+// Group size for grouped_order: every pair in one group (the plain heaviest-first order,
+// which balances causal work best) while the shared tiles of all pairs fit in L2
+// together, else groups whose shared tiles take about 32 MB. `bytes_per_head` is what
+// the CTAs of one head stream in common, `shared` how many consecutive pairs read it
+// (the query heads of one key head under GQA, else 1); the result is a multiple of it.
+inline int locality_group(int pairs, int shared, long long bytes_per_head) {
+  constexpr long long kFitsInL2 = 96ll << 20, kGroupBytes = 32ll << 20;
+  if (static_cast<long long>(pairs / shared) * bytes_per_head <= kFitsInL2) return pairs;
+  long long g = kGroupBytes / (bytes_per_head > 0 ? bytes_per_head : 1);
+  g = (g < 1 ? 1 : g) * shared;
+  return g < pairs ? static_cast<int>(g) : pairs;
+}
+
 __device__ __forceinline__ size_t row_offset(const Strides3& s, int b, int t, int h) {
   return static_cast<size_t>(b) * s.b + static_cast<size_t>(t) * s.t + static_cast<size_t>(h) * s.h;
 }

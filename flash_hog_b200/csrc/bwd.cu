@@ -41,6 +41,8 @@ struct BwdArgs {
   const __nv_bfloat16* dk_acc;
   const __nv_bfloat16* dv_acc;
   int* status;
+  int grp_q;  // dQ pass: (query head, batch) pairs per locality group (grouped_order)
+  int grp_k;  // dK/dV pass: (key head, batch) pairs per locality group
 };
 
 // ----------------------------------------------------------------------------------
@@ -125,10 +127,13 @@ __global__ void __launch_bounds__(kBBThreads, DqPass<HD>::CTAS)
   __shared__ int abort_flag;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int h = blockIdx.x, b = blockIdx.y;
+  const int nq = (a.sh.Tq + kBM - 1) / kBM;
+  int qi, hb;
+  grouped_order(blockIdx.x, nq, a.sh.H * a.sh.B, a.grp_q, &qi, &hb);
+  const int h = hb % a.sh.H, b = hb / a.sh.H;
   SeqRange sr;
   const AttnShape sh = seq_shape<VL>(a.sh, b, &sr);  // this sequence's lengths and mask; sr: where its rows start
-  const int qt = gridDim.z - 1 - blockIdx.z;  // longest causal rows first
+  const int qt = nq - 1 - qi;  // longest causal rows first (within the locality group)
   const int q0 = qt * kBM;
   int j0;
   const int n = key_tiles(sh, q0, kBM, BN, &j0);  // key tiles j0, j0 + 1, ... (0: no row sees a key)
@@ -441,10 +446,12 @@ __global__ void __launch_bounds__(kBBThreads, DkvPass<HD>::CTAS)
   __shared__ int abort_flag;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int hk = blockIdx.x, b = blockIdx.y;
+  int kt, hb;
+  grouped_order(blockIdx.x, (a.sh.Tk + kBM - 1) / kBM, a.sh.Hk * a.sh.B, a.grp_k, &kt, &hb);
+  const int hk = hb % a.sh.Hk, b = hb / a.sh.Hk;
   SeqRange sr;
   const AttnShape sh = seq_shape<VL>(a.sh, b, &sr);
-  const int k0 = blockIdx.z * kBM;  // key tile 0 first: the most causal query tiles
+  const int k0 = kt * kBM;  // key tile 0 first: the most causal query tiles
   int qt_begin;
   const int n = query_tiles(sh, k0, kBM, BN, &qt_begin);  // query tiles that see any of these keys
   const int total = n * sh.G;  // streamed tiles: n per query head of the group
@@ -744,12 +751,16 @@ int launch_bwd_hd(const AttnShape& s, const BwdPtrs& p, int* status, cudaStream_
                static_cast<const __nv_bfloat16*>(p.dq_acc),
                static_cast<const __nv_bfloat16*>(p.dk_acc),
                static_cast<const __nv_bfloat16*>(p.dv_acc),
-               status};
-  bwd_dq_kernel<HD, VL><<<dim3(s.H, s.B, (s.Tq + kBM - 1) / kBM), kBBThreads, GQ::SMEM, stream>>>(mq[0], mq[1], mq[2],
-                                                                                             mq[3], mq[4], args);
+               status,
+               // Shared streamed tiles per head: K and V of a key head (dQ pass); Q and
+               // dO of its query heads (dK/dV pass).
+               locality_group(s.H * s.B, s.H / s.Hk, 2ll * s.Tk * HD * 2),
+               locality_group(s.Hk * s.B, 1, 2ll * (s.H / s.Hk) * s.Tq * HD * 2)};
+  bwd_dq_kernel<HD, VL><<<dim3(s.H * s.B * ((s.Tq + kBM - 1) / kBM)), kBBThreads, GQ::SMEM, stream>>>(
+      mq[0], mq[1], mq[2], mq[3], mq[4], args);
   if (after_launch() != kOk) return kLaunchFailed;
-  bwd_dkdv_kernel<HD, VL><<<dim3(s.Hk, s.B, (s.Tk + kBM - 1) / kBM), kBBThreads, GK::SMEM, stream>>>(mk[0], mk[1], mk[2],
-                                                                                               mk[3], args);
+  bwd_dkdv_kernel<HD, VL><<<dim3(s.Hk * s.B * ((s.Tk + kBM - 1) / kBM)), kBBThreads, GK::SMEM, stream>>>(
+      mk[0], mk[1], mk[2], mk[3], args);
   return after_launch();
 }
 

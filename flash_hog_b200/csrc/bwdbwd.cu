@@ -44,6 +44,8 @@ struct BBArgs {
   __nv_bfloat16* dk2;
   __nv_bfloat16* dv2;
   int* status;
+  int grp_q;  // query pass: (query head, batch) pairs per locality group (grouped_order)
+  int grp_k;  // key pass: (key head, batch) pairs per locality group
 };
 
 // ----------------------------------------------------------------------------------
@@ -216,10 +218,13 @@ __global__ void __launch_bounds__(kBBThreads, 1)
   __shared__ int abort_flag;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int h = blockIdx.x, b = blockIdx.y;
+  const int nq = (a.sh.Tq + kBM - 1) / kBM;
+  int qi, hb;
+  grouped_order(blockIdx.x, nq, a.sh.H * a.sh.B, a.grp_q, &qi, &hb);
+  const int h = hb % a.sh.H, b = hb / a.sh.H;
   SeqRange sr;
   const AttnShape sh = seq_shape<VL>(a.sh, b, &sr);  // this sequence's lengths and mask; sr: where its rows start
-  const int qt = gridDim.z - 1 - blockIdx.z;  // longest causal rows first
+  const int qt = nq - 1 - qi;  // longest causal rows first (within the locality group)
   const int q0 = qt * kBM;
   int j0;
   const int n = key_tiles(sh, q0, kBM, BN, &j0);  // key tiles j0, j0 + 1, ... per sweep (0: no row sees a key)
@@ -615,15 +620,15 @@ struct KItem {
   SeqRange r;
 };
 
-// Work item w in heaviest-first order (key tile 0 first: the most causal query
-// tiles), key heads fastest.
+// Work item w: locality groups of g (key head, batch) pairs, each in heaviest-first
+// order (key tile 0 first: the most causal query tiles) with its pairs fastest.
 template <bool VL>
-__device__ __forceinline__ KItem k_item(const AttnShape& sh, int w, int bn) {
-  const int per_kt = sh.Hk * sh.B;
-  const int kt = w / per_kt, rem = w - kt * per_kt;
+__device__ __forceinline__ KItem k_item(const AttnShape& sh, int w, int bn, int g) {
+  int kt, hb;
+  grouped_order(w, (sh.Tk + kBM - 1) / kBM, sh.Hk * sh.B, g, &kt, &hb);
   KItem it;
-  it.hk = rem % sh.Hk;
-  it.b = rem / sh.Hk;
+  it.hk = hb % sh.Hk;
+  it.b = hb / sh.Hk;
   it.k0 = kt * kBM;
   it.l = seq_shape<VL>(sh, it.b, &it.r);
   it.n = query_tiles(it.l, it.k0, kBM, bn, &it.qt_begin);  // query tiles that see any of these keys
@@ -721,7 +726,7 @@ __global__ void __launch_bounds__(kBBThreads, 1)
     for (int j = 0; ok; ++j) {
       const int wi = snake_item(j, c, P);
       if (wi >= n_items) break;
-      const KItem w = k_item<VL>(sh, wi, BN);
+      const KItem w = k_item<VL>(sh, wi, BN, a.grp_k);
       if (w.total == 0) continue;
       // The previous item's score MMAs no longer read the resident tiles.
       if (ai > 0 && !mbar_wait_warp(&bar_res_empty, (ai - 1) & 1, &abort_flag)) {
@@ -805,7 +810,7 @@ __global__ void __launch_bounds__(kBBThreads, 1)
     for (int j = 0; ok; ++j) {
       const int wi = snake_item(j, c, P);
       if (wi >= n_items) break;
-      const KItem w = k_item<VL>(sh, wi, BN);
+      const KItem w = k_item<VL>(sh, wi, BN, a.grp_k);
       if (w.total == 0) continue;
       if (!mbar_wait_warp(&bar_res, ai & 1, &abort_flag)) {
         if (lane == 0) raise_error(a.status, &abort_flag, kDevTimeoutTmaFull);
@@ -859,7 +864,7 @@ __global__ void __launch_bounds__(kBBThreads, 1)
     for (int j = 0; ok; ++j) {
       const int wi = snake_item(j, c, P);
       if (wi >= n_items) break;
-      const KItem w = k_item<VL>(sh, wi, BN);
+      const KItem w = k_item<VL>(sh, wi, BN, a.grp_k);
       if (w.total == 0) continue;
       for (int it = 0; it < w.total; ++it, ++gt) {
         if (!mbar_wait_warp(&bar_ops_full, gt & 1, &abort_flag)) {
@@ -900,7 +905,7 @@ __global__ void __launch_bounds__(kBBThreads, 1)
     for (int j = 0; ok; ++j) {
       const int wi = snake_item(j, c, P);
       if (wi >= n_items) break;
-      const KItem w = k_item<VL>(sh, wi, BN);
+      const KItem w = k_item<VL>(sh, wi, BN, a.grp_k);
       const int key = w.k0 + r;
       const bool key_ok = key < w.l.Tk;
       const int qhi = query_hi(w.l, key), qlo = query_lo(w.l, key);  // queries that see this key
@@ -1011,7 +1016,12 @@ int launch_bwdbwd_hd(const AttnShape& s, const BwdBwdPtrs& p, int passes, int* s
               static_cast<__nv_bfloat16*>(p.dk2),
               static_cast<__nv_bfloat16*>(p.dv2),
               status};
-  const dim3 gq(s.H, s.B, (s.Tq + kBM - 1) / kBM);
+  // Shared streamed tiles per head: K, V, ddK, ddV of a key head for the query pass;
+  // Q, ddQ and dO of its query heads for the key pass.
+  const int G = s.H / s.Hk;
+  args.grp_q = locality_group(s.H * s.B, G, 4ll * s.Tk * HD * 2);
+  args.grp_k = locality_group(s.Hk * s.B, 1, 3ll * G * s.Tq * HD * 2);
+  const dim3 gq(s.H * s.B * ((s.Tq + kBM - 1) / kBM));
   if (passes & kPassFwdTangent) {
     bwdbwd_q_kernel<HD, VL, true><<<gq, kBBThreads, GQ::SMEM, stream>>>(mq[0], mq[1], mq[2], mq[3], mq[4], mq[5],
                                                                        mq[6], mq[7], args);

@@ -44,6 +44,7 @@ struct FwdArgs {
   __nv_bfloat16* o;
   float* lse;
   int* status;
+  int grp;  // (query head, batch) pairs per locality group (grouped_order)
 };
 
 
@@ -132,10 +133,13 @@ __global__ void __launch_bounds__(FPass<HD>::THREADS, FPass<HD>::CTAS)
   __shared__ int abort_flag;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int h = blockIdx.x, b = blockIdx.y;
+  const int nq = (a.sh.Tq + G::ROWS - 1) / G::ROWS;
+  int qi, hb;
+  grouped_order(blockIdx.x, nq, a.sh.H * a.sh.B, a.grp, &qi, &hb);
+  const int h = hb % a.sh.H, b = hb / a.sh.H;
   SeqRange sr;
   const AttnShape sh = seq_shape<VL>(a.sh, b, &sr);  // this sequence's lengths and mask; sr: where its rows start
-  const int qt = gridDim.z - 1 - blockIdx.z;  // longest causal rows first
+  const int qt = nq - 1 - qi;  // longest causal rows first (within the locality group)
   const int q0 = qt * G::ROWS;
   // Key tiles of each query tile: nt[t] tiles from key tile jt[t] (0 when the
   // tile lies past the last query row or sees no key). The ring streams the
@@ -437,8 +441,10 @@ int launch_fwd_hd(const AttnShape& s, const FwdPtrs& p, int* status, cudaStream_
       !make_seq_map(&mv, p.v, HD, s.total_k, s.Hk, map_batch(s), s.sk, G::BN))
     return kInvalidArgument;
   if (ensure_smem_limit(reinterpret_cast<const void*>(&fwd_kernel<HD, VL>), G::SMEM) != kOk) return kLaunchFailed;
-  FwdArgs args{s, static_cast<__nv_bfloat16*>(p.o), p.lse, status};
-  const dim3 grid(s.H, s.B, (s.Tq + G::ROWS - 1) / G::ROWS);
+  // K and V of a key head are the tiles the query tiles of its heads share.
+  FwdArgs args{s, static_cast<__nv_bfloat16*>(p.o), p.lse, status,
+               locality_group(s.H * s.B, s.H / s.Hk, 2ll * s.Tk * HD * 2)};
+  const dim3 grid(s.H * s.B * ((s.Tq + G::ROWS - 1) / G::ROWS));
   fwd_kernel<HD, VL><<<grid, G::THREADS, G::SMEM, stream>>>(mq, mk, mv, args);
   return after_launch();
 }
