@@ -103,7 +103,7 @@ __device__ __forceinline__ void dq_ops(const uint32_t (&vs)[CW], const uint32_t 
   }
 }
 
-template <int HD, bool VL>
+template <int HD, bool VL, bool GRP>
 __global__ void __launch_bounds__(kBBThreads, DqPass<HD>::CTAS)
     bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
                   const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
@@ -127,13 +127,17 @@ __global__ void __launch_bounds__(kBBThreads, DqPass<HD>::CTAS)
   __shared__ int abort_flag;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nq = (a.sh.Tq + kBM - 1) / kBM;
-  int qi, hb;
-  grouped_order(blockIdx.x, nq, a.sh.H * a.sh.B, a.grp_q, &qi, &hb);
-  const int h = hb % a.sh.H, b = hb / a.sh.H;
+  // Grid (H, B, query tiles), longest causal rows first; GRP: a 1-D grid in the
+  // locality-grouped order.
+  int h = blockIdx.x, b = blockIdx.y, qt = gridDim.z - 1 - blockIdx.z;
+  if constexpr (GRP) {
+    const int nq = (a.sh.Tq + kBM - 1) / kBM;
+    int qi, hb;
+    grouped_order(blockIdx.x, nq, a.sh.H * a.sh.B, a.grp_q, &qi, &hb);
+    h = hb % a.sh.H, b = hb / a.sh.H, qt = nq - 1 - qi;
+  }
   SeqRange sr;
   const AttnShape sh = seq_shape<VL>(a.sh, b, &sr);  // this sequence's lengths and mask; sr: where its rows start
-  const int qt = nq - 1 - qi;  // longest causal rows first (within the locality group)
   const int q0 = qt * kBM;
   int j0;
   const int n = key_tiles(sh, q0, kBM, BN, &j0);  // key tiles j0, j0 + 1, ... (0: no row sees a key)
@@ -427,7 +431,7 @@ __device__ __forceinline__ void dkv_ops(const uint32_t (&vs)[CW], const uint32_t
   }
 }
 
-template <int HD, bool VL>
+template <int HD, bool VL, bool GRP>
 __global__ void __launch_bounds__(kBBThreads, DkvPass<HD>::CTAS)
     bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                     const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
@@ -446,12 +450,17 @@ __global__ void __launch_bounds__(kBBThreads, DkvPass<HD>::CTAS)
   __shared__ int abort_flag;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  int kt, hb;
-  grouped_order(blockIdx.x, (a.sh.Tk + kBM - 1) / kBM, a.sh.Hk * a.sh.B, a.grp_k, &kt, &hb);
-  const int hk = hb % a.sh.Hk, b = hb / a.sh.Hk;
+  // Grid (Hk, B, key tiles), key tile 0 first (the most causal query tiles); GRP: a
+  // 1-D grid in the locality-grouped order.
+  int hk = blockIdx.x, b = blockIdx.y, kt = blockIdx.z;
+  if constexpr (GRP) {
+    int hb;
+    grouped_order(blockIdx.x, (a.sh.Tk + kBM - 1) / kBM, a.sh.Hk * a.sh.B, a.grp_k, &kt, &hb);
+    hk = hb % a.sh.Hk, b = hb / a.sh.Hk;
+  }
   SeqRange sr;
   const AttnShape sh = seq_shape<VL>(a.sh, b, &sr);
-  const int k0 = kt * kBM;  // key tile 0 first: the most causal query tiles
+  const int k0 = kt * kBM;
   int qt_begin;
   const int n = query_tiles(sh, k0, kBM, BN, &qt_begin);  // query tiles that see any of these keys
   const int total = n * sh.G;  // streamed tiles: n per query head of the group
@@ -739,9 +748,14 @@ int launch_bwd_hd(const AttnShape& s, const BwdPtrs& p, int* status, cudaStream_
             make_seq_map(&mk[2], p.q, HD, s.total_q, s.H, map_batch(s), s.sq, GK::BN) &&
             make_seq_map(&mk[3], p.dO, HD, s.total_q, s.H, map_batch(s), s.sq, GK::BN);
   if (!ok) return kInvalidArgument;
-  if (ensure_smem_limit(reinterpret_cast<const void*>(&bwd_dq_kernel<HD, VL>), GQ::SMEM) != kOk ||
-      ensure_smem_limit(reinterpret_cast<const void*>(&bwd_dkdv_kernel<HD, VL>), GK::SMEM) != kOk)
+  if (ensure_smem_limit(reinterpret_cast<const void*>(&bwd_dq_kernel<HD, VL, false>), GQ::SMEM) != kOk ||
+      ensure_smem_limit(reinterpret_cast<const void*>(&bwd_dkdv_kernel<HD, VL, false>), GK::SMEM) != kOk)
     return kLaunchFailed;
+  if constexpr (!VL) {
+    if (ensure_smem_limit(reinterpret_cast<const void*>(&bwd_dq_kernel<HD, false, true>), GQ::SMEM) != kOk ||
+        ensure_smem_limit(reinterpret_cast<const void*>(&bwd_dkdv_kernel<HD, false, true>), GK::SMEM) != kOk)
+      return kLaunchFailed;
+  }
   BwdArgs args{s,
                p.lse,
                p.delta,
@@ -756,11 +770,21 @@ int launch_bwd_hd(const AttnShape& s, const BwdPtrs& p, int* status, cudaStream_
                // dO of its query heads (dK/dV pass).
                locality_group(s.H * s.B, s.H / s.Hk, 2ll * s.Tk * HD * 2),
                locality_group(s.Hk * s.B, 1, 2ll * (s.H / s.Hk) * s.Tq * HD * 2)};
-  bwd_dq_kernel<HD, VL><<<dim3(s.H * s.B * ((s.Tq + kBM - 1) / kBM)), kBBThreads, GQ::SMEM, stream>>>(
-      mq[0], mq[1], mq[2], mq[3], mq[4], args);
+  // The grouped kernels only where the groups split the pairs.
+  const int nq = (s.Tq + kBM - 1) / kBM, nk = (s.Tk + kBM - 1) / kBM;
+  if (!VL && args.grp_q < s.H * s.B)
+    bwd_dq_kernel<HD, false, true><<<dim3(s.H * s.B * nq), kBBThreads, GQ::SMEM, stream>>>(mq[0], mq[1], mq[2], mq[3],
+                                                                                         mq[4], args);
+  else
+    bwd_dq_kernel<HD, VL, false><<<dim3(s.H, s.B, nq), kBBThreads, GQ::SMEM, stream>>>(mq[0], mq[1], mq[2], mq[3],
+                                                                                     mq[4], args);
   if (after_launch() != kOk) return kLaunchFailed;
-  bwd_dkdv_kernel<HD, VL><<<dim3(s.Hk * s.B * ((s.Tk + kBM - 1) / kBM)), kBBThreads, GK::SMEM, stream>>>(
-      mk[0], mk[1], mk[2], mk[3], args);
+  if (!VL && args.grp_k < s.Hk * s.B)
+    bwd_dkdv_kernel<HD, false, true><<<dim3(s.Hk * s.B * nk), kBBThreads, GK::SMEM, stream>>>(mk[0], mk[1], mk[2],
+                                                                                            mk[3], args);
+  else
+    bwd_dkdv_kernel<HD, VL, false><<<dim3(s.Hk, s.B, nk), kBBThreads, GK::SMEM, stream>>>(mk[0], mk[1], mk[2], mk[3],
+                                                                                        args);
   return after_launch();
 }
 

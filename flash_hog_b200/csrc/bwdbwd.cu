@@ -189,7 +189,7 @@ __device__ __forceinline__ void q_ops_tj(const uint32_t (&vs)[CW], const uint32_
 // D = B = 0, dS = dS2 = 0 and dQ' = 0, and the pass reduces to the jvp of the forward:
 // ddO = ddP V + P ddV = tO and dD = rowsum(P ddS) = tL. It skips the dO products, the
 // dQ' products and dO's tile: 8 of the 14 GEMM-equivalents per pair remain.
-template <int HD, bool VL, bool TJ>
+template <int HD, bool VL, bool TJ, bool GRP>
 __global__ void __launch_bounds__(kBBThreads, 1)
     bwdbwd_q_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
                     const __grid_constant__ CUtensorMap tm_ddq, const __grid_constant__ CUtensorMap tm_k,
@@ -218,13 +218,17 @@ __global__ void __launch_bounds__(kBBThreads, 1)
   __shared__ int abort_flag;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nq = (a.sh.Tq + kBM - 1) / kBM;
-  int qi, hb;
-  grouped_order(blockIdx.x, nq, a.sh.H * a.sh.B, a.grp_q, &qi, &hb);
-  const int h = hb % a.sh.H, b = hb / a.sh.H;
+  // Grid (H, B, query tiles), longest causal rows first; GRP: a 1-D grid in the
+  // locality-grouped order.
+  int h = blockIdx.x, b = blockIdx.y, qt = gridDim.z - 1 - blockIdx.z;
+  if constexpr (GRP) {
+    const int nq = (a.sh.Tq + kBM - 1) / kBM;
+    int qi, hb;
+    grouped_order(blockIdx.x, nq, a.sh.H * a.sh.B, a.grp_q, &qi, &hb);
+    h = hb % a.sh.H, b = hb / a.sh.H, qt = nq - 1 - qi;
+  }
   SeqRange sr;
   const AttnShape sh = seq_shape<VL>(a.sh, b, &sr);  // this sequence's lengths and mask; sr: where its rows start
-  const int qt = nq - 1 - qi;  // longest causal rows first (within the locality group)
   const int q0 = qt * kBM;
   int j0;
   const int n = key_tiles(sh, q0, kBM, BN, &j0);  // key tiles j0, j0 + 1, ... per sweep (0: no row sees a key)
@@ -620,12 +624,18 @@ struct KItem {
   SeqRange r;
 };
 
-// Work item w: locality groups of g (key head, batch) pairs, each in heaviest-first
-// order (key tile 0 first: the most causal query tiles) with its pairs fastest.
-template <bool VL>
+// Work item w in heaviest-first order (key tile 0 first: the most causal query
+// tiles), key heads fastest; GRP: in locality groups of g (key head, batch) pairs.
+template <bool VL, bool GRP>
 __device__ __forceinline__ KItem k_item(const AttnShape& sh, int w, int bn, int g) {
   int kt, hb;
-  grouped_order(w, (sh.Tk + kBM - 1) / kBM, sh.Hk * sh.B, g, &kt, &hb);
+  if constexpr (GRP) {
+    grouped_order(w, (sh.Tk + kBM - 1) / kBM, sh.Hk * sh.B, g, &kt, &hb);
+  } else {
+    const int per_kt = sh.Hk * sh.B;
+    kt = w / per_kt;
+    hb = w - kt * per_kt;
+  }
   KItem it;
   it.hk = hb % sh.Hk;
   it.b = hb / sh.Hk;
@@ -643,7 +653,7 @@ __device__ __forceinline__ KItem k_item(const AttnShape& sh, int w, int bn, int 
 // MMAs of the previous item are done (bar_res_empty), so the reload overlaps the
 // previous item's last tile and epilogue, and the operand MMAs of an item start
 // only once the previous item's accumulators were read out (bar_acc_empty).
-template <int HD, bool VL>
+template <int HD, bool VL, bool GRP>
 __global__ void __launch_bounds__(kBBThreads, 1)
     bwdbwd_k_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                     const __grid_constant__ CUtensorMap tm_ddk, const __grid_constant__ CUtensorMap tm_ddv,
@@ -726,7 +736,7 @@ __global__ void __launch_bounds__(kBBThreads, 1)
     for (int j = 0; ok; ++j) {
       const int wi = snake_item(j, c, P);
       if (wi >= n_items) break;
-      const KItem w = k_item<VL>(sh, wi, BN, a.grp_k);
+      const KItem w = k_item<VL, GRP>(sh, wi, BN, a.grp_k);
       if (w.total == 0) continue;
       // The previous item's score MMAs no longer read the resident tiles.
       if (ai > 0 && !mbar_wait_warp(&bar_res_empty, (ai - 1) & 1, &abort_flag)) {
@@ -810,7 +820,7 @@ __global__ void __launch_bounds__(kBBThreads, 1)
     for (int j = 0; ok; ++j) {
       const int wi = snake_item(j, c, P);
       if (wi >= n_items) break;
-      const KItem w = k_item<VL>(sh, wi, BN, a.grp_k);
+      const KItem w = k_item<VL, GRP>(sh, wi, BN, a.grp_k);
       if (w.total == 0) continue;
       if (!mbar_wait_warp(&bar_res, ai & 1, &abort_flag)) {
         if (lane == 0) raise_error(a.status, &abort_flag, kDevTimeoutTmaFull);
@@ -864,7 +874,7 @@ __global__ void __launch_bounds__(kBBThreads, 1)
     for (int j = 0; ok; ++j) {
       const int wi = snake_item(j, c, P);
       if (wi >= n_items) break;
-      const KItem w = k_item<VL>(sh, wi, BN, a.grp_k);
+      const KItem w = k_item<VL, GRP>(sh, wi, BN, a.grp_k);
       if (w.total == 0) continue;
       for (int it = 0; it < w.total; ++it, ++gt) {
         if (!mbar_wait_warp(&bar_ops_full, gt & 1, &abort_flag)) {
@@ -905,7 +915,7 @@ __global__ void __launch_bounds__(kBBThreads, 1)
     for (int j = 0; ok; ++j) {
       const int wi = snake_item(j, c, P);
       if (wi >= n_items) break;
-      const KItem w = k_item<VL>(sh, wi, BN, a.grp_k);
+      const KItem w = k_item<VL, GRP>(sh, wi, BN, a.grp_k);
       const int key = w.k0 + r;
       const bool key_ok = key < w.l.Tk;
       const int qhi = query_hi(w.l, key), qlo = query_lo(w.l, key);  // queries that see this key
@@ -1000,10 +1010,16 @@ int launch_bwdbwd_hd(const AttnShape& s, const BwdBwdPtrs& p, int passes, int* s
        make_seq_map(&mk[5], p.dO ? p.dO : p.q, HD, s.total_q, s.H, map_batch(s), s.sq, GK::BN) &&
        make_seq_map(&mk[6], p.ddq, HD, s.total_q, s.H, map_batch(s), s.sq, GK::BN);
   if (!ok) return kInvalidArgument;
-  if (ensure_smem_limit(reinterpret_cast<const void*>(&bwdbwd_q_kernel<HD, VL, false>), GQ::SMEM) != kOk ||
-      ensure_smem_limit(reinterpret_cast<const void*>(&bwdbwd_q_kernel<HD, VL, true>), GQ::SMEM) != kOk ||
-      ensure_smem_limit(reinterpret_cast<const void*>(&bwdbwd_k_kernel<HD, VL>), GK::SMEM) != kOk)
+  if (ensure_smem_limit(reinterpret_cast<const void*>(&bwdbwd_q_kernel<HD, VL, false, false>), GQ::SMEM) != kOk ||
+      ensure_smem_limit(reinterpret_cast<const void*>(&bwdbwd_q_kernel<HD, VL, true, false>), GQ::SMEM) != kOk ||
+      ensure_smem_limit(reinterpret_cast<const void*>(&bwdbwd_k_kernel<HD, VL, false>), GK::SMEM) != kOk)
     return kLaunchFailed;
+  if constexpr (!VL) {
+    if (ensure_smem_limit(reinterpret_cast<const void*>(&bwdbwd_q_kernel<HD, false, false, true>), GQ::SMEM) != kOk ||
+        ensure_smem_limit(reinterpret_cast<const void*>(&bwdbwd_q_kernel<HD, false, true, true>), GQ::SMEM) != kOk ||
+        ensure_smem_limit(reinterpret_cast<const void*>(&bwdbwd_k_kernel<HD, false, true>), GK::SMEM) != kOk)
+      return kLaunchFailed;
+  }
   // With `o`, the query pass computes D into delta_out and the key pass reads it there.
   BBArgs args{s,
               p.lse,
@@ -1021,21 +1037,37 @@ int launch_bwdbwd_hd(const AttnShape& s, const BwdBwdPtrs& p, int passes, int* s
   const int G = s.H / s.Hk;
   args.grp_q = locality_group(s.H * s.B, G, 4ll * s.Tk * HD * 2);
   args.grp_k = locality_group(s.Hk * s.B, 1, 3ll * G * s.Tq * HD * 2);
-  const dim3 gq(s.H * s.B * ((s.Tq + kBM - 1) / kBM));
-  if (passes & kPassFwdTangent) {
-    bwdbwd_q_kernel<HD, VL, true><<<gq, kBBThreads, GQ::SMEM, stream>>>(mq[0], mq[1], mq[2], mq[3], mq[4], mq[5],
-                                                                       mq[6], mq[7], args);
-    if (after_launch() != kOk) return kLaunchFailed;
-  } else if (passes & kPassQuery) {
-    bwdbwd_q_kernel<HD, VL, false><<<gq, kBBThreads, GQ::SMEM, stream>>>(mq[0], mq[1], mq[2], mq[3], mq[4], mq[5],
-                                                                        mq[6], mq[7], args);
+  // The grouped kernels only where the groups split the pairs (packed ragged batches
+  // keep the plain order).
+  const bool grp_q = !VL && args.grp_q < s.H * s.B, grp_k = !VL && args.grp_k < s.Hk * s.B;
+  const int nq = (s.Tq + kBM - 1) / kBM;
+  const dim3 gq(s.H, s.B, nq), gq_grouped(s.H * s.B * nq);
+  if (passes & (kPassFwdTangent | kPassQuery)) {
+    const bool tj = (passes & kPassFwdTangent) != 0;
+#define FH_Q_LAUNCH(TJ_, GRP_, GRID)                                                                       \
+  bwdbwd_q_kernel<HD, GRP_ ? false : VL, TJ_, GRP_><<<GRID, kBBThreads, GQ::SMEM, stream>>>(                 \
+      mq[0], mq[1], mq[2], mq[3], mq[4], mq[5], mq[6], mq[7], args)
+    if (grp_q) {
+      if (tj) FH_Q_LAUNCH(true, true, gq_grouped);
+      else FH_Q_LAUNCH(false, true, gq_grouped);
+    } else if (tj) {
+      FH_Q_LAUNCH(true, false, gq);
+    } else {
+      FH_Q_LAUNCH(false, false, gq);
+    }
+#undef FH_Q_LAUNCH
     if (after_launch() != kOk) return kLaunchFailed;
   }
   if (passes & kPassKey) {
     // Persistent: one CTA per SM (at most one per work item).
     const int items = s.Hk * s.B * ((s.Tk + kBM - 1) / kBM);
     const dim3 gk(static_cast<unsigned>(items < sm_count() ? items : sm_count()));
-    bwdbwd_k_kernel<HD, VL><<<gk, kBBThreads, GK::SMEM, stream>>>(mk[0], mk[1], mk[2], mk[3], mk[4], mk[5], mk[6], args);
+    if (grp_k)
+      bwdbwd_k_kernel<HD, false, true><<<gk, kBBThreads, GK::SMEM, stream>>>(mk[0], mk[1], mk[2], mk[3], mk[4], mk[5],
+                                                                             mk[6], args);
+    else
+      bwdbwd_k_kernel<HD, VL, false><<<gk, kBBThreads, GK::SMEM, stream>>>(mk[0], mk[1], mk[2], mk[3], mk[4], mk[5],
+                                                                            mk[6], args);
     if (after_launch() != kOk) return kLaunchFailed;
   }
   return kOk;

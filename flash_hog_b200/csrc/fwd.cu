@@ -112,7 +112,7 @@ __device__ __forceinline__ void fwd_warp_arrive(uint64_t* bar) {
   if ((threadIdx.x & 31) == 0) mbar_arrive(bar);
 }
 
-template <int HD, bool VL>
+template <int HD, bool VL, bool GRP>
 __global__ void __launch_bounds__(FPass<HD>::THREADS, FPass<HD>::CTAS)
     fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                const __grid_constant__ CUtensorMap tm_v, const FwdArgs a) {
@@ -133,13 +133,17 @@ __global__ void __launch_bounds__(FPass<HD>::THREADS, FPass<HD>::CTAS)
   __shared__ int abort_flag;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nq = (a.sh.Tq + G::ROWS - 1) / G::ROWS;
-  int qi, hb;
-  grouped_order(blockIdx.x, nq, a.sh.H * a.sh.B, a.grp, &qi, &hb);
-  const int h = hb % a.sh.H, b = hb / a.sh.H;
+  // Grid (H, B, query tiles), longest causal rows first; GRP: a 1-D grid in the
+  // locality-grouped order.
+  int h = blockIdx.x, b = blockIdx.y, qt = gridDim.z - 1 - blockIdx.z;
+  if constexpr (GRP) {
+    const int nq = (a.sh.Tq + G::ROWS - 1) / G::ROWS;
+    int qi, hb;
+    grouped_order(blockIdx.x, nq, a.sh.H * a.sh.B, a.grp, &qi, &hb);
+    h = hb % a.sh.H, b = hb / a.sh.H, qt = nq - 1 - qi;
+  }
   SeqRange sr;
   const AttnShape sh = seq_shape<VL>(a.sh, b, &sr);  // this sequence's lengths and mask; sr: where its rows start
-  const int qt = nq - 1 - qi;  // longest causal rows first (within the locality group)
   const int q0 = qt * G::ROWS;
   // Key tiles of each query tile: nt[t] tiles from key tile jt[t] (0 when the
   // tile lies past the last query row or sees no key). The ring streams the
@@ -440,12 +444,19 @@ int launch_fwd_hd(const AttnShape& s, const FwdPtrs& p, int* status, cudaStream_
       !make_seq_map(&mk, p.k, HD, s.total_k, s.Hk, map_batch(s), s.sk, G::BN) ||
       !make_seq_map(&mv, p.v, HD, s.total_k, s.Hk, map_batch(s), s.sk, G::BN))
     return kInvalidArgument;
-  if (ensure_smem_limit(reinterpret_cast<const void*>(&fwd_kernel<HD, VL>), G::SMEM) != kOk) return kLaunchFailed;
+  if (ensure_smem_limit(reinterpret_cast<const void*>(&fwd_kernel<HD, VL, false>), G::SMEM) != kOk) return kLaunchFailed;
+  if constexpr (!VL) {
+    if (ensure_smem_limit(reinterpret_cast<const void*>(&fwd_kernel<HD, false, true>), G::SMEM) != kOk)
+      return kLaunchFailed;
+  }
   // K and V of a key head are the tiles the query tiles of its heads share.
   FwdArgs args{s, static_cast<__nv_bfloat16*>(p.o), p.lse, status,
                locality_group(s.H * s.B, s.H / s.Hk, 2ll * s.Tk * HD * 2)};
-  const dim3 grid(s.H * s.B * ((s.Tq + G::ROWS - 1) / G::ROWS));
-  fwd_kernel<HD, VL><<<grid, G::THREADS, G::SMEM, stream>>>(mq, mk, mv, args);
+  const int nq = (s.Tq + G::ROWS - 1) / G::ROWS;
+  if (!VL && args.grp < s.H * s.B)  // grouped only where the groups split the pairs
+    fwd_kernel<HD, false, true><<<dim3(s.H * s.B * nq), G::THREADS, G::SMEM, stream>>>(mq, mk, mv, args);
+  else
+    fwd_kernel<HD, VL, false><<<dim3(s.H, s.B, nq), G::THREADS, G::SMEM, stream>>>(mq, mk, mv, args);
   return after_launch();
 }
 
