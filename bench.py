@@ -64,12 +64,22 @@ def set_workload(name):
         METRIC = f"bwd-of-bwd TFLOP/s/GPU, {describe()}"
 
 
+def set_batch(b):
+    """A smaller batch of the same workload (the per-(batch, head) work is unchanged):
+    the small case of an ncu capture, whose traffic scales to the full launch by B."""
+    global B, METRIC
+    B = b
+    METRIC = f"bwd-of-bwd TFLOP/s/GPU, {describe()}"
+
+
 def describe():
     seq = f"S{SQ}" if SQ == SK else f"Sq{SQ} Sk{SK}"
     return f"{'causal' if CAUSAL else 'non-causal'} bf16 B{B} H{H} {seq} D{D}"
 N_SETS = 3  # rotating input sets, each larger than the 126 MB L2
 PEAKS_FILE = os.path.join(ROOT, "MEASURED_PEAKS.json")
-QPASS_DRAM_BYTES = 212.4e6  # ncu dram read + write of one query-pass launch (profiles/)
+# ncu dram read + write of one query-pass launch (profiles/); cfg3 from its B1 capture
+# times 2 (the batches are independent, so the traffic scales with B).
+QPASS_DRAM_BYTES = {"cfg2": 212.4e6, "cfg3": 2 * (556.8e6 + 121.3e6)}
 FALLBACK_PEAKS = {"bf16_tflops": 1590.0, "hbm_gbs": 6650.0}
 
 
@@ -578,6 +588,8 @@ def main():
     ap.add_argument("--skip-e2e", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["gpt", "fwdbwd", "fwdbwd128", "f32"], default="cfg2")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="double-backward workloads: a smaller batch (a small case for ncu captures)")
     args = ap.parse_args()
     if args.workload in ("fwdbwd", "fwdbwd128"):
         args.warmup = max(args.warmup, 3)
@@ -590,7 +602,9 @@ def main():
             args.warmup = 3
         return run_gpt(args)
     set_workload(args.workload)
-    if args.workload != "cfg2":
+    if args.batch:
+        set_batch(args.batch)
+    if args.workload != "cfg2" or args.batch:
         args.skip_cpu = True  # the CPU baseline samples the headline workload only
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
@@ -900,7 +914,7 @@ def run_ours(args):
                 "frac": achieved / peaks["bf16_tflops"], "peak_source": f"{peak_kind} bf16 dense (burst)",
                 # dram__bytes_read.sum + dram__bytes_write.sum of one query-pass launch of this
                 # workload, from the ncu capture summarised in profiles/bwdbwd_b4h16s2048d64_causal.md
-                "traffic": QPASS_DRAM_BYTES if args.workload == "cfg2" else None,
+                "traffic": QPASS_DRAM_BYTES.get(args.workload) if not args.batch else None,
                 "traffic_unit": "bytes per launch (ncu)",
                 "per_launch_ms": {"query_pass": t_q, "key_pass": t_k},
                 "key_pass": {"achieved": credited_flops(b_loc, h_loc, gemms=8) / (t_k * 1e-3) / 1e12,
