@@ -1,7 +1,7 @@
 """Build step of the GPU unit test of the tcgen05 building blocks.
 
-Compiles ``tests/csrc/selftest.cu`` (against the library's ``tc05.cuh`` and
-``tmap.h``) for sm_100a into ``tests/csrc/libfh_selftest.so``, the library
+Compiles ``tests/csrc/selftest.cu`` (against the library's ``tc05.cuh``,
+``tmap.h`` and ``attn_common.cuh``) for sm_100a into ``tests/csrc/libfh_selftest.so``, the library
 ``tests/test_gpu_primitives.py`` loads. Test infrastructure: the product
 library does not contain this kernel.
 """
@@ -22,7 +22,7 @@ def build() -> str:
     sys.path.insert(0, ROOT)
     from flash_hog_b200.build import ARCH, CSRC, NVCC_FLAGS, nvcc
 
-    deps = [SRC] + [os.path.join(CSRC, f) for f in ("tc05.cuh", "tmap.h")]
+    deps = [SRC] + [os.path.join(CSRC, f) for f in ("tc05.cuh", "tmap.h", "attn_common.cuh")]
     if os.path.exists(LIB) and os.path.getmtime(LIB) >= max(os.path.getmtime(p) for p in deps):
         return LIB
     cmd = [nvcc(), *ARCH, *NVCC_FLAGS, "-shared", SRC, "-o", LIB]

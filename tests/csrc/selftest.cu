@@ -1,4 +1,6 @@
-// Unit test of the tcgen05 building blocks (not part of the attention API).
+// Unit test of the tcgen05 building blocks (not part of the attention API), plus
+// host entry points for the launch-order helpers of attn_common.cuh (grouped_order,
+// locality_group), which the CPU tests drive directly.
 //
 // One CTA computes C[128][N] = A[128][K] * B in fp32 through TMA-loaded,
 // 128B-swizzled panels and tcgen05.mma, then reads the accumulator back from
@@ -9,6 +11,7 @@
 
 #include <cuda_runtime.h>
 
+#include "attn_common.cuh"
 #include "tc05.cuh"
 #include "tmap.h"
 
@@ -148,4 +151,13 @@ extern "C" int fh_selftest_umma(const void* A, const void* B, float* C, int N, i
   SelftestArgs args{static_cast<const __nv_bfloat16*>(A), C, N, K, b_mn, a_threads, status};
   umma_selftest_kernel<<<1, kThreads, smem, static_cast<cudaStream_t>(stream)>>>(tmA, tmB, args);
   return cudaGetLastError() == cudaSuccess ? 0 : 3;
+}
+
+// Host wrappers of the attention kernels' launch-order helpers (CPU-testable).
+extern "C" void fh_selftest_grouped_order(int w, int tiles, int pairs, int g, int* ti, int* pair) {
+  fh::grouped_order(w, tiles, pairs, g, ti, pair);
+}
+
+extern "C" int fh_selftest_locality_group(int pairs, int shared, long long bytes_per_head) {
+  return fh::locality_group(pairs, shared, bytes_per_head);
 }
