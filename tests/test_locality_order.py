@@ -28,6 +28,9 @@ CASES = [
     # forward and dQ pass 64 pairs (last 16), dK/dV pass 16 (last 8), double-backward
     # query pass 32 (last 16), key pass 10 (last 4).
     (1, 208, 104, 2048, 128),
+    # head_dim 64 (the two-CTA-per-SM layouts): 208 heads of 0.5-1 MB -> groups of
+    # 64 / 32 / 42 pairs, last groups of 16, 16 and 40.
+    (1, 208, 208, 2048, 64),
 ]
 
 
